@@ -1,0 +1,343 @@
+#!/usr/bin/env python
+"""Benchmark of the INT4 group-wise dequantizing GEMV (m = 1).
+
+One step = one decode GEMV (m = 1) over each of the four Llama-style FFN
+weights of BASELINE.json config 2, W [out x in] in {[5632x2048], [2048x5632],
+[14336x4096], [4096x14336]}, i.e. (K=in, N=out) in {(2048,5632), (5632,2048),
+(4096,14336), (14336,4096)}, INT4 group size 64 quantized on the device by the
+reference quantizer's bit-exact kernel.  Weights ~ N(0, 0.02^2), x ~ N(0, 1),
+synthetic and seeded.
+
+value      whole-job algorithmic HBM GB/s with the weights resident in HBM:
+           bytes/step = sum over the 4 weights of K*ceil(N/2) + G*N*4 + G*N + K*4 + N*4
+           (packed nibbles, fp32 scales, u8 zeros, x read, y write), x N ranks,
+           divided by the max over ranks of the device-timed region.
+e2e        the same metric through the public host-buffer entry point
+           (MatMul.multiply_quantized on pinned numpy arrays -> kt_qmatmul_host):
+           x copied host->device and y device->host inside the timed region.
+L2         each step reads a different copy of the four weights, rotating over
+           enough copies (> 4x the 126 MB L2) that no step hits a weight in L2.
+N > 1      one process per GPU; every rank streams its own independent set of
+           weights (different layers), no collective on the data path
+           ("scaling": "weak").
+
+--impl reference times the reference algorithm on the host cores (the C
+restatement of MatMul.multiplyQuantized in oracle/, all host threads) on the
+same config and metric; the Kotlin reference cannot run on this machine.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "dequant-GEMV HBM GB/s (% of peak); decode tokens/s at batch 1-256"
+UNIT = "GB/s"
+SHAPES = [(2048, 5632), (5632, 2048), (4096, 14336), (14336, 4096)]  # (K = in, N = out)
+BITS, GROUP = 4, 64
+L2_BYTES = 126 * 1024 * 1024
+WORKLOAD = "config2-int4-ffn-gemv-m1"
+
+
+def algo_bytes(k: int, n: int, m: int = 1, bits: int = BITS, g: int = GROUP) -> int:
+    groups = (k + g - 1) // g
+    qbytes = k * ((n + 1) // 2) if bits == 4 else k * n
+    return qbytes + groups * n * 4 + (groups * n if bits == 4 else 0) + m * k * 4 + m * n * 4
+
+
+STEP_BYTES = sum(algo_bytes(k, n) for k, n in SHAPES)
+WEIGHT_BYTES = sum(algo_bytes(k, n) - 4 * (k + n) for k, n in SHAPES)
+
+
+def measured_peaks() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- CPU baseline
+
+def cpu_baseline(budget_s: float = 12.0, threads: int | None = None) -> dict:
+    """The oracle's restatement of MatMul.multiplyQuantized (m = 1 work-unit
+    schedule) on the host cores, over whole steps of the same workload."""
+    import numpy as np
+    from oracle import oracle as O
+
+    threads = threads or (os.cpu_count() or 1)
+    rng = np.random.default_rng(4321)
+    weights, xs = [], []
+    for k, n in SHAPES:
+        w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+        weights.append(O.quantize(w, BITS, GROUP))
+        xs.append(rng.standard_normal((1, k), dtype=np.float32))
+    for t, x in zip(weights, xs):  # warm-up
+        O.multiply_quantized(x, t, threads=threads)
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        for t, x in zip(weights, xs):
+            O.multiply_quantized(x, t, threads=threads)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or steps >= 200:
+            break
+    return {"value": round(STEP_BYTES * steps / el / 1e9, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{steps} full steps (4 INT4 GEMVs, m=1) in {el:.1f} s, oracle/kt_oracle.c "
+                      f"restatement of MatMul.multiplyQuantized, {threads} threads"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(4321)
+    weights, xs = [], []
+    for k, n in SHAPES:
+        w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+        weights.append(O.quantize(w, BITS, GROUP))
+        xs.append(rng.standard_normal((1, k), dtype=np.float32))
+    for _ in range(args.warmup):
+        for t, x in zip(weights, xs):
+            O.multiply_quantized(x, t, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for t, x in zip(weights, xs):
+            O.multiply_quantized(x, t, threads=threads)
+    el = time.perf_counter() - t0
+    value = STEP_BYTES * args.steps / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "shapes_k_n": SHAPES, "bits": BITS, "group_size": GROUP, "m": 1,
+                   "bytes_per_step": STEP_BYTES},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} full steps; the Kotlin reference cannot run here, so this is "
+                                   "oracle/kt_oracle.c, the C restatement of MatMul.multiplyQuantized"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU arm
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import kotensor_b200 as kt
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    copies = max(2, math.ceil(4 * L2_BYTES / WEIGHT_BYTES))
+    gen = torch.Generator(device="cuda")
+    weights = []  # [copy][shape]
+    for c in range(copies):
+        row = []
+        for si, (k, n) in enumerate(SHAPES):
+            gen.manual_seed(1000 * rank + 10 * c + si)
+            w = torch.randn((k, n), generator=gen, device="cuda", dtype=torch.float32) * 0.02
+            row.append(kt.QuantizedTensor.quantize(w, kt.Quantization(BITS, GROUP)))
+            del w
+        weights.append(row)
+    gen.manual_seed(77 + rank)
+    xs = [torch.randn((args.m, k), generator=gen, device="cuda") for k, _ in SHAPES]
+    ys = [torch.empty((args.m, n), device="cuda") for _, n in SHAPES]
+    stream = torch.cuda.current_stream()
+
+    def step(i: int, events=None):
+        row = weights[i % copies]
+        for si in range(len(SHAPES)):
+            if events is not None:
+                events[si][0].record(stream)
+            kt.MatMul.multiply_quantized(xs[si], row[si], ys[si], args.m, accumulate=False)
+            if events is not None:
+                events[si][1].record(stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    # per-launch events for the roofline (one pass over all copies, after warm-up)
+    launch_ms, launch_bytes = [], []
+    for i in range(max(copies, 8)):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in SHAPES]
+        step(args.warmup + i, evs)
+        torch.cuda.synchronize()
+        for si, (k, n) in enumerate(SHAPES):
+            launch_ms.append(evs[si][0].elapsed_time(evs[si][1]))
+            launch_bytes.append(algo_bytes(k, n, args.m))
+
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    elapsed_ms = start.elapsed_time(end)
+    t = torch.tensor([elapsed_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    step_bytes = sum(algo_bytes(k, n, args.m) for k, n in SHAPES)
+    value = world * step_bytes * args.steps / (max_ms / 1e3) / 1e9
+
+    # e2e through the host-buffer entry point (pinned host x / y)
+    xh = [torch.randn((args.m, k)).pin_memory().numpy() for k, _ in SHAPES]
+    yh = [torch.empty((args.m, n)).pin_memory().numpy() for _, n in SHAPES]
+    e2e_steps = max(1, args.steps)
+
+    def host_step(i):
+        row = weights[i % copies]
+        for si in range(len(SHAPES)):
+            kt.MatMul.multiply_quantized(xh[si], row[si], yh[si], args.m, accumulate=False)
+
+    for i in range(max(1, args.warmup)):
+        host_step(i)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        host_step(i)
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * step_bytes * e2e_steps / float(te.item()) / 1e9
+
+    peak, peak_kind = measured_peaks()
+    achieved = sum(launch_bytes) / (sum(launch_ms) / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u4", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "shapes_k_n": SHAPES, "bits": BITS, "group_size": GROUP, "m": args.m,
+                   "bytes_per_step_per_gpu": step_bytes, "parallelism": f"independent weights per rank x{world}",
+                   "l2": f"rotating {copies} weight copies ({copies * WEIGHT_BYTES / 1e6:.0f} MB > 4x L2)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": None, "kernel": "gemv_kernel<4,1,16>",
+                     "per_launch_bytes": launch_bytes[:len(SHAPES)],
+                     "per_launch_us": [round(1e3 * statistics.median(launch_ms[i::len(SHAPES)]), 2)
+                                       for i in range(len(SHAPES))]},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                "h2d_bytes_per_step": sum(args.m * k * 4 for k, _ in SHAPES),
+                "d2h_bytes_per_step": sum(args.m * n * 4 for _, n in SHAPES)},
+        "gpu_launches": len(SHAPES) * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--m", type=int, default=1, help="activation rows per GEMV (decode batch)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

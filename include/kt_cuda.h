@@ -1,0 +1,156 @@
+/*
+ * kt_cuda.h -- C ABI of the B200 (sm_100a) implementation of Kotensor's
+ * group-wise weight-only INT8/INT4 quantized matmul.
+ *
+ * Every entry point is extern "C", takes plain pointers and sizes, returns a
+ * kt_status and never lets a C++ exception cross the boundary.  The message of
+ * the last failure on the calling thread is kt_last_error().
+ *
+ * Reference interfaces (paths inside the Kotensor project, Engine/kotensor/):
+ *   Quantization(bits, groupSize)                      src/main/kotlin/QuantizedTensor.kt:10-25
+ *   QuantizedTensor(qdata, scales, zeros, shape, ...)  src/main/kotlin/QuantizedTensor.kt:36-70
+ *   QuantizedTensor.quantize(data, rows, columns, q)   src/main/kotlin/QuantizedTensor.kt:261-278
+ *   QuantizedTensor.dequantize / dequantizeRow         src/main/kotlin/QuantizedTensor.kt:188-249
+ *   MatMul.multiplyQuantized(a, W, c, m, acc, alpha)   src/main/kotlin/MatMul.kt:460-486
+ *   MatMul.multiplyByQuantizedTransposed(dy,W,dx,m,acc) src/main/kotlin/MatMul.kt:954-981
+ *   QuantizedLinear.forwardInto (+ bias)               src/main/kotlin/QuantizedLinear.kt:18-25
+ *   Tensor.matmulDequantInto(W, out, acc, scale)       src/main/kotlin/Tensor.kt:180-188
+ *
+ * Layout (identical to the reference's heap and safetensors layout,
+ * QuantizedTensor.kt:45-49, Transformer.kt:423-428):
+ *   rows = K = in-features, columns = N = out-features, groups G = ceil(K / groupSize)
+ *   qdata  INT8: int8 [K x N] row-major.
+ *          INT4: uint8 [K x ceil(N/2)] split-half packed: column c < half sits in
+ *          the low nibble of byte c, column c >= half in the high nibble of byte
+ *          c - half (half = ceil(N/2)).
+ *   scales float32 [G x N];  zeros (INT4 only) uint8 [G x N], values 0..15.
+ *   a / c fp32 row-major [m x K] / [m x N].
+ *
+ * Streams: a `stream` argument is a cudaStream_t; NULL selects the context's
+ * own stream.  Calls are stream-ordered and asynchronous unless documented
+ * otherwise.  Results are deterministic: the same inputs give the same bits on
+ * every run (fixed reduction order, no floating-point atomics).
+ */
+#ifndef KT_CUDA_H
+#define KT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t kt_status;
+enum {
+    KT_OK = 0,
+    KT_ERR_INVALID_ARGUMENT = 1, /* reference: require(...) -> IllegalArgumentException */
+    KT_ERR_NAN = 2,              /* reference: Float.roundToInt() on NaN -> IllegalArgumentException */
+    KT_ERR_CUDA = 3,             /* CUDA runtime failure -> IllegalStateException */
+    KT_ERR_OUT_OF_MEMORY = 4,
+    KT_ERR_UNSUPPORTED = 5,
+    KT_ERR_NCCL = 6
+};
+
+typedef struct kt_ctx kt_ctx;
+typedef struct kt_qweight kt_qweight;
+
+/* Read-only view of a device-resident quantized weight. */
+typedef struct {
+    int32_t bits, group_size, rows, columns, groups, bytes_per_row, stored_columns;
+    int64_t size_in_bytes;        /* QuantizedTensor.sizeInBytes, QuantizedTensor.kt:97-98 */
+    const void* qdata;            /* device pointers */
+    const float* scales;
+    const uint8_t* zeros;         /* NULL for INT8 */
+} kt_qweight_info;
+
+/* ------------------------------------------------------------ library */
+int32_t kt_version(void);
+const char* kt_last_error(void);
+/* Quantization(bits, groupSize) validation, QuantizedTensor.kt:14-17. */
+kt_status kt_check_quantization(int32_t bits, int32_t group_size);
+
+/* ------------------------------------------------------------ context (no reference counterpart:
+ * the reference's MatMul is a process-wide object with a ForkJoinPool, MatMul.kt:15-57) */
+kt_status kt_init(int32_t device, kt_ctx** out);
+kt_status kt_destroy(kt_ctx* ctx);
+kt_status kt_ctx_stream(kt_ctx* ctx, void** stream_out);
+kt_status kt_alloc(kt_ctx* ctx, size_t bytes, void** out);
+kt_status kt_free(kt_ctx* ctx, void* ptr);
+kt_status kt_memcpy_h2d(kt_ctx* ctx, void* dst_dev, const void* src_host, size_t bytes, void* stream);
+kt_status kt_memcpy_d2h(kt_ctx* ctx, void* dst_host, const void* src_dev, size_t bytes, void* stream);
+kt_status kt_stream_sync(kt_ctx* ctx, void* stream);
+
+/* ------------------------------------------------------------ quantized weights */
+
+/* QuantizedTensor(qdata, scales, zeros, shape=[rows, columns], bits, groupSize),
+ * QuantizedTensor.kt:36-70: copies host bytes in the reference layout into HBM.
+ * zeros must be NULL for INT8 and non-NULL for INT4 ("4-bit tensors need zero
+ * points").  Synchronous. */
+kt_status kt_qweight_upload(kt_ctx* ctx, int32_t bits, int32_t group_size, int32_t rows, int32_t columns,
+                            const void* qdata, const float* scales, const uint8_t* zeros, kt_qweight** out);
+
+/* Same, from buffers already on the device (copied device-to-device on `stream`). */
+kt_status kt_qweight_from_device(kt_ctx* ctx, int32_t bits, int32_t group_size, int32_t rows, int32_t columns,
+                                 const void* qdata_dev, const float* scales_dev, const uint8_t* zeros_dev,
+                                 void* stream, kt_qweight** out);
+
+/* QuantizedTensor.quantize(data, rows, columns, Quantization(bits, groupSize)),
+ * QuantizedTensor.kt:261-324, run on the GPU: data_dev is fp32 [rows x columns]
+ * row-major on the device.  Bytes, scales and zeros are bit-identical to the
+ * reference quantizer.  Synchronous on `stream` (the NaN check needs the result):
+ * returns KT_ERR_NAN, and no weight, where Kotlin's roundToInt would throw. */
+kt_status kt_quantize(kt_ctx* ctx, int32_t bits, int32_t group_size, int32_t rows, int32_t columns,
+                      const float* data_dev, void* stream, kt_qweight** out);
+
+kt_status kt_qweight_info_get(const kt_qweight* w, kt_qweight_info* out);
+
+/* Copies the weight back to host buffers in the reference layout
+ * (qdata: rows*bytes_per_row bytes, scales: groups*columns floats, zeros:
+ * groups*columns bytes or NULL for INT8).  Synchronous. */
+kt_status kt_qweight_download(const kt_qweight* w, void* qdata, float* scales, uint8_t* zeros);
+
+kt_status kt_qweight_free(kt_qweight* w);
+
+/* QuantizedTensor.dequantize(), QuantizedTensor.kt:243-249: out_dev fp32 [rows x columns]. */
+kt_status kt_dequantize(kt_ctx* ctx, const kt_qweight* w, float* out_dev, void* stream);
+
+/* QuantizedTensor.dequantizeRow(row, dest) for `count` rows gathered by index
+ * (the quantized-embedding lookup, Embedding.kt:96-101): out_dev [count x columns].
+ * Row indices out of range set KT_ERR_INVALID_ARGUMENT in *status_dev (device
+ * int32, may be NULL) and leave that output row untouched. */
+kt_status kt_dequantize_rows(kt_ctx* ctx, const kt_qweight* w, const int32_t* rows_dev, int32_t count,
+                             float* out_dev, int32_t* status_dev, void* stream);
+
+/* ------------------------------------------------------------ matmul */
+
+/* MatMul.multiplyQuantized(a, W, c, m, accumulate, alpha), MatMul.kt:460-486,
+ * followed by QuantizedLinear's `+ bias` (QuantizedLinear.kt:18-25):
+ *   c[m x N] = (accumulate ? c : 0) + alpha * a[m x K] . dequant(W) + bias
+ * bias_dev (fp32 [N]) may be NULL.  m == 0 is a no-op.  Device pointers.
+ * Tolerance against the reference fp32 result: 1e-3 relative to max|c| on the
+ * fp32-accumulate kernels (m <= 8), 2e-2 on the bf16 tensor-core kernel (m >= 9). */
+kt_status kt_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float* c_dev, int32_t m,
+                     int32_t accumulate, float alpha, const float* bias_dev, void* stream);
+
+/* Which kernel family kt_qmatmul runs for this weight and m, and so which
+ * tolerance applies: KT_PATH_GEMV (fp32-accumulate streaming kernel),
+ * KT_PATH_GENERIC (fp32-accumulate kernel for unaligned shapes),
+ * KT_PATH_TENSOR_CORE (bf16 tcgen05 kernel). */
+enum { KT_PATH_GEMV = 0, KT_PATH_GENERIC = 1, KT_PATH_TENSOR_CORE = 2 };
+kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out);
+
+/* The literal FloatArray signature: host a / c / bias, copied through the
+ * context's staging buffers on its own stream.  Synchronous. */
+kt_status kt_qmatmul_host(kt_ctx* ctx, const kt_qweight* w, const float* a_host, float* c_host, int32_t m,
+                          int32_t accumulate, float alpha, const float* bias_host);
+
+/* MatMul.multiplyByQuantizedTransposed(dy, W, dx, m, accumulate), MatMul.kt:954-981:
+ *   dx[m x K] = (accumulate ? dx : 0) + dy[m x N] . dequant(W)^T        (device pointers) */
+kt_status kt_qmatmul_t(kt_ctx* ctx, const kt_qweight* w, const float* dy_dev, float* dx_dev, int32_t m,
+                       int32_t accumulate, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KT_CUDA_H */

@@ -1,0 +1,101 @@
+"""ctypes binding of libkt_cuda.so (the C ABI declared in include/kt_cuda.h).
+
+The library is built in-tree by ``kotensor_b200.build_ext``.  Loading fails
+loudly when it is missing: there is no CPU fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libkt_cuda.so")
+
+KT_OK = 0
+KT_ERR_INVALID_ARGUMENT = 1
+KT_ERR_NAN = 2
+KT_ERR_CUDA = 3
+KT_ERR_OUT_OF_MEMORY = 4
+KT_ERR_UNSUPPORTED = 5
+KT_ERR_NCCL = 6
+
+KT_PATH_GEMV, KT_PATH_GENERIC, KT_PATH_TENSOR_CORE = 0, 1, 2
+
+
+class KtError(RuntimeError):
+    """A failure inside the CUDA library (the reference's IllegalStateException)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[kt status {status}] {message}")
+        self.status = status
+
+
+class KtInfo(ctypes.Structure):
+    _fields_ = [
+        ("bits", ctypes.c_int32), ("group_size", ctypes.c_int32), ("rows", ctypes.c_int32),
+        ("columns", ctypes.c_int32), ("groups", ctypes.c_int32), ("bytes_per_row", ctypes.c_int32),
+        ("stored_columns", ctypes.c_int32), ("size_in_bytes", ctypes.c_int64),
+        ("qdata", ctypes.c_void_p), ("scales", ctypes.c_void_p), ("zeros", ctypes.c_void_p),
+    ]
+
+
+# name -> (argtypes, restype); the single source of the Python-side signatures.
+P, I32, I64, F32, SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+PP = ctypes.POINTER(ctypes.c_void_p)
+SIGNATURES: dict[str, tuple[list, object]] = {
+    "kt_version": ([], I32),
+    "kt_last_error": ([], ctypes.c_char_p),
+    "kt_check_quantization": ([I32, I32], I32),
+    "kt_init": ([I32, PP], I32),
+    "kt_destroy": ([P], I32),
+    "kt_ctx_stream": ([P, PP], I32),
+    "kt_alloc": ([P, SZ, PP], I32),
+    "kt_free": ([P, P], I32),
+    "kt_memcpy_h2d": ([P, P, P, SZ, P], I32),
+    "kt_memcpy_d2h": ([P, P, P, SZ, P], I32),
+    "kt_stream_sync": ([P, P], I32),
+    "kt_qweight_upload": ([P, I32, I32, I32, I32, P, P, P, PP], I32),
+    "kt_qweight_from_device": ([P, I32, I32, I32, I32, P, P, P, P, PP], I32),
+    "kt_quantize": ([P, I32, I32, I32, I32, P, P, PP], I32),
+    "kt_qweight_info_get": ([P, ctypes.POINTER(KtInfo)], I32),
+    "kt_qweight_download": ([P, P, P, P], I32),
+    "kt_qweight_free": ([P], I32),
+    "kt_dequantize": ([P, P, P, P], I32),
+    "kt_dequantize_rows": ([P, P, P, I32, P, P, P], I32),
+    "kt_qmatmul": ([P, P, P, P, I32, I32, F32, P, P], I32),
+    "kt_qmatmul_host": ([P, P, P, P, I32, I32, F32, P], I32),
+    "kt_qmatmul_path": ([P, I32, ctypes.POINTER(I32)], I32),
+    "kt_qmatmul_t": ([P, P, P, P, I32, I32, P], I32),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Loads libkt_cuda.so; raises if it was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(f"{LIB_PATH} is missing: build it with `python -m kotensor_b200.build_ext`")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (argtypes, restype) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = argtypes
+                fn.restype = restype
+            _lib = lib
+    return _lib
+
+
+def check(status: int) -> None:
+    """Maps a kt_status to the reference's exception convention."""
+    if status == KT_OK:
+        return
+    msg = load().kt_last_error().decode(errors="replace")
+    if status in (KT_ERR_INVALID_ARGUMENT, KT_ERR_NAN):
+        raise ValueError(msg)  # IllegalArgumentException
+    raise KtError(status, msg)  # IllegalStateException

@@ -1,0 +1,403 @@
+// kt_api.cu -- the C ABI (include/kt_cuda.h) over the CUDA runtime: contexts,
+// device-resident quantized weights, argument checks with the reference's error
+// convention, and dispatch to the kernels.
+//
+// Argument checks follow the reference's require(...) calls
+// (Engine/kotensor/src/main/kotlin/QuantizedTensor.kt:14-17 and :63-70,
+// MatMul.kt:470-473, MatMul.kt:963-965): a failed check returns
+// KT_ERR_INVALID_ARGUMENT with the reference's message in kt_last_error(),
+// m == 0 is a no-op.  No product path falls back to the CPU: every compute call
+// launches a CUDA kernel or fails.
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "kt_internal.h"
+
+#define KT_VERSION 1
+
+namespace kt {
+namespace {
+thread_local std::string g_last_error;
+
+kt_status fail(kt_status st, const std::string& msg) {
+    g_last_error = msg;
+    return st;
+}
+
+kt_status cuda_fail(cudaError_t e, const char* what) {
+    return fail(e == cudaErrorMemoryAllocation ? KT_ERR_OUT_OF_MEMORY : KT_ERR_CUDA,
+                std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define KT_CUDA_TRY(expr, what)                       \
+    do {                                              \
+        cudaError_t e__ = (expr);                     \
+        if (e__ != cudaSuccess) return cuda_fail(e__, what); \
+    } while (0)
+
+int32_t groups_of(int32_t rows, int32_t g) { return (rows + g - 1) / g; }
+int32_t bytes_per_row_of(int32_t bits, int32_t columns) { return bits == 4 ? (columns + columns % 2) / 2 : columns; }
+
+kt_status check_quant(int32_t bits, int32_t group_size) {
+    if (bits != 4 && bits != 8) return fail(KT_ERR_INVALID_ARGUMENT, "bits must be 4 or 8, got " + std::to_string(bits));
+    if (group_size <= 0) return fail(KT_ERR_INVALID_ARGUMENT, "groupSize must be positive");
+    return KT_OK;
+}
+
+kt_status check_shape(int32_t rows, int32_t columns) {
+    if (rows <= 0 || columns <= 0)
+        return fail(KT_ERR_INVALID_ARGUMENT, "QuantizedTensor needs a 2-D shape, got [" + std::to_string(rows) + ", " +
+                                                 std::to_string(columns) + "]");
+    // Byte offsets are 64-bit everywhere; element counts of one row / one scale
+    // row must stay addressable with 32-bit column indices.
+    return KT_OK;
+}
+
+cudaStream_t pick(kt_ctx* ctx, void* stream) {
+    return stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+}
+
+// Allocates an empty device weight with the reference's size bookkeeping.
+kt_status alloc_weight(kt_ctx* ctx, int32_t bits, int32_t group_size, int32_t rows, int32_t columns,
+                       kt_qweight** out) {
+    auto* w = new (std::nothrow) kt_qweight();
+    if (!w) return fail(KT_ERR_OUT_OF_MEMORY, "host allocation failed");
+    w->ctx = ctx;
+    w->bits = bits;
+    w->group_size = group_size;
+    w->rows = rows;
+    w->columns = columns;
+    w->groups = groups_of(rows, group_size);
+    w->bytes_per_row = bytes_per_row_of(bits, columns);
+    w->stored_columns = bits == 4 ? columns + columns % 2 : columns;
+    const size_t qbytes = static_cast<size_t>(rows) * w->bytes_per_row;
+    const size_t gcols = static_cast<size_t>(w->groups) * columns;
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e == cudaSuccess) e = cudaMalloc(&w->qdata, qbytes);
+    if (e == cudaSuccess) e = cudaMalloc(&w->scales, gcols * sizeof(float));
+    if (e == cudaSuccess && bits == 4) e = cudaMalloc(&w->zeros, gcols);
+    if (e != cudaSuccess) {
+        cudaFree(w->qdata);
+        cudaFree(w->scales);
+        cudaFree(w->zeros);
+        delete w;
+        return cuda_fail(e, "cudaMalloc(quantized weight)");
+    }
+    *out = w;
+    return KT_OK;
+}
+
+void free_weight(kt_qweight* w) {
+    if (!w) return;
+    cudaSetDevice(w->ctx->device);
+    cudaFree(w->qdata);
+    cudaFree(w->scales);
+    cudaFree(w->zeros);
+    delete w;
+}
+
+kt_status grow(float** buf, size_t* cap, size_t need) {
+    if (*cap >= need) return KT_OK;
+    cudaFree(*buf);
+    *buf = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMalloc(buf, need * sizeof(float));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
+    *cap = need;
+    return KT_OK;
+}
+
+kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
+                     float alpha, const float* bias, cudaStream_t s) {
+    const QView v = view(w);
+    const MatmulArgs args{a, c, bias, m, accumulate, alpha};
+    cudaError_t e;
+    if (gemv_fast_supported(v, m)) {
+        e = launch_gemv(v, args, ctx->sm_count, s);
+    } else {
+        e = launch_matmul_generic(v, args, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "qmatmul launch");
+    return KT_OK;
+}
+
+}  // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+}  // namespace kt
+
+using namespace kt;
+
+extern "C" {
+
+int32_t kt_version(void) { return KT_VERSION; }
+
+const char* kt_last_error(void) { return g_last_error.c_str(); }
+
+kt_status kt_check_quantization(int32_t bits, int32_t group_size) { return check_quant(bits, group_size); }
+
+kt_status kt_init(int32_t device, kt_ctx** out) {
+    if (!out) return fail(KT_ERR_INVALID_ARGUMENT, "out is NULL");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= count)
+        return fail(KT_ERR_INVALID_ARGUMENT, "device " + std::to_string(device) + " out of range (" +
+                                                 std::to_string(count) + " devices)");
+    auto* ctx = new (std::nothrow) kt_ctx();
+    if (!ctx) return fail(KT_ERR_OUT_OF_MEMORY, "host allocation failed");
+    ctx->device = device;
+    e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess)
+        e = cudaDeviceGetAttribute(&ctx->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_status, sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(int32_t));
+    if (e != cudaSuccess) {
+        if (ctx->stream) cudaStreamDestroy(ctx->stream);
+        cudaFree(ctx->d_status);
+        delete ctx;
+        return cuda_fail(e, "kt_init");
+    }
+    *out = ctx;
+    return KT_OK;
+}
+
+kt_status kt_destroy(kt_ctx* ctx) {
+    if (!ctx) return KT_OK;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->h2d_a);
+    cudaFree(ctx->d2h_c);
+    cudaFree(ctx->bias_buf);
+    cudaFree(ctx->d_status);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return KT_OK;
+}
+
+kt_status kt_ctx_stream(kt_ctx* ctx, void** stream_out) {
+    if (!ctx || !stream_out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    *stream_out = ctx->stream;
+    return KT_OK;
+}
+
+kt_status kt_alloc(kt_ctx* ctx, size_t bytes, void** out) {
+    if (!ctx || !out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    KT_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    KT_CUDA_TRY(cudaMalloc(out, bytes), "cudaMalloc");
+    return KT_OK;
+}
+
+kt_status kt_free(kt_ctx* ctx, void* ptr) {
+    if (!ctx) return fail(KT_ERR_INVALID_ARGUMENT, "NULL context");
+    KT_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    KT_CUDA_TRY(cudaFree(ptr), "cudaFree");
+    return KT_OK;
+}
+
+kt_status kt_memcpy_h2d(kt_ctx* ctx, void* dst, const void* src, size_t bytes, void* stream) {
+    if (!ctx) return fail(KT_ERR_INVALID_ARGUMENT, "NULL context");
+    KT_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, pick(ctx, stream)), "cudaMemcpyAsync(H2D)");
+    return KT_OK;
+}
+
+kt_status kt_memcpy_d2h(kt_ctx* ctx, void* dst, const void* src, size_t bytes, void* stream) {
+    if (!ctx) return fail(KT_ERR_INVALID_ARGUMENT, "NULL context");
+    KT_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, pick(ctx, stream)), "cudaMemcpyAsync(D2H)");
+    return KT_OK;
+}
+
+kt_status kt_stream_sync(kt_ctx* ctx, void* stream) {
+    if (!ctx) return fail(KT_ERR_INVALID_ARGUMENT, "NULL context");
+    KT_CUDA_TRY(cudaStreamSynchronize(pick(ctx, stream)), "cudaStreamSynchronize");
+    return KT_OK;
+}
+
+kt_status kt_qweight_upload(kt_ctx* ctx, int32_t bits, int32_t group_size, int32_t rows, int32_t columns,
+                            const void* qdata, const float* scales, const uint8_t* zeros, kt_qweight** out) {
+    if (!ctx || !out || !qdata || !scales) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    kt_status st = check_quant(bits, group_size);
+    if (st != KT_OK) return st;
+    if ((st = check_shape(rows, columns)) != KT_OK) return st;
+    if (bits == 4 && !zeros) return fail(KT_ERR_INVALID_ARGUMENT, "4-bit tensors need zero points");
+    if (bits == 8 && zeros) return fail(KT_ERR_INVALID_ARGUMENT, "8-bit tensors have no zero points");
+    kt_qweight* w = nullptr;
+    if ((st = alloc_weight(ctx, bits, group_size, rows, columns, &w)) != KT_OK) return st;
+    const size_t qbytes = static_cast<size_t>(rows) * w->bytes_per_row;
+    const size_t gcols = static_cast<size_t>(w->groups) * columns;
+    cudaError_t e = cudaMemcpy(w->qdata, qdata, qbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(w->scales, scales, gcols * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && bits == 4) e = cudaMemcpy(w->zeros, zeros, gcols, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        free_weight(w);
+        return cuda_fail(e, "kt_qweight_upload");
+    }
+    *out = w;
+    return KT_OK;
+}
+
+kt_status kt_qweight_from_device(kt_ctx* ctx, int32_t bits, int32_t group_size, int32_t rows, int32_t columns,
+                                 const void* qdata, const float* scales, const uint8_t* zeros, void* stream,
+                                 kt_qweight** out) {
+    if (!ctx || !out || !qdata || !scales) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    kt_status st = check_quant(bits, group_size);
+    if (st != KT_OK) return st;
+    if ((st = check_shape(rows, columns)) != KT_OK) return st;
+    if (bits == 4 && !zeros) return fail(KT_ERR_INVALID_ARGUMENT, "4-bit tensors need zero points");
+    kt_qweight* w = nullptr;
+    if ((st = alloc_weight(ctx, bits, group_size, rows, columns, &w)) != KT_OK) return st;
+    cudaStream_t s = pick(ctx, stream);
+    const size_t qbytes = static_cast<size_t>(rows) * w->bytes_per_row;
+    const size_t gcols = static_cast<size_t>(w->groups) * columns;
+    cudaError_t e = cudaMemcpyAsync(w->qdata, qdata, qbytes, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(w->scales, scales, gcols * sizeof(float), cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess && bits == 4) e = cudaMemcpyAsync(w->zeros, zeros, gcols, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) {
+        free_weight(w);
+        return cuda_fail(e, "kt_qweight_from_device");
+    }
+    *out = w;
+    return KT_OK;
+}
+
+kt_status kt_quantize(kt_ctx* ctx, int32_t bits, int32_t group_size, int32_t rows, int32_t columns,
+                      const float* data, void* stream, kt_qweight** out) {
+    if (!ctx || !out || !data) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    kt_status st = check_quant(bits, group_size);
+    if (st != KT_OK) return st;
+    if ((st = check_shape(rows, columns)) != KT_OK) return st;
+    kt_qweight* w = nullptr;
+    if ((st = alloc_weight(ctx, bits, group_size, rows, columns, &w)) != KT_OK) return st;
+    cudaStream_t s = pick(ctx, stream);
+    int32_t status = 0;
+    cudaError_t e = cudaMemsetAsync(ctx->d_status, 0, sizeof(int32_t), s);
+    if (e == cudaSuccess)
+        e = launch_quantize(data, rows, columns, bits, group_size, w->qdata, w->scales, w->zeros, ctx->d_status, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&status, ctx->d_status, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        free_weight(w);
+        return cuda_fail(e, "kt_quantize");
+    }
+    if (status != 0) {
+        free_weight(w);
+        return fail(KT_ERR_NAN, "Cannot round NaN value.");
+    }
+    *out = w;
+    return KT_OK;
+}
+
+kt_status kt_qweight_info_get(const kt_qweight* w, kt_qweight_info* out) {
+    if (!w || !out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    out->bits = w->bits;
+    out->group_size = w->group_size;
+    out->rows = w->rows;
+    out->columns = w->columns;
+    out->groups = w->groups;
+    out->bytes_per_row = w->bytes_per_row;
+    out->stored_columns = w->stored_columns;
+    out->size_in_bytes = static_cast<int64_t>(w->rows) * w->bytes_per_row +
+                         static_cast<int64_t>(w->groups) * w->columns * 4 +
+                         (w->bits == 4 ? static_cast<int64_t>(w->groups) * w->columns : 0);
+    out->qdata = w->qdata;
+    out->scales = w->scales;
+    out->zeros = w->zeros;
+    return KT_OK;
+}
+
+kt_status kt_qweight_download(const kt_qweight* w, void* qdata, float* scales, uint8_t* zeros) {
+    if (!w || !qdata || !scales) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (w->bits == 4 && !zeros) return fail(KT_ERR_INVALID_ARGUMENT, "4-bit tensors need a zeros buffer");
+    KT_CUDA_TRY(cudaSetDevice(w->ctx->device), "cudaSetDevice");
+    const size_t qbytes = static_cast<size_t>(w->rows) * w->bytes_per_row;
+    const size_t gcols = static_cast<size_t>(w->groups) * w->columns;
+    KT_CUDA_TRY(cudaMemcpy(qdata, w->qdata, qbytes, cudaMemcpyDeviceToHost), "download qdata");
+    KT_CUDA_TRY(cudaMemcpy(scales, w->scales, gcols * sizeof(float), cudaMemcpyDeviceToHost), "download scales");
+    if (w->bits == 4) KT_CUDA_TRY(cudaMemcpy(zeros, w->zeros, gcols, cudaMemcpyDeviceToHost), "download zeros");
+    return KT_OK;
+}
+
+kt_status kt_qweight_free(kt_qweight* w) {
+    free_weight(w);
+    return KT_OK;
+}
+
+kt_status kt_dequantize(kt_ctx* ctx, const kt_qweight* w, float* out, void* stream) {
+    if (!ctx || !w || !out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    KT_CUDA_TRY(launch_dequantize(view(w), out, pick(ctx, stream)), "dequantize launch");
+    return KT_OK;
+}
+
+kt_status kt_dequantize_rows(kt_ctx* ctx, const kt_qweight* w, const int32_t* rows, int32_t count, float* out,
+                             int32_t* status, void* stream) {
+    if (!ctx || !w) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (count < 0) return fail(KT_ERR_INVALID_ARGUMENT, "negative row count " + std::to_string(count));
+    if (count == 0) return KT_OK;
+    if (!rows || !out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    KT_CUDA_TRY(launch_dequantize_rows(view(w), rows, count, out, status, pick(ctx, stream)), "dequantize_rows launch");
+    return KT_OK;
+}
+
+kt_status kt_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
+                     float alpha, const float* bias, void* stream) {
+    if (!ctx || !w) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
+    if (m == 0) return KT_OK;
+    if (!a || !c) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    return run_matmul(ctx, w, a, c, m, accumulate, alpha, bias, pick(ctx, stream));
+}
+
+kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out) {
+    if (!w || !path_out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
+    *path_out = gemv_fast_supported(view(w), m) ? KT_PATH_GEMV : KT_PATH_GENERIC;
+    return KT_OK;
+}
+
+kt_status kt_qmatmul_host(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
+                          float alpha, const float* bias) {
+    if (!ctx || !w) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
+    if (m == 0) return KT_OK;
+    if (!a || !c) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    std::lock_guard<std::mutex> lock(ctx->host_mutex);
+    KT_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const size_t an = static_cast<size_t>(m) * w->rows, cn = static_cast<size_t>(m) * w->columns;
+    kt_status st;
+    if ((st = grow(&ctx->h2d_a, &ctx->a_cap, an)) != KT_OK) return st;
+    if ((st = grow(&ctx->d2h_c, &ctx->c_cap, cn)) != KT_OK) return st;
+    if (bias && (st = grow(&ctx->bias_buf, &ctx->bias_cap, w->columns)) != KT_OK) return st;
+    cudaStream_t s = ctx->stream;
+    KT_CUDA_TRY(cudaMemcpyAsync(ctx->h2d_a, a, an * sizeof(float), cudaMemcpyHostToDevice, s), "H2D a");
+    if (accumulate) KT_CUDA_TRY(cudaMemcpyAsync(ctx->d2h_c, c, cn * sizeof(float), cudaMemcpyHostToDevice, s), "H2D c");
+    if (bias)
+        KT_CUDA_TRY(cudaMemcpyAsync(ctx->bias_buf, bias, w->columns * sizeof(float), cudaMemcpyHostToDevice, s),
+                    "H2D bias");
+    if ((st = run_matmul(ctx, w, ctx->h2d_a, ctx->d2h_c, m, accumulate, alpha, bias ? ctx->bias_buf : nullptr, s)) !=
+        KT_OK)
+        return st;
+    KT_CUDA_TRY(cudaMemcpyAsync(c, ctx->d2h_c, cn * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H c");
+    KT_CUDA_TRY(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    return KT_OK;
+}
+
+kt_status kt_qmatmul_t(kt_ctx* ctx, const kt_qweight* w, const float* dy, float* dx, int32_t m, int32_t accumulate,
+                       void* stream) {
+    if (!ctx || !w) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
+    if (m == 0) return KT_OK;
+    if (!dy || !dx) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    KT_CUDA_TRY(launch_matmul_t(view(w), dy, dx, m, accumulate, pick(ctx, stream)), "qmatmul_t launch");
+    return KT_OK;
+}
+
+}  // extern "C"

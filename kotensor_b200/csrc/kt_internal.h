@@ -1,0 +1,80 @@
+// kt_internal.h -- shared host-side declarations of the B200 quantized-matmul
+// library: the weight and context objects behind the C ABI (include/kt_cuda.h)
+// and the launchers each kernel translation unit exports.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "../../include/kt_cuda.h"
+
+struct kt_ctx {
+    int device = 0;
+    int sm_count = 0;
+    int max_smem_optin = 0;
+    cudaStream_t stream = nullptr;  // the context's own non-blocking stream
+    int32_t* d_status = nullptr;    // device status word for kernels that detect NaN / bad input
+    std::mutex host_mutex;          // serialises the host-buffer entry points
+    // staging for kt_qmatmul_host (grown on demand, owned by the context)
+    float* h2d_a = nullptr;
+    float* d2h_c = nullptr;
+    float* bias_buf = nullptr;
+    size_t a_cap = 0, c_cap = 0, bias_cap = 0;
+};
+
+struct kt_qweight {
+    kt_ctx* ctx = nullptr;
+    int32_t bits = 0, group_size = 0, rows = 0, columns = 0;
+    int32_t groups = 0, bytes_per_row = 0, stored_columns = 0;
+    uint8_t* qdata = nullptr;  // device
+    float* scales = nullptr;   // device
+    uint8_t* zeros = nullptr;  // device, INT4 only
+};
+
+namespace kt {
+
+// Thread-local last-error message (kt_last_error()).
+void set_error(const std::string& msg);
+
+// Shape of one quantized matrix as the kernels see it.
+struct QView {
+    const uint8_t* q;
+    const float* scales;
+    const uint8_t* zeros;
+    int32_t bits, group_size, rows, columns, groups, bytes_per_row;
+};
+
+inline QView view(const kt_qweight* w) {
+    return QView{w->qdata, w->scales, w->zeros, w->bits, w->group_size, w->rows, w->columns, w->groups,
+                 w->bytes_per_row};
+}
+
+// ---- kt_quantize.cu
+cudaError_t launch_quantize(const float* data, int32_t rows, int32_t columns, int32_t bits, int32_t group_size,
+                            uint8_t* qdata, float* scales, uint8_t* zeros, int32_t* d_status, cudaStream_t s);
+cudaError_t launch_dequantize(const QView& w, float* out, cudaStream_t s);
+cudaError_t launch_dequantize_rows(const QView& w, const int32_t* rows, int32_t count, float* out,
+                                   int32_t* d_status, cudaStream_t s);
+
+// ---- kt_gemv.cu  (fp32-accumulate CUDA-core kernels; small m)
+struct MatmulArgs {
+    const float* a;
+    float* c;
+    const float* bias;
+    int32_t m;
+    int32_t accumulate;
+    float alpha;
+};
+// Largest m the fp32-accumulate streaming kernel takes.
+constexpr int kGemvMaxM = 8;
+bool gemv_fast_supported(const QView& w, int32_t m);
+cudaError_t launch_gemv(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s);
+cudaError_t launch_matmul_generic(const QView& w, const MatmulArgs& args, cudaStream_t s);
+
+// ---- kt_backward.cu
+cudaError_t launch_matmul_t(const QView& w, const float* dy, float* dx, int32_t m, int32_t accumulate,
+                            cudaStream_t s);
+
+}  // namespace kt

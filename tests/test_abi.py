@@ -1,0 +1,76 @@
+"""CPU checks of the C ABI: libkt_cuda.so loads, exports every function that
+include/kt_cuda.h declares, the Python signatures cover the header, and the
+host-side argument checks behave like the reference's require(...) calls.
+No compute call is made here (no GPU)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    names = set()
+    for fname in os.listdir(os.path.join(ROOT, "include")):
+        if not fname.endswith(".h"):
+            continue
+        text = open(os.path.join(ROOT, "include", fname)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names |= set(re.findall(r"\b(kt_[a-z0-9_]+)\s*\(", text))
+    return names
+
+
+def test_library_exports_every_declared_symbol(kt):
+    lib = kt.load_library()
+    declared = header_functions()
+    assert {"kt_init", "kt_quantize", "kt_qmatmul", "kt_qmatmul_t", "kt_qweight_upload"} <= declared
+    missing = [n for n in sorted(declared) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_signatures_cover_the_header(kt):
+    from kotensor_b200 import _lib
+    declared = header_functions()
+    assert declared <= set(_lib.SIGNATURES), sorted(declared - set(_lib.SIGNATURES))
+
+
+def test_version_and_quantization_checks(kt):
+    lib = kt.load_library()
+    assert lib.kt_version() >= 1
+    assert lib.kt_check_quantization(8, 64) == 0
+    assert lib.kt_check_quantization(4, 1) == 0
+    assert lib.kt_check_quantization(3, 64) == 1
+    assert b"bits must be 4 or 8" in lib.kt_last_error()
+    assert lib.kt_check_quantization(4, 0) == 1
+    assert b"groupSize must be positive" in lib.kt_last_error()
+
+
+def test_python_quantization_mirror(kt):
+    """Quantization(3) is rejected (QuantizationTest.kt:73); INT8/INT4 constants exist."""
+    with pytest.raises(ValueError):
+        kt.Quantization(3)
+    with pytest.raises(ValueError):
+        kt.Quantization(4, 0)
+    assert (kt.Quantization.INT8.bits, kt.Quantization.INT8.group_size) == (8, 64)
+    assert (kt.Quantization.INT4.bits, kt.Quantization.INT4.group_size) == (4, 64)
+    assert repr(kt.Quantization(4, 32)) == "int4/g32"
+
+
+def test_null_arguments_are_rejected_without_a_device(kt):
+    lib = kt.load_library()
+    assert lib.kt_qmatmul(None, None, None, None, 1, 0, ctypes.c_float(1.0), None, None) == 1
+    assert lib.kt_quantize(None, 8, 64, 4, 4, None, None, None) == 1
+    out = ctypes.c_void_p()
+    assert lib.kt_init(-1, ctypes.byref(out)) != 0
+
+
+def test_product_package_does_not_import_the_oracle():
+    """The oracle is test infrastructure: nothing under kotensor_b200/ may import it."""
+    pkg = os.path.join(ROOT, "kotensor_b200")
+    for dirpath, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith((".py", ".cu", ".h", ".cuh", ".cpp")):
+                text = open(os.path.join(dirpath, f), errors="replace").read()
+                assert "oracle" not in re.sub(r"#.*|//.*", "", text).lower().replace("oracle_", ""), f

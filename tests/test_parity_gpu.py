@@ -1,0 +1,290 @@
+"""GPU parity tests: every CUDA entry point of libkt_cuda.so against the CPU
+oracle (oracle/kt_oracle.c) and the committed golden fixtures.
+
+Bars (from the reference's north star):
+  * packed bytes, scales and zeros: bit-exact;
+  * dequantize: bit-exact (one fp32 multiply, as QuantizedTensor.kt:201/210);
+  * matmul on the fp32-accumulate kernels (m <= 8 and the generic kernel):
+    max|y - y_ref| <= 1e-3 * max|y_ref|;
+  * matmul on the bf16 tensor-core kernel (m >= 9, aligned shapes): <= 2e-2 * max|y_ref|;
+  * results are deterministic (identical bits on repeated calls).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+TOL_FP32 = 1e-3
+TOL_BF16 = 2e-2
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def rel_err(y, ref):
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def tol_for(qt, m):
+    from kotensor_b200 import _lib
+    return TOL_BF16 if qt.matmul_path(m) == _lib.KT_PATH_TENSOR_CORE else TOL_FP32
+
+
+def qname_parts(qname):
+    bits = int(qname[3]) if qname[4] == "g" else int(qname[3:5])
+    return bits, int(qname.split("g", 1)[1])
+
+
+def golden_cases(golden):
+    for key in sorted(golden):
+        if key.endswith("/qdata"):
+            base = key[: -len("/qdata")]
+            shape_key, qname = base.rsplit("/", 1)
+            bits, g = qname_parts(qname)
+            yield base, shape_key, bits, g
+
+
+# ----------------------------------------------------------------- quantizer
+
+def test_quantize_matches_golden_bit_for_bit(kt, golden):
+    n = 0
+    for base, shape_key, bits, g in golden_cases(golden):
+        w = golden[f"{shape_key}/w"]
+        qt = kt.QuantizedTensor.quantize(dev(w), kt.Quantization(bits, g))
+        q, s, z = qt.download()
+        assert np.array_equal(q, golden[f"{base}/qdata"]), base
+        assert np.array_equal(s.view(np.uint32), golden[f"{base}/scales"].view(np.uint32)), base
+        if bits == 4:
+            assert np.array_equal(z, golden[f"{base}/zeros"]), base
+        n += 1
+    assert n >= 30
+
+
+@pytest.mark.parametrize("shape", [(2048, 2048), (256, 1537), (1000, 577), (4096, 1024), (3, 5), (130, 9001)])
+@pytest.mark.parametrize("bits,g", [(8, 64), (4, 64), (4, 32), (8, 1000), (4, 1)])
+def test_quantize_matches_oracle_bit_for_bit(kt, oracle, shape, bits, g):
+    rng = np.random.default_rng(hash((shape, bits, g)) % 2**32)
+    w = (rng.standard_normal(shape, dtype=np.float32) * 0.02).astype(np.float32)
+    ref = oracle.quantize(w, bits, g)
+    qt = kt.QuantizedTensor.quantize(dev(w), kt.Quantization(bits, g))
+    q, s, z = qt.download()
+    assert (qt.rows, qt.columns, qt.groups, qt.bytes_per_row, qt.size_in_bytes) == (
+        ref.rows, ref.columns, ref.groups, ref.bytes_per_row, ref.size_in_bytes)
+    assert np.array_equal(q, ref.qdata)
+    assert np.array_equal(s.view(np.uint32), ref.scales.view(np.uint32))
+    if bits == 4:
+        assert np.array_equal(z, ref.zeros)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_quantize_reports_nan_like_the_reference(kt, bits):
+    for bad in (np.nan, np.inf, -np.inf):
+        w = np.zeros((8, 40), np.float32)
+        w[5, 33] = bad
+        with pytest.raises(ValueError, match="NaN"):
+            kt.QuantizedTensor.quantize(dev(w), kt.Quantization(bits, 4))
+    # the context stays usable after the error
+    ok = kt.QuantizedTensor.quantize(dev(np.ones((8, 40), np.float32)), kt.Quantization(bits, 4))
+    assert ok.rows == 8
+
+
+def test_quantize_rejects_bad_arguments(kt):
+    with pytest.raises(ValueError):
+        kt.QuantizedTensor.quantize(dev(np.zeros((4, 4), np.float32)), kt.Quantization(8), rows=4, columns=5)
+    with pytest.raises(ValueError):
+        kt.QuantizedTensor.from_arrays(np.zeros(16, np.uint8), np.zeros(4, np.float32), None, (4, 4), 4, 64)
+    with pytest.raises(ValueError):
+        kt.QuantizedTensor.from_arrays(np.zeros(15, np.uint8), np.zeros(4, np.float32), None, (4, 4), 8, 64)
+
+
+def test_upload_download_round_trip(kt, oracle):
+    rng = np.random.default_rng(5)
+    w = (rng.random((300, 101), dtype=np.float32) - 0.5).astype(np.float32)
+    for bits, g in [(4, 16), (8, 64)]:
+        ref = oracle.quantize(w, bits, g)
+        qt = kt.QuantizedTensor.from_arrays(ref.qdata, ref.scales, ref.zeros, (300, 101), bits, g)
+        q, s, z = qt.download()
+        assert np.array_equal(q, ref.qdata) and np.array_equal(s, ref.scales)
+        if bits == 4:
+            assert np.array_equal(z, ref.zeros)
+        assert qt.raw_value(7, 100) == ref.raw_value(7, 100)
+        assert qt.value(7, 100) == ref.value(7, 100)
+
+
+# ----------------------------------------------------------------- dequantize
+
+@pytest.mark.parametrize("bits,g", [(8, 64), (4, 64), (4, 32), (4, 5)])
+def test_dequantize_bit_exact(kt, oracle, bits, g):
+    rng = np.random.default_rng(6)
+    w = (rng.random((257, 131), dtype=np.float32) - 0.5).astype(np.float32)
+    ref = oracle.quantize(w, bits, g)
+    qt = kt.QuantizedTensor.from_arrays(ref.qdata, ref.scales, ref.zeros, (257, 131), bits, g)
+    got = qt.dequantize().cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.dequantize().view(np.uint32))
+    rows = torch.tensor([0, 256, 64, 3, 3], dtype=torch.int32)
+    got_rows = qt.dequantize_rows(rows).cpu().numpy()
+    for i, r in enumerate(rows.tolist()):
+        assert np.array_equal(got_rows[i].view(np.uint32), ref.dequantize_row(r).view(np.uint32))
+    with pytest.raises(ValueError):
+        qt.dequantize_rows(torch.tensor([257], dtype=torch.int32))
+
+
+# ----------------------------------------------------------------- matmul
+
+def run_matmul(kt, qt, a, c0=None, accumulate=False, alpha=1.0, bias=None):
+    m = a.shape[0]
+    c = dev(c0.copy()) if c0 is not None else torch.zeros((m, qt.columns), device="cuda")
+    kt.MatMul.multiply_quantized(dev(a), qt, c, m, accumulate=accumulate, alpha=alpha,
+                                 bias=dev(bias) if bias is not None else None)
+    return c.cpu().numpy()
+
+
+def test_matmul_matches_golden(kt, golden):
+    for base, shape_key, bits, g in golden_cases(golden):
+        if f"{base}/y" not in golden:
+            continue
+        a = golden[f"{shape_key}/a"]
+        m, k = a.shape
+        n = golden[f"{base}/y"].shape[1]
+        z = golden.get(f"{base}/zeros")
+        qt = kt.QuantizedTensor.from_arrays(golden[f"{base}/qdata"], golden[f"{base}/scales"], z, (k, n), bits, g)
+        tol = tol_for(qt, m)
+        y = run_matmul(kt, qt, a)
+        assert rel_err(y, golden[f"{base}/y"]) <= tol, base
+        if f"{base}/y_acc" in golden:
+            y2 = run_matmul(kt, qt, a, c0=np.ones((m, n), np.float32), accumulate=True, alpha=0.5)
+            assert rel_err(y2, golden[f"{base}/y_acc"]) <= tol, base
+
+
+SHAPES = [(2048, 2048), (4096, 1024), (2048, 5632), (5632, 2048), (768, 32000), (896, 4864), (4864, 896),
+          (896, 128), (1024, 128), (64, 64), (256, 1537), (130, 9001), (300, 2100), (200, 33), (2, 17), (96, 8200)]
+
+
+@pytest.mark.parametrize("k,n", SHAPES)
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 8])
+def test_matmul_matches_oracle(kt, oracle, k, n, bits, m):
+    rng = np.random.default_rng(hash((k, n, bits, m)) % 2**32)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    ref_t = oracle.quantize(w, bits, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), bits, 64)
+    ref = oracle.multiply_quantized(a, ref_t, threads=8)
+    y = run_matmul(kt, qt, a)
+    assert rel_err(y, ref) <= tol_for(qt, m)
+    c0 = rng.standard_normal((m, n), dtype=np.float32)
+    y2 = run_matmul(kt, qt, a, c0=c0, accumulate=True, alpha=-0.5)
+    ref2 = oracle.multiply_quantized(a, ref_t, c=c0, accumulate=True, alpha=-0.5, threads=8)
+    assert rel_err(y2, ref2) <= tol_for(qt, m)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_matmul_is_deterministic(kt, oracle, bits):
+    rng = np.random.default_rng(11)
+    k, n = 4096, 4096
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    qt = kt.QuantizedTensor.quantize(dev(w), kt.Quantization(bits))
+    for m in (1, 3, 8):
+        a = dev(rng.standard_normal((m, k), dtype=np.float32))
+        outs = []
+        for _ in range(3):
+            c = torch.zeros((m, n), device="cuda")
+            kt.MatMul.multiply_quantized(a, qt, c, m, accumulate=False)
+            outs.append(c.cpu().numpy().view(np.uint32))
+        assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+
+
+def test_full_size_int4_ffn_shape_against_oracle(kt, oracle):
+    """BASELINE config 2's largest weight (K=4096, N=14336, INT4 g64) at m=1."""
+    rng = np.random.default_rng(1234)
+    k, n = 4096, 14336
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    a = rng.standard_normal((1, k), dtype=np.float32)
+    qt = kt.QuantizedTensor.quantize(dev(w), kt.Quantization(4))
+    ref_t = oracle.quantize(w, 4, 64)
+    q, s, z = qt.download()
+    assert np.array_equal(q, ref_t.qdata) and np.array_equal(s, ref_t.scales) and np.array_equal(z, ref_t.zeros)
+    ref = oracle.multiply_quantized(a, ref_t, threads=8)
+    y = run_matmul(kt, qt, a)
+    assert rel_err(y, ref) <= TOL_FP32
+    # linearity: y(a1 + a2) == y(a1) + y(a2) within the same tolerance
+    a2 = rng.standard_normal((1, k), dtype=np.float32)
+    y12 = run_matmul(kt, qt, (a + a2).astype(np.float32))
+    assert rel_err(y12, run_matmul(kt, qt, a) + run_matmul(kt, qt, a2)) <= 2 * TOL_FP32
+
+
+def test_bias_and_quantized_linear(kt, oracle):
+    rng = np.random.default_rng(12)
+    k, n, m = 896, 896, 3
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    bias = rng.standard_normal(n, dtype=np.float32)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    layer = kt.QuantizedLinear.from_linear(dev(w), dev(bias), kt.Quantization.INT4)
+    ref_t = oracle.quantize(w, 4, 64)
+    ref = oracle.multiply_quantized(x, ref_t) + bias[None, :]
+    y = layer.forward(dev(x)).cpu().numpy()
+    assert rel_err(y, ref) <= TOL_FP32
+    out = torch.empty((m, n), device="cuda")
+    layer.forward_into(dev(x), out)
+    assert np.array_equal(out.cpu().numpy(), y)
+    assert layer.size_in_bytes == ref_t.size_in_bytes + n * 4
+
+
+def test_host_entry_point(kt, oracle):
+    rng = np.random.default_rng(13)
+    k, n = 1024, 2048
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 8, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, None, (k, n), 8, 64)
+    a = rng.standard_normal((2, k), dtype=np.float32)
+    c = np.ones((2, n), np.float32)
+    kt.MatMul.multiply_quantized(a, qt, c, 2, accumulate=True, alpha=2.0)
+    ref = oracle.multiply_quantized(a, ref_t, c=np.ones((2, n), np.float32), accumulate=True, alpha=2.0)
+    assert rel_err(c, ref) <= TOL_FP32
+
+
+def test_zero_rows_is_a_noop_and_shapes_are_checked(kt):
+    qt = kt.QuantizedTensor.quantize(dev(np.ones((64, 64), np.float32)), kt.Quantization.INT8)
+    c = torch.full((1, 64), 3.0, device="cuda")
+    kt.MatMul.multiply_quantized(torch.zeros((0, 64), device="cuda"), qt, c, 0)
+    assert float(c[0, 0]) == 3.0
+    with pytest.raises(ValueError):
+        kt.MatMul.multiply_quantized(torch.zeros((1, 63), device="cuda"), qt, c, 1)
+    with pytest.raises(ValueError):
+        kt.MatMul.multiply_quantized(torch.zeros((1, 64), device="cuda"), qt, c, -1)
+
+
+# ----------------------------------------------------------------- backward
+
+def test_transposed_matches_golden(kt, golden):
+    for base, shape_key, bits, g in golden_cases(golden):
+        if f"{base}/dx" not in golden:
+            continue
+        dy = golden[f"{shape_key}/dy"]
+        m, n = dy.shape
+        k = golden[f"{shape_key}/a"].shape[1]
+        qt = kt.QuantizedTensor.from_arrays(golden[f"{base}/qdata"], golden[f"{base}/scales"],
+                                            golden.get(f"{base}/zeros"), (k, n), bits, g)
+        dx = torch.zeros((m, k), device="cuda")
+        kt.MatMul.multiply_by_quantized_transposed(dev(dy), qt, dx, m, accumulate=False)
+        assert rel_err(dx.cpu().numpy(), golden[f"{base}/dx"]) <= TOL_FP32, base
+
+
+@pytest.mark.parametrize("k,n,m", [(4096, 1024, 1), (2048, 5632, 4), (896, 4864, 9), (300, 2101, 2)])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_transposed_matches_oracle(kt, oracle, k, n, m, bits):
+    rng = np.random.default_rng(14)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, bits, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), bits, 64)
+    dy = rng.standard_normal((m, n), dtype=np.float32)
+    dx0 = rng.standard_normal((m, k), dtype=np.float32)
+    dx = dev(dx0.copy())
+    kt.MatMul.multiply_by_quantized_transposed(dev(dy), qt, dx, m, accumulate=True)
+    ref = oracle.multiply_by_quantized_transposed(dy, ref_t, dx=dx0, accumulate=True, threads=8)
+    assert rel_err(dx.cpu().numpy(), ref) <= TOL_FP32
