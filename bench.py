@@ -223,30 +223,27 @@ def run_ours(args) -> None:
     gen.manual_seed(77 + rank)
     xs = [torch.randn((args.m, k), generator=gen, device="cuda") for k, _ in SHAPES]
     ys = [torch.empty((args.m, n), device="cuda") for _, n in SHAPES]
-    stream = torch.cuda.current_stream()
 
-    def step(i: int, events=None):
-        row = weights[i % copies]
+    def launch_step(row) -> None:
         for si in range(len(SHAPES)):
-            if events is not None:
-                events[si][0].record(stream)
             kt.MatMul.multiply_quantized(xs[si], row[si], ys[si], args.m, accumulate=False)
-            if events is not None:
-                events[si][1].record(stream)
 
+    # warm-up outside capture (module load, attribute set-up), then one CUDA graph
+    # per weight copy holding that copy's 4 GEMV launches: the timed loop
+    # replays them so host launch overhead stays out of the device timing.
     for i in range(args.warmup):
-        step(i)
+        launch_step(weights[i % copies])
     torch.cuda.synchronize()
-
-    # per-launch events for the roofline (one pass over all copies, after warm-up)
-    launch_ms, launch_bytes = [], []
-    for i in range(max(copies, 8)):
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in SHAPES]
-        step(args.warmup + i, evs)
-        torch.cuda.synchronize()
-        for si, (k, n) in enumerate(SHAPES):
-            launch_ms.append(evs[si][0].elapsed_time(evs[si][1]))
-            launch_bytes.append(algo_bytes(k, n, args.m))
+    graphs = []
+    for c in range(copies):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            launch_step(weights[c])
+        graphs.append(g)
+    for i in range(args.warmup):
+        graphs[i % copies].replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
 
     sampler = ClockSampler(local)
     barrier()
@@ -258,7 +255,7 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     start.record(stream)
     for i in range(args.steps):
-        step(i)
+        graphs[i % copies].replay()
     end.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -270,6 +267,11 @@ def run_ours(args) -> None:
     max_ms = float(t.item())
     step_bytes = sum(algo_bytes(k, n, args.m) for k, n in SHAPES)
     value = world * step_bytes * args.steps / (max_ms / 1e3) / 1e9
+    # roofline: every launch of the step is the same GEMV kernel; its average
+    # launch duration is this rank's step time / 4 launches (events on the
+    # launching stream, gaps between graph nodes included).
+    launch_us = elapsed_ms * 1e3 / (args.steps * len(SHAPES))
+    achieved = step_bytes / (elapsed_ms / 1e3 / args.steps) / 1e9
 
     # e2e through the host-buffer entry point (pinned host x / y)
     xh = [torch.randn((args.m, k)).pin_memory().numpy() for k, _ in SHAPES]
@@ -283,6 +285,7 @@ def run_ours(args) -> None:
 
     for i in range(max(1, args.warmup)):
         host_step(i)
+    torch.cuda.synchronize()
     barrier()
     t0 = time.perf_counter()
     for i in range(e2e_steps):
@@ -294,7 +297,6 @@ def run_ours(args) -> None:
     e2e_value = world * step_bytes * e2e_steps / float(te.item()) / 1e9
 
     peak, peak_kind = measured_peaks()
-    achieved = sum(launch_bytes) / (sum(launch_ms) / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 5), "higher_is_better": True,
@@ -305,9 +307,7 @@ def run_ours(args) -> None:
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": None, "kernel": "gemv_kernel<4,1,16>",
-                     "per_launch_bytes": launch_bytes[:len(SHAPES)],
-                     "per_launch_us": [round(1e3 * statistics.median(launch_ms[i::len(SHAPES)]), 2)
-                                       for i in range(len(SHAPES))]},
+                     "bytes_per_launch_avg": step_bytes // len(SHAPES), "launch_us_avg": round(launch_us, 3)},
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                 "h2d_bytes_per_step": sum(args.m * k * 4 for k, _ in SHAPES),
                 "d2h_bytes_per_step": sum(args.m * n * 4 for _, n in SHAPES)},

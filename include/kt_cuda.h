@@ -26,9 +26,9 @@
  *   scales float32 [G x N];  zeros (INT4 only) uint8 [G x N], values 0..15.
  *   a / c fp32 row-major [m x K] / [m x N].
  *
- * Streams: a `stream` argument is a cudaStream_t; NULL selects the context's
- * own stream.  Calls are stream-ordered and asynchronous unless documented
- * otherwise.  Results are deterministic: the same inputs give the same bits on
+ * Streams: a `stream` argument is a cudaStream_t; NULL is CUDA's default
+ * stream (kt_ctx_stream() returns the context's own non-blocking stream).
+ * Calls are stream-ordered and asynchronous unless documented otherwise.  Results are deterministic: the same inputs give the same bits on
  * every run (fixed reduction order, no floating-point atomics).
  */
 #ifndef KT_CUDA_H

@@ -55,8 +55,11 @@ kt_status check_shape(int32_t rows, int32_t columns) {
     return KT_OK;
 }
 
+// A NULL stream is CUDA's default stream, as everywhere in the CUDA runtime;
+// the context's own stream is reachable through kt_ctx_stream().
 cudaStream_t pick(kt_ctx* ctx, void* stream) {
-    return stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    (void)ctx;
+    return static_cast<cudaStream_t>(stream);
 }
 
 // Allocates an empty device weight with the reference's size bookkeeping.
@@ -318,6 +321,8 @@ kt_status kt_qweight_download(const kt_qweight* w, void* qdata, float* scales, u
     if (!w || !qdata || !scales) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     if (w->bits == 4 && !zeros) return fail(KT_ERR_INVALID_ARGUMENT, "4-bit tensors need a zeros buffer");
     KT_CUDA_TRY(cudaSetDevice(w->ctx->device), "cudaSetDevice");
+    // The weight may have been written on any stream (kt_quantize, kt_qweight_from_device).
+    KT_CUDA_TRY(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
     const size_t qbytes = static_cast<size_t>(w->rows) * w->bytes_per_row;
     const size_t gcols = static_cast<size_t>(w->groups) * w->columns;
     KT_CUDA_TRY(cudaMemcpy(qdata, w->qdata, qbytes, cudaMemcpyDeviceToHost), "download qdata");
