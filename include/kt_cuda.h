@@ -140,6 +140,19 @@ kt_status kt_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float
 enum { KT_PATH_GEMV = 0, KT_PATH_GENERIC = 1, KT_PATH_TENSOR_CORE = 2 };
 kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out);
 
+/* Pins the launch shape of the fp32 streaming kernel (no reference counterpart;
+ * the reference's knobs are MatMul.numThreads / parallelThreshold,
+ * MatMul.kt:30-43): packed bytes per lane and row (4, 8 or 16) and CTAs per
+ * thread-block cluster along K (1..8).  0 restores the built-in choice for that
+ * field.  Process-wide; results stay within the same tolerance for every
+ * setting. */
+kt_status kt_set_gemv_tuning(int32_t lane_bytes, int32_t cluster_k);
+
+/* Reads and clears the context's sticky device error word (no reference
+ * counterpart): non-zero means a kernel's bounded wait on a TMA transfer ran
+ * out of time and that call's output is not valid.  Synchronizes the device. */
+kt_status kt_ctx_take_error(kt_ctx* ctx, int32_t* error_out);
+
 /* The literal FloatArray signature: host a / c / bias, copied through the
  * context's staging buffers on its own stream.  Synchronous. */
 kt_status kt_qmatmul_host(kt_ctx* ctx, const kt_qweight* w, const float* a_host, float* c_host, int32_t m,

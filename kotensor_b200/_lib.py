@@ -66,6 +66,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_qmatmul": ([P, P, P, P, I32, I32, F32, P, P], I32),
     "kt_qmatmul_host": ([P, P, P, P, I32, I32, F32, P], I32),
     "kt_qmatmul_path": ([P, I32, ctypes.POINTER(I32)], I32),
+    "kt_set_gemv_tuning": ([I32, I32], I32),
+    "kt_ctx_take_error": ([P, ctypes.POINTER(I32)], I32),
     "kt_qmatmul_t": ([P, P, P, P, I32, I32, P], I32),
 }
 

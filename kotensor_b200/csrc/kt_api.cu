@@ -88,6 +88,7 @@ kt_status alloc_weight(kt_ctx* ctx, int32_t bits, int32_t group_size, int32_t ro
         delete w;
         return cuda_fail(e, "cudaMalloc(quantized weight)");
     }
+    make_tensor_maps(w);  // absent maps only disable the TMA streaming kernel
     *out = w;
     return KT_OK;
 }
@@ -115,9 +116,9 @@ kt_status grow(float** buf, size_t* cap, size_t need) {
 kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
                      float alpha, const float* bias, cudaStream_t s) {
     const QView v = view(w);
-    const MatmulArgs args{a, c, bias, m, accumulate, alpha};
+    const MatmulArgs args{a, c, bias, m, accumulate, alpha, ctx->d_error};
     cudaError_t e;
-    if (gemv_fast_supported(v, m)) {
+    if (gemv_fast_supported(v, m, a)) {
         e = launch_gemv(v, args, ctx->sm_count, s);
     } else {
         e = launch_matmul_generic(v, args, s);
@@ -126,9 +127,53 @@ kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c,
     return KT_OK;
 }
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = []() -> EncodeTiledFn {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
 }  // namespace
 
 void set_error(const std::string& msg) { g_last_error = msg; }
+
+// qdata as a 2-D u8 tensor {bytes_per_row (inner), rows}, boxes of
+// kStageRows rows x 128 / 256 bytes, out-of-range boxes zero-filled.  TMA
+// needs 16-byte aligned rows, so weights with bytes_per_row % 16 != 0 get none.
+bool make_tensor_maps(kt_qweight* w) {
+    w->has_tmaps = false;
+    if (w->bytes_per_row % 16 != 0) return false;
+    EncodeTiledFn encode = encode_tiled();
+    if (!encode) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w->bytes_per_row), static_cast<cuuint64_t>(w->rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w->bytes_per_row)};
+    const cuuint32_t estr[2] = {1, 1};
+    const cuuint32_t box128[2] = {128, kStageRows};
+    const cuuint32_t box256[2] = {256, kStageRows};
+    if (encode(&w->tmap_w128, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->qdata, dims, strides, box128, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    if (encode(&w->tmap_w256, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->qdata, dims, strides, box256, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    w->has_tmaps = true;
+    return true;
+}
 
 }  // namespace kt
 
@@ -159,8 +204,9 @@ kt_status kt_init(int32_t device, kt_ctx** out) {
     if (e == cudaSuccess)
         e = cudaDeviceGetAttribute(&ctx->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_status, sizeof(int32_t));
-    if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_status, 2 * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, 2 * sizeof(int32_t));
+    if (e == cudaSuccess) ctx->d_error = ctx->d_status + 1;
     if (e != cudaSuccess) {
         if (ctx->stream) cudaStreamDestroy(ctx->stream);
         cudaFree(ctx->d_status);
@@ -364,7 +410,21 @@ kt_status kt_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c,
 kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out) {
     if (!w || !path_out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
-    *path_out = gemv_fast_supported(view(w), m) ? KT_PATH_GEMV : KT_PATH_GENERIC;
+    *path_out = gemv_fast_supported(view(w), m, nullptr) ? KT_PATH_GEMV : KT_PATH_GENERIC;
+    return KT_OK;
+}
+
+kt_status kt_set_gemv_tuning(int32_t lane_bytes, int32_t cluster_k) {
+    set_gemv_tuning(lane_bytes, cluster_k);
+    return KT_OK;
+}
+
+kt_status kt_ctx_take_error(kt_ctx* ctx, int32_t* error_out) {
+    if (!ctx || !error_out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    KT_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    KT_CUDA_TRY(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    KT_CUDA_TRY(cudaMemcpy(error_out, ctx->d_error, sizeof(int32_t), cudaMemcpyDeviceToHost), "read error word");
+    KT_CUDA_TRY(cudaMemset(ctx->d_error, 0, sizeof(int32_t)), "clear error word");
     return KT_OK;
 }
 

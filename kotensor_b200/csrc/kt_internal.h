@@ -3,6 +3,7 @@
 // and the launchers each kernel translation unit exports.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <mutex>
@@ -16,6 +17,7 @@ struct kt_ctx {
     int max_smem_optin = 0;
     cudaStream_t stream = nullptr;  // the context's own non-blocking stream
     int32_t* d_status = nullptr;    // device status word for kernels that detect NaN / bad input
+    int32_t* d_error = nullptr;     // sticky device error word: bounded waits that timed out
     std::mutex host_mutex;          // serialises the host-buffer entry points
     // staging for kt_qmatmul_host (grown on demand, owned by the context)
     float* h2d_a = nullptr;
@@ -31,6 +33,11 @@ struct kt_qweight {
     uint8_t* qdata = nullptr;  // device
     float* scales = nullptr;   // device
     uint8_t* zeros = nullptr;  // device, INT4 only
+    // TMA descriptors of qdata as a 2-D u8 tensor [rows x bytes_per_row] with
+    // boxes of 8 rows x 128 / 256 bytes (built when bytes_per_row % 16 == 0).
+    alignas(64) CUtensorMap tmap_w128;
+    alignas(64) CUtensorMap tmap_w256;
+    bool has_tmaps = false;
 };
 
 namespace kt {
@@ -44,12 +51,20 @@ struct QView {
     const float* scales;
     const uint8_t* zeros;
     int32_t bits, group_size, rows, columns, groups, bytes_per_row;
+    const CUtensorMap* tmap_w128;  // NULL when the weight has no TMA descriptors
+    const CUtensorMap* tmap_w256;
 };
 
 inline QView view(const kt_qweight* w) {
     return QView{w->qdata, w->scales, w->zeros, w->bits, w->group_size, w->rows, w->columns, w->groups,
-                 w->bytes_per_row};
+                 w->bytes_per_row, w->has_tmaps ? &w->tmap_w128 : nullptr,
+                 w->has_tmaps ? &w->tmap_w256 : nullptr};
 }
+
+// Rows per TMA box / pipeline stage of the streaming kernel.
+constexpr int kStageRows = 8;
+// Builds kt_qweight::tmap_w128 / tmap_w256 (kt_api.cu).
+bool make_tensor_maps(kt_qweight* w);
 
 // ---- kt_quantize.cu
 cudaError_t launch_quantize(const float* data, int32_t rows, int32_t columns, int32_t bits, int32_t group_size,
@@ -66,10 +81,12 @@ struct MatmulArgs {
     int32_t m;
     int32_t accumulate;
     float alpha;
+    int32_t* err;  // context error word (bounded-wait timeouts)
 };
 // Largest m the fp32-accumulate streaming kernel takes.
 constexpr int kGemvMaxM = 8;
-bool gemv_fast_supported(const QView& w, int32_t m);
+bool gemv_fast_supported(const QView& w, int32_t m, const float* a);
+void set_gemv_tuning(int lane_bytes, int cluster_k);
 cudaError_t launch_gemv(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s);
 cudaError_t launch_matmul_generic(const QView& w, const MatmulArgs& args, cudaStream_t s);
 

@@ -56,6 +56,13 @@ class Context:
             ctx = cls._by_device[device] = Context(device)
         return ctx
 
+    def take_error(self) -> int:
+        """Reads and clears the device error word (non-zero: a bounded wait in a
+        kernel timed out and that call's output is invalid)."""
+        out = ctypes.c_int32()
+        _lib.check(_lib.load().kt_ctx_take_error(self.handle, ctypes.byref(out)))
+        return out.value
+
     def close(self) -> None:
         if self.handle:
             _lib.load().kt_destroy(self.handle)

@@ -288,3 +288,28 @@ def test_transposed_matches_oracle(kt, oracle, k, n, m, bits):
     kt.MatMul.multiply_by_quantized_transposed(dev(dy), qt, dx, m, accumulate=True)
     ref = oracle.multiply_by_quantized_transposed(dy, ref_t, dx=dx0, accumulate=True, threads=8)
     assert rel_err(dx.cpu().numpy(), ref) <= TOL_FP32
+
+
+def test_no_kernel_reported_a_timeout(kt):
+    """Every bounded wait inside the kernels completed in the calls above."""
+    assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("lane_bytes,cluster_k", [(16, 1), (16, 8), (8, 3), (4, 8), (4, 1)])
+def test_every_launch_shape_matches_the_oracle(kt, oracle, lane_bytes, cluster_k):
+    """The tuning knob changes the launch shape only, never the tolerance."""
+    lib = kt.load_library()
+    rng = np.random.default_rng(21)
+    k, n = 2048, 5632
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 4, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, 64)
+    try:
+        lib.kt_set_gemv_tuning(lane_bytes, cluster_k)
+        for m in (1, 2, 5):
+            a = rng.standard_normal((m, k), dtype=np.float32)
+            y = run_matmul(kt, qt, a)
+            assert rel_err(y, oracle.multiply_quantized(a, ref_t, threads=8)) <= TOL_FP32
+    finally:
+        lib.kt_set_gemv_tuning(0, 0)
+    assert kt.Context.get().take_error() == 0
