@@ -133,12 +133,18 @@ kt_status kt_dequantize_rows(kt_ctx* ctx, const kt_qweight* w, const int32_t* ro
 kt_status kt_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float* c_dev, int32_t m,
                      int32_t accumulate, float alpha, const float* bias_dev, void* stream);
 
-/* Which kernel family kt_qmatmul runs for this weight and m, and so which
- * tolerance applies: KT_PATH_GEMV (fp32-accumulate streaming kernel),
- * KT_PATH_GENERIC (fp32-accumulate kernel for unaligned shapes),
- * KT_PATH_TENSOR_CORE (bf16 tcgen05 kernel). */
-enum { KT_PATH_GEMV = 0, KT_PATH_GENERIC = 1, KT_PATH_TENSOR_CORE = 2 };
+/* Which kernel family kt_qmatmul runs for this weight and m (for a 16-byte
+ * aligned a), and so which tolerance applies: KT_PATH_GEMV (fp32 CUDA-core
+ * streaming kernel), KT_PATH_GENERIC (fp32 kernel for unaligned shapes),
+ * KT_PATH_TENSOR_CORE (bf16 tcgen05 kernel, 2e-2), KT_PATH_GEMV_MMA (INT4,
+ * m <= 4: exact integer weights and a two-term fp16 split of x on tensor
+ * cores, fp32 accumulate and fp32 group combine, 1e-3). */
+enum { KT_PATH_GEMV = 0, KT_PATH_GENERIC = 1, KT_PATH_TENSOR_CORE = 2, KT_PATH_GEMV_MMA = 3 };
 kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out);
+
+/* Pins the thread-block cluster size along K (1..16) of the INT4 tensor-core
+ * GEMV; 0 restores the built-in choice (no reference counterpart). */
+kt_status kt_set_gemv_mma_tuning(int32_t cluster_k);
 
 /* Pins the launch shape of the fp32 streaming kernel (no reference counterpart;
  * the reference's knobs are MatMul.numThreads / parallelThreshold,

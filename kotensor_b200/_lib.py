@@ -20,7 +20,7 @@ KT_ERR_OUT_OF_MEMORY = 4
 KT_ERR_UNSUPPORTED = 5
 KT_ERR_NCCL = 6
 
-KT_PATH_GEMV, KT_PATH_GENERIC, KT_PATH_TENSOR_CORE = 0, 1, 2
+KT_PATH_GEMV, KT_PATH_GENERIC, KT_PATH_TENSOR_CORE, KT_PATH_GEMV_MMA = 0, 1, 2, 3
 
 
 class KtError(RuntimeError):
@@ -67,6 +67,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_qmatmul_host": ([P, P, P, P, I32, I32, F32, P], I32),
     "kt_qmatmul_path": ([P, I32, ctypes.POINTER(I32)], I32),
     "kt_set_gemv_tuning": ([I32, I32], I32),
+    "kt_set_gemv_mma_tuning": ([I32], I32),
     "kt_ctx_take_error": ([P, ctypes.POINTER(I32)], I32),
     "kt_qmatmul_t": ([P, P, P, P, I32, I32, P], I32),
 }

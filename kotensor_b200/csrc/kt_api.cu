@@ -118,7 +118,9 @@ kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c,
     const QView v = view(w);
     const MatmulArgs args{a, c, bias, m, accumulate, alpha, ctx->d_error};
     cudaError_t e;
-    if (gemv_fast_supported(v, m, a)) {
+    if (gemv_mma_supported(v, m, a)) {
+        e = launch_gemv_mma(v, args, ctx->sm_count, s);
+    } else if (gemv_fast_supported(v, m, a)) {
         e = launch_gemv(v, args, ctx->sm_count, s);
     } else {
         e = launch_matmul_generic(v, args, s);
@@ -172,6 +174,13 @@ bool make_tensor_maps(kt_qweight* w) {
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
     w->has_tmaps = true;
+    if (w->bytes_per_row >= 128) {
+        const cuuint32_t box_mma[2] = {128, 16};
+        w->has_tmap_mma =
+            encode(&w->tmap_mma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->qdata, dims, strides, box_mma, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
     return true;
 }
 
@@ -410,12 +419,20 @@ kt_status kt_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c,
 kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out) {
     if (!w || !path_out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
-    *path_out = gemv_fast_supported(view(w), m, nullptr) ? KT_PATH_GEMV : KT_PATH_GENERIC;
+    const QView v = view(w);
+    *path_out = gemv_mma_supported(v, m, nullptr)    ? KT_PATH_GEMV_MMA
+                : gemv_fast_supported(v, m, nullptr) ? KT_PATH_GEMV
+                                                     : KT_PATH_GENERIC;
     return KT_OK;
 }
 
 kt_status kt_set_gemv_tuning(int32_t lane_bytes, int32_t cluster_k) {
     set_gemv_tuning(lane_bytes, cluster_k);
+    return KT_OK;
+}
+
+kt_status kt_set_gemv_mma_tuning(int32_t cluster_k) {
+    set_mma_tuning(cluster_k);
     return KT_OK;
 }
 

@@ -1,0 +1,517 @@
+// kt_gemv_mma.cu -- INT4 decode GEMV (m <= 4) with tensor-core products:
+// MatMul.multiplyQuantized (Engine/kotensor/src/main/kotlin/MatMul.kt:460-536,
+// :599-828) for m = 1..4.
+//
+// Why tensor cores for a memory-bound GEMV.  B200's HBM streams ~13e12 INT4
+// weights/s while its CUDA cores issue ~3.7e13 lane instructions/s; an fp32
+// FMA kernel needs >= 2.4 instructions per weight (unpack + FMA) and measured
+// 3.4, so it is issue-bound well below the HBM roofline.  Here the products
+// run on mma.sync.m16n8k16 (fp16 inputs, fp32 accumulate) and the CUDA cores
+// only turn nibbles into fp16 operands: 10 instructions per 8 weights.
+//
+// Exactness.  The A operand holds the raw nibbles q as fp16 integers 0..15
+// (exact): two bytes of two rows are interleaved with PRMT, LOP3 masks each
+// nibble into the mantissa of 1024.0h (0x6400), and one f16x2 op removes the
+// 1024 (and the 16x of the high nibble) exactly.  The B operand holds x split
+// into two fp16 terms, hi = fp16(x') and lo = fp16(x' - hi), with
+// x' = x * 2^s scaled by a power of two per (warp slice, row of x) so hi is in
+// [2^14, 2^15) for the largest |x| -- a 22-bit significand, products exact,
+// fp32 accumulation.  Each group's accumulator is then combined as in the
+// reference (combineGroup, MatMul.kt:804-828):
+//     y[j] += scale[g,j] * (2^-s * (C_hi + C_lo) - zero[g,j] * sum_l x_l)
+// with sum_l x_l accumulated in fp32 from the unscaled x.
+//
+// Tiling.  A CTA owns 128 packed bytes of every row (INT4: 128 low-nibble
+// columns and 128 high-nibble columns) and 8 warps split K into contiguous
+// slices (multiples of 16 rows); a thread-block cluster of CK CTAs along K
+// splits it further.  In an m16n8k16 tile, A row g (g = lane/4) is the low
+// nibble of one byte and row g+8 the high nibble of the same byte; lane
+// t = lane%4 holds k-slots 2t, 2t+1, 2t+8, 2t+9, i.e. those rows of the
+// 16-row step, so a thread reads one 16-byte chunk of four rows and feeds 16
+// MMAs from it (with the 128-byte swizzle, the 8 lanes of each shared-load
+// phase hit 8 different bank groups).  B column n = 2*token + part
+// (part 0 = hi, 1 = lo), so C columns 2t, 2t+1 of lane (g, t) are token t.
+//
+// Streaming.  Each warp owns a ring of kStages stages of 16 rows x 128 bytes,
+// filled by lane 0 with one 2-D TMA copy per stage (128-byte swizzle, so the
+// four row-reads of a quad hit different banks) plus, on the first stage of
+// each group, 1-D bulk copies of that group's scales and zero points into a
+// per-warp ring of group slots.  Completion is tracked by one mbarrier per
+// stage; every wait is bounded (globaltimer) and a timeout sets the context's
+// error word.  The kernel is launched with programmatic stream serialization:
+// the weight prefetch overlaps the previous kernel, griddepcontrol.wait orders
+// the reads of x and the writes of y after it.
+//
+// Reduction order (deterministic, no atomics, no global scratch): group
+// partials in registers per thread in row order; the 8 warps of a CTA through
+// shared memory in warp order; the CK CTAs of a cluster through distributed
+// shared memory in rank order.
+#include <cooperative_groups.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstdlib>
+
+#include "kt_internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace kt {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kStep = 16;          // rows per MMA step / TMA stage
+constexpr int kTileBytes = 128;    // packed bytes per CTA tile row
+constexpr int kStages = 6;         // stages per warp ring (also group slots)
+constexpr int kMaxSliceGroups = 128;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+constexpr int kStageBytes = kStep * kTileBytes;                  // 2048
+constexpr int kScaleSlotBytes = 2 * kTileBytes * 4 + 2 * kTileBytes;  // 1280
+constexpr int kRingBytes = kStages * kStageBytes;                // per warp
+constexpr int kSlotRingBytes = kStages * kScaleSlotBytes;        // per warp
+constexpr int kRsBytes = kMaxSliceGroups * 4 * 4;                // per warp: rowsums [group][token]
+constexpr int kRedBytes = kWarps * 32 * 32 * 4;                  // reuses the rings
+constexpr int kMainBytes = kWarps * kRingBytes;
+constexpr int kPartBytes = 4 * 2 * kTileBytes * 4;
+constexpr size_t kSmemBytes = static_cast<size_t>(kMainBytes) + kWarps * kSlotRingBytes + kWarps * kRsBytes +
+                              kPartBytes + kWarps * kStages * 8;
+static_assert(kRedBytes <= kMainBytes, "reduction buffer must fit in the rings");
+
+struct MmaParams {
+    const float* scales;
+    const uint8_t* zeros;
+    const float* x;
+    float* y;
+    const float* bias;
+    int32_t* err;
+    int32_t K, N, R, gs;
+    int32_t slice_rows;  // multiple of kStep
+    uint32_t h1024;      // 0x64006400: f16x2 {1024, 1024}
+    uint32_t h_sixteenth;  // 0x2C002C00: f16x2 {1/16, 1/16}
+    uint32_t h_neg64;    // 0xD400D400: f16x2 {-64, -64}
+    float alpha;
+    int32_t accumulate;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > kWaitLimitNs) return false;
+    }
+    return true;
+}
+// 2-D TMA tile load into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+// 1-D bulk copy global -> this CTA's shared memory (no multicast).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "n"(MASK), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Shared memory: rings[8][NS][16][128] (later red) | slots[8][NS][1280] |
+// rowsum[8][128][4] | part[4][256] | mbarriers[8][NS].
+template <int M>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap, MmaParams p) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int g = lane >> 2;  // MMA row group: byte chunk g of the tile
+    const int t = lane & 3;   // MMA k quad: rows 2t, 2t+1, 2t+8, 2t+9; token t of C
+    const int tile_b0 = blockIdx.x * kTileBytes;
+    const int tile_cols = min(kTileBytes, p.R - tile_b0);  // packed bytes of this tile inside the row
+    const int half = p.R;
+
+    const int slice = blockIdx.y * kWarps + warp;
+    const int r_begin = min(slice * p.slice_rows, p.K);
+    const int r_end = min(r_begin + p.slice_rows, p.K);
+    const int n_steps = (r_end - r_begin) / kStep;  // K and slices are multiples of kStep
+
+    unsigned char* ring = smem + warp * kRingBytes;
+    unsigned char* slots = smem + kMainBytes + warp * kSlotRingBytes;
+    float* rs_s = reinterpret_cast<float*>(smem + kMainBytes + kWarps * kSlotRingBytes) + warp * kMaxSliceGroups * 4;
+    float* part = reinterpret_cast<float*>(smem + kMainBytes + kWarps * kSlotRingBytes + kWarps * kRsBytes);
+    const uint32_t bars = smem_u32(smem + kMainBytes + kWarps * kSlotRingBytes + kWarps * kRsBytes + kPartBytes) +
+                          warp * kStages * 8;
+    const uint32_t ring_s = smem_u32(ring);
+    const uint32_t slots_s = smem_u32(slots);
+    const int g_first = r_begin / p.gs;
+
+    if (lane == 0) {
+        for (int s = 0; s < kStages; ++s) mbar_init(bars + 8 * s, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    // Stage st: rows [r_begin + 16 st, +16) into ring slot st % NS; the first
+    // stage of a group (and of the slice) also brings the group's scales and
+    // zero points into group slot (group - g_first) % NS.
+    auto issue = [&](int st) {  // lane 0 only
+        const int slot = st % kStages;
+        const uint32_t bar = bars + 8 * slot;
+        const int row0 = r_begin + st * kStep;
+        const bool group_start = st == 0 || row0 % p.gs == 0;
+        const uint32_t sbytes = static_cast<uint32_t>(tile_cols) * 10;  // 2 x fp32 scales + 2 x u8 zeros
+        mbar_expect_tx(bar, kStageBytes + (group_start ? sbytes : 0));
+        tma_load_2d(ring_s + slot * kStageBytes, &tmap, tile_b0, row0, bar);
+        if (group_start) {
+            const int gi = row0 / p.gs;
+            const uint32_t dst = slots_s + ((gi - g_first) % kStages) * kScaleSlotBytes;
+            const int64_t go = static_cast<int64_t>(gi) * p.N;
+            bulk_load(dst, p.scales + go + tile_b0, tile_cols * 4, bar);
+            bulk_load(dst + kTileBytes * 4, p.scales + go + half + tile_b0, tile_cols * 4, bar);
+            bulk_load(dst + kTileBytes * 8, p.zeros + go + tile_b0, tile_cols, bar);
+            bulk_load(dst + kTileBytes * 9, p.zeros + go + half + tile_b0, tile_cols, bar);
+        }
+    };
+    if (lane == 0) {
+        for (int s = 0; s < kStages - 1 && s < n_steps; ++s) issue(s);
+    }
+    pdl_launch_dependents();
+    pdl_wait();  // x and y below may belong to the previous kernel
+
+    // Slice prologue: per token, the power-of-two scale of x' and each group's
+    // row sum of the unscaled x (fixed lane and shuffle order).
+    float xscale[M], xunscale[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        const float* xm = p.x + static_cast<int64_t>(m) * p.K;
+        float mx = 0.0f;
+        for (int r = r_begin + lane; r < r_end; r += 32) mx = fmaxf(mx, fabsf(__ldg(xm + r)));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        int e = mx > 0.0f ? ilogbf(mx) : 0;
+        int sh = 14 - e;
+        sh = max(-126, min(126, sh));
+        xscale[m] = ldexpf(1.0f, sh);
+        xunscale[m] = ldexpf(1.0f, -sh);
+        for (int gi = g_first; gi * p.gs < r_end; ++gi) {
+            const int a0 = max(gi * p.gs, r_begin), a1 = min((gi + 1) * p.gs, r_end);
+            float s = 0.0f;
+            for (int r = a0 + lane; r < a1; r += 32) s += __ldg(xm + r);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == 0) rs_s[(gi - g_first) * 4 + m] = s;
+        }
+    }
+    __syncwarp();
+
+    // This lane's B column: token g/2, part g%2 (0 = hi, 1 = lo); tokens >= M are zero.
+    const int btok = g >> 1;
+    const bool bpart_lo = g & 1;
+    const float* xb = p.x + static_cast<int64_t>(btok < M ? btok : 0) * p.K;
+    float bscale = 1.0f;
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+        if (m == btok) bscale = xscale[m];
+
+    float y[32];  // token t: [0,16) low-nibble columns 16g + jj, [16,32) high-nibble columns
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = 0.0f;
+    float c[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0.0f;
+
+    const uint32_t h1024 = p.h1024, h16 = p.h_sixteenth, hm64 = p.h_neg64;
+    bool ok = true;
+    int gi = g_first;
+    int group_end = min((gi + 1) * p.gs, r_end);
+    for (int st = 0; st < n_steps; ++st) {
+        const int slot = st % kStages;
+        if (ok && !mbar_wait_bounded(bars + 8 * slot, (st / kStages) & 1)) {
+            ok = false;
+            if (lane == 0) atomicOr(p.err, 1);
+        }
+        __syncwarp();  // every lane is done with the stage consumed at st - 1
+        if (lane == 0 && ok && st + kStages - 1 < n_steps) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(st + kStages - 1);
+        }
+        const int row0 = r_begin + st * kStep;
+        // B fragment: rows 2t, 2t+1 (b0) and 2t+8, 2t+9 (b1) of x' for this lane's column.
+        uint32_t b0 = 0u, b1 = 0u;
+        if (btok < M) {
+            float xv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xv[i] = __ldg(xb + row0 + 2 * t + (i & 1) + 8 * (i >> 1)) * bscale;
+            float hv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float h = __half2float(__float2half_rn(xv[i]));
+                hv[i] = bpart_lo ? xv[i] - h : h;
+            }
+            b0 = pack_h2(hv[0], hv[1]);
+            b1 = pack_h2(hv[2], hv[3]);
+        }
+        // A: chunk g of rows 2t, 2t+1, 2t+8, 2t+9 (128-byte swizzle: chunk ^ (row & 7)).
+        const unsigned char* stage = ring + slot * kStageBytes;
+        uint4 w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = 2 * t + (i & 1) + 8 * (i >> 1);
+            w[i] = *reinterpret_cast<const uint4*>(stage + r * kTileBytes + ((g ^ (r & 7)) << 4));
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t w0 = (&w[0].x)[k], w1 = (&w[1].x)[k], w2 = (&w[2].x)[k], w3 = (&w[3].x)[k];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t sel = static_cast<uint32_t>(j | ((4 + j) << 8));
+                const uint32_t p01 = prmt(w0, w1, sel);  // byte j of rows 2t and 2t+1 at bits 0-7 / 16-23
+                const uint32_t p23 = prmt(w2, w3, sel);
+                uint32_t a[4];
+                a[0] = hsub2(lop3_and_or<0x000F000Fu>(p01, h1024), h1024);                 // low nibbles
+                a[1] = hfma2(lop3_and_or<0x00F000F0u>(p01, h1024), h16, hm64);             // high nibbles
+                a[2] = hsub2(lop3_and_or<0x000F000Fu>(p23, h1024), h1024);
+                a[3] = hfma2(lop3_and_or<0x00F000F0u>(p23, h1024), h16, hm64);
+                mma_16816(c[4 * k + j], a, b0, b1);
+            }
+        }
+        if (row0 + kStep >= group_end) {
+            // Group epilogue for token t: y += scale * (2^-s * (C_hi + C_lo) - zero * rowSum).
+            if (t < M) {
+                const unsigned char* sl = slots + ((gi - g_first) % kStages) * kScaleSlotBytes;
+                const float* s_lo = reinterpret_cast<const float*>(sl);
+                const float* s_hi = reinterpret_cast<const float*>(sl + kTileBytes * 4);
+                const uint8_t* z_lo = sl + kTileBytes * 8;
+                const uint8_t* z_hi = sl + kTileBytes * 9;
+                float un = 1.0f;
+#pragma unroll
+                for (int m = 0; m < M; ++m)
+                    if (m == t) un = xunscale[m];
+                const float rs = rs_s[(gi - g_first) * 4 + t];
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) {
+                    const int col = 16 * g + jj;
+                    if (col < tile_cols) {
+                        y[jj] = fmaf(s_lo[col], fmaf(c[jj][0] + c[jj][1], un, -static_cast<float>(z_lo[col]) * rs), y[jj]);
+                        y[16 + jj] = fmaf(s_hi[col],
+                                          fmaf(c[jj][2] + c[jj][3], un, -static_cast<float>(z_hi[col]) * rs),
+                                          y[16 + jj]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0.0f;
+            ++gi;
+            group_end = min((gi + 1) * p.gs, r_end);
+        }
+    }
+
+    // (1) warps of the CTA in warp order; red[w][jj][lane] reuses the rings.
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(smem);
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) red[(warp * 32 + jj) * 32 + lane] = y[jj];
+    __syncthreads();
+    constexpr int CT = 2 * kTileBytes;  // 256 columns per tile: [0,128) low, [128,256) high
+    for (int idx = tid; idx < M * CT; idx += kThreads) {
+        const int m = idx / CT, col = idx % CT;
+        const int hi = col >= kTileBytes;
+        const int cb = hi ? col - kTileBytes : col;
+        const int jj = (hi ? 16 : 0) + cb % 16;
+        const int ln = 4 * (cb / 16) + m;
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) v += red[(w * 32 + jj) * 32 + ln];
+        part[idx] = v;
+    }
+    // (2) CTAs of the cluster along K in rank order; rank r finishes columns [r*CT/CK, (r+1)*CT/CK).
+    cg::cluster_group cluster = cg::this_cluster();
+    const int CK = gridDim.y;
+    if (CK > 1) cluster.sync(); else __syncthreads();
+    const int rank = CK > 1 ? static_cast<int>(cluster.block_rank()) : 0;
+    const int j0 = rank * CT / CK, j1 = (rank + 1) * CT / CK;
+    const int span = j1 - j0;
+    for (int idx = tid; idx < M * span; idx += kThreads) {
+        const int m = idx / span;
+        const int col = j0 + idx % span;
+        float v;
+        if (CK > 1) {
+            v = 0.0f;
+            for (int q = 0; q < CK; ++q) v += cluster.map_shared_rank(part, q)[m * CT + col];
+        } else {
+            v = part[m * CT + col];
+        }
+        const int byte = tile_b0 + (col < kTileBytes ? col : col - kTileBytes);
+        const int out_col = col < kTileBytes ? byte : half + byte;
+        if (byte < p.R && out_col < p.N) {
+            float* out = p.y + static_cast<int64_t>(m) * p.N + out_col;
+            float r = fmaf(p.alpha, v, p.accumulate ? *out : 0.0f);
+            if (p.bias != nullptr) r += p.bias[out_col];
+            *out = r;
+        }
+    }
+    if (CK > 1) cluster.sync();  // keep this CTA's shared memory alive until every rank has read it
+}
+
+struct MmaOverrides {
+    int ck;
+};
+MmaOverrides& mma_overrides() {
+    static MmaOverrides o{[] {
+        const char* v = std::getenv("KT_MMA_CK");
+        return v ? std::atoi(v) : 0;
+    }()};
+    return o;
+}
+
+// One CTA per SM: the largest cluster along K (<= 16) that keeps the grid in one
+// wave and >= 32 rows per warp.
+int choose_ck(int R, int K, int sm_count) {
+    const int tiles = (R + kTileBytes - 1) / kTileBytes;
+    int best = 1;
+    for (int ck = 1; ck <= 16; ++ck) {
+        if (tiles * ck > sm_count) break;
+        if (K / (kWarps * ck) < 32) break;
+        best = ck;
+    }
+    return best;
+}
+
+template <int M>
+cudaError_t launch_m(const QView& w, const MmaParams& p, int ck, cudaStream_t s) {
+    auto kernel = gemv_mma_kernel<M>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return e;
+    if (ck > 8) {
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
+    MmaParams q = p;
+    const int slices = kWarps * ck;
+    const int per = (p.K + slices - 1) / slices;
+    q.slice_rows = (per + kStep - 1) / kStep * kStep;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((p.R + kTileBytes - 1) / kTileBytes, ck, 1);
+    lc.blockDim = dim3(kThreads, 1, 1);
+    lc.dynamicSmemBytes = kSmemBytes;
+    lc.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = ck;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 2;
+    return cudaLaunchKernelEx(&lc, kernel, *w.tmap_mma, q);
+}
+
+}  // namespace
+
+void set_mma_tuning(int cluster_k) { mma_overrides().ck = cluster_k; }
+
+bool gemv_mma_supported(const QView& w, int32_t m, const float* a) {
+    if (w.bits != 4 || m < 1 || m > kGemvMmaMaxM || w.tmap_mma == nullptr) return false;
+    if (w.columns % 32 != 0 || w.rows % kStep != 0 || w.group_size % kStep != 0) return false;
+    if (reinterpret_cast<uintptr_t>(a) % 4 != 0) return false;
+    // Every warp slice must keep its group row sums in shared memory, at the
+    // latest with the largest cluster (16 CTAs x 8 warps).
+    const int per = ((w.rows + 16 * kWarps - 1) / (16 * kWarps) + kStep - 1) / kStep * kStep;
+    return per / w.group_size + 2 <= kMaxSliceGroups;
+}
+
+cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s) {
+    MmaParams p{};
+    p.scales = w.scales;
+    p.zeros = w.zeros;
+    p.x = a.a;
+    p.y = a.c;
+    p.bias = a.bias;
+    p.err = a.err;
+    p.K = w.rows;
+    p.N = w.columns;
+    p.R = w.bytes_per_row;
+    p.gs = w.group_size;
+    p.h1024 = 0x64006400u;
+    p.h_sixteenth = 0x2C002C00u;
+    p.h_neg64 = 0xD400D400u;
+    p.alpha = a.alpha;
+    p.accumulate = a.accumulate;
+    int ck = choose_ck(p.R, p.K, sm_count);
+    const int o = mma_overrides().ck;
+    if (o >= 1 && o <= 16) ck = o;
+    // Each warp slice must fit kMaxSliceGroups group row sums.
+    while (ck < 16 && ((p.K + kWarps * ck - 1) / (kWarps * ck)) / p.gs + 2 > kMaxSliceGroups) ++ck;
+    switch (a.m) {
+        case 1: return launch_m<1>(w, p, ck, s);
+        case 2: return launch_m<2>(w, p, ck, s);
+        case 3: return launch_m<3>(w, p, ck, s);
+        case 4: return launch_m<4>(w, p, ck, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace kt

@@ -38,6 +38,10 @@ struct kt_qweight {
     alignas(64) CUtensorMap tmap_w128;
     alignas(64) CUtensorMap tmap_w256;
     bool has_tmaps = false;
+    // Box of 16 rows x 128 bytes with the 128-byte swizzle (INT4 tensor-core
+    // GEMV; built when bytes_per_row % 16 == 0 and bytes_per_row >= 128).
+    alignas(64) CUtensorMap tmap_mma;
+    bool has_tmap_mma = false;
 };
 
 namespace kt {
@@ -53,12 +57,13 @@ struct QView {
     int32_t bits, group_size, rows, columns, groups, bytes_per_row;
     const CUtensorMap* tmap_w128;  // NULL when the weight has no TMA descriptors
     const CUtensorMap* tmap_w256;
+    const CUtensorMap* tmap_mma;
 };
 
 inline QView view(const kt_qweight* w) {
     return QView{w->qdata, w->scales, w->zeros, w->bits, w->group_size, w->rows, w->columns, w->groups,
                  w->bytes_per_row, w->has_tmaps ? &w->tmap_w128 : nullptr,
-                 w->has_tmaps ? &w->tmap_w256 : nullptr};
+                 w->has_tmaps ? &w->tmap_w256 : nullptr, w->has_tmap_mma ? &w->tmap_mma : nullptr};
 }
 
 // Rows per TMA box / pipeline stage of the streaming kernel.
@@ -89,6 +94,12 @@ bool gemv_fast_supported(const QView& w, int32_t m, const float* a);
 void set_gemv_tuning(int lane_bytes, int cluster_k);
 cudaError_t launch_gemv(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s);
 cudaError_t launch_matmul_generic(const QView& w, const MatmulArgs& args, cudaStream_t s);
+
+// ---- kt_gemv_mma.cu  (INT4, m <= kGemvMmaMaxM: tensor-core products, fp32 group combine)
+constexpr int kGemvMmaMaxM = 4;
+bool gemv_mma_supported(const QView& w, int32_t m, const float* a);
+void set_mma_tuning(int cluster_k);
+cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s);
 
 // ---- kt_backward.cu
 cudaError_t launch_matmul_t(const QView& w, const float* dy, float* dx, int32_t m, int32_t accumulate,

@@ -313,3 +313,47 @@ def test_every_launch_shape_matches_the_oracle(kt, oracle, lane_bytes, cluster_k
     finally:
         lib.kt_set_gemv_tuning(0, 0)
     assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("cluster_k", [1, 2, 5, 16])
+@pytest.mark.parametrize("k,n,g", [(2048, 5632, 64), (4864, 896, 64), (1024, 4096, 16), (960, 2048, 48)])
+def test_int4_tensor_core_gemv_matches_the_oracle(kt, oracle, cluster_k, k, n, g):
+    """The INT4 m <= 4 tensor-core GEMV at every cluster size, ragged last tiles
+    (896 columns) and group sizes 16 / 48 / 64, within the fp32 tolerance."""
+    from kotensor_b200 import _lib
+    lib = kt.load_library()
+    rng = np.random.default_rng(k + n + g)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 4, g)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, g)
+    assert qt.matmul_path(1) == _lib.KT_PATH_GEMV_MMA
+    try:
+        lib.kt_set_gemv_mma_tuning(cluster_k)
+        for m in (1, 2, 4):
+            a = (rng.standard_normal((m, k), dtype=np.float32) * np.float32(3.0)).astype(np.float32)
+            a[0, : k // 3] *= np.float32(1e-3)  # a wide dynamic range inside one row
+            c0 = rng.standard_normal((m, n), dtype=np.float32)
+            y = run_matmul(kt, qt, a, c0=c0, accumulate=True, alpha=0.75)
+            ref = oracle.multiply_quantized(a, ref_t, c=c0, accumulate=True, alpha=0.75, threads=8)
+            assert rel_err(y, ref) <= TOL_FP32, (m, rel_err(y, ref))
+    finally:
+        lib.kt_set_gemv_mma_tuning(0)
+    assert kt.Context.get().take_error() == 0
+
+
+def test_int4_tensor_core_gemv_huge_and_tiny_activations(kt, oracle):
+    """x rows scaled by 1e30 and 1e-30: the per-slice power-of-two scaling keeps
+    the fp16 split in range."""
+    rng = np.random.default_rng(33)
+    k, n = 2048, 2048
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 4, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, 64)
+    for s in (1e30, 1e-30, 0.0):
+        a = (rng.standard_normal((2, k), dtype=np.float32) * np.float32(s)).astype(np.float32)
+        y = run_matmul(kt, qt, a)
+        ref = oracle.multiply_quantized(a, ref_t, threads=8)
+        if s == 0.0:
+            assert not np.any(y)
+        else:
+            assert rel_err(y, ref) <= TOL_FP32, s
