@@ -175,7 +175,7 @@ bool make_tensor_maps(kt_qweight* w) {
         return false;
     w->has_tmaps = true;
     if (w->bytes_per_row >= 128) {
-        const cuuint32_t box_mma[2] = {128, 16};
+        const cuuint32_t box_mma[2] = {128, 32};
         w->has_tmap_mma =
             encode(&w->tmap_mma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->qdata, dims, strides, box_mma, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -32,11 +32,10 @@
 // phase hit 8 different bank groups).  B column n = 2*token + part
 // (part 0 = hi, 1 = lo), so C columns 2t, 2t+1 of lane (g, t) are token t.
 //
-// Streaming.  Each warp owns a ring of kStages stages of 16 rows x 128 bytes,
-// filled by lane 0 with one 2-D TMA copy per stage (128-byte swizzle, so the
-// four row-reads of a quad hit different banks) plus, on the first stage of
-// each group, 1-D bulk copies of that group's scales and zero points into a
-// per-warp ring of group slots.  Completion is tracked by one mbarrier per
+// Streaming.  Each warp owns a ring of kStages stages of 32 rows x 128 bytes,
+// filled by lane 0 with one 2-D TMA copy per stage (128-byte swizzle) plus, on
+// the first stage of each group, 1-D bulk copies of that group's scales and
+// zero points into a per-warp ring of group slots.  Completion is tracked by one mbarrier per
 // stage; every wait is bounded (globaltimer) and a timeout sets the context's
 // error word.  The kernel is launched with programmatic stream serialization:
 // the weight prefetch overlaps the previous kernel, griddepcontrol.wait orders
@@ -61,23 +60,25 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStep = 16;          // rows per MMA step / TMA stage
+constexpr int kStep = 16;          // rows per MMA step
+constexpr int kRowsPerStage = 32;     // rows per TMA stage (two MMA steps)
 constexpr int kTileBytes = 128;    // packed bytes per CTA tile row
-constexpr int kStages = 6;         // stages per warp ring (also group slots)
+constexpr int kStages = 4;         // stages per warp ring (also group slots)
 constexpr int kMaxSliceGroups = 128;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-constexpr int kStageBytes = kStep * kTileBytes;                  // 2048
+constexpr int kStageBytes = kRowsPerStage * kTileBytes;                 // 4096
 constexpr int kScaleSlotBytes = 2 * kTileBytes * 4 + 2 * kTileBytes;  // 1280
-constexpr int kRingBytes = kStages * kStageBytes;                // per warp
-constexpr int kSlotRingBytes = kStages * kScaleSlotBytes;        // per warp
-constexpr int kRsBytes = kMaxSliceGroups * 4 * 4;                // per warp: rowsums [group][token]
-constexpr int kRedBytes = kWarps * 32 * 32 * 4;                  // reuses the rings
+constexpr int kRingBytes = kStages * kStageBytes;                    // per warp
+constexpr int kSlotRingBytes = kStages * kScaleSlotBytes;            // per warp
+constexpr int kRsBytes = kMaxSliceGroups * 4 * 4;                    // per warp: rowsums [group][token]
+constexpr int kRedBytes = kWarps * 32 * 32 * 4;                      // reuses the rings
 constexpr int kMainBytes = kWarps * kRingBytes;
 constexpr int kPartBytes = 4 * 2 * kTileBytes * 4;
 constexpr size_t kSmemBytes = static_cast<size_t>(kMainBytes) + kWarps * kSlotRingBytes + kWarps * kRsBytes +
                               kPartBytes + kWarps * kStages * 8;
 static_assert(kRedBytes <= kMainBytes, "reduction buffer must fit in the rings");
+static_assert(kRowsPerStage == 32, "the TMA box of QView::tmap_mma is 32 rows");
 
 struct MmaParams {
     const float* scales;
@@ -87,10 +88,10 @@ struct MmaParams {
     const float* bias;
     int32_t* err;
     int32_t K, N, R, gs;
-    int32_t slice_rows;  // multiple of kStep
-    uint32_t h1024;      // 0x64006400: f16x2 {1024, 1024}
+    int32_t slice_rows;    // multiple of kRowsPerStage
+    uint32_t h1024;        // 0x64006400: f16x2 {1024, 1024}
     uint32_t h_sixteenth;  // 0x2C002C00: f16x2 {1/16, 1/16}
-    uint32_t h_neg64;    // 0xD400D400: f16x2 {-64, -64}
+    uint32_t h_neg64;      // 0xD400D400: f16x2 {-64, -64}
     float alpha;
     int32_t accumulate;
 };
@@ -177,7 +178,42 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Shared memory: rings[8][NS][16][128] (later red) | slots[8][NS][1280] |
+__device__ __forceinline__ void mma_16816_zero(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+// A fragments of the 16 MMAs of one 16-row step from the four 16-byte row
+// chunks w[0..3] (rows 2t, 2t+1, 2t+8, 2t+9), MMA i = 4k + j <-> byte 4k + j.
+template <bool kFresh>
+__device__ __forceinline__ void mma_step(float (&c)[16][4], const uint4 (&w)[4], uint32_t b0, uint32_t b1,
+                                         uint32_t h1024, uint32_t h16, uint32_t hm64) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t w0 = (&w[0].x)[k], w1 = (&w[1].x)[k], w2 = (&w[2].x)[k], w3 = (&w[3].x)[k];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t sel = static_cast<uint32_t>(j | ((4 + j) << 8));
+            const uint32_t p01 = prmt(w0, w1, sel);  // byte j of rows 2t and 2t+1 at bits 0-7 / 16-23
+            const uint32_t p23 = prmt(w2, w3, sel);
+            uint32_t a[4];
+            a[0] = hsub2(lop3_and_or<0x000F000Fu>(p01, h1024), h1024);      // low nibbles
+            a[1] = hfma2(lop3_and_or<0x00F000F0u>(p01, h1024), h16, hm64);  // high nibbles
+            a[2] = hsub2(lop3_and_or<0x000F000Fu>(p23, h1024), h1024);
+            a[3] = hfma2(lop3_and_or<0x00F000F0u>(p23, h1024), h16, hm64);
+            if constexpr (kFresh) {
+                mma_16816_zero(c[4 * k + j], a, b0, b1);
+            } else {
+                mma_16816(c[4 * k + j], a, b0, b1);
+            }
+        }
+    }
+}
+
+// Shared memory: rings[8][NS][32][128] (later red) | slots[8][NS][1280] |
 // rowsum[8][128][4] | part[4][256] | mbarriers[8][NS].
 template <int M>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -195,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int slice = blockIdx.y * kWarps + warp;
     const int r_begin = min(slice * p.slice_rows, p.K);
     const int r_end = min(r_begin + p.slice_rows, p.K);
-    const int n_steps = (r_end - r_begin) / kStep;  // K and slices are multiples of kStep
+    const int n_stages = (r_end - r_begin) / kRowsPerStage;  // K and slices are multiples of kRowsPerStage
 
     unsigned char* ring = smem + warp * kRingBytes;
     unsigned char* slots = smem + kMainBytes + warp * kSlotRingBytes;
@@ -212,20 +248,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncwarp();
-    // Stage st: rows [r_begin + 16 st, +16) into ring slot st % NS; the first
-    // stage of a group (and of the slice) also brings the group's scales and
-    // zero points into group slot (group - g_first) % NS.
+    // Stage st: rows [r_begin + 32 st, +32) into ring slot st % NS; a stage that
+    // starts a group (or the slice) also brings the group's scales and zero
+    // points into group slot (group - g_first) % NS.
     auto issue = [&](int st) {  // lane 0 only
-        const int slot = st % kStages;
+        const int slot = st & (kStages - 1);
         const uint32_t bar = bars + 8 * slot;
-        const int row0 = r_begin + st * kStep;
+        const int row0 = r_begin + st * kRowsPerStage;
         const bool group_start = st == 0 || row0 % p.gs == 0;
         const uint32_t sbytes = static_cast<uint32_t>(tile_cols) * 10;  // 2 x fp32 scales + 2 x u8 zeros
         mbar_expect_tx(bar, kStageBytes + (group_start ? sbytes : 0));
         tma_load_2d(ring_s + slot * kStageBytes, &tmap, tile_b0, row0, bar);
         if (group_start) {
             const int gi = row0 / p.gs;
-            const uint32_t dst = slots_s + ((gi - g_first) % kStages) * kScaleSlotBytes;
+            const uint32_t dst = slots_s + ((gi - g_first) & (kStages - 1)) * kScaleSlotBytes;
             const int64_t go = static_cast<int64_t>(gi) * p.N;
             bulk_load(dst, p.scales + go + tile_b0, tile_cols * 4, bar);
             bulk_load(dst + kTileBytes * 4, p.scales + go + half + tile_b0, tile_cols * 4, bar);
@@ -234,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     };
     if (lane == 0) {
-        for (int s = 0; s < kStages - 1 && s < n_steps; ++s) issue(s);
+        for (int s = 0; s < kStages - 1 && s < n_stages; ++s) issue(s);
     }
     pdl_launch_dependents();
     pdl_wait();  // x and y below may belong to the previous kernel
@@ -249,8 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int r = r_begin + lane; r < r_end; r += 32) mx = fmaxf(mx, fabsf(__ldg(xm + r)));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        int e = mx > 0.0f ? ilogbf(mx) : 0;
-        int sh = 14 - e;
+        int sh = 14 - (mx > 0.0f ? ilogbf(mx) : 0);
         sh = max(-126, min(126, sh));
         xscale[m] = ldexpf(1.0f, sh);
         xunscale[m] = ldexpf(1.0f, -sh);
@@ -265,103 +300,101 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
 
-    // This lane's B column: token g/2, part g%2 (0 = hi, 1 = lo); tokens >= M are zero.
+    // This lane's B column: token g/2, part g%2 (0 = hi, 1 = lo); tokens >= M
+    // read token 0 and scale it by 0.
     const int btok = g >> 1;
     const bool bpart_lo = g & 1;
     const float* xb = p.x + static_cast<int64_t>(btok < M ? btok : 0) * p.K;
-    float bscale = 1.0f;
+    float bscale = 0.0f, un_t = 1.0f;
 #pragma unroll
-    for (int m = 0; m < M; ++m)
+    for (int m = 0; m < M; ++m) {
         if (m == btok) bscale = xscale[m];
+        if (m == t) un_t = xunscale[m];
+    }
+    // Row offsets of this lane's four rows inside a step and their swizzled chunk offsets.
+    int roff[4], soff[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        roff[i] = 2 * t + (i & 1) + 8 * (i >> 1);
+        soff[i] = roff[i] * kTileBytes + ((g ^ (roff[i] & 7)) << 4);
+    }
 
     float y[32];  // token t: [0,16) low-nibble columns 16g + jj, [16,32) high-nibble columns
 #pragma unroll
     for (int j = 0; j < 32; ++j) y[j] = 0.0f;
     float c[16][4];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0.0f;
 
     const uint32_t h1024 = p.h1024, h16 = p.h_sixteenth, hm64 = p.h_neg64;
     bool ok = true;
     int gi = g_first;
     int group_end = min((gi + 1) * p.gs, r_end);
-    for (int st = 0; st < n_steps; ++st) {
-        const int slot = st % kStages;
+    bool fresh = true;  // the next step starts a new accumulation run
+    for (int st = 0; st < n_stages; ++st) {
+        const int slot = st & (kStages - 1);
         if (ok && !mbar_wait_bounded(bars + 8 * slot, (st / kStages) & 1)) {
             ok = false;
             if (lane == 0) atomicOr(p.err, 1);
         }
         __syncwarp();  // every lane is done with the stage consumed at st - 1
-        if (lane == 0 && ok && st + kStages - 1 < n_steps) {
+        if (lane == 0 && ok && st + kStages - 1 < n_stages) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             issue(st + kStages - 1);
         }
-        const int row0 = r_begin + st * kStep;
-        // B fragment: rows 2t, 2t+1 (b0) and 2t+8, 2t+9 (b1) of x' for this lane's column.
-        uint32_t b0 = 0u, b1 = 0u;
-        if (btok < M) {
+        const unsigned char* stage = ring + slot * kStageBytes;
+#pragma unroll
+        for (int ks = 0; ks < kRowsPerStage / kStep; ++ks) {
+            const int row0 = r_begin + st * kRowsPerStage + ks * kStep;
             float xv[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) xv[i] = __ldg(xb + row0 + 2 * t + (i & 1) + 8 * (i >> 1)) * bscale;
+            for (int i = 0; i < 4; ++i) xv[i] = __ldg(xb + row0 + roff[i]) * bscale;
             float hv[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const float h = __half2float(__float2half_rn(xv[i]));
                 hv[i] = bpart_lo ? xv[i] - h : h;
             }
-            b0 = pack_h2(hv[0], hv[1]);
-            b1 = pack_h2(hv[2], hv[3]);
-        }
-        // A: chunk g of rows 2t, 2t+1, 2t+8, 2t+9 (128-byte swizzle: chunk ^ (row & 7)).
-        const unsigned char* stage = ring + slot * kStageBytes;
-        uint4 w[4];
+            const uint32_t b0 = pack_h2(hv[0], hv[1]);
+            const uint32_t b1 = pack_h2(hv[2], hv[3]);
+            uint4 w[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = 2 * t + (i & 1) + 8 * (i >> 1);
-            w[i] = *reinterpret_cast<const uint4*>(stage + r * kTileBytes + ((g ^ (r & 7)) << 4));
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t w0 = (&w[0].x)[k], w1 = (&w[1].x)[k], w2 = (&w[2].x)[k], w3 = (&w[3].x)[k];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint32_t sel = static_cast<uint32_t>(j | ((4 + j) << 8));
-                const uint32_t p01 = prmt(w0, w1, sel);  // byte j of rows 2t and 2t+1 at bits 0-7 / 16-23
-                const uint32_t p23 = prmt(w2, w3, sel);
-                uint32_t a[4];
-                a[0] = hsub2(lop3_and_or<0x000F000Fu>(p01, h1024), h1024);                 // low nibbles
-                a[1] = hfma2(lop3_and_or<0x00F000F0u>(p01, h1024), h16, hm64);             // high nibbles
-                a[2] = hsub2(lop3_and_or<0x000F000Fu>(p23, h1024), h1024);
-                a[3] = hfma2(lop3_and_or<0x00F000F0u>(p23, h1024), h16, hm64);
-                mma_16816(c[4 * k + j], a, b0, b1);
+            for (int i = 0; i < 4; ++i)
+                w[i] = *reinterpret_cast<const uint4*>(stage + ks * kStep * kTileBytes + soff[i]);
+            if (fresh) {
+                mma_step<true>(c, w, b0, b1, h1024, h16, hm64);
+                fresh = false;
+            } else {
+                mma_step<false>(c, w, b0, b1, h1024, h16, hm64);
             }
         }
-        if (row0 + kStep >= group_end) {
+        if (r_begin + (st + 1) * kRowsPerStage >= group_end) {
             // Group epilogue for token t: y += scale * (2^-s * (C_hi + C_lo) - zero * rowSum).
+            // Columns beyond the tile's bytes hold stale slot data; their
+            // outputs are never written.
             if (t < M) {
-                const unsigned char* sl = slots + ((gi - g_first) % kStages) * kScaleSlotBytes;
-                const float* s_lo = reinterpret_cast<const float*>(sl);
-                const float* s_hi = reinterpret_cast<const float*>(sl + kTileBytes * 4);
-                const uint8_t* z_lo = sl + kTileBytes * 8;
-                const uint8_t* z_hi = sl + kTileBytes * 9;
-                float un = 1.0f;
-#pragma unroll
-                for (int m = 0; m < M; ++m)
-                    if (m == t) un = xunscale[m];
+                const unsigned char* sl = slots + ((gi - g_first) & (kStages - 1)) * kScaleSlotBytes;
+                const float4* s_lo = reinterpret_cast<const float4*>(sl) + 4 * g;
+                const float4* s_hi = reinterpret_cast<const float4*>(sl + kTileBytes * 4) + 4 * g;
+                const uint4 z_lo = *reinterpret_cast<const uint4*>(sl + kTileBytes * 8 + 16 * g);
+                const uint4 z_hi = *reinterpret_cast<const uint4*>(sl + kTileBytes * 9 + 16 * g);
                 const float rs = rs_s[(gi - g_first) * 4 + t];
 #pragma unroll
-                for (int jj = 0; jj < 16; ++jj) {
-                    const int col = 16 * g + jj;
-                    if (col < tile_cols) {
-                        y[jj] = fmaf(s_lo[col], fmaf(c[jj][0] + c[jj][1], un, -static_cast<float>(z_lo[col]) * rs), y[jj]);
-                        y[16 + jj] = fmaf(s_hi[col],
-                                          fmaf(c[jj][2] + c[jj][3], un, -static_cast<float>(z_hi[col]) * rs),
-                                          y[16 + jj]);
+                for (int q = 0; q < 4; ++q) {
+                    const float4 sl4 = s_lo[q], sh4 = s_hi[q];
+                    const uint32_t zl = (&z_lo.x)[q], zh = (&z_hi.x)[q];
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const int jj = 4 * q + b;
+                        // byte b -> float via the 2^23 pattern: [b, 0, 0, 0x4B] - 2^23
+                        const uint32_t sel = static_cast<uint32_t>(b | (4 << 4) | (4 << 8) | (7 << 12));
+                        const float zlf = __uint_as_float(prmt(zl, 0x4B000000u, sel)) - 8388608.0f;
+                        const float zhf = __uint_as_float(prmt(zh, 0x4B000000u, sel)) - 8388608.0f;
+                        const float sl_b = (&sl4.x)[b], sh_b = (&sh4.x)[b];
+                        y[jj] = fmaf(sl_b, fmaf(c[jj][0] + c[jj][1], un_t, -zlf * rs), y[jj]);
+                        y[16 + jj] = fmaf(sh_b, fmaf(c[jj][2] + c[jj][3], un_t, -zhf * rs), y[16 + jj]);
                     }
                 }
             }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0.0f;
+            fresh = true;
             ++gi;
             group_end = min((gi + 1) * p.gs, r_end);
         }
@@ -426,16 +459,22 @@ MmaOverrides& mma_overrides() {
 }
 
 // One CTA per SM: the largest cluster along K (<= 16) that keeps the grid in one
-// wave and >= 32 rows per warp.
+// wave and >= 64 rows per warp.
 int choose_ck(int R, int K, int sm_count) {
     const int tiles = (R + kTileBytes - 1) / kTileBytes;
     int best = 1;
     for (int ck = 1; ck <= 16; ++ck) {
         if (tiles * ck > sm_count) break;
-        if (K / (kWarps * ck) < 32) break;
+        if (K / (kWarps * ck) < 64) break;
         best = ck;
     }
     return best;
+}
+
+int slice_rows_for(int K, int ck) {
+    const int slices = kWarps * ck;
+    const int per = (K + slices - 1) / slices;
+    return (per + kRowsPerStage - 1) / kRowsPerStage * kRowsPerStage;
 }
 
 template <int M>
@@ -449,9 +488,7 @@ cudaError_t launch_m(const QView& w, const MmaParams& p, int ck, cudaStream_t s)
         if (e != cudaSuccess) return e;
     }
     MmaParams q = p;
-    const int slices = kWarps * ck;
-    const int per = (p.K + slices - 1) / slices;
-    q.slice_rows = (per + kStep - 1) / kStep * kStep;
+    q.slice_rows = slice_rows_for(p.K, ck);
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3((p.R + kTileBytes - 1) / kTileBytes, ck, 1);
     lc.blockDim = dim3(kThreads, 1, 1);
@@ -475,12 +512,11 @@ void set_mma_tuning(int cluster_k) { mma_overrides().ck = cluster_k; }
 
 bool gemv_mma_supported(const QView& w, int32_t m, const float* a) {
     if (w.bits != 4 || m < 1 || m > kGemvMmaMaxM || w.tmap_mma == nullptr) return false;
-    if (w.columns % 32 != 0 || w.rows % kStep != 0 || w.group_size % kStep != 0) return false;
+    if (w.columns % 32 != 0 || w.rows % kRowsPerStage != 0 || w.group_size % kRowsPerStage != 0) return false;
     if (reinterpret_cast<uintptr_t>(a) % 4 != 0) return false;
     // Every warp slice must keep its group row sums in shared memory, at the
     // latest with the largest cluster (16 CTAs x 8 warps).
-    const int per = ((w.rows + 16 * kWarps - 1) / (16 * kWarps) + kStep - 1) / kStep * kStep;
-    return per / w.group_size + 2 <= kMaxSliceGroups;
+    return slice_rows_for(w.rows, 16) / w.group_size + 2 <= kMaxSliceGroups;
 }
 
 cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s) {
@@ -504,7 +540,7 @@ cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, c
     const int o = mma_overrides().ck;
     if (o >= 1 && o <= 16) ck = o;
     // Each warp slice must fit kMaxSliceGroups group row sums.
-    while (ck < 16 && ((p.K + kWarps * ck - 1) / (kWarps * ck)) / p.gs + 2 > kMaxSliceGroups) ++ck;
+    while (ck < 16 && slice_rows_for(p.K, ck) / p.gs + 2 > kMaxSliceGroups) ++ck;
     switch (a.m) {
         case 1: return launch_m<1>(w, p, ck, s);
         case 2: return launch_m<2>(w, p, ck, s);

@@ -38,7 +38,7 @@ struct kt_qweight {
     alignas(64) CUtensorMap tmap_w128;
     alignas(64) CUtensorMap tmap_w256;
     bool has_tmaps = false;
-    // Box of 16 rows x 128 bytes with the 128-byte swizzle (INT4 tensor-core
+    // Box of 32 rows x 128 bytes with the 128-byte swizzle (INT4 tensor-core
     // GEMV; built when bytes_per_row % 16 == 0 and bytes_per_row >= 128).
     alignas(64) CUtensorMap tmap_mma;
     bool has_tmap_mma = false;
