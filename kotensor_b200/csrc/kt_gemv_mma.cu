@@ -7,43 +7,52 @@
 // FMA kernel needs >= 2.4 instructions per weight (unpack + FMA) and measured
 // 3.4, so it is issue-bound well below the HBM roofline.  Here the products
 // run on mma.sync.m16n8k16 (fp16 inputs, fp32 accumulate) and the CUDA cores
-// only turn nibbles into fp16 operands: 10 instructions per 8 weights.
+// only turn nibbles into fp16 operands: 6 instructions per 256 weights.
 //
-// Exactness.  The A operand holds the raw nibbles q as fp16 integers 0..15
-// (exact): two bytes of two rows are interleaved with PRMT, LOP3 masks each
-// nibble into the mantissa of 1024.0h (0x6400), and one f16x2 op removes the
-// 1024 (and the 16x of the high nibble) exactly.  The B operand holds x split
-// into two fp16 terms, hi = fp16(x') and lo = fp16(x' - hi), with
-// x' = x * 2^s scaled by a power of two per (warp slice, row of x) so hi is in
-// [2^14, 2^15) for the largest |x| -- a 22-bit significand, products exact,
-// fp32 accumulation.  Each group's accumulator is then combined as in the
-// reference (combineGroup, MatMul.kt:804-828):
-//     y[j] += scale[g,j] * (2^-s * (C_hi + C_lo) - zero[g,j] * sum_l x_l)
-// with sum_l x_l accumulated in fp32 from the unscaled x.
+// Exactness.  The A operand holds the raw nibbles as exact fp16 values: two
+// bytes of two rows are interleaved with PRMT and LOP3 masks each nibble into
+// the mantissa of 1024.0h (0x6400), giving 1024 + q (low nibble) and
+// 1024 + 16 q (high nibble).  The offsets are removed per group with the sum
+// of x.  The B operand holds x split into two fp16 terms, hi = fp16(x') and
+// lo = fp16(x' - hi), with x' = x * 2^s and 2^s a power of two per (slice,
+// token) that puts the slice's max|x| in [2^14, 2^15): a 22-bit significand,
+// exact products, fp32 accumulation.  Each group's accumulator C is then
+// combined as in the reference (combineGroup, MatMul.kt:804-828):
+//     y[j] += scale[g,j] * (2^-s C - (1024 + zero[g,j]) * sum_l x_l)    (low)
+//     y[j] += scale[g,j] * (2^-s C / 16 - (64 + zero[g,j]) * sum_l x_l) (high)
+// with sum_l x_l the group's sum of (hi + lo) * 2^-s, i.e. of what the tensor
+// cores saw.
 //
-// Tiling.  A CTA owns 128 packed bytes of every row (INT4: 128 low-nibble
-// columns and 128 high-nibble columns) and 8 warps split K into contiguous
-// slices (multiples of 16 rows); a thread-block cluster of CK CTAs along K
-// splits it further.  In an m16n8k16 tile, A row g (g = lane/4) is the low
-// nibble of one byte and row g+8 the high nibble of the same byte; lane
-// t = lane%4 holds k-slots 2t, 2t+1, 2t+8, 2t+9, i.e. those rows of the
-// 16-row step, so a thread reads one 16-byte chunk of four rows and feeds 16
-// MMAs from it (with the 128-byte swizzle, the 8 lanes of each shared-load
-// phase hit 8 different bank groups).  B column n = 2*token + part
-// (part 0 = hi, 1 = lo), so C columns 2t, 2t+1 of lane (g, t) are token t.
+// Tiling.  A CTA owns 128 packed bytes of every row (INT4: 128 low-nibble and
+// 128 high-nibble columns).  Its 16 warps form 8 pairs; each pair owns a
+// contiguous K-slice (a multiple of 32 rows) and its two warps the two 64-byte
+// halves of the tile row.  A thread-block cluster of CK CTAs along K splits K
+// further.  In an m16n8k16 tile, A row g (g = lane/4) is the low nibble of one
+// byte and row g+8 the high nibble of the same byte; lane t = lane%4 holds
+// k-slots 2t, 2t+1, 2t+8, 2t+9, i.e. those rows of the 16-row step, so a
+// thread reads one 8-byte chunk of four rows and feeds 8 MMAs from it.  B
+// column n = 2q + part (part 0 = hi, 1 = lo) carries token q % M (tokens are
+// replicated when M < 4), so C columns 2t, 2t+1 of lane (g, t) are token t % M.
 //
-// Streaming.  Each warp owns a ring of kStages stages of 32 rows x 128 bytes,
-// filled by lane 0 with one 2-D TMA copy per stage (128-byte swizzle) plus, on
-// the first stage of each group, 1-D bulk copies of that group's scales and
-// zero points into a per-warp ring of group slots.  Completion is tracked by one mbarrier per
-// stage; every wait is bounded (globaltimer) and a timeout sets the context's
-// error word.  The kernel is launched with programmatic stream serialization:
-// the weight prefetch overlaps the previous kernel, griddepcontrol.wait orders
-// the reads of x and the writes of y after it.
+// Activations.  Once per slice the pair loads its rows of x, finds the power
+// of two per token, and writes the fp16 terms (padded rows, conflict-free B
+// loads) and the 32-row chunk sums of x to shared memory; the weight ring is
+// already filling meanwhile.
+//
+// Streaming.  Each pair owns a ring of kStages stages of 32 rows x 128 bytes,
+// filled by one lane with one 2-D TMA copy per stage (128-byte swizzle) plus,
+// on the first stage of each group, 1-D bulk copies of that group's scales and
+// zero points into a ring of group slots.  A "full" mbarrier per stage tracks
+// the copies and an "empty" mbarrier per stage the release by both warps; every
+// wait is bounded (globaltimer) and a timeout sets the context's error word and
+// drains the copies still in flight before the CTA exits.  The kernel is
+// launched with programmatic stream serialization: the weight prefetch overlaps
+// the previous kernel, griddepcontrol.wait orders the reads of x and the writes
+// of y after it.
 //
 // Reduction order (deterministic, no atomics, no global scratch): group
-// partials in registers per thread in row order; the 8 warps of a CTA through
-// shared memory in warp order; the CK CTAs of a cluster through distributed
+// partials in registers per thread in row order; the 8 slices of a CTA through
+// shared memory in slice order; the CK CTAs of a cluster through distributed
 // shared memory in rank order.
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
@@ -65,22 +74,31 @@ constexpr int kStep = 16;               // rows per MMA step
 constexpr int kRowsPerStage = 32;       // rows per TMA stage (two MMA steps)
 constexpr int kTileBytes = 128;         // packed bytes per CTA tile row
 constexpr int kStages = 4;              // stages per slice ring (also group slots)
-constexpr int kMaxSliceGroups = 128;
+constexpr int kMaxSliceRows = 384;      // rows of x a slice stages in shared memory
+constexpr int kMaxCluster = 16;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 constexpr int kStageBytes = kRowsPerStage * kTileBytes;               // 4096
 constexpr int kScaleSlotBytes = 2 * kTileBytes * 4 + 2 * kTileBytes;  // 1280
 constexpr int kRingBytes = kStages * kStageBytes;                     // per slice
 constexpr int kSlotRingBytes = kStages * kScaleSlotBytes;             // per slice
-constexpr int kRsBytes = kMaxSliceGroups * 4 * 4;                     // per slice: rowsums [group][token]
 constexpr int kRedBytes = kWarps * 16 * 32 * 4;                       // reuses the rings
 constexpr int kMainBytes = kPairs * kRingBytes;
 constexpr int kPartBytes = 4 * 2 * kTileBytes * 4;
-constexpr size_t kSmemBytes = static_cast<size_t>(kMainBytes) + kPairs * kSlotRingBytes + kPairs * kRsBytes +
-                              kPartBytes + kPairs * kStages * 16;
+// staged x per slice: [token][part][kXsStride] fp16; the 8-half pad puts the
+// 8 (token, part) rows a warp reads at once in different banks
+constexpr int kXsStride = kMaxSliceRows + 8;
+constexpr int kXsBytes = 4 * 2 * kXsStride * 2;
+constexpr int kChunkBytes = (kMaxSliceRows / kRowsPerStage) * 4 * 4;  // chunk sums [chunk][token]
+constexpr int kXmaxBytes = 2 * 4 * 4;                                 // [warp of the pair][token]
+constexpr int kXsPairBytes = kXsBytes + kChunkBytes + kXmaxBytes;
+constexpr size_t kSmemBytes = static_cast<size_t>(kMainBytes) + kPairs * kSlotRingBytes + kPartBytes +
+                              kPairs * kXsPairBytes + kPairs * kStages * 16;
 static_assert(kRedBytes <= kMainBytes, "reduction buffer must fit in the rings");
 static_assert(kRowsPerStage == 32, "the TMA box of QView::tmap_mma is 32 rows");
-
+static_assert(kMaxSliceRows % 64 == 0, "a pair stages its slice 64 rows at a time");
+static_assert(kXsPairBytes % 16 == 0, "slice staging areas stay 16-byte aligned");
+static_assert(kSmemBytes <= 232448, "one CTA per SM");
 
 struct MmaParams {
     const float* scales;
@@ -90,7 +108,7 @@ struct MmaParams {
     const float* bias;
     int32_t* err;
     int32_t K, N, R, gs;
-    int32_t slice_rows;    // multiple of kRowsPerStage
+    int32_t slice_rows;    // multiple of kRowsPerStage, <= kMaxSliceRows
     uint32_t h1024;        // 0x64006400: f16x2 {1024, 1024}
     float alpha;
     int32_t accumulate;
@@ -166,23 +184,6 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4],
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-    const __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-
-
-// A fragments of the 16 MMAs of one 16-row step from the four 16-byte row
-// chunks w[0..3] (rows 2t, 2t+1, 2t+8, 2t+9), MMA i = 4k + j <-> byte 4k + j.
-// Two-term fp16 split of (v0, v1): the hi pair fp16(v) or the lo pair fp16(v - hi).
-__device__ __forceinline__ uint32_t split_part(float v0, float v1, bool lo) {
-    const __half2 h = __floats2half2_rn(v0, v1);
-    const float2 hf = __half22float2(h);
-    const __half2 l = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
-    const __half2 r = lo ? l : h;
-    return *reinterpret_cast<const uint32_t*>(&r);
-}
 
 // The 8 MMAs of one 16-row step from the four 8-byte row chunks w[0..3]
 // (rows 2t, 2t+1, 2t+8, 2t+9); MMA i = 4k + j <-> byte 4k + j of the chunk.
@@ -213,7 +214,7 @@ __device__ __forceinline__ void pair_barrier(int pair) {
 }
 
 // Shared memory: rings[8 slices][NS][32][128] (later red[16][16][32]) |
-// slots[8][NS][1280] | rowsum[8][128][4] | part[4][256] | mbarriers[8][NS].
+// slots[8][NS][1280] | part[4][256] | x staging[8][kXsPairBytes] | mbarriers[8][2][NS].
 template <int M>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap, MmaParams p) {
@@ -237,11 +238,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     unsigned char* ring = smem + pair * kRingBytes;
     unsigned char* slots = smem + kMainBytes + pair * kSlotRingBytes;
-    float* rs_s = reinterpret_cast<float*>(smem + kMainBytes + kPairs * kSlotRingBytes) + pair * kMaxSliceGroups * 4;
-    float* part = reinterpret_cast<float*>(smem + kMainBytes + kPairs * kSlotRingBytes + kPairs * kRsBytes);
+    float* part = reinterpret_cast<float*>(smem + kMainBytes + kPairs * kSlotRingBytes);
+    unsigned char* xstage = smem + kMainBytes + kPairs * kSlotRingBytes + kPartBytes + pair * kXsPairBytes;
+    __half* xs = reinterpret_cast<__half*>(xstage);                      // [token][part][kXsStride]
+    float* chunk_sum = reinterpret_cast<float*>(xstage + kXsBytes);       // [chunk][4]
+    float* xmax = reinterpret_cast<float*>(xstage + kXsBytes + kChunkBytes);  // [2][4]
     // per slice: "full" mbarriers (TMA completion) then "empty" mbarriers (both warps released the slot)
-    const uint32_t bars = smem_u32(smem + kMainBytes + kPairs * kSlotRingBytes + kPairs * kRsBytes + kPartBytes) +
-                          pair * kStages * 16;
+    const uint32_t bars =
+        smem_u32(smem + kMainBytes + kPairs * kSlotRingBytes + kPartBytes + kPairs * kXsPairBytes) +
+        pair * kStages * 16;
     const uint32_t empty = bars + kStages * 8;
     const uint32_t ring_s = smem_u32(ring);
     const uint32_t slots_s = smem_u32(slots);
@@ -260,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // points into group slot (group - g_first) % NS.
     // Producer state: the next stage's first row, the next group to fetch and
     // the row where it starts (the slice's first stage always fetches).
-    int p_row = r_begin, p_gi = g_first, p_gstart = r_begin;
+    int p_row = r_begin, p_gi = g_first, p_gstart = r_begin, p_issued = 0;
     auto issue = [&](int st) {  // producer only, stages in order
         const int slot = st & (kStages - 1);
         const uint32_t bar = bars + 8 * slot;
@@ -279,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             p_gstart = p_gi * p.gs;
         }
         p_row += kRowsPerStage;
+        ++p_issued;
     };
     if (producer) {
         for (int s = 0; s < kStages - 1 && s < n_stages; ++s) issue(s);
@@ -286,49 +292,72 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_launch_dependents();
     pdl_wait();  // x and y below may belong to the previous kernel
 
-    // Slice prologue (both warps of the pair compute the scales; warp 0 of the
-    // pair writes the group row sums of exactly what the tensor cores see:
-    // hi + lo of x * 2^s, in fixed lane and shuffle order).
-    float xscale[M], xunscale[M];
+    // Stage this slice's rows of x: thread pt of the pair holds rows pt + 64 j.
+    const int pt = hw * 32 + lane;
+    const int n_rows = r_end - r_begin;
+    constexpr int kPer = kMaxSliceRows / 64;
+    float xv[M][kPer];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-        const float* xm = p.x + static_cast<int64_t>(m) * p.K;
+        const float* xm = p.x + static_cast<int64_t>(m) * p.K + r_begin;
         float mx = 0.0f;
-        for (int r = r_begin + lane; r < r_end; r += 32) mx = fmaxf(mx, fabsf(__ldg(xm + r)));
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int r = pt + 64 * j;
+            xv[m][j] = r < n_rows ? __ldg(xm + r) : 0.0f;
+            mx = fmaxf(mx, fabsf(xv[m][j]));
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        int sh = 14 - (mx > 0.0f ? ilogbf(mx) : 0);
-        sh = max(-126, min(126, sh));
-        xscale[m] = ldexpf(1.0f, sh);
-        xunscale[m] = ldexpf(1.0f, -sh);
-        if (hw == 0) {
-            for (int gi = g_first; gi * p.gs < r_end; ++gi) {
-                const int a0 = max(gi * p.gs, r_begin), a1 = min((gi + 1) * p.gs, r_end);
-                float s = 0.0f;
-                for (int r = a0 + lane; r < a1; r += 32) {
-                    const float v = __ldg(xm + r) * xscale[m];
-                    const float h = __half2float(__float2half_rn(v));
-                    s += h + __half2float(__float2half_rn(v - h));
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-                if (lane == 0) rs_s[(gi - g_first) * 4 + m] = s * xunscale[m];
-            }
-        }
+        if (lane == 0) xmax[hw * 4 + m] = mx;
     }
-    pair_barrier(pair);  // mbarrier init and row sums visible to both warps of the pair
-
-    // This lane's B column: token g/2, part g%2 (0 = hi, 1 = lo); tokens >= M
-    // read token 0 and scale it by 0.
-    const int btok = g >> 1;
-    const bool bpart_lo = g & 1;
-    const float* xb = p.x + static_cast<int64_t>(btok < M ? btok : 0) * p.K;
-    float bscale = 0.0f, un_t = 1.0f;
+    pair_barrier(pair);  // mbarrier init and the two warps' maxima
+    float unscale[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-        if (m == btok) bscale = xscale[m];
-        if (m == t) un_t = xunscale[m];
+        const float mx = fmaxf(xmax[m], xmax[4 + m]);
+        int sh = 14 - (mx > 0.0f ? ilogbf(mx) : 0);
+        sh = max(-126, min(126, sh));
+        const float sc = ldexpf(1.0f, sh);
+        unscale[m] = ldexpf(1.0f, -sh);
+        __half* hi = xs + (2 * m) * kXsStride;
+        __half* lo = hi + kXsStride;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int r = pt + 64 * j;
+            const float v = xv[m][j] * sc;
+            const __half h = __float2half_rn(v);
+            const __half l = __float2half_rn(v - __half2float(h));
+            if (r < n_rows) {
+                hi[r] = h;
+                lo[r] = l;
+            }
+            // chunk 2j + hw: the 32 rows this warp holds, summed in butterfly order
+            float s = __half2float(h) + __half2float(l);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == 0 && 64 * j + 32 * hw < n_rows) chunk_sum[(2 * j + hw) * 4 + m] = s * unscale[m];
+        }
     }
+    pair_barrier(pair);  // staged x visible to both warps of the pair
+
+    // B column n = 2 q + part (q = g/2, part = g%2: 0 = hi, 1 = lo) carries
+    // token q % M: with M < 4 each token is replicated into kRep column pairs,
+    // so the C columns 2t, 2t+1 of every lane t hold token t % M and the kRep
+    // lanes of a token split the group epilogue's columns between them.
+    // (M == 3 leaves q = 3 / lane t = 3 unused: B is 0 there.)
+    constexpr int kRep = M == 1 ? 4 : (M == 2 ? 2 : 1);
+    const int q = g >> 1;
+    const int btok = q % M;
+    const bool b_active = q < kRep * M;
+    const __half* xb = xs + (2 * btok + (g & 1)) * kXsStride;
+    const int ttok = t % M;
+    const bool t_active = t < kRep * M;
+    const int sub = t / M;  // which share of the columns this lane finishes
+    float un_t = unscale[0];
+#pragma unroll
+    for (int m = 1; m < M; ++m)
+        if (ttok == m) un_t = unscale[m];
     // This lane's four rows inside a step and their swizzled 8-byte offsets:
     // 16-byte chunk gb/2 of row r sits at chunk (gb/2) ^ (r & 7).
     int roff[4], soff[4];
@@ -338,22 +367,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         soff[i] = roff[i] * kTileBytes + (((gb >> 1) ^ (roff[i] & 7)) << 4) + 8 * (gb & 1);
     }
 
-    float y[16];  // token t: [0,8) low-nibble columns 8 gb + i, [8,16) high-nibble columns
+    // token t % M, bytes [sub*NB, (sub+1)*NB) of the chunk: [0,NB) low-nibble
+    // columns, [NB,2NB) high-nibble columns
+    constexpr int kNB = 8 / kRep;
+    float y[2 * kNB];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) y[j] = 0.0f;
+    for (int j = 0; j < 2 * kNB; ++j) y[j] = 0.0f;
     float c[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0.0f;
 
     const uint32_t h1024 = p.h1024;
+    float rs = 0.0f;  // this token's sum of x over the group's rows in this slice
     bool ok = true;
+    int done = 0;     // stages whose copies this lane saw complete
     int gi = g_first;
     int group_end = min((gi + 1) * p.gs, r_end);
     for (int st = 0; st < n_stages; ++st) {
         const int slot = st & (kStages - 1);
-        if (ok && !mbar_wait_bounded(bars + 8 * slot, (st / kStages) & 1)) {
-            ok = false;
-            if (lane == 0) atomicOr(p.err, 1);
+        if (ok) {
+            if (mbar_wait_bounded(bars + 8 * slot, (st / kStages) & 1)) {
+                done = st + 1;
+            } else {
+                ok = false;
+                if (lane == 0) atomicOr(p.err, 1);
+            }
         }
         if (producer && ok && st + kStages - 1 < n_stages) {
             // stage st + NS - 1 goes into the slot of stage st - 1 (unused when
@@ -370,12 +408,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const unsigned char* stage = ring + slot * kStageBytes;
 #pragma unroll
         for (int ks = 0; ks < kRowsPerStage / kStep; ++ks) {
-            const int row0 = r_begin + st * kRowsPerStage + ks * kStep;
-            // rows 2t, 2t+1 and 2t+8, 2t+9 are adjacent pairs: two 8-byte loads
-            const float2 xa = __ldg(reinterpret_cast<const float2*>(xb + row0 + roff[0]));
-            const float2 xc = __ldg(reinterpret_cast<const float2*>(xb + row0 + roff[2]));
-            const uint32_t b0 = split_part(xa.x * bscale, xa.y * bscale, bpart_lo);
-            const uint32_t b1 = split_part(xc.x * bscale, xc.y * bscale, bpart_lo);
+            const int row0 = st * kRowsPerStage + ks * kStep;  // inside the slice
+            // rows 2t, 2t+1 and 2t+8, 2t+9 are adjacent fp16 pairs: two 4-byte loads
+            uint32_t b0 = *reinterpret_cast<const uint32_t*>(xb + row0 + roff[0]);
+            uint32_t b1 = *reinterpret_cast<const uint32_t*>(xb + row0 + roff[2]);
+            if (!b_active) b0 = b1 = 0u;
             uint2 w[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -384,40 +421,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();  // every lane of this warp has read the stage
         if (lane == 0) mbar_arrive(empty + 8 * slot);
+        rs += chunk_sum[st * 4 + ttok];
         if (r_begin + (st + 1) * kRowsPerStage >= group_end) {
             // Group epilogue for token t:
             //   low:  y += scale * (2^-s C - (1024 + zero) rowSum)
             //   high: y += scale * (2^-s C / 16 - (64 + zero) rowSum)
             // Columns beyond the tile's bytes hold stale slot data; their
             // outputs are never written.
-            if (t < M) {
+            if (t_active) {
+                // this lane's share: bytes [i0, i0 + NB) of its 8-byte chunk
+                const int i0 = sub * kNB;
+                float cs[kNB][4];
+#pragma unroll
+                for (int e = 0; e < kNB; ++e)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        float v = c[e][k];
+#pragma unroll
+                        for (int s = 1; s < kRep; ++s)
+                            if (sub == s) v = c[s * kNB + e][k];
+                        cs[e][k] = v;
+                    }
                 const unsigned char* sl = slots + ((gi - g_first) & (kStages - 1)) * kScaleSlotBytes;
-                const float4* s_lo = reinterpret_cast<const float4*>(sl) + 2 * gb;
-                const float4* s_hi = reinterpret_cast<const float4*>(sl + kTileBytes * 4) + 2 * gb;
-                const uint2 z_lo = *reinterpret_cast<const uint2*>(sl + kTileBytes * 8 + 8 * gb);
-                const uint2 z_hi = *reinterpret_cast<const uint2*>(sl + kTileBytes * 9 + 8 * gb);
-                const float rs = rs_s[(gi - g_first) * 4 + t];
+                const float* s_lo = reinterpret_cast<const float*>(sl) + 8 * gb + i0;
+                const float* s_hi = reinterpret_cast<const float*>(sl + kTileBytes * 4) + 8 * gb + i0;
+                const uint8_t* z_lo = sl + kTileBytes * 8 + 8 * gb + i0;
+                const uint8_t* z_hi = sl + kTileBytes * 9 + 8 * gb + i0;
                 const float un16 = un_t * 0.0625f;
 #pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const float4 sl4 = s_lo[q], sh4 = s_hi[q];
-                    const uint32_t zl = (&z_lo.x)[q], zh = (&z_hi.x)[q];
-#pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        const int i = 4 * q + b;
-                        // byte b -> float via the 2^23 pattern: [b, 0, 0, 0x4B] - 2^23
-                        const uint32_t sel = static_cast<uint32_t>(b | (4 << 4) | (4 << 8) | (7 << 12));
-                        const float zlf = __uint_as_float(prmt(zl, 0x4B000000u, sel)) - 8388608.0f;
-                        const float zhf = __uint_as_float(prmt(zh, 0x4B000000u, sel)) - 8388608.0f;
-                        y[i] = fmaf((&sl4.x)[b], fmaf(c[i][0] + c[i][1], un_t, -(1024.0f + zlf) * rs), y[i]);
-                        y[8 + i] = fmaf((&sh4.x)[b], fmaf(c[i][2] + c[i][3], un16, -(64.0f + zhf) * rs), y[8 + i]);
-                    }
+                for (int e = 0; e < kNB; ++e) {
+                    const float zlf = static_cast<float>(z_lo[e]), zhf = static_cast<float>(z_hi[e]);
+                    y[e] = fmaf(s_lo[e], fmaf(cs[e][0] + cs[e][1], un_t, -(1024.0f + zlf) * rs), y[e]);
+                    y[kNB + e] = fmaf(s_hi[e], fmaf(cs[e][2] + cs[e][3], un16, -(64.0f + zhf) * rs), y[kNB + e]);
                 }
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0.0f;
+            rs = 0.0f;
             ++gi;
             group_end = min((gi + 1) * p.gs, r_end);
+        }
+    }
+    // After a timeout: wait (bounded) for this slice's copies still in flight
+    // before the rings are reused and before the CTA's shared memory is released.
+    if (producer) {
+        for (int s = done; s < p_issued; ++s) {
+            if (!mbar_wait_bounded(bars + 8 * (s & (kStages - 1)), (s / kStages) & 1)) break;
         }
     }
 
@@ -425,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     float* red = reinterpret_cast<float*>(smem);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) red[(warp * 16 + e) * 32 + lane] = y[e];
+    for (int e = 0; e < 2 * kNB; ++e) red[(warp * 2 * kNB + e) * 32 + lane] = y[e];
     __syncthreads();
     constexpr int CT = 2 * kTileBytes;  // 256 columns per tile: [0,128) low, [128,256) high
     for (int idx = tid; idx < M * CT; idx += kThreads) {
@@ -433,12 +482,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int hi = col >= kTileBytes;
         const int cb = hi ? col - kTileBytes : col;  // byte of the tile row
         const int cgb = cb >> 3, i = cb & 7;
-        const int e = (hi ? 8 : 0) + i;
-        const int ln = 4 * (cgb & 7) + m;
+        const int e = (hi ? kNB : 0) + i % kNB;
+        const int ln = 4 * (cgb & 7) + m + M * (i / kNB);
         const int hw_c = cgb >> 3;
         float v = 0.0f;
 #pragma unroll
-        for (int pr = 0; pr < kPairs; ++pr) v += red[((2 * pr + hw_c) * 16 + e) * 32 + ln];
+        for (int pr = 0; pr < kPairs; ++pr) v += red[((2 * pr + hw_c) * 2 * kNB + e) * 32 + ln];
         part[idx] = v;
     }
     // (2) CTAs of the cluster along K in rank order; rank r finishes columns [r*CT/CK, (r+1)*CT/CK).
@@ -454,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v;
         if (CK > 1) {
             v = 0.0f;
-            for (int q = 0; q < CK; ++q) v += cluster.map_shared_rank(part, q)[m * CT + col];
+            for (int r = 0; r < CK; ++r) v += cluster.map_shared_rank(part, r)[m * CT + col];
         } else {
             v = part[m * CT + col];
         }
@@ -481,13 +530,15 @@ MmaOverrides& mma_overrides() {
     return o;
 }
 
-// One CTA per SM: the largest cluster along K (<= 16) that keeps the grid in one
-// wave and >= 64 rows per warp.
-// Clusters of `ck` CTAs of this kernel that the device holds at once (cached;
-// clusters must fit in one GPC, so this is not sm_count / ck).
+// Clusters of `ck` CTAs of this kernel that the device holds at once (cached
+// per device; clusters must fit in one GPC, so this is not sm_count / ck).
 int max_active_clusters(int ck) {
-    static int cache[17] = {0};
-    if (cache[ck] != 0) return cache[ck];
+    constexpr int kMaxDevices = 64;
+    static int cache[kMaxDevices][kMaxCluster + 1] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int* slot = dev >= 0 && dev < kMaxDevices ? &cache[dev][ck] : nullptr;
+    if (slot != nullptr && *slot != 0) return *slot;
     auto kernel = gemv_mma_kernel<1>;
     int n = 0;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) ==
@@ -507,23 +558,31 @@ int max_active_clusters(int ck) {
         if (cudaOccupancyMaxActiveClusters(&n, kernel, &lc) != cudaSuccess) n = 0;
     }
     cudaGetLastError();  // a refused query only rules this cluster size out
-    cache[ck] = n > 0 ? n : -1;
-    return cache[ck];
+    n = n > 0 ? n : -1;
+    if (slot != nullptr) *slot = n;
+    return n;
 }
 
+// Smallest cluster along K whose slices fit the x staging area.
+int min_ck(int K) { return (K + kPairs * kMaxSliceRows - 1) / (kPairs * kMaxSliceRows); }
+
 // The largest cluster along K whose whole grid is co-resident in one wave and
-// that leaves >= 32 rows per slice.
+// that leaves >= 32 rows per slice; at least min_ck(K); 0 if no cluster size
+// the kernel needs can be placed.
 int choose_ck(int R, int K, int sm_count) {
     const int tiles = (R + kTileBytes - 1) / kTileBytes;
-    int best = 1;
-    for (int ck = 1; ck <= 16; ++ck) {
-        if (tiles * ck > sm_count) break;
-        if (K / (kPairs * ck) < 32) break;
-        if (tiles <= max_active_clusters(ck)) best = ck;
+    const int lo = std::max(1, min_ck(K));
+    int best = 0;
+    for (int ck = lo; ck <= kMaxCluster; ++ck) {
+        if (ck > lo && (tiles * ck > sm_count || K / (kPairs * ck) < 32)) break;
+        const int n = max_active_clusters(ck);
+        if (n <= 0) continue;
+        if (best == 0 || tiles <= n) best = ck;
     }
     return best;
 }
 
+// Rows per slice: a multiple of the stage height.
 int slice_rows_for(int K, int ck) {
     const int slices = kPairs * ck;
     const int per = (K + slices - 1) / slices;
@@ -564,12 +623,10 @@ cudaError_t launch_m(const QView& w, const MmaParams& p, int ck, cudaStream_t s)
 void set_mma_tuning(int cluster_k) { mma_overrides().ck = cluster_k; }
 
 bool gemv_mma_supported(const QView& w, int32_t m, const float* a) {
+    (void)a;
     if (w.bits != 4 || m < 1 || m > kGemvMmaMaxM || w.tmap_mma == nullptr) return false;
-    if (w.columns % 32 != 0 || w.rows % kRowsPerStage != 0 || w.group_size % kRowsPerStage != 0) return false;
-    if (reinterpret_cast<uintptr_t>(a) % 8 != 0) return false;  // paired 8-byte loads of x
-    // Every warp slice must keep its group row sums in shared memory, at the
-    // latest with the largest cluster (16 CTAs x 8 slices).
-    return slice_rows_for(w.rows, 16) / w.group_size + 2 <= kMaxSliceGroups;
+    return w.columns % 32 == 0 && w.rows % kRowsPerStage == 0 && w.group_size % kRowsPerStage == 0 &&
+           min_ck(w.rows) <= kMaxCluster;
 }
 
 cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s) {
@@ -589,9 +646,8 @@ cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, c
     p.accumulate = a.accumulate;
     int ck = choose_ck(p.R, p.K, sm_count);
     const int o = mma_overrides().ck;
-    if (o >= 1 && o <= 16) ck = o;
-    // Each warp slice must fit kMaxSliceGroups group row sums.
-    while (ck < 16 && slice_rows_for(p.K, ck) / p.gs + 2 > kMaxSliceGroups) ++ck;
+    if (o >= 1 && o <= kMaxCluster) ck = std::max(o, min_ck(p.K));
+    if (ck == 0) return cudaErrorInvalidConfiguration;
     switch (a.m) {
         case 1: return launch_m<1>(w, p, ck, s);
         case 2: return launch_m<2>(w, p, ck, s);
