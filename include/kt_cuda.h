@@ -142,9 +142,10 @@ kt_status kt_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float
 enum { KT_PATH_GEMV = 0, KT_PATH_GENERIC = 1, KT_PATH_TENSOR_CORE = 2, KT_PATH_GEMV_MMA = 3 };
 kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out);
 
-/* Pins the thread-block cluster size along K (1..16) of the INT4 tensor-core
- * GEMV; 0 restores the built-in choice (no reference counterpart). */
-kt_status kt_set_gemv_mma_tuning(int32_t cluster_k);
+/* Pins the number of K-splits per column tile (>= 1; raised to the minimum
+ * the shape needs) of the INT4 tensor-core GEMV; 0 restores the built-in
+ * choice (no reference counterpart). */
+kt_status kt_set_gemv_mma_tuning(int32_t k_splits);
 
 /* Pins the launch shape of the fp32 streaming kernel (no reference counterpart;
  * the reference's knobs are MatMul.numThreads / parallelThreshold,

@@ -9,6 +9,7 @@
 // m == 0 is a no-op.  No product path falls back to the CPU: every compute call
 // launches a CUDA kernel or fails.
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <new>
 #include <string>
@@ -102,6 +103,45 @@ void free_weight(kt_qweight* w) {
     delete w;
 }
 
+}  // namespace
+
+cudaError_t stream_workspace(kt_ctx* ctx, cudaStream_t s, size_t bytes, void** out) {
+    std::lock_guard<std::mutex> lock(ctx->ws_mutex);
+    kt_ctx::Workspace* hit = nullptr;
+    for (auto& ws : ctx->workspaces)
+        if (ws.stream == s) hit = &ws;
+    if (hit != nullptr && hit->bytes >= bytes) {
+        *out = hit->ptr;
+        return cudaSuccess;
+    }
+    // Grow to at least 1 MiB at a time.  cudaMalloc is not a stream operation;
+    // while `s` is being captured into a CUDA graph it is allowed in relaxed
+    // capture mode, and the zeroing below then becomes a node of that graph.
+    const size_t cap = std::max(bytes, static_cast<size_t>(1) << 20);
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, cap);
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(p, 0, cap, s);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return e;
+    }
+    if (hit != nullptr) {
+        ctx->retired.push_back(hit->ptr);  // queued launches may still use it
+        hit->ptr = p;
+        hit->bytes = cap;
+    } else {
+        ctx->workspaces.push_back({s, p, cap});
+    }
+    *out = p;
+    return cudaSuccess;
+}
+
+namespace {
+
 kt_status grow(float** buf, size_t* cap, size_t need) {
     if (*cap >= need) return KT_OK;
     cudaFree(*buf);
@@ -119,7 +159,13 @@ kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c,
     const MatmulArgs args{a, c, bias, m, accumulate, alpha, ctx->d_error};
     cudaError_t e;
     if (gemv_mma_supported(v, m, a)) {
-        e = launch_gemv_mma(v, args, ctx->sm_count, s);
+        const size_t need = gemv_mma_workspace_bytes(v, m, ctx->sm_count);
+        void* ws = nullptr;
+        if (need > 0) {
+            e = stream_workspace(ctx, s, need, &ws);
+            if (e != cudaSuccess) return cuda_fail(e, "qmatmul workspace");
+        }
+        e = launch_gemv_mma(v, args, ctx->sm_count, s, ws, need);
     } else if (gemv_fast_supported(v, m, a)) {
         e = launch_gemv(v, args, ctx->sm_count, s);
     } else {
@@ -229,7 +275,9 @@ kt_status kt_init(int32_t device, kt_ctx** out) {
 kt_status kt_destroy(kt_ctx* ctx) {
     if (!ctx) return KT_OK;
     cudaSetDevice(ctx->device);
-    cudaStreamSynchronize(ctx->stream);
+    cudaDeviceSynchronize();  // workspaces may be in use on any stream
+    for (auto& ws : ctx->workspaces) cudaFree(ws.ptr);
+    for (void* p : ctx->retired) cudaFree(p);
     cudaFree(ctx->h2d_a);
     cudaFree(ctx->d2h_c);
     cudaFree(ctx->bias_buf);
@@ -431,8 +479,8 @@ kt_status kt_set_gemv_tuning(int32_t lane_bytes, int32_t cluster_k) {
     return KT_OK;
 }
 
-kt_status kt_set_gemv_mma_tuning(int32_t cluster_k) {
-    set_mma_tuning(cluster_k);
+kt_status kt_set_gemv_mma_tuning(int32_t k_splits) {
+    set_mma_tuning(k_splits);
     return KT_OK;
 }
 

@@ -54,7 +54,6 @@
 // partials in registers per thread in row order; the 8 slices of a CTA through
 // shared memory in slice order; the CK CTAs of a cluster through distributed
 // shared memory in rank order.
-#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -62,20 +61,17 @@
 
 #include "kt_internal.h"
 
-namespace cg = cooperative_groups;
-
 namespace kt {
 namespace {
 
-constexpr int kPairs = 8;               // K-slices per CTA; two warps (column halves) per slice
+constexpr int kPairs = 4;               // K-slices per CTA; two warps (column halves) per slice
 constexpr int kWarps = 2 * kPairs;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStep = 16;               // rows per MMA step
 constexpr int kRowsPerStage = 32;       // rows per TMA stage (two MMA steps)
 constexpr int kTileBytes = 128;         // packed bytes per CTA tile row
 constexpr int kStages = 4;              // stages per slice ring (also group slots)
-constexpr int kMaxSliceRows = 384;      // rows of x a slice stages in shared memory
-constexpr int kMaxCluster = 16;
+constexpr int kXsRows = 1024;           // token-rows of x a slice stages in shared memory
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 constexpr int kStageBytes = kRowsPerStage * kTileBytes;               // 4096
@@ -85,20 +81,27 @@ constexpr int kSlotRingBytes = kStages * kScaleSlotBytes;             // per sli
 constexpr int kRedBytes = kWarps * 16 * 32 * 4;                       // reuses the rings
 constexpr int kMainBytes = kPairs * kRingBytes;
 constexpr int kPartBytes = 4 * 2 * kTileBytes * 4;
-// staged x per slice: [token][part][kXsStride] fp16; the 8-half pad puts the
-// 8 (token, part) rows a warp reads at once in different banks
-constexpr int kXsStride = kMaxSliceRows + 8;
-constexpr int kXsBytes = 4 * 2 * kXsStride * 2;
-constexpr int kChunkBytes = (kMaxSliceRows / kRowsPerStage) * 4 * 4;  // chunk sums [chunk][token]
+// Rows of one slice for M tokens (a multiple of 64).
+template <int M>
+__host__ __device__ constexpr int max_slice_rows() { return kXsRows / M / 64 * 64; }
+// staged x per slice: [token][part][stride] fp16; the 8-half pad puts the 8
+// (token, part) rows a warp reads at once in different banks
+template <int M>
+__host__ __device__ constexpr int xs_stride() { return max_slice_rows<M>() + 8; }
+template <int M>
+__host__ __device__ constexpr int xs_bytes() { return M * 2 * xs_stride<M>() * 2; }
+constexpr int kXsBytes = 4224;  // the largest xs_bytes<M>() over M = 1..4
+constexpr int kChunkBytes = kXsRows / kRowsPerStage * 4;  // chunk sums [chunk][token]
 constexpr int kXmaxBytes = 2 * 4 * 4;                                 // [warp of the pair][token]
 constexpr int kXsPairBytes = kXsBytes + kChunkBytes + kXmaxBytes;
 constexpr size_t kSmemBytes = static_cast<size_t>(kMainBytes) + kPairs * kSlotRingBytes + kPartBytes +
                               kPairs * kXsPairBytes + kPairs * kStages * 16;
 static_assert(kRedBytes <= kMainBytes, "reduction buffer must fit in the rings");
 static_assert(kRowsPerStage == 32, "the TMA box of QView::tmap_mma is 32 rows");
-static_assert(kMaxSliceRows % 64 == 0, "a pair stages its slice 64 rows at a time");
+static_assert(xs_bytes<1>() <= kXsBytes && xs_bytes<2>() <= kXsBytes && xs_bytes<3>() <= kXsBytes &&
+                  xs_bytes<4>() == kXsBytes, "x staging area");
 static_assert(kXsPairBytes % 16 == 0, "slice staging areas stay 16-byte aligned");
-static_assert(kSmemBytes <= 232448, "one CTA per SM");
+static_assert(2 * (kSmemBytes + 1024) <= 233472, "two CTAs per SM");
 
 struct MmaParams {
     const float* scales;
@@ -108,10 +111,13 @@ struct MmaParams {
     const float* bias;
     int32_t* err;
     int32_t K, N, R, gs;
-    int32_t slice_rows;    // multiple of kRowsPerStage, <= kMaxSliceRows
     uint32_t h1024;        // 0x64006400: f16x2 {1024, 1024}
     float alpha;
     int32_t accumulate;
+    // split-K (gridDim.y > 1): per-CTA partial tiles and per-tile arrival
+    // counters (zero on entry, left zero on exit)
+    float* partials;       // [tiles][splits][M][256]
+    int32_t* tickets;      // [tiles]
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -162,6 +168,11 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
+}
+__device__ __forceinline__ int atomic_add_acq_rel(int32_t* p, int v) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
@@ -216,7 +227,7 @@ __device__ __forceinline__ void pair_barrier(int pair) {
 // Shared memory: rings[8 slices][NS][32][128] (later red[16][16][32]) |
 // slots[8][NS][1280] | part[4][256] | x staging[8][kXsPairBytes] | mbarriers[8][2][NS].
 template <int M>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     gemv_mma_kernel(const __grid_constant__ CUtensorMap tmap, MmaParams p) {
     extern __shared__ __align__(1024) unsigned char smem[];
     const int tid = threadIdx.x;
@@ -231,17 +242,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tile_cols = min(kTileBytes, p.R - tile_b0);  // packed bytes of this tile inside the row
     const int half = p.R;
 
+    // K-slices: the K/32 stages spread evenly over splits x kPairs slices
+    // (the host keeps every slice within max_slice_rows<M>())
+    const int n_slices = gridDim.y * kPairs;
     const int slice = blockIdx.y * kPairs + pair;
-    const int r_begin = min(slice * p.slice_rows, p.K);
-    const int r_end = min(r_begin + p.slice_rows, p.K);
-    const int n_stages = (r_end - r_begin) / kRowsPerStage;  // K and slices are multiples of kRowsPerStage
+    const int k_stages = p.K / kRowsPerStage;
+    const int s_begin = static_cast<int>(static_cast<int64_t>(slice) * k_stages / n_slices);
+    const int s_end = static_cast<int>(static_cast<int64_t>(slice + 1) * k_stages / n_slices);
+    const int r_begin = s_begin * kRowsPerStage;
+    const int r_end = s_end * kRowsPerStage;
+    const int n_stages = s_end - s_begin;
 
     unsigned char* ring = smem + pair * kRingBytes;
     unsigned char* slots = smem + kMainBytes + pair * kSlotRingBytes;
     float* part = reinterpret_cast<float*>(smem + kMainBytes + kPairs * kSlotRingBytes);
     unsigned char* xstage = smem + kMainBytes + kPairs * kSlotRingBytes + kPartBytes + pair * kXsPairBytes;
     __half* xs = reinterpret_cast<__half*>(xstage);                      // [token][part][kXsStride]
-    float* chunk_sum = reinterpret_cast<float*>(xstage + kXsBytes);       // [chunk][4]
+    float* chunk_sum = reinterpret_cast<float*>(xstage + kXsBytes);       // [chunk][M]
     float* xmax = reinterpret_cast<float*>(xstage + kXsBytes + kChunkBytes);  // [2][4]
     // per slice: "full" mbarriers (TMA completion) then "empty" mbarriers (both warps released the slot)
     const uint32_t bars =
@@ -260,34 +277,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    __syncwarp();
     // Stage st: rows [r_begin + 32 st, +32) into ring slot st % NS; a stage that
     // starts a group (or the slice) also brings the group's scales and zero
     // points into group slot (group - g_first) % NS.
     // Producer state: the next stage's first row, the next group to fetch and
     // the row where it starts (the slice's first stage always fetches).
     int p_row = r_begin, p_gi = g_first, p_gstart = r_begin, p_issued = 0;
-    auto issue = [&](int st) {  // producer only, stages in order
+    // Issued by the whole warp 0 of the pair, stages in order: lane 0 arms the
+    // stage's mbarrier and copies the weights, lanes 1-4 copy a new group's
+    // low / high scales and zero points (complete_tx before the arming
+    // arrive cannot complete the phase: the arrive is still pending).
+    const uint32_t sbytes = static_cast<uint32_t>(tile_cols) * 10;  // 2 x fp32 scales + 2 x u8 zeros
+    const uint32_t lane_off = lane <= 2 ? (lane - 1) * kTileBytes * 4 : kTileBytes * (5 + lane);
+    const uint32_t lane_bytes = lane <= 2 ? tile_cols * 4 : tile_cols;
+    const unsigned char* lane_src =
+        lane <= 2 ? reinterpret_cast<const unsigned char*>(p.scales + tile_b0 + (lane == 2 ? half : 0))
+                  : p.zeros + tile_b0 + (lane == 4 ? half : 0);
+    const int lane_esize = lane <= 2 ? 4 : 1;
+    auto issue = [&](int st) {
         const int slot = st & (kStages - 1);
         const uint32_t bar = bars + 8 * slot;
         const bool group_start = p_row == p_gstart;
-        const uint32_t sbytes = static_cast<uint32_t>(tile_cols) * 10;  // 2 x fp32 scales + 2 x u8 zeros
-        mbar_expect_tx(bar, kStageBytes + (group_start ? sbytes : 0));
-        tma_load_2d(ring_s + slot * kStageBytes, &tmap, tile_b0, p_row, bar);
+        if (lane == 0) {
+            mbar_expect_tx(bar, kStageBytes + (group_start ? sbytes : 0));
+            tma_load_2d(ring_s + slot * kStageBytes, &tmap, tile_b0, p_row, bar);
+        }
         if (group_start) {
-            const uint32_t dst = slots_s + ((p_gi - g_first) & (kStages - 1)) * kScaleSlotBytes;
-            const int64_t go = static_cast<int64_t>(p_gi) * p.N;
-            bulk_load(dst, p.scales + go + tile_b0, tile_cols * 4, bar);
-            bulk_load(dst + kTileBytes * 4, p.scales + go + half + tile_b0, tile_cols * 4, bar);
-            bulk_load(dst + kTileBytes * 8, p.zeros + go + tile_b0, tile_cols, bar);
-            bulk_load(dst + kTileBytes * 9, p.zeros + go + half + tile_b0, tile_cols, bar);
+            if (lane >= 1 && lane <= 4) {
+                const uint32_t dst = slots_s + ((p_gi - g_first) & (kStages - 1)) * kScaleSlotBytes + lane_off;
+                bulk_load(dst, lane_src + static_cast<int64_t>(p_gi) * p.N * lane_esize, lane_bytes, bar);
+            }
             ++p_gi;
             p_gstart = p_gi * p.gs;
         }
         p_row += kRowsPerStage;
         ++p_issued;
     };
-    if (producer) {
-        for (int s = 0; s < kStages - 1 && s < n_stages; ++s) issue(s);
+    if (hw == 0) {
+        for (int s = 0; s < kStages && s < n_stages; ++s) issue(s);  // the whole ring, before the wait
     }
     pdl_launch_dependents();
     pdl_wait();  // x and y below may belong to the previous kernel
@@ -295,7 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Stage this slice's rows of x: thread pt of the pair holds rows pt + 64 j.
     const int pt = hw * 32 + lane;
     const int n_rows = r_end - r_begin;
-    constexpr int kPer = kMaxSliceRows / 64;
+    constexpr int kPer = max_slice_rows<M>() / 64;
+    constexpr int kXsStride = xs_stride<M>();
     float xv[M][kPer];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
@@ -306,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int r = pt + 64 * j;
             xv[m][j] = r < n_rows ? __ldg(xm + r) : 0.0f;
             mx = fmaxf(mx, fabsf(xv[m][j]));
+            if (64 * (j + 1) >= n_rows) break;  // pair-uniform
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -324,6 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __half* lo = hi + kXsStride;
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
+            if (64 * j >= n_rows) break;  // pair-uniform
             const int r = pt + 64 * j;
             const float v = xv[m][j] * sc;
             const __half h = __float2half_rn(v);
@@ -336,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float s = __half2float(h) + __half2float(l);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            if (lane == 0 && 64 * j + 32 * hw < n_rows) chunk_sum[(2 * j + hw) * 4 + m] = s * unscale[m];
+            if (lane == 0 && 64 * j + 32 * hw < n_rows) chunk_sum[(2 * j + hw) * M + m] = s * unscale[m];
         }
     }
     pair_barrier(pair);  // staged x visible to both warps of the pair
@@ -390,17 +421,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 done = st + 1;
             } else {
                 ok = false;
-                if (lane == 0) atomicOr(p.err, 1);
-            }
-        }
-        if (producer && ok && st + kStages - 1 < n_stages) {
-            // stage st + NS - 1 goes into the slot of stage st - 1 (unused when
-            // st == 0) once both warps have released that stage
-            const int prev = st - 1;
-            if (st > 0 && !mbar_wait_bounded(empty + 8 * (prev & (kStages - 1)), (prev / kStages) & 1)) {
-                ok = false;
                 atomicOr(p.err, 1);
-            } else {
+            }
+            ok = __all_sync(0xffffffffu, ok);  // the warp stops waiting together
+        }
+        if (hw == 0 && st > 0 && st + kStages - 1 < n_stages) {
+            // stage st + NS - 1 goes into the slot of stage st - 1 once both
+            // warps have released that stage (lane 0 waits for the warp)
+            const int prev = st - 1;
+            int go = 0;
+            if (lane == 0 && ok) go = mbar_wait_bounded(empty + 8 * (prev & (kStages - 1)), (prev / kStages) & 1) ? 1 : 2;
+            go = __shfl_sync(0xffffffffu, go, 0);
+            if (go == 2) {
+                ok = false;
+                if (lane == 0) atomicOr(p.err, 1);
+            } else if (go == 1) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 issue(st + kStages - 1);
             }
@@ -412,7 +447,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // rows 2t, 2t+1 and 2t+8, 2t+9 are adjacent fp16 pairs: two 4-byte loads
             uint32_t b0 = *reinterpret_cast<const uint32_t*>(xb + row0 + roff[0]);
             uint32_t b1 = *reinterpret_cast<const uint32_t*>(xb + row0 + roff[2]);
-            if (!b_active) b0 = b1 = 0u;
+            if constexpr (M == 3) {
+                if (!b_active) b0 = b1 = 0u;
+            }
             uint2 w[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -421,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();  // every lane of this warp has read the stage
         if (lane == 0) mbar_arrive(empty + 8 * slot);
-        rs += chunk_sum[st * 4 + ttok];
+        rs += chunk_sum[st * M + ttok];
         if (r_begin + (st + 1) * kRowsPerStage >= group_end) {
             // Group epilogue for token t:
             //   low:  y += scale * (2^-s C - (1024 + zero) rowSum)
@@ -490,23 +527,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int pr = 0; pr < kPairs; ++pr) v += red[((2 * pr + hw_c) * 2 * kNB + e) * 32 + ln];
         part[idx] = v;
     }
-    // (2) CTAs of the cluster along K in rank order; rank r finishes columns [r*CT/CK, (r+1)*CT/CK).
-    cg::cluster_group cluster = cg::this_cluster();
-    const int CK = gridDim.y;
-    if (CK > 1) cluster.sync(); else __syncthreads();
-    const int rank = CK > 1 ? static_cast<int>(cluster.block_rank()) : 0;
-    const int j0 = rank * CT / CK, j1 = (rank + 1) * CT / CK;
-    const int span = j1 - j0;
-    for (int idx = tid; idx < M * span; idx += kThreads) {
-        const int m = idx / span;
-        const int col = j0 + idx % span;
-        float v;
-        if (CK > 1) {
-            v = 0.0f;
-            for (int r = 0; r < CK; ++r) v += cluster.map_shared_rank(part, r)[m * CT + col];
-        } else {
-            v = part[m * CT + col];
-        }
+    __syncthreads();  // part[] complete
+    auto emit = [&](int idx, float v) {
+        const int m = idx / CT, col = idx % CT;
         const int byte = tile_b0 + (col < kTileBytes ? col : col - kTileBytes);
         const int out_col = col < kTileBytes ? byte : half + byte;
         if (byte < p.R && out_col < p.N) {
@@ -515,121 +538,150 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (p.bias != nullptr) r += p.bias[out_col];
             *out = r;
         }
+    };
+    const int S = gridDim.y;
+    if (S == 1) {
+        for (int idx = tid; idx < M * CT; idx += kThreads) emit(idx, part[idx]);
+        return;
     }
-    if (CK > 1) cluster.sync();  // keep this CTA's shared memory alive until every rank has read it
+    // (2) split-K: every CTA of the tile publishes its partial tile; the last
+    // to arrive sums all of them in split order and writes y.
+    // The CTA barrier orders every thread's partial stores before thread 0's
+    // acq_rel atomic (fence cumulativity), which publishes them at GPU scope
+    // and, in the last CTA, acquires the other CTAs' partials for the whole
+    // CTA through the second barrier.
+    __shared__ int s_last;
+    float* tile_parts = p.partials + static_cast<int64_t>(blockIdx.x) * S * (M * CT);
+    float* mine = tile_parts + static_cast<int64_t>(blockIdx.y) * (M * CT);
+    for (int idx = tid; idx < M * CT; idx += kThreads) __stcg(mine + idx, part[idx]);
+    __syncthreads();
+    if (tid == 0) s_last = atomic_add_acq_rel(p.tickets + blockIdx.x, 1) == S - 1;
+    __syncthreads();
+    if (!s_last) return;
+    for (int idx = tid; idx < M * CT; idx += kThreads) {
+        // issue the loads of up to 8 splits before summing them in split order
+        float v = 0.0f;
+        for (int s0 = 0; s0 < S; s0 += 8) {
+            float t[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                t[j] = s0 + j < S ? __ldcg(tile_parts + static_cast<int64_t>(s0 + j) * (M * CT) + idx) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (s0 + j < S) v += t[j];
+        }
+        emit(idx, v);
+    }
+    if (tid == 0) p.tickets[blockIdx.x] = 0;  // ready for the next launch on this workspace
 }
 
 struct MmaOverrides {
-    int ck;
+    int splits;
 };
 MmaOverrides& mma_overrides() {
     static MmaOverrides o{[] {
-        const char* v = std::getenv("KT_MMA_CK");
+        const char* v = std::getenv("KT_MMA_SPLITS");
         return v ? std::atoi(v) : 0;
     }()};
     return o;
 }
 
-// Clusters of `ck` CTAs of this kernel that the device holds at once (cached
-// per device; clusters must fit in one GPC, so this is not sm_count / ck).
-int max_active_clusters(int ck) {
+// CTAs of this kernel one SM holds (cached per device).
+int blocks_per_sm() {
     constexpr int kMaxDevices = 64;
-    static int cache[kMaxDevices][kMaxCluster + 1] = {};
+    static int cache[kMaxDevices] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    int* slot = dev >= 0 && dev < kMaxDevices ? &cache[dev][ck] : nullptr;
+    int* slot = dev >= 0 && dev < kMaxDevices ? &cache[dev] : nullptr;
     if (slot != nullptr && *slot != 0) return *slot;
-    auto kernel = gemv_mma_kernel<1>;
     int n = 0;
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) ==
-            cudaSuccess &&
-        (ck <= 8 || cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess)) {
-        cudaLaunchConfig_t lc = {};
-        lc.gridDim = dim3(1, ck, 1);
-        lc.blockDim = dim3(kThreads, 1, 1);
-        lc.dynamicSmemBytes = kSmemBytes;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = ck;
-        attr[0].val.clusterDim.z = 1;
-        lc.attrs = attr;
-        lc.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&n, kernel, &lc) != cudaSuccess) n = 0;
-    }
-    cudaGetLastError();  // a refused query only rules this cluster size out
-    n = n > 0 ? n : -1;
+    auto kernel = gemv_mma_kernel<1>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, kSmemBytes) != cudaSuccess)
+        n = 1;
+    cudaGetLastError();
+    n = std::max(n, 1);
     if (slot != nullptr) *slot = n;
     return n;
 }
 
-// Smallest cluster along K whose slices fit the x staging area.
-int min_ck(int K) { return (K + kPairs * kMaxSliceRows - 1) / (kPairs * kMaxSliceRows); }
+int tiles_of(int R) { return (R + kTileBytes - 1) / kTileBytes; }
 
-// The largest cluster along K whose whole grid is co-resident in one wave and
-// that leaves >= 32 rows per slice; at least min_ck(K); 0 if no cluster size
-// the kernel needs can be placed.
-int choose_ck(int R, int K, int sm_count) {
-    const int tiles = (R + kTileBytes - 1) / kTileBytes;
-    const int lo = std::max(1, min_ck(K));
-    int best = 0;
-    for (int ck = lo; ck <= kMaxCluster; ++ck) {
-        if (ck > lo && (tiles * ck > sm_count || K / (kPairs * ck) < 32)) break;
-        const int n = max_active_clusters(ck);
-        if (n <= 0) continue;
-        if (best == 0 || tiles <= n) best = ck;
+// Workspace layout: tickets[kTicketCap] (always at the front, so that no
+// launch's partial tiles ever land where another launch keeps its tickets) |
+// partial tiles.
+constexpr int kTicketCap = 16384;
+constexpr size_t kTicketBytes = kTicketCap * sizeof(int32_t);
+
+int max_slice_rows_of(int m) {
+    switch (m) {
+        case 1: return max_slice_rows<1>();
+        case 2: return max_slice_rows<2>();
+        case 3: return max_slice_rows<3>();
+        default: return max_slice_rows<4>();
     }
-    return best;
 }
 
-// Rows per slice: a multiple of the stage height.
-int slice_rows_for(int K, int ck) {
-    const int slices = kPairs * ck;
-    const int per = (K + slices - 1) / slices;
-    return (per + kRowsPerStage - 1) / kRowsPerStage * kRowsPerStage;
+// Fewest K-splits that keep every slice within max_slice_rows.
+int min_splits(int K, int m) {
+    const int per = kPairs * max_slice_rows_of(m);
+    return (K + per - 1) / per;
+}
+
+// K-splits per column tile: enough CTAs to fill every SM slot in one wave
+// (at least one stage per slice), never fewer than min_splits.
+int choose_splits(int R, int K, int m, int sm_count) {
+    const int tiles = tiles_of(R);
+    const int slots = blocks_per_sm() * sm_count;
+    const int k_stages = K / kRowsPerStage;
+    int s = std::max(1, slots / tiles);
+    s = std::min(s, std::max(1, k_stages / kPairs));
+    const int o = mma_overrides().splits;
+    if (o >= 1) s = o;
+    s = std::max(s, min_splits(K, m));
+    return tiles > kTicketCap ? min_splits(K, m) : s;
 }
 
 template <int M>
-cudaError_t launch_m(const QView& w, const MmaParams& p, int ck, cudaStream_t s) {
+cudaError_t launch_m(const QView& w, const MmaParams& p, int splits, cudaStream_t s) {
     auto kernel = gemv_mma_kernel<M>;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
-    if (ck > 8) {
-        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
-    }
-    MmaParams q = p;
-    q.slice_rows = slice_rows_for(p.K, ck);
     cudaLaunchConfig_t lc = {};
-    lc.gridDim = dim3((p.R + kTileBytes - 1) / kTileBytes, ck, 1);
+    lc.gridDim = dim3(tiles_of(p.R), splits, 1);
     lc.blockDim = dim3(kThreads, 1, 1);
     lc.dynamicSmemBytes = kSmemBytes;
     lc.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = ck;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     lc.attrs = attr;
-    lc.numAttrs = 2;
-    return cudaLaunchKernelEx(&lc, kernel, *w.tmap_mma, q);
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, kernel, *w.tmap_mma, p);
 }
 
 }  // namespace
 
-void set_mma_tuning(int cluster_k) { mma_overrides().ck = cluster_k; }
+void set_mma_tuning(int k_splits) { mma_overrides().splits = k_splits; }
 
 bool gemv_mma_supported(const QView& w, int32_t m, const float* a) {
     (void)a;
     if (w.bits != 4 || m < 1 || m > kGemvMmaMaxM || w.tmap_mma == nullptr) return false;
     return w.columns % 32 == 0 && w.rows % kRowsPerStage == 0 && w.group_size % kRowsPerStage == 0 &&
-           min_ck(w.rows) <= kMaxCluster;
+           min_splits(w.rows, m) <= 65535 && (min_splits(w.rows, m) == 1 || tiles_of(w.bytes_per_row) <= kTicketCap);
 }
 
-cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s) {
+size_t gemv_mma_workspace_bytes(const QView& w, int32_t m, int sm_count) {
+    const int splits = choose_splits(w.bytes_per_row, w.rows, m, sm_count);
+    if (splits <= 1) return 0;
+    const size_t tiles = static_cast<size_t>(tiles_of(w.bytes_per_row));
+    return kTicketBytes + tiles * splits * static_cast<size_t>(m) * 2 * kTileBytes * sizeof(float);
+}
+
+cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s, void* workspace,
+                            size_t workspace_bytes) {
     MmaParams p{};
     p.scales = w.scales;
     p.zeros = w.zeros;
@@ -644,15 +696,18 @@ cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, c
     p.h1024 = 0x64006400u;
     p.alpha = a.alpha;
     p.accumulate = a.accumulate;
-    int ck = choose_ck(p.R, p.K, sm_count);
-    const int o = mma_overrides().ck;
-    if (o >= 1 && o <= kMaxCluster) ck = std::max(o, min_ck(p.K));
-    if (ck == 0) return cudaErrorInvalidConfiguration;
+    const int splits = choose_splits(p.R, p.K, a.m, sm_count);
+    if (splits > 1) {
+        if (workspace == nullptr || workspace_bytes < gemv_mma_workspace_bytes(w, a.m, sm_count))
+            return cudaErrorInvalidValue;
+        p.tickets = static_cast<int32_t*>(workspace);
+        p.partials = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kTicketBytes);
+    }
     switch (a.m) {
-        case 1: return launch_m<1>(w, p, ck, s);
-        case 2: return launch_m<2>(w, p, ck, s);
-        case 3: return launch_m<3>(w, p, ck, s);
-        case 4: return launch_m<4>(w, p, ck, s);
+        case 1: return launch_m<1>(w, p, splits, s);
+        case 2: return launch_m<2>(w, p, splits, s);
+        case 3: return launch_m<3>(w, p, splits, s);
+        case 4: return launch_m<4>(w, p, splits, s);
         default: return cudaErrorInvalidValue;
     }
 }

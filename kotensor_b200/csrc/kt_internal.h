@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/kt_cuda.h"
 
@@ -24,6 +25,17 @@ struct kt_ctx {
     float* d2h_c = nullptr;
     float* bias_buf = nullptr;
     size_t a_cap = 0, c_cap = 0, bias_cap = 0;
+    // Kernel workspaces, one per stream that launched on this context (launches
+    // on one stream are ordered, so they may share one); grown by replacement,
+    // the replaced ones kept until kt_destroy because queued work may use them.
+    struct Workspace {
+        cudaStream_t stream;
+        void* ptr;
+        size_t bytes;
+    };
+    std::mutex ws_mutex;
+    std::vector<Workspace> workspaces;
+    std::vector<void*> retired;
 };
 
 struct kt_qweight {
@@ -66,6 +78,10 @@ inline QView view(const kt_qweight* w) {
                  w->has_tmaps ? &w->tmap_w256 : nullptr, w->has_tmap_mma ? &w->tmap_mma : nullptr};
 }
 
+// Zero-initialised device workspace of at least `bytes` for launches on stream
+// `s` (kt_api.cu).
+cudaError_t stream_workspace(kt_ctx* ctx, cudaStream_t s, size_t bytes, void** out);
+
 // Rows per TMA box / pipeline stage of the streaming kernel.
 constexpr int kStageRows = 8;
 // Builds kt_qweight::tmap_w128 / tmap_w256 (kt_api.cu).
@@ -98,8 +114,14 @@ cudaError_t launch_matmul_generic(const QView& w, const MatmulArgs& args, cudaSt
 // ---- kt_gemv_mma.cu  (INT4, m <= kGemvMmaMaxM: tensor-core products, fp32 group combine)
 constexpr int kGemvMmaMaxM = 4;
 bool gemv_mma_supported(const QView& w, int32_t m, const float* a);
-void set_mma_tuning(int cluster_k);
-cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s);
+void set_mma_tuning(int k_splits);
+// Device workspace one launch needs (0: none): split-K partial tiles and
+// per-tile arrival counters.  The counters must be zero before the first
+// launch; every launch leaves them zero.  Launches that share a workspace
+// must be ordered (one stream).
+size_t gemv_mma_workspace_bytes(const QView& w, int32_t m, int sm_count);
+cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s, void* workspace,
+                            size_t workspace_bytes);
 
 // ---- kt_backward.cu
 cudaError_t launch_matmul_t(const QView& w, const float* dy, float* dx, int32_t m, int32_t accumulate,

@@ -315,11 +315,12 @@ def test_every_launch_shape_matches_the_oracle(kt, oracle, lane_bytes, cluster_k
     assert kt.Context.get().take_error() == 0
 
 
-@pytest.mark.parametrize("cluster_k", [1, 2, 5, 16])
+@pytest.mark.parametrize("k_splits", [1, 2, 5, 37])
 @pytest.mark.parametrize("k,n,g", [(2048, 5632, 64), (4864, 896, 64), (1024, 4096, 32), (960, 2048, 96)])
-def test_int4_tensor_core_gemv_matches_the_oracle(kt, oracle, cluster_k, k, n, g):
-    """The INT4 m <= 4 tensor-core GEMV at every cluster size, ragged last tiles
-    (896 columns) and group sizes 32 / 64 / 96, within the fp32 tolerance."""
+def test_int4_tensor_core_gemv_matches_the_oracle(kt, oracle, k_splits, k, n, g):
+    """The INT4 m <= 4 tensor-core GEMV at several K-split counts (slices that
+    start and end inside groups, empty slices), ragged last tiles (896 columns)
+    and group sizes 32 / 64 / 96, within the fp32 tolerance."""
     from kotensor_b200 import _lib
     lib = kt.load_library()
     rng = np.random.default_rng(k + n + g)
@@ -328,7 +329,7 @@ def test_int4_tensor_core_gemv_matches_the_oracle(kt, oracle, cluster_k, k, n, g
     qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, g)
     assert qt.matmul_path(1) == _lib.KT_PATH_GEMV_MMA
     try:
-        lib.kt_set_gemv_mma_tuning(cluster_k)
+        lib.kt_set_gemv_mma_tuning(k_splits)
         for m in (1, 2, 4):
             a = (rng.standard_normal((m, k), dtype=np.float32) * np.float32(3.0)).astype(np.float32)
             a[0, : k // 3] *= np.float32(1e-3)  # a wide dynamic range inside one row
@@ -357,3 +358,25 @@ def test_int4_tensor_core_gemv_huge_and_tiny_activations(kt, oracle):
             assert not np.any(y)
         else:
             assert rel_err(y, ref) <= TOL_FP32, s
+
+
+def test_int4_tensor_core_gemv_split_k_workspace_is_reused_safely(kt, oracle):
+    """Launches with few column tiles and many K-splits alternate with launches
+    with many tiles on one stream's workspace: no launch's partial tiles may
+    disturb another's arrival counters."""
+    from kotensor_b200 import _lib
+    rng = np.random.default_rng(44)
+    cases = []
+    for k, n in [(5632, 2048), (768, 32000), (4096, 1024), (1024, 16384)]:
+        w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+        ref_t = oracle.quantize(w, 4, 64)
+        qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, 64)
+        assert qt.matmul_path(1) == _lib.KT_PATH_GEMV_MMA
+        cases.append((qt, ref_t, k))
+    for _ in range(2):
+        for qt, ref_t, k in cases:
+            for m in (1, 4):
+                a = rng.standard_normal((m, k), dtype=np.float32)
+                y = run_matmul(kt, qt, a)
+                assert rel_err(y, oracle.multiply_quantized(a, ref_t, threads=8)) <= TOL_FP32, (k, m)
+    assert kt.Context.get().take_error() == 0
