@@ -47,7 +47,7 @@ BITS, GROUP = 4, 64
 L2_BYTES = 126 * 1024 * 1024
 # DRAM bytes / algorithmic bytes of one gemv_mma_kernel<1> launch on the
 # 4096 x 14336 shape, from `ncu --set full` (profiles/gemv_mma_int4_m1_4096x14336.md).
-NCU_TRAFFIC_RATIO = 33986560 / 34021376
+NCU_TRAFFIC_RATIO = 34004224 / 34021376
 WORKLOAD = "config2-int4-ffn-gemv-m1"
 
 
