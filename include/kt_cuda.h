@@ -133,6 +133,17 @@ kt_status kt_dequantize_rows(kt_ctx* ctx, const kt_qweight* w, const int32_t* ro
 kt_status kt_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float* c_dev, int32_t m,
                      int32_t accumulate, float alpha, const float* bias_dev, void* stream);
 
+/* kt_qmatmul for callers that must not have the library allocate device
+ * memory (no counterpart in the reference, whose MatMul works in host
+ * memory).  Same kernels and results; the split-K workspace of the INT4
+ * tensor-core GEMV is a 4 MiB array inside the library image instead of a
+ * buffer allocated on first use.  The first call on a device looks up that
+ * array's address: make it before capturing a stream.  One array per device:
+ * calls that overlap in time on a device race on it, so order them on one
+ * stream.  Shapes whose workspace exceeds 4 MiB return KT_ERR_INVALID_ARGUMENT. */
+kt_status kt_qmatmul_noalloc(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float* c_dev, int32_t m,
+                             int32_t accumulate, float alpha, const float* bias_dev, void* stream);
+
 /* Which kernel family kt_qmatmul runs for this weight and m (for a 16-byte
  * aligned a), and so which tolerance applies: KT_PATH_GEMV (fp32 CUDA-core
  * streaming kernel), KT_PATH_GENERIC (fp32 kernel for unaligned shapes),

@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_dequantize": ([P, P, P, P], I32),
     "kt_dequantize_rows": ([P, P, P, I32, P, P, P], I32),
     "kt_qmatmul": ([P, P, P, P, I32, I32, F32, P, P], I32),
+    "kt_qmatmul_noalloc": ([P, P, P, P, I32, I32, F32, P, P], I32),
     "kt_qmatmul_host": ([P, P, P, P, I32, I32, F32, P], I32),
     "kt_qmatmul_path": ([P, I32, ctypes.POINTER(I32)], I32),
     "kt_set_gemv_tuning": ([I32, I32], I32),
