@@ -168,6 +168,12 @@ kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c,
         e = launch_gemv_mma(v, args, ctx->sm_count, s, ws, need);
     } else if (gemv_fast_supported(v, m, a)) {
         e = launch_gemv(v, args, ctx->sm_count, s);
+    } else if (gemm_tc_supported(v, m, a)) {
+        void* ws = nullptr;
+        const size_t need = gemm_tc_workspace_bytes(v, m, ctx->sm_count);
+        e = stream_workspace(ctx, s, need, &ws);
+        if (e != cudaSuccess) return cuda_fail(e, "qmatmul workspace");
+        e = launch_gemm_tc(v, args, ctx->sm_count, s, ws, need);
     } else {
         e = launch_matmul_generic(v, args, s);
     }
@@ -226,8 +232,27 @@ bool make_tensor_maps(kt_qweight* w) {
             encode(&w->tmap_mma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->qdata, dims, strides, box_mma, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        const cuuint32_t box_raw[2] = {128, 64};
+        w->has_tmap_raw64 =
+            encode(&w->tmap_raw64, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->qdata, dims, strides, box_raw, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
     return true;
+}
+
+bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType type, uint32_t elem_bytes, const void* base,
+                    uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                    CUtensorMapSwizzle swizzle) {
+    (void)elem_bytes;
+    EncodeTiledFn encode = encode_tiled();
+    if (!encode) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace kt
@@ -470,6 +495,7 @@ kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out) {
     const QView v = view(w);
     *path_out = gemv_mma_supported(v, m, nullptr)    ? KT_PATH_GEMV_MMA
                 : gemv_fast_supported(v, m, nullptr) ? KT_PATH_GEMV
+                : gemm_tc_supported(v, m, nullptr)   ? KT_PATH_TENSOR_CORE
                                                      : KT_PATH_GENERIC;
     return KT_OK;
 }

@@ -1,0 +1,545 @@
+// kt_gemm_tc.cu -- INT4 dequantizing GEMM on the 5th-generation tensor cores:
+// MatMul.multiplyQuantized (Engine/kotensor/src/main/kotlin/MatMul.kt:460-486)
+// for m >= 9, the tile path of the reference (computeQuantizedTile,
+// MatMul.kt:830-952) used by prefill and batched decode.
+//
+// Product.  c[m x N] = (accumulate ? c : 0) + alpha * a[m x K] . dequant(W) + bias,
+// with W dequantized as in the reference (scale * (q - zero), fp32) and then
+// rounded to bf16, a rounded to bf16, bf16 x bf16 products accumulated in fp32
+// by tcgen05.mma (kind::f16) in tensor memory.  Tolerance 2e-2 relative to
+// max|c| against the reference's fp32 result.
+//
+// Mapping.  The MMA computes D[128 x nt] = A[128 x K] . B[nt x K]^T with
+//   A = dequantized weights, one row per output column (K-major, 128-byte swizzle)
+//   B = bf16 activations, one row per token (K-major, 128-byte swizzle)
+// so tokens are the MMA's N (16..256 per CTA, any m) and the 128 output
+// columns its M.  A CTA owns 128 packed bytes of every weight row: INT4 packs
+// column c and column c + half into one byte, so those bytes feed two A tiles
+// (low and high nibble columns) and two accumulators of nt TMEM columns each.
+//
+// Pipeline per 64-row K-block, kStages deep:
+//   warp 8  (one lane): TMA of the packed bytes [64 x 128] and of the bf16 x
+//                       tile [nt x 64] (128-byte swizzle) -> "full_raw"
+//   warps 0-7         : dequantize the packed bytes into the two A tiles
+//                       (swizzled 16-byte stores), fence.proxy.async -> "full_a"
+//   warp 9  (one lane): 2 x 4 tcgen05.mma (K = 16 each), tcgen05.commit -> "empty"
+// then tcgen05.commit -> "done", and warps 0-7 read the accumulators with
+// tcgen05.ld and write c.  Every mbarrier wait is bounded (globaltimer); a
+// timeout sets the context's error word.
+//
+// The activations are converted to bf16 once per call by a small pre-pass
+// kernel into the stream's workspace (after its reserved front).
+#include <cuda_bf16.h>
+
+#include <algorithm>
+
+#include "kt_internal.h"
+
+namespace kt {
+namespace {
+
+constexpr int kBK = 64;                 // K rows per stage
+constexpr int kTileBytes = 128;         // packed bytes per CTA (256 INT4 output columns)
+constexpr int kMaxNT = 256;             // tokens per CTA (MMA N)
+constexpr int kStages = 3;
+constexpr int kWorkers = 8;             // dequantizing warps, then the epilogue
+constexpr int kProducerWarp = kWorkers;
+constexpr int kMmaWarp = kWorkers + 1;
+constexpr int kThreads = (kWorkers + 2) * 32;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+constexpr int kRawBytes = kBK * kTileBytes;          // 8 KiB packed
+constexpr int kXBytes = kMaxNT * kBK * 2;            // 32 KiB bf16 activations
+constexpr int kABytes = 128 * kBK * 2;               // 16 KiB bf16 weights per nibble half
+constexpr int kStageBytes = kRawBytes + kXBytes + 2 * kABytes;
+// per stage, the scales and zero points of the (at most two) groups its rows touch:
+// scales low [128] | scales high [128] | zeros low [128] | zeros high [128]
+constexpr int kGroupSlotBytes = 2 * kTileBytes * 4 + 2 * kTileBytes;
+constexpr int kMaxGroupsPerStage = 2;
+constexpr int kScaleStageBytes = kMaxGroupsPerStage * kGroupSlotBytes;
+constexpr int kBarBytes = 128;
+constexpr size_t kSmemBytes =
+    1024 + static_cast<size_t>(kStages) * (kStageBytes + kScaleStageBytes) + kBarBytes;
+static_assert(kStageBytes % 1024 == 0 && kRawBytes % 1024 == 0 && kXBytes % 1024 == 0 && kABytes % 1024 == 0,
+              "swizzled tiles start on 1024-byte boundaries");
+static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+
+struct GemmParams {
+    const float* scales;
+    const uint8_t* zeros;
+    float* y;
+    const float* bias;
+    int32_t* err;
+    int32_t M, K, N, R, gs, G;
+    int32_t nt;        // tokens per CTA: multiple of 16, <= kMaxNT
+    int32_t nt_cols;   // TMEM columns between the two accumulators
+    int32_t tmem_cols; // TMEM columns allocated (power of two >= 32)
+    uint32_t idesc;    // instruction descriptor of the MMA
+    float alpha;
+    int32_t accumulate;
+    // split-K (gridDim.z > 1): partial tiles and per-tile arrival counters
+    float* partials;   // [tile][split][nt][256]
+    int32_t* tickets;  // [tile], zero between launches
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > kWaitLimitNs) return false;
+    }
+    return true;
+}
+// 1-D bulk copy global -> this CTA's shared memory (no multicast).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// 2-D TMA tile load into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major bf16 tile with 128-byte rows,
+// 128-byte swizzle, 8-row atoms 1024 bytes apart (start address in 16-byte
+// units; leading byte offset 1 (unused when swizzled); descriptor version 1).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
+    return static_cast<uint64_t>((addr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+           (static_cast<uint64_t>(2) << 61);
+}
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive fp32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(mask), "r"(c));
+    return d;
+}
+// bf16x2 (a - b) * s, each lane of the pair rounded once to bf16 (a - b is exact here)
+__device__ __forceinline__ uint32_t bf2_sub_mul(uint32_t a, uint32_t b, uint32_t s) {
+    const __nv_bfloat162 r = __hmul2(__hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                                             *reinterpret_cast<const __nv_bfloat162*>(&b)),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&s));
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t bf2_splat(float v) {
+    const __nv_bfloat162 h = __float2bfloat162_rn(v);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ int atomic_add_acq_rel(int32_t* p, int v) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void workers_barrier() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkers * 32) : "memory"); }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                   GemmParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tile_b0 = blockIdx.x * kTileBytes;
+    const int tok0 = blockIdx.y * p.nt;
+    // this CTA's K-blocks: split blockIdx.z of gridDim.z, spread evenly
+    const int kb_total = (p.K + kBK - 1) / kBK;
+    const int kb_begin = static_cast<int>(static_cast<int64_t>(blockIdx.z) * kb_total / gridDim.z);
+    const int kb_end = static_cast<int>(static_cast<int64_t>(blockIdx.z + 1) * kb_total / gridDim.z);
+    const int n_kb = kb_end - kb_begin;  // >= 1 (the host keeps splits <= kb_total)
+
+    // 1024-aligned base for the swizzled tiles
+    const uint32_t raw_s = smem_u32(smem_raw);
+    const uint32_t base = (raw_s + 1023u) & ~1023u;
+    unsigned char* gbase = smem_raw + (base - raw_s);
+    const uint32_t scl = base + kStages * kStageBytes;  // scale slots [stage][group]
+    const uint32_t bars = scl + kStages * kScaleStageBytes;
+    auto full_raw = [&](int s) { return bars + 8 * s; };
+    auto full_a = [&](int s) { return bars + 8 * (kStages + s); };
+    auto empty = [&](int s) { return bars + 8 * (2 * kStages + s); };
+    const uint32_t done = bars + 8 * (3 * kStages);
+    uint32_t* tmem_slot =
+        reinterpret_cast<uint32_t*>(gbase + kStages * (kStageBytes + kScaleStageBytes) + 8 * (3 * kStages + 1));
+    const int tile_cols = min(kTileBytes, p.R - tile_b0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full_raw(s), 1);
+            mbar_init(full_a(s), kWorkers);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(p.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            const uint32_t tx = static_cast<uint32_t>(kRawBytes + p.nt * kBK * 2);
+            const uint32_t gbytes = static_cast<uint32_t>(tile_cols) * 10;
+            int issued = 0;
+            for (int i = 0; i < n_kb; ++i) {
+                const int s = i % kStages;
+                if (i >= kStages && !mbar_wait_bounded(empty(s), ((i / kStages) - 1) & 1)) {
+                    atomicOr(p.err, 1);
+                    break;
+                }
+                const uint32_t st = base + s * kStageBytes;
+                const int kb = kb_begin + i;
+                const int ga = min(kb * kBK / p.gs, p.G - 1);
+                const int gb = min((kb * kBK + kBK - 1) / p.gs, p.G - 1);
+                mbar_expect_tx(full_raw(s), tx + (gb - ga + 1) * gbytes);
+                tma_load_2d(st, &tmap_w, tile_b0, kb * kBK, full_raw(s));
+                tma_load_2d(st + kRawBytes, &tmap_x, kb * kBK, tok0, full_raw(s));
+                for (int g = ga; g <= gb; ++g) {
+                    const uint32_t dst = scl + s * kScaleStageBytes + (g - ga) * kGroupSlotBytes;
+                    const int64_t go = static_cast<int64_t>(g) * p.N;
+                    bulk_load(dst, p.scales + go + tile_b0, tile_cols * 4, full_raw(s));
+                    bulk_load(dst + kTileBytes * 4, p.scales + go + p.R + tile_b0, tile_cols * 4, full_raw(s));
+                    bulk_load(dst + kTileBytes * 8, p.zeros + go + tile_b0, tile_cols, full_raw(s));
+                    bulk_load(dst + kTileBytes * 9, p.zeros + go + p.R + tile_b0, tile_cols, full_raw(s));
+                }
+                ++issued;
+            }
+            // the last copy issued into each slot has landed before the CTA may exit
+            for (int i = max(0, issued - kStages); i < issued; ++i)
+                if (!mbar_wait_bounded(full_raw(i % kStages), (i / kStages) & 1)) break;
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            for (int i = 0; i < n_kb; ++i) {
+                const int s = i % kStages;
+                const uint32_t par = (i / kStages) & 1;
+                if (!mbar_wait_bounded(full_raw(s), par) || !mbar_wait_bounded(full_a(s), par)) {
+                    atomicOr(p.err, 1);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = base + s * kStageBytes;
+                const uint32_t xs = st + kRawBytes, alo = xs + kXBytes, ahi = alo + kABytes;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                    const uint64_t bdesc = umma_desc_sw128(xs + kk * 32);
+                    const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+                    umma_bf16(tmem, umma_desc_sw128(alo + kk * 32), bdesc, p.idesc, acc);
+                    umma_bf16(tmem + p.nt_cols, umma_desc_sw128(ahi + kk * 32), bdesc, p.idesc, acc);
+                }
+                umma_commit(empty(s));  // the stage is free once these MMAs have read it
+            }
+            umma_commit(done);
+            if (!mbar_wait_bounded(done, 0)) atomicOr(p.err, 1);  // no MMA in flight past this point
+        }
+    } else {
+        // ---- dequantize: warp w owns rows 8w..8w+7 of each stage (one 16-byte
+        // k-chunk of every A row); lane l owns tile columns l + 32 i.  The
+        // next K-block's group constants are loaded while this one is
+        // converted.  A pair of rows (k, k+1) of one column becomes one bf16x2
+        // word: PRMT puts the two bytes in the two halves, LOP3 ORs each nibble
+        // into the mantissa of 128.0 (0x4300), and (128 + q) - (128 + zero)
+        // is exact before the one rounding of the scale multiply.
+        bool ok = true;
+        for (int i = 0; i < n_kb; ++i) {
+            const int s = i % kStages;
+            const int kb = kb_begin + i;
+            if (!mbar_wait_bounded(full_raw(s), (i / kStages) & 1)) {
+                if (lane == 0) atomicOr(p.err, 1);
+                ok = false;
+                break;
+            }
+            const unsigned char* raw = gbase + s * kStageBytes;
+            unsigned char* alo = gbase + s * kStageBytes + kRawBytes + kXBytes;
+            unsigned char* ahi = alo + kABytes;
+            // this warp's rows (8 of them, gs % 32 == 0) lie in one group
+            const int ga = min(kb * kBK / p.gs, p.G - 1);
+            const int gw = min((kb * kBK + 8 * warp) / p.gs, p.G - 1);
+            const unsigned char* slot = gbase + kStages * kStageBytes + s * kScaleStageBytes + (gw - ga) * kGroupSlotBytes;
+            const float* sc_lo = reinterpret_cast<const float*>(slot);
+            const float* sc_hi = sc_lo + kTileBytes;
+            const unsigned char* z_lo = slot + kTileBytes * 8;
+            const unsigned char* z_hi = slot + kTileBytes * 9;
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+                const int c = lane + 32 * c4;
+                // columns beyond the tile's bytes read stale slot data; their A rows
+                // only reach accumulator rows that are never stored
+                const uint32_t s2_lo = bf2_splat(sc_lo[c]), s2_hi = bf2_splat(sc_hi[c]);
+                const uint32_t zb_lo = bf2_splat(128.0f + static_cast<float>(z_lo[c]));
+                const uint32_t zb_hi = bf2_splat(128.0f + static_cast<float>(z_hi[c]));
+                uint32_t b[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) b[j] = raw[(8 * warp + j) * kTileBytes + c];
+                uint4 vlo, vhi;
+                uint32_t* wl = &vlo.x;
+                uint32_t* wh = &vhi.x;
+#pragma unroll
+                for (int jp = 0; jp < 4; ++jp) {
+                    const uint32_t pr = prmt(b[2 * jp], b[2 * jp + 1], 0x5410u);  // rows 2jp, 2jp+1 in the halves
+                    const uint32_t ql = lop3_and_or(pr, 0x000F000Fu, 0x43004300u);
+                    const uint32_t qh = lop3_and_or(pr >> 4, 0x000F000Fu, 0x43004300u);
+                    wl[jp] = bf2_sub_mul(ql, zb_lo, s2_lo);
+                    wh[jp] = bf2_sub_mul(qh, zb_hi, s2_hi);
+                }
+                const uint32_t off = static_cast<uint32_t>(c * 128 + ((warp ^ (c & 7)) << 4));
+                *reinterpret_cast<uint4*>(alo + off) = vlo;
+                *reinterpret_cast<uint4*>(ahi + off) = vhi;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> MMA reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full_a(s));
+        }
+        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 of the low
+        // (w < 4) or high (w >= 4) accumulator: one tile column per thread.
+        const bool have = ok && mbar_wait_bounded(done, 0);
+        if (!have && lane == 0) atomicOr(p.err, 1);
+        tc_fence_after();
+        const int quarter = warp & 3;
+        const int nib = warp >> 2;
+        const int c = 32 * quarter + lane;  // 0..127 in this accumulator
+        const int col256 = nib * 128 + c;   // 0..255 in the CTA's partial tile
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + (nib ? p.nt_cols : 0);
+        auto emit = [&](int tok, int col256, float v) {
+            const int cb = tile_b0 + (col256 & 127);
+            const int oc = col256 < 128 ? cb : p.R + cb;
+            if (!have || cb >= p.R || oc >= p.N || tok >= p.M) return;
+            float* out = p.y + static_cast<int64_t>(tok) * p.N + oc;
+            float r = fmaf(p.alpha, v, p.accumulate ? *out : 0.0f);
+            if (p.bias != nullptr) r += p.bias[oc];
+            *out = r;
+        };
+        const int S = gridDim.z;
+        const int64_t tile_id = static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x;
+        float* parts = p.partials + tile_id * S * (static_cast<int64_t>(p.nt) * 256);  // [S][nt][256]
+        for (int t0 = 0; t0 < p.nt; t0 += 16) {
+            float v[16];
+            tmem_ld16(taddr + t0, v);  // every lane takes part (.sync.aligned)
+            if (S == 1) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) emit(tok0 + t0 + j, col256, v[j]);
+            } else {
+                float* mine = parts + static_cast<int64_t>(blockIdx.z) * p.nt * 256;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) __stcg(mine + (t0 + j) * 256 + col256, v[j]);
+            }
+        }
+        if (S > 1) {
+            // split-K: the last CTA of the tile to arrive sums the partial tiles in
+            // split order (the worker barrier orders every worker's stores before
+            // thread 0's acq_rel atomic, which publishes them at GPU scope).
+            workers_barrier();
+            if (threadIdx.x == 0)
+                s_last = atomic_add_acq_rel(p.tickets + tile_id, 1) == S - 1;
+            workers_barrier();
+            if (s_last) {
+                // thread: 4 adjacent columns, every 4th token, two tokens in flight
+                const int q4 = (threadIdx.x & 63) * 4;
+                for (int t = threadIdx.x >> 6; t < p.nt; t += 8) {
+                    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+                    const bool two = t + 4 < p.nt;
+                    for (int sp = 0; sp < S; ++sp) {
+                        const float* src = parts + static_cast<int64_t>(sp) * p.nt * 256 + q4;
+                        const float4 u = __ldcg(reinterpret_cast<const float4*>(src + t * 256));
+                        a0.x += u.x; a0.y += u.y; a0.z += u.z; a0.w += u.w;
+                        if (two) {
+                            const float4 w4 = __ldcg(reinterpret_cast<const float4*>(src + (t + 4) * 256));
+                            a1.x += w4.x; a1.y += w4.y; a1.z += w4.z; a1.w += w4.w;
+                        }
+                    }
+                    emit(tok0 + t, q4, a0.x); emit(tok0 + t, q4 + 1, a0.y);
+                    emit(tok0 + t, q4 + 2, a0.z); emit(tok0 + t, q4 + 3, a0.w);
+                    if (two) {
+                        emit(tok0 + t + 4, q4, a1.x); emit(tok0 + t + 4, q4 + 1, a1.y);
+                        emit(tok0 + t + 4, q4 + 2, a1.z); emit(tok0 + t + 4, q4 + 3, a1.w);
+                    }
+                }
+                if (threadIdx.x == 0) p.tickets[tile_id] = 0;  // ready for the next launch on this workspace
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols)
+                     : "memory");
+    }
+}
+
+// x (fp32 [M x K]) -> bf16, 8 elements per thread (K % 8 == 0).
+__global__ void x_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ xb, int64_t n8) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n8) return;
+    const float4 a = __ldg(reinterpret_cast<const float4*>(x) + 2 * i);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(x) + 2 * i + 1);
+    uint4 o;
+    o.x = pack_bf16(a.x, a.y);
+    o.y = pack_bf16(a.z, a.w);
+    o.z = pack_bf16(b.x, b.y);
+    o.w = pack_bf16(b.z, b.w);
+    reinterpret_cast<uint4*>(xb)[i] = o;
+}
+
+int nt_for(int m) { return std::min(kMaxNT, (m + 15) / 16 * 16); }
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+// K-splits: up to one CTA per SM, at most 4 splits of at least 16 K-blocks each.
+int splits_for(const QView& w, int m, int sm_count) {
+    const int tiles = (w.bytes_per_row + kTileBytes - 1) / kTileBytes;
+    const int ttiles = (m + nt_for(m) - 1) / nt_for(m);
+    const int kb_total = (w.rows + kBK - 1) / kBK;
+    int s = std::max(1, sm_count / (tiles * ttiles));
+    s = std::min({s, std::max(1, kb_total / 16), 4});
+    if (static_cast<int64_t>(tiles) * ttiles > kTicketCapEach) s = 1;
+    return std::min(s, 65535);
+}
+
+size_t x_bytes(const QView& w, int m) { return align256(static_cast<size_t>(m) * w.rows * 2); }
+
+}  // namespace
+
+bool gemm_tc_supported(const QView& w, int32_t m, const float* a) {
+    if (w.bits != 4 || m < 9 || w.tmap_raw64 == nullptr) return false;
+    if (a != nullptr && reinterpret_cast<uintptr_t>(a) % 16 != 0) return false;
+    return w.rows % 8 == 0 && w.group_size % 32 == 0 && w.columns % 32 == 0;
+}
+
+size_t gemm_tc_workspace_bytes(const QView& w, int32_t m, int sm_count) {
+    const int S = splits_for(w, m, sm_count);
+    size_t bytes = kWorkspaceReservedBytes + x_bytes(w, m);
+    if (S > 1) {
+        const size_t tiles = (w.bytes_per_row + kTileBytes - 1) / kTileBytes;
+        const size_t ttiles = (m + nt_for(m) - 1) / nt_for(m);
+        bytes += tiles * ttiles * S * static_cast<size_t>(nt_for(m)) * 256 * sizeof(float);
+    }
+    return bytes;
+}
+
+cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s, void* workspace,
+                           size_t workspace_bytes) {
+    if (workspace == nullptr || workspace_bytes < gemm_tc_workspace_bytes(w, a.m, sm_count))
+        return cudaErrorInvalidValue;
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(ws + kWorkspaceReservedBytes);
+    const int64_t n8 = static_cast<int64_t>(a.m) * w.rows / 8;
+    x_to_bf16_kernel<<<static_cast<unsigned>((n8 + 255) / 256), 256, 0, s>>>(a.a, xb, n8);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    GemmParams p{};
+    p.scales = w.scales;
+    p.zeros = w.zeros;
+    p.y = a.c;
+    p.bias = a.bias;
+    p.err = a.err;
+    p.M = a.m;
+    p.K = w.rows;
+    p.N = w.columns;
+    p.R = w.bytes_per_row;
+    p.gs = w.group_size;
+    p.G = w.groups;
+    p.nt = nt_for(a.m);
+    p.nt_cols = p.nt;
+    int cols = 32;
+    while (cols < 2 * p.nt) cols *= 2;
+    p.tmem_cols = cols;
+    // kind::f16: D f32 (bits 4-5 = 1), A bf16 (7-9 = 1), B bf16 (10-12 = 1),
+    // both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+    p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(p.nt >> 3) << 17) |
+              (static_cast<uint32_t>(128 >> 4) << 24);
+    p.alpha = a.alpha;
+    p.accumulate = a.accumulate;
+    const int S = splits_for(w, a.m, sm_count);
+    p.tickets = reinterpret_cast<int32_t*>(ws + kGemmTicketOffset);
+    p.partials = reinterpret_cast<float*>(ws + kWorkspaceReservedBytes + x_bytes(w, a.m));
+
+    alignas(64) CUtensorMap tmap_x;
+    if (!encode_tmap_2d(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, static_cast<uint64_t>(w.rows),
+                        static_cast<uint64_t>(a.m), static_cast<uint64_t>(w.rows) * 2, kBK,
+                        static_cast<uint32_t>(p.nt), CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return e;
+    const dim3 grid((w.bytes_per_row + kTileBytes - 1) / kTileBytes, (a.m + p.nt - 1) / p.nt, S);
+    gemm_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(*w.tmap_raw64, tmap_x, p);
+    return cudaGetLastError();
+}
+
+}  // namespace kt

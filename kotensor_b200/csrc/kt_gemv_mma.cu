@@ -608,11 +608,11 @@ int blocks_per_sm() {
 
 int tiles_of(int R) { return (R + kTileBytes - 1) / kTileBytes; }
 
-// Workspace layout: tickets[kTicketCap] (always at the front, so that no
-// launch's partial tiles ever land where another launch keeps its tickets) |
-// partial tiles.
-constexpr int kTicketCap = 16384;
-constexpr size_t kTicketBytes = kTicketCap * sizeof(int32_t);
+// Workspace layout: the arrival counters sit at a fixed offset in the
+// reserved front (so no launch's partial tiles ever land where another launch
+// keeps its counters) | partial tiles after the reserved front.
+constexpr int kTicketCap = kTicketCapEach;
+constexpr size_t kTicketBytes = kWorkspaceReservedBytes;
 
 int max_slice_rows_of(int m) {
     switch (m) {
@@ -700,7 +700,7 @@ cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, c
     if (splits > 1) {
         if (workspace == nullptr || workspace_bytes < gemv_mma_workspace_bytes(w, a.m, sm_count))
             return cudaErrorInvalidValue;
-        p.tickets = static_cast<int32_t*>(workspace);
+        p.tickets = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) + kGemvTicketOffset);
         p.partials = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kTicketBytes);
     }
     switch (a.m) {

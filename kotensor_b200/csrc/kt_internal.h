@@ -54,6 +54,9 @@ struct kt_qweight {
     // GEMV; built when bytes_per_row % 16 == 0 and bytes_per_row >= 128).
     alignas(64) CUtensorMap tmap_mma;
     bool has_tmap_mma = false;
+    // Box of 64 rows x 128 bytes, no swizzle (INT4 tensor-core GEMM; same condition).
+    alignas(64) CUtensorMap tmap_raw64;
+    bool has_tmap_raw64 = false;
 };
 
 namespace kt {
@@ -70,17 +73,31 @@ struct QView {
     const CUtensorMap* tmap_w128;  // NULL when the weight has no TMA descriptors
     const CUtensorMap* tmap_w256;
     const CUtensorMap* tmap_mma;
+    const CUtensorMap* tmap_raw64;
 };
 
 inline QView view(const kt_qweight* w) {
     return QView{w->qdata, w->scales, w->zeros, w->bits, w->group_size, w->rows, w->columns, w->groups,
                  w->bytes_per_row, w->has_tmaps ? &w->tmap_w128 : nullptr,
-                 w->has_tmaps ? &w->tmap_w256 : nullptr, w->has_tmap_mma ? &w->tmap_mma : nullptr};
+                 w->has_tmaps ? &w->tmap_w256 : nullptr, w->has_tmap_mma ? &w->tmap_mma : nullptr,
+                 w->has_tmap_raw64 ? &w->tmap_raw64 : nullptr};
 }
 
 // Zero-initialised device workspace of at least `bytes` for launches on stream
-// `s` (kt_api.cu).
+// `s` (kt_api.cu).  Its first kWorkspaceReservedBytes hold the split-K arrival
+// counters of the INT4 GEMV and of the INT4 GEMM at fixed offsets (zero
+// between launches, whatever shapes ran before); kernels use the rest freely.
 cudaError_t stream_workspace(kt_ctx* ctx, cudaStream_t s, size_t bytes, void** out);
+constexpr size_t kWorkspaceReservedBytes = static_cast<size_t>(64) << 10;
+constexpr size_t kGemvTicketOffset = 0;
+constexpr size_t kGemmTicketOffset = static_cast<size_t>(32) << 10;
+constexpr int kTicketCapEach = 8192;  // counters per kernel family
+
+// A 2-D tiled TMA descriptor (kt_api.cu): `inner` x `outer` elements of
+// `elem_bytes`, rows `row_bytes` apart, box `box_inner` x `box_outer`.
+bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType type, uint32_t elem_bytes, const void* base,
+                    uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                    CUtensorMapSwizzle swizzle);
 
 // Rows per TMA box / pipeline stage of the streaming kernel.
 constexpr int kStageRows = 8;
@@ -122,6 +139,12 @@ void set_mma_tuning(int k_splits);
 size_t gemv_mma_workspace_bytes(const QView& w, int32_t m, int sm_count);
 cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s, void* workspace,
                             size_t workspace_bytes);
+
+// ---- kt_gemm_tc.cu  (INT4, m >= 9: bf16 tcgen05 MMAs, TMEM accumulators)
+bool gemm_tc_supported(const QView& w, int32_t m, const float* a);
+size_t gemm_tc_workspace_bytes(const QView& w, int32_t m, int sm_count);
+cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s, void* workspace,
+                           size_t workspace_bytes);
 
 // ---- kt_backward.cu
 cudaError_t launch_matmul_t(const QView& w, const float* dy, float* dx, int32_t m, int32_t accumulate,

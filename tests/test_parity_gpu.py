@@ -380,3 +380,25 @@ def test_int4_tensor_core_gemv_split_k_workspace_is_reused_safely(kt, oracle):
                 y = run_matmul(kt, qt, a)
                 assert rel_err(y, oracle.multiply_quantized(a, ref_t, threads=8)) <= TOL_FP32, (k, m)
     assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("k,n,g", [(2048, 5632, 64), (4096, 1024, 64), (896, 4864, 64), (960, 2048, 96),
+                                   (1024, 4096, 32), (4864, 896, 64)])
+@pytest.mark.parametrize("m", [9, 16, 64, 128, 200, 256, 512])
+def test_int4_tensor_core_gemm_matches_the_oracle(kt, oracle, m, k, n, g):
+    """The tcgen05 bf16 GEMM (m >= 9): partial token tiles (9, 200), two token
+    tiles (512), a K that is not a multiple of the 64-row stage (960), group
+    sizes 32 / 64 / 96, accumulate / alpha / bias, within the bf16 tolerance."""
+    from kotensor_b200 import _lib
+    rng = np.random.default_rng(k * 3 + n + m + g)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 4, g)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, g)
+    assert qt.matmul_path(m) == _lib.KT_PATH_TENSOR_CORE
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    c0 = rng.standard_normal((m, n), dtype=np.float32)
+    bias = rng.standard_normal(n, dtype=np.float32)
+    y = run_matmul(kt, qt, a, c0=c0, accumulate=True, alpha=0.5, bias=bias)
+    ref = oracle.multiply_quantized(a, ref_t, c=c0, accumulate=True, alpha=0.5, threads=8) + bias[None, :]
+    assert rel_err(y, ref) <= TOL_BF16, rel_err(y, ref)
+    assert kt.Context.get().take_error() == 0
