@@ -70,6 +70,16 @@ def measured_peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+def measured_tensor_peak() -> tuple[float, str]:
+    """Dense bf16 TFLOP/s: the burst figure (a kernel timed on its own)."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
 # ----------------------------------------------------------------- clocks
 
 class ClockSampler:
@@ -309,6 +319,43 @@ def run_ours(args) -> None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = world * step_bytes * e2e_steps / float(te.item()) / 1e9
 
+    # prefill GEMM (BASELINE config 2 at M = GEMM_M): the same four weights
+    # through the tcgen05 kernel, CUDA graphs over the rotating copies, device
+    # timed; reported beside the GEMV line (tensor-pipe roofline).
+    gemm = None
+    if args.gemm_m > 0:
+        gm = args.gemm_m
+        gxs = [torch.randn((gm, k), generator=gen, device="cuda") for k, _ in SHAPES]
+        gys = [torch.empty((gm, n), device="cuda") for _, n in SHAPES]
+
+        def gemm_cycle():
+            for c in range(copies):
+                for si in range(len(SHAPES)):
+                    kt.MatMul.multiply_quantized(gxs[si], weights[c][si], gys[si], gm, accumulate=False)
+
+        gemm_cycle()
+        torch.cuda.synchronize()
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gg):
+            gemm_cycle()
+        gg.replay()
+        torch.cuda.synchronize()
+        reps = 3
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(reps):
+            gg.replay()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        g_ms = g0.elapsed_time(g1) / (reps * copies)
+        flops = sum(2.0 * gm * k * n for k, n in SHAPES)
+        tpeak, tpeak_kind = measured_tensor_peak()
+        tflops = flops / (g_ms / 1e3) / 1e12
+        gemm = {"m": gm, "tflops": round(tflops, 1), "peak_tflops": tpeak, "peak_kind": tpeak_kind,
+                "frac": round(tflops / tpeak, 4), "ms_per_step": round(g_ms, 4), "kernel": "gemm_tc_kernel",
+                "dtype": "bf16 x bf16 -> f32 (INT4 weights dequantized)", "launches_per_step": len(SHAPES)}
+        del gg
+
     peak, peak_kind = measured_peaks()
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -331,6 +378,8 @@ def run_ours(args) -> None:
         "gpu_launches": len(SHAPES) * args.steps,
         "clocks": clocks,
     }
+    if gemm is not None:
+        line["prefill_gemm"] = gemm
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -347,6 +396,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--m", type=int, default=1, help="activation rows per GEMV (decode batch)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-m", type=int, default=512,
+                    help="also time the prefill GEMM at this M on the same weights (0: skip)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

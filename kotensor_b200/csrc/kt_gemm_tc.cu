@@ -32,6 +32,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "kt_internal.h"
 
@@ -459,13 +460,16 @@ int nt_for(int m) { return std::min(kMaxNT, (m + 15) / 16 * 16); }
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
-// K-splits: up to one CTA per SM, at most 4 splits of at least 16 K-blocks each.
+// K-splits: up to one CTA per SM, at most kMaxSplits splits of at least
+// kMinSplitBlocks K-blocks each (overridable for tuning).
+int kMinSplitBlocks = [] { const char* v = std::getenv("KT_GEMM_MIN_SPLIT_BLOCKS"); return v ? std::max(1, std::atoi(v)) : 8; }();
+int kMaxSplits = [] { const char* v = std::getenv("KT_GEMM_MAX_SPLITS"); return v ? std::max(1, std::atoi(v)) : 8; }();
 int splits_for(const QView& w, int m, int sm_count) {
     const int tiles = (w.bytes_per_row + kTileBytes - 1) / kTileBytes;
     const int ttiles = (m + nt_for(m) - 1) / nt_for(m);
     const int kb_total = (w.rows + kBK - 1) / kBK;
     int s = std::max(1, sm_count / (tiles * ttiles));
-    s = std::min({s, std::max(1, kb_total / 16), 4});
+    s = std::min({s, std::max(1, kb_total / kMinSplitBlocks), kMaxSplits});
     if (static_cast<int64_t>(tiles) * ttiles > kTicketCapEach) s = 1;
     return std::min(s, 65535);
 }
