@@ -112,6 +112,46 @@ kt_status kt_qweight_download(const kt_qweight* w, void* qdata, float* scales, u
 
 kt_status kt_qweight_free(kt_qweight* w);
 
+/* ------------------------------------------------------------ tensor parallelism
+ * Shards of one weight for P ranks (no reference counterpart: the reference runs
+ * on one host).  Quantization is per (row group, column), so a shard is exactly
+ * the quantization of the same block of the fp32 weight: bytes, scales and
+ * zeros bit-identical to quantizing the sliced fp32 weight.
+ *   axis 0 (row-parallel, split K): shard `index` holds whole groups
+ *     [index*G/P, (index+1)*G/P) of the G = ceil(K/groupSize) groups;
+ *   axis 1 (column-parallel, split N): columns [index*N/P, (index+1)*N/P), INT4
+ *     repacked with half = ceil(N_shard / 2).
+ * kt_shard_bounds gives [begin, end) along that axis (host only, no GPU). */
+kt_status kt_shard_bounds(int32_t axis, int32_t extent, int32_t group_size, int32_t parts, int32_t index,
+                          int32_t* begin, int32_t* end);
+/* A new device weight holding shard `index` of `parts` of w, built on `stream`. */
+kt_status kt_qweight_shard(kt_ctx* ctx, const kt_qweight* w, int32_t axis, int32_t parts, int32_t index,
+                           void* stream, kt_qweight** out);
+
+/* One NCCL communicator per rank (one process per GPU).  NCCL is loaded at run
+ * time (libnccl.so.2, or the file named by KT_NCCL_LIBRARY); without it these
+ * return KT_ERR_NCCL.  Rank 0 makes the 128-byte id, every rank passes it to
+ * kt_comm_init (which blocks until all nranks have joined).  Calls on one
+ * communicator must be made in the same order on every rank, each rank on one
+ * stream. */
+typedef struct kt_comm kt_comm;
+kt_status kt_comm_unique_id(void* id_out /* 128 bytes */);
+kt_status kt_comm_init(kt_ctx* ctx, int32_t nranks, int32_t rank, const void* unique_id, kt_comm** out);
+kt_status kt_comm_destroy(kt_comm* comm);
+
+/* Row-parallel multiplyQuantized: w_shard = kt_qweight_shard(W, axis 0, P, rank),
+ * a_shard = the matching columns of a, contiguous [m x K_rank] on the device:
+ *   c[m x N] = (accumulate ? c : 0) + alpha * sum_ranks a_shard . dequant(w_shard) + bias
+ * on every rank (ncclAllReduce of the fp32 partial products, bias added once). */
+kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* w_shard, const float* a_shard_dev,
+                                  float* c_dev, int32_t m, int32_t accumulate, float alpha, const float* bias_dev,
+                                  void* stream);
+
+/* Column-parallel outputs (kt_qmatmul on w_shard = kt_qweight_shard(W, axis 1,
+ * P, rank), equal widths n_shard = N / P) gathered into y_full [m x N] on every rank. */
+kt_status kt_allgather_columns(kt_comm* comm, const float* y_shard_dev, float* y_full_dev, int32_t m,
+                               int32_t n_shard, void* stream);
+
 /* QuantizedTensor.dequantize(), QuantizedTensor.kt:243-249: out_dev fp32 [rows x columns]. */
 kt_status kt_dequantize(kt_ctx* ctx, const kt_qweight* w, float* out_dev, void* stream);
 

@@ -71,6 +71,13 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_set_gemv_mma_tuning": ([I32], I32),
     "kt_ctx_take_error": ([P, ctypes.POINTER(I32)], I32),
     "kt_qmatmul_t": ([P, P, P, P, I32, I32, P], I32),
+    "kt_shard_bounds": ([I32, I32, I32, I32, I32, ctypes.POINTER(I32), ctypes.POINTER(I32)], I32),
+    "kt_qweight_shard": ([P, P, I32, I32, I32, P, PP], I32),
+    "kt_comm_unique_id": ([P], I32),
+    "kt_comm_init": ([P, I32, I32, P, PP], I32),
+    "kt_comm_destroy": ([P], I32),
+    "kt_qmatmul_row_parallel": ([P, P, P, P, P, I32, I32, F32, P, P], I32),
+    "kt_allgather_columns": ([P, P, P, I32, I32, P], I32),
 }
 
 _lib = None

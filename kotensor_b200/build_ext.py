@@ -63,7 +63,7 @@ def build(verbose: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, verbose), sources()))
     newest = max(os.path.getmtime(o) for o in objs)
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < newest:
-        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-ldl"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")

@@ -255,6 +255,11 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType type, uint32_t elem_by
                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+kt_status run_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
+                      float alpha, const float* bias, cudaStream_t s) {
+    return run_matmul(ctx, w, a, c, m, accumulate, alpha, bias, s);
+}
+
 }  // namespace kt
 
 using namespace kt;
@@ -461,6 +466,62 @@ kt_status kt_qweight_download(const kt_qweight* w, void* qdata, float* scales, u
 
 kt_status kt_qweight_free(kt_qweight* w) {
     free_weight(w);
+    return KT_OK;
+}
+
+kt_status kt_shard_bounds(int32_t axis, int32_t extent, int32_t group_size, int32_t parts, int32_t index,
+                          int32_t* begin, int32_t* end) {
+    if (!begin || !end) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (!shard_bounds(axis, extent, group_size, parts, index, begin, end))
+        return fail(KT_ERR_INVALID_ARGUMENT, "no shard " + std::to_string(index) + " of " + std::to_string(parts) +
+                                                 " along axis " + std::to_string(axis) + " of extent " +
+                                                 std::to_string(extent));
+    return KT_OK;
+}
+
+kt_status kt_qweight_shard(kt_ctx* ctx, const kt_qweight* w, int32_t axis, int32_t parts, int32_t index,
+                           void* stream, kt_qweight** out) {
+    if (!ctx || !w || !out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    int32_t b = 0, e = 0;
+    const int32_t extent = axis == 0 ? w->rows : w->columns;
+    kt_status st = kt_shard_bounds(axis, extent, w->group_size, parts, index, &b, &e);
+    if (st != KT_OK) return st;
+    kt_qweight* d = nullptr;
+    if ((st = alloc_weight(ctx, w->bits, w->group_size, axis == 0 ? e - b : w->rows, axis == 0 ? w->columns : e - b,
+                           &d)) != KT_OK)
+        return st;
+    cudaStream_t s = pick(ctx, stream);
+    cudaError_t err = cudaSuccess;
+    if (axis == 0) {
+        // whole groups: contiguous slices of every array
+        const int32_t g0 = b / w->group_size;
+        const size_t gcols = static_cast<size_t>(d->groups) * w->columns;
+        err = cudaMemcpyAsync(d->qdata, w->qdata + static_cast<size_t>(b) * w->bytes_per_row,
+                              static_cast<size_t>(d->rows) * d->bytes_per_row, cudaMemcpyDeviceToDevice, s);
+        if (err == cudaSuccess)
+            err = cudaMemcpyAsync(d->scales, w->scales + static_cast<size_t>(g0) * w->columns, gcols * sizeof(float),
+                                  cudaMemcpyDeviceToDevice, s);
+        if (err == cudaSuccess && w->bits == 4)
+            err = cudaMemcpyAsync(d->zeros, w->zeros + static_cast<size_t>(g0) * w->columns, gcols,
+                                  cudaMemcpyDeviceToDevice, s);
+    } else {
+        const size_t n = static_cast<size_t>(e - b);
+        if (w->bits == 8)
+            err = cudaMemcpy2DAsync(d->qdata, n, w->qdata + b, w->bytes_per_row, n, w->rows, cudaMemcpyDeviceToDevice, s);
+        else
+            err = launch_repack_int4_columns(w, b, d, s);
+        if (err == cudaSuccess)
+            err = cudaMemcpy2DAsync(d->scales, n * sizeof(float), w->scales + b, w->columns * sizeof(float),
+                                    n * sizeof(float), w->groups, cudaMemcpyDeviceToDevice, s);
+        if (err == cudaSuccess && w->bits == 4)
+            err = cudaMemcpy2DAsync(d->zeros, n, w->zeros + b, w->columns, n, w->groups, cudaMemcpyDeviceToDevice, s);
+    }
+    if (err != cudaSuccess) {
+        free_weight(d);
+        return cuda_fail(err, "kt_qweight_shard");
+    }
+    *out = d;
     return KT_OK;
 }
 

@@ -5,6 +5,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstdint>
 #include <mutex>
 #include <string>
@@ -83,6 +84,10 @@ inline QView view(const kt_qweight* w) {
                  w->has_tmap_raw64 ? &w->tmap_raw64 : nullptr};
 }
 
+// The dispatch behind kt_qmatmul (kt_api.cu): argument-checked by the caller.
+kt_status run_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
+                      float alpha, const float* bias, cudaStream_t s);
+
 // Zero-initialised device workspace of at least `bytes` for launches on stream
 // `s` (kt_api.cu).  Its first kWorkspaceReservedBytes hold the split-K arrival
 // counters of the INT4 GEMV and of the INT4 GEMM at fixed offsets (zero
@@ -145,6 +150,14 @@ bool gemm_tc_supported(const QView& w, int32_t m, const float* a);
 size_t gemm_tc_workspace_bytes(const QView& w, int32_t m, int sm_count);
 cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s, void* workspace,
                            size_t workspace_bytes);
+
+// ---- kt_shard.cu  (tensor-parallel shards)
+// [begin, end) of shard `index` of `parts` along rows (axis 0: whole groups of
+// group_size rows) or columns (axis 1); false for bad arguments or an empty shard.
+bool shard_bounds(int32_t axis, int32_t extent, int32_t group_size, int32_t parts, int32_t index, int32_t* begin,
+                  int32_t* end);
+// dst (INT4, allocated, dst->columns wide) <- columns [c0, c0 + dst->columns) of src, repacked.
+cudaError_t launch_repack_int4_columns(const kt_qweight* src, int32_t c0, const kt_qweight* dst, cudaStream_t s);
 
 // ---- kt_backward.cu
 cudaError_t launch_matmul_t(const QView& w, const float* dy, float* dx, int32_t m, int32_t accumulate,

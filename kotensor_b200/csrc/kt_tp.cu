@@ -1,0 +1,231 @@
+// kt_tp.cu -- tensor parallelism over NCCL for the quantized matmul: one
+// process per GPU, weights sharded with kt_qweight_shard (kt_shard.cu).
+//
+//   row-parallel    (split K, e.g. attention out / FFN down): each rank computes
+//                   alpha * a[:, K_r] . W_r, the partial products are summed with
+//                   ncclAllReduce, then c = (acc ? c : 0) + sum + bias on every rank.
+//   column-parallel (split N, e.g. q/k/v, gate/up, lm head): each rank computes
+//                   its columns with kt_qmatmul, no exchange; kt_allgather_columns
+//                   assembles [m x N] when a rank needs the whole output.
+//
+// NCCL is loaded at run time (dlopen of libnccl.so.2, or KT_NCCL_LIBRARY): the
+// rest of the library does not depend on it.  Calls on one communicator must be
+// issued in the same order on every rank, on one stream per rank.
+#include <dlfcn.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <mutex>
+#include <string>
+
+#include "kt_internal.h"
+
+namespace {
+
+// The few NCCL types and constants this file uses (nccl.h, NCCL 2.x ABI).
+typedef struct ncclComm* ncclComm_t;
+typedef struct {
+    char internal[128];
+} ncclUniqueId;
+typedef int ncclResult_t;
+constexpr int kNcclFloat32 = 7;
+constexpr int kNcclSum = 0;
+
+struct NcclApi {
+    bool ok = false;
+    std::string why;
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char* names[] = {std::getenv("KT_NCCL_LIBRARY"), "libnccl.so.2", "libnccl.so"};
+        void* h = nullptr;
+        for (const char* n : names)
+            if (n != nullptr && (h = dlopen(n, RTLD_NOW | RTLD_LOCAL)) != nullptr) break;
+        if (h == nullptr) {
+            api.why = "libnccl.so.2 not found (set KT_NCCL_LIBRARY)";
+            return;
+        }
+        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+        api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+        api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+        api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+        api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_reduce && api.all_gather &&
+                 api.error_string;
+        if (!api.ok) api.why = "libnccl.so.2 lacks an expected symbol";
+    });
+    return api;
+}
+
+kt_status fail_tp(kt_status st, const std::string& msg) {
+    kt::set_error(msg);
+    return st;
+}
+
+kt_status nccl_fail(ncclResult_t r, const char* what) {
+    return fail_tp(KT_ERR_NCCL, std::string(what) + ": " + nccl().error_string(r));
+}
+
+// c = (accumulate ? c : 0) + sum + bias[col]
+__global__ void row_parallel_epilogue_kernel(float* __restrict__ c, const float* __restrict__ sum,
+                                             const float* __restrict__ bias, int64_t total, int32_t n,
+                                             int32_t accumulate) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float r = sum[i] + (accumulate ? c[i] : 0.0f);
+        if (bias != nullptr) r += bias[i % n];
+        c[i] = r;
+    }
+}
+
+// gathered [P][m][ns] -> y [m][P * ns]
+__global__ void gather_columns_kernel(const float* __restrict__ gathered, float* __restrict__ y, int32_t parts,
+                                      int32_t m, int32_t ns) {
+    const int64_t total = static_cast<int64_t>(parts) * m * ns;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t p = i / (static_cast<int64_t>(m) * ns);
+        const int64_t rem = i - p * m * ns;
+        const int64_t t = rem / ns, j = rem - t * ns;
+        y[t * parts * ns + p * ns + j] = gathered[i];
+    }
+}
+
+int blocks_for(int64_t total) { return static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16)); }
+
+}  // namespace
+
+struct kt_comm {
+    kt_ctx* ctx = nullptr;
+    ncclComm_t comm = nullptr;
+    int32_t nranks = 0, rank = 0;
+    float* scratch = nullptr;  // partial sums / gathered columns, grown on demand
+    size_t scratch_floats = 0;
+};
+
+namespace {
+
+// Scratch of the communicator (calls on one communicator are ordered on one
+// stream, so they may share it).  Allocation is not a stream operation; it is
+// allowed in relaxed capture mode while that stream is being captured.
+cudaError_t comm_scratch(kt_comm* c, size_t floats, float** out) {
+    if (c->scratch_floats < floats) {
+        cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+        cudaThreadExchangeStreamCaptureMode(&mode);
+        float* p = nullptr;
+        cudaError_t e = cudaMalloc(&p, floats * sizeof(float));
+        cudaThreadExchangeStreamCaptureMode(&mode);
+        if (e != cudaSuccess) return e;
+        if (c->scratch != nullptr) {
+            cudaDeviceSynchronize();  // queued collectives may still use the old buffer
+            cudaFree(c->scratch);
+        }
+        c->scratch = p;
+        c->scratch_floats = floats;
+    }
+    *out = c->scratch;
+    return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" {
+
+kt_status kt_comm_unique_id(void* id_out) {
+    if (!id_out) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    const NcclApi& api = nccl();
+    if (!api.ok) return fail_tp(KT_ERR_NCCL, api.why);
+    ncclUniqueId id;
+    const ncclResult_t r = api.get_unique_id(&id);
+    if (r != 0) return nccl_fail(r, "ncclGetUniqueId");
+    std::memcpy(id_out, &id, sizeof(id));
+    return KT_OK;
+}
+
+kt_status kt_comm_init(kt_ctx* ctx, int32_t nranks, int32_t rank, const void* unique_id, kt_comm** out) {
+    if (!ctx || !unique_id || !out) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    if (nranks <= 0 || rank < 0 || rank >= nranks)
+        return fail_tp(KT_ERR_INVALID_ARGUMENT, "rank " + std::to_string(rank) + " of " + std::to_string(nranks));
+    const NcclApi& api = nccl();
+    if (!api.ok) return fail_tp(KT_ERR_NCCL, api.why);
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof(id));
+    auto* c = new (std::nothrow) kt_comm();
+    if (!c) return fail_tp(KT_ERR_OUT_OF_MEMORY, "host allocation failed");
+    const ncclResult_t r = api.comm_init_rank(&c->comm, nranks, id, rank);
+    if (r != 0) {
+        delete c;
+        return nccl_fail(r, "ncclCommInitRank");
+    }
+    c->ctx = ctx;
+    c->nranks = nranks;
+    c->rank = rank;
+    *out = c;
+    return KT_OK;
+}
+
+kt_status kt_comm_destroy(kt_comm* c) {
+    if (!c) return KT_OK;
+    cudaSetDevice(c->ctx->device);
+    cudaDeviceSynchronize();
+    if (c->comm != nullptr) nccl().comm_destroy(c->comm);
+    cudaFree(c->scratch);
+    delete c;
+    return KT_OK;
+}
+
+kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* w_shard, const float* a_shard,
+                                  float* c, int32_t m, int32_t accumulate, float alpha, const float* bias,
+                                  void* stream) {
+    if (!ctx || !comm || !w_shard) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (m < 0) return fail_tp(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
+    if (m == 0) return KT_OK;
+    if (!a_shard || !c) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t total = static_cast<int64_t>(m) * w_shard->columns;
+    float* sum = nullptr;
+    cudaError_t e = comm_scratch(comm, static_cast<size_t>(total), &sum);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_OUT_OF_MEMORY, std::string("TP scratch: ") + cudaGetErrorString(e));
+    // partial = alpha * a_shard . W_shard
+    kt_status st = kt::run_qmatmul(ctx, w_shard, a_shard, sum, m, 0, alpha, nullptr, s);
+    if (st != KT_OK) return st;
+    const ncclResult_t r = nccl().all_reduce(sum, sum, static_cast<size_t>(total), kNcclFloat32, kNcclSum, comm->comm, s);
+    if (r != 0) return nccl_fail(r, "ncclAllReduce");
+    row_parallel_epilogue_kernel<<<blocks_for(total), 256, 0, s>>>(c, sum, bias, total, w_shard->columns, accumulate);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("row-parallel epilogue: ") + cudaGetErrorString(e));
+    return KT_OK;
+}
+
+kt_status kt_allgather_columns(kt_comm* comm, const float* y_shard, float* y_full, int32_t m, int32_t n_shard,
+                               void* stream) {
+    if (!comm || !y_shard || !y_full) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (m <= 0 || n_shard <= 0) return fail_tp(KT_ERR_INVALID_ARGUMENT, "empty shard");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t per = static_cast<int64_t>(m) * n_shard;
+    float* gathered = nullptr;
+    cudaError_t e = comm_scratch(comm, static_cast<size_t>(per * comm->nranks), &gathered);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_OUT_OF_MEMORY, std::string("TP scratch: ") + cudaGetErrorString(e));
+    const ncclResult_t r = nccl().all_gather(y_shard, gathered, static_cast<size_t>(per), kNcclFloat32, comm->comm, s);
+    if (r != 0) return nccl_fail(r, "ncclAllGather");
+    gather_columns_kernel<<<blocks_for(per * comm->nranks), 256, 0, s>>>(gathered, y_full, comm->nranks, m, n_shard);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("gather columns: ") + cudaGetErrorString(e));
+    return KT_OK;
+}
+
+}  // extern "C"

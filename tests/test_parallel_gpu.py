@@ -1,0 +1,127 @@
+"""GPU checks of tensor parallelism: device shards (kt_qweight_shard) against
+the host restatement and the quantized fp32 slices, the NCCL row-parallel
+product and column gather on one rank, and on two GPUs when the box has them."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+TOL_FP32 = 1e-3
+
+
+def rel_err(y, ref):
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+@pytest.mark.parametrize("bits,g", [(4, 64), (4, 32), (8, 64)])
+@pytest.mark.parametrize("shape", [(4096, 1024), (256, 1537), (960, 96)])
+@pytest.mark.parametrize("parts", [2, 3, 8])
+def test_device_shards_equal_host_shards(kt, oracle, bits, g, shape, parts):
+    from kotensor_b200 import parallel as P
+    rng = np.random.default_rng(sum(shape) * bits + parts)
+    w = (rng.standard_normal(shape, dtype=np.float32) * 0.03).astype(np.float32)
+    ref = oracle.quantize(w, bits, g)
+    qt = kt.QuantizedTensor.from_arrays(ref.qdata, ref.scales, ref.zeros, shape, bits, g)
+    for axis in (P.ROWS, P.COLUMNS):
+        if axis == P.ROWS and parts > (shape[0] + g - 1) // g:
+            continue
+        for i in range(parts):
+            d = P.shard(qt, axis, parts, i)
+            q, s, z = d.download()
+            hq, hs, hz, hsh = P.shard_host(ref.qdata, ref.scales, ref.zeros, shape, bits, g, axis, parts, i)
+            assert d.shape == hsh
+            assert np.array_equal(q.reshape(-1), hq.reshape(-1))
+            assert np.array_equal(s.reshape(-1).view(np.uint32), hs.reshape(-1).view(np.uint32))
+            if bits == 4:
+                assert np.array_equal(z.reshape(-1), hz.reshape(-1))
+
+
+def test_row_parallel_and_gather_on_one_rank(kt):
+    from kotensor_b200 import parallel as P
+    comm = P.Comm(1, 0, P.Comm.unique_id())
+    try:
+        k, n, m = 2048, 1024, 4
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(3)
+        w = torch.randn((k, n), generator=gen, device="cuda") * 0.02
+        qt = kt.QuantizedTensor.quantize(w, kt.Quantization(4))
+        x = torch.randn((m, k), generator=gen, device="cuda")
+        bias = torch.randn(n, generator=gen, device="cuda")
+        c0 = torch.randn((m, n), generator=gen, device="cuda")
+        ref = c0.clone()
+        kt.MatMul.multiply_quantized(x, qt, ref, m, accumulate=True, alpha=0.5, bias=bias)
+        shard = P.shard(qt, P.ROWS, 1, 0)
+        y = c0.clone()
+        P.matmul_row_parallel(comm, x, shard, y, m, accumulate=True, alpha=0.5, bias=bias)
+        full = torch.empty((m, n), device="cuda")
+        P.allgather_columns(comm, y, full, m)
+        torch.cuda.synchronize()
+        assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) <= TOL_FP32
+        assert torch.equal(full, y)
+    finally:
+        comm.close()
+    assert kt.Context.get().take_error() == 0
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _two_gpu_rank(rank, world, port, out_dir):
+    from datetime import timedelta
+    import torch.distributed as dist
+    import kotensor_b200 as kt
+    from kotensor_b200 import parallel as P
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    comm = None
+    try:
+        ctx = kt.Context.get(rank)
+        comm = P.Comm.from_process_group(ctx=ctx)
+        k, n, m = 4096, 2048, 4
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(11)  # same weights and inputs on every rank
+        w = torch.randn((k, n), generator=gen, device="cuda") * 0.02
+        x = torch.randn((m, k), generator=gen, device="cuda")
+        bias = torch.randn(n, generator=gen, device="cuda")
+        qt = kt.QuantizedTensor.quantize(w, kt.Quantization(4))
+        ref = torch.empty((m, n), device="cuda")
+        kt.MatMul.multiply_quantized(x, qt, ref, m, accumulate=False, bias=bias)
+        row = P.RowParallelQuantizedLinear(qt, comm, bias)
+        y_row = torch.empty((m, n), device="cuda")
+        row.forward_into(x[:, row.k_begin:row.k_end], y_row)
+        col = P.ColumnParallelQuantizedLinear(qt, comm, bias)
+        ys = torch.empty((m, col.n_end - col.n_begin), device="cuda")
+        col.forward_into(x, ys)
+        y_col = torch.empty((m, n), device="cuda")
+        col.gather_into(ys, y_col)
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"r{rank}.npy"),
+                np.stack([ref.cpu().numpy(), y_row.cpu().numpy(), y_col.cpu().numpy()]))
+        assert ctx.take_error() == 0
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_on_two_gpus(kt, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_two_gpu_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        ref, y_row, y_col = np.load(tmp_path / f"r{r}.npy")
+        assert rel_err(y_row, ref) <= TOL_FP32
+        assert rel_err(y_col, ref) <= TOL_FP32
