@@ -1,4 +1,4 @@
-// kt_gemm_tc.cu -- INT4 dequantizing GEMM on the 5th-generation tensor cores:
+// kt_gemm_tc.cu -- INT4 / INT8 dequantizing GEMM on the 5th-generation tensor cores:
 // MatMul.multiplyQuantized (Engine/kotensor/src/main/kotlin/MatMul.kt:460-486)
 // for m >= 9, the tile path of the reference (computeQuantizedTile,
 // MatMul.kt:830-952) used by prefill and batched decode.
@@ -202,9 +202,13 @@ __device__ __forceinline__ int atomic_add_acq_rel(int32_t* p, int v) {
 }
 __device__ __forceinline__ void workers_barrier() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkers * 32) : "memory"); }
 
+// BITS = 4: a CTA's 128 packed bytes are 256 output columns (two A tiles, two
+// accumulators); BITS = 8: 128 output columns (one A tile, one accumulator).
+template <int BITS>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                    GemmParams p) {
+    constexpr int kCT = BITS == 4 ? 2 * kTileBytes : kTileBytes;  // output columns per CTA
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     __shared__ int s_last;
     const int warp = threadIdx.x >> 5;
@@ -254,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kProducerWarp) {
         if (lane == 0) {
             const uint32_t tx = static_cast<uint32_t>(kRawBytes + p.nt * kBK * 2);
-            const uint32_t gbytes = static_cast<uint32_t>(tile_cols) * 10;
+            const uint32_t gbytes = static_cast<uint32_t>(tile_cols) * (BITS == 4 ? 10 : 4);
             int issued = 0;
             for (int i = 0; i < n_kb; ++i) {
                 const int s = i % kStages;
@@ -273,9 +277,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t dst = scl + s * kScaleStageBytes + (g - ga) * kGroupSlotBytes;
                     const int64_t go = static_cast<int64_t>(g) * p.N;
                     bulk_load(dst, p.scales + go + tile_b0, tile_cols * 4, full_raw(s));
-                    bulk_load(dst + kTileBytes * 4, p.scales + go + p.R + tile_b0, tile_cols * 4, full_raw(s));
-                    bulk_load(dst + kTileBytes * 8, p.zeros + go + tile_b0, tile_cols, full_raw(s));
-                    bulk_load(dst + kTileBytes * 9, p.zeros + go + p.R + tile_b0, tile_cols, full_raw(s));
+                    if constexpr (BITS == 4) {
+                        bulk_load(dst + kTileBytes * 4, p.scales + go + p.R + tile_b0, tile_cols * 4, full_raw(s));
+                        bulk_load(dst + kTileBytes * 8, p.zeros + go + tile_b0, tile_cols, full_raw(s));
+                        bulk_load(dst + kTileBytes * 9, p.zeros + go + p.R + tile_b0, tile_cols, full_raw(s));
+                    }
                 }
                 ++issued;
             }
@@ -300,7 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t bdesc = umma_desc_sw128(xs + kk * 32);
                     const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
                     umma_bf16(tmem, umma_desc_sw128(alo + kk * 32), bdesc, p.idesc, acc);
-                    umma_bf16(tmem + p.nt_cols, umma_desc_sw128(ahi + kk * 32), bdesc, p.idesc, acc);
+                    if constexpr (BITS == 4)
+                        umma_bf16(tmem + p.nt_cols, umma_desc_sw128(ahi + kk * 32), bdesc, p.idesc, acc);
                 }
                 umma_commit(empty(s));  // the stage is free once these MMAs have read it
             }
@@ -340,26 +347,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int c = lane + 32 * c4;
                 // columns beyond the tile's bytes read stale slot data; their A rows
                 // only reach accumulator rows that are never stored
-                const uint32_t s2_lo = bf2_splat(sc_lo[c]), s2_hi = bf2_splat(sc_hi[c]);
-                const uint32_t zb_lo = bf2_splat(128.0f + static_cast<float>(z_lo[c]));
-                const uint32_t zb_hi = bf2_splat(128.0f + static_cast<float>(z_hi[c]));
                 uint32_t b[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) b[j] = raw[(8 * warp + j) * kTileBytes + c];
-                uint4 vlo, vhi;
-                uint32_t* wl = &vlo.x;
-                uint32_t* wh = &vhi.x;
-#pragma unroll
-                for (int jp = 0; jp < 4; ++jp) {
-                    const uint32_t pr = prmt(b[2 * jp], b[2 * jp + 1], 0x5410u);  // rows 2jp, 2jp+1 in the halves
-                    const uint32_t ql = lop3_and_or(pr, 0x000F000Fu, 0x43004300u);
-                    const uint32_t qh = lop3_and_or(pr >> 4, 0x000F000Fu, 0x43004300u);
-                    wl[jp] = bf2_sub_mul(ql, zb_lo, s2_lo);
-                    wh[jp] = bf2_sub_mul(qh, zb_hi, s2_hi);
-                }
                 const uint32_t off = static_cast<uint32_t>(c * 128 + ((warp ^ (c & 7)) << 4));
-                *reinterpret_cast<uint4*>(alo + off) = vlo;
-                *reinterpret_cast<uint4*>(ahi + off) = vhi;
+                if constexpr (BITS == 4) {
+                    const uint32_t s2_lo = bf2_splat(sc_lo[c]), s2_hi = bf2_splat(sc_hi[c]);
+                    const uint32_t zb_lo = bf2_splat(128.0f + static_cast<float>(z_lo[c]));
+                    const uint32_t zb_hi = bf2_splat(128.0f + static_cast<float>(z_hi[c]));
+                    uint4 vlo, vhi;
+                    uint32_t* wl = &vlo.x;
+                    uint32_t* wh = &vhi.x;
+#pragma unroll
+                    for (int jp = 0; jp < 4; ++jp) {
+                        const uint32_t pr = prmt(b[2 * jp], b[2 * jp + 1], 0x5410u);  // rows 2jp, 2jp+1 in the halves
+                        const uint32_t ql = lop3_and_or(pr, 0x000F000Fu, 0x43004300u);
+                        const uint32_t qh = lop3_and_or(pr >> 4, 0x000F000Fu, 0x43004300u);
+                        wl[jp] = bf2_sub_mul(ql, zb_lo, s2_lo);
+                        wh[jp] = bf2_sub_mul(qh, zb_hi, s2_hi);
+                    }
+                    *reinterpret_cast<uint4*>(alo + off) = vlo;
+                    *reinterpret_cast<uint4*>(ahi + off) = vhi;
+                } else {
+                    // signed byte q: 2^23 + (q + 128) as a float (byte ^ 0x80 in the
+                    // mantissa) minus 2^23 + 128 is exactly q; one fp32 multiply by
+                    // the scale as the reference (QuantizedTensor.kt:201), then bf16
+                    const float sc = sc_lo[c];
+                    uint4 v;
+                    uint32_t* wv = &v.x;
+#pragma unroll
+                    for (int jp = 0; jp < 4; ++jp) {
+                        const float q0 = __uint_as_float(b[2 * jp] ^ 0x4B000080u) - 8388736.0f;
+                        const float q1 = __uint_as_float(b[2 * jp + 1] ^ 0x4B000080u) - 8388736.0f;
+                        wv[jp] = pack_bf16(__fmul_rn(sc, q0), __fmul_rn(sc, q1));
+                    }
+                    *reinterpret_cast<uint4*>(alo + off) = v;
+                }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> MMA reads
             __syncwarp();
@@ -371,13 +394,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!have && lane == 0) atomicOr(p.err, 1);
         tc_fence_after();
         const int quarter = warp & 3;
-        const int nib = warp >> 2;
-        const int c = 32 * quarter + lane;  // 0..127 in this accumulator
-        const int col256 = nib * 128 + c;   // 0..255 in the CTA's partial tile
-        const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + (nib ? p.nt_cols : 0);
-        auto emit = [&](int tok, int col256, float v) {
-            const int cb = tile_b0 + (col256 & 127);
-            const int oc = col256 < 128 ? cb : p.R + cb;
+        const int half_w = warp >> 2;  // INT4: low / high accumulator; INT8: even / odd token chunks
+        const int c = 32 * quarter + lane;  // 0..127 in the accumulator
+        const int colt = BITS == 4 ? half_w * 128 + c : c;  // column of the CTA's partial tile
+        const uint32_t taddr =
+            tmem + (static_cast<uint32_t>(32 * quarter) << 16) + (BITS == 4 && half_w ? p.nt_cols : 0);
+        auto emit = [&](int tok, int col, float v) {
+            const int cb = tile_b0 + (col & 127);
+            const int oc = (BITS == 4 && col >= 128) ? p.R + cb : cb;
             if (!have || cb >= p.R || oc >= p.N || tok >= p.M) return;
             float* out = p.y + static_cast<int64_t>(tok) * p.N + oc;
             float r = fmaf(p.alpha, v, p.accumulate ? *out : 0.0f);
@@ -386,17 +410,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         const int S = gridDim.z;
         const int64_t tile_id = static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x;
-        float* parts = p.partials + tile_id * S * (static_cast<int64_t>(p.nt) * 256);  // [S][nt][256]
-        for (int t0 = 0; t0 < p.nt; t0 += 16) {
+        float* parts = p.partials + tile_id * S * (static_cast<int64_t>(p.nt) * kCT);  // [S][nt][kCT]
+        for (int t0 = (BITS == 4 ? 0 : 16 * half_w); t0 < p.nt; t0 += (BITS == 4 ? 16 : 32)) {
             float v[16];
-            tmem_ld16(taddr + t0, v);  // every lane takes part (.sync.aligned)
+            tmem_ld16(taddr + t0, v);  // every lane of the warp takes part (.sync.aligned)
             if (S == 1) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) emit(tok0 + t0 + j, col256, v[j]);
+                for (int j = 0; j < 16; ++j) emit(tok0 + t0 + j, colt, v[j]);
             } else {
-                float* mine = parts + static_cast<int64_t>(blockIdx.z) * p.nt * 256;
+                float* mine = parts + static_cast<int64_t>(blockIdx.z) * p.nt * kCT;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) __stcg(mine + (t0 + j) * 256 + col256, v[j]);
+                for (int j = 0; j < 16; ++j) __stcg(mine + (t0 + j) * kCT + colt, v[j]);
             }
         }
         if (S > 1) {
@@ -408,26 +432,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 s_last = atomic_add_acq_rel(p.tickets + tile_id, 1) == S - 1;
             workers_barrier();
             if (s_last) {
-                // thread: 4 adjacent columns, every 4th token, two tokens in flight
-                const int q4 = (threadIdx.x & 63) * 4;
-                for (int t = threadIdx.x >> 6; t < p.nt; t += 8) {
-                    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
-                    const bool two = t + 4 < p.nt;
+                // thread: 4 adjacent columns of one token at a time, tokens strided
+                constexpr int kQuads = kCT / 4;
+                const int q4 = (threadIdx.x % kQuads) * 4;
+#pragma unroll 2
+                for (int t = threadIdx.x / kQuads; t < p.nt; t += kWorkers * 32 / kQuads) {
+                    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f);
                     for (int sp = 0; sp < S; ++sp) {
-                        const float* src = parts + static_cast<int64_t>(sp) * p.nt * 256 + q4;
-                        const float4 u = __ldcg(reinterpret_cast<const float4*>(src + t * 256));
+                        const float4 u = __ldcg(reinterpret_cast<const float4*>(
+                            parts + (static_cast<int64_t>(sp) * p.nt + t) * kCT + q4));
                         a0.x += u.x; a0.y += u.y; a0.z += u.z; a0.w += u.w;
-                        if (two) {
-                            const float4 w4 = __ldcg(reinterpret_cast<const float4*>(src + (t + 4) * 256));
-                            a1.x += w4.x; a1.y += w4.y; a1.z += w4.z; a1.w += w4.w;
-                        }
                     }
                     emit(tok0 + t, q4, a0.x); emit(tok0 + t, q4 + 1, a0.y);
                     emit(tok0 + t, q4 + 2, a0.z); emit(tok0 + t, q4 + 3, a0.w);
-                    if (two) {
-                        emit(tok0 + t + 4, q4, a1.x); emit(tok0 + t + 4, q4 + 1, a1.y);
-                        emit(tok0 + t + 4, q4 + 2, a1.z); emit(tok0 + t + 4, q4 + 3, a1.w);
-                    }
                 }
                 if (threadIdx.x == 0) p.tickets[tile_id] = 0;  // ready for the next launch on this workspace
             }
@@ -479,7 +496,7 @@ size_t x_bytes(const QView& w, int m) { return align256(static_cast<size_t>(m) *
 }  // namespace
 
 bool gemm_tc_supported(const QView& w, int32_t m, const float* a) {
-    if (w.bits != 4 || m < 9 || w.tmap_raw64 == nullptr) return false;
+    if ((w.bits != 4 && w.bits != 8) || m < 9 || w.tmap_raw64 == nullptr) return false;
     if (a != nullptr && reinterpret_cast<uintptr_t>(a) % 16 != 0) return false;
     return w.rows % 8 == 0 && w.group_size % 32 == 0 && w.columns % 32 == 0;
 }
@@ -521,7 +538,7 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
     p.nt = nt_for(a.m);
     p.nt_cols = p.nt;
     int cols = 32;
-    while (cols < 2 * p.nt) cols *= 2;
+    while (cols < (w.bits == 4 ? 2 : 1) * p.nt) cols *= 2;
     p.tmem_cols = cols;
     // kind::f16: D f32 (bits 4-5 = 1), A bf16 (7-9 = 1), B bf16 (10-12 = 1),
     // both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
@@ -538,11 +555,11 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
                         static_cast<uint64_t>(a.m), static_cast<uint64_t>(w.rows) * 2, kBK,
                         static_cast<uint32_t>(p.nt), CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes));
+    auto kernel = w.bits == 4 ? gemm_tc_kernel<4> : gemm_tc_kernel<8>;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
     const dim3 grid((w.bytes_per_row + kTileBytes - 1) / kTileBytes, (a.m + p.nt - 1) / p.nt, S);
-    gemm_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(*w.tmap_raw64, tmap_x, p);
+    kernel<<<grid, kThreads, kSmemBytes, s>>>(*w.tmap_raw64, tmap_x, p);
     return cudaGetLastError();
 }
 

@@ -402,3 +402,23 @@ def test_int4_tensor_core_gemm_matches_the_oracle(kt, oracle, m, k, n, g):
     ref = oracle.multiply_quantized(a, ref_t, c=c0, accumulate=True, alpha=0.5, threads=8) + bias[None, :]
     assert rel_err(y, ref) <= TOL_BF16, rel_err(y, ref)
     assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("k,n,g", [(2048, 2048, 64), (4096, 1024, 64), (960, 2048, 96), (1024, 4096, 32)])
+@pytest.mark.parametrize("m", [9, 64, 200, 512])
+def test_int8_tensor_core_gemm_matches_the_oracle(kt, oracle, m, k, n, g):
+    """The tcgen05 bf16 GEMM on INT8 weights (BASELINE config 1 at M = 64 and
+    around it), accumulate / alpha / bias, within the bf16 tolerance."""
+    from kotensor_b200 import _lib
+    rng = np.random.default_rng(k * 5 + n + m + g)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 8, g)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, None, (k, n), 8, g)
+    assert qt.matmul_path(m) == _lib.KT_PATH_TENSOR_CORE
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    c0 = rng.standard_normal((m, n), dtype=np.float32)
+    bias = rng.standard_normal(n, dtype=np.float32)
+    y = run_matmul(kt, qt, a, c0=c0, accumulate=True, alpha=0.5, bias=bias)
+    ref = oracle.multiply_quantized(a, ref_t, c=c0, accumulate=True, alpha=0.5, threads=8) + bias[None, :]
+    assert rel_err(y, ref) <= TOL_BF16, rel_err(y, ref)
+    assert kt.Context.get().take_error() == 0
