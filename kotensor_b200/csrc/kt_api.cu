@@ -613,7 +613,12 @@ kt_status kt_qmatmul_t(kt_ctx* ctx, const kt_qweight* w, const float* dy, float*
     if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
     if (m == 0) return KT_OK;
     if (!dy || !dx) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
-    KT_CUDA_TRY(launch_matmul_t(view(w), dy, dx, m, accumulate, pick(ctx, stream)), "qmatmul_t launch");
+    const QView v = view(w);
+    const cudaStream_t s = pick(ctx, stream);
+    const size_t need = matmul_t_workspace_bytes(v, m);
+    void* ws = nullptr;
+    if (need > 0) KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "qmatmul_t workspace");
+    KT_CUDA_TRY(launch_matmul_t(v, dy, dx, m, accumulate, s, ws, need), "qmatmul_t launch");
     return KT_OK;
 }
 

@@ -160,7 +160,9 @@ bool shard_bounds(int32_t axis, int32_t extent, int32_t group_size, int32_t part
 cudaError_t launch_repack_int4_columns(const kt_qweight* src, int32_t c0, const kt_qweight* dst, cudaStream_t s);
 
 // ---- kt_backward.cu
+// Workspace of one call (0: none); the per-chunk partial sums follow the reserved front.
+size_t matmul_t_workspace_bytes(const QView& w, int32_t m);
 cudaError_t launch_matmul_t(const QView& w, const float* dy, float* dx, int32_t m, int32_t accumulate,
-                            cudaStream_t s);
+                            cudaStream_t s, void* workspace, size_t workspace_bytes);
 
 }  // namespace kt
