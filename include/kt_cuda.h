@@ -221,6 +221,47 @@ kt_status kt_qmatmul_host(kt_ctx* ctx, const kt_qweight* w, const float* a_host,
 kt_status kt_qmatmul_t(kt_ctx* ctx, const kt_qweight* w, const float* dy_dev, float* dx_dev, int32_t m,
                        int32_t accumulate, void* stream);
 
+/* ------------------------------------------------------------ decode step
+ * The device-resident pieces of Transformer.decode around the quantized
+ * matmul (Transformer.kt:141-154, TransformerBlock.kt:40-47,
+ * Attention.kt:207-239 and :295-328).  Positions and token ids are read from
+ * device memory so that a whole step can be captured into a CUDA graph.
+ * KV cache layout is the reference's (KVCache.kt:3-59): fp32
+ * [layers][kv_heads][max_seq][head_dim] for keys and for values. */
+
+/* RMSNorm.forwardInto (RMSNorm.kt:71-90), `rows` rows of `dim`. */
+kt_status kt_rmsnorm(kt_ctx* ctx, const float* x_dev, const float* weight_dev, float* out_dev, int32_t rows,
+                     int32_t dim, float eps, void* stream);
+/* RoPE.applyInPlace / applyRowsInPlace (RoPE.kt:117-155): row r of v [rows x width]
+ * at position *position_dev + r, heads of head_dim, pairs (i, i + head_dim/2),
+ * inv_freq_dev [head_dim/2] as RoPE.invFreq (RoPE.kt:39-42, Llama-3 scaling included). */
+kt_status kt_rope(kt_ctx* ctx, float* v_dev, int32_t rows, int32_t width, int32_t head_dim, const float* inv_freq_dev,
+                  const int32_t* position_dev, void* stream);
+/* The cache writes of Attention.decodeInto / prefillInto (Attention.kt:225-232). */
+kt_status kt_kv_store(kt_ctx* ctx, const float* k_dev, const float* v_dev, float* k_cache, float* v_cache,
+                      int32_t rows, int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t layer,
+                      const int32_t* position_dev, void* stream);
+/* attendHead for every query head of one token at *position_dev (Attention.kt:295-328):
+ * scores (dot * scale) over positions 0..pos, softmax from the reference's -1e9
+ * initial maximum, context = weighted sum of values.  scores_dev: [heads x max_seq] scratch. */
+kt_status kt_attention_decode(kt_ctx* ctx, const float* q_dev, const float* k_cache, const float* v_cache,
+                              float* context_dev, float* scores_dev, int32_t heads, int32_t kv_heads,
+                              int32_t head_dim, int32_t max_seq, int32_t layer, float scale,
+                              const int32_t* position_dev, void* stream);
+/* gate = silu(gate) * up (SwiGLU.forwardInto, Tensor.kt:231-237). */
+kt_status kt_silu_mul(kt_ctx* ctx, float* gate_dev, const float* up_dev, int64_t n, void* stream);
+/* x += y (Tensor.addInPlace). */
+kt_status kt_add(kt_ctx* ctx, float* x_dev, const float* y_dev, int64_t n, void* stream);
+/* argmaxOfLastToken per row (Transformer.kt:255-266): the largest logit above
+ * -1e9, the lowest index among equal ones, 0 if none. */
+kt_status kt_argmax(kt_ctx* ctx, const float* logits_dev, int32_t rows, int32_t n, int32_t* out_dev, void* stream);
+/* QuantizedTensor.dequantizeColumn(*column_dev) (the tied embedding lookup, Embedding.kt:129-135):
+ * out_dev [rows]; an out-of-range column sets KT_ERR_INVALID_ARGUMENT in *status_dev. */
+kt_status kt_dequantize_column(kt_ctx* ctx, const kt_qweight* w, const int32_t* column_dev, float* out_dev,
+                               int32_t* status_dev, void* stream);
+/* *value_dev += delta on `stream` (advances a captured step's position). */
+kt_status kt_increment(kt_ctx* ctx, int32_t* value_dev, int32_t delta, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -622,4 +622,80 @@ kt_status kt_qmatmul_t(kt_ctx* ctx, const kt_qweight* w, const float* dy, float*
     return KT_OK;
 }
 
+// ---- decode step (kt_decode.cu)
+
+kt_status kt_rmsnorm(kt_ctx* ctx, const float* x, const float* weight, float* out, int32_t rows, int32_t dim, float eps,
+                     void* stream) {
+    if (!ctx || !x || !weight || !out || rows <= 0 || dim <= 0) return fail(KT_ERR_INVALID_ARGUMENT, "bad rmsnorm arguments");
+    KT_CUDA_TRY(launch_rmsnorm(x, weight, out, rows, dim, eps, pick(ctx, stream)), "rmsnorm launch");
+    return KT_OK;
+}
+
+kt_status kt_rope(kt_ctx* ctx, float* v, int32_t rows, int32_t width, int32_t head_dim, const float* inv_freq,
+                  const int32_t* position_dev, void* stream) {
+    if (!ctx || !v || !inv_freq || !position_dev || rows <= 0 || head_dim <= 0 || head_dim % 2 != 0 ||
+        width % head_dim != 0)
+        return fail(KT_ERR_INVALID_ARGUMENT, "bad rope arguments");
+    KT_CUDA_TRY(launch_rope(v, rows, width, head_dim, inv_freq, position_dev, pick(ctx, stream)), "rope launch");
+    return KT_OK;
+}
+
+kt_status kt_kv_store(kt_ctx* ctx, const float* k, const float* v, float* k_cache, float* v_cache, int32_t rows,
+                      int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t layer, const int32_t* position_dev,
+                      void* stream) {
+    if (!ctx || !k || !v || !k_cache || !v_cache || !position_dev || rows <= 0 || kv_heads <= 0 || head_dim <= 0 ||
+        max_seq <= 0 || layer < 0)
+        return fail(KT_ERR_INVALID_ARGUMENT, "bad kv_store arguments");
+    KT_CUDA_TRY(launch_kv_store(k, v, k_cache, v_cache, rows, kv_heads, head_dim, max_seq, layer, position_dev,
+                                pick(ctx, stream)),
+                "kv_store launch");
+    return KT_OK;
+}
+
+kt_status kt_attention_decode(kt_ctx* ctx, const float* q, const float* k_cache, const float* v_cache, float* context,
+                              float* scores, int32_t heads, int32_t kv_heads, int32_t head_dim, int32_t max_seq,
+                              int32_t layer, float scale, const int32_t* position_dev, void* stream) {
+    if (!ctx || !q || !k_cache || !v_cache || !context || !scores || !position_dev || heads <= 0 || kv_heads <= 0 ||
+        heads % kv_heads != 0 || head_dim <= 0 || max_seq <= 0 || layer < 0)
+        return fail(KT_ERR_INVALID_ARGUMENT, "bad attention arguments");
+    KT_CUDA_TRY(launch_attention_decode(q, k_cache, v_cache, context, scores, heads, kv_heads, head_dim, max_seq,
+                                        layer, scale, position_dev, pick(ctx, stream)),
+                "attention launch");
+    return KT_OK;
+}
+
+kt_status kt_silu_mul(kt_ctx* ctx, float* gate, const float* up, int64_t n, void* stream) {
+    if (!ctx || !gate || !up || n < 0) return fail(KT_ERR_INVALID_ARGUMENT, "bad silu_mul arguments");
+    if (n == 0) return KT_OK;
+    KT_CUDA_TRY(launch_silu_mul(gate, up, n, pick(ctx, stream)), "silu_mul launch");
+    return KT_OK;
+}
+
+kt_status kt_add(kt_ctx* ctx, float* x, const float* y, int64_t n, void* stream) {
+    if (!ctx || !x || !y || n < 0) return fail(KT_ERR_INVALID_ARGUMENT, "bad add arguments");
+    if (n == 0) return KT_OK;
+    KT_CUDA_TRY(launch_add(x, y, n, pick(ctx, stream)), "add launch");
+    return KT_OK;
+}
+
+kt_status kt_argmax(kt_ctx* ctx, const float* logits, int32_t rows, int32_t n, int32_t* out_dev, void* stream) {
+    if (!ctx || !logits || !out_dev || rows <= 0 || n <= 0) return fail(KT_ERR_INVALID_ARGUMENT, "bad argmax arguments");
+    KT_CUDA_TRY(launch_argmax(logits, rows, n, out_dev, pick(ctx, stream)), "argmax launch");
+    return KT_OK;
+}
+
+kt_status kt_dequantize_column(kt_ctx* ctx, const kt_qweight* w, const int32_t* column_dev, float* out_dev,
+                               int32_t* status_dev, void* stream) {
+    if (!ctx || !w || !column_dev || !out_dev) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    KT_CUDA_TRY(launch_dequantize_column(view(w), column_dev, out_dev, status_dev, pick(ctx, stream)),
+                "dequantize_column launch");
+    return KT_OK;
+}
+
+kt_status kt_increment(kt_ctx* ctx, int32_t* value_dev, int32_t delta, void* stream) {
+    if (!ctx || !value_dev) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    KT_CUDA_TRY(launch_increment(value_dev, delta, pick(ctx, stream)), "increment launch");
+    return KT_OK;
+}
+
 }  // extern "C"

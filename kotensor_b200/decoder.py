@@ -1,0 +1,218 @@
+"""Device-resident greedy decode step: Transformer.decode
+(Engine/kotensor/src/main/kotlin/Transformer.kt:141-154) with every layer
+(TransformerBlock.decodeInto, TransformerBlock.kt:40-47; Attention.decodeInto,
+Attention.kt:207-239; SwiGLU.forwardInto, SwiGLU.kt:19-25) on the GPU: the
+projections are the quantized matmul (kt_qmatmul, with QuantizedLinear's bias),
+the rest are the decode kernels of libkt_cuda.so (kt_rmsnorm, kt_rope,
+kt_kv_store, kt_attention_decode, kt_silu_mul, kt_add, kt_argmax, the
+quantized / tied embedding lookups).  The token id and position live on the
+device, so one step is captured into a CUDA graph and replayed per token with
+no host work between tokens.  The KV cache has the reference's layout
+(KVCache.kt:3-59): fp32 [layers][kvHeads][maxSeq][headDim].
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+from . import _lib
+from .quantized import Context, MatMul, QuantizedTensor
+
+try:
+    import torch
+except ImportError:  # pragma: no cover
+    torch = None
+
+
+@dataclass
+class DecoderConfig:
+    """Transformer(vocabularySize, dimension, numLayers, numHeads, hiddenDimension,
+    numKeyValueHeads, normEps, ropeTheta, ropeScaling, quantization), Transformer.kt:3-14."""
+    vocab: int
+    dim: int
+    layers: int
+    heads: int
+    kv_heads: int
+    hidden: int
+    eps: float = 1e-6
+    rope_theta: float = 10000.0
+    rope_scaling: Optional[tuple] = None  # RoPEScaling(factor, low, high, originalMaxPositions)
+    bits: int = 4
+    group_size: int = 64
+    tied: bool = False        # Transformer.tieEmbeddingToHead (Transformer.kt:380-386)
+    qkv_bias: bool = False
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.heads
+
+
+def rope_inv_freq(head_dim: int, base: float, scaling: Optional[tuple]) -> np.ndarray:
+    """RoPE.invFreq (RoPE.kt:39-42) and RoPEScaling.scale (RoPE.kt:15-27) in float32."""
+    half = head_dim // 2
+    out = np.empty(half, np.float32)
+    for i in range(half):
+        raw = np.float32(1.0) / np.float32(math.pow(float(np.float32(base)),
+                                                    float(np.float32(2 * i) / np.float32(head_dim))))
+        if scaling is not None:
+            factor, low, high = np.float32(scaling[0]), np.float32(scaling[1]), np.float32(scaling[2])
+            orig = np.float32(int(scaling[3]))
+            wl = np.float32(2.0 * math.pi / float(raw))
+            if wl < orig / high:
+                pass
+            elif wl > orig / low:
+                raw = raw / factor
+            else:
+                smooth = (orig / wl - low) / (high - low)
+                raw = (np.float32(1.0) - smooth) * raw / factor + smooth * raw
+        out[i] = np.float32(raw)
+    return out
+
+
+def _upload(w) -> QuantizedTensor:
+    """A QuantizedTensor, or host arrays in the reference layout (objects with
+    qdata / scales / zeros / rows / columns / bits / group_size)."""
+    if isinstance(w, QuantizedTensor):
+        return w
+    return QuantizedTensor.from_arrays(w.qdata, w.scales, w.zeros, (w.rows, w.columns), w.bits, w.group_size)
+
+
+class DeviceDecoder:
+    """Greedy decoding of one sequence with weights, KV cache and buffers in HBM.
+
+    ``weights``: ``embedding`` ([vocab x dim], None when tied), ``layers`` (a list
+    of dicts with wq wk wv wo wg wu wd, their biases bq bk bv bo bg bu bd and the
+    RMSNorm weights norm1 norm2), ``final_norm``, ``head`` ([dim x vocab]),
+    ``head_bias``."""
+
+    def __init__(self, cfg: DecoderConfig, weights, max_seq: int, device: Optional[int] = None):
+        self.cfg = cfg
+        self.max_seq = max_seq
+        self.ctx = Context.get(device)
+        dev = torch.device("cuda", self.ctx.device)
+        f32 = dict(dtype=torch.float32, device=dev)
+
+        def vec(a):
+            return torch.as_tensor(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
+
+        self.layers = []
+        for L in weights.layers:
+            self.layers.append({k: (_upload(v) if k.startswith("w") else vec(v)) for k, v in L.items()})
+        self.head = _upload(weights.head)
+        self.head_bias = vec(weights.head_bias)
+        self.embedding = None if cfg.tied else _upload(weights.embedding)
+        self.final_norm = vec(weights.final_norm)
+        kv = cfg.kv_heads * cfg.head_dim
+        self.keys = torch.zeros((cfg.layers, cfg.kv_heads, max_seq, cfg.head_dim), **f32)
+        self.values = torch.zeros_like(self.keys)
+        self.inv_freq = vec(rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling))
+        self.x = torch.empty(cfg.dim, **f32)
+        self.normed = torch.empty(cfg.dim, **f32)
+        self.q = torch.empty(cfg.dim, **f32)
+        self.k = torch.empty(kv, **f32)
+        self.v = torch.empty(kv, **f32)
+        self.context = torch.empty(cfg.dim, **f32)
+        self.attn_out = torch.empty(cfg.dim, **f32)
+        self.gate = torch.empty(cfg.hidden, **f32)
+        self.up = torch.empty(cfg.hidden, **f32)
+        self.ffn_out = torch.empty(cfg.dim, **f32)
+        self.logits = torch.empty(cfg.vocab, **f32)
+        self.scores = torch.empty((cfg.heads, max_seq), **f32)
+        self.token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.position = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.next_token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.length = 0
+        self.scale = float(np.float32(1.0) / np.float32(math.sqrt(float(cfg.head_dim))))
+        self._graph = None
+
+    # -- helpers
+    @staticmethod
+    def _p(t) -> ctypes.c_void_p:
+        return ctypes.c_void_p(t.data_ptr())
+
+    def _stream(self) -> ctypes.c_void_p:
+        return ctypes.c_void_p(torch.cuda.current_stream(self.ctx.device).cuda_stream)
+
+    def reset(self) -> None:
+        self.length = 0
+        self.position.zero_()
+
+    def _linear(self, x, w: QuantizedTensor, y, bias) -> None:
+        MatMul.multiply_quantized(x.view(1, -1), w, y.view(1, -1), 1, accumulate=False, bias=bias)
+
+    def _launch_step(self) -> None:
+        """One decode step on the current stream: reads self.token and
+        self.position, writes self.logits and self.next_token, advances
+        the position and feeds the next token back."""
+        L_ = _lib.load()
+        cfg, h = self.cfg, self.ctx.handle
+        s, p = self._stream(), self._p
+        hd, kvh = cfg.head_dim, cfg.kv_heads
+        if cfg.tied:
+            _lib.check(L_.kt_dequantize_column(h, self.head.handle, p(self.token), p(self.x), p(self.status), s))
+        else:
+            _lib.check(L_.kt_dequantize_rows(h, self.embedding.handle, p(self.token), 1, p(self.x), p(self.status), s))
+        for l, L in enumerate(self.layers):
+            _lib.check(L_.kt_rmsnorm(h, p(self.x), p(L["norm1"]), p(self.normed), 1, cfg.dim, cfg.eps, s))
+            self._linear(self.normed, L["wq"], self.q, L["bq"])
+            self._linear(self.normed, L["wk"], self.k, L["bk"])
+            self._linear(self.normed, L["wv"], self.v, L["bv"])
+            _lib.check(L_.kt_rope(h, p(self.q), 1, cfg.dim, hd, p(self.inv_freq), p(self.position), s))
+            _lib.check(L_.kt_rope(h, p(self.k), 1, kvh * hd, hd, p(self.inv_freq), p(self.position), s))
+            _lib.check(L_.kt_kv_store(h, p(self.k), p(self.v), p(self.keys), p(self.values), 1, kvh, hd,
+                                      self.max_seq, l, p(self.position), s))
+            _lib.check(L_.kt_attention_decode(h, p(self.q), p(self.keys), p(self.values), p(self.context),
+                                              p(self.scores), cfg.heads, kvh, hd, self.max_seq, l, self.scale,
+                                              p(self.position), s))
+            self._linear(self.context, L["wo"], self.attn_out, L["bo"])
+            _lib.check(L_.kt_add(h, p(self.x), p(self.attn_out), cfg.dim, s))
+            _lib.check(L_.kt_rmsnorm(h, p(self.x), p(L["norm2"]), p(self.normed), 1, cfg.dim, cfg.eps, s))
+            self._linear(self.normed, L["wg"], self.gate, L["bg"])
+            self._linear(self.normed, L["wu"], self.up, L["bu"])
+            _lib.check(L_.kt_silu_mul(h, p(self.gate), p(self.up), cfg.hidden, s))
+            self._linear(self.gate, L["wd"], self.ffn_out, L["bd"])
+            _lib.check(L_.kt_add(h, p(self.x), p(self.ffn_out), cfg.dim, s))
+        _lib.check(L_.kt_rmsnorm(h, p(self.x), p(self.final_norm), p(self.normed), 1, cfg.dim, cfg.eps, s))
+        self._linear(self.normed, self.head, self.logits, self.head_bias)
+        _lib.check(L_.kt_argmax(h, p(self.logits), 1, cfg.vocab, p(self.next_token), s))
+        _lib.check(L_.kt_increment(h, p(self.position), 1, s))
+        self.token.copy_(self.next_token)
+
+    def step(self, token: int):
+        """Transformer.decode(token): the logits of this step (device tensor)."""
+        if not 0 <= token < self.cfg.vocab:
+            raise ValueError(f"{token} out of vocab bounds {self.cfg.vocab}")
+        if self.length >= self.max_seq:
+            raise ValueError(f"KV cache full: maxSequenceLength {self.max_seq}")
+        self.token.fill_(token)
+        self._launch_step()
+        self.length += 1
+        return self.logits
+
+    def capture(self) -> None:
+        """Records one step (from the current self.token / self.position) into a CUDA graph."""
+        torch.cuda.synchronize()
+        self._graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._graph):
+            self._launch_step()
+
+    def generate(self, prompt: list[int], max_tokens: int) -> list[int]:
+        """Greedy continuation: the prompt fed step by step (eager), then
+        ``max_tokens`` replays of the captured step."""
+        if len(prompt) + max_tokens > self.max_seq:
+            raise ValueError("prompt + max_tokens exceed max_seq")
+        for t in prompt:
+            self.step(t)
+        out = [int(self.next_token.item())]
+        if self._graph is None:
+            self.capture()  # captures the position reached after the prompt
+        for _ in range(max_tokens - 1):
+            self._graph.replay()
+            self.length += 1
+            out.append(int(self.next_token.item()))
+        return out
