@@ -201,6 +201,68 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------- decode
+
+QWEN2_05B = dict(vocab=151936, dim=896, layers=24, heads=14, kv_heads=2, hidden=4864, eps=1e-6,
+                 rope_theta=1000000.0, bits=4, group_size=64, tied=True, qkv_bias=True)
+
+
+def measure_decode(kt, torch, steps: int, prompt_len: int, seed: int) -> dict:
+    """Greedy decode tokens/s of the Qwen2-0.5B-shaped INT4 model (random N(0, 0.02^2)
+    weights quantized on the device, tied embeddings, q/k/v biases), batch 1."""
+    import numpy as np
+    from types import SimpleNamespace
+    from kotensor_b200 import decoder as D
+    cfg = D.DecoderConfig(**QWEN2_05B)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    q = kt.Quantization(cfg.bits, cfg.group_size)
+
+    def proj(k, n):
+        w = torch.randn((k, n), generator=gen, device="cuda") * 0.02
+        return kt.QuantizedTensor.quantize(w, q)
+
+    rng = np.random.default_rng(seed)
+    kv = cfg.kv_heads * cfg.head_dim
+    layers = []
+    for _ in range(cfg.layers):
+        layers.append({
+            "norm1": np.ones(cfg.dim, np.float32), "norm2": np.ones(cfg.dim, np.float32),
+            "wq": proj(cfg.dim, cfg.dim), "wk": proj(cfg.dim, kv), "wv": proj(cfg.dim, kv), "wo": proj(cfg.dim, cfg.dim),
+            "bq": rng.standard_normal(cfg.dim).astype(np.float32) * 0.02,
+            "bk": rng.standard_normal(kv).astype(np.float32) * 0.02,
+            "bv": rng.standard_normal(kv).astype(np.float32) * 0.02,
+            "bo": np.zeros(cfg.dim, np.float32),
+            "wg": proj(cfg.dim, cfg.hidden), "wu": proj(cfg.dim, cfg.hidden), "wd": proj(cfg.hidden, cfg.dim),
+            "bg": np.zeros(cfg.hidden, np.float32), "bu": np.zeros(cfg.hidden, np.float32),
+            "bd": np.zeros(cfg.dim, np.float32)})
+    head = proj(cfg.dim, cfg.vocab)
+    weights = SimpleNamespace(embedding=None, layers=layers, final_norm=np.ones(cfg.dim, np.float32), head=head,
+                              head_bias=np.zeros(cfg.vocab, np.float32))
+    dec = D.DeviceDecoder(cfg, weights, max_seq=prompt_len + steps + 8)
+    prompt = rng.integers(0, cfg.vocab, size=prompt_len).tolist()
+    for t in prompt:  # the prompt, one eager step per token
+        dec.step(t)
+    dec.capture()
+    for _ in range(3):  # warm-up replays
+        dec._graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        dec._graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    weight_bytes = sum(w.size_in_bytes for L in dec.layers for k, w in L.items() if k.startswith("w"))
+    weight_bytes += dec.head.size_in_bytes
+    return {"model": "qwen2-0.5b-shaped int4 g64 (random weights, tied, qkv bias)", "batch": 1,
+            "prompt": prompt_len, "steps": steps, "ms_per_token": round(ms, 4),
+            "tokens_per_s": round(1e3 / ms, 1), "weight_bytes_per_token": int(weight_bytes),
+            "weight_gbs": round(weight_bytes / (ms / 1e3) / 1e9, 1),
+            "context_end": prompt_len + steps + 3}
+
+
 # ----------------------------------------------------------------- GPU arm
 
 def run_ours(args) -> None:
@@ -356,6 +418,13 @@ def run_ours(args) -> None:
                 "dtype": "bf16 x bf16 -> f32 (INT4 weights dequantized)", "launches_per_step": len(SHAPES)}
         del gg
 
+    # decode tokens/s (Qwen2-0.5B-shaped INT4, batch 1): the
+    # device decode step captured once, prompt fed step by step, then timed
+    # greedy steps replaying the graph (no host work between tokens).
+    decode = None
+    if args.decode_steps > 0:
+        decode = measure_decode(kt, torch, args.decode_steps, args.decode_prompt, seed=99 + rank)
+
     peak, peak_kind = measured_peaks()
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -380,6 +449,8 @@ def run_ours(args) -> None:
     }
     if gemm is not None:
         line["prefill_gemm"] = gemm
+    if decode is not None:
+        line["decode"] = decode
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -396,6 +467,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--m", type=int, default=1, help="activation rows per GEMV (decode batch)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-steps", type=int, default=128, help="timed greedy decode steps (0: skip)")
+    ap.add_argument("--decode-prompt", type=int, default=512, help="prompt tokens before the timed decode")
     ap.add_argument("--gemm-m", type=int, default=512,
                     help="also time the prefill GEMM at this M on the same weights (0: skip)")
     args = ap.parse_args()

@@ -128,6 +128,13 @@ kt_status kt_shard_bounds(int32_t axis, int32_t extent, int32_t group_size, int3
 kt_status kt_qweight_shard(kt_ctx* ctx, const kt_qweight* w, int32_t axis, int32_t parts, int32_t index,
                            void* stream, kt_qweight** out);
 
+/* The inverse of column shards: one weight whose columns are those of ws[0..count-1]
+ * side by side (1 <= count <= 4; same bits, group size and rows), e.g. q|k|v or
+ * gate|up projections fused into one matmul.  Bytes, scales and zeros equal the
+ * quantization of the concatenated fp32 columns. */
+kt_status kt_qweight_concat_columns(kt_ctx* ctx, const kt_qweight* const* ws, int32_t count, void* stream,
+                                    kt_qweight** out);
+
 /* One NCCL communicator per rank (one process per GPU).  NCCL is loaded at run
  * time (libnccl.so.2, or the file named by KT_NCCL_LIBRARY); without it these
  * return KT_ERR_NCCL.  Rank 0 makes the 128-byte id, every rank passes it to
@@ -243,13 +250,25 @@ kt_status kt_kv_store(kt_ctx* ctx, const float* k_dev, const float* v_dev, float
                       const int32_t* position_dev, void* stream);
 /* attendHead for every query head of one token at *position_dev (Attention.kt:295-328):
  * scores (dot * scale) over positions 0..pos, softmax from the reference's -1e9
- * initial maximum, context = weighted sum of values.  scores_dev: [heads x max_seq] scratch. */
+ * initial maximum, context = weighted sum of values (split over blocks of 64
+ * positions and merged with a log-sum-exp in block order).  scores_dev: scratch of
+ * kt_attention_scratch_floats(heads, head_dim, max_seq) floats; head_dim <= 254. */
+size_t kt_attention_scratch_floats(int32_t heads, int32_t head_dim, int32_t max_seq);
 kt_status kt_attention_decode(kt_ctx* ctx, const float* q_dev, const float* k_cache, const float* v_cache,
                               float* context_dev, float* scores_dev, int32_t heads, int32_t kv_heads,
                               int32_t head_dim, int32_t max_seq, int32_t layer, float scale,
                               const int32_t* position_dev, void* stream);
 /* gate = silu(gate) * up (SwiGLU.forwardInto, Tensor.kt:231-237). */
 kt_status kt_silu_mul(kt_ctx* ctx, float* gate_dev, const float* up_dev, int64_t n, void* stream);
+/* x += y, then out = RMSNorm(x) with `weight` (the residual add of
+ * TransformerBlock.decodeInto fused with the norm that follows it). */
+kt_status kt_add_rmsnorm(kt_ctx* ctx, float* x_dev, const float* y_dev, const float* weight_dev, float* out_dev,
+                         int32_t rows, int32_t dim, float eps, void* stream);
+/* RoPE on the q and k parts of one fused q|k|v row (widths q_width and
+ * kv_heads*head_dim), then k and v into the cache at *position_dev. */
+kt_status kt_rope_kv(kt_ctx* ctx, float* qkv_dev, int32_t q_width, int32_t kv_heads, int32_t head_dim,
+                     const float* inv_freq_dev, float* k_cache, float* v_cache, int32_t max_seq, int32_t layer,
+                     const int32_t* position_dev, void* stream);
 /* x += y (Tensor.addInPlace). */
 kt_status kt_add(kt_ctx* ctx, float* x_dev, const float* y_dev, int64_t n, void* stream);
 /* argmaxOfLastToken per row (Transformer.kt:255-266): the largest logit above

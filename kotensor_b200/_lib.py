@@ -73,12 +73,16 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_qmatmul_t": ([P, P, P, P, I32, I32, P], I32),
     "kt_shard_bounds": ([I32, I32, I32, I32, I32, ctypes.POINTER(I32), ctypes.POINTER(I32)], I32),
     "kt_qweight_shard": ([P, P, I32, I32, I32, P, PP], I32),
+    "kt_qweight_concat_columns": ([P, PP, I32, P, PP], I32),
     "kt_comm_unique_id": ([P], I32),
     "kt_comm_init": ([P, I32, I32, P, PP], I32),
     "kt_comm_destroy": ([P], I32),
     "kt_qmatmul_row_parallel": ([P, P, P, P, P, I32, I32, F32, P, P], I32),
     "kt_allgather_columns": ([P, P, P, I32, I32, P], I32),
     "kt_rmsnorm": ([P, P, P, P, I32, I32, F32, P], I32),
+    "kt_add_rmsnorm": ([P, P, P, P, P, I32, I32, F32, P], I32),
+    "kt_rope_kv": ([P, P, I32, I32, I32, P, P, P, I32, I32, P, P], I32),
+    "kt_attention_scratch_floats": ([I32, I32, I32], SZ),
     "kt_rope": ([P, P, I32, I32, I32, P, P, P], I32),
     "kt_kv_store": ([P, P, P, P, P, I32, I32, I32, I32, I32, P, P], I32),
     "kt_attention_decode": ([P, P, P, P, P, P, I32, I32, I32, I32, I32, F32, P, P], I32),

@@ -469,6 +469,46 @@ kt_status kt_qweight_free(kt_qweight* w) {
     return KT_OK;
 }
 
+kt_status kt_qweight_concat_columns(kt_ctx* ctx, const kt_qweight* const* ws, int32_t count, void* stream,
+                                    kt_qweight** out) {
+    if (!ctx || !ws || !out || count < 1 || count > 4) return fail(KT_ERR_INVALID_ARGUMENT, "1 to 4 weights");
+    *out = nullptr;
+    int64_t n = 0;
+    for (int i = 0; i < count; ++i) {
+        if (!ws[i]) return fail(KT_ERR_INVALID_ARGUMENT, "NULL weight");
+        if (ws[i]->bits != ws[0]->bits || ws[i]->group_size != ws[0]->group_size || ws[i]->rows != ws[0]->rows)
+            return fail(KT_ERR_INVALID_ARGUMENT, "weights differ in bits, group size or rows");
+        n += ws[i]->columns;
+    }
+    if (n > INT32_MAX) return fail(KT_ERR_INVALID_ARGUMENT, "too many columns");
+    kt_qweight* d = nullptr;
+    kt_status st = alloc_weight(ctx, ws[0]->bits, ws[0]->group_size, ws[0]->rows, static_cast<int32_t>(n), &d);
+    if (st != KT_OK) return st;
+    cudaStream_t s = pick(ctx, stream);
+    cudaError_t err = cudaSuccess;
+    if (d->bits == 4) err = launch_concat_int4_columns(ws, count, d, s);
+    size_t c0 = 0;
+    for (int i = 0; i < count && err == cudaSuccess; ++i) {
+        const kt_qweight* w = ws[i];
+        const size_t nc = static_cast<size_t>(w->columns);
+        if (d->bits == 8)
+            err = cudaMemcpy2DAsync(d->qdata + c0, d->bytes_per_row, w->qdata, w->bytes_per_row, nc, w->rows,
+                                    cudaMemcpyDeviceToDevice, s);
+        if (err == cudaSuccess)
+            err = cudaMemcpy2DAsync(d->scales + c0, d->columns * sizeof(float), w->scales, nc * sizeof(float),
+                                    nc * sizeof(float), w->groups, cudaMemcpyDeviceToDevice, s);
+        if (err == cudaSuccess && d->bits == 4)
+            err = cudaMemcpy2DAsync(d->zeros + c0, d->columns, w->zeros, nc, nc, w->groups, cudaMemcpyDeviceToDevice, s);
+        c0 += nc;
+    }
+    if (err != cudaSuccess) {
+        free_weight(d);
+        return cuda_fail(err, "kt_qweight_concat_columns");
+    }
+    *out = d;
+    return KT_OK;
+}
+
 kt_status kt_shard_bounds(int32_t axis, int32_t extent, int32_t group_size, int32_t parts, int32_t index,
                           int32_t* begin, int32_t* end) {
     if (!begin || !end) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
@@ -631,6 +671,31 @@ kt_status kt_rmsnorm(kt_ctx* ctx, const float* x, const float* weight, float* ou
     return KT_OK;
 }
 
+kt_status kt_add_rmsnorm(kt_ctx* ctx, float* x, const float* y, const float* weight, float* out, int32_t rows,
+                         int32_t dim, float eps, void* stream) {
+    if (!ctx || !x || !y || !weight || !out || rows <= 0 || dim <= 0)
+        return fail(KT_ERR_INVALID_ARGUMENT, "bad add_rmsnorm arguments");
+    KT_CUDA_TRY(launch_add_rmsnorm(x, y, weight, out, rows, dim, eps, pick(ctx, stream)), "add_rmsnorm launch");
+    return KT_OK;
+}
+
+kt_status kt_rope_kv(kt_ctx* ctx, float* qkv, int32_t q_width, int32_t kv_heads, int32_t head_dim,
+                     const float* inv_freq, float* k_cache, float* v_cache, int32_t max_seq, int32_t layer,
+                     const int32_t* position_dev, void* stream) {
+    if (!ctx || !qkv || !inv_freq || !k_cache || !v_cache || !position_dev || head_dim <= 0 || head_dim % 2 != 0 ||
+        q_width % head_dim != 0 || kv_heads <= 0 || max_seq <= 0 || layer < 0)
+        return fail(KT_ERR_INVALID_ARGUMENT, "bad rope_kv arguments");
+    KT_CUDA_TRY(launch_rope_kv(qkv, q_width, kv_heads, head_dim, inv_freq, k_cache, v_cache, max_seq, layer,
+                               position_dev, pick(ctx, stream)),
+                "rope_kv launch");
+    return KT_OK;
+}
+
+size_t kt_attention_scratch_floats(int32_t heads, int32_t head_dim, int32_t max_seq) {
+    if (heads <= 0 || head_dim <= 0 || max_seq <= 0) return 0;
+    return attention_scratch_floats(heads, head_dim, max_seq);
+}
+
 kt_status kt_rope(kt_ctx* ctx, float* v, int32_t rows, int32_t width, int32_t head_dim, const float* inv_freq,
                   const int32_t* position_dev, void* stream) {
     if (!ctx || !v || !inv_freq || !position_dev || rows <= 0 || head_dim <= 0 || head_dim % 2 != 0 ||
@@ -680,7 +745,11 @@ kt_status kt_add(kt_ctx* ctx, float* x, const float* y, int64_t n, void* stream)
 
 kt_status kt_argmax(kt_ctx* ctx, const float* logits, int32_t rows, int32_t n, int32_t* out_dev, void* stream) {
     if (!ctx || !logits || !out_dev || rows <= 0 || n <= 0) return fail(KT_ERR_INVALID_ARGUMENT, "bad argmax arguments");
-    KT_CUDA_TRY(launch_argmax(logits, rows, n, out_dev, pick(ctx, stream)), "argmax launch");
+    const cudaStream_t s = pick(ctx, stream);
+    void* ws = nullptr;
+    KT_CUDA_TRY(stream_workspace(ctx, s, kWorkspaceReservedBytes + argmax_scratch_bytes(rows), &ws), "argmax workspace");
+    KT_CUDA_TRY(launch_argmax(logits, rows, n, out_dev, static_cast<unsigned char*>(ws) + kWorkspaceReservedBytes, s),
+                "argmax launch");
     return KT_OK;
 }
 

@@ -56,6 +56,60 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* __restri
     for (int d = threadIdx.x; d < dim; d += blockDim.x) orow[d] = xr[d] * r * w[d];
 }
 
+// x += y, then out = RMSNorm(x) (the residual add of TransformerBlock.decodeInto
+// followed by the next norm), one block per row.
+__global__ void __launch_bounds__(kThreads) add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ y,
+                                                              const float* __restrict__ w, float* __restrict__ out,
+                                                              int dim, float eps) {
+    __shared__ float red[32];
+    float* xr = x + static_cast<int64_t>(blockIdx.x) * dim;
+    const float* yr = y + static_cast<int64_t>(blockIdx.x) * dim;
+    float* orow = out + static_cast<int64_t>(blockIdx.x) * dim;
+    float ss = 0.0f;
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+        const float v = xr[d] + yr[d];
+        xr[d] = v;
+        ss = fmaf(v, v, ss);
+    }
+    ss = block_sum(ss, red);  // its barriers also order the x writes before the reads below
+    const float r = 1.0f / sqrtf(ss / static_cast<float>(dim) + eps);
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) orow[d] = xr[d] * r * w[d];
+}
+
+// RoPE on the q and k parts of one fused q|k|v row, then the k and v parts
+// into the cache at *pos (Attention.decodeInto, Attention.kt:222-232).
+__global__ void rope_kv_kernel(float* __restrict__ qkv, int q_width, int kv_heads, int head_dim,
+                               const float* __restrict__ inv_freq, float* __restrict__ kc, float* __restrict__ vc,
+                               int max_seq, int layer, const int32_t* __restrict__ pos) {
+    const int half = head_dim / 2;
+    const int kv_width = kv_heads * head_dim;
+    const int rope_pairs = (q_width + kv_width) / 2;  // pairs over the q heads then the k heads
+    const int p = *pos;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < rope_pairs + kv_width; idx += gridDim.x * blockDim.x) {
+        if (idx < rope_pairs) {
+            const int head = idx / half, i = idx % half;
+            float* v = qkv + head * head_dim;  // q heads, then k heads (contiguous)
+            const float theta = static_cast<float>(p) * inv_freq[i];
+            float sn, cs;
+            sincosf(theta, &sn, &cs);
+            const float x1 = v[i], x2 = v[i + half];
+            v[i] = x1 * cs - x2 * sn;
+            v[i + half] = x1 * sn + x2 * cs;
+            if (head * head_dim >= q_width) {  // a key: store both rotated halves
+                const int kh = (head * head_dim - q_width) / head_dim;
+                const int64_t off = ((static_cast<int64_t>(layer) * kv_heads + kh) * max_seq + p) * head_dim;
+                kc[off + i] = v[i];
+                kc[off + i + half] = v[i + half];
+            }
+        } else {
+            const int e = idx - rope_pairs;  // a value element
+            const int vh = e / head_dim, d = e % head_dim;
+            const int64_t off = ((static_cast<int64_t>(layer) * kv_heads + vh) * max_seq + p) * head_dim + d;
+            vc[off] = qkv[q_width + kv_width + e];
+        }
+    }
+}
+
 // RoPE.applyInPlace at position *pos (+ row): pairs (i, i + half) of every head.
 __global__ void rope_kernel(float* __restrict__ v, int rows, int width, int head_dim, const float* __restrict__ inv_freq,
                             const int32_t* __restrict__ pos) {
@@ -95,51 +149,102 @@ __global__ void kv_store_kernel(const float* __restrict__ k, const float* __rest
     }
 }
 
-// attendHead (Attention.kt:295-328) for one query row at position *pos: one
-// block per query head; scores over 0..pos kept in global scratch
-// [heads][max_seq]; softmax with the reference's max; context = sum w_j v_j.
-__global__ void __launch_bounds__(kThreads) attention_decode_kernel(
-    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc, float* __restrict__ ctx,
-    float* __restrict__ scores, int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale,
+// attendHead (Attention.kt:295-328) for one query row at position *pos, split
+// over the positions (the reference's single softmax restated as a
+// log-sum-exp merge): block (head, s) takes positions [s*kSpan, s*kSpan +
+// kSpan) up to pos and leaves in scratch[head][s][0 .. head_dim + 2) its local maximum
+// m, sum l of exp(score - m) and the unnormalised context acc[d]; the merge
+// kernel combines the splits in order: M = max m_s (at least -1e9, the
+// reference's initial maximum), ctx = sum acc_s e^(m_s - M) / sum l_s e^(m_s - M).
+constexpr int kMaxHeadDim = 254;
+constexpr int kSpan = 64;  // positions per block
+
+__global__ void __launch_bounds__(kThreads) attention_partial_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    float* __restrict__ scratch, int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale,
     const int32_t* __restrict__ pos) {
     __shared__ float red[32];
-    extern __shared__ float qs[];  // head_dim
-    const int h = blockIdx.x;
+    __shared__ float qs[kMaxHeadDim + 2];
+    __shared__ float sc[kSpan];
+    __shared__ float part[kThreads / 32][kMaxHeadDim + 2];
+    const int h = blockIdx.x, split = blockIdx.y;
+    const int j0 = split * kSpan;
+    const int j1 = min(j0 + kSpan, *pos + 1);
+    if (j0 >= j1) return;  // past the current position: the merge skips this split
     const int group = heads / kv_heads;
-    const int position = *pos;
     const float* qh = q + static_cast<int64_t>(h) * head_dim;
     for (int d = threadIdx.x; d < head_dim; d += blockDim.x) qs[d] = qh[d];
     __syncthreads();
     const int64_t base = ((static_cast<int64_t>(layer) * kv_heads + h / group) * max_seq) * head_dim;
-    float* sc = scores + static_cast<int64_t>(h) * max_seq;
-    // scores: one warp per position
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int j = warp; j <= position; j += nw) {
+    float mx = -FLT_MAX;
+    for (int j = j0 + warp; j < j1; j += nw) {
         const float* kr = kc + base + static_cast<int64_t>(j) * head_dim;
-        float s = 0.0f;
-        for (int d = lane; d < head_dim; d += 32) s = fmaf(qs[d], kr[d], s);
+        float sdot = 0.0f;
+        for (int d = lane; d < head_dim; d += 32) sdot = fmaf(qs[d], kr[d], sdot);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) sc[j] = s * scale;
+        for (int o = 16; o > 0; o >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o);
+        sdot *= scale;
+        if (lane == 0) sc[j - j0] = sdot;
+        mx = fmaxf(mx, sdot);
     }
-    __syncthreads();
-    float mx = -1e9f;  // the reference's initial maximum
-    for (int j = threadIdx.x; j <= position; j += blockDim.x) mx = fmaxf(mx, sc[j]);
-    mx = block_max(mx, red);
+    mx = block_max(mx, red);  // its barriers also publish sc[]
     float sum = 0.0f;
-    for (int j = threadIdx.x; j <= position; j += blockDim.x) {
-        const float e = expf(sc[j] - mx);
-        sc[j] = e;
+    for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+        const float e = expf(sc[j - j0] - mx);
+        sc[j - j0] = e;
         sum += e;
     }
     sum = block_sum(sum, red);
-    const float inv = 1.0f / sum;
     __syncthreads();
-    // context: thread per head dimension, positions in order
+    constexpr int kPer = (kMaxHeadDim + 2 + 31) / 32;
+    float acc[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) acc[i] = 0.0f;
+    for (int j = j0 + warp; j < j1; j += nw) {
+        const float wj = sc[j - j0];
+        const float* vr = vc + base + static_cast<int64_t>(j) * head_dim;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int d = lane + 32 * i;
+            if (d < head_dim) acc[i] = fmaf(wj, vr[d], acc[i]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int d = lane + 32 * i;
+        if (d < head_dim) part[warp][d] = acc[i];
+    }
+    __syncthreads();
+    // this split's partial: scratch[(h * splits + split) * (head_dim + 2) ..]
+    const int64_t splits = (max_seq + kSpan - 1) / kSpan;
+    float* out = scratch + (static_cast<int64_t>(h) * splits + split) * (head_dim + 2);
     for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
-        float acc = 0.0f;
-        for (int j = 0; j <= position; ++j) acc = fmaf(sc[j] * inv, vc[base + static_cast<int64_t>(j) * head_dim + d], acc);
-        ctx[static_cast<int64_t>(h) * head_dim + d] = acc;
+        float v = 0.0f;
+        for (int w = 0; w < nw; ++w) v += part[w][d];
+        out[2 + d] = v;
+    }
+    if (threadIdx.x == 0) {
+        out[0] = mx;
+        out[1] = sum;
+    }
+}
+
+__global__ void attention_merge_kernel(const float* __restrict__ scratch, float* __restrict__ ctx, int head_dim,
+                                       int max_seq, const int32_t* __restrict__ pos) {
+    const int h = blockIdx.x;
+    const int splits = *pos / kSpan + 1;
+    const int stride = head_dim + 2;
+    const float* base = scratch + static_cast<int64_t>(h) * ((max_seq + kSpan - 1) / kSpan) * stride;
+    float m = -1e9f;
+    for (int s = 0; s < splits; ++s) m = fmaxf(m, base[s * stride]);
+    float l = 0.0f;
+    for (int s = 0; s < splits; ++s) l += base[s * stride + 1] * expf(base[s * stride] - m);
+    const float inv = 1.0f / l;
+    for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+        float v = 0.0f;
+        for (int s = 0; s < splits; ++s) v += base[s * stride + 2 + d] * expf(base[s * stride] - m);
+        ctx[static_cast<int64_t>(h) * head_dim + d] = v * inv;
     }
 }
 
@@ -160,14 +265,25 @@ __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, i
 
 // Greedy pick of one row (argmaxOfLastToken, Transformer.kt:255-266): the
 // largest logit above -1e9, the lowest index among equal ones, 0 if none.
-__global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restrict__ logits, int n,
-                                                          int32_t* __restrict__ out) {
+// Stage 1: block (c, row) scans chunk c; stage 2: one block per row merges the
+// chunks in order.
+__device__ __forceinline__ void better(float& bv, int& bi, float ov, int oi) {
+    if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) argmax_partial_kernel(const float* __restrict__ logits, int n, int chunk,
+                                                                  float* __restrict__ pv, int* __restrict__ pi) {
     __shared__ float bv[kThreads];
     __shared__ int bi[kThreads];
+    const int row = blockIdx.y, c = blockIdx.x;
+    const int v0 = c * chunk, v1 = min(v0 + chunk, n);
     float best = -1e9f;
     int idx = 0x7fffffff;
-    for (int v = threadIdx.x; v < n; v += blockDim.x) {
-        const float x = logits[static_cast<int64_t>(blockIdx.x) * n + v];
+    for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+        const float x = logits[static_cast<int64_t>(row) * n + v];
         if (x > best) {  // strictly greater: the first (lowest) index of a tie stays
             best = x;
             idx = v;
@@ -176,18 +292,24 @@ __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restric
     bv[threadIdx.x] = best;
     bi[threadIdx.x] = idx;
     __syncthreads();
-    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-        if (threadIdx.x < s) {
-            const float ov = bv[threadIdx.x + s];
-            const int oi = bi[threadIdx.x + s];
-            if (ov > bv[threadIdx.x] || (ov == bv[threadIdx.x] && oi < bi[threadIdx.x])) {
-                bv[threadIdx.x] = ov;
-                bi[threadIdx.x] = oi;
-            }
-        }
+    for (int st = blockDim.x / 2; st > 0; st >>= 1) {
+        if (threadIdx.x < st) better(bv[threadIdx.x], bi[threadIdx.x], bv[threadIdx.x + st], bi[threadIdx.x + st]);
         __syncthreads();
     }
-    if (threadIdx.x == 0) out[blockIdx.x] = bi[0] == 0x7fffffff ? 0 : bi[0];
+    if (threadIdx.x == 0) {
+        pv[row * gridDim.x + c] = bv[0];
+        pi[row * gridDim.x + c] = bi[0];
+    }
+}
+
+__global__ void argmax_merge_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int chunks,
+                                    int32_t* __restrict__ out) {
+    if (threadIdx.x != 0) return;
+    const int row = blockIdx.x;
+    float best = -1e9f;
+    int idx = 0x7fffffff;
+    for (int c = 0; c < chunks; ++c) better(best, idx, pv[row * chunks + c], pi[row * chunks + c]);
+    out[row] = idx == 0x7fffffff ? 0 : idx;
 }
 
 // dequantizeColumn(token) of a weight [K x N] (the tied embedding lookup):
@@ -224,6 +346,21 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int rows,
     rmsnorm_kernel<<<rows, kThreads, 0, s>>>(x, w, out, dim, eps);
     return cudaGetLastError();
 }
+cudaError_t launch_add_rmsnorm(float* x, const float* y, const float* w, float* out, int rows, int dim, float eps,
+                               cudaStream_t s) {
+    add_rmsnorm_kernel<<<rows, kThreads, 0, s>>>(x, y, w, out, dim, eps);
+    return cudaGetLastError();
+}
+cudaError_t launch_rope_kv(float* qkv, int q_width, int kv_heads, int head_dim, const float* inv_freq, float* kc,
+                           float* vc, int max_seq, int layer, const int32_t* pos, cudaStream_t s) {
+    const int total = (q_width + kv_heads * head_dim) / 2 + kv_heads * head_dim;
+    rope_kv_kernel<<<(total + kThreads - 1) / kThreads, kThreads, 0, s>>>(qkv, q_width, kv_heads, head_dim, inv_freq,
+                                                                          kc, vc, max_seq, layer, pos);
+    return cudaGetLastError();
+}
+size_t attention_scratch_floats(int heads, int head_dim, int max_seq) {
+    return static_cast<size_t>(heads) * ((max_seq + kSpan - 1) / kSpan) * (head_dim + 2);
+}
 cudaError_t launch_rope(float* v, int rows, int width, int head_dim, const float* inv_freq, const int32_t* pos,
                         cudaStream_t s) {
     rope_kernel<<<grid_for(static_cast<int64_t>(rows) * width / 2), kThreads, 0, s>>>(v, rows, width, head_dim,
@@ -239,8 +376,13 @@ cudaError_t launch_kv_store(const float* k, const float* v, float* kc, float* vc
 cudaError_t launch_attention_decode(const float* q, const float* kc, const float* vc, float* ctx, float* scores,
                                     int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale,
                                     const int32_t* pos, cudaStream_t s) {
-    attention_decode_kernel<<<heads, kThreads, head_dim * sizeof(float), s>>>(q, kc, vc, ctx, scores, heads, kv_heads,
-                                                                              head_dim, max_seq, layer, scale, pos);
+    if (head_dim > kMaxHeadDim) return cudaErrorInvalidValue;
+    const dim3 grid(heads, (max_seq + kSpan - 1) / kSpan);
+    attention_partial_kernel<<<grid, kThreads, 0, s>>>(q, kc, vc, scores, heads, kv_heads, head_dim, max_seq, layer,
+                                                       scale, pos);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    attention_merge_kernel<<<heads, 128, 0, s>>>(scores, ctx, head_dim, max_seq, pos);
     return cudaGetLastError();
 }
 cudaError_t launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s) {
@@ -251,8 +393,17 @@ cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s) {
     add_kernel<<<grid_for(n), kThreads, 0, s>>>(x, y, n);
     return cudaGetLastError();
 }
-cudaError_t launch_argmax(const float* logits, int rows, int n, int32_t* out, cudaStream_t s) {
-    argmax_kernel<<<rows, kThreads, 0, s>>>(logits, n, out);
+size_t argmax_scratch_bytes(int rows) { return static_cast<size_t>(rows) * 128 * 8; }
+
+cudaError_t launch_argmax(const float* logits, int rows, int n, int32_t* out, void* scratch, cudaStream_t s) {
+    const int chunks = std::min(128, std::max(1, (n + 2047) / 2048));
+    const int chunk = (n + chunks - 1) / chunks;
+    float* pv = static_cast<float*>(scratch);
+    int* pi = reinterpret_cast<int*>(pv + static_cast<size_t>(rows) * 128);
+    argmax_partial_kernel<<<dim3(chunks, rows), kThreads, 0, s>>>(logits, n, chunk, pv, pi);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    argmax_merge_kernel<<<rows, 32, 0, s>>>(pv, pi, chunks, out);
     return cudaGetLastError();
 }
 cudaError_t launch_dequantize_column(const QView& w, const int32_t* col, float* out, int32_t* status, cudaStream_t s) {

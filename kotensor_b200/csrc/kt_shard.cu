@@ -33,7 +33,56 @@ __global__ void repack_int4_columns_kernel(const uint8_t* __restrict__ src, int3
     }
 }
 
+// One thread per output byte of one row of an INT4 weight made of up to
+// kMaxConcat column blocks (sources in order).
+constexpr int kMaxConcat = 4;
+struct ConcatSources {
+    const uint8_t* q[kMaxConcat];
+    int32_t half[kMaxConcat];    // bytes per row of each source
+    int32_t begin[kMaxConcat + 1];  // first destination column of each source; begin[count] = N
+    int32_t count;
+};
+
+__global__ void concat_int4_columns_kernel(ConcatSources src, int32_t n_dst, int32_t dst_half, int32_t rows,
+                                           uint8_t* __restrict__ dst) {
+    const int64_t total = static_cast<int64_t>(rows) * dst_half;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / dst_half;
+        const int32_t b = static_cast<int32_t>(i - r * dst_half);
+        auto nibble = [&](int32_t j) -> uint32_t {  // destination column j
+            int p = 0;
+            while (p + 1 < src.count && j >= src.begin[p + 1]) ++p;
+            const int32_t c = j - src.begin[p], h = src.half[p];
+            const uint32_t byte = src.q[p][r * h + (c < h ? c : c - h)];
+            return c < h ? (byte & 15u) : (byte >> 4);
+        };
+        const uint32_t lo = nibble(b);
+        const uint32_t hi = dst_half + b < n_dst ? nibble(dst_half + b) : 0u;
+        dst[r * dst_half + b] = static_cast<uint8_t>(lo | (hi << 4));
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_concat_int4_columns(const kt_qweight* const* srcs, int32_t count, const kt_qweight* dst,
+                                       cudaStream_t s) {
+    if (count < 1 || count > kMaxConcat) return cudaErrorInvalidValue;
+    ConcatSources cs{};
+    cs.count = count;
+    int32_t c = 0;
+    for (int i = 0; i < count; ++i) {
+        cs.q[i] = srcs[i]->qdata;
+        cs.half[i] = srcs[i]->bytes_per_row;
+        cs.begin[i] = c;
+        c += srcs[i]->columns;
+    }
+    cs.begin[count] = c;
+    const int64_t total = static_cast<int64_t>(dst->rows) * dst->bytes_per_row;
+    const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 32));
+    concat_int4_columns_kernel<<<blocks, 256, 0, s>>>(cs, dst->columns, dst->bytes_per_row, dst->rows, dst->qdata);
+    return cudaGetLastError();
+}
 
 bool shard_bounds(int32_t axis, int32_t extent, int32_t group_size, int32_t parts, int32_t index, int32_t* begin,
                   int32_t* end) {

@@ -99,9 +99,19 @@ class DeviceDecoder:
         def vec(a):
             return torch.as_tensor(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
 
+        from .parallel import concat_columns
         self.layers = []
         for L in weights.layers:
-            self.layers.append({k: (_upload(v) if k.startswith("w") else vec(v)) for k, v in L.items()})
+            d = {k: (_upload(v) if k.startswith("w") else vec(v)) for k, v in L.items()}
+            # q|k|v and gate|up as one matmul each: per-column quantization makes
+            # the fused weight's columns exactly the separate weights' columns
+            d["wqkv"] = concat_columns([d["wq"], d["wk"], d["wv"]])
+            d["bqkv"] = torch.cat([d["bq"], d["bk"], d["bv"]])
+            d["wgu"] = concat_columns([d["wg"], d["wu"]])
+            d["bgu"] = torch.cat([d["bg"], d["bu"]])
+            for k in ("wq", "wk", "wv", "wg", "wu", "bq", "bk", "bv", "bg", "bu"):
+                del d[k]
+            self.layers.append(d)
         self.head = _upload(weights.head)
         self.head_bias = vec(weights.head_bias)
         self.embedding = None if cfg.tied else _upload(weights.embedding)
@@ -112,16 +122,16 @@ class DeviceDecoder:
         self.inv_freq = vec(rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling))
         self.x = torch.empty(cfg.dim, **f32)
         self.normed = torch.empty(cfg.dim, **f32)
-        self.q = torch.empty(cfg.dim, **f32)
-        self.k = torch.empty(kv, **f32)
-        self.v = torch.empty(kv, **f32)
+        self.qkv = torch.empty(cfg.dim + 2 * kv, **f32)
+        self.q, self.k, self.v = self.qkv[:cfg.dim], self.qkv[cfg.dim:cfg.dim + kv], self.qkv[cfg.dim + kv:]
         self.context = torch.empty(cfg.dim, **f32)
         self.attn_out = torch.empty(cfg.dim, **f32)
-        self.gate = torch.empty(cfg.hidden, **f32)
-        self.up = torch.empty(cfg.hidden, **f32)
+        self.gu = torch.empty(2 * cfg.hidden, **f32)
+        self.gate, self.up = self.gu[:cfg.hidden], self.gu[cfg.hidden:]
         self.ffn_out = torch.empty(cfg.dim, **f32)
         self.logits = torch.empty(cfg.vocab, **f32)
-        self.scores = torch.empty((cfg.heads, max_seq), **f32)
+        self.scores = torch.empty(_lib.load().kt_attention_scratch_floats(cfg.heads, cfg.head_dim, max_seq),
+                                  **f32)  # attention scratch
         self.token = torch.zeros(1, dtype=torch.int32, device=dev)
         self.position = torch.zeros(1, dtype=torch.int32, device=dev)
         self.next_token = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -157,27 +167,22 @@ class DeviceDecoder:
             _lib.check(L_.kt_dequantize_column(h, self.head.handle, p(self.token), p(self.x), p(self.status), s))
         else:
             _lib.check(L_.kt_dequantize_rows(h, self.embedding.handle, p(self.token), 1, p(self.x), p(self.status), s))
+        _lib.check(L_.kt_rmsnorm(h, p(self.x), p(self.layers[0]["norm1"]), p(self.normed), 1, cfg.dim, cfg.eps, s))
         for l, L in enumerate(self.layers):
-            _lib.check(L_.kt_rmsnorm(h, p(self.x), p(L["norm1"]), p(self.normed), 1, cfg.dim, cfg.eps, s))
-            self._linear(self.normed, L["wq"], self.q, L["bq"])
-            self._linear(self.normed, L["wk"], self.k, L["bk"])
-            self._linear(self.normed, L["wv"], self.v, L["bv"])
-            _lib.check(L_.kt_rope(h, p(self.q), 1, cfg.dim, hd, p(self.inv_freq), p(self.position), s))
-            _lib.check(L_.kt_rope(h, p(self.k), 1, kvh * hd, hd, p(self.inv_freq), p(self.position), s))
-            _lib.check(L_.kt_kv_store(h, p(self.k), p(self.v), p(self.keys), p(self.values), 1, kvh, hd,
-                                      self.max_seq, l, p(self.position), s))
+            self._linear(self.normed, L["wqkv"], self.qkv, L["bqkv"])
+            _lib.check(L_.kt_rope_kv(h, p(self.qkv), cfg.dim, kvh, hd, p(self.inv_freq), p(self.keys),
+                                     p(self.values), self.max_seq, l, p(self.position), s))
             _lib.check(L_.kt_attention_decode(h, p(self.q), p(self.keys), p(self.values), p(self.context),
                                               p(self.scores), cfg.heads, kvh, hd, self.max_seq, l, self.scale,
                                               p(self.position), s))
             self._linear(self.context, L["wo"], self.attn_out, L["bo"])
-            _lib.check(L_.kt_add(h, p(self.x), p(self.attn_out), cfg.dim, s))
-            _lib.check(L_.kt_rmsnorm(h, p(self.x), p(L["norm2"]), p(self.normed), 1, cfg.dim, cfg.eps, s))
-            self._linear(self.normed, L["wg"], self.gate, L["bg"])
-            self._linear(self.normed, L["wu"], self.up, L["bu"])
+            _lib.check(L_.kt_add_rmsnorm(h, p(self.x), p(self.attn_out), p(L["norm2"]), p(self.normed), 1, cfg.dim,
+                                         cfg.eps, s))
+            self._linear(self.normed, L["wgu"], self.gu, L["bgu"])
             _lib.check(L_.kt_silu_mul(h, p(self.gate), p(self.up), cfg.hidden, s))
             self._linear(self.gate, L["wd"], self.ffn_out, L["bd"])
-            _lib.check(L_.kt_add(h, p(self.x), p(self.ffn_out), cfg.dim, s))
-        _lib.check(L_.kt_rmsnorm(h, p(self.x), p(self.final_norm), p(self.normed), 1, cfg.dim, cfg.eps, s))
+            nxt = self.layers[l + 1]["norm1"] if l + 1 < len(self.layers) else self.final_norm
+            _lib.check(L_.kt_add_rmsnorm(h, p(self.x), p(self.ffn_out), p(nxt), p(self.normed), 1, cfg.dim, cfg.eps, s))
         self._linear(self.normed, self.head, self.logits, self.head_bias)
         _lib.check(L_.kt_argmax(h, p(self.logits), 1, cfg.vocab, p(self.next_token), s))
         _lib.check(L_.kt_increment(h, p(self.position), 1, s))

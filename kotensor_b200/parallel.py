@@ -83,6 +83,17 @@ def shard(qt: QuantizedTensor, axis: int, parts: int, index: int) -> QuantizedTe
     return QuantizedTensor(h, qt._ctx)
 
 
+def concat_columns(weights: list) -> QuantizedTensor:
+    """One weight whose columns are those of ``weights`` side by side
+    (kt_qweight_concat_columns; e.g. q|k|v or gate|up fused into one matmul)."""
+    import torch
+    arr = (ctypes.c_void_p * len(weights))(*[w.handle.value for w in weights])
+    h = ctypes.c_void_p()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(weights[0].device).cuda_stream)
+    _lib.check(_lib.load().kt_qweight_concat_columns(weights[0]._ctx.handle, arr, len(weights), stream, ctypes.byref(h)))
+    return QuantizedTensor(h, weights[0]._ctx)
+
+
 class Comm:
     """One NCCL communicator per rank (kt_comm_init)."""
 

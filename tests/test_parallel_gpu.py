@@ -43,6 +43,24 @@ def test_device_shards_equal_host_shards(kt, oracle, bits, g, shape, parts):
                 assert np.array_equal(z.reshape(-1), hz.reshape(-1))
 
 
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("shape", [(640, 1537), (256, 96), (130, 4096)])
+def test_concatenated_shards_give_back_the_weight(kt, oracle, bits, shape):
+    from kotensor_b200 import parallel as P
+    rng = np.random.default_rng(sum(shape) + bits)
+    w = (rng.standard_normal(shape, dtype=np.float32) * 0.03).astype(np.float32)
+    ref = oracle.quantize(w, bits, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref.qdata, ref.scales, ref.zeros, shape, bits, 64)
+    parts = [P.shard(qt, P.COLUMNS, 3, i) for i in range(3)]
+    back = P.concat_columns(parts)
+    q, s, z = back.download()
+    assert back.shape == shape
+    assert np.array_equal(q.reshape(-1), ref.qdata.reshape(-1))
+    assert np.array_equal(s.reshape(-1).view(np.uint32), ref.scales.reshape(-1).view(np.uint32))
+    if bits == 4:
+        assert np.array_equal(z.reshape(-1), ref.zeros.reshape(-1))
+
+
 def test_row_parallel_and_gather_on_one_rank(kt):
     from kotensor_b200 import parallel as P
     comm = P.Comm(1, 0, P.Comm.unique_id())
