@@ -208,8 +208,9 @@ QWEN2_05B = dict(vocab=151936, dim=896, layers=24, heads=14, kv_heads=2, hidden=
 
 
 def measure_decode(kt, torch, steps: int, prompt_len: int, seed: int) -> dict:
-    """Greedy decode tokens/s of the Qwen2-0.5B-shaped INT4 model (random N(0, 0.02^2)
-    weights quantized on the device, tied embeddings, q/k/v biases), batch 1."""
+    """Prefill and greedy decode of the Qwen2-0.5B-shaped INT4 model (random N(0, 0.02^2)
+    weights quantized on the device, tied embeddings, q/k/v biases), batch 1: the
+    prompt as one block (Transformer.prefill), then timed CUDA-graph decode steps."""
     import numpy as np
     from types import SimpleNamespace
     from kotensor_b200 import decoder as D
@@ -239,10 +240,17 @@ def measure_decode(kt, torch, steps: int, prompt_len: int, seed: int) -> dict:
     head = proj(cfg.dim, cfg.vocab)
     weights = SimpleNamespace(embedding=None, layers=layers, final_norm=np.ones(cfg.dim, np.float32), head=head,
                               head_bias=np.zeros(cfg.vocab, np.float32))
-    dec = D.DeviceDecoder(cfg, weights, max_seq=prompt_len + steps + 8)
+    dec = D.DeviceDecoder(cfg, weights, max_seq=2 * prompt_len + steps + 8)
     prompt = rng.integers(0, cfg.vocab, size=prompt_len).tolist()
-    for t in prompt:  # the prompt, one eager step per token
-        dec.step(t)
+    dec.prefill(prompt)  # warm-up prefill (module set-up, workspaces), then a timed one
+    dec.reset()
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    dec.prefill(prompt)
+    p1.record()
+    torch.cuda.synchronize()
+    prefill_ms = p0.elapsed_time(p1)
     dec.capture()
     for _ in range(3):  # warm-up replays
         dec._graph.replay()
@@ -257,7 +265,9 @@ def measure_decode(kt, torch, steps: int, prompt_len: int, seed: int) -> dict:
     weight_bytes = sum(w.size_in_bytes for L in dec.layers for k, w in L.items() if k.startswith("w"))
     weight_bytes += dec.head.size_in_bytes
     return {"model": "qwen2-0.5b-shaped int4 g64 (random weights, tied, qkv bias)", "batch": 1,
-            "prompt": prompt_len, "steps": steps, "ms_per_token": round(ms, 4),
+            "prompt": prompt_len, "prefill_ms": round(prefill_ms, 3),
+            "prefill_tokens_per_s": round(prompt_len / (prefill_ms / 1e3), 1),
+            "steps": steps, "ms_per_token": round(ms, 4),
             "tokens_per_s": round(1e3 / ms, 1), "weight_bytes_per_token": int(weight_bytes),
             "weight_gbs": round(weight_bytes / (ms / 1e3) / 1e9, 1),
             "context_end": prompt_len + steps + 3}

@@ -248,15 +248,19 @@ kt_status kt_rope(kt_ctx* ctx, float* v_dev, int32_t rows, int32_t width, int32_
 kt_status kt_kv_store(kt_ctx* ctx, const float* k_dev, const float* v_dev, float* k_cache, float* v_cache,
                       int32_t rows, int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t layer,
                       const int32_t* position_dev, void* stream);
-/* attendHead for every query head of one token at *position_dev (Attention.kt:295-328):
+/* attendHead for every query head of `rows` tokens, row t at position *position_dev + t
+ * attending to positions 0..that position (Attention.kt:295-328; rows > 1 is the
+ * causal prefill of Attention.prefillInto, Attention.kt:241-293):
  * scores (dot * scale) over positions 0..pos, softmax from the reference's -1e9
  * initial maximum, context = weighted sum of values (split over blocks of 64
  * positions and merged with a log-sum-exp in block order).  scores_dev: scratch of
- * kt_attention_scratch_floats(heads, head_dim, max_seq) floats; head_dim <= 254. */
-size_t kt_attention_scratch_floats(int32_t heads, int32_t head_dim, int32_t max_seq);
+ * kt_attention_scratch_floats(rows, heads, head_dim, max_seq) floats; head_dim <= 254.
+ * q_dev: rows q_stride floats apart (a fused q|k|v row is wider than the q part);
+ * context_dev: [rows x heads*head_dim]. */
+size_t kt_attention_scratch_floats(int32_t rows, int32_t heads, int32_t head_dim, int32_t max_seq);
 kt_status kt_attention_decode(kt_ctx* ctx, const float* q_dev, const float* k_cache, const float* v_cache,
-                              float* context_dev, float* scores_dev, int32_t heads, int32_t kv_heads,
-                              int32_t head_dim, int32_t max_seq, int32_t layer, float scale,
+                              float* context_dev, float* scores_dev, int32_t rows, int32_t q_stride, int32_t heads,
+                              int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t layer, float scale,
                               const int32_t* position_dev, void* stream);
 /* gate = silu(gate) * up (SwiGLU.forwardInto, Tensor.kt:231-237). */
 kt_status kt_silu_mul(kt_ctx* ctx, float* gate_dev, const float* up_dev, int64_t n, void* stream);
@@ -264,20 +268,24 @@ kt_status kt_silu_mul(kt_ctx* ctx, float* gate_dev, const float* up_dev, int64_t
  * TransformerBlock.decodeInto fused with the norm that follows it). */
 kt_status kt_add_rmsnorm(kt_ctx* ctx, float* x_dev, const float* y_dev, const float* weight_dev, float* out_dev,
                          int32_t rows, int32_t dim, float eps, void* stream);
-/* RoPE on the q and k parts of one fused q|k|v row (widths q_width and
- * kv_heads*head_dim), then k and v into the cache at *position_dev. */
-kt_status kt_rope_kv(kt_ctx* ctx, float* qkv_dev, int32_t q_width, int32_t kv_heads, int32_t head_dim,
+/* RoPE on the q and k parts of fused q|k|v rows (widths q_width and
+ * kv_heads*head_dim; row r at position *position_dev + r), then k and v into the cache. */
+kt_status kt_rope_kv(kt_ctx* ctx, float* qkv_dev, int32_t rows, int32_t q_width, int32_t kv_heads, int32_t head_dim,
                      const float* inv_freq_dev, float* k_cache, float* v_cache, int32_t max_seq, int32_t layer,
                      const int32_t* position_dev, void* stream);
+/* out[t][j] = silu(gu[t][j]) * gu[t][hidden + j] for fused gate|up rows [rows x 2*hidden]. */
+kt_status kt_silu_mul_rows(kt_ctx* ctx, const float* gu_dev, float* out_dev, int32_t rows, int32_t hidden,
+                           void* stream);
 /* x += y (Tensor.addInPlace). */
 kt_status kt_add(kt_ctx* ctx, float* x_dev, const float* y_dev, int64_t n, void* stream);
 /* argmaxOfLastToken per row (Transformer.kt:255-266): the largest logit above
  * -1e9, the lowest index among equal ones, 0 if none. */
 kt_status kt_argmax(kt_ctx* ctx, const float* logits_dev, int32_t rows, int32_t n, int32_t* out_dev, void* stream);
-/* QuantizedTensor.dequantizeColumn(*column_dev) (the tied embedding lookup, Embedding.kt:129-135):
- * out_dev [rows]; an out-of-range column sets KT_ERR_INVALID_ARGUMENT in *status_dev. */
-kt_status kt_dequantize_column(kt_ctx* ctx, const kt_qweight* w, const int32_t* column_dev, float* out_dev,
-                               int32_t* status_dev, void* stream);
+/* QuantizedTensor.dequantizeColumn for `count` columns (the tied embedding lookup,
+ * Embedding.kt:119-135): out_dev [count x rows]; an out-of-range column sets
+ * KT_ERR_INVALID_ARGUMENT in *status_dev and leaves its output row untouched. */
+kt_status kt_dequantize_column(kt_ctx* ctx, const kt_qweight* w, const int32_t* columns_dev, int32_t count,
+                               float* out_dev, int32_t* status_dev, void* stream);
 /* *value_dev += delta on `stream` (advances a captured step's position). */
 kt_status kt_increment(kt_ctx* ctx, int32_t* value_dev, int32_t delta, void* stream);
 

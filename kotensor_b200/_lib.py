@@ -81,15 +81,16 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_allgather_columns": ([P, P, P, I32, I32, P], I32),
     "kt_rmsnorm": ([P, P, P, P, I32, I32, F32, P], I32),
     "kt_add_rmsnorm": ([P, P, P, P, P, I32, I32, F32, P], I32),
-    "kt_rope_kv": ([P, P, I32, I32, I32, P, P, P, I32, I32, P, P], I32),
-    "kt_attention_scratch_floats": ([I32, I32, I32], SZ),
+    "kt_rope_kv": ([P, P, I32, I32, I32, I32, P, P, P, I32, I32, P, P], I32),
+    "kt_attention_scratch_floats": ([I32, I32, I32, I32], SZ),
+    "kt_silu_mul_rows": ([P, P, P, I32, I32, P], I32),
     "kt_rope": ([P, P, I32, I32, I32, P, P, P], I32),
     "kt_kv_store": ([P, P, P, P, P, I32, I32, I32, I32, I32, P, P], I32),
-    "kt_attention_decode": ([P, P, P, P, P, P, I32, I32, I32, I32, I32, F32, P, P], I32),
+    "kt_attention_decode": ([P, P, P, P, P, P, I32, I32, I32, I32, I32, I32, I32, F32, P, P], I32),
     "kt_silu_mul": ([P, P, P, I64, P], I32),
     "kt_add": ([P, P, P, I64, P], I32),
     "kt_argmax": ([P, P, I32, I32, P, P], I32),
-    "kt_dequantize_column": ([P, P, P, P, P, P], I32),
+    "kt_dequantize_column": ([P, P, P, I32, P, P, P], I32),
     "kt_increment": ([P, P, I32, P], I32),
 }
 

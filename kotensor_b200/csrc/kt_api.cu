@@ -679,21 +679,27 @@ kt_status kt_add_rmsnorm(kt_ctx* ctx, float* x, const float* y, const float* wei
     return KT_OK;
 }
 
-kt_status kt_rope_kv(kt_ctx* ctx, float* qkv, int32_t q_width, int32_t kv_heads, int32_t head_dim,
+kt_status kt_rope_kv(kt_ctx* ctx, float* qkv, int32_t rows, int32_t q_width, int32_t kv_heads, int32_t head_dim,
                      const float* inv_freq, float* k_cache, float* v_cache, int32_t max_seq, int32_t layer,
                      const int32_t* position_dev, void* stream) {
-    if (!ctx || !qkv || !inv_freq || !k_cache || !v_cache || !position_dev || head_dim <= 0 || head_dim % 2 != 0 ||
-        q_width % head_dim != 0 || kv_heads <= 0 || max_seq <= 0 || layer < 0)
+    if (!ctx || !qkv || !inv_freq || !k_cache || !v_cache || !position_dev || rows <= 0 || rows > 65535 ||
+        head_dim <= 0 || head_dim % 2 != 0 || q_width % head_dim != 0 || kv_heads <= 0 || max_seq <= 0 || layer < 0)
         return fail(KT_ERR_INVALID_ARGUMENT, "bad rope_kv arguments");
-    KT_CUDA_TRY(launch_rope_kv(qkv, q_width, kv_heads, head_dim, inv_freq, k_cache, v_cache, max_seq, layer,
+    KT_CUDA_TRY(launch_rope_kv(qkv, rows, q_width, kv_heads, head_dim, inv_freq, k_cache, v_cache, max_seq, layer,
                                position_dev, pick(ctx, stream)),
                 "rope_kv launch");
     return KT_OK;
 }
 
-size_t kt_attention_scratch_floats(int32_t heads, int32_t head_dim, int32_t max_seq) {
-    if (heads <= 0 || head_dim <= 0 || max_seq <= 0) return 0;
-    return attention_scratch_floats(heads, head_dim, max_seq);
+size_t kt_attention_scratch_floats(int32_t rows, int32_t heads, int32_t head_dim, int32_t max_seq) {
+    if (rows <= 0 || heads <= 0 || head_dim <= 0 || max_seq <= 0) return 0;
+    return attention_scratch_floats(rows, heads, head_dim, max_seq);
+}
+
+kt_status kt_silu_mul_rows(kt_ctx* ctx, const float* gu, float* out, int32_t rows, int32_t hidden, void* stream) {
+    if (!ctx || !gu || !out || rows <= 0 || hidden <= 0) return fail(KT_ERR_INVALID_ARGUMENT, "bad silu_mul_rows arguments");
+    KT_CUDA_TRY(launch_silu_mul_rows(gu, out, rows, hidden, pick(ctx, stream)), "silu_mul_rows launch");
+    return KT_OK;
 }
 
 kt_status kt_rope(kt_ctx* ctx, float* v, int32_t rows, int32_t width, int32_t head_dim, const float* inv_freq,
@@ -718,13 +724,16 @@ kt_status kt_kv_store(kt_ctx* ctx, const float* k, const float* v, float* k_cach
 }
 
 kt_status kt_attention_decode(kt_ctx* ctx, const float* q, const float* k_cache, const float* v_cache, float* context,
-                              float* scores, int32_t heads, int32_t kv_heads, int32_t head_dim, int32_t max_seq,
-                              int32_t layer, float scale, const int32_t* position_dev, void* stream) {
-    if (!ctx || !q || !k_cache || !v_cache || !context || !scores || !position_dev || heads <= 0 || kv_heads <= 0 ||
-        heads % kv_heads != 0 || head_dim <= 0 || max_seq <= 0 || layer < 0)
+                              float* scores, int32_t rows, int32_t q_stride, int32_t heads, int32_t kv_heads,
+                              int32_t head_dim, int32_t max_seq, int32_t layer, float scale,
+                              const int32_t* position_dev, void* stream) {
+    if (!ctx || !q || !k_cache || !v_cache || !context || !scores || !position_dev || rows <= 0 || rows > 65535 ||
+        q_stride < heads * head_dim ||
+        heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || head_dim <= 0 || head_dim > 254 || max_seq <= 0 ||
+        layer < 0)
         return fail(KT_ERR_INVALID_ARGUMENT, "bad attention arguments");
-    KT_CUDA_TRY(launch_attention_decode(q, k_cache, v_cache, context, scores, heads, kv_heads, head_dim, max_seq,
-                                        layer, scale, position_dev, pick(ctx, stream)),
+    KT_CUDA_TRY(launch_attention_decode(q, k_cache, v_cache, context, scores, rows, q_stride, heads, kv_heads,
+                                        head_dim, max_seq, layer, scale, position_dev, pick(ctx, stream)),
                 "attention launch");
     return KT_OK;
 }
@@ -753,10 +762,11 @@ kt_status kt_argmax(kt_ctx* ctx, const float* logits, int32_t rows, int32_t n, i
     return KT_OK;
 }
 
-kt_status kt_dequantize_column(kt_ctx* ctx, const kt_qweight* w, const int32_t* column_dev, float* out_dev,
-                               int32_t* status_dev, void* stream) {
-    if (!ctx || !w || !column_dev || !out_dev) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
-    KT_CUDA_TRY(launch_dequantize_column(view(w), column_dev, out_dev, status_dev, pick(ctx, stream)),
+kt_status kt_dequantize_column(kt_ctx* ctx, const kt_qweight* w, const int32_t* columns_dev, int32_t count,
+                               float* out_dev, int32_t* status_dev, void* stream) {
+    if (!ctx || !w || !columns_dev || !out_dev || count <= 0 || count > 65535)
+        return fail(KT_ERR_INVALID_ARGUMENT, "bad dequantize_column arguments");
+    KT_CUDA_TRY(launch_dequantize_column(view(w), columns_dev, count, out_dev, status_dev, pick(ctx, stream)),
                 "dequantize_column launch");
     return KT_OK;
 }

@@ -76,19 +76,22 @@ __global__ void __launch_bounds__(kThreads) add_rmsnorm_kernel(float* __restrict
     for (int d = threadIdx.x; d < dim; d += blockDim.x) orow[d] = xr[d] * r * w[d];
 }
 
-// RoPE on the q and k parts of one fused q|k|v row, then the k and v parts
-// into the cache at *pos (Attention.decodeInto, Attention.kt:222-232).
+// RoPE on the q and k parts of fused q|k|v rows (row r at position *pos + r),
+// then the k and v parts into the cache (Attention.decodeInto / prefillInto,
+// Attention.kt:222-232, :256-276).  blockIdx.y = row.
 __global__ void rope_kv_kernel(float* __restrict__ qkv, int q_width, int kv_heads, int head_dim,
                                const float* __restrict__ inv_freq, float* __restrict__ kc, float* __restrict__ vc,
                                int max_seq, int layer, const int32_t* __restrict__ pos) {
     const int half = head_dim / 2;
     const int kv_width = kv_heads * head_dim;
     const int rope_pairs = (q_width + kv_width) / 2;  // pairs over the q heads then the k heads
-    const int p = *pos;
+    const int r = blockIdx.y;
+    const int p = *pos + r;
+    float* row = qkv + static_cast<int64_t>(r) * (q_width + 2 * kv_width);
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < rope_pairs + kv_width; idx += gridDim.x * blockDim.x) {
         if (idx < rope_pairs) {
             const int head = idx / half, i = idx % half;
-            float* v = qkv + head * head_dim;  // q heads, then k heads (contiguous)
+            float* v = row + head * head_dim;  // q heads, then k heads (contiguous)
             const float theta = static_cast<float>(p) * inv_freq[i];
             float sn, cs;
             sincosf(theta, &sn, &cs);
@@ -105,7 +108,7 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int q_width, int kv_head
             const int e = idx - rope_pairs;  // a value element
             const int vh = e / head_dim, d = e % head_dim;
             const int64_t off = ((static_cast<int64_t>(layer) * kv_heads + vh) * max_seq + p) * head_dim + d;
-            vc[off] = qkv[q_width + kv_width + e];
+            vc[off] = row[q_width + kv_width + e];
         }
     }
 }
@@ -162,17 +165,18 @@ constexpr int kSpan = 64;  // positions per block
 __global__ void __launch_bounds__(kThreads) attention_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
     float* __restrict__ scratch, int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale,
-    const int32_t* __restrict__ pos) {
+    int q_stride, const int32_t* __restrict__ pos) {
     __shared__ float red[32];
+    const int t = blockIdx.z;  // query row: position *pos + t, attending to 0..*pos + t
     __shared__ float qs[kMaxHeadDim + 2];
     __shared__ float sc[kSpan];
     __shared__ float part[kThreads / 32][kMaxHeadDim + 2];
     const int h = blockIdx.x, split = blockIdx.y;
     const int j0 = split * kSpan;
-    const int j1 = min(j0 + kSpan, *pos + 1);
+    const int j1 = min(j0 + kSpan, *pos + t + 1);
     if (j0 >= j1) return;  // past the current position: the merge skips this split
     const int group = heads / kv_heads;
-    const float* qh = q + static_cast<int64_t>(h) * head_dim;
+    const float* qh = q + static_cast<int64_t>(t) * q_stride + static_cast<int64_t>(h) * head_dim;
     for (int d = threadIdx.x; d < head_dim; d += blockDim.x) qs[d] = qh[d];
     __syncthreads();
     const int64_t base = ((static_cast<int64_t>(layer) * kv_heads + h / group) * max_seq) * head_dim;
@@ -218,7 +222,7 @@ __global__ void __launch_bounds__(kThreads) attention_partial_kernel(
     __syncthreads();
     // this split's partial: scratch[(h * splits + split) * (head_dim + 2) ..]
     const int64_t splits = (max_seq + kSpan - 1) / kSpan;
-    float* out = scratch + (static_cast<int64_t>(h) * splits + split) * (head_dim + 2);
+    float* out = scratch + ((static_cast<int64_t>(t) * heads + h) * splits + split) * (head_dim + 2);
     for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
         float v = 0.0f;
         for (int w = 0; w < nw; ++w) v += part[w][d];
@@ -230,12 +234,13 @@ __global__ void __launch_bounds__(kThreads) attention_partial_kernel(
     }
 }
 
-__global__ void attention_merge_kernel(const float* __restrict__ scratch, float* __restrict__ ctx, int head_dim,
-                                       int max_seq, const int32_t* __restrict__ pos) {
-    const int h = blockIdx.x;
-    const int splits = *pos / kSpan + 1;
+__global__ void attention_merge_kernel(const float* __restrict__ scratch, float* __restrict__ ctx, int heads,
+                                       int head_dim, int max_seq, const int32_t* __restrict__ pos) {
+    const int h = blockIdx.x, t = blockIdx.y;
+    const int splits = (*pos + t) / kSpan + 1;
     const int stride = head_dim + 2;
-    const float* base = scratch + static_cast<int64_t>(h) * ((max_seq + kSpan - 1) / kSpan) * stride;
+    const float* base =
+        scratch + (static_cast<int64_t>(t) * heads + h) * ((max_seq + kSpan - 1) / kSpan) * stride;
     float m = -1e9f;
     for (int s = 0; s < splits; ++s) m = fmaxf(m, base[s * stride]);
     float l = 0.0f;
@@ -244,7 +249,7 @@ __global__ void attention_merge_kernel(const float* __restrict__ scratch, float*
     for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
         float v = 0.0f;
         for (int s = 0; s < splits; ++s) v += base[s * stride + 2 + d] * expf(base[s * stride] - m);
-        ctx[static_cast<int64_t>(h) * head_dim + d] = v * inv;
+        ctx[(static_cast<int64_t>(t) * heads + h) * head_dim + d] = v * inv;
     }
 }
 
@@ -254,6 +259,17 @@ __global__ void silu_mul_kernel(float* __restrict__ gate, const float* __restric
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const float x = gate[i];
         gate[i] = x / (1.0f + expf(-x)) * up[i];
+    }
+}
+
+// out[t][j] = silu(gu[t][j]) * gu[t][hidden + j] for fused gate|up rows.
+__global__ void silu_mul_rows_kernel(const float* __restrict__ gu, float* __restrict__ out, int rows, int hidden) {
+    const int64_t n = static_cast<int64_t>(rows) * hidden;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t t = i / hidden, j = i - t * hidden;
+        const float x = gu[t * 2 * hidden + j];
+        out[i] = x / (1.0f + expf(-x)) * gu[t * 2 * hidden + hidden + j];
     }
 }
 
@@ -314,9 +330,10 @@ __global__ void argmax_merge_kernel(const float* __restrict__ pv, const int* __r
 
 // dequantizeColumn(token) of a weight [K x N] (the tied embedding lookup):
 // out[k] = value(k, *col) for k < K.
-__global__ void dequantize_column_kernel(QView w, const int32_t* __restrict__ col, float* __restrict__ out,
+__global__ void dequantize_column_kernel(QView w, const int32_t* __restrict__ cols, float* __restrict__ outs,
                                          int32_t* __restrict__ status) {
-    const int c = *col;
+    const int c = cols[blockIdx.y];
+    float* out = outs + static_cast<int64_t>(blockIdx.y) * w.rows;
     if (c < 0 || c >= w.columns) {
         if (blockIdx.x == 0 && threadIdx.x == 0 && status != nullptr) atomicOr(status, KT_ERR_INVALID_ARGUMENT);
         return;
@@ -351,15 +368,15 @@ cudaError_t launch_add_rmsnorm(float* x, const float* y, const float* w, float* 
     add_rmsnorm_kernel<<<rows, kThreads, 0, s>>>(x, y, w, out, dim, eps);
     return cudaGetLastError();
 }
-cudaError_t launch_rope_kv(float* qkv, int q_width, int kv_heads, int head_dim, const float* inv_freq, float* kc,
-                           float* vc, int max_seq, int layer, const int32_t* pos, cudaStream_t s) {
+cudaError_t launch_rope_kv(float* qkv, int rows, int q_width, int kv_heads, int head_dim, const float* inv_freq,
+                           float* kc, float* vc, int max_seq, int layer, const int32_t* pos, cudaStream_t s) {
     const int total = (q_width + kv_heads * head_dim) / 2 + kv_heads * head_dim;
-    rope_kv_kernel<<<(total + kThreads - 1) / kThreads, kThreads, 0, s>>>(qkv, q_width, kv_heads, head_dim, inv_freq,
-                                                                          kc, vc, max_seq, layer, pos);
+    rope_kv_kernel<<<dim3((total + kThreads - 1) / kThreads, rows), kThreads, 0, s>>>(
+        qkv, q_width, kv_heads, head_dim, inv_freq, kc, vc, max_seq, layer, pos);
     return cudaGetLastError();
 }
-size_t attention_scratch_floats(int heads, int head_dim, int max_seq) {
-    return static_cast<size_t>(heads) * ((max_seq + kSpan - 1) / kSpan) * (head_dim + 2);
+size_t attention_scratch_floats(int rows, int heads, int head_dim, int max_seq) {
+    return static_cast<size_t>(rows) * heads * ((max_seq + kSpan - 1) / kSpan) * (head_dim + 2);
 }
 cudaError_t launch_rope(float* v, int rows, int width, int head_dim, const float* inv_freq, const int32_t* pos,
                         cudaStream_t s) {
@@ -374,19 +391,23 @@ cudaError_t launch_kv_store(const float* k, const float* v, float* kc, float* vc
     return cudaGetLastError();
 }
 cudaError_t launch_attention_decode(const float* q, const float* kc, const float* vc, float* ctx, float* scores,
-                                    int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale,
-                                    const int32_t* pos, cudaStream_t s) {
+                                    int rows, int q_stride, int heads, int kv_heads, int head_dim, int max_seq,
+                                    int layer, float scale, const int32_t* pos, cudaStream_t s) {
     if (head_dim > kMaxHeadDim) return cudaErrorInvalidValue;
-    const dim3 grid(heads, (max_seq + kSpan - 1) / kSpan);
+    const dim3 grid(heads, (max_seq + kSpan - 1) / kSpan, rows);
     attention_partial_kernel<<<grid, kThreads, 0, s>>>(q, kc, vc, scores, heads, kv_heads, head_dim, max_seq, layer,
-                                                       scale, pos);
+                                                       scale, q_stride, pos);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    attention_merge_kernel<<<heads, 128, 0, s>>>(scores, ctx, head_dim, max_seq, pos);
+    attention_merge_kernel<<<dim3(heads, rows), 128, 0, s>>>(scores, ctx, heads, head_dim, max_seq, pos);
     return cudaGetLastError();
 }
 cudaError_t launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s) {
     silu_mul_kernel<<<grid_for(n), kThreads, 0, s>>>(gate, up, n);
+    return cudaGetLastError();
+}
+cudaError_t launch_silu_mul_rows(const float* gu, float* out, int rows, int hidden, cudaStream_t s) {
+    silu_mul_rows_kernel<<<grid_for(static_cast<int64_t>(rows) * hidden), kThreads, 0, s>>>(gu, out, rows, hidden);
     return cudaGetLastError();
 }
 cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s) {
@@ -406,8 +427,9 @@ cudaError_t launch_argmax(const float* logits, int rows, int n, int32_t* out, vo
     argmax_merge_kernel<<<rows, 32, 0, s>>>(pv, pi, chunks, out);
     return cudaGetLastError();
 }
-cudaError_t launch_dequantize_column(const QView& w, const int32_t* col, float* out, int32_t* status, cudaStream_t s) {
-    dequantize_column_kernel<<<grid_for(w.rows), kThreads, 0, s>>>(w, col, out, status);
+cudaError_t launch_dequantize_column(const QView& w, const int32_t* col, int count, float* out, int32_t* status,
+                                     cudaStream_t s) {
+    dequantize_column_kernel<<<dim3(grid_for(w.rows), count), kThreads, 0, s>>>(w, col, out, status);
     return cudaGetLastError();
 }
 cudaError_t launch_increment(int32_t* p, int32_t delta, cudaStream_t s) {

@@ -130,8 +130,9 @@ class DeviceDecoder:
         self.gate, self.up = self.gu[:cfg.hidden], self.gu[cfg.hidden:]
         self.ffn_out = torch.empty(cfg.dim, **f32)
         self.logits = torch.empty(cfg.vocab, **f32)
-        self.scores = torch.empty(_lib.load().kt_attention_scratch_floats(cfg.heads, cfg.head_dim, max_seq),
+        self.scores = torch.empty(_lib.load().kt_attention_scratch_floats(1, cfg.heads, cfg.head_dim, max_seq),
                                   **f32)  # attention scratch
+        self._prefill_rows = 0  # prefill buffers, allocated on first use
         self.token = torch.zeros(1, dtype=torch.int32, device=dev)
         self.position = torch.zeros(1, dtype=torch.int32, device=dev)
         self.next_token = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -164,17 +165,17 @@ class DeviceDecoder:
         s, p = self._stream(), self._p
         hd, kvh = cfg.head_dim, cfg.kv_heads
         if cfg.tied:
-            _lib.check(L_.kt_dequantize_column(h, self.head.handle, p(self.token), p(self.x), p(self.status), s))
+            _lib.check(L_.kt_dequantize_column(h, self.head.handle, p(self.token), 1, p(self.x), p(self.status), s))
         else:
             _lib.check(L_.kt_dequantize_rows(h, self.embedding.handle, p(self.token), 1, p(self.x), p(self.status), s))
         _lib.check(L_.kt_rmsnorm(h, p(self.x), p(self.layers[0]["norm1"]), p(self.normed), 1, cfg.dim, cfg.eps, s))
         for l, L in enumerate(self.layers):
             self._linear(self.normed, L["wqkv"], self.qkv, L["bqkv"])
-            _lib.check(L_.kt_rope_kv(h, p(self.qkv), cfg.dim, kvh, hd, p(self.inv_freq), p(self.keys),
+            _lib.check(L_.kt_rope_kv(h, p(self.qkv), 1, cfg.dim, kvh, hd, p(self.inv_freq), p(self.keys),
                                      p(self.values), self.max_seq, l, p(self.position), s))
             _lib.check(L_.kt_attention_decode(h, p(self.q), p(self.keys), p(self.values), p(self.context),
-                                              p(self.scores), cfg.heads, kvh, hd, self.max_seq, l, self.scale,
-                                              p(self.position), s))
+                                              p(self.scores), 1, cfg.dim, cfg.heads, kvh, hd, self.max_seq, l,
+                                              self.scale, p(self.position), s))
             self._linear(self.context, L["wo"], self.attn_out, L["bo"])
             _lib.check(L_.kt_add_rmsnorm(h, p(self.x), p(self.attn_out), p(L["norm2"]), p(self.normed), 1, cfg.dim,
                                          cfg.eps, s))
@@ -187,6 +188,74 @@ class DeviceDecoder:
         _lib.check(L_.kt_argmax(h, p(self.logits), 1, cfg.vocab, p(self.next_token), s))
         _lib.check(L_.kt_increment(h, p(self.position), 1, s))
         self.token.copy_(self.next_token)
+
+    def _prefill_buffers(self, rows: int) -> None:
+        if rows <= self._prefill_rows:
+            return
+        cfg = self.cfg
+        dev = self.x.device
+        f32 = dict(dtype=torch.float32, device=dev)
+        kv = cfg.kv_heads * cfg.head_dim
+        self.px = torch.empty((rows, cfg.dim), **f32)
+        self.pnormed = torch.empty((rows, cfg.dim), **f32)
+        self.pqkv = torch.empty((rows, cfg.dim + 2 * kv), **f32)
+        self.pctx = torch.empty((rows, cfg.dim), **f32)
+        self.pattn = torch.empty((rows, cfg.dim), **f32)
+        self.pgu = torch.empty((rows, 2 * cfg.hidden), **f32)
+        self.pact = torch.empty((rows, cfg.hidden), **f32)
+        self.pffn = torch.empty((rows, cfg.dim), **f32)
+        self.ptokens = torch.empty(rows, dtype=torch.int32, device=dev)
+        self.pscores = torch.empty(
+            _lib.load().kt_attention_scratch_floats(rows, cfg.heads, cfg.head_dim, self.max_seq), **f32)
+        self._prefill_rows = rows
+
+    def prefill(self, prompt: list[int]):
+        """Transformer.prefill (Transformer.kt:99-132): the whole prompt as one
+        [T x dim] block through every layer (the matmuls at m = T on the tensor-core
+        GEMM, causal attention over the cache); returns the last token's logits and
+        leaves its greedy successor in next_token / token."""
+        T = len(prompt)
+        if T == 0:
+            raise ValueError("Prompt cannot be empty")
+        if any(not 0 <= t < self.cfg.vocab for t in prompt):
+            raise ValueError("token out of vocab bounds")
+        if self.length + T > self.max_seq:
+            raise ValueError(f"KV cache full: {self.length} + {T} positions exceed maxSequenceLength {self.max_seq}")
+        self._prefill_buffers(T)
+        L_ = _lib.load()
+        cfg, h = self.cfg, self.ctx.handle
+        s, p = self._stream(), self._p
+        hd, kvh = cfg.head_dim, cfg.kv_heads
+        kv = kvh * hd
+        self.ptokens[:T].copy_(torch.tensor(prompt, dtype=torch.int32))
+        px, pn = self.px[:T], self.pnormed[:T]
+        pqkv, pctx, pattn = self.pqkv[:T], self.pctx[:T], self.pattn[:T]
+        pgu, pact, pffn = self.pgu[:T], self.pact[:T], self.pffn[:T]
+        if cfg.tied:
+            _lib.check(L_.kt_dequantize_column(h, self.head.handle, p(self.ptokens), T, p(px), p(self.status), s))
+        else:
+            _lib.check(L_.kt_dequantize_rows(h, self.embedding.handle, p(self.ptokens), T, p(px), p(self.status), s))
+        _lib.check(L_.kt_rmsnorm(h, p(px), p(self.layers[0]["norm1"]), p(pn), T, cfg.dim, cfg.eps, s))
+        for l, L in enumerate(self.layers):
+            MatMul.multiply_quantized(pn, L["wqkv"], pqkv, T, accumulate=False, bias=L["bqkv"])
+            _lib.check(L_.kt_rope_kv(h, p(pqkv), T, cfg.dim, kvh, hd, p(self.inv_freq), p(self.keys), p(self.values),
+                                     self.max_seq, l, p(self.position), s))
+            _lib.check(L_.kt_attention_decode(h, p(pqkv), p(self.keys), p(self.values), p(pctx), p(self.pscores), T,
+                                              cfg.dim + 2 * kv, cfg.heads, kvh, hd, self.max_seq, l, self.scale,
+                                              p(self.position), s))
+            MatMul.multiply_quantized(pctx, L["wo"], pattn, T, accumulate=False, bias=L["bo"])
+            _lib.check(L_.kt_add_rmsnorm(h, p(px), p(pattn), p(L["norm2"]), p(pn), T, cfg.dim, cfg.eps, s))
+            MatMul.multiply_quantized(pn, L["wgu"], pgu, T, accumulate=False, bias=L["bgu"])
+            _lib.check(L_.kt_silu_mul_rows(h, p(pgu), p(pact), T, cfg.hidden, s))
+            MatMul.multiply_quantized(pact, L["wd"], pffn, T, accumulate=False, bias=L["bd"])
+            nxt = self.layers[l + 1]["norm1"] if l + 1 < len(self.layers) else self.final_norm
+            _lib.check(L_.kt_add_rmsnorm(h, p(px), p(pffn), p(nxt), p(pn), T, cfg.dim, cfg.eps, s))
+        self._linear(pn[T - 1], self.head, self.logits, self.head_bias)
+        _lib.check(L_.kt_argmax(h, p(self.logits), 1, cfg.vocab, p(self.next_token), s))
+        _lib.check(L_.kt_increment(h, p(self.position), T, s))
+        self.token.copy_(self.next_token)
+        self.length += T
+        return self.logits
 
     def step(self, token: int):
         """Transformer.decode(token): the logits of this step (device tensor)."""

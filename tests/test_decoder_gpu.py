@@ -68,3 +68,35 @@ def test_captured_step_replays_like_eager_steps(kt, oracle):
     assert out_graph == out_eager
     assert torch.equal(a.logits, b.logits)
     assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("name", sorted(CONFIGS))
+@pytest.mark.parametrize("prompt_len", [5, 37])
+def test_prefill_matches_stepwise_oracle(kt, oracle, name, prompt_len):
+    """Transformer.prefill on the device (the prompt as one block, matmuls at
+    m = prompt length on the tensor-core GEMM when m >= 9, bf16 tolerance)
+    against the oracle fed the prompt token by token; then decode steps from
+    the prefilled cache stay within the fp32 step tolerance of the oracle's."""
+    from oracle import decoder_oracle as DO
+    from kotensor_b200 import decoder as D
+    cfg_o, cfg_d = DO.DecoderConfig(**CONFIGS[name]), D.DecoderConfig(**CONFIGS[name])
+    weights = DO.DecoderWeights.random(cfg_o, seed=100 + prompt_len)
+    ref = DO.OracleDecoder(weights, max_seq=64)
+    dev = D.DeviceDecoder(cfg_d, weights, max_seq=64)
+    rng = np.random.default_rng(prompt_len)
+    prompt = rng.integers(0, cfg_o.vocab, size=prompt_len).tolist()
+    for t in prompt:
+        ref_logits = ref.step(t)
+    logits = dev.prefill(prompt).cpu().numpy()
+    tol = 2e-2 if prompt_len >= 9 else TOL
+    scale = np.abs(ref_logits).max()
+    assert np.abs(logits - ref_logits).max() <= tol * scale
+    token = int(dev.next_token.item())
+    for _ in range(4):
+        logits = dev.step(token).cpu().numpy()
+        ref_logits = ref.step(token)
+        scale = np.abs(ref_logits).max()
+        assert np.abs(logits - ref_logits).max() <= tol * scale
+        token = int(dev.next_token.item())
+    assert int(dev.status.item()) == 0
+    assert kt.Context.get().take_error() == 0
