@@ -49,7 +49,8 @@ enum {
     KT_ERR_CUDA = 3,             /* CUDA runtime failure -> IllegalStateException */
     KT_ERR_OUT_OF_MEMORY = 4,
     KT_ERR_UNSUPPORTED = 5,
-    KT_ERR_NCCL = 6
+    KT_ERR_NCCL = 6,
+    KT_ERR_IO = 7                /* reference: IOException / FileNotFoundException */
 };
 
 typedef struct kt_ctx kt_ctx;
@@ -127,6 +128,11 @@ kt_status kt_shard_bounds(int32_t axis, int32_t extent, int32_t group_size, int3
 /* A new device weight holding shard `index` of `parts` of w, built on `stream`. */
 kt_status kt_qweight_shard(kt_ctx* ctx, const kt_qweight* w, int32_t axis, int32_t parts, int32_t index,
                            void* stream, kt_qweight** out);
+/* A new device weight holding rows (axis 0) or columns (axis 1) [begin, end) of w;
+ * a row slice must start on a group boundary and end on one or at K (the blocks
+ * kt_qweight_shard takes, and e.g. q / k / v out of a fused q|k|v weight). */
+kt_status kt_qweight_slice(kt_ctx* ctx, const kt_qweight* w, int32_t axis, int32_t begin, int32_t end, void* stream,
+                           kt_qweight** out);
 
 /* The inverse of column shards: one weight whose columns are those of ws[0..count-1]
  * side by side (1 <= count <= 4; same bits, group size and rows), e.g. q|k|v or
@@ -288,6 +294,79 @@ kt_status kt_dequantize_column(kt_ctx* ctx, const kt_qweight* w, const int32_t* 
                                float* out_dev, int32_t* status_dev, void* stream);
 /* *value_dev += delta on `stream` (advances a captured step's position). */
 kt_status kt_increment(kt_ctx* ctx, int32_t* value_dev, int32_t delta, void* stream);
+
+/* ------------------------------------------------------------ safetensors files
+ * The reference's model files (SafeTensors.kt:12-249, written by
+ * Transformer.saveQuantized, Transformer.kt:402-431): an 8-byte little-endian
+ * header length, a JSON header {name: {"dtype", "shape", "data_offsets"},
+ * "__metadata__": {key: value}} padded with spaces to a multiple of 8 bytes,
+ * then every tensor's bytes.  Parsing and writing run on the host (no GPU
+ * needed for host data); tensor bytes move between the file and HBM through
+ * two pinned staging buffers per file, so reading chunk i+1 from the file
+ * overlaps the copy of chunk i.  A quantized weight is stored as
+ * <name>.qweight (I8 for INT8, U8 for INT4) [K, bytesPerRow], <name>.scales
+ * F32 [G, N] and, INT4 only, <name>.zeros U8 [G, N]. */
+typedef struct kt_stfile kt_stfile;
+
+typedef struct {
+    char dtype[8];     /* "F32", "BF16", "U8", ... NUL-terminated */
+    int32_t rank;      /* number of dimensions, at most 8 */
+    int64_t shape[8];
+    int64_t offset;    /* first byte, counted from the start of the data section */
+    int64_t bytes;
+} kt_st_entry_info;
+
+/* SafeTensorsFile(file) (SafeTensors.kt:33-69): opens and parses the header;
+ * KT_ERR_IO if the file cannot be read, KT_ERR_INVALID_ARGUMENT for a header
+ * the reference rejects (length outside 1..100 MiB, not a JSON object, a
+ * tensor without dtype or data_offsets, a data range past the end of file). */
+kt_status kt_st_open(const char* path, kt_stfile** out);
+/* close(): waits for copies in flight from or to this file's staging buffers. */
+kt_status kt_st_close(kt_stfile* f);
+/* names (header order) and entry(name); kt_st_entry fails for a missing name. */
+int32_t kt_st_tensor_count(const kt_stfile* f);
+const char* kt_st_tensor_name(const kt_stfile* f, int32_t index);  /* NULL when out of range */
+kt_status kt_st_entry(const kt_stfile* f, const char* name, kt_st_entry_info* out);
+/* metadata, in header order; the strings live until kt_st_close. */
+int32_t kt_st_metadata_count(const kt_stfile* f);
+kt_status kt_st_metadata_at(const kt_stfile* f, int32_t index, const char** key, const char** value);
+/* readRaw(name, dest) (SafeTensors.kt:90-98): the tensor's bytes into host
+ * memory of `capacity` bytes.  Synchronous. */
+kt_status kt_st_read_raw(kt_stfile* f, const char* name, void* dst_host, int64_t capacity);
+/* The tensor's bytes straight into device memory of `capacity` bytes, ordered
+ * on `stream` (the host returns once the last chunk is queued). */
+kt_status kt_st_read_raw_device(kt_ctx* ctx, kt_stfile* f, const char* name, void* dst_dev, int64_t capacity,
+                                void* stream);
+/* readInto(name, dest) (SafeTensors.kt:86-88, :110-170): the tensor as float32
+ * into device memory of `capacity` floats, converted on the GPU from F32, F16,
+ * BF16, F64, I8, U8, BOOL, I16, I32 or I64 with the reference's rounding
+ * (round to nearest even for F64, I32 and I64; the others are exact). */
+kt_status kt_st_read_f32_device(kt_ctx* ctx, kt_stfile* f, const char* name, float* dst_dev, int64_t capacity,
+                                void* stream);
+/* QuantizedTensor.mapFrom(reader, name) (QuantizedTensor.kt:109-126) into HBM:
+ * a new device weight of the given quantization and shape from <name>.qweight,
+ * <name>.scales and (INT4) <name>.zeros, with the reference's size checks. */
+kt_status kt_qweight_load(kt_ctx* ctx, kt_stfile* f, const char* name, int32_t bits, int32_t group_size,
+                          int32_t rows, int32_t columns, void* stream, kt_qweight** out);
+
+/* One tensor to write: `data` is host memory, or device memory when on_device != 0. */
+typedef struct {
+    const char* name;
+    const char* dtype;
+    int32_t rank;
+    const int64_t* shape;
+    const void* data;
+    int64_t bytes;
+    int32_t on_device;
+} kt_st_tensor;
+/* SafeTensors.saveEntries(file, entries, metadata) (SafeTensors.kt:220-249):
+ * the same bytes as the reference writes (header key order, JSON escaping,
+ * space padding, data in entry order).  Device tensors are copied out on
+ * `stream` through the staging buffers; ctx may be NULL when every tensor is
+ * host memory.  Synchronous. */
+kt_status kt_st_write(kt_ctx* ctx, const char* path, const kt_st_tensor* tensors, int32_t count,
+                      const char* const* meta_keys, const char* const* meta_values, int32_t meta_count,
+                      void* stream);
 
 #ifdef __cplusplus
 }

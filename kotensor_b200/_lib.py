@@ -19,6 +19,7 @@ KT_ERR_CUDA = 3
 KT_ERR_OUT_OF_MEMORY = 4
 KT_ERR_UNSUPPORTED = 5
 KT_ERR_NCCL = 6
+KT_ERR_IO = 7
 
 KT_PATH_GEMV, KT_PATH_GENERIC, KT_PATH_TENSOR_CORE, KT_PATH_GEMV_MMA = 0, 1, 2, 3
 
@@ -29,6 +30,21 @@ class KtError(RuntimeError):
     def __init__(self, status: int, message: str):
         super().__init__(f"[kt status {status}] {message}")
         self.status = status
+
+
+class KtStEntryInfo(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_char * 8), ("rank", ctypes.c_int32), ("shape", ctypes.c_int64 * 8),
+        ("offset", ctypes.c_int64), ("bytes", ctypes.c_int64),
+    ]
+
+
+class KtStTensor(ctypes.Structure):
+    _fields_ = [
+        ("name", ctypes.c_char_p), ("dtype", ctypes.c_char_p), ("rank", ctypes.c_int32),
+        ("shape", ctypes.POINTER(ctypes.c_int64)), ("data", ctypes.c_void_p), ("bytes", ctypes.c_int64),
+        ("on_device", ctypes.c_int32),
+    ]
 
 
 class KtInfo(ctypes.Structure):
@@ -92,6 +108,20 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_argmax": ([P, P, I32, I32, P, P], I32),
     "kt_dequantize_column": ([P, P, P, I32, P, P, P], I32),
     "kt_increment": ([P, P, I32, P], I32),
+    "kt_qweight_slice": ([P, P, I32, I32, I32, P, PP], I32),
+    "kt_st_open": ([ctypes.c_char_p, PP], I32),
+    "kt_st_close": ([P], I32),
+    "kt_st_tensor_count": ([P], I32),
+    "kt_st_tensor_name": ([P, I32], ctypes.c_char_p),
+    "kt_st_entry": ([P, ctypes.c_char_p, ctypes.POINTER(KtStEntryInfo)], I32),
+    "kt_st_metadata_count": ([P], I32),
+    "kt_st_metadata_at": ([P, I32, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_char_p)], I32),
+    "kt_st_read_raw": ([P, ctypes.c_char_p, P, I64], I32),
+    "kt_st_read_raw_device": ([P, P, ctypes.c_char_p, P, I64, P], I32),
+    "kt_st_read_f32_device": ([P, P, ctypes.c_char_p, P, I64, P], I32),
+    "kt_qweight_load": ([P, P, ctypes.c_char_p, I32, I32, I32, I32, P, PP], I32),
+    "kt_st_write": ([P, ctypes.c_char_p, ctypes.POINTER(KtStTensor), I32, ctypes.POINTER(ctypes.c_char_p),
+                     ctypes.POINTER(ctypes.c_char_p), I32, P], I32),
 }
 
 _lib = None
@@ -123,4 +153,6 @@ def check(status: int) -> None:
     msg = load().kt_last_error().decode(errors="replace")
     if status in (KT_ERR_INVALID_ARGUMENT, KT_ERR_NAN):
         raise ValueError(msg)  # IllegalArgumentException
+    if status == KT_ERR_IO:
+        raise OSError(msg)  # IOException
     raise KtError(status, msg)  # IllegalStateException

@@ -519,18 +519,21 @@ kt_status kt_shard_bounds(int32_t axis, int32_t extent, int32_t group_size, int3
     return KT_OK;
 }
 
-kt_status kt_qweight_shard(kt_ctx* ctx, const kt_qweight* w, int32_t axis, int32_t parts, int32_t index,
-                           void* stream, kt_qweight** out) {
+kt_status kt_qweight_slice(kt_ctx* ctx, const kt_qweight* w, int32_t axis, int32_t b, int32_t e, void* stream,
+                           kt_qweight** out) {
     if (!ctx || !w || !out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     *out = nullptr;
-    int32_t b = 0, e = 0;
+    if (axis != 0 && axis != 1) return fail(KT_ERR_INVALID_ARGUMENT, "axis must be 0 (rows) or 1 (columns)");
     const int32_t extent = axis == 0 ? w->rows : w->columns;
-    kt_status st = kt_shard_bounds(axis, extent, w->group_size, parts, index, &b, &e);
-    if (st != KT_OK) return st;
+    if (b < 0 || e > extent || e <= b)
+        return fail(KT_ERR_INVALID_ARGUMENT, "slice [" + std::to_string(b) + ", " + std::to_string(e) +
+                                                 ") outside [0, " + std::to_string(extent) + ")");
+    if (axis == 0 && (b % w->group_size != 0 || (e % w->group_size != 0 && e != w->rows)))
+        return fail(KT_ERR_INVALID_ARGUMENT, "a row slice must start and end on group boundaries");
     kt_qweight* d = nullptr;
-    if ((st = alloc_weight(ctx, w->bits, w->group_size, axis == 0 ? e - b : w->rows, axis == 0 ? w->columns : e - b,
-                           &d)) != KT_OK)
-        return st;
+    kt_status st = alloc_weight(ctx, w->bits, w->group_size, axis == 0 ? e - b : w->rows,
+                                axis == 0 ? w->columns : e - b, &d);
+    if (st != KT_OK) return st;
     cudaStream_t s = pick(ctx, stream);
     cudaError_t err = cudaSuccess;
     if (axis == 0) {
@@ -559,9 +562,62 @@ kt_status kt_qweight_shard(kt_ctx* ctx, const kt_qweight* w, int32_t axis, int32
     }
     if (err != cudaSuccess) {
         free_weight(d);
-        return cuda_fail(err, "kt_qweight_shard");
+        return cuda_fail(err, "kt_qweight_slice");
     }
     *out = d;
+    return KT_OK;
+}
+
+kt_status kt_qweight_shard(kt_ctx* ctx, const kt_qweight* w, int32_t axis, int32_t parts, int32_t index,
+                           void* stream, kt_qweight** out) {
+    if (!ctx || !w || !out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    int32_t b = 0, e = 0;
+    const int32_t extent = axis == 0 ? w->rows : w->columns;
+    kt_status st = kt_shard_bounds(axis, extent, w->group_size, parts, index, &b, &e);
+    if (st != KT_OK) return st;
+    return kt_qweight_slice(ctx, w, axis, b, e, stream, out);
+}
+
+kt_status kt_qweight_load(kt_ctx* ctx, kt_stfile* f, const char* name, int32_t bits, int32_t group_size,
+                          int32_t rows, int32_t columns, void* stream, kt_qweight** out) {
+    if (!ctx || !f || !name || !out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    kt_status st = check_quant(bits, group_size);
+    if (st != KT_OK) return st;
+    if ((st = check_shape(rows, columns)) != KT_OK) return st;
+    // QuantizedTensor.mapFrom's checks (QuantizedTensor.kt:109-116), with its messages
+    const std::string base(name);
+    const int64_t groups = groups_of(rows, group_size);
+    const int64_t qbytes = static_cast<int64_t>(rows) * bytes_per_row_of(bits, columns);
+    const int64_t gcols = groups * columns;
+    kt_st_entry_info qi{}, si{}, zi{};
+    if ((st = kt_st_entry(f, (base + ".qweight").c_str(), &qi)) != KT_OK) return st;
+    if (qi.bytes != qbytes)
+        return fail(KT_ERR_INVALID_ARGUMENT, base + ".qweight has " + std::to_string(qi.bytes) + " bytes, expected " +
+                                                 std::to_string(qbytes));
+    if ((st = kt_st_entry(f, (base + ".scales").c_str(), &si)) != KT_OK) return st;
+    if (std::strcmp(si.dtype, "F32") != 0 || si.bytes != gcols * 4)
+        return fail(KT_ERR_INVALID_ARGUMENT, base + ".scales is " + si.dtype + " with " + std::to_string(si.bytes) +
+                                                 " bytes, expected F32 with " + std::to_string(gcols * 4));
+    if (bits == 4) {
+        if ((st = kt_st_entry(f, (base + ".zeros").c_str(), &zi)) != KT_OK) return st;
+        if (zi.bytes != gcols)
+            return fail(KT_ERR_INVALID_ARGUMENT, base + ".zeros has " + std::to_string(zi.bytes) + " bytes, expected " +
+                                                     std::to_string(gcols));
+    }
+    kt_qweight* w = nullptr;
+    if ((st = alloc_weight(ctx, bits, group_size, rows, columns, &w)) != KT_OK) return st;
+    st = kt_st_read_raw_device(ctx, f, (base + ".qweight").c_str(), w->qdata, qbytes, stream);
+    if (st == KT_OK) st = kt_st_read_raw_device(ctx, f, (base + ".scales").c_str(), w->scales, gcols * 4, stream);
+    if (st == KT_OK && bits == 4) st = kt_st_read_raw_device(ctx, f, (base + ".zeros").c_str(), w->zeros, gcols, stream);
+    if (st != KT_OK) {
+        // copies already queued read the staging buffers into this weight: let them finish first
+        cudaStreamSynchronize(pick(ctx, stream));
+        free_weight(w);
+        return st;
+    }
+    *out = w;
     return KT_OK;
 }
 

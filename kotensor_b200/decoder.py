@@ -97,7 +97,9 @@ class DeviceDecoder:
         f32 = dict(dtype=torch.float32, device=dev)
 
         def vec(a):
-            return torch.as_tensor(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
+            if isinstance(a, torch.Tensor):
+                return a.detach().to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+            return torch.as_tensor(np.ascontiguousarray(a, dtype=np.float32).reshape(-1)).to(dev)
 
         from .parallel import concat_columns
         self.layers = []
@@ -290,3 +292,140 @@ class DeviceDecoder:
             self.length += 1
             out.append(int(self.next_token.item()))
         return out
+
+    # -- files (Transformer.saveQuantized / loadQuantized, Transformer.kt:402-471)
+    def save_quantized(self, path) -> None:
+        """Transformer.saveQuantized: the reference's file, byte for byte, written
+        from HBM (q|k|v and gate|up are split back into their projections)."""
+        from .parallel import COLUMNS, slice_weight
+        from .safetensors import SafeTensorsEntry, quantized_entries, save_entries
+        cfg = self.cfg
+        kv = cfg.kv_heads * cfg.head_dim
+        meta = quantized_metadata(cfg)
+        entries, keep = [], []
+
+        def f32(name, t, n):
+            entries.append(SafeTensorsEntry(name, "F32", [1, n], t.contiguous()))
+
+        for l, L in enumerate(self.layers):
+            f32(f"block.{l}.norm1.weight", L["norm1"], cfg.dim)
+            f32(f"block.{l}.norm2.weight", L["norm2"], cfg.dim)
+        f32("finalNorm.weight", self.final_norm, cfg.dim)
+        q_cols = [(0, cfg.dim), (cfg.dim, cfg.dim + kv), (cfg.dim + kv, cfg.dim + 2 * kv)]
+        g_cols = [(0, cfg.hidden), (cfg.hidden, 2 * cfg.hidden)]
+        projections = []
+        for l, L in enumerate(self.layers):
+            parts = {}
+            for key, (b, e) in zip(("wq", "wk", "wv"), q_cols):
+                parts[key] = (slice_weight(L["wqkv"], COLUMNS, b, e), L["bqkv"][b:e])
+            parts["wo"] = (L["wo"], L["bo"])
+            for key, (b, e) in zip(("wg", "wu"), g_cols):
+                parts[key] = (slice_weight(L["wgu"], COLUMNS, b, e), L["bgu"][b:e])
+            parts["wd"] = (L["wd"], L["bd"])
+            for suffix, key in PROJECTION_NAMES:
+                projections.append((f"block.{l}.{suffix}",) + parts[key])
+        projections.append(("lmHead", self.head, self.head_bias))
+        for name, w, b in projections:
+            f32(f"{name}.bias", b, w.columns)
+        quantized = ([] if cfg.tied else [("embedding", self.embedding)]) + [(n, w) for n, w, _ in projections]
+        for name, w in quantized:
+            entries += quantized_entries(name, w)
+            keep.append(w)  # the slices stay alive until the file is written
+        save_entries(path, entries, meta)
+
+    @staticmethod
+    def load_quantized(path, max_seq: int, device: Optional[int] = None) -> "DeviceDecoder":
+        """Transformer.loadQuantized: a decoder whose weights go from the file
+        straight into HBM."""
+        cfg, weights = load_quantized_weights(path, device)
+        return DeviceDecoder(cfg, weights, max_seq, device)
+
+
+# (file name suffix, decoder weight key) in Transformer.namedProjections order (Transformer.kt:268-282)
+PROJECTION_NAMES = [("attention.wQ", "wq"), ("attention.wK", "wk"), ("attention.wV", "wv"),
+                    ("attention.wOut", "wo"), ("ffn.wGate", "wg"), ("ffn.wUp", "wu"), ("ffn.wDown", "wd")]
+
+
+def quantized_metadata(cfg: DecoderConfig) -> dict:
+    """The kotensor.* metadata of Transformer.saveQuantized (Transformer.kt:403-419)."""
+    from .safetensors import java_float_string as js
+    meta = {
+        "kotensor.vocabularySize": str(cfg.vocab),
+        "kotensor.dimension": str(cfg.dim),
+        "kotensor.numLayers": str(cfg.layers),
+        "kotensor.numHeads": str(cfg.heads),
+        "kotensor.hiddenDimension": str(cfg.hidden),
+        "kotensor.numKeyValueHeads": str(cfg.kv_heads),
+        "kotensor.normEps": js(cfg.eps),
+        "kotensor.ropeTheta": js(cfg.rope_theta),
+    }
+    if cfg.rope_scaling is not None:
+        f, lo, hi, orig = cfg.rope_scaling
+        meta["kotensor.ropeScaling"] = f"{js(f)},{js(lo)},{js(hi)},{int(orig)}"
+    meta["kotensor.quantization.bits"] = str(cfg.bits)
+    meta["kotensor.quantization.groupSize"] = str(cfg.group_size)
+    if cfg.tied:
+        meta["kotensor.tiedEmbedding"] = "true"
+    return meta
+
+
+class LoadedWeights:
+    """Device weights read from a file, in DeviceDecoder's ``weights`` shape."""
+
+    def __init__(self):
+        self.embedding = None
+        self.layers = []
+        self.final_norm = None
+        self.head = None
+        self.head_bias = None
+
+
+def load_quantized_weights(path, device: Optional[int] = None):
+    """(config, weights) of a file written by Transformer.saveQuantized
+    (Transformer.loadQuantized, Transformer.kt:433-471), weights in HBM."""
+    from .quantized import Quantization
+    from .safetensors import SafeTensorsFile
+    with SafeTensorsFile(path) as f:
+        meta = f.metadata
+
+        def value(key):
+            if key not in meta:
+                raise ValueError(f"{path} has no {key} metadata; was it written by saveQuantized?")
+            return meta[key]
+
+        scaling = None
+        if "kotensor.ropeScaling" in meta:
+            p = meta["kotensor.ropeScaling"].split(",")
+            scaling = (float(np.float32(p[0])), float(np.float32(p[1])), float(np.float32(p[2])), int(p[3]))
+        q = Quantization(int(value("kotensor.quantization.bits")), int(value("kotensor.quantization.groupSize")))
+        cfg = DecoderConfig(vocab=int(value("kotensor.vocabularySize")), dim=int(value("kotensor.dimension")),
+                            layers=int(value("kotensor.numLayers")), heads=int(value("kotensor.numHeads")),
+                            kv_heads=int(value("kotensor.numKeyValueHeads")),
+                            hidden=int(value("kotensor.hiddenDimension")),
+                            eps=float(np.float32(value("kotensor.normEps"))),
+                            rope_theta=float(np.float32(value("kotensor.ropeTheta"))), rope_scaling=scaling,
+                            bits=q.bits, group_size=q.group_size, tied=meta.get("kotensor.tiedEmbedding") == "true")
+        kv = cfg.kv_heads * cfg.head_dim
+        shapes = {"wq": (cfg.dim, cfg.dim), "wk": (cfg.dim, kv), "wv": (cfg.dim, kv), "wo": (cfg.dim, cfg.dim),
+                  "wg": (cfg.dim, cfg.hidden), "wu": (cfg.dim, cfg.hidden), "wd": (cfg.hidden, cfg.dim)}
+
+        def param(name):
+            if name not in f:
+                raise ValueError(f"{path} is missing {name}")
+            return f.load(name, device).reshape(-1)
+
+        w = LoadedWeights()
+        for l in range(cfg.layers):
+            L = {"norm1": param(f"block.{l}.norm1.weight"), "norm2": param(f"block.{l}.norm2.weight")}
+            for suffix, key in PROJECTION_NAMES:
+                name = f"block.{l}.{suffix}"
+                L["b" + key[1]] = param(f"{name}.bias")
+                L[key] = f.load_quantized(name, q, *shapes[key], device=device)
+            w.layers.append(L)
+        w.final_norm = param("finalNorm.weight")
+        w.head_bias = param("lmHead.bias")
+        w.head = f.load_quantized("lmHead", q, cfg.dim, cfg.vocab, device=device)
+        if not cfg.tied:
+            w.embedding = f.load_quantized("embedding", q, cfg.vocab, cfg.dim, device=device)
+        torch.cuda.current_stream(w.head.device).synchronize()  # the file's staging buffers are released on close
+    return cfg, w

@@ -83,6 +83,17 @@ def shard(qt: QuantizedTensor, axis: int, parts: int, index: int) -> QuantizedTe
     return QuantizedTensor(h, qt._ctx)
 
 
+def slice_weight(qt: QuantizedTensor, axis: int, begin: int, end: int) -> QuantizedTensor:
+    """Device weight of rows (axis 0, group-aligned) or columns (axis 1) [begin, end)
+    of ``qt`` (kt_qweight_slice), built on torch's current stream."""
+    import torch
+    h = ctypes.c_void_p()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(qt.device).cuda_stream)
+    _lib.check(_lib.load().kt_qweight_slice(qt._ctx.handle, qt.handle, axis, int(begin), int(end), stream,
+                                            ctypes.byref(h)))
+    return QuantizedTensor(h, qt._ctx)
+
+
 def concat_columns(weights: list) -> QuantizedTensor:
     """One weight whose columns are those of ``weights`` side by side
     (kt_qweight_concat_columns; e.g. q|k|v or gate|up fused into one matmul)."""
