@@ -295,6 +295,47 @@ kt_status kt_dequantize_column(kt_ctx* ctx, const kt_qweight* w, const int32_t* 
 /* *value_dev += delta on `stream` (advances a captured step's position). */
 kt_status kt_increment(kt_ctx* ctx, int32_t* value_dev, int32_t delta, void* stream);
 
+/* ------------------------------------------------------------ LoRA adapters over a quantized base
+ * LoRALinear (LoRA.kt:7-57) with a QuantizedLinear base: lora_a fp32 [K x rank],
+ * lora_b fp32 [rank x N], scaling = alpha / rank, all row-major on the device;
+ * 1 <= rank <= 256. */
+/* projected[m x rank] = a[m x K] . lora_a (the low-rank projection of forwardInto). */
+kt_status kt_lora_project(kt_ctx* ctx, const float* a_dev, int32_t m, int32_t k, const float* lora_a, int32_t rank,
+                          float* projected_dev, void* stream);
+/* LoRALinear.forwardInto (LoRA.kt:39-46): projected = a . A, then
+ * c = (accumulate ? c : 0) + alpha * a . deq(W) + bias + scaling * projected . B,
+ * the low-rank term added in the quantized matmul's own epilogue (no extra pass
+ * over c).  `projected` [m x rank] is kept for the backward. */
+kt_status kt_lora_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float* c_dev, int32_t m,
+                          int32_t accumulate, float alpha, const float* bias_dev, const float* lora_a,
+                          const float* lora_b, int32_t rank, float scaling, float* projected_dev, void* stream);
+/* Gradients of LoRALinear.forward (LoRA.kt:31-36 through the autograd of
+ * matmulDequant, Tensor.kt:171-177, and of its two matmuls).  With
+ * G = dy . B^T [m x rank]:
+ *   dx = (accumulate_dx ? dx : 0) + dy . deq(W)^T + scaling * G . A^T   (dx NULL: skipped)
+ *   grad_a += scaling * a^T . G         [K x rank]                        (NULL: skipped)
+ *   grad_b += scaling * projected^T . dy [rank x N]                       (NULL: skipped)
+ * The base weight gets no gradient (frozen, LoRAAdapter, LoRA.kt:86-91). */
+kt_status kt_lora_backward(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, const float* dy_dev,
+                           const float* projected_dev, const float* lora_a, const float* lora_b, int32_t rank,
+                           float scaling, int32_t m, float* dx_dev, int32_t accumulate_dx, float* grad_a,
+                           float* grad_b, void* stream);
+
+/* fusedCrossEntropyLoss(hidden, head, targets, ignoreIndex) with a QuantizedLinear
+ * head (Loss.kt:114-220): head = W [dim x vocab] with bias_dev [vocab] (NULL:
+ * zero), hidden_dev fp32 [rows x dim], targets_host int32 [rows] in host
+ * memory (ignore_index marks rows without a target; a target outside
+ * 0..vocab-1 fails with the reference's message).  *loss_dev = mean over the
+ * active rows of max + ln(sum exp) - logit[target] (0 with no active row, and
+ * then no gradients).  With upstream gradient 1: hidden_grad_dev (NULL:
+ * skipped) += the rows' gradients through the head (ignored rows untouched),
+ * bias_grad_dev (NULL: skipped) += the column sums of the logit gradients.
+ * Rows are processed in chunks of at most 2^26 logits; the logits come from
+ * the same matmul paths as kt_qmatmul. */
+kt_status kt_fused_cross_entropy(kt_ctx* ctx, const kt_qweight* head, const float* bias_dev, const float* hidden_dev,
+                                 int32_t rows, const int32_t* targets_host, int32_t ignore_index, float* loss_dev,
+                                 float* hidden_grad_dev, float* bias_grad_dev, void* stream);
+
 /* ------------------------------------------------------------ safetensors files
  * The reference's model files (SafeTensors.kt:12-249, written by
  * Transformer.saveQuantized, Transformer.kt:402-431): an 8-byte little-endian

@@ -109,6 +109,10 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_dequantize_column": ([P, P, P, I32, P, P, P], I32),
     "kt_increment": ([P, P, I32, P], I32),
     "kt_qweight_slice": ([P, P, I32, I32, I32, P, PP], I32),
+    "kt_lora_project": ([P, P, I32, I32, P, I32, P, P], I32),
+    "kt_lora_qmatmul": ([P, P, P, P, I32, I32, F32, P, P, P, I32, F32, P, P], I32),
+    "kt_lora_backward": ([P, P, P, P, P, P, P, I32, F32, I32, P, I32, P, P, P], I32),
+    "kt_fused_cross_entropy": ([P, P, P, P, I32, P, I32, P, P, P, P], I32),
     "kt_st_open": ([ctypes.c_char_p, PP], I32),
     "kt_st_close": ([P], I32),
     "kt_st_tensor_count": ([P], I32),

@@ -154,9 +154,10 @@ kt_status grow(float** buf, size_t* cap, size_t need) {
 }
 
 kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
-                     float alpha, const float* bias, cudaStream_t s) {
+                     float alpha, const float* bias, cudaStream_t s, const LoraEpilogue* lora = nullptr) {
     const QView v = view(w);
-    const MatmulArgs args{a, c, bias, m, accumulate, alpha, ctx->d_error};
+    MatmulArgs args{a, c, bias, m, accumulate, alpha, ctx->d_error};
+    if (lora) args.lora = *lora;
     cudaError_t e;
     if (gemv_mma_supported(v, m, a)) {
         const size_t need = gemv_mma_workspace_bytes(v, m, ctx->sm_count);
@@ -256,8 +257,8 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType type, uint32_t elem_by
 }
 
 kt_status run_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
-                      float alpha, const float* bias, cudaStream_t s) {
-    return run_matmul(ctx, w, a, c, m, accumulate, alpha, bias, s);
+                      float alpha, const float* bias, cudaStream_t s, const LoraEpilogue* lora) {
+    return run_matmul(ctx, w, a, c, m, accumulate, alpha, bias, s, lora);
 }
 
 }  // namespace kt
@@ -715,6 +716,152 @@ kt_status kt_qmatmul_t(kt_ctx* ctx, const kt_qweight* w, const float* dy, float*
     void* ws = nullptr;
     if (need > 0) KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "qmatmul_t workspace");
     KT_CUDA_TRY(launch_matmul_t(v, dy, dx, m, accumulate, s, ws, need), "qmatmul_t launch");
+    return KT_OK;
+}
+
+// ---- LoRALinear over a quantized base (kt_lora.cu)
+
+namespace {
+kt_status check_lora(int32_t m, int32_t k, int32_t rank, const float* lora_a) {
+    if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
+    if (k <= 0) return fail(KT_ERR_INVALID_ARGUMENT, "in-features must be positive");
+    if (rank < 1 || rank > kLoraMaxRank)
+        return fail(KT_ERR_INVALID_ARGUMENT, "LoRA rank must be in 1.." + std::to_string(kLoraMaxRank) + ", got " +
+                                                 std::to_string(rank));
+    if (!lora_a) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    return KT_OK;
+}
+}  // namespace
+
+kt_status kt_lora_project(kt_ctx* ctx, const float* a, int32_t m, int32_t k, const float* lora_a, int32_t rank,
+                          float* projected, void* stream) {
+    if (!ctx) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    kt_status st = check_lora(m, k, rank, lora_a);
+    if (st != KT_OK || m == 0) return st;
+    if (!a || !projected) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    const cudaStream_t s = pick(ctx, stream);
+    void* ws = nullptr;
+    KT_CUDA_TRY(stream_workspace(ctx, s, lora_workspace_bytes(m, k, 1, rank), &ws), "lora workspace");
+    KT_CUDA_TRY(launch_lora_project(a, m, k, lora_a, rank, projected, ws, s), "lora project launch");
+    return KT_OK;
+}
+
+kt_status kt_lora_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
+                          float alpha, const float* bias, const float* lora_a, const float* lora_b, int32_t rank,
+                          float scaling, float* projected, void* stream) {
+    if (!ctx || !w) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    kt_status st = check_lora(m, w->rows, rank, lora_a);
+    if (st != KT_OK || m == 0) return st;
+    if (!a || !c || !lora_b || !projected) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if ((st = kt_lora_project(ctx, a, m, w->rows, lora_a, rank, projected, stream)) != KT_OK) return st;
+    LoraEpilogue lora;
+    lora.p = projected;
+    lora.b = lora_b;
+    lora.rank = rank;
+    lora.scale = scaling;
+    return run_matmul(ctx, w, a, c, m, accumulate, alpha, bias, pick(ctx, stream), &lora);
+}
+
+kt_status kt_lora_backward(kt_ctx* ctx, const kt_qweight* w, const float* a, const float* dy, const float* projected,
+                           const float* lora_a, const float* lora_b, int32_t rank, float scaling, int32_t m, float* dx,
+                           int32_t accumulate_dx, float* grad_a, float* grad_b, void* stream) {
+    if (!ctx || !w) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    kt_status st = check_lora(m, w->rows, rank, lora_a);
+    if (st != KT_OK || m == 0) return st;
+    if (!dy || !lora_b || (grad_a && !a) || (grad_b && !projected))
+        return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    const cudaStream_t s = pick(ctx, stream);
+    if (dx && (st = kt_qmatmul_t(ctx, w, dy, dx, m, accumulate_dx, stream)) != KT_OK) return st;
+    if (!dx && !grad_a && !grad_b) return KT_OK;
+    void* ws = nullptr;
+    KT_CUDA_TRY(stream_workspace(ctx, s, lora_workspace_bytes(m, w->rows, w->columns, rank), &ws), "lora workspace");
+    KT_CUDA_TRY(launch_lora_backward(a, dy, projected, lora_a, lora_b, m, w->rows, w->columns, rank, scaling, dx,
+                                     grad_a, grad_b, ws, s),
+                "lora backward launch");
+    return KT_OK;
+}
+
+// ---- fusedCrossEntropyLoss with a quantized head (kt_loss.cu)
+
+kt_status kt_fused_cross_entropy(kt_ctx* ctx, const kt_qweight* head, const float* bias, const float* hidden,
+                                 int32_t rows, const int32_t* targets, int32_t ignore_index, float* loss,
+                                 float* hidden_grad, float* bias_grad, void* stream) {
+    if (!ctx || !head || !hidden || !targets || !loss) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (rows <= 0) return fail(KT_ERR_INVALID_ARGUMENT, "targets cannot be empty");
+    const int32_t vocab = head->columns, dim = head->rows;
+    std::vector<int32_t> active_rows, active_targets;
+    for (int32_t i = 0; i < rows; ++i) {
+        if (targets[i] == ignore_index) continue;
+        if (targets[i] < 0 || targets[i] >= vocab)
+            return fail(KT_ERR_INVALID_ARGUMENT,
+                        "target " + std::to_string(targets[i]) + " out of bounds " + std::to_string(vocab));
+        active_rows.push_back(i);
+        active_targets.push_back(targets[i]);
+    }
+    const cudaStream_t s = pick(ctx, stream);
+    KT_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const int32_t active = static_cast<int32_t>(active_rows.size());
+    if (active == 0) {  // emptyLoss(): 0, no gradients
+        KT_CUDA_TRY(cudaMemsetAsync(loss, 0, sizeof(float), s), "loss");
+        return KT_OK;
+    }
+    const int32_t chunk = loss_chunk_rows(vocab, active);
+    const bool grads = hidden_grad != nullptr || bias_grad != nullptr;
+    int32_t* d_rows = nullptr;
+    int32_t* d_targets = nullptr;
+    float *stats = nullptr, *inputs = nullptr, *logits = nullptr, *chunk_grad = nullptr;
+    auto release = [&] {
+        cudaFreeAsync(d_rows, s);
+        cudaFreeAsync(d_targets, s);
+        cudaFreeAsync(stats, s);
+        cudaFreeAsync(inputs, s);
+        cudaFreeAsync(logits, s);
+        if (chunk_grad) cudaFreeAsync(chunk_grad, s);
+    };
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&d_rows), active * sizeof(int32_t), s);
+    if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&d_targets), active * sizeof(int32_t), s);
+    if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&stats), 3 * static_cast<size_t>(active) * 4, s);
+    if (e == cudaSuccess)
+        e = cudaMallocAsync(reinterpret_cast<void**>(&inputs), static_cast<size_t>(chunk) * dim * sizeof(float), s);
+    if (e == cudaSuccess)
+        e = cudaMallocAsync(reinterpret_cast<void**>(&logits), static_cast<size_t>(chunk) * vocab * sizeof(float), s);
+    if (e == cudaSuccess && hidden_grad)
+        e = cudaMallocAsync(reinterpret_cast<void**>(&chunk_grad), static_cast<size_t>(chunk) * dim * sizeof(float), s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(d_rows, active_rows.data(), active * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(d_targets, active_targets.data(), active * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // the host vectors go out of scope with this call
+    if (e != cudaSuccess) {
+        release();
+        return cuda_fail(e, "fused cross entropy setup");
+    }
+    float* row_max = stats;
+    float* row_sum = stats + active;
+    float* row_loss = stats + 2 * static_cast<size_t>(active);
+    const float scale = 1.0f / static_cast<float>(active);
+    kt_status st = KT_OK;
+    for (int32_t start = 0; start < active && st == KT_OK; start += chunk) {
+        const int32_t count = std::min(chunk, active - start);
+        e = launch_gather_rows(hidden, d_rows + start, count, dim, inputs, s);
+        if (e != cudaSuccess) break;
+        if ((st = run_matmul(ctx, head, inputs, logits, count, 0, 1.0f, bias, s)) != KT_OK) break;
+        e = launch_loss_rows(logits, count, vocab, d_targets + start, row_max + start, row_sum + start,
+                             row_loss + start, s);
+        if (e != cudaSuccess) break;
+        if (!grads) continue;
+        e = launch_loss_grads(logits, count, vocab, d_targets + start, row_max + start, row_sum + start, scale,
+                              bias_grad, s);
+        if (e != cudaSuccess) break;
+        if (!hidden_grad) continue;
+        if ((st = kt_qmatmul_t(ctx, head, logits, chunk_grad, count, 0, s)) != KT_OK) break;
+        e = launch_scatter_add_rows(chunk_grad, d_rows + start, count, dim, hidden_grad, s);
+        if (e != cudaSuccess) break;
+    }
+    if (st == KT_OK && e == cudaSuccess) e = launch_mean_loss(row_loss, active, loss, s);
+    release();
+    if (st != KT_OK) return st;
+    if (e != cudaSuccess) return cuda_fail(e, "fused cross entropy");
     return KT_OK;
 }
 

@@ -78,6 +78,7 @@ struct GemmParams {
     uint32_t idesc;    // instruction descriptor of the MMA
     float alpha;
     int32_t accumulate;
+    LoraEpilogue lora;
     // split-K (gridDim.z > 1): partial tiles and per-tile arrival counters
     float* partials;   // [tile][split][nt][256]
     int32_t* tickets;  // [tile], zero between launches
@@ -406,6 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float* out = p.y + static_cast<int64_t>(tok) * p.N + oc;
             float r = fmaf(p.alpha, v, p.accumulate ? *out : 0.0f);
             if (p.bias != nullptr) r += p.bias[oc];
+            if (p.lora.p != nullptr) r += lora_term(p.lora, tok, oc, p.N);
             *out = r;
         };
         const int S = gridDim.z;
@@ -546,6 +548,7 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
               (static_cast<uint32_t>(128 >> 4) << 24);
     p.alpha = a.alpha;
     p.accumulate = a.accumulate;
+    p.lora = a.lora;
     const int S = splits_for(w, a.m, sm_count);
     p.tickets = reinterpret_cast<int32_t*>(ws + kGemmTicketOffset);
     p.partials = reinterpret_cast<float*>(ws + kWorkspaceReservedBytes + x_bytes(w, a.m));

@@ -73,6 +73,7 @@ struct GemvParams {
     uint32_t magic;      // 0x4B000000, the float 2^23
     float alpha;
     int32_t accumulate;
+    LoraEpilogue lora;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -441,6 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float* out = p.y + static_cast<int64_t>(m) * p.N + col;
             float r = fmaf(p.alpha, v, p.accumulate ? *out : 0.0f);
             if (p.bias != nullptr) r += p.bias[col];
+            if (p.lora.p != nullptr) r += lora_term(p.lora, m, col, p.N);
             *out = r;
         }
     }
@@ -501,6 +503,7 @@ __global__ void __launch_bounds__(256) matmul_generic_kernel(GemvParams p) {
             float* out = p.y + static_cast<int64_t>(m) * p.N + col;
             float r = fmaf(p.alpha, v, p.accumulate ? *out : 0.0f);
             if (p.bias != nullptr) r += p.bias[col];
+            if (p.lora.p != nullptr) r += lora_term(p.lora, m, col, p.N);
             *out = r;
         }
     }
@@ -628,6 +631,7 @@ GemvParams make_params(const QView& w, const MatmulArgs& a) {
     p.magic = 0x4B000000u;
     p.alpha = a.alpha;
     p.accumulate = a.accumulate;
+    p.lora = a.lora;
     return p;
 }
 

@@ -114,6 +114,7 @@ struct MmaParams {
     uint32_t h1024;        // 0x64006400: f16x2 {1024, 1024}
     float alpha;
     int32_t accumulate;
+    LoraEpilogue lora;
     // split-K (gridDim.y > 1): per-CTA partial tiles and per-tile arrival
     // counters (zero on entry, left zero on exit)
     float* partials;       // [tiles][splits][M][256]
@@ -536,6 +537,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             float* out = p.y + static_cast<int64_t>(m) * p.N + out_col;
             float r = fmaf(p.alpha, v, p.accumulate ? *out : 0.0f);
             if (p.bias != nullptr) r += p.bias[out_col];
+            if (p.lora.p != nullptr) r += lora_term(p.lora, m, out_col, p.N);
             *out = r;
         }
     };
@@ -696,6 +698,7 @@ cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, c
     p.h1024 = 0x64006400u;
     p.alpha = a.alpha;
     p.accumulate = a.accumulate;
+    p.lora = a.lora;
     const int splits = choose_splits(p.R, p.K, a.m, sm_count);
     if (splits > 1) {
         if (workspace == nullptr || workspace_bytes < gemv_mma_workspace_bytes(w, a.m, sm_count))

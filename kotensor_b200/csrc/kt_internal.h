@@ -84,18 +84,38 @@ inline QView view(const kt_qweight* w) {
                  w->has_tmap_raw64 ? &w->tmap_raw64 : nullptr};
 }
 
+// The low-rank term of LoRALinear.forwardInto (LoRA.kt:39-46) applied in a
+// matmul's epilogue: c[t][j] += scale * sum_r p[t][r] * b[r][j], with
+// p = a . A ([m x rank], computed before the matmul) and b = B ([rank x N]).
+struct LoraEpilogue {
+    const float* p = nullptr;  // NULL: no LoRA term
+    const float* b = nullptr;
+    int32_t rank = 0;
+    float scale = 0.0f;
+};
+#ifdef __CUDACC__
+__device__ __forceinline__ float lora_term(const LoraEpilogue& l, int t, int col, int n) {
+    const float* pr = l.p + static_cast<int64_t>(t) * l.rank;
+    const float* bc = l.b + col;
+    float s = 0.0f;
+    for (int r = 0; r < l.rank; ++r) s = fmaf(__ldg(pr + r), __ldg(bc + static_cast<int64_t>(r) * n), s);
+    return l.scale * s;
+}
+#endif
+
 // The dispatch behind kt_qmatmul (kt_api.cu): argument-checked by the caller.
 kt_status run_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
-                      float alpha, const float* bias, cudaStream_t s);
+                      float alpha, const float* bias, cudaStream_t s, const LoraEpilogue* lora = nullptr);
 
 // Zero-initialised device workspace of at least `bytes` for launches on stream
 // `s` (kt_api.cu).  Its first kWorkspaceReservedBytes hold the split-K arrival
 // counters of the INT4 GEMV and of the INT4 GEMM at fixed offsets (zero
 // between launches, whatever shapes ran before); kernels use the rest freely.
 cudaError_t stream_workspace(kt_ctx* ctx, cudaStream_t s, size_t bytes, void** out);
-constexpr size_t kWorkspaceReservedBytes = static_cast<size_t>(64) << 10;
+constexpr size_t kWorkspaceReservedBytes = static_cast<size_t>(96) << 10;
 constexpr size_t kGemvTicketOffset = 0;
 constexpr size_t kGemmTicketOffset = static_cast<size_t>(32) << 10;
+constexpr size_t kLoraTicketOffset = static_cast<size_t>(64) << 10;
 constexpr int kTicketCapEach = 8192;  // counters per kernel family
 
 // A 2-D tiled TMA descriptor (kt_api.cu): `inner` x `outer` elements of
@@ -108,6 +128,28 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType type, uint32_t elem_by
 constexpr int kStageRows = 8;
 // Builds kt_qweight::tmap_w128 / tmap_w256 (kt_api.cu).
 bool make_tensor_maps(kt_qweight* w);
+
+// ---- kt_lora.cu  (LoRALinear over a quantized base; rank 1..kLoraMaxRank)
+constexpr int kLoraMaxRank = 256;
+size_t lora_workspace_bytes(int32_t m, int32_t K, int32_t N, int32_t rank);
+cudaError_t launch_lora_project(const float* a, int32_t m, int32_t K, const float* A, int32_t rank, float* p,
+                                void* workspace, cudaStream_t s);
+cudaError_t launch_lora_backward(const float* a, const float* dy, const float* p, const float* A, const float* B,
+                                 int32_t m, int32_t K, int32_t N, int32_t rank, float scale, float* dx, float* dA,
+                                 float* dB, void* workspace, cudaStream_t s);
+
+// ---- kt_loss.cu  (fusedCrossEntropyLoss with a quantized head)
+int32_t loss_chunk_rows(int32_t vocab, int32_t active);
+cudaError_t launch_gather_rows(const float* src, const int32_t* rows, int32_t count, int32_t dim, float* dst,
+                               cudaStream_t s);
+cudaError_t launch_loss_rows(const float* logits, int32_t count, int32_t vocab, const int32_t* targets,
+                             float* row_max, float* row_sum, float* row_loss, cudaStream_t s);
+cudaError_t launch_loss_grads(float* logits, int32_t count, int32_t vocab, const int32_t* targets,
+                              const float* row_max, const float* row_sum, float scale, float* bias_grad,
+                              cudaStream_t s);
+cudaError_t launch_scatter_add_rows(const float* src, const int32_t* rows, int32_t count, int32_t dim, float* dst,
+                                    cudaStream_t s);
+cudaError_t launch_mean_loss(const float* row_loss, int32_t active, float* out, cudaStream_t s);
 
 // ---- kt_quantize.cu
 cudaError_t launch_quantize(const float* data, int32_t rows, int32_t columns, int32_t bits, int32_t group_size,
@@ -125,6 +167,7 @@ struct MatmulArgs {
     int32_t accumulate;
     float alpha;
     int32_t* err;  // context error word (bounded-wait timeouts)
+    LoraEpilogue lora;
 };
 // Largest m the fp32-accumulate streaming kernel takes.
 constexpr int kGemvMaxM = 8;
