@@ -159,7 +159,15 @@ kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c,
     MatmulArgs args{a, c, bias, m, accumulate, alpha, ctx->d_error};
     if (lora) args.lora = *lora;
     cudaError_t e;
-    if (gemv_mma_supported(v, m, a)) {
+    if (gemv_imma_supported(v, m, a)) {
+        const size_t need = gemv_imma_workspace_bytes(v, ctx->sm_count);
+        void* ws = nullptr;
+        if (need > 0) {
+            e = stream_workspace(ctx, s, need, &ws);
+            if (e != cudaSuccess) return cuda_fail(e, "qmatmul workspace");
+        }
+        e = launch_gemv_imma(v, args, ctx->sm_count, s, ws, need);
+    } else if (gemv_mma_supported(v, m, a)) {
         const size_t need = gemv_mma_workspace_bytes(v, m, ctx->sm_count);
         void* ws = nullptr;
         if (need > 0) {
@@ -651,7 +659,7 @@ kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out) {
     if (!w || !path_out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
     const QView v = view(w);
-    *path_out = gemv_mma_supported(v, m, nullptr)    ? KT_PATH_GEMV_MMA
+    *path_out = gemv_imma_supported(v, m, nullptr) || gemv_mma_supported(v, m, nullptr) ? KT_PATH_GEMV_MMA
                 : gemv_fast_supported(v, m, nullptr) ? KT_PATH_GEMV
                 : gemm_tc_supported(v, m, nullptr)   ? KT_PATH_TENSOR_CORE
                                                      : KT_PATH_GENERIC;
@@ -665,6 +673,7 @@ kt_status kt_set_gemv_tuning(int32_t lane_bytes, int32_t cluster_k) {
 
 kt_status kt_set_gemv_mma_tuning(int32_t k_splits) {
     set_mma_tuning(k_splits);
+    set_imma_tuning(k_splits);
     return KT_OK;
 }
 

@@ -1,0 +1,510 @@
+// kt_gemv_imma.cu -- INT4 decode GEMV for one token (m = 1) on integer
+// tensor-core products: MatMul.multiplyQuantized (Engine/kotensor/src/main/
+// kotlin/MatMul.kt:460-536, :599-828) for m = 1, the decode step's shape.
+//
+// Operands.  mma.sync.m16n8k32 u8 x s8 -> s32.  The reduction index k of one
+// MMA is split as k = 4 rho + sigma: rho (0..7) is one of 8 weight rows,
+// sigma (0..3) a byte position inside a 32-bit word of that row.  MMA row g
+// (0..7) is one word column of the tile row and row g + 8 the same word's high
+// nibbles, so every A register is a weight word as it lies in shared memory,
+// masked: w & 0x0F0F0F0F (low nibbles, q) or w & 0xF0F0F0F0 (high nibbles,
+// 16 q).  No byte shuffling: two AND per word per row.  B row 4 rho + sigma,
+// column n carries the activation part (n / 4: 0 = high, 1 = low byte) of row
+// rho when sigma == n % 4 and 0 otherwise, so D[g][n] is the dot product of
+// the rows with column "byte n % 4 of word g" -- 32 columns x 8 rows x 2
+// nibbles per MMA, every output lane of the MMA useful.
+//
+// Exactness.  x is scaled by a power of two 2^sh per slice (max|x 2^sh| in
+// [2^13, 2^14)), rounded to an integer X (15-bit magnitude) and split
+// X = 256 xh + xl with xh, xl signed bytes; the products are exact integers in
+// s32.  Per group (combineGroup, MatMul.kt:804-828), with SX the group's sum
+// of X over this warp's rows and D = 256 D_hi + D_lo:
+//     low nibble:  y += scale * (D - zero * SX)
+//     high nibble: y += scale * (D / 16 - zero * SX)
+// and y is multiplied by 2^-sh once at the end.  The products are exact, so
+// the only rounding besides fp32 accumulation is x's 15-bit quantization
+// (relative to the slice's max|x|).
+//
+// Tiling and streaming are those of the fp16 kernel (kt_gemv_mma.cu): a CTA
+// owns 128 packed bytes of every row (256 output columns); 4 pairs of warps
+// own consecutive K-slices; each pair streams its slice through a ring of
+// 32-row x 128-byte TMA stages (128-byte swizzle) plus bulk copies of each
+// group's scales and zero points, with bounded mbarrier waits; inside a stage
+// warp 0 of the pair takes 8-row blocks 0 and 2, warp 1 blocks 1 and 3.  K is
+// split over CTAs when the column tiles alone cannot fill the GPU; the last
+// CTA of a tile sums the split partials in split order (deterministic).
+#include <algorithm>
+#include <cstdlib>
+
+#include "kt_device.cuh"
+#include "kt_internal.h"
+
+namespace kt {
+namespace {
+
+using namespace dev;
+
+constexpr int kPairs = 4;
+constexpr int kWarps = 2 * kPairs;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRowsPerStage = 32;       // TMA box height (QView::tmap_mma)
+constexpr int kBlockRows = 8;           // weight rows per MMA
+constexpr int kTileBytes = 128;
+constexpr int kStages = 4;
+constexpr int kMaxSliceRows = 1024;     // rows of x one slice stages
+
+constexpr int kStageBytes = kRowsPerStage * kTileBytes;               // 4096
+constexpr int kScaleSlotBytes = 2 * kTileBytes * 4 + 2 * kTileBytes;  // 1280: s_lo, s_hi, z_lo, z_hi
+constexpr int kRingBytes = kStages * kStageBytes;
+constexpr int kSlotRingBytes = kStages * kScaleSlotBytes;
+constexpr int kMainBytes = kPairs * kRingBytes;
+constexpr int kCT = 2 * kTileBytes;                                   // 256 output columns per tile
+constexpr int kRedBytes = kWarps * 8 * 32 * 4;                        // reuses the rings
+constexpr int kXsBytes = kMaxSliceRows * 2;                           // [row]{xh, xl}
+constexpr int kSxBytes = kMaxSliceRows / kBlockRows * 4;              // [block] sum of X
+constexpr int kXsPairBytes = kXsBytes + kSxBytes;
+constexpr size_t kSmemBytes = static_cast<size_t>(kMainBytes) + kPairs * kSlotRingBytes +
+                              kPairs * kXsPairBytes + kPairs * kStages * 16;
+static_assert(kRedBytes <= kMainBytes, "reduction buffer must fit in the rings");
+static_assert(kXsPairBytes % 16 == 0, "slice staging areas stay 16-byte aligned");
+static_assert(2 * (kSmemBytes + 1024) <= 233472, "two CTAs per SM");
+
+struct ImmaParams {
+    const float* scales;
+    const uint8_t* zeros;
+    const float* x;
+    float* y;
+    const float* bias;
+    int32_t* err;
+    int32_t K, N, R, gs;
+    float alpha;
+    int32_t accumulate;
+    LoraEpilogue lora;
+    float* partials;   // split-K: [tiles][splits][256]
+    int32_t* tickets;  // [tiles], zero on entry and on exit
+};
+
+__device__ __forceinline__ void imma_16832(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void pair_barrier(int pair) {
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
+}
+
+// Shared memory: rings[4 slices][NS][32][128] (later red[8][8][32]) |
+// slots[4][NS][1280] | x staging[4][kXsPairBytes] | mbarriers[4][2][NS].
+__global__ void __launch_bounds__(kThreads, 2)
+    gemv_imma_kernel(const __grid_constant__ CUtensorMap tmap, ImmaParams p) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int pair = warp >> 1;
+    const int hw = warp & 1;
+    const int g = lane >> 2;  // word column of the tile row (A rows g, g + 8); B column n = g
+    const int t = lane & 3;   // rows 2t, 2t+1 of an 8-row block; C columns 2t, 2t+1
+    const int tile_b0 = blockIdx.x * kTileBytes;
+    const int tile_cols = min(kTileBytes, p.R - tile_b0);
+    const int half = p.R;
+
+    const int n_slices = gridDim.y * kPairs;
+    const int slice = blockIdx.y * kPairs + pair;
+    const int k_stages = p.K / kRowsPerStage;
+    const int s_begin = static_cast<int>(static_cast<int64_t>(slice) * k_stages / n_slices);
+    const int s_end = static_cast<int>(static_cast<int64_t>(slice + 1) * k_stages / n_slices);
+    const int r_begin = s_begin * kRowsPerStage;
+    const int r_end = s_end * kRowsPerStage;
+    const int n_stages = s_end - s_begin;
+
+    unsigned char* ring = smem + pair * kRingBytes;
+    unsigned char* slots = smem + kMainBytes + pair * kSlotRingBytes;
+    unsigned char* xstage = smem + kMainBytes + kPairs * kSlotRingBytes + pair * kXsPairBytes;
+    uint8_t* xs = xstage;                                                   // [row]{xh, xl}
+    int32_t* sxb = reinterpret_cast<int32_t*>(xstage + kXsBytes);           // [block] sum of X
+    const uint32_t bars =
+        smem_u32(smem + kMainBytes + kPairs * kSlotRingBytes + kPairs * kXsPairBytes) +
+        pair * kStages * 16;
+    const uint32_t empty = bars + kStages * 8;
+    const uint32_t ring_s = smem_u32(ring);
+    const uint32_t slots_s = smem_u32(slots);
+    const int g_first = r_begin / p.gs;
+    const bool producer = hw == 0 && lane == 0;
+
+    if (producer) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(bars + 8 * s, 1);
+            mbar_init(empty + 8 * s, 2);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    // Stage st: rows [r_begin + 32 st, +32) into ring slot st % NS; a stage that
+    // starts a group also brings the group's scales and zero points into group
+    // slot (group - g_first) % NS (lanes 1-4 of warp 0; the arming arrive of
+    // lane 0 is still pending, so their complete_tx cannot finish the phase).
+    int p_row = r_begin, p_gi = g_first, p_gstart = r_begin, p_issued = 0;
+    const uint32_t sbytes = static_cast<uint32_t>(tile_cols) * 10;
+    const uint32_t lane_off = lane <= 2 ? (lane - 1) * kTileBytes * 4 : kTileBytes * (5 + lane);
+    const uint32_t lane_bytes = lane <= 2 ? tile_cols * 4 : tile_cols;
+    const unsigned char* lane_src =
+        lane <= 2 ? reinterpret_cast<const unsigned char*>(p.scales + tile_b0 + (lane == 2 ? half : 0))
+                  : p.zeros + tile_b0 + (lane == 4 ? half : 0);
+    const int lane_esize = lane <= 2 ? 4 : 1;
+    auto issue = [&](int st) {
+        const int slot = st & (kStages - 1);
+        const uint32_t bar = bars + 8 * slot;
+        const bool group_start = p_row == p_gstart;
+        if (lane == 0) {
+            mbar_expect_tx(bar, kStageBytes + (group_start ? sbytes : 0));
+            tma_load_2d(ring_s + slot * kStageBytes, &tmap, tile_b0, p_row, bar);
+        }
+        if (group_start) {
+            if (lane >= 1 && lane <= 4) {
+                const uint32_t dst = slots_s + ((p_gi - g_first) & (kStages - 1)) * kScaleSlotBytes + lane_off;
+                bulk_load(dst, lane_src + static_cast<int64_t>(p_gi) * p.N * lane_esize, lane_bytes, bar);
+            }
+            ++p_gi;
+            p_gstart = p_gi * p.gs;
+        }
+        p_row += kRowsPerStage;
+        ++p_issued;
+    };
+    if (hw == 0) {
+        for (int s = 0; s < kStages && s < n_stages; ++s) issue(s);  // the whole ring, before the wait
+    }
+    pair_barrier(pair);  // the mbarriers are initialised before warp 1 waits on them
+    pdl_launch_dependents();
+    pdl_wait();  // x and y below may belong to the previous kernel
+
+    // ---- stage x for this warp's rows, the 8-row blocks hw, hw + 2, ... of the
+    // slice: float4 f of the warp is rows 8 (2 (f / 2) + hw) + 4 (f % 2) .. + 3.
+    // Each warp picks its own power of two 2^sh (max|x 2^sh| in [2^13, 2^14)),
+    // so X fits 15 bits and xh = (X + 128) >> 8 stays in [-64, 64]; the warp's
+    // results are unscaled before the warps are summed.
+    const int n_rows = r_end - r_begin;
+    const int n_f4 = n_rows / 8;  // <= 128: four per lane
+    float4 xv[4];
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int f = lane + 32 * i;
+        const int row = 8 * (2 * (f >> 1) + hw) + 4 * (f & 1);
+        xv[i] = f < n_f4 ? __ldg(reinterpret_cast<const float4*>(p.x + r_begin + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xv[i].x), fabsf(xv[i].y)), fmaxf(fabsf(xv[i].z), fabsf(xv[i].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    int sh = mx > 0.0f ? 13 - ilogbf(mx) : 0;
+    sh = max(-126, min(126, sh));
+    const float sc = ldexpf(1.0f, sh);
+    const float unscale = ldexpf(1.0f, -sh);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int f = lane + 32 * i;
+        const int row = 8 * (2 * (f >> 1) + hw) + 4 * (f & 1);
+        const float v[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+        int X[4];
+        uint32_t packed_lo = 0, packed_hi = 0;  // {xh, xl} of rows row, row+1 | row+2, row+3
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            X[k] = __float2int_rn(v[k] * sc);
+            const int xh = (X[k] + 128) >> 8;
+            const int xl = X[k] - (xh << 8);
+            const uint32_t pr = (static_cast<uint32_t>(xh) & 0xFFu) | ((static_cast<uint32_t>(xl) & 0xFFu) << 8);
+            if (k < 2) packed_lo |= pr << (16 * k);
+            else packed_hi |= pr << (16 * (k - 2));
+        }
+        const int s4 = X[0] + X[1] + X[2] + X[3];
+        const int s8 = s4 + __shfl_xor_sync(0xffffffffu, s4, 1);  // the block's 8 rows (lanes f, f ^ 1)
+        if (f < n_f4) {
+            *reinterpret_cast<uint2*>(xs + 2 * row) = make_uint2(packed_lo, packed_hi);
+            if ((f & 1) == 0) sxb[row / kBlockRows] = s8;
+        }
+    }
+    __syncwarp();  // staged x visible to the warp (each warp reads only its own rows)
+
+    // B fragments: column n = g carries part g / 4 (0 = xh, 1 = xl) in byte g % 4.
+    // From the word {xh, xl}(row 2t), {xh, xl}(row 2t+1) of a block:
+    // b0 = that part of row 2t in byte g % 4, b1 the same of row 2t+1.
+    const uint32_t part_byte = static_cast<uint32_t>(g >> 2);
+    const uint32_t pos = static_cast<uint32_t>(g & 3);
+    uint32_t sel0 = 0x4444u, sel1 = 0x4444u;  // selector nibbles >= 4 pick the zero operand
+    sel0 = (sel0 & ~(0xFu << (4 * pos))) | (part_byte << (4 * pos));
+    sel1 = (sel1 & ~(0xFu << (4 * pos))) | ((2u + part_byte) << (4 * pos));
+    // this lane's 16-byte chunk (words 4g .. 4g+3) of rows 2t and 2t+1 of a block, swizzled
+    // (16-byte chunk c of row r sits at chunk c ^ (r & 7)); blocks start on multiples of 8 rows
+    const int off0 = (2 * t) * kTileBytes + ((g ^ (2 * t)) << 4);
+    const int off1 = (2 * t + 1) * kTileBytes + ((g ^ (2 * t + 1)) << 4);
+
+    // Epilogue columns of this lane: words 4g + j (j = 0..3), bytes 2u, 2u + 1 of
+    // each (u = t & 1); low nibbles for t < 2, high nibbles for t >= 2.
+    const int u = t & 1;
+    const bool low_owner = t < 2;
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = 0.0f;
+    int c[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0;
+    int sx = 0;  // this warp's sum of X over the group's rows so far
+    bool ok = true;
+    int done = 0;
+    int gi = g_first;
+    int group_end = min((gi + 1) * p.gs, r_end);
+    for (int st = 0; st < n_stages; ++st) {
+        const int slot = st & (kStages - 1);
+        if (ok) {
+            if (mbar_wait_bounded(bars + 8 * slot, (st / kStages) & 1)) {
+                done = st + 1;
+            } else {
+                ok = false;
+                atomicOr(p.err, 1);
+            }
+            ok = __all_sync(0xffffffffu, ok);
+        }
+        if (hw == 0 && st > 0 && st + kStages - 1 < n_stages) {
+            // stage st + NS - 1 into the slot of stage st - 1 once both warps released it
+            const int prev = st - 1;
+            int go = 0;
+            if (lane == 0 && ok)
+                go = mbar_wait_bounded(empty + 8 * (prev & (kStages - 1)), (prev / kStages) & 1) ? 1 : 2;
+            go = __shfl_sync(0xffffffffu, go, 0);
+            if (go == 2) {
+                ok = false;
+                if (lane == 0) atomicOr(p.err, 1);
+            } else if (go == 1) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue(st + kStages - 1);
+            }
+        }
+        const unsigned char* stage = ring + slot * kStageBytes;
+#pragma unroll
+        for (int bb = 0; bb < 2; ++bb) {
+            const int blk = 2 * bb + hw;                  // 8-row block of the stage
+            const int brow = st * kRowsPerStage + blk * kBlockRows;  // inside the slice
+            const uint32_t xw = *reinterpret_cast<const uint32_t*>(xs + 2 * (brow + 2 * t));
+            const uint32_t b0 = prmt(xw, 0u, sel0), b1 = prmt(xw, 0u, sel1);
+            const uint4 w0 = *reinterpret_cast<const uint4*>(stage + blk * kBlockRows * kTileBytes + off0);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(stage + blk * kBlockRows * kTileBytes + off1);
+            sx += sxb[brow / kBlockRows];
+            imma_16832(c[0], w0.x & 0x0F0F0F0Fu, w0.x & 0xF0F0F0F0u, w1.x & 0x0F0F0F0Fu, w1.x & 0xF0F0F0F0u, b0, b1);
+            imma_16832(c[1], w0.y & 0x0F0F0F0Fu, w0.y & 0xF0F0F0F0u, w1.y & 0x0F0F0F0Fu, w1.y & 0xF0F0F0F0u, b0, b1);
+            imma_16832(c[2], w0.z & 0x0F0F0F0Fu, w0.z & 0xF0F0F0F0u, w1.z & 0x0F0F0F0Fu, w1.z & 0xF0F0F0F0u, b0, b1);
+            imma_16832(c[3], w0.w & 0x0F0F0F0Fu, w0.w & 0xF0F0F0F0u, w1.w & 0x0F0F0F0Fu, w1.w & 0xF0F0F0F0u, b0, b1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + 8 * slot);
+        if (r_begin + (st + 1) * kRowsPerStage >= group_end) {
+            // Group epilogue.  C of lane (g, t): c[j][0..1] = D[g][2t..2t+1] (low
+            // nibbles, byte 2u + 0/1, part t / 2), c[j][2..3] the high nibbles.
+            // Lanes t and t ^ 2 hold the two parts of the same bytes.
+            const unsigned char* sl = slots + ((gi - g_first) & (kStages - 1)) * kScaleSlotBytes;
+            const float* s_arr = reinterpret_cast<const float*>(sl + (low_owner ? 0 : kTileBytes * 4));
+            const uint8_t* z_arr = sl + kTileBytes * (low_owner ? 8 : 9);
+            const float sxf = static_cast<float>(sx);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int send0 = low_owner ? c[j][2] : c[j][0];
+                const int send1 = low_owner ? c[j][3] : c[j][1];
+                const int recv0 = __shfl_xor_sync(0xffffffffu, send0, 2);
+                const int recv1 = __shfl_xor_sync(0xffffffffu, send1, 2);
+                // D = 256 D_hi + D_lo in fp32 (no int32 overflow for any group size)
+                const float d0 = low_owner ? fmaf(static_cast<float>(c[j][0]), 256.0f, static_cast<float>(recv0))
+                                           : fmaf(static_cast<float>(recv0), 256.0f, static_cast<float>(c[j][2]));
+                const float d1 = low_owner ? fmaf(static_cast<float>(c[j][1]), 256.0f, static_cast<float>(recv1))
+                                           : fmaf(static_cast<float>(recv1), 256.0f, static_cast<float>(c[j][3]));
+                const int b = 16 * g + 4 * j + 2 * u;  // byte of the tile row
+                const float2 s2 = *reinterpret_cast<const float2*>(s_arr + b);
+                const uint32_t z2 = *reinterpret_cast<const uint16_t*>(z_arr + b);
+                const float k16 = low_owner ? 1.0f : 0.0625f;
+                y[2 * j] = fmaf(s2.x, fmaf(d0, k16, -static_cast<float>(z2 & 0xFFu) * sxf), y[2 * j]);
+                y[2 * j + 1] = fmaf(s2.y, fmaf(d1, k16, -static_cast<float>(z2 >> 8) * sxf), y[2 * j + 1]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0;
+            sx = 0;
+            ++gi;
+            group_end = min((gi + 1) * p.gs, r_end);
+        }
+    }
+    // After a timeout: wait (bounded) for this slice's copies still in flight
+    // before the rings are reused and the CTA's shared memory is released.
+    if (producer) {
+        for (int s = done; s < p_issued; ++s) {
+            if (!mbar_wait_bounded(bars + 8 * (s & (kStages - 1)), (s / kStages) & 1)) break;
+        }
+    }
+
+    // (1) warps of the CTA in order; red[w][e][lane] reuses the rings.
+    __shared__ int s_last;
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(smem);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) red[(warp * 8 + e) * 32 + lane] = y[e] * unscale;
+    __syncthreads();
+    // column col = tid: byte b = col % 128 of the tile row, high nibble if
+    // col >= 128; its lane (g, t) and register e as assigned above
+    float v = 0.0f;
+    {
+        const int b = tid & (kTileBytes - 1);
+        const int hi = tid >> 7;
+        const int gg = b >> 4, j = (b >> 2) & 3, sg = b & 3;
+        const int ln = 4 * gg + 2 * hi + (sg >> 1);
+        const int e = 2 * j + (sg & 1);
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) v += red[(w * 8 + e) * 32 + ln];
+    }
+    auto emit = [&](int col, float val) {
+        const int byte = tile_b0 + (col & (kTileBytes - 1));
+        const int out_col = col < kTileBytes ? byte : half + byte;
+        if (byte < p.R && out_col < p.N) {
+            float* out = p.y + out_col;
+            float r = fmaf(p.alpha, val, p.accumulate ? *out : 0.0f);
+            if (p.bias != nullptr) r += p.bias[out_col];
+            if (p.lora.p != nullptr) r += lora_term(p.lora, 0, out_col, p.N);
+            *out = r;
+        }
+    };
+    const int S = gridDim.y;
+    if (S == 1) {
+        emit(tid, v);
+        return;
+    }
+    // (2) split-K: every CTA of the tile publishes its partial tile; the last to
+    // arrive sums all of them in split order (the CTA barrier orders every
+    // thread's store before thread 0's acq_rel atomic; the second barrier hands
+    // the acquire to the whole CTA).
+    float* tile_parts = p.partials + static_cast<int64_t>(blockIdx.x) * S * kCT;
+    __stcg(tile_parts + static_cast<int64_t>(blockIdx.y) * kCT + tid, v);
+    __syncthreads();
+    if (tid == 0) s_last = atomic_add_acq_rel(p.tickets + blockIdx.x, 1) == S - 1;
+    __syncthreads();
+    if (!s_last) return;
+    // up to 32 partial loads in flight per thread, summed in split order
+    float sum = 0.0f;
+    for (int s0 = 0; s0 < S; s0 += 32) {
+        float tv[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            tv[j] = s0 + j == static_cast<int>(blockIdx.y) ? v
+                    : s0 + j < S ? __ldcg(tile_parts + static_cast<int64_t>(s0 + j) * kCT + tid) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (s0 + j < S) sum += tv[j];
+    }
+    emit(tid, sum);
+    if (tid == 0) p.tickets[blockIdx.x] = 0;  // ready for the next launch on this workspace
+}
+
+int tiles_of(int R) { return (R + kTileBytes - 1) / kTileBytes; }
+
+int blocks_per_sm() {
+    constexpr int kMaxDevices = 64;
+    static int cache[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int* slot = dev >= 0 && dev < kMaxDevices ? &cache[dev] : nullptr;
+    if (slot != nullptr && *slot != 0) return *slot;
+    int n = 0;
+    if (cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_imma_kernel, kThreads, kSmemBytes) != cudaSuccess)
+        n = 1;
+    cudaGetLastError();
+    n = std::max(n, 1);
+    if (slot != nullptr) *slot = n;
+    return n;
+}
+
+int min_splits(int K) {
+    const int per = kPairs * kMaxSliceRows;
+    return (K + per - 1) / per;
+}
+
+int& split_override() {
+    static int o = [] {
+        const char* v = std::getenv("KT_IMMA_SPLITS");
+        return v ? std::atoi(v) : 0;
+    }();
+    return o;
+}
+
+// K-splits per column tile: enough CTAs to fill the SM slots of one wave, at
+// most kMaxSplits (each split adds a partial the finishing CTA must read and a
+// CTA's fixed costs; measured on B200, more than 16 splits of a tile never paid
+// off), at least one stage per slice, never fewer than min_splits.
+constexpr int kMaxSplits = 16;
+int choose_splits(int R, int K, int sm_count) {
+    const int tiles = tiles_of(R);
+    const int slots = blocks_per_sm() * sm_count;
+    const int k_stages = K / kRowsPerStage;
+    int s = std::min(kMaxSplits, std::max(1, slots / tiles));
+    s = std::min(s, std::max(1, k_stages / kPairs));
+    if (split_override() >= 1) s = split_override();
+    s = std::max(s, min_splits(K));
+    return tiles > kTicketCapEach ? min_splits(K) : s;
+}
+
+}  // namespace
+
+void set_imma_tuning(int k_splits) { split_override() = k_splits; }
+
+bool gemv_imma_supported(const QView& w, int32_t m, const float* a) {
+    if (w.bits != 4 || m != 1 || w.tmap_mma == nullptr) return false;
+    if (a != nullptr && reinterpret_cast<uintptr_t>(a) % 16 != 0) return false;
+    return w.columns % 32 == 0 && w.rows % kRowsPerStage == 0 && w.group_size % kRowsPerStage == 0 &&
+           min_splits(w.rows) <= 65535 &&
+           (min_splits(w.rows) == 1 || tiles_of(w.bytes_per_row) <= kTicketCapEach);
+}
+
+size_t gemv_imma_workspace_bytes(const QView& w, int sm_count) {
+    const int splits = choose_splits(w.bytes_per_row, w.rows, sm_count);
+    if (splits <= 1) return 0;
+    return kWorkspaceReservedBytes + static_cast<size_t>(tiles_of(w.bytes_per_row)) * splits * kCT * sizeof(float);
+}
+
+cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s, void* workspace,
+                             size_t workspace_bytes) {
+    ImmaParams p{};
+    p.scales = w.scales;
+    p.zeros = w.zeros;
+    p.x = a.a;
+    p.y = a.c;
+    p.bias = a.bias;
+    p.err = a.err;
+    p.K = w.rows;
+    p.N = w.columns;
+    p.R = w.bytes_per_row;
+    p.gs = w.group_size;
+    p.alpha = a.alpha;
+    p.accumulate = a.accumulate;
+    p.lora = a.lora;
+    const int splits = choose_splits(p.R, p.K, sm_count);
+    if (splits > 1) {
+        if (workspace == nullptr || workspace_bytes < gemv_imma_workspace_bytes(w, sm_count))
+            return cudaErrorInvalidValue;
+        p.tickets = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) + kGemvTicketOffset);
+        p.partials = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kWorkspaceReservedBytes);
+    }
+    const cudaError_t e = cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(tiles_of(p.R), splits, 1);
+    lc.blockDim = dim3(kThreads, 1, 1);
+    lc.dynamicSmemBytes = kSmemBytes;
+    lc.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, gemv_imma_kernel, *w.tmap_mma, p);
+}
+
+}  // namespace kt

@@ -188,6 +188,14 @@ size_t gemv_mma_workspace_bytes(const QView& w, int32_t m, int sm_count);
 cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s, void* workspace,
                             size_t workspace_bytes);
 
+// ---- kt_gemv_imma.cu  (INT4, m = 1: integer tensor-core products, fp32 group combine)
+bool gemv_imma_supported(const QView& w, int32_t m, const float* a);
+void set_imma_tuning(int k_splits);
+size_t gemv_imma_workspace_bytes(const QView& w, int sm_count);
+cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s, void* workspace,
+                             size_t workspace_bytes);
+
+
 // ---- kt_gemm_tc.cu  (INT4, m >= 9: bf16 tcgen05 MMAs, TMEM accumulators)
 bool gemm_tc_supported(const QView& w, int32_t m, const float* a);
 size_t gemm_tc_workspace_bytes(const QView& w, int32_t m, int sm_count);

@@ -70,7 +70,14 @@ extern "C" kt_status kt_qmatmul_noalloc(kt_ctx* ctx, const kt_qweight* w, const 
     const QView v = view(w);
     const MatmulArgs args{a, c, bias, m, accumulate, alpha, ctx->d_error};
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (gemv_mma_supported(v, m, a)) {
+    if (gemv_imma_supported(v, m, a)) {
+        const size_t need = gemv_imma_workspace_bytes(v, ctx->sm_count);
+        if (need > kStaticWorkspaceBytes)
+            return fail_noalloc(KT_ERR_INVALID_ARGUMENT,
+                                "this shape needs " + std::to_string(need) + " bytes of workspace; the static workspace holds " +
+                                    std::to_string(kStaticWorkspaceBytes) + " (use kt_qmatmul)");
+        e = launch_gemv_imma(v, args, ctx->sm_count, s, need > 0 ? ws : nullptr, kStaticWorkspaceBytes);
+    } else if (gemv_mma_supported(v, m, a)) {
         const size_t need = gemv_mma_workspace_bytes(v, m, ctx->sm_count);
         if (need > kStaticWorkspaceBytes)
             return fail_noalloc(KT_ERR_INVALID_ARGUMENT,
