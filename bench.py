@@ -45,9 +45,9 @@ UNIT = "GB/s"
 SHAPES = [(2048, 5632), (5632, 2048), (4096, 14336), (14336, 4096)]  # (K = in, N = out)
 BITS, GROUP = 4, 64
 L2_BYTES = 126 * 1024 * 1024
-# DRAM bytes / algorithmic bytes of one gemv_mma_kernel<1> launch on the
-# 4096 x 14336 shape, from `ncu --set full` (profiles/gemv_mma_int4_m1_4096x14336.md).
-NCU_TRAFFIC_RATIO = 34004224 / 34021376
+# DRAM bytes / algorithmic bytes of one gemv_imma_kernel launch on the
+# 4096 x 14336 shape, from `ncu --set full` (profiles/gemv_imma_int4_m1_4096x14336.md).
+NCU_TRAFFIC_RATIO = 34011648 / 34021376
 WORKLOAD = "config2-int4-ffn-gemv-m1"
 
 
@@ -447,9 +447,9 @@ def run_ours(args) -> None:
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": round(NCU_TRAFFIC_RATIO * (step_bytes // len(SHAPES))),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
-                                       f"gemv_mma_kernel<1> launch (4096 x 14336): {NCU_TRAFFIC_RATIO:.4f} x "
+                                       f"gemv_imma_kernel launch (4096 x 14336): {NCU_TRAFFIC_RATIO:.4f} x "
                                        "its algorithmic bytes, applied to the average launch",
-                     "kernel": "gemv_mma_kernel<1>",
+                     "kernel": "gemv_imma_kernel",
                      "bytes_per_launch_avg": step_bytes // len(SHAPES), "launch_us_avg": round(launch_us, 3)},
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                 "h2d_bytes_per_step": sum(args.m * k * 4 for k, _ in SHAPES),
