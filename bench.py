@@ -207,10 +207,9 @@ QWEN2_05B = dict(vocab=151936, dim=896, layers=24, heads=14, kv_heads=2, hidden=
                  rope_theta=1000000.0, bits=4, group_size=64, tied=True, qkv_bias=True)
 
 
-def measure_decode(kt, torch, steps: int, prompt_len: int, seed: int) -> dict:
-    """Prefill and greedy decode of the Qwen2-0.5B-shaped INT4 model (random N(0, 0.02^2)
-    weights quantized on the device, tied embeddings, q/k/v biases), batch 1: the
-    prompt as one block (Transformer.prefill), then timed CUDA-graph decode steps."""
+def decode_weights(kt, torch, seed: int):
+    """The Qwen2-0.5B-shaped INT4 model (random N(0, 0.02^2) weights quantized on
+    the device, tied embeddings, q/k/v biases)."""
     import numpy as np
     from types import SimpleNamespace
     from kotensor_b200 import decoder as D
@@ -240,14 +239,24 @@ def measure_decode(kt, torch, steps: int, prompt_len: int, seed: int) -> dict:
     head = proj(cfg.dim, cfg.vocab)
     weights = SimpleNamespace(embedding=None, layers=layers, final_norm=np.ones(cfg.dim, np.float32), head=head,
                               head_bias=np.zeros(cfg.vocab, np.float32))
-    dec = D.DeviceDecoder(cfg, weights, max_seq=2 * prompt_len + steps + 8)
-    prompt = rng.integers(0, cfg.vocab, size=prompt_len).tolist()
-    dec.prefill(prompt)  # warm-up prefill (module set-up, workspaces), then a timed one
+    return cfg, weights
+
+
+def measure_decode(kt, torch, cfg, weights, batch: int, steps: int, prompt_len: int, seed: int) -> dict:
+    """Batched greedy decode: `batch` random prompts prefilled as blocks
+    (Transformer.prefill, all sequences in one pass), then timed CUDA-graph decode
+    steps of the whole batch (every matmul at m = batch)."""
+    import numpy as np
+    from kotensor_b200 import decoder as D
+    rng = np.random.default_rng(seed + batch)
+    dec = D.DeviceDecoder(cfg, weights, max_seq=2 * prompt_len + steps + 8, batch=batch)
+    prompts = [rng.integers(0, cfg.vocab, size=prompt_len).tolist() for _ in range(batch)]
+    dec.prefill(prompts)  # warm-up prefill (module set-up, workspaces), then a timed one
     dec.reset()
     torch.cuda.synchronize()
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     p0.record()
-    dec.prefill(prompt)
+    dec.prefill(prompts)
     p1.record()
     torch.cuda.synchronize()
     prefill_ms = p0.elapsed_time(p1)
@@ -264,13 +273,16 @@ def measure_decode(kt, torch, steps: int, prompt_len: int, seed: int) -> dict:
     ms = e0.elapsed_time(e1) / steps
     weight_bytes = sum(w.size_in_bytes for L in dec.layers for k, w in L.items() if k.startswith("w"))
     weight_bytes += dec.head.size_in_bytes
-    return {"model": "qwen2-0.5b-shaped int4 g64 (random weights, tied, qkv bias)", "batch": 1,
-            "prompt": prompt_len, "prefill_ms": round(prefill_ms, 3),
-            "prefill_tokens_per_s": round(prompt_len / (prefill_ms / 1e3), 1),
-            "steps": steps, "ms_per_token": round(ms, 4),
-            "tokens_per_s": round(1e3 / ms, 1), "weight_bytes_per_token": int(weight_bytes),
-            "weight_gbs": round(weight_bytes / (ms / 1e3) / 1e9, 1),
-            "context_end": prompt_len + steps + 3}
+    out = {"model": "qwen2-0.5b-shaped int4 g64 (random weights, tied, qkv bias)", "batch": batch,
+           "prompt": prompt_len, "prefill_ms": round(prefill_ms, 3),
+           "prefill_tokens_per_s": round(batch * prompt_len / (prefill_ms / 1e3), 1),
+           "steps": steps, "ms_per_step": round(ms, 4),
+           "tokens_per_s": round(batch * 1e3 / ms, 1), "weight_bytes_per_step": int(weight_bytes),
+           "weight_gbs": round(weight_bytes / (ms / 1e3) / 1e9, 1),
+           "context_end": prompt_len + steps + 3}
+    del dec
+    torch.cuda.empty_cache()
+    return out
 
 
 # ----------------------------------------------------------------- GPU arm
@@ -428,12 +440,17 @@ def run_ours(args) -> None:
                 "dtype": "bf16 x bf16 -> f32 (INT4 weights dequantized)", "launches_per_step": len(SHAPES)}
         del gg
 
-    # decode tokens/s (Qwen2-0.5B-shaped INT4, batch 1): the
-    # device decode step captured once, prompt fed step by step, then timed
-    # greedy steps replaying the graph (no host work between tokens).
-    decode = None
+    # decode tokens/s (Qwen2-0.5B-shaped INT4 at batch 1, 8, 64):
+    # the prompts prefilled as blocks, the batched decode step captured once,
+    # then timed greedy steps replaying the graph (no host work between tokens).
+    decode, decode_batches = None, []
     if args.decode_steps > 0:
-        decode = measure_decode(kt, torch, args.decode_steps, args.decode_prompt, seed=99 + rank)
+        dcfg, dweights = decode_weights(kt, torch, seed=99 + rank)
+        for b in [int(v) for v in args.decode_batches.split(",") if v.strip()]:
+            decode_batches.append(measure_decode(kt, torch, dcfg, dweights, b, args.decode_steps, args.decode_prompt,
+                                                 seed=99 + rank))
+        decode = next((d for d in decode_batches if d["batch"] == 1), decode_batches[0] if decode_batches else None)
+        del dweights
 
     peak, peak_kind = measured_peaks()
     line = {
@@ -461,6 +478,8 @@ def run_ours(args) -> None:
         line["prefill_gemm"] = gemm
     if decode is not None:
         line["decode"] = decode
+        line["decode_batches"] = [{k: d[k] for k in ("batch", "ms_per_step", "tokens_per_s", "prefill_tokens_per_s",
+                                                     "weight_gbs")} for d in decode_batches]
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -479,6 +498,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-steps", type=int, default=128, help="timed greedy decode steps (0: skip)")
     ap.add_argument("--decode-prompt", type=int, default=512, help="prompt tokens before the timed decode")
+    ap.add_argument("--decode-batches", default="1,8,64", help="decode batch sizes to time (comma-separated)")
     ap.add_argument("--gemm-m", type=int, default=512,
                     help="also time the prefill GEMM at this M on the same weights (0: skip)")
     args = ap.parse_args()

@@ -264,6 +264,14 @@ kt_status kt_kv_store(kt_ctx* ctx, const float* k_dev, const float* v_dev, float
  * q_dev: rows q_stride floats apart (a fused q|k|v row is wider than the q part);
  * context_dev: [rows x heads*head_dim]. */
 size_t kt_attention_scratch_floats(int32_t rows, int32_t heads, int32_t head_dim, int32_t max_seq);
+/* The same for rows of several sequences (batched decode and prefill): row r
+ * belongs to sequence r / rows_per_seq, whose caches start cache_stride floats
+ * after the previous sequence's, and sits at position *position_dev +
+ * r % rows_per_seq.  rows is a multiple of rows_per_seq. */
+kt_status kt_attention_seqs(kt_ctx* ctx, const float* q_dev, const float* k_cache, const float* v_cache,
+                            float* context_dev, float* scores_dev, int32_t rows, int32_t q_stride, int32_t heads,
+                            int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t layer, float scale,
+                            const int32_t* position_dev, int32_t rows_per_seq, int64_t cache_stride, void* stream);
 kt_status kt_attention_decode(kt_ctx* ctx, const float* q_dev, const float* k_cache, const float* v_cache,
                               float* context_dev, float* scores_dev, int32_t rows, int32_t q_stride, int32_t heads,
                               int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t layer, float scale,
@@ -279,6 +287,12 @@ kt_status kt_add_rmsnorm(kt_ctx* ctx, float* x_dev, const float* y_dev, const fl
 kt_status kt_rope_kv(kt_ctx* ctx, float* qkv_dev, int32_t rows, int32_t q_width, int32_t kv_heads, int32_t head_dim,
                      const float* inv_freq_dev, float* k_cache, float* v_cache, int32_t max_seq, int32_t layer,
                      const int32_t* position_dev, void* stream);
+/* kt_rope_kv for rows of several sequences (row r: sequence r / rows_per_seq at
+ * position *position_dev + r % rows_per_seq, caches cache_stride floats apart). */
+kt_status kt_rope_kv_seqs(kt_ctx* ctx, float* qkv_dev, int32_t rows, int32_t q_width, int32_t kv_heads,
+                          int32_t head_dim, const float* inv_freq_dev, float* k_cache, float* v_cache, int32_t max_seq,
+                          int32_t layer, const int32_t* position_dev, int32_t rows_per_seq, int64_t cache_stride,
+                          void* stream);
 /* out[t][j] = silu(gu[t][j]) * gu[t][hidden + j] for fused gate|up rows [rows x 2*hidden]. */
 kt_status kt_silu_mul_rows(kt_ctx* ctx, const float* gu_dev, float* out_dev, int32_t rows, int32_t hidden,
                            void* stream);
@@ -292,6 +306,10 @@ kt_status kt_argmax(kt_ctx* ctx, const float* logits_dev, int32_t rows, int32_t 
  * KT_ERR_INVALID_ARGUMENT in *status_dev and leaves its output row untouched. */
 kt_status kt_dequantize_column(kt_ctx* ctx, const kt_qweight* w, const int32_t* columns_dev, int32_t count,
                                float* out_dev, int32_t* status_dev, void* stream);
+/* dst_dev[i] = src_dev[rows_dev[i]] for i < count, rows of `width` floats (e.g.
+ * the last prompt row of every sequence before the head). */
+kt_status kt_gather_rows(kt_ctx* ctx, const float* src_dev, const int32_t* rows_dev, int32_t count, int32_t width,
+                         float* dst_dev, void* stream);
 /* *value_dev += delta on `stream` (advances a captured step's position). */
 kt_status kt_increment(kt_ctx* ctx, int32_t* value_dev, int32_t delta, void* stream);
 

@@ -103,6 +103,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_rope": ([P, P, I32, I32, I32, P, P, P], I32),
     "kt_kv_store": ([P, P, P, P, P, I32, I32, I32, I32, I32, P, P], I32),
     "kt_attention_decode": ([P, P, P, P, P, P, I32, I32, I32, I32, I32, I32, I32, F32, P, P], I32),
+    "kt_attention_seqs": ([P, P, P, P, P, P, I32, I32, I32, I32, I32, I32, I32, F32, P, I32, I64, P], I32),
+    "kt_rope_kv_seqs": ([P, P, I32, I32, I32, I32, P, P, P, I32, I32, P, I32, I64, P], I32),
     "kt_silu_mul": ([P, P, P, I64, P], I32),
     "kt_add": ([P, P, P, I64, P], I32),
     "kt_argmax": ([P, P, I32, I32, P, P], I32),
@@ -112,6 +114,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_lora_project": ([P, P, I32, I32, P, I32, P, P], I32),
     "kt_lora_qmatmul": ([P, P, P, P, I32, I32, F32, P, P, P, I32, F32, P, P], I32),
     "kt_lora_backward": ([P, P, P, P, P, P, P, I32, F32, I32, P, I32, P, P, P], I32),
+    "kt_gather_rows": ([P, P, P, I32, I32, P, P], I32),
     "kt_fused_cross_entropy": ([P, P, P, P, I32, P, I32, P, P, P, P], I32),
     "kt_st_open": ([ctypes.c_char_p, PP], I32),
     "kt_st_close": ([P], I32),

@@ -790,6 +790,15 @@ kt_status kt_lora_backward(kt_ctx* ctx, const kt_qweight* w, const float* a, con
     return KT_OK;
 }
 
+kt_status kt_gather_rows(kt_ctx* ctx, const float* src, const int32_t* rows, int32_t count, int32_t width, float* dst,
+                         void* stream) {
+    if (!ctx || count < 0 || width <= 0) return fail(KT_ERR_INVALID_ARGUMENT, "bad gather_rows arguments");
+    if (count == 0) return KT_OK;
+    if (!src || !rows || !dst) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    KT_CUDA_TRY(launch_gather_rows(src, rows, count, width, dst, pick(ctx, stream)), "gather_rows launch");
+    return KT_OK;
+}
+
 // ---- fusedCrossEntropyLoss with a quantized head (kt_loss.cu)
 
 kt_status kt_fused_cross_entropy(kt_ctx* ctx, const kt_qweight* head, const float* bias, const float* hidden,
@@ -891,16 +900,26 @@ kt_status kt_add_rmsnorm(kt_ctx* ctx, float* x, const float* y, const float* wei
     return KT_OK;
 }
 
+kt_status kt_rope_kv_seqs(kt_ctx* ctx, float* qkv, int32_t rows, int32_t q_width, int32_t kv_heads,
+                          int32_t head_dim, const float* inv_freq, float* k_cache, float* v_cache, int32_t max_seq,
+                          int32_t layer, const int32_t* position_dev, int32_t rows_per_seq, int64_t cache_stride,
+                          void* stream) {
+    if (!ctx || !qkv || !inv_freq || !k_cache || !v_cache || !position_dev || rows <= 0 || rows > 65535 ||
+        head_dim <= 0 || head_dim % 2 != 0 || q_width % head_dim != 0 || kv_heads <= 0 || max_seq <= 0 || layer < 0 ||
+        rows_per_seq <= 0 || rows % rows_per_seq != 0 || cache_stride < 0 ||
+        (rows / rows_per_seq > 1 && cache_stride == 0))
+        return fail(KT_ERR_INVALID_ARGUMENT, "bad rope_kv arguments");
+    KT_CUDA_TRY(launch_rope_kv(qkv, rows, q_width, kv_heads, head_dim, inv_freq, k_cache, v_cache, max_seq, layer,
+                               position_dev, rows_per_seq, cache_stride, pick(ctx, stream)),
+                "rope_kv launch");
+    return KT_OK;
+}
+
 kt_status kt_rope_kv(kt_ctx* ctx, float* qkv, int32_t rows, int32_t q_width, int32_t kv_heads, int32_t head_dim,
                      const float* inv_freq, float* k_cache, float* v_cache, int32_t max_seq, int32_t layer,
                      const int32_t* position_dev, void* stream) {
-    if (!ctx || !qkv || !inv_freq || !k_cache || !v_cache || !position_dev || rows <= 0 || rows > 65535 ||
-        head_dim <= 0 || head_dim % 2 != 0 || q_width % head_dim != 0 || kv_heads <= 0 || max_seq <= 0 || layer < 0)
-        return fail(KT_ERR_INVALID_ARGUMENT, "bad rope_kv arguments");
-    KT_CUDA_TRY(launch_rope_kv(qkv, rows, q_width, kv_heads, head_dim, inv_freq, k_cache, v_cache, max_seq, layer,
-                               position_dev, pick(ctx, stream)),
-                "rope_kv launch");
-    return KT_OK;
+    return kt_rope_kv_seqs(ctx, qkv, rows, q_width, kv_heads, head_dim, inv_freq, k_cache, v_cache, max_seq, layer,
+                           position_dev, rows > 0 ? rows : 1, 0, stream);
 }
 
 size_t kt_attention_scratch_floats(int32_t rows, int32_t heads, int32_t head_dim, int32_t max_seq) {
@@ -935,19 +954,29 @@ kt_status kt_kv_store(kt_ctx* ctx, const float* k, const float* v, float* k_cach
     return KT_OK;
 }
 
+kt_status kt_attention_seqs(kt_ctx* ctx, const float* q, const float* k_cache, const float* v_cache, float* context,
+                            float* scores, int32_t rows, int32_t q_stride, int32_t heads, int32_t kv_heads,
+                            int32_t head_dim, int32_t max_seq, int32_t layer, float scale,
+                            const int32_t* position_dev, int32_t rows_per_seq, int64_t cache_stride, void* stream) {
+    if (!ctx || !q || !k_cache || !v_cache || !context || !scores || !position_dev || rows <= 0 || rows > 65535 ||
+        q_stride < heads * head_dim ||
+        heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || head_dim <= 0 || head_dim > 254 || max_seq <= 0 ||
+        layer < 0 || rows_per_seq <= 0 || rows % rows_per_seq != 0 || cache_stride < 0 ||
+        (rows / rows_per_seq > 1 && cache_stride == 0))
+        return fail(KT_ERR_INVALID_ARGUMENT, "bad attention arguments");
+    KT_CUDA_TRY(launch_attention_decode(q, k_cache, v_cache, context, scores, rows, q_stride, heads, kv_heads,
+                                        head_dim, max_seq, layer, scale, position_dev, rows_per_seq, cache_stride,
+                                        pick(ctx, stream)),
+                "attention launch");
+    return KT_OK;
+}
+
 kt_status kt_attention_decode(kt_ctx* ctx, const float* q, const float* k_cache, const float* v_cache, float* context,
                               float* scores, int32_t rows, int32_t q_stride, int32_t heads, int32_t kv_heads,
                               int32_t head_dim, int32_t max_seq, int32_t layer, float scale,
                               const int32_t* position_dev, void* stream) {
-    if (!ctx || !q || !k_cache || !v_cache || !context || !scores || !position_dev || rows <= 0 || rows > 65535 ||
-        q_stride < heads * head_dim ||
-        heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || head_dim <= 0 || head_dim > 254 || max_seq <= 0 ||
-        layer < 0)
-        return fail(KT_ERR_INVALID_ARGUMENT, "bad attention arguments");
-    KT_CUDA_TRY(launch_attention_decode(q, k_cache, v_cache, context, scores, rows, q_stride, heads, kv_heads,
-                                        head_dim, max_seq, layer, scale, position_dev, pick(ctx, stream)),
-                "attention launch");
-    return KT_OK;
+    return kt_attention_seqs(ctx, q, k_cache, v_cache, context, scores, rows, q_stride, heads, kv_heads, head_dim,
+                             max_seq, layer, scale, position_dev, rows > 0 ? rows : 1, 0, stream);
 }
 
 kt_status kt_silu_mul(kt_ctx* ctx, float* gate, const float* up, int64_t n, void* stream) {

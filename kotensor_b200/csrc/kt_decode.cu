@@ -81,12 +81,16 @@ __global__ void __launch_bounds__(kThreads) add_rmsnorm_kernel(float* __restrict
 // Attention.kt:222-232, :256-276).  blockIdx.y = row.
 __global__ void rope_kv_kernel(float* __restrict__ qkv, int q_width, int kv_heads, int head_dim,
                                const float* __restrict__ inv_freq, float* __restrict__ kc, float* __restrict__ vc,
-                               int max_seq, int layer, const int32_t* __restrict__ pos) {
+                               int max_seq, int layer, const int32_t* __restrict__ pos, int rows_per_seq,
+                               int64_t cache_stride) {
     const int half = head_dim / 2;
     const int kv_width = kv_heads * head_dim;
     const int rope_pairs = (q_width + kv_width) / 2;  // pairs over the q heads then the k heads
     const int r = blockIdx.y;
-    const int p = *pos + r;
+    const int seq = r / rows_per_seq;
+    const int p = *pos + (r - seq * rows_per_seq);
+    kc += seq * cache_stride;
+    vc += seq * cache_stride;
     float* row = qkv + static_cast<int64_t>(r) * (q_width + 2 * kv_width);
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < rope_pairs + kv_width; idx += gridDim.x * blockDim.x) {
         if (idx < rope_pairs) {
@@ -165,15 +169,21 @@ constexpr int kSpan = 64;  // positions per block
 __global__ void __launch_bounds__(kThreads) attention_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
     float* __restrict__ scratch, int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale,
-    int q_stride, const int32_t* __restrict__ pos) {
+    int q_stride, const int32_t* __restrict__ pos, int rows_per_seq, int64_t cache_stride) {
     __shared__ float red[32];
-    const int t = blockIdx.z;  // query row: position *pos + t, attending to 0..*pos + t
+    // query row t: sequence t / rows_per_seq (its cache cache_stride floats further),
+    // position *pos + t % rows_per_seq, attending to 0..that position
+    const int t = blockIdx.z;
+    const int seq = t / rows_per_seq;
+    const int tp = t - seq * rows_per_seq;
+    kc += seq * cache_stride;
+    vc += seq * cache_stride;
     __shared__ float qs[kMaxHeadDim + 2];
     __shared__ float sc[kSpan];
     __shared__ float part[kThreads / 32][kMaxHeadDim + 2];
     const int h = blockIdx.x, split = blockIdx.y;
     const int j0 = split * kSpan;
-    const int j1 = min(j0 + kSpan, *pos + t + 1);
+    const int j1 = min(j0 + kSpan, *pos + tp + 1);
     if (j0 >= j1) return;  // past the current position: the merge skips this split
     const int group = heads / kv_heads;
     const float* qh = q + static_cast<int64_t>(t) * q_stride + static_cast<int64_t>(h) * head_dim;
@@ -235,9 +245,9 @@ __global__ void __launch_bounds__(kThreads) attention_partial_kernel(
 }
 
 __global__ void attention_merge_kernel(const float* __restrict__ scratch, float* __restrict__ ctx, int heads,
-                                       int head_dim, int max_seq, const int32_t* __restrict__ pos) {
+                                       int head_dim, int max_seq, const int32_t* __restrict__ pos, int rows_per_seq) {
     const int h = blockIdx.x, t = blockIdx.y;
-    const int splits = (*pos + t) / kSpan + 1;
+    const int splits = (*pos + t % rows_per_seq) / kSpan + 1;
     const int stride = head_dim + 2;
     const float* base =
         scratch + (static_cast<int64_t>(t) * heads + h) * ((max_seq + kSpan - 1) / kSpan) * stride;
@@ -369,10 +379,11 @@ cudaError_t launch_add_rmsnorm(float* x, const float* y, const float* w, float* 
     return cudaGetLastError();
 }
 cudaError_t launch_rope_kv(float* qkv, int rows, int q_width, int kv_heads, int head_dim, const float* inv_freq,
-                           float* kc, float* vc, int max_seq, int layer, const int32_t* pos, cudaStream_t s) {
+                           float* kc, float* vc, int max_seq, int layer, const int32_t* pos, int rows_per_seq,
+                           int64_t cache_stride, cudaStream_t s) {
     const int total = (q_width + kv_heads * head_dim) / 2 + kv_heads * head_dim;
     rope_kv_kernel<<<dim3((total + kThreads - 1) / kThreads, rows), kThreads, 0, s>>>(
-        qkv, q_width, kv_heads, head_dim, inv_freq, kc, vc, max_seq, layer, pos);
+        qkv, q_width, kv_heads, head_dim, inv_freq, kc, vc, max_seq, layer, pos, rows_per_seq, cache_stride);
     return cudaGetLastError();
 }
 size_t attention_scratch_floats(int rows, int heads, int head_dim, int max_seq) {
@@ -392,14 +403,16 @@ cudaError_t launch_kv_store(const float* k, const float* v, float* kc, float* vc
 }
 cudaError_t launch_attention_decode(const float* q, const float* kc, const float* vc, float* ctx, float* scores,
                                     int rows, int q_stride, int heads, int kv_heads, int head_dim, int max_seq,
-                                    int layer, float scale, const int32_t* pos, cudaStream_t s) {
+                                    int layer, float scale, const int32_t* pos, int rows_per_seq,
+                                    int64_t cache_stride, cudaStream_t s) {
     if (head_dim > kMaxHeadDim) return cudaErrorInvalidValue;
     const dim3 grid(heads, (max_seq + kSpan - 1) / kSpan, rows);
     attention_partial_kernel<<<grid, kThreads, 0, s>>>(q, kc, vc, scores, heads, kv_heads, head_dim, max_seq, layer,
-                                                       scale, q_stride, pos);
+                                                       scale, q_stride, pos, rows_per_seq, cache_stride);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    attention_merge_kernel<<<dim3(heads, rows), 128, 0, s>>>(scores, ctx, heads, head_dim, max_seq, pos);
+    attention_merge_kernel<<<dim3(heads, rows), 128, 0, s>>>(scores, ctx, heads, head_dim, max_seq, pos,
+                                                             rows_per_seq);
     return cudaGetLastError();
 }
 cudaError_t launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s) {

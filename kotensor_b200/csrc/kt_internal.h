@@ -217,8 +217,11 @@ cudaError_t launch_concat_int4_columns(const kt_qweight* const* srcs, int32_t co
 cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int rows, int dim, float eps, cudaStream_t s);
 cudaError_t launch_add_rmsnorm(float* x, const float* y, const float* w, float* out, int rows, int dim, float eps,
                                cudaStream_t s);
+// Row r of rope_kv / attention: sequence r / rows_per_seq (its KV cache
+// cache_stride floats after the previous sequence's), position *pos + r % rows_per_seq.
 cudaError_t launch_rope_kv(float* qkv, int rows, int q_width, int kv_heads, int head_dim, const float* inv_freq,
-                           float* kc, float* vc, int max_seq, int layer, const int32_t* pos, cudaStream_t s);
+                           float* kc, float* vc, int max_seq, int layer, const int32_t* pos, int rows_per_seq,
+                           int64_t cache_stride, cudaStream_t s);
 size_t attention_scratch_floats(int rows, int heads, int head_dim, int max_seq);
 cudaError_t launch_silu_mul_rows(const float* gu, float* out, int rows, int hidden, cudaStream_t s);
 cudaError_t launch_rope(float* v, int rows, int width, int head_dim, const float* inv_freq, const int32_t* pos,
@@ -227,7 +230,8 @@ cudaError_t launch_kv_store(const float* k, const float* v, float* kc, float* vc
                             int max_seq, int layer, const int32_t* pos, cudaStream_t s);
 cudaError_t launch_attention_decode(const float* q, const float* kc, const float* vc, float* ctx, float* scores,
                                     int rows, int q_stride, int heads, int kv_heads, int head_dim, int max_seq,
-                                    int layer, float scale, const int32_t* pos, cudaStream_t s);
+                                    int layer, float scale, const int32_t* pos, int rows_per_seq,
+                                    int64_t cache_stride, cudaStream_t s);
 cudaError_t launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s);
 cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s);
 size_t argmax_scratch_bytes(int rows);

@@ -81,15 +81,20 @@ def _upload(w) -> QuantizedTensor:
     return QuantizedTensor.from_arrays(w.qdata, w.scales, w.zeros, (w.rows, w.columns), w.bits, w.group_size)
 
 
+class _Rows:
+    """Activation buffers for a block of rows (one decode step, or a prefill)."""
+
+
 class DeviceDecoder:
     """Greedy decoding of one sequence with weights, KV cache and buffers in HBM.
 
     ``weights``: ``embedding`` ([vocab x dim], None when tied), ``layers`` (a list
     of dicts with wq wk wv wo wg wu wd, their biases bq bk bv bo bg bu bd and the
     RMSNorm weights norm1 norm2), ``final_norm``, ``head`` ([dim x vocab]),
-    ``head_bias``."""
+    ``head_bias``.  ``batch`` sequences decode together (one KV cache each, the
+    same position): every matmul of a step runs at m = batch."""
 
-    def __init__(self, cfg: DecoderConfig, weights, max_seq: int, device: Optional[int] = None):
+    def __init__(self, cfg: DecoderConfig, weights, max_seq: int, device: Optional[int] = None, batch: int = 1):
         self.cfg = cfg
         self.max_seq = max_seq
         self.ctx = Context.get(device)
@@ -118,27 +123,23 @@ class DeviceDecoder:
         self.head_bias = vec(weights.head_bias)
         self.embedding = None if cfg.tied else _upload(weights.embedding)
         self.final_norm = vec(weights.final_norm)
-        kv = cfg.kv_heads * cfg.head_dim
-        self.keys = torch.zeros((cfg.layers, cfg.kv_heads, max_seq, cfg.head_dim), **f32)
+        if batch < 1:
+            raise ValueError(f"batch must be positive, got {batch}")
+        self.batch = batch
+        # one KV cache per sequence, each in the reference's layout [L][kvH][maxSeq][hd]
+        self.keys = torch.zeros((batch, cfg.layers, cfg.kv_heads, max_seq, cfg.head_dim), **f32)
         self.values = torch.zeros_like(self.keys)
+        self.cache_stride = cfg.layers * cfg.kv_heads * max_seq * cfg.head_dim
         self.inv_freq = vec(rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling))
-        self.x = torch.empty(cfg.dim, **f32)
-        self.normed = torch.empty(cfg.dim, **f32)
-        self.qkv = torch.empty(cfg.dim + 2 * kv, **f32)
-        self.q, self.k, self.v = self.qkv[:cfg.dim], self.qkv[cfg.dim:cfg.dim + kv], self.qkv[cfg.dim + kv:]
-        self.context = torch.empty(cfg.dim, **f32)
-        self.attn_out = torch.empty(cfg.dim, **f32)
-        self.gu = torch.empty(2 * cfg.hidden, **f32)
-        self.gate, self.up = self.gu[:cfg.hidden], self.gu[cfg.hidden:]
-        self.ffn_out = torch.empty(cfg.dim, **f32)
-        self.logits = torch.empty(cfg.vocab, **f32)
-        self.scores = torch.empty(_lib.load().kt_attention_scratch_floats(1, cfg.heads, cfg.head_dim, max_seq),
-                                  **f32)  # attention scratch
-        self._prefill_rows = 0  # prefill buffers, allocated on first use
-        self.token = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.position = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.next_token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.token = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.next_token = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.position = torch.zeros(1, dtype=torch.int32, device=dev)  # shared: sequences advance together
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.logits = torch.empty((batch, cfg.vocab), **f32)
+        self._head_in = torch.empty((batch, cfg.dim), **f32)
+        self._last_rows = torch.empty(batch, dtype=torch.int32, device=dev)
+        self._step_bufs = self._buffers(batch, tokens=self.token)
+        self._prefill_bufs = None  # prefill buffers, allocated on first use
         self.length = 0
         self.scale = float(np.float32(1.0) / np.float32(math.sqrt(float(cfg.head_dim))))
         self._graph = None
@@ -155,120 +156,129 @@ class DeviceDecoder:
         self.length = 0
         self.position.zero_()
 
-    def _linear(self, x, w: QuantizedTensor, y, bias) -> None:
-        MatMul.multiply_quantized(x.view(1, -1), w, y.view(1, -1), 1, accumulate=False, bias=bias)
-
-    def _launch_step(self) -> None:
-        """One decode step on the current stream: reads self.token and
-        self.position, writes self.logits and self.next_token, advances
-        the position and feeds the next token back."""
-        L_ = _lib.load()
-        cfg, h = self.cfg, self.ctx.handle
-        s, p = self._stream(), self._p
-        hd, kvh = cfg.head_dim, cfg.kv_heads
-        if cfg.tied:
-            _lib.check(L_.kt_dequantize_column(h, self.head.handle, p(self.token), 1, p(self.x), p(self.status), s))
-        else:
-            _lib.check(L_.kt_dequantize_rows(h, self.embedding.handle, p(self.token), 1, p(self.x), p(self.status), s))
-        _lib.check(L_.kt_rmsnorm(h, p(self.x), p(self.layers[0]["norm1"]), p(self.normed), 1, cfg.dim, cfg.eps, s))
-        for l, L in enumerate(self.layers):
-            self._linear(self.normed, L["wqkv"], self.qkv, L["bqkv"])
-            _lib.check(L_.kt_rope_kv(h, p(self.qkv), 1, cfg.dim, kvh, hd, p(self.inv_freq), p(self.keys),
-                                     p(self.values), self.max_seq, l, p(self.position), s))
-            _lib.check(L_.kt_attention_decode(h, p(self.q), p(self.keys), p(self.values), p(self.context),
-                                              p(self.scores), 1, cfg.dim, cfg.heads, kvh, hd, self.max_seq, l,
-                                              self.scale, p(self.position), s))
-            self._linear(self.context, L["wo"], self.attn_out, L["bo"])
-            _lib.check(L_.kt_add_rmsnorm(h, p(self.x), p(self.attn_out), p(L["norm2"]), p(self.normed), 1, cfg.dim,
-                                         cfg.eps, s))
-            self._linear(self.normed, L["wgu"], self.gu, L["bgu"])
-            _lib.check(L_.kt_silu_mul(h, p(self.gate), p(self.up), cfg.hidden, s))
-            self._linear(self.gate, L["wd"], self.ffn_out, L["bd"])
-            nxt = self.layers[l + 1]["norm1"] if l + 1 < len(self.layers) else self.final_norm
-            _lib.check(L_.kt_add_rmsnorm(h, p(self.x), p(self.ffn_out), p(nxt), p(self.normed), 1, cfg.dim, cfg.eps, s))
-        self._linear(self.normed, self.head, self.logits, self.head_bias)
-        _lib.check(L_.kt_argmax(h, p(self.logits), 1, cfg.vocab, p(self.next_token), s))
-        _lib.check(L_.kt_increment(h, p(self.position), 1, s))
-        self.token.copy_(self.next_token)
-
-    def _prefill_buffers(self, rows: int) -> None:
-        if rows <= self._prefill_rows:
-            return
+    def _buffers(self, rows: int, tokens=None) -> "_Rows":
         cfg = self.cfg
-        dev = self.x.device
+        dev = self.position.device
         f32 = dict(dtype=torch.float32, device=dev)
         kv = cfg.kv_heads * cfg.head_dim
-        self.px = torch.empty((rows, cfg.dim), **f32)
-        self.pnormed = torch.empty((rows, cfg.dim), **f32)
-        self.pqkv = torch.empty((rows, cfg.dim + 2 * kv), **f32)
-        self.pctx = torch.empty((rows, cfg.dim), **f32)
-        self.pattn = torch.empty((rows, cfg.dim), **f32)
-        self.pgu = torch.empty((rows, 2 * cfg.hidden), **f32)
-        self.pact = torch.empty((rows, cfg.hidden), **f32)
-        self.pffn = torch.empty((rows, cfg.dim), **f32)
-        self.ptokens = torch.empty(rows, dtype=torch.int32, device=dev)
-        self.pscores = torch.empty(
-            _lib.load().kt_attention_scratch_floats(rows, cfg.heads, cfg.head_dim, self.max_seq), **f32)
-        self._prefill_rows = rows
+        b = _Rows()
+        b.rows = rows
+        b.x = torch.empty((rows, cfg.dim), **f32)
+        b.normed = torch.empty((rows, cfg.dim), **f32)
+        b.qkv = torch.empty((rows, cfg.dim + 2 * kv), **f32)
+        b.ctx = torch.empty((rows, cfg.dim), **f32)
+        b.attn = torch.empty((rows, cfg.dim), **f32)
+        b.gu = torch.empty((rows, 2 * cfg.hidden), **f32)
+        b.act = torch.empty((rows, cfg.hidden), **f32)
+        b.ffn = torch.empty((rows, cfg.dim), **f32)
+        b.tokens = tokens if tokens is not None else torch.empty(rows, dtype=torch.int32, device=dev)
+        b.scores = torch.empty(_lib.load().kt_attention_scratch_floats(rows, cfg.heads, cfg.head_dim, self.max_seq),
+                               **f32)  # attention scratch
+        return b
 
-    def prefill(self, prompt: list[int]):
-        """Transformer.prefill (Transformer.kt:99-132): the whole prompt as one
-        [T x dim] block through every layer (the matmuls at m = T on the tensor-core
-        GEMM, causal attention over the cache); returns the last token's logits and
-        leaves its greedy successor in next_token / token."""
-        T = len(prompt)
-        if T == 0:
-            raise ValueError("Prompt cannot be empty")
-        if any(not 0 <= t < self.cfg.vocab for t in prompt):
-            raise ValueError("token out of vocab bounds")
-        if self.length + T > self.max_seq:
-            raise ValueError(f"KV cache full: {self.length} + {T} positions exceed maxSequenceLength {self.max_seq}")
-        self._prefill_buffers(T)
+    def _layers(self, b: "_Rows", rows: int, rows_per_seq: int) -> None:
+        """Embedding lookup of b.tokens[:rows] through every block; leaves the
+        final-normed rows in b.normed.  Row r is sequence r / rows_per_seq at
+        position *position + r % rows_per_seq (one sequence's prompt, or one
+        token of each of `rows` sequences)."""
         L_ = _lib.load()
         cfg, h = self.cfg, self.ctx.handle
         s, p = self._stream(), self._p
         hd, kvh = cfg.head_dim, cfg.kv_heads
         kv = kvh * hd
-        self.ptokens[:T].copy_(torch.tensor(prompt, dtype=torch.int32))
-        px, pn = self.px[:T], self.pnormed[:T]
-        pqkv, pctx, pattn = self.pqkv[:T], self.pctx[:T], self.pattn[:T]
-        pgu, pact, pffn = self.pgu[:T], self.pact[:T], self.pffn[:T]
         if cfg.tied:
-            _lib.check(L_.kt_dequantize_column(h, self.head.handle, p(self.ptokens), T, p(px), p(self.status), s))
+            _lib.check(L_.kt_dequantize_column(h, self.head.handle, p(b.tokens), rows, p(b.x), p(self.status), s))
         else:
-            _lib.check(L_.kt_dequantize_rows(h, self.embedding.handle, p(self.ptokens), T, p(px), p(self.status), s))
-        _lib.check(L_.kt_rmsnorm(h, p(px), p(self.layers[0]["norm1"]), p(pn), T, cfg.dim, cfg.eps, s))
+            _lib.check(L_.kt_dequantize_rows(h, self.embedding.handle, p(b.tokens), rows, p(b.x), p(self.status), s))
+        _lib.check(L_.kt_rmsnorm(h, p(b.x), p(self.layers[0]["norm1"]), p(b.normed), rows, cfg.dim, cfg.eps, s))
         for l, L in enumerate(self.layers):
-            MatMul.multiply_quantized(pn, L["wqkv"], pqkv, T, accumulate=False, bias=L["bqkv"])
-            _lib.check(L_.kt_rope_kv(h, p(pqkv), T, cfg.dim, kvh, hd, p(self.inv_freq), p(self.keys), p(self.values),
-                                     self.max_seq, l, p(self.position), s))
-            _lib.check(L_.kt_attention_decode(h, p(pqkv), p(self.keys), p(self.values), p(pctx), p(self.pscores), T,
-                                              cfg.dim + 2 * kv, cfg.heads, kvh, hd, self.max_seq, l, self.scale,
-                                              p(self.position), s))
-            MatMul.multiply_quantized(pctx, L["wo"], pattn, T, accumulate=False, bias=L["bo"])
-            _lib.check(L_.kt_add_rmsnorm(h, p(px), p(pattn), p(L["norm2"]), p(pn), T, cfg.dim, cfg.eps, s))
-            MatMul.multiply_quantized(pn, L["wgu"], pgu, T, accumulate=False, bias=L["bgu"])
-            _lib.check(L_.kt_silu_mul_rows(h, p(pgu), p(pact), T, cfg.hidden, s))
-            MatMul.multiply_quantized(pact, L["wd"], pffn, T, accumulate=False, bias=L["bd"])
+            MatMul.multiply_quantized(b.normed[:rows], L["wqkv"], b.qkv[:rows], rows, accumulate=False,
+                                      bias=L["bqkv"])
+            _lib.check(L_.kt_rope_kv_seqs(h, p(b.qkv), rows, cfg.dim, kvh, hd, p(self.inv_freq), p(self.keys),
+                                          p(self.values), self.max_seq, l, p(self.position), rows_per_seq,
+                                          self.cache_stride, s))
+            _lib.check(L_.kt_attention_seqs(h, p(b.qkv), p(self.keys), p(self.values), p(b.ctx), p(b.scores), rows,
+                                            cfg.dim + 2 * kv, cfg.heads, kvh, hd, self.max_seq, l, self.scale,
+                                            p(self.position), rows_per_seq, self.cache_stride, s))
+            MatMul.multiply_quantized(b.ctx[:rows], L["wo"], b.attn[:rows], rows, accumulate=False, bias=L["bo"])
+            _lib.check(L_.kt_add_rmsnorm(h, p(b.x), p(b.attn), p(L["norm2"]), p(b.normed), rows, cfg.dim, cfg.eps, s))
+            MatMul.multiply_quantized(b.normed[:rows], L["wgu"], b.gu[:rows], rows, accumulate=False, bias=L["bgu"])
+            _lib.check(L_.kt_silu_mul_rows(h, p(b.gu), p(b.act), rows, cfg.hidden, s))
+            MatMul.multiply_quantized(b.act[:rows], L["wd"], b.ffn[:rows], rows, accumulate=False, bias=L["bd"])
             nxt = self.layers[l + 1]["norm1"] if l + 1 < len(self.layers) else self.final_norm
-            _lib.check(L_.kt_add_rmsnorm(h, p(px), p(pffn), p(nxt), p(pn), T, cfg.dim, cfg.eps, s))
-        self._linear(pn[T - 1], self.head, self.logits, self.head_bias)
-        _lib.check(L_.kt_argmax(h, p(self.logits), 1, cfg.vocab, p(self.next_token), s))
-        _lib.check(L_.kt_increment(h, p(self.position), T, s))
-        self.token.copy_(self.next_token)
-        self.length += T
-        return self.logits
+            _lib.check(L_.kt_add_rmsnorm(h, p(b.x), p(b.ffn), p(nxt), p(b.normed), rows, cfg.dim, cfg.eps, s))
 
-    def step(self, token: int):
-        """Transformer.decode(token): the logits of this step (device tensor)."""
-        if not 0 <= token < self.cfg.vocab:
-            raise ValueError(f"{token} out of vocab bounds {self.cfg.vocab}")
+    def _head(self, normed, advance: int) -> None:
+        """The head on `batch` normed rows, greedy argmax per row, position += advance."""
+        L_ = _lib.load()
+        h, s, p = self.ctx.handle, self._stream(), self._p
+        MatMul.multiply_quantized(normed, self.head, self.logits, self.batch, accumulate=False, bias=self.head_bias)
+        _lib.check(L_.kt_argmax(h, p(self.logits), self.batch, self.cfg.vocab, p(self.next_token), s))
+        _lib.check(L_.kt_increment(h, p(self.position), advance, s))
+        self.token.copy_(self.next_token)
+
+    def _launch_step(self) -> None:
+        """One decode step on the current stream: reads self.token and
+        self.position, writes self.logits and self.next_token, advances
+        the position and feeds the next tokens back."""
+        b = self._step_bufs
+        self._layers(b, self.batch, 1)
+        self._head(b.normed, 1)
+
+    def _result(self):
+        return self.logits[0] if self.batch == 1 else self.logits
+
+    def prefill(self, prompts):
+        """Transformer.prefill (Transformer.kt:99-132) for every sequence: each
+        prompt (a list of token ids; one per sequence, equal lengths) runs as one
+        block of rows through every layer (the matmuls at m = batch x T on the
+        tensor-core GEMM, causal attention over each sequence's cache); returns
+        the last tokens' logits and leaves their greedy successors in
+        next_token / token."""
+        if len(prompts) > 0 and not isinstance(prompts[0], (list, tuple, np.ndarray)):
+            prompts = [prompts]
+        if len(prompts) != self.batch:
+            raise ValueError(f"{len(prompts)} prompts for a batch of {self.batch}")
+        T = len(prompts[0])
+        if T == 0:
+            raise ValueError("Prompt cannot be empty")
+        if any(len(pr) != T for pr in prompts):
+            raise ValueError("prompts of one batch must have equal lengths")
+        if any(not 0 <= t < self.cfg.vocab for pr in prompts for t in pr):
+            raise ValueError("token out of vocab bounds")
+        if self.length + T > self.max_seq:
+            raise ValueError(f"KV cache full: {self.length} + {T} positions exceed maxSequenceLength {self.max_seq}")
+        rows = self.batch * T
+        if rows > 65535:
+            raise ValueError(f"{rows} prefill rows exceed 65535")
+        if self._prefill_bufs is None or self._prefill_bufs.rows < rows:
+            self._prefill_bufs = self._buffers(rows)
+        b = self._prefill_bufs
+        b.tokens[:rows].copy_(torch.tensor([t for pr in prompts for t in pr], dtype=torch.int32))
+        self._layers(b, rows, T)
+        # the head only on each sequence's last row
+        self._last_rows.copy_(torch.tensor([q * T + T - 1 for q in range(self.batch)], dtype=torch.int32))
+        _lib.check(_lib.load().kt_gather_rows(self.ctx.handle, self._p(b.normed), self._p(self._last_rows), self.batch,
+                                              self.cfg.dim, self._p(self._head_in), self._stream()))
+        self._head(self._head_in, T)
+        self.length += T
+        return self._result()
+
+    def step(self, tokens):
+        """Transformer.decode(token) for every sequence (an int when batch == 1):
+        the logits of this step (device tensor)."""
+        tokens = [tokens] if isinstance(tokens, (int, np.integer)) else list(tokens)
+        if len(tokens) != self.batch:
+            raise ValueError(f"{len(tokens)} tokens for a batch of {self.batch}")
+        for t in tokens:
+            if not 0 <= t < self.cfg.vocab:
+                raise ValueError(f"{t} out of vocab bounds {self.cfg.vocab}")
         if self.length >= self.max_seq:
             raise ValueError(f"KV cache full: maxSequenceLength {self.max_seq}")
-        self.token.fill_(token)
+        self.token.copy_(torch.tensor(tokens, dtype=torch.int32))
         self._launch_step()
         self.length += 1
-        return self.logits
+        return self._result()
 
     def capture(self) -> None:
         """Records one step (from the current self.token / self.position) into a CUDA graph."""
@@ -278,20 +288,37 @@ class DeviceDecoder:
             self._launch_step()
 
     def generate(self, prompt: list[int], max_tokens: int) -> list[int]:
-        """Greedy continuation: the prompt fed step by step (eager), then
-        ``max_tokens`` replays of the captured step."""
+        """Greedy continuation of one sequence (batch 1): the prompt fed step by
+        step (eager), then ``max_tokens`` replays of the captured step."""
+        if self.batch != 1:
+            raise ValueError("generate is for batch 1; use generate_batch")
         if len(prompt) + max_tokens > self.max_seq:
             raise ValueError("prompt + max_tokens exceed max_seq")
         for t in prompt:
             self.step(t)
-        out = [int(self.next_token.item())]
+        out = [int(self.next_token[0].item())]
         if self._graph is None:
             self.capture()  # captures the position reached after the prompt
         for _ in range(max_tokens - 1):
             self._graph.replay()
             self.length += 1
-            out.append(int(self.next_token.item()))
+            out.append(int(self.next_token[0].item()))
         return out
+
+    def generate_batch(self, prompts, max_tokens: int) -> list:
+        """Greedy continuation of every sequence: the prompts prefilled as blocks,
+        then ``max_tokens`` - 1 replays of the captured batched step."""
+        if len(prompts[0]) + max_tokens > self.max_seq:
+            raise ValueError("prompt + max_tokens exceed max_seq")
+        self.prefill(prompts)
+        out = [self.next_token.cpu().tolist()]
+        if self._graph is None:
+            self.capture()
+        for _ in range(max_tokens - 1):
+            self._graph.replay()
+            self.length += 1
+            out.append(self.next_token.cpu().tolist())
+        return [[row[q] for row in out] for q in range(self.batch)]
 
     # -- files (Transformer.saveQuantized / loadQuantized, Transformer.kt:402-471)
     def save_quantized(self, path) -> None:

@@ -100,3 +100,54 @@ def test_prefill_matches_stepwise_oracle(kt, oracle, name, prompt_len):
         token = int(dev.next_token.item())
     assert int(dev.status.item()) == 0
     assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("batch", [3, 12])
+def test_batched_decode_matches_single_sequences(kt, oracle, batch):
+    """`batch` sequences decoding together (one KV cache each, every matmul at
+    m = batch, the prompts prefilled as one block of batch x T rows) give each
+    sequence the logits its own batch-1 decoder gives (teacher-forced with the
+    batched greedy tokens); bf16 tensor-core tolerance wherever a matmul of
+    either side takes the tcgen05 GEMM."""
+    from oracle import decoder_oracle as DO
+    from kotensor_b200 import decoder as D
+    params = CONFIGS["int4_gqa_bias_scaled_rope"]
+    weights = DO.DecoderWeights.random(DO.DecoderConfig(**params), seed=11)
+    rng = np.random.default_rng(batch)
+    T = 6
+    prompts = [rng.integers(0, params["vocab"], T).tolist() for _ in range(batch)]
+    dec = D.DeviceDecoder(D.DecoderConfig(**params), weights, max_seq=32, batch=batch)
+    singles = [D.DeviceDecoder(D.DecoderConfig(**params), weights, max_seq=32) for _ in range(batch)]
+    tol = 3e-2
+    got = dec.prefill(prompts).cpu().numpy()
+    for q, single in enumerate(singles):
+        want = single.prefill(prompts[q]).cpu().numpy()
+        assert np.abs(got[q] - want).max() <= tol * np.abs(want).max(), q
+    for _ in range(4):
+        tokens = dec.next_token.cpu().tolist()
+        got = dec.step(tokens).cpu().numpy()
+        for q, single in enumerate(singles):
+            want = single.step(tokens[q]).cpu().numpy()
+            assert np.abs(got[q] - want).max() <= tol * np.abs(want).max(), q
+    assert int(dec.status.item()) == 0
+    assert kt.Context.get().take_error() == 0
+
+
+def test_batched_graph_replay_matches_eager_steps(kt, oracle):
+    from oracle import decoder_oracle as DO
+    from kotensor_b200 import decoder as D
+    params = CONFIGS["int8_tied_mha"]
+    weights = DO.DecoderWeights.random(DO.DecoderConfig(**params), seed=4)
+    prompts = [[5, 17, 99, 4], [1, 2, 3, 4], [700, 8, 9, 10], [42, 42, 42, 42]]
+    a = D.DeviceDecoder(D.DecoderConfig(**params), weights, max_seq=40, batch=4)
+    b = D.DeviceDecoder(D.DecoderConfig(**params), weights, max_seq=40, batch=4)
+    out_graph = a.generate_batch(prompts, 10)
+    b.prefill(prompts)
+    out_eager = [[t] for t in b.next_token.cpu().tolist()]
+    for _ in range(9):
+        b.step(b.next_token.cpu().tolist())
+        for q, t in enumerate(b.next_token.cpu().tolist()):
+            out_eager[q].append(t)
+    assert out_graph == out_eager
+    assert torch.equal(a.logits, b.logits)
+    assert kt.Context.get().take_error() == 0
