@@ -244,6 +244,120 @@ __global__ void __launch_bounds__(kThreads) attention_partial_kernel(
     }
 }
 
+// The same partials for the G query heads that share one key/value head
+// (grouped-query attention, head h -> kv head h / G), one block per (kv head,
+// split, row): each key and value row is read once for the G heads instead of
+// once per head.  Warps take positions; a lane holds KPER dims of the G query
+// vectors in registers; warp w finishes head w's softmax statistics.
+template <int G, int KPER>
+__global__ void __launch_bounds__(kThreads) attention_group_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    float* __restrict__ scratch, int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale,
+    int q_stride, const int32_t* __restrict__ pos, int rows_per_seq, int64_t cache_stride) {
+    constexpr int kWarps = kThreads / 32;
+    static_assert(G <= kWarps, "one warp per query head finishes the statistics");
+    __shared__ float sc[G][kSpan];
+    __shared__ float stat[G][2];  // max, sum of exponentials
+    __shared__ float part[kWarps][G][KPER * 32];
+    const int kvh = blockIdx.x, split = blockIdx.y, t = blockIdx.z;
+    const int seq = t / rows_per_seq;
+    const int tp = t - seq * rows_per_seq;
+    kc += seq * cache_stride;
+    vc += seq * cache_stride;
+    const int j0 = split * kSpan;
+    const int j1 = min(j0 + kSpan, *pos + tp + 1);
+    if (j0 >= j1) return;  // past the current position: the merge skips this split
+    const int n = j1 - j0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float qv[G][KPER];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float* qh = q + static_cast<int64_t>(t) * q_stride + static_cast<int64_t>(kvh * G + g) * head_dim;
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) {
+            const int d = lane + 32 * i;
+            qv[g][i] = d < head_dim ? qh[d] : 0.0f;
+        }
+    }
+    const int64_t base = ((static_cast<int64_t>(layer) * kv_heads + kvh) * max_seq) * head_dim;
+    for (int j = j0 + warp; j < j1; j += kWarps) {
+        const float* kr = kc + base + static_cast<int64_t>(j) * head_dim;
+        float kv[KPER];
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) {
+            const int d = lane + 32 * i;
+            kv[i] = d < head_dim ? kr[d] : 0.0f;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float dot = 0.0f;
+#pragma unroll
+            for (int i = 0; i < KPER; ++i) dot = fmaf(qv[g][i], kv[i], dot);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            if (lane == 0) sc[g][j - j0] = dot * scale;
+        }
+    }
+    __syncthreads();
+    if (warp < G) {  // head `warp`: max and sum of exponentials over this split
+        const float s0 = lane < n ? sc[warp][lane] : -FLT_MAX;
+        const float s1 = lane + 32 < n ? sc[warp][lane + 32] : -FLT_MAX;
+        float mx = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float e0 = lane < n ? expf(s0 - mx) : 0.0f;
+        const float e1 = lane + 32 < n ? expf(s1 - mx) : 0.0f;
+        if (lane < n) sc[warp][lane] = e0;
+        if (lane + 32 < n) sc[warp][lane + 32] = e1;
+        float sum = e0 + e1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            stat[warp][0] = mx;
+            stat[warp][1] = sum;
+        }
+    }
+    __syncthreads();
+    float acc[G][KPER];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) acc[g][i] = 0.0f;
+    for (int j = j0 + warp; j < j1; j += kWarps) {
+        const float* vr = vc + base + static_cast<int64_t>(j) * head_dim;
+        float vv[KPER];
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) {
+            const int d = lane + 32 * i;
+            vv[i] = d < head_dim ? vr[d] : 0.0f;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float w = sc[g][j - j0];
+#pragma unroll
+            for (int i = 0; i < KPER; ++i) acc[g][i] = fmaf(w, vv[i], acc[g][i]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) part[warp][g][lane + 32 * i] = acc[g][i];
+    __syncthreads();
+    const int64_t splits = (max_seq + kSpan - 1) / kSpan;
+    for (int idx = threadIdx.x; idx < G * head_dim; idx += kThreads) {
+        const int g = idx / head_dim, d = idx - g * head_dim;
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) v += part[w][g][d];
+        float* out = scratch + ((static_cast<int64_t>(t) * heads + kvh * G + g) * splits + split) * (head_dim + 2);
+        out[2 + d] = v;
+        if (d == 0) {
+            out[0] = stat[g][0];
+            out[1] = stat[g][1];
+        }
+    }
+}
+
 __global__ void attention_merge_kernel(const float* __restrict__ scratch, float* __restrict__ ctx, int heads,
                                        int head_dim, int max_seq, const int32_t* __restrict__ pos, int rows_per_seq) {
     const int h = blockIdx.x, t = blockIdx.y;
@@ -406,9 +520,43 @@ cudaError_t launch_attention_decode(const float* q, const float* kc, const float
                                     int layer, float scale, const int32_t* pos, int rows_per_seq,
                                     int64_t cache_stride, cudaStream_t s) {
     if (head_dim > kMaxHeadDim) return cudaErrorInvalidValue;
-    const dim3 grid(heads, (max_seq + kSpan - 1) / kSpan, rows);
-    attention_partial_kernel<<<grid, kThreads, 0, s>>>(q, kc, vc, scores, heads, kv_heads, head_dim, max_seq, layer,
-                                                       scale, q_stride, pos, rows_per_seq, cache_stride);
+    const int splits = (max_seq + kSpan - 1) / kSpan;
+    const int group = heads / kv_heads;
+    const dim3 ggrid(kv_heads, splits, rows);
+#define KT_GROUP_CASE(G_, KP_)                                                                                     \
+    attention_group_kernel<G_, KP_><<<ggrid, kThreads, 0, s>>>(q, kc, vc, scores, heads, kv_heads, head_dim,       \
+                                                               max_seq, layer, scale, q_stride, pos, rows_per_seq, \
+                                                               cache_stride)
+    bool grouped = true;
+    if (group >= 2 && group <= 8 && head_dim <= 64) {
+        switch (group) {
+            case 2: KT_GROUP_CASE(2, 2); break;
+            case 3: KT_GROUP_CASE(3, 2); break;
+            case 4: KT_GROUP_CASE(4, 2); break;
+            case 5: KT_GROUP_CASE(5, 2); break;
+            case 6: KT_GROUP_CASE(6, 2); break;
+            case 7: KT_GROUP_CASE(7, 2); break;
+            default: KT_GROUP_CASE(8, 2); break;
+        }
+    } else if (group >= 2 && group <= 8 && head_dim <= 128) {
+        switch (group) {
+            case 2: KT_GROUP_CASE(2, 4); break;
+            case 3: KT_GROUP_CASE(3, 4); break;
+            case 4: KT_GROUP_CASE(4, 4); break;
+            case 5: KT_GROUP_CASE(5, 4); break;
+            case 6: KT_GROUP_CASE(6, 4); break;
+            case 7: KT_GROUP_CASE(7, 4); break;
+            default: KT_GROUP_CASE(8, 4); break;
+        }
+    } else {
+        grouped = false;
+    }
+#undef KT_GROUP_CASE
+    if (!grouped) {
+        const dim3 grid(heads, splits, rows);
+        attention_partial_kernel<<<grid, kThreads, 0, s>>>(q, kc, vc, scores, heads, kv_heads, head_dim, max_seq,
+                                                           layer, scale, q_stride, pos, rows_per_seq, cache_stride);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     attention_merge_kernel<<<dim3(heads, rows), 128, 0, s>>>(scores, ctx, heads, head_dim, max_seq, pos,
