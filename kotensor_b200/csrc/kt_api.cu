@@ -175,6 +175,24 @@ kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c,
             if (e != cudaSuccess) return cuda_fail(e, "qmatmul workspace");
         }
         e = launch_gemv_mma(v, args, ctx->sm_count, s, ws, need);
+    } else if (m > kGemvMmaMaxM && m <= 2 * kGemvMmaMaxM && gemv_mma_supported(v, kGemvMmaMaxM, a)) {
+        // 5..8 rows: the INT4 tensor-core GEMV on rows [0, 4) and [4, m) (two
+        // launches, each streaming the weight; faster than one fp32 pass)
+        e = cudaSuccess;
+        for (int32_t r0 = 0; r0 < m && e == cudaSuccess; r0 += kGemvMmaMaxM) {
+            MatmulArgs part = args;
+            part.m = std::min<int32_t>(kGemvMmaMaxM, m - r0);
+            part.a = a + static_cast<int64_t>(r0) * w->rows;
+            part.c = c + static_cast<int64_t>(r0) * w->columns;
+            if (part.lora.p != nullptr) part.lora.p += static_cast<int64_t>(r0) * part.lora.rank;
+            const size_t need = gemv_mma_workspace_bytes(v, part.m, ctx->sm_count);
+            void* ws = nullptr;
+            if (need > 0) {
+                e = stream_workspace(ctx, s, need, &ws);
+                if (e != cudaSuccess) return cuda_fail(e, "qmatmul workspace");
+            }
+            e = launch_gemv_mma(v, part, ctx->sm_count, s, ws, need);
+        }
     } else if (gemv_fast_supported(v, m, a)) {
         e = launch_gemv(v, args, ctx->sm_count, s);
     } else if (gemm_tc_supported(v, m, a)) {
@@ -659,7 +677,9 @@ kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out) {
     if (!w || !path_out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
     const QView v = view(w);
-    *path_out = gemv_imma_supported(v, m, nullptr) || gemv_mma_supported(v, m, nullptr) ? KT_PATH_GEMV_MMA
+    const bool mma_rows = gemv_mma_supported(v, m, nullptr) ||
+                          (m > kGemvMmaMaxM && m <= 2 * kGemvMmaMaxM && gemv_mma_supported(v, kGemvMmaMaxM, nullptr));
+    *path_out = gemv_imma_supported(v, m, nullptr) || mma_rows ? KT_PATH_GEMV_MMA
                 : gemv_fast_supported(v, m, nullptr) ? KT_PATH_GEMV
                 : gemm_tc_supported(v, m, nullptr)   ? KT_PATH_TENSOR_CORE
                                                      : KT_PATH_GENERIC;

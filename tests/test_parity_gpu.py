@@ -167,7 +167,7 @@ SHAPES = [(2048, 2048), (4096, 1024), (2048, 5632), (5632, 2048), (768, 32000), 
 
 @pytest.mark.parametrize("k,n", SHAPES)
 @pytest.mark.parametrize("bits", [4, 8])
-@pytest.mark.parametrize("m", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 6, 8])
 def test_matmul_matches_oracle(kt, oracle, k, n, bits, m):
     rng = np.random.default_rng(hash((k, n, bits, m)) % 2**32)
     w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
