@@ -201,9 +201,9 @@ kt_status kt_qmatmul_noalloc(kt_ctx* ctx, const kt_qweight* w, const float* a_de
  * aligned a), and so which tolerance applies: KT_PATH_GEMV (fp32 CUDA-core
  * streaming kernel), KT_PATH_GENERIC (fp32 kernel for unaligned shapes),
  * KT_PATH_TENSOR_CORE (bf16 tcgen05 kernel, 2e-2), KT_PATH_GEMV_MMA (INT4,
- * m <= 8: exact integer weights on tensor cores with x as two integer parts
- * (m = 1) or two fp16 terms (m = 2..8, in passes of at most 4 rows), fp32
- * group combine, 1e-3). */
+ * m <= 4, and m = 5..8 in two passes on weights of 16 MB or more: exact
+ * integer weights on tensor cores with x as two integer parts (m = 1) or two
+ * fp16 terms (m >= 2), fp32 group combine, 1e-3). */
 enum { KT_PATH_GEMV = 0, KT_PATH_GENERIC = 1, KT_PATH_TENSOR_CORE = 2, KT_PATH_GEMV_MMA = 3 };
 kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out);
 

@@ -153,6 +153,16 @@ kt_status grow(float** buf, size_t* cap, size_t need) {
     return KT_OK;
 }
 
+// 5..8 rows in two passes of the INT4 tensor-core GEMV: measured faster than
+// the fp32 streaming kernel from ~16 MB of weight bytes (4096 x 14336 INT4:
+// 2 x 19.9 us against 54 us), slower on small weights where the extra launch
+// dominates.
+bool mma_in_two_passes(const QView& v, int32_t m, const float* a) {
+    const int64_t weight_bytes = static_cast<int64_t>(v.rows) * v.bytes_per_row;
+    return m > kGemvMmaMaxM && m <= 2 * kGemvMmaMaxM && weight_bytes >= (static_cast<int64_t>(16) << 20) &&
+           gemv_mma_supported(v, kGemvMmaMaxM, a);
+}
+
 kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
                      float alpha, const float* bias, cudaStream_t s, const LoraEpilogue* lora = nullptr) {
     const QView v = view(w);
@@ -175,9 +185,10 @@ kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c,
             if (e != cudaSuccess) return cuda_fail(e, "qmatmul workspace");
         }
         e = launch_gemv_mma(v, args, ctx->sm_count, s, ws, need);
-    } else if (m > kGemvMmaMaxM && m <= 2 * kGemvMmaMaxM && gemv_mma_supported(v, kGemvMmaMaxM, a)) {
-        // 5..8 rows: the INT4 tensor-core GEMV on rows [0, 4) and [4, m) (two
-        // launches, each streaming the weight; faster than one fp32 pass)
+    } else if (mma_in_two_passes(v, m, a)) {
+        // 5..8 rows of a large weight: the INT4 tensor-core GEMV on rows [0, 4)
+        // and [4, m) (two launches, each streaming the weight; faster than one
+        // fp32 pass once the weight is large enough to amortise the extra launch)
         e = cudaSuccess;
         for (int32_t r0 = 0; r0 < m && e == cudaSuccess; r0 += kGemvMmaMaxM) {
             MatmulArgs part = args;
@@ -677,8 +688,7 @@ kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out) {
     if (!w || !path_out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
     const QView v = view(w);
-    const bool mma_rows = gemv_mma_supported(v, m, nullptr) ||
-                          (m > kGemvMmaMaxM && m <= 2 * kGemvMmaMaxM && gemv_mma_supported(v, kGemvMmaMaxM, nullptr));
+    const bool mma_rows = gemv_mma_supported(v, m, nullptr) || mma_in_two_passes(v, m, nullptr);
     *path_out = gemv_imma_supported(v, m, nullptr) || mma_rows ? KT_PATH_GEMV_MMA
                 : gemv_fast_supported(v, m, nullptr) ? KT_PATH_GEMV
                 : gemm_tc_supported(v, m, nullptr)   ? KT_PATH_TENSOR_CORE

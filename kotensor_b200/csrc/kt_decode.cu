@@ -12,6 +12,7 @@
 // cache is the reference's: fp32 keys / values [layers][kvHeads][maxSeq][headDim].
 #include <cfloat>
 
+#include "kt_device.cuh"
 #include "kt_internal.h"
 
 namespace kt {
@@ -46,6 +47,8 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 // out[r] = x[r] * (1 / sqrt(mean(x[r]^2) + eps)) * weight, one block per row (RMSNorm.kt:71-90).
 __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                           float* __restrict__ out, int dim, float eps) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     __shared__ float red[32];
     const float* xr = x + static_cast<int64_t>(blockIdx.x) * dim;
     float* orow = out + static_cast<int64_t>(blockIdx.x) * dim;
@@ -61,6 +64,8 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* __restri
 __global__ void __launch_bounds__(kThreads) add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ y,
                                                               const float* __restrict__ w, float* __restrict__ out,
                                                               int dim, float eps) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     __shared__ float red[32];
     float* xr = x + static_cast<int64_t>(blockIdx.x) * dim;
     const float* yr = y + static_cast<int64_t>(blockIdx.x) * dim;
@@ -83,6 +88,8 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int q_width, int kv_head
                                const float* __restrict__ inv_freq, float* __restrict__ kc, float* __restrict__ vc,
                                int max_seq, int layer, const int32_t* __restrict__ pos, int rows_per_seq,
                                int64_t cache_stride) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     const int half = head_dim / 2;
     const int kv_width = kv_heads * head_dim;
     const int rope_pairs = (q_width + kv_width) / 2;  // pairs over the q heads then the k heads
@@ -120,6 +127,8 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int q_width, int kv_head
 // RoPE.applyInPlace at position *pos (+ row): pairs (i, i + half) of every head.
 __global__ void rope_kernel(float* __restrict__ v, int rows, int width, int head_dim, const float* __restrict__ inv_freq,
                             const int32_t* __restrict__ pos) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     const int half = head_dim / 2;
     const int heads = width / head_dim;
     const int64_t total = static_cast<int64_t>(rows) * heads * half;
@@ -143,6 +152,8 @@ __global__ void rope_kernel(float* __restrict__ v, int rows, int width, int head
 __global__ void kv_store_kernel(const float* __restrict__ k, const float* __restrict__ v, float* __restrict__ kc,
                                 float* __restrict__ vc, int rows, int kv_heads, int head_dim, int max_seq, int layer,
                                 const int32_t* __restrict__ pos) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     const int width = kv_heads * head_dim;
     const int64_t total = static_cast<int64_t>(rows) * width;
     for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
@@ -170,6 +181,8 @@ __global__ void __launch_bounds__(kThreads) attention_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
     float* __restrict__ scratch, int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale,
     int q_stride, const int32_t* __restrict__ pos, int rows_per_seq, int64_t cache_stride) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     __shared__ float red[32];
     // query row t: sequence t / rows_per_seq (its cache cache_stride floats further),
     // position *pos + t % rows_per_seq, attending to 0..that position
@@ -254,6 +267,8 @@ __global__ void __launch_bounds__(kThreads) attention_group_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
     float* __restrict__ scratch, int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale,
     int q_stride, const int32_t* __restrict__ pos, int rows_per_seq, int64_t cache_stride) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     constexpr int kWarps = kThreads / 32;
     static_assert(G <= kWarps, "one warp per query head finishes the statistics");
     __shared__ float sc[G][kSpan];
@@ -360,6 +375,8 @@ __global__ void __launch_bounds__(kThreads) attention_group_kernel(
 
 __global__ void attention_merge_kernel(const float* __restrict__ scratch, float* __restrict__ ctx, int heads,
                                        int head_dim, int max_seq, const int32_t* __restrict__ pos, int rows_per_seq) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     const int h = blockIdx.x, t = blockIdx.y;
     const int splits = (*pos + t % rows_per_seq) / kSpan + 1;
     const int stride = head_dim + 2;
@@ -379,6 +396,8 @@ __global__ void attention_merge_kernel(const float* __restrict__ scratch, float*
 
 // gate = silu(gate) * up (Tensor.siluInPlace then mulInPlace)
 __global__ void silu_mul_kernel(float* __restrict__ gate, const float* __restrict__ up, int64_t n) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const float x = gate[i];
@@ -388,6 +407,8 @@ __global__ void silu_mul_kernel(float* __restrict__ gate, const float* __restric
 
 // out[t][j] = silu(gu[t][j]) * gu[t][hidden + j] for fused gate|up rows.
 __global__ void silu_mul_rows_kernel(const float* __restrict__ gu, float* __restrict__ out, int rows, int hidden) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     const int64_t n = static_cast<int64_t>(rows) * hidden;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -398,6 +419,8 @@ __global__ void silu_mul_rows_kernel(const float* __restrict__ gu, float* __rest
 }
 
 __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, int64_t n) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x)
         x[i] += y[i];
@@ -416,6 +439,8 @@ __device__ __forceinline__ void better(float& bv, int& bi, float ov, int oi) {
 
 __global__ void __launch_bounds__(kThreads) argmax_partial_kernel(const float* __restrict__ logits, int n, int chunk,
                                                                   float* __restrict__ pv, int* __restrict__ pi) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     __shared__ float bv[kThreads];
     __shared__ int bi[kThreads];
     const int row = blockIdx.y, c = blockIdx.x;
@@ -444,6 +469,8 @@ __global__ void __launch_bounds__(kThreads) argmax_partial_kernel(const float* _
 
 __global__ void argmax_merge_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int chunks,
                                     int32_t* __restrict__ out) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     if (threadIdx.x != 0) return;
     const int row = blockIdx.x;
     float best = -1e9f;
@@ -456,6 +483,8 @@ __global__ void argmax_merge_kernel(const float* __restrict__ pv, const int* __r
 // out[k] = value(k, *col) for k < K.
 __global__ void dequantize_column_kernel(QView w, const int32_t* __restrict__ cols, float* __restrict__ outs,
                                          int32_t* __restrict__ status) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
     const int c = cols[blockIdx.y];
     float* out = outs + static_cast<int64_t>(blockIdx.y) * w.rows;
     if (c < 0 || c >= w.columns) {
@@ -477,26 +506,47 @@ __global__ void dequantize_column_kernel(QView w, const int32_t* __restrict__ co
     }
 }
 
-__global__ void increment_kernel(int32_t* p, int32_t delta) { *p += delta; }
+__global__ void increment_kernel(int32_t* p, int32_t delta) {
+    dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents(); *p += delta; }
 
 int grid_for(int64_t n) { return static_cast<int>(std::min<int64_t>((n + kThreads - 1) / kThreads, 148 * 8)); }
 
 }  // namespace
 
+
+// Launches with programmatic stream serialization: the kernel may start while
+// the previous kernel on the stream finishes; every kernel here waits
+// (griddepcontrol.wait) before touching memory the previous one wrote.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, kernel, static_cast<Params>(args)...);
+}
+
 cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int rows, int dim, float eps, cudaStream_t s) {
-    rmsnorm_kernel<<<rows, kThreads, 0, s>>>(x, w, out, dim, eps);
+    launch_pdl(rmsnorm_kernel, dim3(rows), dim3(kThreads), 0, s, x, w, out, dim, eps);
     return cudaGetLastError();
 }
 cudaError_t launch_add_rmsnorm(float* x, const float* y, const float* w, float* out, int rows, int dim, float eps,
                                cudaStream_t s) {
-    add_rmsnorm_kernel<<<rows, kThreads, 0, s>>>(x, y, w, out, dim, eps);
+    launch_pdl(add_rmsnorm_kernel, dim3(rows), dim3(kThreads), 0, s, x, y, w, out, dim, eps);
     return cudaGetLastError();
 }
 cudaError_t launch_rope_kv(float* qkv, int rows, int q_width, int kv_heads, int head_dim, const float* inv_freq,
                            float* kc, float* vc, int max_seq, int layer, const int32_t* pos, int rows_per_seq,
                            int64_t cache_stride, cudaStream_t s) {
     const int total = (q_width + kv_heads * head_dim) / 2 + kv_heads * head_dim;
-    rope_kv_kernel<<<dim3((total + kThreads - 1) / kThreads, rows), kThreads, 0, s>>>(
+    launch_pdl(rope_kv_kernel, dim3(dim3((total + kThreads - 1) / kThreads, rows)), dim3(kThreads), 0, s, 
         qkv, q_width, kv_heads, head_dim, inv_freq, kc, vc, max_seq, layer, pos, rows_per_seq, cache_stride);
     return cudaGetLastError();
 }
@@ -505,13 +555,13 @@ size_t attention_scratch_floats(int rows, int heads, int head_dim, int max_seq) 
 }
 cudaError_t launch_rope(float* v, int rows, int width, int head_dim, const float* inv_freq, const int32_t* pos,
                         cudaStream_t s) {
-    rope_kernel<<<grid_for(static_cast<int64_t>(rows) * width / 2), kThreads, 0, s>>>(v, rows, width, head_dim,
+    launch_pdl(rope_kernel, dim3(grid_for(static_cast<int64_t>(rows) * width / 2)), dim3(kThreads), 0, s, v, rows, width, head_dim,
                                                                                        inv_freq, pos);
     return cudaGetLastError();
 }
 cudaError_t launch_kv_store(const float* k, const float* v, float* kc, float* vc, int rows, int kv_heads, int head_dim,
                             int max_seq, int layer, const int32_t* pos, cudaStream_t s) {
-    kv_store_kernel<<<grid_for(static_cast<int64_t>(rows) * kv_heads * head_dim), kThreads, 0, s>>>(
+    launch_pdl(kv_store_kernel, dim3(grid_for(static_cast<int64_t>(rows) * kv_heads * head_dim)), dim3(kThreads), 0, s, 
         k, v, kc, vc, rows, kv_heads, head_dim, max_seq, layer, pos);
     return cudaGetLastError();
 }
@@ -524,7 +574,7 @@ cudaError_t launch_attention_decode(const float* q, const float* kc, const float
     const int group = heads / kv_heads;
     const dim3 ggrid(kv_heads, splits, rows);
 #define KT_GROUP_CASE(G_, KP_)                                                                                     \
-    attention_group_kernel<G_, KP_><<<ggrid, kThreads, 0, s>>>(q, kc, vc, scores, heads, kv_heads, head_dim,       \
+    launch_pdl(attention_group_kernel<G_, KP_>, dim3(ggrid), dim3(kThreads), 0, s, q, kc, vc, scores, heads, kv_heads, head_dim,       \
                                                                max_seq, layer, scale, q_stride, pos, rows_per_seq, \
                                                                cache_stride)
     bool grouped = true;
@@ -554,25 +604,25 @@ cudaError_t launch_attention_decode(const float* q, const float* kc, const float
 #undef KT_GROUP_CASE
     if (!grouped) {
         const dim3 grid(heads, splits, rows);
-        attention_partial_kernel<<<grid, kThreads, 0, s>>>(q, kc, vc, scores, heads, kv_heads, head_dim, max_seq,
+        launch_pdl(attention_partial_kernel, dim3(grid), dim3(kThreads), 0, s, q, kc, vc, scores, heads, kv_heads, head_dim, max_seq,
                                                            layer, scale, q_stride, pos, rows_per_seq, cache_stride);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    attention_merge_kernel<<<dim3(heads, rows), 128, 0, s>>>(scores, ctx, heads, head_dim, max_seq, pos,
+    launch_pdl(attention_merge_kernel, dim3(dim3(heads, rows)), dim3(128), 0, s, scores, ctx, heads, head_dim, max_seq, pos,
                                                              rows_per_seq);
     return cudaGetLastError();
 }
 cudaError_t launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s) {
-    silu_mul_kernel<<<grid_for(n), kThreads, 0, s>>>(gate, up, n);
+    launch_pdl(silu_mul_kernel, dim3(grid_for(n)), dim3(kThreads), 0, s, gate, up, n);
     return cudaGetLastError();
 }
 cudaError_t launch_silu_mul_rows(const float* gu, float* out, int rows, int hidden, cudaStream_t s) {
-    silu_mul_rows_kernel<<<grid_for(static_cast<int64_t>(rows) * hidden), kThreads, 0, s>>>(gu, out, rows, hidden);
+    launch_pdl(silu_mul_rows_kernel, dim3(grid_for(static_cast<int64_t>(rows) * hidden)), dim3(kThreads), 0, s, gu, out, rows, hidden);
     return cudaGetLastError();
 }
 cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s) {
-    add_kernel<<<grid_for(n), kThreads, 0, s>>>(x, y, n);
+    launch_pdl(add_kernel, dim3(grid_for(n)), dim3(kThreads), 0, s, x, y, n);
     return cudaGetLastError();
 }
 size_t argmax_scratch_bytes(int rows) { return static_cast<size_t>(rows) * 128 * 8; }
@@ -582,19 +632,19 @@ cudaError_t launch_argmax(const float* logits, int rows, int n, int32_t* out, vo
     const int chunk = (n + chunks - 1) / chunks;
     float* pv = static_cast<float*>(scratch);
     int* pi = reinterpret_cast<int*>(pv + static_cast<size_t>(rows) * 128);
-    argmax_partial_kernel<<<dim3(chunks, rows), kThreads, 0, s>>>(logits, n, chunk, pv, pi);
+    launch_pdl(argmax_partial_kernel, dim3(dim3(chunks, rows)), dim3(kThreads), 0, s, logits, n, chunk, pv, pi);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    argmax_merge_kernel<<<rows, 32, 0, s>>>(pv, pi, chunks, out);
+    launch_pdl(argmax_merge_kernel, dim3(rows), dim3(32), 0, s, pv, pi, chunks, out);
     return cudaGetLastError();
 }
 cudaError_t launch_dequantize_column(const QView& w, const int32_t* col, int count, float* out, int32_t* status,
                                      cudaStream_t s) {
-    dequantize_column_kernel<<<dim3(grid_for(w.rows), count), kThreads, 0, s>>>(w, col, out, status);
+    launch_pdl(dequantize_column_kernel, dim3(dim3(grid_for(w.rows), count)), dim3(kThreads), 0, s, w, col, out, status);
     return cudaGetLastError();
 }
 cudaError_t launch_increment(int32_t* p, int32_t delta, cudaStream_t s) {
-    increment_kernel<<<1, 1, 0, s>>>(p, delta);
+    launch_pdl(increment_kernel, dim3(1), dim3(1), 0, s, p, delta);
     return cudaGetLastError();
 }
 
