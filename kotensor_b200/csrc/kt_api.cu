@@ -730,15 +730,25 @@ kt_status kt_qmatmul_host(kt_ctx* ctx, const kt_qweight* w, const float* a, floa
     if ((st = grow(&ctx->d2h_c, &ctx->c_cap, cn)) != KT_OK) return st;
     if (bias && (st = grow(&ctx->bias_buf, &ctx->bias_cap, w->columns)) != KT_OK) return st;
     cudaStream_t s = ctx->stream;
+    // c in page-locked host memory (cudaHostAlloc / cudaHostRegister, mapped into
+    // the device's address space): the kernel writes it directly over the bus
+    // (posted writes, no device-to-host copy); otherwise through device staging.
+    // a is always staged: every column tile of the product reads it.
+    cudaPointerAttributes pa{};
+    float* c_dev = ctx->d2h_c;
+    if (cudaPointerGetAttributes(&pa, c) == cudaSuccess && pa.type == cudaMemoryTypeHost && pa.devicePointer != nullptr)
+        c_dev = static_cast<float*>(pa.devicePointer);
+    cudaGetLastError();  // a pageable pointer is not an error here
     KT_CUDA_TRY(cudaMemcpyAsync(ctx->h2d_a, a, an * sizeof(float), cudaMemcpyHostToDevice, s), "H2D a");
-    if (accumulate) KT_CUDA_TRY(cudaMemcpyAsync(ctx->d2h_c, c, cn * sizeof(float), cudaMemcpyHostToDevice, s), "H2D c");
+    if (accumulate && c_dev == ctx->d2h_c)
+        KT_CUDA_TRY(cudaMemcpyAsync(ctx->d2h_c, c, cn * sizeof(float), cudaMemcpyHostToDevice, s), "H2D c");
     if (bias)
         KT_CUDA_TRY(cudaMemcpyAsync(ctx->bias_buf, bias, w->columns * sizeof(float), cudaMemcpyHostToDevice, s),
                     "H2D bias");
-    if ((st = run_matmul(ctx, w, ctx->h2d_a, ctx->d2h_c, m, accumulate, alpha, bias ? ctx->bias_buf : nullptr, s)) !=
-        KT_OK)
+    if ((st = run_matmul(ctx, w, ctx->h2d_a, c_dev, m, accumulate, alpha, bias ? ctx->bias_buf : nullptr, s)) != KT_OK)
         return st;
-    KT_CUDA_TRY(cudaMemcpyAsync(c, ctx->d2h_c, cn * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H c");
+    if (c_dev == ctx->d2h_c)
+        KT_CUDA_TRY(cudaMemcpyAsync(c, ctx->d2h_c, cn * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H c");
     KT_CUDA_TRY(cudaStreamSynchronize(s), "cudaStreamSynchronize");
     return KT_OK;
 }

@@ -476,6 +476,22 @@ int choose_splits(int R, int K, int sm_count) {
     return tiles > kTicketCapEach ? min_splits(K) : s;
 }
 
+// The kernel's shared-memory and cluster-size attributes, set once per device
+// (setting them on every launch costs host time on a latency-bound call).
+cudaError_t prepare_kernel() {
+    constexpr int kMaxDevices = 64;
+    static bool done[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < kMaxDevices && done[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) done[dev] = true;
+    return e;
+}
+
 // Clusters of `c` CTAs of this kernel the GPU holds at once (cached per device).
 int active_clusters(int c) {
     constexpr int kMaxDevices = 64;
@@ -580,10 +596,7 @@ cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, 
         p.tickets = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) + kGemvTicketOffset);
         p.partials = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kWorkspaceReservedBytes);
     }
-    cudaError_t e = cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
-    if (e == cudaSuccess && plan.cluster)
-        e = cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    const cudaError_t e = prepare_kernel();
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(tiles_of(p.R), plan.splits, 1);

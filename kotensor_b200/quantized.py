@@ -133,6 +133,7 @@ class QuantizedTensor:
         info = _lib.KtInfo()
         _lib.check(_lib.load().kt_qweight_info_get(handle, ctypes.byref(info)))
         self._info = info
+        self._rows, self._columns = int(info.rows), int(info.columns)
 
     # -- construction
     @staticmethod
@@ -209,8 +210,8 @@ class QuantizedTensor:
     handle = property(lambda self: self._handle)
     bits = property(lambda self: self._info.bits)
     group_size = property(lambda self: self._info.group_size)
-    rows = property(lambda self: self._info.rows)
-    columns = property(lambda self: self._info.columns)
+    rows = property(lambda self: self._rows)
+    columns = property(lambda self: self._columns)
     groups = property(lambda self: self._info.groups)
     stored_columns = property(lambda self: self._info.stored_columns)
     bytes_per_row = property(lambda self: self._info.bytes_per_row)
@@ -318,13 +319,15 @@ class MatMul:
                                     ctypes.c_void_p(c.data_ptr()), m, int(bool(accumulate)), float(alpha),
                                     ctypes.c_void_p(bias.data_ptr()) if bias is not None else None, _stream_of(c)))
             return
-        a_h = np.ascontiguousarray(a, dtype=np.float32)
+        a_h = a if (type(a) is np.ndarray and a.dtype == np.float32 and a.flags.c_contiguous) else \
+            np.ascontiguousarray(a, dtype=np.float32)
         if not (isinstance(c, np.ndarray) and c.dtype == np.float32 and c.flags.c_contiguous):
             raise ValueError("c must be a contiguous float32 numpy array")
         b_h = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
-        _lib.check(L.kt_qmatmul_host(weight._ctx.handle, weight.handle, a_h.ctypes.data_as(ctypes.c_void_p),
-                                     c.ctypes.data_as(ctypes.c_void_p), m, int(bool(accumulate)), float(alpha),
-                                     b_h.ctypes.data_as(ctypes.c_void_p) if b_h is not None else None))
+        st = L.kt_qmatmul_host(weight._ctx.handle, weight.handle, a_h.ctypes.data, c.ctypes.data, m,
+                               1 if accumulate else 0, alpha, b_h.ctypes.data if b_h is not None else None)
+        if st:
+            _lib.check(st)
 
     @staticmethod
     def multiply_by_quantized_transposed(dy, weight: QuantizedTensor, dx, m: int, accumulate: bool = True) -> None:
