@@ -18,8 +18,9 @@
 // (low and high nibble columns) and two accumulators of nt TMEM columns each.
 //
 // Pipeline per 64-row K-block, kStages deep:
-//   warp 8  (one lane): TMA of the packed bytes [64 x 128] and of the bf16 x
-//                       tile [nt x 64] (128-byte swizzle) -> "full_raw"
+//   warp 8  (one lane): TMA of the packed bytes [64 x 128] and the block's
+//                       group scales / zero points -> "full_w"; TMA of the
+//                       bf16 x tile [nt x 64] (128-byte swizzle) -> "full_x"
 //   warps 0-7         : dequantize the packed bytes into the two A tiles
 //                       (swizzled 16-byte stores), fence.proxy.async -> "full_a"
 //   warp 9  (one lane): 2 x 4 tcgen05.mma (K = 16 each), tcgen05.commit -> "empty"
@@ -28,12 +29,23 @@
 // timeout sets the context's error word.
 //
 // The activations are converted to bf16 once per call by a small pre-pass
-// kernel into the stream's workspace (after its reserved front).
+// kernel into the stream's workspace (after its reserved front).  Pre-pass,
+// GEMM and split-K reduction are chained by programmatic dependent launch: the
+// GEMM's CTAs start while the kernel before them runs, allocate tensor memory,
+// load and dequantize the first stages of weights (which no kernel of the
+// chain writes) and wait (griddepcontrol.wait) only before the first x tile.
+//
+// Split-K (when column x token tiles leave SMs idle): every split writes its
+// fp32 partial tile to the workspace; the partials are summed in split order
+// (deterministic) by the last CTA of the tile to arrive when they are small,
+// or by a separate reduction kernel spread over the whole GPU when they are
+// large (one CTA reading megabytes of partials would take tens of us).
 #include <cuda_bf16.h>
 
 #include <algorithm>
 #include <cstdlib>
 
+#include "kt_device.cuh"
 #include "kt_internal.h"
 
 namespace kt {
@@ -82,6 +94,7 @@ struct GemmParams {
     // split-K (gridDim.z > 1): partial tiles and per-tile arrival counters
     float* partials;   // [tile][split][nt][256]
     int32_t* tickets;  // [tile], zero between launches
+    int32_t reduce_kernel;  // 1: the partials are summed by split_reduce_kernel, not the last CTA
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -228,17 +241,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char* gbase = smem_raw + (base - raw_s);
     const uint32_t scl = base + kStages * kStageBytes;  // scale slots [stage][group]
     const uint32_t bars = scl + kStages * kScaleStageBytes;
-    auto full_raw = [&](int s) { return bars + 8 * s; };
-    auto full_a = [&](int s) { return bars + 8 * (kStages + s); };
-    auto empty = [&](int s) { return bars + 8 * (2 * kStages + s); };
-    const uint32_t done = bars + 8 * (3 * kStages);
+    auto full_w = [&](int s) { return bars + 8 * s; };
+    auto full_x = [&](int s) { return bars + 8 * (kStages + s); };
+    auto full_a = [&](int s) { return bars + 8 * (2 * kStages + s); };
+    auto empty = [&](int s) { return bars + 8 * (3 * kStages + s); };
+    const uint32_t done = bars + 8 * (4 * kStages);
     uint32_t* tmem_slot =
-        reinterpret_cast<uint32_t*>(gbase + kStages * (kStageBytes + kScaleStageBytes) + 8 * (3 * kStages + 1));
+        reinterpret_cast<uint32_t*>(gbase + kStages * (kStageBytes + kScaleStageBytes) + 8 * (4 * kStages + 1));
     const int tile_cols = min(kTileBytes, p.R - tile_b0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(full_raw(s), 1);
+            mbar_init(full_w(s), 1);
+            mbar_init(full_x(s), 1);
             mbar_init(full_a(s), kWorkers);
             mbar_init(empty(s), 1);
         }
@@ -256,46 +271,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    dev::pdl_launch_dependents();
     if (warp == kProducerWarp) {
         if (lane == 0) {
-            const uint32_t tx = static_cast<uint32_t>(kRawBytes + p.nt * kBK * 2);
+            const uint32_t xtx = static_cast<uint32_t>(p.nt * kBK * 2);
             const uint32_t gbytes = static_cast<uint32_t>(tile_cols) * (BITS == 4 ? 10 : 4);
-            int issued = 0;
-            for (int i = 0; i < n_kb; ++i) {
+            // the packed bytes and group constants of block i -> full_w(i % NS)
+            auto issue_w = [&](int i) {
                 const int s = i % kStages;
-                if (i >= kStages && !mbar_wait_bounded(empty(s), ((i / kStages) - 1) & 1)) {
-                    atomicOr(p.err, 1);
-                    break;
-                }
                 const uint32_t st = base + s * kStageBytes;
                 const int kb = kb_begin + i;
                 const int ga = min(kb * kBK / p.gs, p.G - 1);
                 const int gb = min((kb * kBK + kBK - 1) / p.gs, p.G - 1);
-                mbar_expect_tx(full_raw(s), tx + (gb - ga + 1) * gbytes);
-                tma_load_2d(st, &tmap_w, tile_b0, kb * kBK, full_raw(s));
-                tma_load_2d(st + kRawBytes, &tmap_x, kb * kBK, tok0, full_raw(s));
+                mbar_expect_tx(full_w(s), kRawBytes + (gb - ga + 1) * gbytes);
+                tma_load_2d(st, &tmap_w, tile_b0, kb * kBK, full_w(s));
                 for (int g = ga; g <= gb; ++g) {
                     const uint32_t dst = scl + s * kScaleStageBytes + (g - ga) * kGroupSlotBytes;
                     const int64_t go = static_cast<int64_t>(g) * p.N;
-                    bulk_load(dst, p.scales + go + tile_b0, tile_cols * 4, full_raw(s));
+                    bulk_load(dst, p.scales + go + tile_b0, tile_cols * 4, full_w(s));
                     if constexpr (BITS == 4) {
-                        bulk_load(dst + kTileBytes * 4, p.scales + go + p.R + tile_b0, tile_cols * 4, full_raw(s));
-                        bulk_load(dst + kTileBytes * 8, p.zeros + go + tile_b0, tile_cols, full_raw(s));
-                        bulk_load(dst + kTileBytes * 9, p.zeros + go + p.R + tile_b0, tile_cols, full_raw(s));
+                        bulk_load(dst + kTileBytes * 4, p.scales + go + p.R + tile_b0, tile_cols * 4, full_w(s));
+                        bulk_load(dst + kTileBytes * 8, p.zeros + go + tile_b0, tile_cols, full_w(s));
+                        bulk_load(dst + kTileBytes * 9, p.zeros + go + p.R + tile_b0, tile_cols, full_w(s));
                     }
                 }
+            };
+            // the bf16 x tile of block i -> full_x(i % NS)
+            auto issue_x = [&](int i) {
+                const int s = i % kStages;
+                mbar_expect_tx(full_x(s), xtx);
+                tma_load_2d(base + s * kStageBytes + kRawBytes, &tmap_x, (kb_begin + i) * kBK, tok0, full_x(s));
+            };
+            // Weights of the first stages before the wait (no kernel of the
+            // chain writes them), x only after it: x is the previous kernel's output.
+            const int pre = min(n_kb, kStages);
+            for (int i = 0; i < pre; ++i) issue_w(i);
+            dev::pdl_wait();
+            for (int i = 0; i < pre; ++i) issue_x(i);
+            int issued = pre;
+            for (int i = pre; i < n_kb; ++i) {
+                const int s = i % kStages;
+                if (!mbar_wait_bounded(empty(s), ((i / kStages) - 1) & 1)) {
+                    atomicOr(p.err, 1);
+                    break;
+                }
+                issue_w(i);
+                issue_x(i);
                 ++issued;
             }
-            // the last copy issued into each slot has landed before the CTA may exit
-            for (int i = max(0, issued - kStages); i < issued; ++i)
-                if (!mbar_wait_bounded(full_raw(i % kStages), (i / kStages) & 1)) break;
+            // the last copies issued into each slot have landed before the CTA may exit
+            for (int i = max(0, issued - kStages); i < issued; ++i) {
+                if (!mbar_wait_bounded(full_w(i % kStages), (i / kStages) & 1)) break;
+                if (!mbar_wait_bounded(full_x(i % kStages), (i / kStages) & 1)) break;
+            }
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             for (int i = 0; i < n_kb; ++i) {
                 const int s = i % kStages;
                 const uint32_t par = (i / kStages) & 1;
-                if (!mbar_wait_bounded(full_raw(s), par) || !mbar_wait_bounded(full_a(s), par)) {
+                if (!mbar_wait_bounded(full_x(s), par) || !mbar_wait_bounded(full_a(s), par)) {
                     atomicOr(p.err, 1);
                     break;
                 }
@@ -327,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < n_kb; ++i) {
             const int s = i % kStages;
             const int kb = kb_begin + i;
-            if (!mbar_wait_bounded(full_raw(s), (i / kStages) & 1)) {
+            if (!mbar_wait_bounded(full_w(s), (i / kStages) & 1)) {
                 if (lane == 0) atomicOr(p.err, 1);
                 ok = false;
                 break;
@@ -391,6 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 of the low
         // (w < 4) or high (w >= 4) accumulator: one tile column per thread.
+        dev::pdl_wait();  // c may be read or written by the kernel before this one
         const bool have = ok && mbar_wait_bounded(done, 0);
         if (!have && lane == 0) atomicOr(p.err, 1);
         tc_fence_after();
@@ -425,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 16; ++j) __stcg(mine + (t0 + j) * kCT + colt, v[j]);
             }
         }
-        if (S > 1) {
+        if (S > 1 && !p.reduce_kernel) {
             // split-K: the last CTA of the tile to arrive sums the partial tiles in
             // split order (the worker barrier orders every worker's stores before
             // thread 0's acq_rel atomic, which publishes them at GPU scope).
@@ -461,8 +497,53 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Split-K partial tiles [tile][split][nt][columns] summed in split order, then
+// c = (accumulate ? c : 0) + alpha * sum + bias (+ LoRA term): the arithmetic,
+// in the same order, of the last-CTA reduction in gemm_tc_kernel, spread over
+// the whole GPU (thread: 4 adjacent columns of one token of one tile).
+template <int BITS>
+__global__ void __launch_bounds__(256) split_reduce_kernel(GemmParams p, int tiles_x, int tiles_y, int S) {
+    constexpr int kCT = BITS == 4 ? 2 * kTileBytes : kTileBytes;
+    constexpr int kQuads = kCT / 4;
+    dev::pdl_launch_dependents();
+    dev::pdl_wait();  // the partials are the previous kernel's output
+    const int64_t total = static_cast<int64_t>(tiles_x) * tiles_y * p.nt * kQuads;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int q4 = static_cast<int>(i % kQuads) * 4;
+        const int64_t rest = i / kQuads;
+        const int t = static_cast<int>(rest % p.nt);
+        const int64_t tile_id = rest / p.nt;
+        const int bx = static_cast<int>(tile_id % tiles_x);
+        const int tok = static_cast<int>(tile_id / tiles_x) * p.nt + t;
+        const float* parts = p.partials + tile_id * S * (static_cast<int64_t>(p.nt) * kCT);
+        float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int sp = 0; sp < S; ++sp) {
+            const float4 u =
+                __ldcg(reinterpret_cast<const float4*>(parts + (static_cast<int64_t>(sp) * p.nt + t) * kCT + q4));
+            a0.x += u.x; a0.y += u.y; a0.z += u.z; a0.w += u.w;
+        }
+        const float v[4] = {a0.x, a0.y, a0.z, a0.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int col = q4 + j;
+            const int cb = bx * kTileBytes + (col & 127);
+            const int oc = (BITS == 4 && col >= 128) ? p.R + cb : cb;
+            if (cb >= p.R || oc >= p.N || tok >= p.M) continue;
+            float* out = p.y + static_cast<int64_t>(tok) * p.N + oc;
+            float r = fmaf(p.alpha, v[j], p.accumulate ? *out : 0.0f);
+            if (p.bias != nullptr) r += p.bias[oc];
+            if (p.lora.p != nullptr) r += lora_term(p.lora, tok, oc, p.N);
+            *out = r;
+        }
+    }
+}
+
 // x (fp32 [M x K]) -> bf16, 8 elements per thread (K % 8 == 0).
 __global__ void x_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ xb, int64_t n8) {
+    dev::pdl_launch_dependents();
+    dev::pdl_wait();  // x is the previous kernel's output
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n8) return;
     const float4 a = __ldg(reinterpret_cast<const float4*>(x) + 2 * i);
@@ -481,8 +562,12 @@ size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 // K-splits: up to one CTA per SM, at most kMaxSplits splits of at least
 // kMinSplitBlocks K-blocks each (overridable for tuning).
-int kMinSplitBlocks = [] { const char* v = std::getenv("KT_GEMM_MIN_SPLIT_BLOCKS"); return v ? std::max(1, std::atoi(v)) : 8; }();
-int kMaxSplits = [] { const char* v = std::getenv("KT_GEMM_MAX_SPLITS"); return v ? std::max(1, std::atoi(v)) : 8; }();
+// Measured on B200 with the split reduction on its own kernel: at least 2
+// blocks and at most 16 splits was the fastest setting over decode (m 16-64)
+// and prefill (m 512) shapes; 8 blocks per split left small weights on a
+// handful of SMs (2x slower at m 16-64).
+int kMinSplitBlocks = [] { const char* v = std::getenv("KT_GEMM_MIN_SPLIT_BLOCKS"); return v ? std::max(1, std::atoi(v)) : 2; }();
+int kMaxSplits = [] { const char* v = std::getenv("KT_GEMM_MAX_SPLITS"); return v ? std::max(1, std::atoi(v)) : 16; }();
 int splits_for(const QView& w, int m, int sm_count) {
     const int tiles = (w.bytes_per_row + kTileBytes - 1) / kTileBytes;
     const int ttiles = (m + nt_for(m) - 1) / nt_for(m);
@@ -494,6 +579,31 @@ int splits_for(const QView& w, int m, int sm_count) {
 }
 
 size_t x_bytes(const QView& w, int m) { return align256(static_cast<size_t>(m) * w.rows * 2); }
+
+// Split-K partials of at least this many token rows x splits per tile are
+// summed by split_reduce_kernel instead of the tile's last CTA.  Measured on
+// B200, the separate kernel was as fast or faster at every m >= 16 (the last
+// CTA of a tile reads S partial tiles alone: 2 MB at m = 512, S = 8), so by
+// default it takes every split; a larger value keeps small partials on the
+// last-CTA path.
+int kReduceKernelMin = [] { const char* v = std::getenv("KT_GEMM_REDUCE_MIN"); return v ? std::max(1, std::atoi(v)) : 16; }();
+
+// cudaLaunchKernelEx with programmatic dependent launch allowed.
+template <typename... Params, typename... Args>
+cudaError_t launch_chained(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                           Args... args) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, kernel, static_cast<Params>(args)...);
+}
 
 }  // namespace
 
@@ -521,8 +631,8 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(ws + kWorkspaceReservedBytes);
     const int64_t n8 = static_cast<int64_t>(a.m) * w.rows / 8;
-    x_to_bf16_kernel<<<static_cast<unsigned>((n8 + 255) / 256), 256, 0, s>>>(a.a, xb, n8);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_chained(x_to_bf16_kernel, dim3(static_cast<unsigned>((n8 + 255) / 256)), dim3(256), 0, s,
+                                   a.a, xb, n8);
     if (e != cudaSuccess) return e;
 
     GemmParams p{};
@@ -552,6 +662,7 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
     const int S = splits_for(w, a.m, sm_count);
     p.tickets = reinterpret_cast<int32_t*>(ws + kGemmTicketOffset);
     p.partials = reinterpret_cast<float*>(ws + kWorkspaceReservedBytes + x_bytes(w, a.m));
+    p.reduce_kernel = S > 1 && p.nt * S >= kReduceKernelMin ? 1 : 0;
 
     alignas(64) CUtensorMap tmap_x;
     if (!encode_tmap_2d(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, static_cast<uint64_t>(w.rows),
@@ -562,8 +673,12 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
     const dim3 grid((w.bytes_per_row + kTileBytes - 1) / kTileBytes, (a.m + p.nt - 1) / p.nt, S);
-    kernel<<<grid, kThreads, kSmemBytes, s>>>(*w.tmap_raw64, tmap_x, p);
-    return cudaGetLastError();
+    e = launch_chained(kernel, grid, dim3(kThreads), kSmemBytes, s, *w.tmap_raw64, tmap_x, p);
+    if (e != cudaSuccess || !p.reduce_kernel) return e;
+    const int64_t quads = static_cast<int64_t>(grid.x) * grid.y * p.nt * (w.bits == 4 ? 64 : 32);
+    const int blocks = static_cast<int>(std::min<int64_t>((quads + 255) / 256, static_cast<int64_t>(sm_count) * 8));
+    return launch_chained(w.bits == 4 ? split_reduce_kernel<4> : split_reduce_kernel<8>, dim3(blocks), dim3(256), 0,
+                          s, p, static_cast<int>(grid.x), static_cast<int>(grid.y), S);
 }
 
 }  // namespace kt

@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(256) quantize_int8_kernel(const float* __restr
     }
     if (nan_seen) atomicOr(status, 1);
     }
+    __threadfence();  // weight bytes visible GPU-wide before exit: matmuls read weights before their PDL wait
 }
 
 // Scale and zero point of one INT4 column over the group rows (:297-308).
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(256) quantize_int4_kernel(const float* __restr
     }
     if (!ok) atomicOr(status, 1);
     }
+    __threadfence();  // weight bytes visible GPU-wide before exit: matmuls read weights before their PDL wait
 }
 
 // QuantizedTensor.dequantizeRow (:188-213): w = scale * q (INT8) or scale * (raw - zero) (INT4).

@@ -14,6 +14,12 @@
 namespace kt {
 namespace {
 
+// The matmul kernels read weights before griddepcontrol.wait (no kernel of a
+// matmul chain writes them); a kernel that does write weight bytes makes its
+// stores visible GPU-wide before its threads exit, so that a matmul launched
+// right after it under programmatic dependent launch reads the new bytes.
+__device__ __forceinline__ void weight_writes_visible() { __threadfence(); }
+
 // One thread per output byte of one row of an INT4 column shard.
 __global__ void repack_int4_columns_kernel(const uint8_t* __restrict__ src, int32_t src_half, int32_t c0,
                                            int32_t n_dst, int32_t dst_half, int32_t rows, uint8_t* __restrict__ dst) {
@@ -31,6 +37,7 @@ __global__ void repack_int4_columns_kernel(const uint8_t* __restrict__ src, int3
         const uint32_t hi = dst_half + b < n_dst ? nibble(c0 + dst_half + b) : 0u;  // odd width: pad nibble 0
         dst[r * dst_half + b] = static_cast<uint8_t>(lo | (hi << 4));
     }
+    weight_writes_visible();
 }
 
 // One thread per output byte of one row of an INT4 weight made of up to
@@ -61,6 +68,7 @@ __global__ void concat_int4_columns_kernel(ConcatSources src, int32_t n_dst, int
         const uint32_t hi = dst_half + b < n_dst ? nibble(dst_half + b) : 0u;
         dst[r * dst_half + b] = static_cast<uint8_t>(lo | (hi << 4));
     }
+    weight_writes_visible();
 }
 
 }  // namespace
