@@ -216,6 +216,80 @@ __device__ __forceinline__ int atomic_add_acq_rel(int32_t* p, int v) {
 }
 __device__ __forceinline__ void workers_barrier() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkers * 32) : "memory"); }
 
+// Epilogue of the worker warps (0-7): warp w reads TMEM lanes 32 (w % 4) .. +32
+// of the low (w < 4) or high (w >= 4) accumulator (INT8: even / odd token
+// chunks of the one accumulator), one tile column per thread, and writes c --
+// or, split-K, its partial tile (summed by the tile's last CTA or by
+// split_reduce_kernel).  acc_hi: TMEM column of the high-nibble accumulator.
+template <int BITS>
+__device__ __forceinline__ void gemm_epilogue(const GemmParams& p, uint32_t tmem, uint32_t acc_hi, uint32_t done,
+                                              bool ok, int tile_b0, int tok0, int* s_last) {
+    constexpr int kCT = BITS == 4 ? 2 * kTileBytes : kTileBytes;  // output columns per CTA
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    dev::pdl_wait();  // c may be read or written by the kernel before this one
+    const bool have = ok && mbar_wait_bounded(done, 0);
+    if (!have && lane == 0) atomicOr(p.err, 1);
+    tc_fence_after();
+    const int quarter = warp & 3;
+    const int half_w = warp >> 2;  // INT4: low / high accumulator; INT8: even / odd token chunks
+    const int c = 32 * quarter + lane;  // 0..127 in the accumulator
+    const int colt = BITS == 4 ? half_w * 128 + c : c;  // column of the CTA's partial tile
+    const uint32_t taddr =
+        tmem + (static_cast<uint32_t>(32 * quarter) << 16) + (BITS == 4 && half_w ? acc_hi : 0);
+    auto emit = [&](int tok, int col, float v) {
+        const int cb = tile_b0 + (col & 127);
+        const int oc = (BITS == 4 && col >= 128) ? p.R + cb : cb;
+        if (!have || cb >= p.R || oc >= p.N || tok >= p.M) return;
+        float* out = p.y + static_cast<int64_t>(tok) * p.N + oc;
+        float r = fmaf(p.alpha, v, p.accumulate ? *out : 0.0f);
+        if (p.bias != nullptr) r += p.bias[oc];
+        if (p.lora.p != nullptr) r += lora_term(p.lora, tok, oc, p.N);
+        *out = r;
+    };
+    const int S = gridDim.z;
+    const int64_t tile_id = static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x;
+    float* parts = p.partials + tile_id * S * (static_cast<int64_t>(p.nt) * kCT);  // [S][nt][kCT]
+    for (int t0 = (BITS == 4 ? 0 : 16 * half_w); t0 < p.nt; t0 += (BITS == 4 ? 16 : 32)) {
+        float v[16];
+        tmem_ld16(taddr + t0, v);  // every lane of the warp takes part (.sync.aligned)
+        if (S == 1) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) emit(tok0 + t0 + j, colt, v[j]);
+        } else {
+            float* mine = parts + static_cast<int64_t>(blockIdx.z) * p.nt * kCT;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) __stcg(mine + (t0 + j) * kCT + colt, v[j]);
+        }
+    }
+    if (S > 1 && !p.reduce_kernel) {
+        // split-K: the last CTA of the tile to arrive sums the partial tiles in
+        // split order (the worker barrier orders every worker's stores before
+        // thread 0's acq_rel atomic, which publishes them at GPU scope).
+        workers_barrier();
+        if (threadIdx.x == 0)
+            *s_last = atomic_add_acq_rel(p.tickets + tile_id, 1) == S - 1;
+        workers_barrier();
+        if (*s_last) {
+            // thread: 4 adjacent columns of one token at a time, tokens strided
+            constexpr int kQuads = kCT / 4;
+            const int q4 = (threadIdx.x % kQuads) * 4;
+#pragma unroll 2
+            for (int t = threadIdx.x / kQuads; t < p.nt; t += kWorkers * 32 / kQuads) {
+                float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int sp = 0; sp < S; ++sp) {
+                    const float4 u = __ldcg(reinterpret_cast<const float4*>(
+                        parts + (static_cast<int64_t>(sp) * p.nt + t) * kCT + q4));
+                    a0.x += u.x; a0.y += u.y; a0.z += u.z; a0.w += u.w;
+                }
+                emit(tok0 + t, q4, a0.x); emit(tok0 + t, q4 + 1, a0.y);
+                emit(tok0 + t, q4 + 2, a0.z); emit(tok0 + t, q4 + 3, a0.w);
+            }
+            if (threadIdx.x == 0) p.tickets[tile_id] = 0;  // ready for the next launch on this workspace
+        }
+    }
+}
+
 // BITS = 4: a CTA's 128 packed bytes are 256 output columns (two A tiles, two
 // accumulators); BITS = 8: 128 output columns (one A tile, one accumulator).
 template <int BITS>
@@ -424,69 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(full_a(s));
         }
-        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +32 of the low
-        // (w < 4) or high (w >= 4) accumulator: one tile column per thread.
-        dev::pdl_wait();  // c may be read or written by the kernel before this one
-        const bool have = ok && mbar_wait_bounded(done, 0);
-        if (!have && lane == 0) atomicOr(p.err, 1);
-        tc_fence_after();
-        const int quarter = warp & 3;
-        const int half_w = warp >> 2;  // INT4: low / high accumulator; INT8: even / odd token chunks
-        const int c = 32 * quarter + lane;  // 0..127 in the accumulator
-        const int colt = BITS == 4 ? half_w * 128 + c : c;  // column of the CTA's partial tile
-        const uint32_t taddr =
-            tmem + (static_cast<uint32_t>(32 * quarter) << 16) + (BITS == 4 && half_w ? p.nt_cols : 0);
-        auto emit = [&](int tok, int col, float v) {
-            const int cb = tile_b0 + (col & 127);
-            const int oc = (BITS == 4 && col >= 128) ? p.R + cb : cb;
-            if (!have || cb >= p.R || oc >= p.N || tok >= p.M) return;
-            float* out = p.y + static_cast<int64_t>(tok) * p.N + oc;
-            float r = fmaf(p.alpha, v, p.accumulate ? *out : 0.0f);
-            if (p.bias != nullptr) r += p.bias[oc];
-            if (p.lora.p != nullptr) r += lora_term(p.lora, tok, oc, p.N);
-            *out = r;
-        };
-        const int S = gridDim.z;
-        const int64_t tile_id = static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x;
-        float* parts = p.partials + tile_id * S * (static_cast<int64_t>(p.nt) * kCT);  // [S][nt][kCT]
-        for (int t0 = (BITS == 4 ? 0 : 16 * half_w); t0 < p.nt; t0 += (BITS == 4 ? 16 : 32)) {
-            float v[16];
-            tmem_ld16(taddr + t0, v);  // every lane of the warp takes part (.sync.aligned)
-            if (S == 1) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) emit(tok0 + t0 + j, colt, v[j]);
-            } else {
-                float* mine = parts + static_cast<int64_t>(blockIdx.z) * p.nt * kCT;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) __stcg(mine + (t0 + j) * kCT + colt, v[j]);
-            }
-        }
-        if (S > 1 && !p.reduce_kernel) {
-            // split-K: the last CTA of the tile to arrive sums the partial tiles in
-            // split order (the worker barrier orders every worker's stores before
-            // thread 0's acq_rel atomic, which publishes them at GPU scope).
-            workers_barrier();
-            if (threadIdx.x == 0)
-                s_last = atomic_add_acq_rel(p.tickets + tile_id, 1) == S - 1;
-            workers_barrier();
-            if (s_last) {
-                // thread: 4 adjacent columns of one token at a time, tokens strided
-                constexpr int kQuads = kCT / 4;
-                const int q4 = (threadIdx.x % kQuads) * 4;
-#pragma unroll 2
-                for (int t = threadIdx.x / kQuads; t < p.nt; t += kWorkers * 32 / kQuads) {
-                    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int sp = 0; sp < S; ++sp) {
-                        const float4 u = __ldcg(reinterpret_cast<const float4*>(
-                            parts + (static_cast<int64_t>(sp) * p.nt + t) * kCT + q4));
-                        a0.x += u.x; a0.y += u.y; a0.z += u.z; a0.w += u.w;
-                    }
-                    emit(tok0 + t, q4, a0.x); emit(tok0 + t, q4 + 1, a0.y);
-                    emit(tok0 + t, q4 + 2, a0.z); emit(tok0 + t, q4 + 3, a0.w);
-                }
-                if (threadIdx.x == 0) p.tickets[tile_id] = 0;  // ready for the next launch on this workspace
-            }
-        }
+        gemm_epilogue<BITS>(p, tmem, p.nt_cols, done, ok, tile_b0, tok0, &s_last);
     }
     tc_fence_before();
     __syncthreads();
@@ -494,6 +506,292 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols)
                      : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// INT4 with the dequantized weights in tensor memory (the "A from TMEM" form of
+// tcgen05.mma), for tiles of at most 128 tokens.  Same mapping, split-K and
+// epilogue as gemm_tc_kernel; what changes is where the A tiles live and how
+// the pipeline is cut.  In gemm_tc_kernel every 64-row K-block costs ~1,000
+// shared-memory wavefronts (byte loads of the packed tile, scale loads by all
+// eight warps, 32 KB of A stores and the MMA's A reads) and its 3-stage ring
+// exposes the TMA latency (~1 us) on every block.  Here:
+//   * an 8-stage shared-memory ring of packed bytes + x tiles, decoupled from
+//     a 4-stage ring of A tiles in tensor memory (own full / free barriers);
+//   * 16 dequantizing warps in two groups of 8 that take alternate K-blocks
+//     (a warp's chain of loads, shuffles, conversions and tcgen05.st takes
+//     ~0.5 us; two blocks in flight hide half of it).  They write A with
+//     tcgen05.st (TMEM lane L = A row L = byte column L of the tile): warp w of
+//     a group takes TMEM lanes 32 (w % 4) .. +32 and rows 32 (w / 4) .. +32;
+//   * the group scales and zero points are read by the dequantizing lanes
+//     straight from global memory (one block of their own ahead): issuing them
+//     as four small bulk copies per block cost the single producer thread
+//     ~0.3 us per block, which bounded the pipeline;
+//   * conflict-free 32-bit loads of the packed bytes: lane (i = lane % 4,
+//     j = lane / 4) loads word 8 (w % 4) + j of rows b + 2i (b = 0, 1) of an
+//     8-row atom -- with the 128-byte swizzle the 32 lanes hit 32 distinct
+//     banks -- and a 4 x 4 byte transpose across lanes 4j .. 4j + 3 (two
+//     shuffles, two PRMT) leaves lane L with byte column L of rows b, b + 2,
+//     b + 4, b + 6.  A PRMT pairs rows (2p, 2p + 1) into the two halves of a
+//     word and the nibbles become bf16 exactly as in gemm_tc_kernel.
+// TMEM columns: low accumulator 0 .. nt, high 128 .. 128 + nt, A tiles of A-stage
+// a at 256 + 64 a (low nibbles) and 256 + 64 a + 32 (high): all 512 columns, so
+// one CTA per SM (its shared memory is more than half an SM's).
+constexpr int kTsMaxNT = 128;
+constexpr int kTsRing = 8;             // shared-memory stages (packed bytes + x)
+constexpr int kTsAStages = 4;          // tensor-memory stages (A tiles)
+constexpr int kTsDequant = 16;         // dequantizing warps, two groups of 8 (the first 8 also run the epilogue)
+constexpr int kTsGroupWarps = kTsDequant / 2;
+constexpr int kTsProducerWarp = kTsDequant;
+constexpr int kTsMmaWarp = kTsDequant + 1;
+constexpr int kTsThreads = (kTsDequant + 2) * 32;
+constexpr int kTsRawBytes = kBK * kTileBytes;        // two 32-row TMA boxes, 128-byte swizzle
+constexpr int kTsXBytes = kTsMaxNT * kBK * 2;
+constexpr int kTsStageBytes = kTsRawBytes + kTsXBytes;
+constexpr uint32_t kTsAccHi = 128;
+constexpr uint32_t kTsACol = 256;
+constexpr int kTsBarBytes = 512;
+constexpr size_t kTsSmemBytes = 1024 + static_cast<size_t>(kTsRing) * kTsStageBytes + kTsBarBytes;
+static_assert(kTsStageBytes % 1024 == 0 && kTsRawBytes % 1024 == 0, "swizzled tiles start on 1024-byte boundaries");
+static_assert(2 * kTsSmemBytes > 233472 && kTsSmemBytes <= 232448, "exactly one CTA per SM");
+static_assert(kTsACol + 64 * kTsAStages <= 512, "tensor memory columns");
+static_assert(8 * (3 * kTsRing + 2 * kTsAStages + 1) + 4 <= kTsBarBytes, "barrier area");
+
+// A from tensor memory: D (TMEM) += A (TMEM) . B (shared memory descriptor).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// 16 consecutive 32-bit TMEM columns of this warp's 32 lanes from registers.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+// The group constants one dequantizing lane needs for a K-block: scale and
+// zero point of its low- and high-nibble columns.
+struct ColumnConstants {
+    float s_lo, s_hi;
+    uint32_t z_lo, z_hi;
+};
+__device__ __forceinline__ ColumnConstants load_constants(const GemmParams& p, int row, int col) {
+    const int64_t g = static_cast<int64_t>(min(row / p.gs, p.G - 1)) * p.N;
+    ColumnConstants c;
+    c.s_lo = __ldg(p.scales + g + col);
+    c.s_hi = __ldg(p.scales + g + p.R + col);
+    c.z_lo = __ldg(p.zeros + g + col);
+    c.z_hi = __ldg(p.zeros + g + p.R + col);
+    return c;
+}
+// 4 x 4 byte transpose across lanes 4j .. 4j + 3 (li = lane % 4): lane li holds
+// bytes [a(li,0) .. a(li,3)] and returns [a(0,li) .. a(3,li)].
+__device__ __forceinline__ uint32_t transpose4x4(uint32_t w, int li) {
+    const uint32_t x = __shfl_xor_sync(0xffffffffu, w, 1);
+    const uint32_t v = prmt(w, x, (li & 1) ? 0x3715u : 0x6240u);
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, v, 2);
+    return prmt(v, y, (li & 2) ? 0x3276u : 0x5410u);
+}
+
+__global__ void __launch_bounds__(kTsThreads, 1)
+    gemm_ts_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                   GemmParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tile_b0 = blockIdx.x * kTileBytes;
+    const int tok0 = blockIdx.y * p.nt;
+    const int kb_total = (p.K + kBK - 1) / kBK;
+    const int kb_begin = static_cast<int>(static_cast<int64_t>(blockIdx.z) * kb_total / gridDim.z);
+    const int kb_end = static_cast<int>(static_cast<int64_t>(blockIdx.z + 1) * kb_total / gridDim.z);
+    const int n_kb = kb_end - kb_begin;
+
+    const uint32_t raw_s = smem_u32(smem_raw);
+    const uint32_t base = (raw_s + 1023u) & ~1023u;
+    unsigned char* gbase = smem_raw + (base - raw_s);
+    const uint32_t bars = base + kTsRing * kTsStageBytes;
+    auto full_w = [&](int s) { return bars + 8 * s; };                       // ring slot s: packed bytes
+    auto full_x = [&](int s) { return bars + 8 * (kTsRing + s); };           // ring slot s: x tile
+    auto empty = [&](int s) { return bars + 8 * (2 * kTsRing + s); };        // ring slot s consumed by the MMAs
+    auto full_a = [&](int a) { return bars + 8 * (3 * kTsRing + a); };       // A-stage a written
+    auto free_a = [&](int a) { return bars + 8 * (3 * kTsRing + kTsAStages + a); };  // A-stage a read by the MMAs
+    const uint32_t done = bars + 8 * (3 * kTsRing + 2 * kTsAStages);
+    uint32_t* tmem_slot =
+        reinterpret_cast<uint32_t*>(gbase + kTsRing * kTsStageBytes + 8 * (3 * kTsRing + 2 * kTsAStages + 1));
+    const int tile_cols = min(kTileBytes, p.R - tile_b0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTsRing; ++s) {
+            mbar_init(full_w(s), 1);
+            mbar_init(full_x(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int a = 0; a < kTsAStages; ++a) {
+            mbar_init(full_a(a), kTsGroupWarps);
+            mbar_init(free_a(a), 1);
+        }
+        mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    dev::pdl_launch_dependents();
+
+    if (warp == kTsProducerWarp) {
+        // lane 0 arms full_w and loads rows 0-31 of the packed tile, lane 1 rows
+        // 32-63 (a copy landing before lane 0's arming arrive cannot complete the
+        // phase: that arrive is still pending), lane 2 arms full_x and loads x
+        const uint32_t xtx = static_cast<uint32_t>(p.nt * kBK * 2);
+        auto issue = [&](int i, bool w, bool x) {
+            const int s = i % kTsRing;
+            const uint32_t st = base + s * kTsStageBytes;
+            const int kb = kb_begin + i;
+            if (w) {
+                if (lane == 0) {
+                    mbar_expect_tx(full_w(s), kTsRawBytes);
+                    tma_load_2d(st, &tmap_w, tile_b0, kb * kBK, full_w(s));
+                } else if (lane == 1) {
+                    tma_load_2d(st + kTsRawBytes / 2, &tmap_w, tile_b0, kb * kBK + kBK / 2, full_w(s));
+                }
+            }
+            if (x && lane == 2) {
+                mbar_expect_tx(full_x(s), xtx);
+                tma_load_2d(st + kTsRawBytes, &tmap_x, kb * kBK, tok0, full_x(s));
+            }
+        };
+        // weights of the first stages before the wait (no kernel of the chain
+        // writes them), x only after it
+        const int pre = min(n_kb, kTsRing);
+        for (int i = 0; i < pre; ++i) issue(i, true, false);
+        dev::pdl_wait();
+        for (int i = 0; i < pre; ++i) issue(i, false, true);
+        int issued = pre;
+        for (int i = pre; i < n_kb; ++i) {
+            const int s = i % kTsRing;
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(empty(s), ((i / kTsRing) - 1) & 1))) {
+                if (lane == 0) atomicOr(p.err, 1);
+                break;
+            }
+            issue(i, true, true);
+            ++issued;
+        }
+        // the last copies issued into each slot have landed before the CTA may exit
+        if (lane == 0) {
+            for (int i = max(0, issued - kTsRing); i < issued; ++i) {
+                if (!mbar_wait_bounded(full_w(i % kTsRing), (i / kTsRing) & 1)) break;
+                if (!mbar_wait_bounded(full_x(i % kTsRing), (i / kTsRing) & 1)) break;
+            }
+        }
+    } else if (warp == kTsMmaWarp) {
+        if (lane == 0) {
+            for (int i = 0; i < n_kb; ++i) {
+                const int s = i % kTsRing, a = i % kTsAStages;
+                if (!mbar_wait_bounded(full_x(s), (i / kTsRing) & 1) ||
+                    !mbar_wait_bounded(full_a(a), (i / kTsAStages) & 1)) {
+                    atomicOr(p.err, 1);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t xs = base + s * kTsStageBytes + kTsRawBytes;
+                const uint32_t a_lo = tmem + kTsACol + 64 * a;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                    const uint64_t bdesc = umma_desc_sw128(xs + kk * 32);
+                    const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+                    umma_bf16_ts(tmem, a_lo + 8 * kk, bdesc, p.idesc, acc);
+                    umma_bf16_ts(tmem + kTsAccHi, a_lo + 32 + 8 * kk, bdesc, p.idesc, acc);
+                }
+                umma_commit(empty(s));   // ring slot free once these MMAs have read it
+                umma_commit(free_a(a));  // and the A-stage
+            }
+            umma_commit(done);
+            if (!mbar_wait_bounded(done, 0)) atomicOr(p.err, 1);
+        }
+    } else {
+        const int grp = warp / kTsGroupWarps;  // this warp's K-blocks: i = grp, grp + 2, ...
+        const int wg = warp % kTsGroupWarps;
+        const int q = wg & 3;   // TMEM lanes / byte columns 32 q .. 32 q + 31
+        const int h = wg >> 2;  // rows 32 h .. 32 h + 31 of each K-block
+        const int li = lane & 3, lj = lane >> 2;
+        const int bc = 32 * q + lane;  // this lane's byte column after the transpose
+        const int wc = 8 * q + lj;     // the 32-bit word column this lane loads
+        const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
+        // columns beyond the tile's bytes (last tile) read column 0's constants:
+        // their A rows only reach accumulator rows that are never stored
+        const int col = tile_b0 + (bc < tile_cols ? bc : 0);
+        bool ok = true;
+        ColumnConstants cc{};
+        if (grp < n_kb) cc = load_constants(p, (kb_begin + grp) * kBK + 32 * h, col);
+        for (int i = grp; i < n_kb; i += 2) {
+            const int s = i % kTsRing, as = i % kTsAStages;
+            const ColumnConstants cur = cc;
+            if (i + 2 < n_kb) cc = load_constants(p, (kb_begin + i + 2) * kBK + 32 * h, col);  // next block's, early
+            // warp-uniform waits: the tcgen05.st below is .sync.aligned
+            bool got = mbar_wait_bounded(full_w(s), (i / kTsRing) & 1);
+            if (i >= kTsAStages) got = got && mbar_wait_bounded(free_a(as), ((i / kTsAStages) - 1) & 1);
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0) atomicOr(p.err, 1);
+                ok = false;
+                break;
+            }
+            tc_fence_after();  // the MMAs that read this A-stage before have completed
+            const unsigned char* raw = gbase + s * kTsStageBytes;
+            const uint32_t s2_lo = bf2_splat(cur.s_lo), s2_hi = bf2_splat(cur.s_hi);
+            const uint32_t zb_lo = bf2_splat(128.0f + static_cast<float>(cur.z_lo));
+            const uint32_t zb_hi = bf2_splat(128.0f + static_cast<float>(cur.z_hi));
+            uint32_t lo[16], hi[16];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                uint32_t t[2];
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    const int r = 32 * h + 8 * a + b + 2 * li;  // (r & 7) == b + 2 li
+                    const uint32_t w = *reinterpret_cast<const uint32_t*>(
+                        raw + r * kTileBytes + ((((wc >> 2) ^ (b + 2 * li)) << 4) | ((wc & 3) << 2)));
+                    t[b] = transpose4x4(w, li);  // byte column bc, rows 32h + 8a + b + {0, 2, 4, 6}
+                }
+#pragma unroll
+                for (int pp = 0; pp < 4; ++pp) {
+                    // rows 8a + 2pp (low half of the word) and 8a + 2pp + 1 (high half)
+                    const uint32_t pr =
+                        prmt(t[0], t[1], static_cast<uint32_t>(pp | (pp << 4) | ((4 + pp) << 8) | ((4 + pp) << 12)));
+                    const uint32_t ql = lop3_and_or(pr, 0x000F000Fu, 0x43004300u);
+                    const uint32_t qh = lop3_and_or(pr >> 4, 0x000F000Fu, 0x43004300u);
+                    lo[4 * a + pp] = bf2_sub_mul(ql, zb_lo, s2_lo);
+                    hi[4 * a + pp] = bf2_sub_mul(qh, zb_hi, s2_hi);
+                }
+            }
+            const uint32_t a_col = tmem + lane_base + kTsACol + 64 * as + 16 * h;
+            tmem_st16(a_col, lo);
+            tmem_st16(a_col + 32, hi);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full_a(as));
+        }
+        if (warp < kWorkers) gemm_epilogue<4>(p, tmem, kTsAccHi, done, ok, tile_b0, tok0, &s_last);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
     }
 }
 
@@ -556,7 +854,20 @@ __global__ void x_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __r
     reinterpret_cast<uint4*>(xb)[i] = o;
 }
 
-int nt_for(int m) { return std::min(kMaxNT, (m + 15) / 16 * 16); }
+// INT4 weights with the 32-row swizzled TMA descriptor take gemm_ts_kernel up
+// to m = 128 (one token tile); above, gemm_tc_kernel's 256-token tiles
+// dequantize each weight tile half as often (measured faster at m = 512).
+// KT_GEMM_TS=0 keeps every m on gemm_tc_kernel, for comparison.
+bool use_ts(const QView& w, int m) {
+    static const bool on = [] {
+        const char* v = std::getenv("KT_GEMM_TS");
+        return v == nullptr || std::atoi(v) != 0;
+    }();
+    return on && w.bits == 4 && w.tmap_mma != nullptr && m <= kTsMaxNT;
+}
+
+// Tokens per CTA (the MMA's N): m rounded up to 16, at most 256.
+int nt_for(const QView& w, int m) { return std::min(kMaxNT, (m + 15) / 16 * 16); }
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
@@ -570,7 +881,7 @@ int kMinSplitBlocks = [] { const char* v = std::getenv("KT_GEMM_MIN_SPLIT_BLOCKS
 int kMaxSplits = [] { const char* v = std::getenv("KT_GEMM_MAX_SPLITS"); return v ? std::max(1, std::atoi(v)) : 16; }();
 int splits_for(const QView& w, int m, int sm_count) {
     const int tiles = (w.bytes_per_row + kTileBytes - 1) / kTileBytes;
-    const int ttiles = (m + nt_for(m) - 1) / nt_for(m);
+    const int ttiles = (m + nt_for(w, m) - 1) / nt_for(w, m);
     const int kb_total = (w.rows + kBK - 1) / kBK;
     int s = std::max(1, sm_count / (tiles * ttiles));
     s = std::min({s, std::max(1, kb_total / kMinSplitBlocks), kMaxSplits});
@@ -618,8 +929,8 @@ size_t gemm_tc_workspace_bytes(const QView& w, int32_t m, int sm_count) {
     size_t bytes = kWorkspaceReservedBytes + x_bytes(w, m);
     if (S > 1) {
         const size_t tiles = (w.bytes_per_row + kTileBytes - 1) / kTileBytes;
-        const size_t ttiles = (m + nt_for(m) - 1) / nt_for(m);
-        bytes += tiles * ttiles * S * static_cast<size_t>(nt_for(m)) * 256 * sizeof(float);
+        const size_t ttiles = (m + nt_for(w, m) - 1) / nt_for(w, m);
+        bytes += tiles * ttiles * S * static_cast<size_t>(nt_for(w, m)) * 256 * sizeof(float);
     }
     return bytes;
 }
@@ -647,7 +958,7 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
     p.R = w.bytes_per_row;
     p.gs = w.group_size;
     p.G = w.groups;
-    p.nt = nt_for(a.m);
+    p.nt = nt_for(w, a.m);
     p.nt_cols = p.nt;
     int cols = 32;
     while (cols < (w.bits == 4 ? 2 : 1) * p.nt) cols *= 2;
@@ -669,11 +980,15 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
                         static_cast<uint64_t>(a.m), static_cast<uint64_t>(w.rows) * 2, kBK,
                         static_cast<uint32_t>(p.nt), CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    auto kernel = w.bits == 4 ? gemm_tc_kernel<4> : gemm_tc_kernel<8>;
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    const bool ts = use_ts(w, a.m);
+    if (ts) p.nt_cols = kTsAccHi;
+    auto kernel = ts ? gemm_ts_kernel : w.bits == 4 ? gemm_tc_kernel<4> : gemm_tc_kernel<8>;
+    const size_t smem = ts ? kTsSmemBytes : kSmemBytes;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     const dim3 grid((w.bytes_per_row + kTileBytes - 1) / kTileBytes, (a.m + p.nt - 1) / p.nt, S);
-    e = launch_chained(kernel, grid, dim3(kThreads), kSmemBytes, s, *w.tmap_raw64, tmap_x, p);
+    e = launch_chained(kernel, grid, dim3(ts ? kTsThreads : kThreads), smem, s, ts ? *w.tmap_mma : *w.tmap_raw64,
+                       tmap_x, p);
     if (e != cudaSuccess || !p.reduce_kernel) return e;
     const int64_t quads = static_cast<int64_t>(grid.x) * grid.y * p.nt * (w.bits == 4 ? 64 : 32);
     const int blocks = static_cast<int>(std::min<int64_t>((quads + 255) / 256, static_cast<int64_t>(sm_count) * 8));

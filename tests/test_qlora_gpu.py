@@ -60,13 +60,16 @@ CASES = [(4, 256, 333, 1), (4, 512, 1024, 3), (8, 256, 333, 1), (8, 384, 640, 6)
 def test_lora_forward_matches_oracle(kt, oracle, bits, k, n, m, rank):
     layer, q = _layer(kt, oracle, k, n, bits, seed=k + n + m)
     lora = _adapter(layer, rank, seed=rank)
-    x = torch.randn(m, k, device="cuda")
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(k * m + rank)).cuda()
     out = lora(x)
     base = layer(x)
     torch.cuda.synchronize()
     ref, ref_p = QO.lora_forward(x.cpu().numpy(), q, layer.bias.cpu().numpy(), lora.lora_a.cpu().numpy(),
                                  lora.lora_b.cpu().numpy(), lora.scaling)
-    assert _rel(lora._projected[:m].cpu().numpy(), ref_p) <= 1e-5
+    # fp32 sums in another order: bounded relative to sum |x_k A_kr| (a projection
+    # that cancels to a small value is not held to 1e-5 of itself)
+    scale_p = np.abs(x.cpu().numpy()).astype(np.float64) @ np.abs(lora.lora_a.cpu().numpy()).astype(np.float64)
+    assert np.abs(lora._projected[:m].cpu().numpy() - ref_p).max() <= 1e-5 * scale_p.max()
     tensor_core = _tensor_core(layer, m)
     assert _rel(out.cpu().numpy(), ref) <= (2e-2 if tensor_core else 1e-3)
     # the epilogue's low-rank term alone, against float64 (isolates it from the base path's rounding)
@@ -91,8 +94,9 @@ def test_fresh_adapter_leaves_the_base_output_unchanged(kt, oracle):
 def test_lora_backward_matches_oracle(kt, oracle, bits, k, n, m, rank):
     layer, q = _layer(kt, oracle, k, n, bits, seed=k * m)
     lora = _adapter(layer, rank, seed=7)
-    x = torch.randn(m, k, device="cuda")
-    dy = torch.randn(m, n, device="cuda")
+    g_in = torch.Generator().manual_seed(k + n * m + rank)
+    x = torch.randn(m, k, generator=g_in).cuda()
+    dy = torch.randn(m, n, generator=g_in).cuda()
     lora(x)
     dx = torch.full((m, k), 0.5, device="cuda")
     lora.backward(x, dy, dx, accumulate_dx=True)
