@@ -384,11 +384,13 @@ def test_int4_tensor_core_gemv_split_k_workspace_is_reused_safely(kt, oracle):
 
 @pytest.mark.parametrize("k,n,g", [(2048, 5632, 64), (4096, 1024, 64), (896, 4864, 64), (960, 2048, 96),
                                    (1024, 4096, 32), (4864, 896, 64)])
-@pytest.mark.parametrize("m", [9, 16, 64, 128, 200, 256, 512])
+@pytest.mark.parametrize("m", [9, 16, 24, 40, 64, 128, 200, 256, 512])
 def test_int4_tensor_core_gemm_matches_the_oracle(kt, oracle, m, k, n, g):
-    """The tcgen05 bf16 GEMM (m >= 9): partial token tiles (9, 200), two token
-    tiles (512), a K that is not a multiple of the 64-row stage (960), group
-    sizes 32 / 64 / 96, accumulate / alpha / bias, within the bf16 tolerance."""
+    """The bf16 tcgen05 GEMMs (m >= 9): A in tensor memory for m <= 128
+    (partial token tiles at 9, 24, 40), A in shared memory above (partial token
+    tiles at 200, two token tiles at 512), a K that is not a multiple of the
+    64-row stage (960), group sizes 32 / 64 / 96, accumulate / alpha / bias,
+    within the bf16 tolerance."""
     from kotensor_b200 import _lib
     rng = np.random.default_rng(k * 3 + n + m + g)
     w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
