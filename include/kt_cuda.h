@@ -165,6 +165,15 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
 kt_status kt_allgather_columns(kt_comm* comm, const float* y_shard_dev, float* y_full_dev, int32_t m,
                                int32_t n_shard, void* stream);
 
+/* Greedy decoding over a column-parallel lm head (argmaxOfLastToken,
+ * Transformer.kt:255-266, across shards): logits_shard_dev [rows x n_shard] holds
+ * global columns [col_begin, col_begin + n_shard) of the logits on this rank;
+ * out_dev[row] (device int32) receives, on every rank, the column of the largest
+ * logit above -1e9 over all ranks, the lowest column among equal ones, 0 if none
+ * -- what kt_argmax gives on the whole row.  One ncclAllGather of rows x 8 bytes. */
+kt_status kt_argmax_column_parallel(kt_comm* comm, const float* logits_shard_dev, int32_t rows, int32_t n_shard,
+                                    int32_t col_begin, int32_t* out_dev, void* stream);
+
 /* QuantizedTensor.dequantize(), QuantizedTensor.kt:243-249: out_dev fp32 [rows x columns]. */
 kt_status kt_dequantize(kt_ctx* ctx, const kt_qweight* w, float* out_dev, void* stream);
 

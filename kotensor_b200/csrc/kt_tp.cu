@@ -104,6 +104,60 @@ __global__ void gather_columns_kernel(const float* __restrict__ gathered, float*
 
 int blocks_for(int64_t total) { return static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16)); }
 
+// Greedy decoding over an lm head split along N (argmaxOfLastToken,
+// Transformer.kt:255-266, kept across shards): per row the largest logit above
+// -1e9 and, among equal ones, the lowest column.  Stage 1 on every rank: the
+// best of its shard as the pair {value bits, global column} (column INT_MAX
+// when no logit is above -1e9).  Stage 2, after an all-gather of the pairs:
+// the ranks' pairs merged in rank order with the same rule, 0 when none.
+constexpr int kArgmaxThreads = 256;
+constexpr int32_t kNoColumn = 0x7fffffff;
+__device__ __forceinline__ void better_pair(float& bv, int32_t& bi, float ov, int32_t oi) {
+    if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+    }
+}
+__global__ void __launch_bounds__(kArgmaxThreads) shard_argmax_kernel(const float* __restrict__ logits, int32_t n_shard,
+                                                                      int32_t col_begin, int32_t* __restrict__ pairs) {
+    __shared__ float sv[kArgmaxThreads];
+    __shared__ int32_t si[kArgmaxThreads];
+    const int row = blockIdx.x;
+    float best = -1e9f;
+    int32_t idx = kNoColumn;
+    for (int v = threadIdx.x; v < n_shard; v += kArgmaxThreads) {
+        const float x = logits[static_cast<int64_t>(row) * n_shard + v];
+        if (x > best) {  // strictly greater: the first (lowest) column of a tie stays
+            best = x;
+            idx = col_begin + v;
+        }
+    }
+    sv[threadIdx.x] = best;
+    si[threadIdx.x] = idx;
+    __syncthreads();
+    for (int st = kArgmaxThreads / 2; st > 0; st >>= 1) {
+        if (threadIdx.x < st) better_pair(sv[threadIdx.x], si[threadIdx.x], sv[threadIdx.x + st], si[threadIdx.x + st]);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        pairs[2 * row] = __float_as_int(sv[0]);
+        pairs[2 * row + 1] = si[0];
+    }
+}
+// gathered [P][rows][2] -> out[row]
+__global__ void merge_argmax_kernel(const int32_t* __restrict__ gathered, int32_t parts, int32_t rows,
+                                    int32_t* __restrict__ out) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= rows) return;
+    float best = -1e9f;
+    int32_t idx = kNoColumn;
+    for (int p = 0; p < parts; ++p) {
+        const int64_t o = (static_cast<int64_t>(p) * rows + row) * 2;
+        better_pair(best, idx, __int_as_float(gathered[o]), gathered[o + 1]);
+    }
+    out[row] = idx == kNoColumn ? 0 : idx;
+}
+
 }  // namespace
 
 struct kt_comm {
@@ -225,6 +279,30 @@ kt_status kt_allgather_columns(kt_comm* comm, const float* y_shard, float* y_ful
     gather_columns_kernel<<<blocks_for(per * comm->nranks), 256, 0, s>>>(gathered, y_full, comm->nranks, m, n_shard);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("gather columns: ") + cudaGetErrorString(e));
+    return KT_OK;
+}
+
+kt_status kt_argmax_column_parallel(kt_comm* comm, const float* logits_shard, int32_t rows, int32_t n_shard,
+                                    int32_t col_begin, int32_t* out, void* stream) {
+    if (!comm || !logits_shard || !out) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (rows <= 0 || n_shard <= 0 || col_begin < 0 || static_cast<int64_t>(col_begin) + n_shard > kNoColumn)
+        return fail_tp(KT_ERR_INVALID_ARGUMENT, "bad column-parallel argmax arguments");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* scratch = nullptr;
+    const size_t pair_words = 2 * static_cast<size_t>(rows);
+    cudaError_t e = comm_scratch(comm, pair_words * (1 + comm->nranks), &scratch);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_OUT_OF_MEMORY, std::string("TP scratch: ") + cudaGetErrorString(e));
+    int32_t* mine = reinterpret_cast<int32_t*>(scratch);
+    int32_t* gathered = mine + pair_words;
+    shard_argmax_kernel<<<rows, kArgmaxThreads, 0, s>>>(logits_shard, n_shard, col_begin, mine);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("shard argmax: ") + cudaGetErrorString(e));
+    // the pairs travel as 32-bit words (a float32 all-gather copies bits)
+    const ncclResult_t r = nccl().all_gather(mine, gathered, pair_words, kNcclFloat32, comm->comm, s);
+    if (r != 0) return nccl_fail(r, "ncclAllGather");
+    merge_argmax_kernel<<<(rows + 127) / 128, 128, 0, s>>>(gathered, comm->nranks, rows, out);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("merge argmax: ") + cudaGetErrorString(e));
     return KT_OK;
 }
 

@@ -21,7 +21,7 @@ from typing import Optional
 import numpy as np
 
 from . import _lib
-from .quantized import Context, QuantizedTensor, _require_f32_device, _stream_of
+from .quantized import Context, QuantizedTensor, _require_f32_device, _stream_of, torch
 
 ROWS, COLUMNS = 0, 1
 
@@ -174,6 +174,24 @@ def allgather_columns(comm: Comm, y_shard, y_full, m: int) -> None:
                                                 ctypes.c_void_p(y_full.data_ptr()), m, ns, _stream_of(y_full)))
 
 
+def argmax_column_parallel(comm: Comm, logits_shard, col_begin: int, out) -> None:
+    """Greedy token per row over an lm head split along N (argmaxOfLastToken,
+    Transformer.kt:255-266, across shards): ``logits_shard`` [rows x n_shard]
+    holds global columns [col_begin, col_begin + n_shard); ``out`` (int32,
+    [rows], on the device) receives on every rank the column of the largest
+    logit above -1e9 over all ranks, the lowest one among equal logits, 0 if
+    none -- the single-GPU argmax of the whole row."""
+    _require_f32_device("logits_shard", logits_shard)
+    if out.dtype != torch.int32 or not out.is_cuda or not out.is_contiguous():
+        raise ValueError("out must be a contiguous int32 CUDA tensor")
+    rows, n_shard = logits_shard.shape
+    if out.numel() < rows:
+        raise ValueError("out too small")
+    _lib.check(_lib.load().kt_argmax_column_parallel(comm.handle, ctypes.c_void_p(logits_shard.data_ptr()), rows,
+                                                     n_shard, int(col_begin), ctypes.c_void_p(out.data_ptr()),
+                                                     _stream_of(out)))
+
+
 class RowParallelQuantizedLinear:
     """QuantizedLinear (QuantizedLinear.kt:18-25) with its weight split along K:
     ``forward_into(x_shard, out)`` takes this rank's K-columns of x."""
@@ -210,3 +228,9 @@ class ColumnParallelQuantizedLinear:
     def gather_into(self, out_shard, out_full):
         allgather_columns(self.comm, out_shard, out_full, out_shard.shape[0])
         return out_full
+
+    def argmax_into(self, out_shard, tokens):
+        """Greedy decoding when this layer is the lm head: the winning global
+        column per row of the sharded logits ``out_shard``, on every rank."""
+        argmax_column_parallel(self.comm, out_shard, self.n_begin, tokens)
+        return tokens

@@ -88,7 +88,34 @@ def _tp_rank(rank, world, port, out_dir):
         parts = [None] * world
         dist.all_gather_object(parts, ycol)
         y_col = np.concatenate(parts, axis=1)
+        # column-parallel greedy argmax: each rank's best (value, global column) pair,
+        # gathered, merged in rank order (larger value, then lower column)
+        lg = rng.standard_normal((4, 90), dtype=np.float32)
+        lg[0, 5] = lg[0, 80] = 9.0   # a tie across the shard boundary
+        lg[1] = -3e9                 # nothing above -1e9: column 0
+        lg[2, 89] = 9.0              # the last column
+        b, e = P.shard_bounds(P.COLUMNS, 90, 1, world, rank)
+        pairs = []
+        for row in lg[:, b:e]:
+            best, idx = np.float32(-1e9), None
+            for j, v in enumerate(row):
+                if v > best:
+                    best, idx = v, b + j
+            pairs.append((best, idx))
+        every = [None] * world
+        dist.all_gather_object(every, pairs)
+        tokens = []
+        for r in range(lg.shape[0]):
+            best, idx = np.float32(-1e9), None
+            for p in range(world):
+                v, i = every[p][r]
+                if i is not None and (v > best or (v == best and i < idx)):
+                    best, idx = v, i
+            tokens.append(0 if idx is None else idx)
         if rank == 0:
+            masked = np.where(lg > np.float32(-1e9), lg, -np.inf)
+            want = [int(np.argmax(m)) if np.isfinite(m).any() else 0 for m in masked]
+            np.save(os.path.join(out_dir, "argmax.npy"), np.array([tokens, want]))
             ref = O.multiply_quantized(x, full, threads=2)
             np.save(os.path.join(out_dir, "ref.npy"), ref)
             np.save(os.path.join(out_dir, "row.npy"), y_row - bias[None, :])
@@ -104,3 +131,5 @@ def test_tensor_parallel_plan_with_gloo(kt, oracle, tmp_path):
     scale = np.abs(ref).max()
     assert np.abs(np.load(tmp_path / "row.npy") - ref).max() <= 1e-5 * scale
     assert np.abs(np.load(tmp_path / "col.npy") - ref).max() <= 1e-5 * scale
+    tokens, want = np.load(tmp_path / "argmax.npy")
+    assert np.array_equal(tokens, want) and want[0] == 5 and want[1] == 0 and want[2] == 89

@@ -1,6 +1,7 @@
 """GPU checks of tensor parallelism: device shards (kt_qweight_shard) against
 the host restatement and the quantized fp32 slices, the NCCL row-parallel
-product and column gather on one rank, and on two GPUs when the box has them."""
+product, column gather and column-parallel greedy argmax on one rank, and on
+two GPUs when the box has them."""
 import os
 import socket
 
@@ -88,6 +89,47 @@ def test_row_parallel_and_gather_on_one_rank(kt):
     assert kt.Context.get().take_error() == 0
 
 
+def _argmax_rule(logits):
+    """argmaxOfLastToken per row: the largest logit above -1e9, the lowest column of a tie, 0 if none."""
+    out = []
+    for row in np.asarray(logits, np.float32):
+        masked = np.where(row > np.float32(-1e9), row, -np.inf)
+        out.append(int(np.argmax(masked)) if np.isfinite(masked).any() else 0)
+    return np.array(out, np.int32)
+
+
+@pytest.mark.parametrize("col_begin", [0, 1000])
+def test_column_parallel_argmax_on_one_rank(kt, col_begin):
+    import ctypes
+    from kotensor_b200 import _lib, parallel as P
+    comm = P.Comm(1, 0, P.Comm.unique_id())
+    try:
+        rows, n = 5, 70001
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(5)
+        logits = torch.randn((rows, n), generator=gen, device="cuda")
+        logits[1, 123] = 100.0
+        logits[1, 4567] = 100.0        # a tie: the lower column wins
+        logits[2] = -2e9               # nothing above -1e9: column 0
+        logits[3, n - 1] = 50.0        # the last column
+        logits[4, :] = 7.0             # all equal: the first column
+        out = torch.full((rows,), -1, dtype=torch.int32, device="cuda")
+        P.argmax_column_parallel(comm, logits, col_begin, out)
+        whole = torch.full((rows,), -1, dtype=torch.int32, device="cuda")
+        ctx = kt.Context.get()
+        _lib.check(_lib.load().kt_argmax(ctx.handle, ctypes.c_void_p(logits.data_ptr()), rows, n,
+                                         ctypes.c_void_p(whole.data_ptr()),
+                                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        torch.cuda.synchronize()
+        want = _argmax_rule(logits.cpu().numpy())
+        assert np.array_equal(whole.cpu().numpy(), want)
+        got = out.cpu().numpy()
+        assert np.array_equal(got, np.where(np.arange(rows) == 2, 0, want + col_begin))
+    finally:
+        comm.close()
+    assert kt.Context.get().take_error() == 0
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -123,7 +165,18 @@ def _two_gpu_rank(rank, world, port, out_dir):
         col.forward_into(x, ys)
         y_col = torch.empty((m, n), device="cuda")
         col.gather_into(ys, y_col)
+        # greedy decoding over logits split along the vocabulary: ties across the shard boundary
+        rows, nv = 3, 1000
+        lg = torch.randn((rows, nv), generator=gen, device="cuda")
+        lg[0, 10] = 99.0
+        lg[0, 900] = 99.0   # same logit on the other rank's shard: column 10 wins
+        lg[1, 700] = 98.0   # the winner on rank 1's shard
+        lg[2] = -5e9        # nothing above -1e9 anywhere: column 0
+        b, e = P.shard_bounds(P.COLUMNS, nv, 1, world, rank)
+        tokens = torch.full((rows,), -1, dtype=torch.int32, device="cuda")
+        P.argmax_column_parallel(comm, lg[:, b:e].contiguous(), b, tokens)
         torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"t{rank}.npy"), tokens.cpu().numpy())
         np.save(os.path.join(out_dir, f"r{rank}.npy"),
                 np.stack([ref.cpu().numpy(), y_row.cpu().numpy(), y_col.cpu().numpy()]))
         assert ctx.take_error() == 0
@@ -143,3 +196,4 @@ def test_tensor_parallel_on_two_gpus(kt, tmp_path):
         ref, y_row, y_col = np.load(tmp_path / f"r{r}.npy")
         assert rel_err(y_row, ref) <= TOL_FP32
         assert rel_err(y_col, ref) <= TOL_FP32
+        assert np.array_equal(np.load(tmp_path / f"t{r}.npy"), np.array([10, 700, 0], np.int32))
