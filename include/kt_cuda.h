@@ -155,7 +155,10 @@ kt_status kt_comm_destroy(kt_comm* comm);
 /* Row-parallel multiplyQuantized: w_shard = kt_qweight_shard(W, axis 0, P, rank),
  * a_shard = the matching columns of a, contiguous [m x K_rank] on the device:
  *   c[m x N] = (accumulate ? c : 0) + alpha * sum_ranks a_shard . dequant(w_shard) + bias
- * on every rank (ncclAllReduce of the fp32 partial products, bias added once). */
+ * on every rank (ncclAllReduce of the fp32 partial products, bias added once).
+ * At m = 1 on INT4 shards the exchange runs inside the GEMV's epilogue over peer
+ * memory (CUDA IPC areas set up on the first such call -- a collective -- and
+ * agreed once per shard by every rank); KT_TP_FUSED=0 keeps the NCCL path. */
 kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* w_shard, const float* a_shard_dev,
                                   float* c_dev, int32_t m, int32_t accumulate, float alpha, const float* bias_dev,
                                   void* stream);

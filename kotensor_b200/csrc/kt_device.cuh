@@ -93,6 +93,25 @@ __device__ __forceinline__ float ld_dsmem(uint32_t local, uint32_t rank) {
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
     return v;
 }
+// System-scope flag store / load (peer GPUs' memory) and a bounded wait for a
+// flag to reach `epoch` (wrap-around safe); false after the 2 s limit.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ bool wait_epoch_sys(const uint32_t* p, uint32_t epoch) {
+    if (static_cast<int32_t>(ld_acquire_sys(p) - epoch) >= 0) return true;
+    const uint64_t t0 = globaltimer();
+    while (static_cast<int32_t>(ld_acquire_sys(p) - epoch) < 0) {
+        if (globaltimer() - t0 > kWaitLimitNs) return false;
+        __nanosleep(100);
+    }
+    return true;
+}
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {

@@ -84,6 +84,7 @@ struct ImmaParams {
     int32_t cluster;   // split-K inside a cluster (1) or through partials in global memory (0)
     float* partials;   // split-K: [tiles][splits][256]
     int32_t* tickets;  // [tiles], zero on entry and on exit
+    TpExchange tp;     // row-parallel exchange fused into the epilogue (nranks 0: none)
 };
 
 __device__ __forceinline__ void imma_16832(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -372,9 +373,51 @@ __global__ void __launch_bounds__(kThreads, 2)
             *out = r;
         }
     };
+    // Row-parallel exchange (p.tp.nranks > 0), every thread of the CTA with its
+    // column: alpha * partial to every rank's receive area (slot epoch & 1, row
+    // of this rank), a CTA barrier, then thread 0 publishes the tile's flag on
+    // every rank (release at system scope, after the barrier: cumulative over
+    // the CTA's stores) and waits for every rank's flag of the tile here
+    // (acquire, bounded); the barrier hands the acquire to the CTA, which sums
+    // the ranks' rows in rank order (the same bits on every rank).
+    __shared__ int s_tp_ok;
+    auto finish = [&](int col, float val) {
+        if (p.tp.nranks == 0) {
+            emit(col, val);
+            return;
+        }
+        const int P = p.tp.nranks;
+        const int byte = tile_b0 + (col & (kTileBytes - 1));
+        const int out_col = col < kTileBytes ? byte : half + byte;
+        const bool valid = byte < p.R && out_col < p.N;
+        const int64_t slot_base = static_cast<int64_t>(p.tp.epoch & 1u) * P * p.tp.n_cap;
+        if (valid) {
+            const float mine = p.alpha * val;
+            for (int q = 0; q < P; ++q) p.tp.recv[q][slot_base + static_cast<int64_t>(p.tp.rank) * p.tp.n_cap + out_col] = mine;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const int64_t f = (static_cast<int64_t>(p.tp.epoch & 1u) * p.tp.tile_cap + blockIdx.x) * P;
+            for (int q = 0; q < P; ++q) st_release_sys(p.tp.flags[q] + f + p.tp.rank, p.tp.epoch);
+            bool ok = true;
+            for (int src = 0; src < P && ok; ++src) ok = wait_epoch_sys(p.tp.flags[p.tp.rank] + f + src, p.tp.epoch);
+            if (!ok) atomicOr(p.err, 1);
+            s_tp_ok = ok ? 1 : 0;
+        }
+        __syncthreads();
+        if (valid && s_tp_ok) {
+            const float* row0 = p.tp.recv[p.tp.rank] + slot_base + out_col;
+            float sum = 0.0f;
+            for (int src = 0; src < P; ++src) sum += __ldcv(row0 + static_cast<int64_t>(src) * p.tp.n_cap);
+            float* out = p.y + out_col;
+            float r = sum + (p.accumulate ? *out : 0.0f);
+            if (p.bias != nullptr) r += p.bias[out_col];
+            *out = r;
+        }
+    };
     const int S = gridDim.y;
     if (S == 1) {
-        emit(tid, v);
+        finish(tid, v);
         return;
     }
     if (p.cluster) {
@@ -424,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int j = 0; j < 32; ++j)
             if (s0 + j < S) sum += tv[j];
     }
-    emit(tid, sum);
+    finish(tid, sum);
     if (tid == 0) p.tickets[blockIdx.x] = 0;  // ready for the next launch on this workspace
 }
 
@@ -541,11 +584,11 @@ struct Plan {
 // saves ~0.2-0.3 us where the tail dominates (slices of <= 4 stages) and
 // costs ~1 us on long slices (cluster co-scheduling delays the early start of
 // CTAs behind the previous kernel).
-Plan plan_for(int R, int K, int sm_count) {
+Plan plan_for(int R, int K, int sm_count, bool no_cluster = false) {
     const int s = choose_splits(R, K, sm_count);
     const int tiles = tiles_of(R);
     const int stages_per_slice = K / kRowsPerStage / (s * kPairs);
-    if (s > 1 && s <= kMaxSplits && clusters_enabled() && stages_per_slice <= 4) {
+    if (!no_cluster && s > 1 && s <= kMaxSplits && clusters_enabled() && stages_per_slice <= 4) {
         for (int c = s; c >= std::max(2, min_splits(K)); --c) {
             if (active_clusters(c) >= tiles) return {c, true};
             if (split_override() >= 1) break;  // a pinned count is used as given
@@ -565,11 +608,18 @@ bool gemv_imma_supported(const QView& w, int32_t m, const float* a) {
            min_splits(w.rows) <= 65535 && (min_splits(w.rows) == 1 || tiles_of(w.bytes_per_row) <= kTicketCapEach);
 }
 
-size_t gemv_imma_workspace_bytes(const QView& w, int sm_count) {
-    const Plan plan = plan_for(w.bytes_per_row, w.rows, sm_count);
+size_t gemv_imma_workspace_bytes(const QView& w, int sm_count, bool no_cluster) {
+    const Plan plan = plan_for(w.bytes_per_row, w.rows, sm_count, no_cluster);
     if (plan.splits <= 1 || plan.cluster) return 0;
     return kWorkspaceReservedBytes +
            static_cast<size_t>(tiles_of(w.bytes_per_row)) * plan.splits * kCT * sizeof(float);
+}
+
+bool gemv_imma_tp_supported(const QView& w, int sm_count) {
+    if (!gemv_imma_supported(w, 1, nullptr)) return false;
+    const Plan plan = plan_for(w.bytes_per_row, w.rows, sm_count, true);
+    return static_cast<int64_t>(tiles_of(w.bytes_per_row)) * plan.splits <=
+           static_cast<int64_t>(blocks_per_sm()) * sm_count;
 }
 
 cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s, void* workspace,
@@ -588,10 +638,12 @@ cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, 
     p.alpha = a.alpha;
     p.accumulate = a.accumulate;
     p.lora = a.lora;
-    const Plan plan = plan_for(p.R, p.K, sm_count);
+    p.tp = a.tp;
+    const bool no_cluster = a.tp.nranks > 0;
+    const Plan plan = plan_for(p.R, p.K, sm_count, no_cluster);
     p.cluster = plan.cluster ? 1 : 0;
     if (plan.splits > 1 && !plan.cluster) {
-        if (workspace == nullptr || workspace_bytes < gemv_imma_workspace_bytes(w, sm_count))
+        if (workspace == nullptr || workspace_bytes < gemv_imma_workspace_bytes(w, sm_count, no_cluster))
             return cudaErrorInvalidValue;
         p.tickets = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) + kGemvTicketOffset);
         p.partials = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kWorkspaceReservedBytes);

@@ -58,6 +58,9 @@ struct kt_qweight {
     // Box of 64 rows x 128 bytes, no swizzle (INT4 tensor-core GEMM; same condition).
     alignas(64) CUtensorMap tmap_raw64;
     bool has_tmap_raw64 = false;
+    // row-parallel exchange-fused GEMV agreed by every rank for this shard
+    // (kt_qmatmul_row_parallel): 0 not asked yet, 1 fused, 2 NCCL
+    int32_t tp_fused = 0;
 };
 
 namespace kt {
@@ -159,6 +162,19 @@ cudaError_t launch_dequantize_rows(const QView& w, const int32_t* rows, int32_t 
                                    int32_t* d_status, cudaStream_t s);
 
 // ---- kt_gemv.cu  (fp32-accumulate CUDA-core kernels; small m)
+// Row-parallel exchange fused into the m = 1 INT4 GEMV (set up by kt_tp.cu):
+// the last CTA of each column tile publishes alpha * its partial to every
+// rank's receive area over peer memory, raises its flag there, waits (bounded)
+// for every rank's flag of the tile and writes
+// c = sum over ranks in rank order + (accumulate ? c : 0) + bias.
+// nranks == 0: no exchange (the plain kernel).
+struct TpExchange {
+    float* const* recv = nullptr;      // device array [P]: rank q's receive area, mapped here ([2][P][n_cap] floats)
+    uint32_t* const* flags = nullptr;  // device array [P]: rank q's flags, mapped here ([2][tile_cap][P])
+    int32_t nranks = 0, rank = 0, n_cap = 0, tile_cap = 0;
+    uint32_t epoch = 0;                // this call's number (>= 1); slot = epoch & 1
+};
+
 struct MatmulArgs {
     const float* a;
     float* c;
@@ -168,6 +184,7 @@ struct MatmulArgs {
     float alpha;
     int32_t* err;  // context error word (bounded-wait timeouts)
     LoraEpilogue lora;
+    TpExchange tp;
 };
 // Largest m the fp32-accumulate streaming kernel takes.
 constexpr int kGemvMaxM = 8;
@@ -191,7 +208,11 @@ cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& args, int sm_count
 // ---- kt_gemv_imma.cu  (INT4, m = 1: integer tensor-core products, fp32 group combine)
 bool gemv_imma_supported(const QView& w, int32_t m, const float* a);
 void set_imma_tuning(int k_splits);
-size_t gemv_imma_workspace_bytes(const QView& w, int sm_count);
+size_t gemv_imma_workspace_bytes(const QView& w, int sm_count, bool no_cluster = false);
+// The shard can run the exchange-fused GEMV: the m = 1 kernel applies, and its
+// whole grid is resident at once (a CTA waiting on other ranks must not keep
+// another CTA of its grid from running).
+bool gemv_imma_tp_supported(const QView& w, int sm_count);
 cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s, void* workspace,
                              size_t workspace_bytes);
 

@@ -8,10 +8,24 @@
 //                   its columns with kt_qmatmul, no exchange; kt_allgather_columns
 //                   assembles [m x N] when a rank needs the whole output.
 //
+// Row-parallel at m = 1 (decode) with INT4 shards runs one kernel per rank
+// instead: the m = 1 GEMV with the exchange fused into its epilogue (one-shot
+// all-reduce over peer memory, kt_gemv_imma.cu).  Each rank owns an exchange
+// area -- receive rows [2][P][kTpNCap] floats and flags [2][kTpTileCap][P] --
+// mapped into every other rank's process with CUDA IPC (handles all-gathered
+// through NCCL); the last CTA of a column tile stores its partial into every
+// rank's area, raises the tile's flag there, waits for every rank's flag and
+// sums the rows in rank order.  Set up on the first such call (a collective:
+// every rank takes part and all use the fused kernel or none), and agreed once
+// per shard; KT_TP_FUSED=0 keeps the NCCL path.
+//
 // NCCL is loaded at run time (dlopen of libnccl.so.2, or KT_NCCL_LIBRARY): the
 // rest of the library does not depend on it.  Calls on one communicator must be
 // issued in the same order on every rank, on one stream per rank.
 #include <dlfcn.h>
+
+#include <algorithm>
+#include <vector>
 
 #include <cstdlib>
 #include <cstring>
@@ -160,12 +174,23 @@ __global__ void merge_argmax_kernel(const int32_t* __restrict__ gathered, int32_
 
 }  // namespace
 
+constexpr int kTpMaxRanks = 8;
+constexpr int32_t kTpNCap = 65536;     // output columns of a fused row-parallel GEMV
+constexpr int32_t kTpTileCap = 256;    // its column tiles (256 columns each)
+
 struct kt_comm {
     kt_ctx* ctx = nullptr;
     ncclComm_t comm = nullptr;
     int32_t nranks = 0, rank = 0;
     float* scratch = nullptr;  // partial sums / gathered columns, grown on demand
     size_t scratch_floats = 0;
+    // exchange areas of the fused row-parallel GEMV
+    int p2p_state = 0;                  // 0 not set up, 1 ready, 2 unavailable
+    void* area = nullptr;               // this rank's area (cudaMalloc)
+    void* peers[kTpMaxRanks] = {};      // every rank's area as mapped here (own at [rank])
+    float** d_recv = nullptr;           // device arrays of the P receive / flag pointers
+    uint32_t** d_flags = nullptr;
+    uint32_t epoch = 0;                 // fused calls so far
 };
 
 namespace {
@@ -190,6 +215,101 @@ cudaError_t comm_scratch(kt_comm* c, size_t floats, float** out) {
     }
     *out = c->scratch;
     return cudaSuccess;
+}
+
+size_t tp_recv_bytes(int P) { return static_cast<size_t>(2) * P * kTpNCap * sizeof(float); }
+size_t tp_area_bytes(int P) { return tp_recv_bytes(P) + static_cast<size_t>(2) * kTpTileCap * P * sizeof(uint32_t); }
+
+bool tp_fused_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("KT_TP_FUSED");
+        return v == nullptr || std::atoi(v) != 0;
+    }();
+    return on;
+}
+
+// Every rank's agreement on a local yes / no (sum of ones over NCCL).
+kt_status all_agree(kt_comm* c, bool mine, cudaStream_t s, bool* all) {
+    float* f = nullptr;
+    cudaError_t e = comm_scratch(c, 1, &f);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_OUT_OF_MEMORY, std::string("TP scratch: ") + cudaGetErrorString(e));
+    const float one = mine ? 1.0f : 0.0f;
+    e = cudaMemcpyAsync(f, &one, sizeof(float), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("agreement copy: ") + cudaGetErrorString(e));
+    const ncclResult_t r = nccl().all_reduce(f, f, 1, kNcclFloat32, kNcclSum, c->comm, s);
+    if (r != 0) return nccl_fail(r, "ncclAllReduce (agreement)");
+    float sum = 0.0f;
+    e = cudaMemcpyAsync(&sum, f, sizeof(float), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("agreement copy: ") + cudaGetErrorString(e));
+    *all = sum == static_cast<float>(c->nranks);
+    return KT_OK;
+}
+
+void release_p2p(kt_comm* c) {
+    for (int q = 0; q < c->nranks && q < kTpMaxRanks; ++q)
+        if (q != c->rank && c->peers[q] != nullptr) cudaIpcCloseMemHandle(c->peers[q]);
+    cudaFree(c->area);
+    cudaFree(c->d_recv);
+    cudaFree(c->d_flags);
+    c->area = nullptr;
+    c->d_recv = nullptr;
+    c->d_flags = nullptr;
+    for (void*& p : c->peers) p = nullptr;
+    cudaGetLastError();
+}
+
+// Collective: every rank allocates and zeroes its area, the IPC handles are
+// all-gathered through NCCL, every rank maps the others', and all of them
+// agree (or none uses the fused path).
+kt_status setup_p2p(kt_comm* c, cudaStream_t s) {
+    const int P = c->nranks;
+    bool ok = P <= kTpMaxRanks;
+    cudaIpcMemHandle_t mine{};
+    const size_t bytes = tp_area_bytes(std::min(P, kTpMaxRanks));
+    if (ok) ok = cudaMalloc(&c->area, bytes) == cudaSuccess;
+    if (ok) ok = cudaMemset(c->area, 0, bytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+    if (ok) ok = cudaIpcGetMemHandle(&mine, c->area) == cudaSuccess;
+    cudaGetLastError();
+    // handles: 64 bytes = 16 32-bit words per rank (a float32 all-gather copies bits)
+    constexpr int kWords = sizeof(cudaIpcMemHandle_t) / 4;
+    static_assert(sizeof(cudaIpcMemHandle_t) % 4 == 0, "IPC handle size");
+    float* f = nullptr;
+    cudaError_t e = comm_scratch(c, static_cast<size_t>(kWords) * (P + 1), &f);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_OUT_OF_MEMORY, std::string("TP scratch: ") + cudaGetErrorString(e));
+    e = cudaMemcpyAsync(f, &mine, sizeof(mine), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("IPC handle copy: ") + cudaGetErrorString(e));
+    const ncclResult_t r = nccl().all_gather(f, f + kWords, kWords, kNcclFloat32, c->comm, s);
+    if (r != 0) return nccl_fail(r, "ncclAllGather (IPC handles)");
+    std::vector<cudaIpcMemHandle_t> all(P);
+    e = cudaMemcpyAsync(all.data(), f + kWords, sizeof(cudaIpcMemHandle_t) * P, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("IPC handle copy: ") + cudaGetErrorString(e));
+    if (ok) {
+        c->peers[c->rank] = c->area;
+        for (int q = 0; q < P && ok; ++q)
+            if (q != c->rank)
+                ok = cudaIpcOpenMemHandle(&c->peers[q], all[q], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    }
+    if (ok) {
+        float* recv[kTpMaxRanks];
+        uint32_t* flags[kTpMaxRanks];
+        for (int q = 0; q < P; ++q) {
+            recv[q] = static_cast<float*>(c->peers[q]);
+            flags[q] = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(c->peers[q]) + tp_recv_bytes(P));
+        }
+        ok = cudaMalloc(&c->d_recv, sizeof(float*) * P) == cudaSuccess &&
+             cudaMalloc(&c->d_flags, sizeof(uint32_t*) * P) == cudaSuccess &&
+             cudaMemcpy(c->d_recv, recv, sizeof(float*) * P, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemcpy(c->d_flags, flags, sizeof(uint32_t*) * P, cudaMemcpyHostToDevice) == cudaSuccess;
+    }
+    cudaGetLastError();
+    bool every = false;
+    const kt_status st = all_agree(c, ok, s, &every);
+    if (st != KT_OK) return st;
+    if (!every) release_p2p(c);
+    c->p2p_state = every ? 1 : 2;
+    return KT_OK;
 }
 
 }  // namespace
@@ -236,6 +356,9 @@ kt_status kt_comm_destroy(kt_comm* c) {
     if (!c) return KT_OK;
     cudaSetDevice(c->ctx->device);
     cudaDeviceSynchronize();
+    // Peers wrote into this rank's area only inside calls this rank also made,
+    // before raising the flags its kernels waited for: nothing is in flight now.
+    if (c->p2p_state == 1) release_p2p(c);
     if (c->comm != nullptr) nccl().comm_destroy(c->comm);
     cudaFree(c->scratch);
     delete c;
@@ -250,6 +373,52 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
     if (m == 0) return KT_OK;
     if (!a_shard || !c) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (m == 1 && tp_fused_enabled()) {
+        // decided once per shard with every rank (collective, same call order everywhere)
+        kt_qweight* w = const_cast<kt_qweight*>(w_shard);
+        if (w->tp_fused == 0) {
+            if (comm->p2p_state == 0) {
+                const kt_status st = setup_p2p(comm, s);
+                if (st != KT_OK) return st;
+            }
+            const kt::QView v = kt::view(w);
+            const bool mine = comm->p2p_state == 1 && w->columns <= kTpNCap &&
+                              (w->bytes_per_row + 127) / 128 <= kTpTileCap &&
+                              kt::gemv_imma_tp_supported(v, ctx->sm_count);
+            bool every = false;
+            const kt_status st = all_agree(comm, mine, s, &every);
+            if (st != KT_OK) return st;
+            w->tp_fused = every ? 1 : 2;
+        }
+        if (w->tp_fused == 1) {
+            const kt::QView v = kt::view(w);
+            const float* a = a_shard;
+            if (reinterpret_cast<uintptr_t>(a) % 16 != 0) {  // the kernel loads x in 16-byte vectors
+                float* copy = nullptr;
+                cudaError_t e = comm_scratch(comm, static_cast<size_t>(w->rows) + 4, &copy);
+                if (e == cudaSuccess)
+                    e = cudaMemcpyAsync(copy, a_shard, sizeof(float) * w->rows, cudaMemcpyDeviceToDevice, s);
+                if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("x copy: ") + cudaGetErrorString(e));
+                a = copy;
+            }
+            kt::MatmulArgs args{a, c, bias, 1, accumulate, alpha, ctx->d_error};
+            args.tp.recv = comm->d_recv;
+            args.tp.flags = comm->d_flags;
+            args.tp.nranks = comm->nranks;
+            args.tp.rank = comm->rank;
+            args.tp.n_cap = kTpNCap;
+            args.tp.tile_cap = kTpTileCap;
+            args.tp.epoch = ++comm->epoch;
+            if (args.tp.epoch == 0) args.tp.epoch = ++comm->epoch;  // 0 is the areas' initial value
+            const size_t need = kt::gemv_imma_workspace_bytes(v, ctx->sm_count, true);
+            void* ws = nullptr;
+            cudaError_t e = cudaSuccess;
+            if (need > 0) e = kt::stream_workspace(ctx, s, need, &ws);
+            if (e == cudaSuccess) e = kt::launch_gemv_imma(v, args, ctx->sm_count, s, ws, need);
+            if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("fused row-parallel GEMV: ") + cudaGetErrorString(e));
+            return KT_OK;
+        }
+    }
     const int64_t total = static_cast<int64_t>(m) * w_shard->columns;
     float* sum = nullptr;
     cudaError_t e = comm_scratch(comm, static_cast<size_t>(total), &sum);

@@ -89,6 +89,36 @@ def test_row_parallel_and_gather_on_one_rank(kt):
     assert kt.Context.get().take_error() == 0
 
 
+def test_fused_row_parallel_gemv_on_one_rank(kt):
+    """m = 1 on an INT4 row shard runs the GEMV with the exchange fused into its
+    epilogue (one rank: its own area); two calls in a row use both slots of the
+    area; accumulate / alpha / bias as the reference's multiplyQuantized +
+    QuantizedLinear; an x that is not 16-byte aligned is copied first."""
+    from kotensor_b200 import parallel as P
+    comm = P.Comm(1, 0, P.Comm.unique_id())
+    try:
+        k, n = 4096, 2048
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(21)
+        w = torch.randn((k, n), generator=gen, device="cuda") * 0.02
+        qt = kt.QuantizedTensor.quantize(w, kt.Quantization(4))
+        shard = P.shard(qt, P.ROWS, 1, 0)
+        bias = torch.randn(n, generator=gen, device="cuda")
+        for call in range(3):
+            buf = torch.randn(k + 1, generator=gen, device="cuda")
+            x = buf[1:].view(1, k) if call == 2 else buf[:k].view(1, k)  # call 2: offset by 4 bytes
+            c0 = torch.randn((1, n), generator=gen, device="cuda")
+            ref = c0.clone()
+            kt.MatMul.multiply_quantized(x.contiguous().clone(), qt, ref, 1, accumulate=True, alpha=0.5, bias=bias)
+            y = c0.clone()
+            P.matmul_row_parallel(comm, x, shard, y, 1, accumulate=True, alpha=0.5, bias=bias)
+            torch.cuda.synchronize()
+            assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) <= 1e-6, call
+    finally:
+        comm.close()
+    assert kt.Context.get().take_error() == 0
+
+
 def _argmax_rule(logits):
     """argmaxOfLastToken per row: the largest logit above -1e9, the lowest column of a tie, 0 if none."""
     out = []
@@ -165,6 +195,17 @@ def _two_gpu_rank(rank, world, port, out_dir):
         col.forward_into(x, ys)
         y_col = torch.empty((m, n), device="cuda")
         col.gather_into(ys, y_col)
+        # m = 1: the GEMV with the exchange over peer memory fused into its epilogue,
+        # three calls in a row (both slots of the exchange areas, then the first again)
+        y_one = []
+        for call in range(3):
+            x1 = x[call:call + 1]
+            ref1 = torch.empty((1, n), device="cuda")
+            kt.MatMul.multiply_quantized(x1.contiguous(), qt, ref1, 1, accumulate=False, bias=bias)
+            y1 = torch.empty((1, n), device="cuda")
+            row.forward_into(x1[:, row.k_begin:row.k_end], y1)
+            y_one.append(np.stack([ref1.cpu().numpy()[0], y1.cpu().numpy()[0]]))
+        np.save(os.path.join(out_dir, f"m1_{rank}.npy"), np.stack(y_one))
         # greedy decoding over logits split along the vocabulary: ties across the shard boundary
         rows, nv = 3, 1000
         lg = torch.randn((rows, nv), generator=gen, device="cuda")
@@ -197,3 +238,7 @@ def test_tensor_parallel_on_two_gpus(kt, tmp_path):
         assert rel_err(y_row, ref) <= TOL_FP32
         assert rel_err(y_col, ref) <= TOL_FP32
         assert np.array_equal(np.load(tmp_path / f"t{r}.npy"), np.array([10, 700, 0], np.int32))
+        for ref1, y1 in np.load(tmp_path / f"m1_{r}.npy"):
+            assert rel_err(y1, ref1) <= TOL_FP32
+    # every rank holds the same bits (rank-order sum of the same partials)
+    assert np.array_equal(np.load(tmp_path / "m1_0.npy")[:, 1], np.load(tmp_path / "m1_1.npy")[:, 1])
