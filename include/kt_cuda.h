@@ -163,6 +163,10 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
                                   float* c_dev, int32_t m, int32_t accumulate, float alpha, const float* bias_dev,
                                   void* stream);
 
+/* 1 in *ready once this communicator's peer-memory exchange areas are set up
+ * and every rank agreed to use them (the fused m = 1 row-parallel GEMV), else 0. */
+kt_status kt_comm_exchange_ready(const kt_comm* comm, int32_t* ready);
+
 /* Column-parallel outputs (kt_qmatmul on w_shard = kt_qweight_shard(W, axis 1,
  * P, rank), equal widths n_shard = N / P) gathered into y_full [m x N] on every rank. */
 kt_status kt_allgather_columns(kt_comm* comm, const float* y_shard_dev, float* y_full_dev, int32_t m,

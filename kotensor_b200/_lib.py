@@ -96,6 +96,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_qmatmul_row_parallel": ([P, P, P, P, P, I32, I32, F32, P, P], I32),
     "kt_allgather_columns": ([P, P, P, I32, I32, P], I32),
     "kt_argmax_column_parallel": ([P, P, I32, I32, I32, P, P], I32),
+    "kt_comm_exchange_ready": ([P, ctypes.POINTER(I32)], I32),
     "kt_rmsnorm": ([P, P, P, P, I32, I32, F32, P], I32),
     "kt_add_rmsnorm": ([P, P, P, P, P, I32, I32, F32, P], I32),
     "kt_rope_kv": ([P, P, I32, I32, I32, I32, P, P, P, I32, I32, P, P], I32),

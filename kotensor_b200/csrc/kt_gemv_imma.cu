@@ -374,33 +374,47 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
     };
     // Row-parallel exchange (p.tp.nranks > 0), every thread of the CTA with its
-    // column: alpha * partial to every rank's receive area (slot epoch & 1, row
-    // of this rank), a CTA barrier, then thread 0 publishes the tile's flag on
+    // column: the call's number is this rank's count of completed calls + 1
+    // (the counter advances only when every CTA of the grid has exited, so the
+    // whole grid reads one value, and a replayed CUDA graph gets new ones);
+    // alpha * partial goes to every rank's receive area (slot epoch & 1, row of
+    // this rank), a CTA barrier, then thread 0 publishes the tile's flag on
     // every rank (release at system scope, after the barrier: cumulative over
     // the CTA's stores) and waits for every rank's flag of the tile here
     // (acquire, bounded); the barrier hands the acquire to the CTA, which sums
     // the ranks' rows in rank order (the same bits on every rank).
     __shared__ int s_tp_ok;
+    auto tp_exit = [&]() {
+        if (p.tp.nranks == 0 || tid != 0) return;
+        __threadfence();
+        const uint32_t total = gridDim.x * gridDim.y;
+        if (atomicAdd(p.tp.state + 1, 1u) == total - 1) {  // the grid's last CTA
+            p.tp.state[1] = 0;
+            p.tp.state[0] += 1;
+            __threadfence();
+        }
+    };
     auto finish = [&](int col, float val) {
         if (p.tp.nranks == 0) {
             emit(col, val);
             return;
         }
         const int P = p.tp.nranks;
+        const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.tp.state) + 1u;
         const int byte = tile_b0 + (col & (kTileBytes - 1));
         const int out_col = col < kTileBytes ? byte : half + byte;
         const bool valid = byte < p.R && out_col < p.N;
-        const int64_t slot_base = static_cast<int64_t>(p.tp.epoch & 1u) * P * p.tp.n_cap;
+        const int64_t slot_base = static_cast<int64_t>(epoch & 1u) * P * p.tp.n_cap;
         if (valid) {
             const float mine = p.alpha * val;
             for (int q = 0; q < P; ++q) p.tp.recv[q][slot_base + static_cast<int64_t>(p.tp.rank) * p.tp.n_cap + out_col] = mine;
         }
         __syncthreads();
         if (tid == 0) {
-            const int64_t f = (static_cast<int64_t>(p.tp.epoch & 1u) * p.tp.tile_cap + blockIdx.x) * P;
-            for (int q = 0; q < P; ++q) st_release_sys(p.tp.flags[q] + f + p.tp.rank, p.tp.epoch);
+            const int64_t f = (static_cast<int64_t>(epoch & 1u) * p.tp.tile_cap + blockIdx.x) * P;
+            for (int q = 0; q < P; ++q) st_release_sys(p.tp.flags[q] + f + p.tp.rank, epoch);
             bool ok = true;
-            for (int src = 0; src < P && ok; ++src) ok = wait_epoch_sys(p.tp.flags[p.tp.rank] + f + src, p.tp.epoch);
+            for (int src = 0; src < P && ok; ++src) ok = wait_epoch_sys(p.tp.flags[p.tp.rank] + f + src, epoch);
             if (!ok) atomicOr(p.err, 1);
             s_tp_ok = ok ? 1 : 0;
         }
@@ -418,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int S = gridDim.y;
     if (S == 1) {
         finish(tid, v);
+        tp_exit();
         return;
     }
     if (p.cluster) {
@@ -454,7 +469,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     if (tid == 0) s_last = atomic_add_acq_rel(p.tickets + blockIdx.x, 1) == S - 1;
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+        tp_exit();
+        return;
+    }
     // up to 32 partial loads in flight per thread, summed in split order
     float sum = 0.0f;
     for (int s0 = 0; s0 < S; s0 += 32) {
@@ -469,6 +487,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     finish(tid, sum);
     if (tid == 0) p.tickets[blockIdx.x] = 0;  // ready for the next launch on this workspace
+    tp_exit();
 }
 
 int tiles_of(int R) { return (R + kTileBytes - 1) / kTileBytes; }

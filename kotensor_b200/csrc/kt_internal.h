@@ -171,8 +171,8 @@ cudaError_t launch_dequantize_rows(const QView& w, const int32_t* rows, int32_t 
 struct TpExchange {
     float* const* recv = nullptr;      // device array [P]: rank q's receive area, mapped here ([2][P][n_cap] floats)
     uint32_t* const* flags = nullptr;  // device array [P]: rank q's flags, mapped here ([2][tile_cap][P])
+    uint32_t* state = nullptr;         // this rank's own {calls completed, CTAs exited in this call}
     int32_t nranks = 0, rank = 0, n_cap = 0, tile_cap = 0;
-    uint32_t epoch = 0;                // this call's number (>= 1); slot = epoch & 1
 };
 
 struct MatmulArgs {

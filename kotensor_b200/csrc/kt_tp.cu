@@ -190,7 +190,6 @@ struct kt_comm {
     void* peers[kTpMaxRanks] = {};      // every rank's area as mapped here (own at [rank])
     float** d_recv = nullptr;           // device arrays of the P receive / flag pointers
     uint32_t** d_flags = nullptr;
-    uint32_t epoch = 0;                 // fused calls so far
 };
 
 namespace {
@@ -218,7 +217,9 @@ cudaError_t comm_scratch(kt_comm* c, size_t floats, float** out) {
 }
 
 size_t tp_recv_bytes(int P) { return static_cast<size_t>(2) * P * kTpNCap * sizeof(float); }
-size_t tp_area_bytes(int P) { return tp_recv_bytes(P) + static_cast<size_t>(2) * kTpTileCap * P * sizeof(uint32_t); }
+size_t tp_flag_bytes(int P) { return static_cast<size_t>(2) * kTpTileCap * P * sizeof(uint32_t); }
+// receive rows | flags | this rank's own call counter and CTA exit count
+size_t tp_area_bytes(int P) { return tp_recv_bytes(P) + tp_flag_bytes(P) + 16; }
 
 bool tp_fused_enabled() {
     static const bool on = [] {
@@ -408,8 +409,8 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
             args.tp.rank = comm->rank;
             args.tp.n_cap = kTpNCap;
             args.tp.tile_cap = kTpTileCap;
-            args.tp.epoch = ++comm->epoch;
-            if (args.tp.epoch == 0) args.tp.epoch = ++comm->epoch;  // 0 is the areas' initial value
+            args.tp.state = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(comm->area) +
+                                                        tp_recv_bytes(comm->nranks) + tp_flag_bytes(comm->nranks));
             const size_t need = kt::gemv_imma_workspace_bytes(v, ctx->sm_count, true);
             void* ws = nullptr;
             cudaError_t e = cudaSuccess;
@@ -448,6 +449,12 @@ kt_status kt_allgather_columns(kt_comm* comm, const float* y_shard, float* y_ful
     gather_columns_kernel<<<blocks_for(per * comm->nranks), 256, 0, s>>>(gathered, y_full, comm->nranks, m, n_shard);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("gather columns: ") + cudaGetErrorString(e));
+    return KT_OK;
+}
+
+kt_status kt_comm_exchange_ready(const kt_comm* comm, int32_t* ready) {
+    if (!comm || !ready) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    *ready = comm->p2p_state == 1 ? 1 : 0;
     return KT_OK;
 }
 

@@ -138,6 +138,13 @@ class Comm:
     def handle(self) -> ctypes.c_void_p:
         return self._handle
 
+    def exchange_ready(self) -> bool:
+        """True once the peer-memory exchange of the fused m = 1 row-parallel
+        GEMV is set up and agreed by every rank."""
+        out = ctypes.c_int32()
+        _lib.check(_lib.load().kt_comm_exchange_ready(self.handle, ctypes.byref(out)))
+        return bool(out.value)
+
     def close(self) -> None:
         if self._handle:
             _lib.load().kt_comm_destroy(self._handle)

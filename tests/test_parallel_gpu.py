@@ -114,6 +114,7 @@ def test_fused_row_parallel_gemv_on_one_rank(kt):
             P.matmul_row_parallel(comm, x, shard, y, 1, accumulate=True, alpha=0.5, bias=bias)
             torch.cuda.synchronize()
             assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) <= 1e-6, call
+        assert comm.exchange_ready()
     finally:
         comm.close()
     assert kt.Context.get().take_error() == 0
@@ -205,7 +206,28 @@ def _two_gpu_rank(rank, world, port, out_dir):
             y1 = torch.empty((1, n), device="cuda")
             row.forward_into(x1[:, row.k_begin:row.k_end], y1)
             y_one.append(np.stack([ref1.cpu().numpy()[0], y1.cpu().numpy()[0]]))
+        # the fused call captured in a CUDA graph and replayed with new inputs: the
+        # call numbers come from the device, so every replay exchanges fresh partials
+        xg = x[3:4, row.k_begin:row.k_end].contiguous()
+        yg = torch.empty((1, n), device="cuda")
+        row.forward_into(xg, yg)
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            row.forward_into(xg, yg)
+        for rep in range(3):
+            xr = torch.randn((1, k), generator=gen, device="cuda")
+            xg.copy_(xr[:, row.k_begin:row.k_end])
+            graph.replay()
+            ref_r = torch.empty((1, n), device="cuda")
+            kt.MatMul.multiply_quantized(xr, qt, ref_r, 1, accumulate=False, bias=bias)
+            torch.cuda.synchronize()
+            y_one.append(np.stack([ref_r.cpu().numpy()[0], yg.cpu().numpy()[0]]))
+        del graph
         np.save(os.path.join(out_dir, f"m1_{rank}.npy"), np.stack(y_one))
+        assert comm.exchange_ready()  # the fused kernel ran, not the NCCL fallback
         # greedy decoding over logits split along the vocabulary: ties across the shard boundary
         rows, nv = 3, 1000
         lg = torch.randn((rows, nv), generator=gen, device="cuda")
