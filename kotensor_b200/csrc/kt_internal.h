@@ -58,9 +58,10 @@ struct kt_qweight {
     // Box of 64 rows x 128 bytes, no swizzle (INT4 tensor-core GEMM; same condition).
     alignas(64) CUtensorMap tmap_raw64;
     bool has_tmap_raw64 = false;
-    // row-parallel exchange-fused GEMV agreed by every rank for this shard
-    // (kt_qmatmul_row_parallel): 0 not asked yet, 1 fused, 2 NCCL
+    // row-parallel exchange-fused GEMV agreed by every rank for this shard on
+    // communicator tp_comm (kt_qmatmul_row_parallel): 0 not asked yet, 1 fused, 2 NCCL
     int32_t tp_fused = 0;
+    const void* tp_comm = nullptr;
 };
 
 namespace kt {

@@ -377,7 +377,7 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
     if (m == 1 && tp_fused_enabled()) {
         // decided once per shard with every rank (collective, same call order everywhere)
         kt_qweight* w = const_cast<kt_qweight*>(w_shard);
-        if (w->tp_fused == 0) {
+        if (w->tp_fused == 0 || w->tp_comm != comm) {
             if (comm->p2p_state == 0) {
                 const kt_status st = setup_p2p(comm, s);
                 if (st != KT_OK) return st;
@@ -390,6 +390,7 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
             const kt_status st = all_agree(comm, mine, s, &every);
             if (st != KT_OK) return st;
             w->tp_fused = every ? 1 : 2;
+            w->tp_comm = comm;
         }
         if (w->tp_fused == 1) {
             const kt::QView v = kt::view(w);
