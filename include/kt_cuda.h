@@ -158,7 +158,10 @@ kt_status kt_comm_destroy(kt_comm* comm);
  * on every rank (ncclAllReduce of the fp32 partial products, bias added once).
  * At m = 1 on INT4 shards the exchange runs inside the GEMV's epilogue over peer
  * memory (CUDA IPC areas set up on the first such call -- a collective -- and
- * agreed once per shard by every rank); KT_TP_FUSED=0 keeps the NCCL path. */
+ * agreed once per shard by every rank); KT_TP_FUSED=0 keeps the NCCL path.
+ * Its waits for the other ranks are bounded: ranks that reach the same call more
+ * than 2 s apart make it fail (context error word set, kt_ctx_take_error), where
+ * NCCL would wait indefinitely. */
 kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* w_shard, const float* a_shard_dev,
                                   float* c_dev, int32_t m, int32_t accumulate, float alpha, const float* bias_dev,
                                   void* stream);
