@@ -264,6 +264,24 @@ class QuantizedTensor:
             raise ValueError(f"row index out of range for {self.rows} rows")
         return out
 
+    def dequantize_columns(self, columns):
+        """dequantizeColumn for each index in ``columns`` (QuantizedTensor.kt:235-241;
+        an int32 CUDA tensor or a sequence): [len(columns), rows], bit-identical."""
+        idx = torch.as_tensor(columns).to(device=f"cuda:{self.device}", dtype=torch.int32).contiguous().reshape(-1)
+        out = torch.empty((idx.numel(), self.rows), dtype=torch.float32, device=idx.device)
+        if idx.numel() == 0:
+            return out
+        status = torch.zeros(1, dtype=torch.int32, device=idx.device)
+        _lib.check(_lib.load().kt_dequantize_column(self._ctx.handle, self._handle, ctypes.c_void_p(idx.data_ptr()),
+                                                    idx.numel(), ctypes.c_void_p(out.data_ptr()),
+                                                    ctypes.c_void_p(status.data_ptr()), _stream_of(out)))
+        if int(status.item()) != 0:
+            raise ValueError(f"column index out of range for {self.columns} columns")
+        return out
+
+    def dequantize_column(self, column: int):
+        return self.dequantize_columns([column])[0]
+
     def dequantize_row(self, row: int):
         import torch as _t
         return self.dequantize_rows(_t.tensor([row], dtype=_t.int32))[0]

@@ -275,6 +275,26 @@ def test_transposed_matches_golden(kt, golden):
         assert rel_err(dx.cpu().numpy(), golden[f"{base}/dx"]) <= TOL_FP32, base
 
 
+@pytest.mark.parametrize("bits,g", [(8, 64), (4, 64), (4, 32), (4, 5)])
+@pytest.mark.parametrize("shape", [(256, 1537), (1000, 577), (130, 9)])
+def test_dequantize_column_matches_the_oracle(kt, oracle, bits, g, shape):
+    """dequantizeColumn (QuantizedTensor.kt:235-241): every column of odd-width INT4
+    and INT8 weights, bit-identical to the oracle's dequantize(); out of range raises."""
+    rng = np.random.default_rng(sum(shape) + bits + g)
+    w = (rng.standard_normal(shape, dtype=np.float32) * 0.05).astype(np.float32)
+    ref = oracle.quantize(w, bits, g)
+    qt = kt.QuantizedTensor.from_arrays(ref.qdata, ref.scales, ref.zeros, shape, bits, g)
+    want = ref.dequantize()
+    cols = list(range(shape[1]))[::-1]
+    got = qt.dequantize_columns(cols).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), np.ascontiguousarray(want.T[cols]).view(np.uint32))
+    assert np.array_equal(qt.dequantize_column(0).cpu().numpy().view(np.uint32),
+                          np.ascontiguousarray(want[:, 0]).view(np.uint32))
+    with pytest.raises(ValueError):
+        qt.dequantize_column(shape[1])
+    assert kt.Context.get().take_error() == 0
+
+
 @pytest.mark.parametrize("k,n,m", [(4096, 1024, 1), (2048, 5632, 4), (896, 4864, 9), (300, 2101, 2)])
 @pytest.mark.parametrize("bits", [4, 8])
 def test_transposed_matches_oracle(kt, oracle, k, n, m, bits):
