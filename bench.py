@@ -205,15 +205,18 @@ def run_reference(args) -> None:
 
 QWEN2_05B = dict(vocab=151936, dim=896, layers=24, heads=14, kv_heads=2, hidden=4864, eps=1e-6,
                  rope_theta=1000000.0, bits=4, group_size=64, tied=True, qkv_bias=True)
+# a ~163M-parameter Llama-style decoder, INT8, untied embeddings
+LLAMA_163M = dict(vocab=32000, dim=768, layers=12, heads=12, kv_heads=12, hidden=2048, eps=1e-5,
+                  rope_theta=10000.0, bits=8, group_size=64, tied=False, qkv_bias=False)
 
 
-def decode_weights(kt, torch, seed: int):
-    """The Qwen2-0.5B-shaped INT4 model (random N(0, 0.02^2) weights quantized on
-    the device, tied embeddings, q/k/v biases)."""
+def decode_weights(kt, torch, seed: int, spec=None):
+    """A decoder with random N(0, 0.02^2) weights quantized on the device: by
+    default the Qwen2-0.5B-shaped INT4 model (tied embeddings, q/k/v biases)."""
     import numpy as np
     from types import SimpleNamespace
     from kotensor_b200 import decoder as D
-    cfg = D.DecoderConfig(**QWEN2_05B)
+    cfg = D.DecoderConfig(**(spec or QWEN2_05B))
     gen = torch.Generator(device="cuda")
     gen.manual_seed(seed)
     q = kt.Quantization(cfg.bits, cfg.group_size)
@@ -229,20 +232,22 @@ def decode_weights(kt, torch, seed: int):
         layers.append({
             "norm1": np.ones(cfg.dim, np.float32), "norm2": np.ones(cfg.dim, np.float32),
             "wq": proj(cfg.dim, cfg.dim), "wk": proj(cfg.dim, kv), "wv": proj(cfg.dim, kv), "wo": proj(cfg.dim, cfg.dim),
-            "bq": rng.standard_normal(cfg.dim).astype(np.float32) * 0.02,
-            "bk": rng.standard_normal(kv).astype(np.float32) * 0.02,
-            "bv": rng.standard_normal(kv).astype(np.float32) * 0.02,
+            "bq": rng.standard_normal(cfg.dim).astype(np.float32) * (0.02 if cfg.qkv_bias else 0.0),
+            "bk": rng.standard_normal(kv).astype(np.float32) * (0.02 if cfg.qkv_bias else 0.0),
+            "bv": rng.standard_normal(kv).astype(np.float32) * (0.02 if cfg.qkv_bias else 0.0),
             "bo": np.zeros(cfg.dim, np.float32),
             "wg": proj(cfg.dim, cfg.hidden), "wu": proj(cfg.dim, cfg.hidden), "wd": proj(cfg.hidden, cfg.dim),
             "bg": np.zeros(cfg.hidden, np.float32), "bu": np.zeros(cfg.hidden, np.float32),
             "bd": np.zeros(cfg.dim, np.float32)})
     head = proj(cfg.dim, cfg.vocab)
-    weights = SimpleNamespace(embedding=None, layers=layers, final_norm=np.ones(cfg.dim, np.float32), head=head,
+    embedding = None if cfg.tied else proj(cfg.vocab, cfg.dim)
+    weights = SimpleNamespace(embedding=embedding, layers=layers, final_norm=np.ones(cfg.dim, np.float32), head=head,
                               head_bias=np.zeros(cfg.vocab, np.float32))
     return cfg, weights
 
 
-def measure_decode(kt, torch, cfg, weights, batch: int, steps: int, prompt_len: int, seed: int) -> dict:
+def measure_decode(kt, torch, cfg, weights, batch: int, steps: int, prompt_len: int, seed: int,
+                   model: str = "qwen2-0.5b-shaped int4 g64 (random weights, tied, qkv bias)") -> dict:
     """Batched greedy decode: `batch` random prompts prefilled as blocks
     (Transformer.prefill, all sequences in one pass), then timed CUDA-graph decode
     steps of the whole batch (every matmul at m = batch)."""
@@ -273,7 +278,7 @@ def measure_decode(kt, torch, cfg, weights, batch: int, steps: int, prompt_len: 
     ms = e0.elapsed_time(e1) / steps
     weight_bytes = sum(w.size_in_bytes for L in dec.layers for k, w in L.items() if k.startswith("w"))
     weight_bytes += dec.head.size_in_bytes
-    out = {"model": "qwen2-0.5b-shaped int4 g64 (random weights, tied, qkv bias)", "batch": batch,
+    out = {"model": model, "batch": batch,
            "prompt": prompt_len, "prefill_ms": round(prefill_ms, 3),
            "prefill_tokens_per_s": round(batch * prompt_len / (prefill_ms / 1e3), 1),
            "steps": steps, "ms_per_step": round(ms, 4),
@@ -451,6 +456,14 @@ def run_ours(args) -> None:
                                                  seed=99 + rank))
         decode = next((d for d in decode_batches if d["batch"] == 1), decode_batches[0] if decode_batches else None)
         del dweights
+    # the INT8 ~163M Llama-style decoder, 128-token prompt, 256 greedy steps, batch 1
+    decode_int8 = None
+    if args.int8_decode_steps > 0:
+        icfg, iweights = decode_weights(kt, torch, seed=7 + rank, spec=LLAMA_163M)
+        decode_int8 = measure_decode(kt, torch, icfg, iweights, 1, args.int8_decode_steps, 128, seed=7 + rank,
+                                     model="llama-style 163M int8 g64 (d768, 12 layers, vocab 32000, untied, "
+                                           "random weights)")
+        del iweights
 
     peak, peak_kind = measured_peaks()
     line = {
@@ -480,6 +493,9 @@ def run_ours(args) -> None:
         line["decode"] = decode
         line["decode_batches"] = [{k: d[k] for k in ("batch", "ms_per_step", "tokens_per_s", "prefill_tokens_per_s",
                                                      "weight_gbs")} for d in decode_batches]
+    if decode_int8 is not None:
+        line["decode_int8"] = {k: decode_int8[k] for k in ("model", "batch", "prompt", "prefill_ms", "steps",
+                                                          "ms_per_step", "tokens_per_s", "weight_gbs")}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -499,6 +515,8 @@ def main() -> None:
     ap.add_argument("--decode-steps", type=int, default=128, help="timed greedy decode steps (0: skip)")
     ap.add_argument("--decode-prompt", type=int, default=512, help="prompt tokens before the timed decode")
     ap.add_argument("--decode-batches", default="1,8,64", help="decode batch sizes to time (comma-separated)")
+    ap.add_argument("--int8-decode-steps", type=int, default=256,
+                    help="timed greedy steps of the INT8 163M decoder (BASELINE config 3; 0: skip)")
     ap.add_argument("--gemm-m", type=int, default=512,
                     help="also time the prefill GEMM at this M on the same weights (0: skip)")
     args = ap.parse_args()
