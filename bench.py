@@ -205,6 +205,10 @@ def run_reference(args) -> None:
 
 QWEN2_05B = dict(vocab=151936, dim=896, layers=24, heads=14, kv_heads=2, hidden=4864, eps=1e-6,
                  rope_theta=1000000.0, bits=4, group_size=64, tied=True, qkv_bias=True)
+# Llama-3-8B-shaped INT4 (untied, Llama-3 RoPE scaling)
+LLAMA3_8B = dict(vocab=128256, dim=4096, layers=32, heads=32, kv_heads=8, hidden=14336, eps=1e-5,
+                 rope_theta=500000.0, rope_scaling=(8.0, 1.0, 4.0, 8192), bits=4, group_size=64, tied=False,
+                 qkv_bias=False)
 # a ~163M-parameter Llama-style decoder, INT8, untied embeddings
 LLAMA_163M = dict(vocab=32000, dim=768, layers=12, heads=12, kv_heads=12, hidden=2048, eps=1e-5,
                   rope_theta=10000.0, bits=8, group_size=64, tied=False, qkv_bias=False)
@@ -456,6 +460,17 @@ def run_ours(args) -> None:
                                                  seed=99 + rank))
         decode = next((d for d in decode_batches if d["batch"] == 1), decode_batches[0] if decode_batches else None)
         del dweights
+    # BASELINE config 5 on one GPU: Llama-3-8B-shaped INT4, 1024-token prompts, batches of --llama-batches
+    # (batch 256 is left out: its fp32 KV cache at context 2048 alone is ~137 GB)
+    llama = []
+    if args.llama_steps > 0 and args.llama_batches.strip():
+        lcfg, lweights = decode_weights(kt, torch, seed=5 + rank, spec=LLAMA3_8B)
+        for b in [int(v) for v in args.llama_batches.split(",") if v.strip()]:
+            # one prefill block holds at most 65,535 rows: batch 64 prefills 1,023-token prompts
+            llama.append(measure_decode(kt, torch, lcfg, lweights, b, args.llama_steps, min(1024, 65535 // b),
+                                        seed=5 + rank, model="llama-3-8b-shaped int4 g64 (random weights, untied)"))
+        del lweights
+        torch.cuda.empty_cache()
     # the INT8 ~163M Llama-style decoder, 128-token prompt, 256 greedy steps, batch 1
     decode_int8 = None
     if args.int8_decode_steps > 0:
@@ -493,6 +508,9 @@ def run_ours(args) -> None:
         line["decode"] = decode
         line["decode_batches"] = [{k: d[k] for k in ("batch", "ms_per_step", "tokens_per_s", "prefill_tokens_per_s",
                                                      "weight_gbs")} for d in decode_batches]
+    if llama:
+        line["decode_llama3_8b"] = [{k: d[k] for k in ("batch", "prompt", "prefill_ms", "prefill_tokens_per_s",
+                                                        "ms_per_step", "tokens_per_s", "weight_gbs")} for d in llama]
     if decode_int8 is not None:
         line["decode_int8"] = {k: decode_int8[k] for k in ("model", "batch", "prompt", "prefill_ms", "steps",
                                                           "ms_per_step", "tokens_per_s", "weight_gbs")}
@@ -515,6 +533,9 @@ def main() -> None:
     ap.add_argument("--decode-steps", type=int, default=128, help="timed greedy decode steps (0: skip)")
     ap.add_argument("--decode-prompt", type=int, default=512, help="prompt tokens before the timed decode")
     ap.add_argument("--decode-batches", default="1,8,64", help="decode batch sizes to time (comma-separated)")
+    ap.add_argument("--llama-batches", default="1,16,64",
+                    help="decode batch sizes of the Llama-3-8B-shaped INT4 model (BASELINE config 5; empty: skip)")
+    ap.add_argument("--llama-steps", type=int, default=32, help="timed greedy steps of the Llama-3-8B-shaped model")
     ap.add_argument("--int8-decode-steps", type=int, default=256,
                     help="timed greedy steps of the INT8 163M decoder (BASELINE config 3; 0: skip)")
     ap.add_argument("--gemm-m", type=int, default=512,
