@@ -466,9 +466,8 @@ def run_ours(args) -> None:
     if args.llama_steps > 0 and args.llama_batches.strip():
         lcfg, lweights = decode_weights(kt, torch, seed=5 + rank, spec=LLAMA3_8B)
         for b in [int(v) for v in args.llama_batches.split(",") if v.strip()]:
-            # one prefill block holds at most 65,535 rows: batch 64 prefills 1,023-token prompts
-            llama.append(measure_decode(kt, torch, lcfg, lweights, b, args.llama_steps, min(1024, 65535 // b),
-                                        seed=5 + rank, model="llama-3-8b-shaped int4 g64 (random weights, untied)"))
+            llama.append(measure_decode(kt, torch, lcfg, lweights, b, args.llama_steps, 1024, seed=5 + rank,
+                                        model="llama-3-8b-shaped int4 g64 (random weights, untied)"))
         del lweights
         torch.cuda.empty_cache()
     # the INT8 ~163M Llama-style decoder, 128-token prompt, 256 greedy steps, batch 1

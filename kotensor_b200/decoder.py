@@ -88,11 +88,17 @@ class _Rows:
 class DeviceDecoder:
     """Greedy decoding of one sequence with weights, KV cache and buffers in HBM.
 
+    ``max_block_rows`` (65,535, the row kernels' grid limit) bounds the rows of
+    one prefill block; a batch with more prompt rows is prefilled in blocks of
+    whole sequences.
+
     ``weights``: ``embedding`` ([vocab x dim], None when tied), ``layers`` (a list
     of dicts with wq wk wv wo wg wu wd, their biases bq bk bv bo bg bu bd and the
     RMSNorm weights norm1 norm2), ``final_norm``, ``head`` ([dim x vocab]),
     ``head_bias``.  ``batch`` sequences decode together (one KV cache each, the
     same position): every matmul of a step runs at m = batch."""
+
+    max_block_rows = 65535
 
     def __init__(self, cfg: DecoderConfig, weights, max_seq: int, device: Optional[int] = None, batch: int = 1):
         self.cfg = cfg
@@ -176,14 +182,16 @@ class DeviceDecoder:
                                **f32)  # attention scratch
         return b
 
-    def _layers(self, b: "_Rows", rows: int, rows_per_seq: int) -> None:
+    def _layers(self, b: "_Rows", rows: int, rows_per_seq: int, seq0: int = 0) -> None:
         """Embedding lookup of b.tokens[:rows] through every block; leaves the
-        final-normed rows in b.normed.  Row r is sequence r / rows_per_seq at
-        position *position + r % rows_per_seq (one sequence's prompt, or one
+        final-normed rows in b.normed.  Row r is sequence seq0 + r / rows_per_seq
+        at position *position + r % rows_per_seq (one sequence's prompt, or one
         token of each of `rows` sequences)."""
         L_ = _lib.load()
         cfg, h = self.cfg, self.ctx.handle
         s, p = self._stream(), self._p
+        keys = ctypes.c_void_p(self.keys.data_ptr() + seq0 * self.cache_stride * self.keys.element_size())
+        values = ctypes.c_void_p(self.values.data_ptr() + seq0 * self.cache_stride * self.values.element_size())
         hd, kvh = cfg.head_dim, cfg.kv_heads
         kv = kvh * hd
         if cfg.tied:
@@ -194,10 +202,10 @@ class DeviceDecoder:
         for l, L in enumerate(self.layers):
             MatMul.multiply_quantized(b.normed[:rows], L["wqkv"], b.qkv[:rows], rows, accumulate=False,
                                       bias=L["bqkv"])
-            _lib.check(L_.kt_rope_kv_seqs(h, p(b.qkv), rows, cfg.dim, kvh, hd, p(self.inv_freq), p(self.keys),
-                                          p(self.values), self.max_seq, l, p(self.position), rows_per_seq,
+            _lib.check(L_.kt_rope_kv_seqs(h, p(b.qkv), rows, cfg.dim, kvh, hd, p(self.inv_freq), keys,
+                                          values, self.max_seq, l, p(self.position), rows_per_seq,
                                           self.cache_stride, s))
-            _lib.check(L_.kt_attention_seqs(h, p(b.qkv), p(self.keys), p(self.values), p(b.ctx), p(b.scores), rows,
+            _lib.check(L_.kt_attention_seqs(h, p(b.qkv), keys, values, p(b.ctx), p(b.scores), rows,
                                             cfg.dim + 2 * kv, cfg.heads, kvh, hd, self.max_seq, l, self.scale,
                                             p(self.position), rows_per_seq, self.cache_stride, s))
             MatMul.multiply_quantized(b.ctx[:rows], L["wo"], b.attn[:rows], rows, accumulate=False, bias=L["bo"])
@@ -248,18 +256,26 @@ class DeviceDecoder:
             raise ValueError("token out of vocab bounds")
         if self.length + T > self.max_seq:
             raise ValueError(f"KV cache full: {self.length} + {T} positions exceed maxSequenceLength {self.max_seq}")
-        rows = self.batch * T
-        if rows > 65535:
-            raise ValueError(f"{rows} prefill rows exceed 65535")
-        if self._prefill_bufs is None or self._prefill_bufs.rows < rows:
-            self._prefill_bufs = self._buffers(rows)
+        if T > self.max_block_rows:
+            raise ValueError(f"{T} prompt tokens exceed {self.max_block_rows} rows of one prefill block")
+        # whole sequences per block: a block holds at most max_block_rows rows (the
+        # kernels' grid rows); larger batches are prefilled in several blocks
+        per = min(self.batch, self.max_block_rows // T)
+        if self._prefill_bufs is None or self._prefill_bufs.rows < per * T:
+            self._prefill_bufs = self._buffers(per * T)
         b = self._prefill_bufs
-        b.tokens[:rows].copy_(torch.tensor([t for pr in prompts for t in pr], dtype=torch.int32))
-        self._layers(b, rows, T)
-        # the head only on each sequence's last row
-        self._last_rows.copy_(torch.tensor([q * T + T - 1 for q in range(self.batch)], dtype=torch.int32))
-        _lib.check(_lib.load().kt_gather_rows(self.ctx.handle, self._p(b.normed), self._p(self._last_rows), self.batch,
-                                              self.cfg.dim, self._p(self._head_in), self._stream()))
+        flat = torch.tensor([t for pr in prompts for t in pr], dtype=torch.int32)
+        L_ = _lib.load()
+        for s0 in range(0, self.batch, per):
+            s1 = min(self.batch, s0 + per)
+            rows = (s1 - s0) * T
+            b.tokens[:rows].copy_(flat[s0 * T:s1 * T])
+            self._layers(b, rows, T, seq0=s0)
+            # the head only on each sequence's last row
+            self._last_rows[:s1 - s0].copy_(torch.tensor([q * T + T - 1 for q in range(s1 - s0)], dtype=torch.int32))
+            dst = ctypes.c_void_p(self._head_in.data_ptr() + s0 * self.cfg.dim * self._head_in.element_size())
+            _lib.check(L_.kt_gather_rows(self.ctx.handle, self._p(b.normed), self._p(self._last_rows), s1 - s0,
+                                         self.cfg.dim, dst, self._stream()))
         self._head(self._head_in, T)
         self.length += T
         return self._result()

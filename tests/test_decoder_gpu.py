@@ -133,6 +133,39 @@ def test_batched_decode_matches_single_sequences(kt, oracle, batch):
     assert kt.Context.get().take_error() == 0
 
 
+def test_prefill_in_several_blocks_matches_one_block(kt, oracle):
+    """A batch whose prompt rows exceed one prefill block is prefilled in blocks
+    of whole sequences (here the block limit is lowered to 2 sequences of 7 rows
+    so a batch of 5 takes 3 blocks); every sequence gets the logits, cache and
+    next steps of the one-block prefill (bf16 tolerance: the blocks' matmuls run
+    at other m)."""
+    from oracle import decoder_oracle as DO
+    from kotensor_b200 import decoder as D
+    params = CONFIGS["int4_gqa_bias_scaled_rope"]
+    weights = DO.DecoderWeights.random(DO.DecoderConfig(**params), seed=23)
+    rng = np.random.default_rng(23)
+    batch, T = 5, 7
+    prompts = [rng.integers(0, params["vocab"], T).tolist() for _ in range(batch)]
+    whole = D.DeviceDecoder(D.DecoderConfig(**params), weights, max_seq=24, batch=batch)
+    split = D.DeviceDecoder(D.DecoderConfig(**params), weights, max_seq=24, batch=batch)
+    split.max_block_rows = 2 * T + 3
+    tol = 3e-2
+    want = whole.prefill(prompts).cpu().numpy()
+    got = split.prefill(prompts).cpu().numpy()
+    assert np.abs(got - want).max() <= tol * np.abs(want).max()
+    for _ in range(3):
+        tokens = whole.next_token.cpu().tolist()
+        want = whole.step(tokens).cpu().numpy()
+        got = split.step(tokens).cpu().numpy()
+        assert np.abs(got - want).max() <= tol * np.abs(want).max()
+    tiny = D.DeviceDecoder(D.DecoderConfig(**params), weights, max_seq=24)
+    tiny.max_block_rows = T - 1  # one prompt longer than a block
+    with pytest.raises(ValueError):
+        tiny.prefill(prompts[0])
+    assert int(split.status.item()) == 0
+    assert kt.Context.get().take_error() == 0
+
+
 def test_batched_graph_replay_matches_eager_steps(kt, oracle):
     from oracle import decoder_oracle as DO
     from kotensor_b200 import decoder as D
