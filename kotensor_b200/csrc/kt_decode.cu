@@ -59,6 +59,8 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const float* __restri
     for (int d = threadIdx.x; d < dim; d += blockDim.x) orow[d] = xr[d] * r * w[d];
 }
 
+constexpr int kRowRegs = 16;  // rows of up to kThreads * 16 values are normalised from registers
+
 // x += y, then out = RMSNorm(x) (the residual add of TransformerBlock.decodeInto
 // followed by the next norm), one block per row.
 __global__ void __launch_bounds__(kThreads) add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ y,
@@ -71,6 +73,25 @@ __global__ void __launch_bounds__(kThreads) add_rmsnorm_kernel(float* __restrict
     const float* yr = y + static_cast<int64_t>(blockIdx.x) * dim;
     float* orow = out + static_cast<int64_t>(blockIdx.x) * dim;
     float ss = 0.0f;
+    if (dim <= kThreads * kRowRegs) {
+        // the row stays in registers between the sum of squares and the scaling
+        float v[kRowRegs];
+#pragma unroll
+        for (int i = 0; i < kRowRegs; ++i) {
+            const int d = threadIdx.x + i * kThreads;
+            v[i] = d < dim ? xr[d] + yr[d] : 0.0f;
+            if (d < dim) xr[d] = v[i];
+            ss = fmaf(v[i], v[i], ss);
+        }
+        ss = block_sum(ss, red);
+        const float r = 1.0f / sqrtf(ss / static_cast<float>(dim) + eps);
+#pragma unroll
+        for (int i = 0; i < kRowRegs; ++i) {
+            const int d = threadIdx.x + i * kThreads;
+            if (d < dim) orow[d] = v[i] * r * w[d];
+        }
+        return;
+    }
     for (int d = threadIdx.x; d < dim; d += blockDim.x) {
         const float v = xr[d] + yr[d];
         xr[d] = v;
