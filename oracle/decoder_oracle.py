@@ -12,11 +12,19 @@ Follows (paths inside the Kotensor project, Engine/kotensor/src/main/kotlin/):
   SwiGLU.forwardInto, siluInPlace    SwiGLU.kt:19-25, Tensor.kt:231-237
   QuantizedEmbedding / TiedQuantizedEmbedding lookupInto  Embedding.kt:96-101, :129-135
   KVCache layout                     KVCache.kt:3-59
+  Transformer.prefill / prefillLayers Transformer.kt:99-132 (32-row chunks, MatMul.TILE_M)
+  Attention.prefillInto / attendCached Attention.kt:241-293
 The projections are the C oracle's MatMul.multiplyQuantized (m = 1 schedule)
-plus QuantizedLinear's bias (QuantizedLinear.kt:18-25).  Everything else is
-float32 numpy; summation orders of the sums (RMSNorm, dot products, softmax)
-follow numpy, not the reference's sequential loops, so results agree with the
-reference within float32 rounding, not bit for bit ("parity unpinned").
+plus QuantizedLinear's bias (QuantizedLinear.kt:18-25) for quantized weights,
+or a float32 product plus Linear's bias (Linear.kt) for float32 weights (the
+reference's unquantized model).  Everything else is float32 numpy; summation
+orders of the sums (RMSNorm, dot products, softmax) follow numpy, not the
+reference's sequential loops, so results agree with the reference within
+float32 rounding, not bit for bit.  The float32 mode is pinned to the
+reference's own known answers: the logits its test suite holds for three tiny
+Hugging Face checkpoints (GQA, q/k/v biases, tied embeddings, Llama-3 RoPE
+scaling; HuggingFaceImportTest.kt:29-36, checked there at 2e-4), see
+oracle/hf_oracle.py.
 """
 from __future__ import annotations
 
@@ -118,9 +126,43 @@ class DecoderWeights:
         return DecoderWeights(cfg, emb, layers, vec(cfg.dim, 1.0, 0.1), head, np.zeros(cfg.vocab, np.float32))
 
 
-def _linear(x: np.ndarray, w: O.OracleQTensor, bias: np.ndarray) -> np.ndarray:
-    y = O.multiply_quantized(x.reshape(1, -1), w, threads=8).reshape(-1)
+THREADS = 8  # host threads of the C oracle's matmul
+
+
+def _linear(x: np.ndarray, w, bias: np.ndarray) -> np.ndarray:
+    """QuantizedLinear.forward (quantized weight) or Linear.forward (float32
+    [in x out] weight) on one row, plus the bias."""
+    if isinstance(w, np.ndarray):
+        y = (x.reshape(1, -1).astype(np.float32) @ w).reshape(-1).astype(np.float32)
+    else:
+        y = O.multiply_quantized(x.reshape(1, -1), w, threads=THREADS).reshape(-1)
     return (y + bias).astype(np.float32)
+
+
+def _linear_rows(x: np.ndarray, w, bias: np.ndarray) -> np.ndarray:
+    """forwardInto on [rows x in] (multiplyQuantized at m = rows), plus the bias."""
+    if isinstance(w, np.ndarray):
+        y = (x.astype(np.float32) @ w).astype(np.float32)
+    else:
+        y = O.multiply_quantized(x, w, threads=THREADS)
+    return (y + bias[None, :]).astype(np.float32)
+
+
+def dequantize_column(w: O.OracleQTensor, column: int) -> np.ndarray:
+    """QuantizedTensor.dequantizeColumn (the value() of every row of one column,
+    QuantizedTensor.kt:172-186): scale * (q - zero) in float32, vectorised."""
+    rows, cols, g = w.rows, w.columns, w.group_size
+    groups = (rows + g - 1) // g
+    grp = np.arange(rows) // g
+    scales = w.scales.reshape(groups, cols)[grp, column]
+    if w.bits == 8:
+        q = w.qdata.view(np.int8).reshape(rows, cols)[:, column].astype(np.int32)
+        return (scales * q.astype(np.float32)).astype(np.float32)
+    half = (cols + 1) // 2
+    byte = w.qdata.reshape(rows, half)[:, column % half]
+    q = (byte & 15) if column < half else (byte >> 4)
+    zero = w.zeros.reshape(groups, cols)[grp, column].astype(np.int32)
+    return (scales * (q.astype(np.int32) - zero).astype(np.float32)).astype(np.float32)
 
 
 def _rmsnorm(x, w, eps):
@@ -159,7 +201,11 @@ class OracleDecoder:
         cfg = self.cfg
         if cfg.tied:
             head = self.w.head  # dequantizeColumn(token): column of the [dim x vocab] head
-            return np.array([head.value(k, token) for k in range(cfg.dim)], np.float32)
+            if isinstance(head, np.ndarray):
+                return head[:, token].astype(np.float32)
+            return dequantize_column(head, token)
+        if isinstance(self.w.embedding, np.ndarray):  # Embedding.lookup: a row of the float32 table
+            return self.w.embedding[token].astype(np.float32)
         return self.w.embedding.dequantize_row(token).astype(np.float32)
 
     def step(self, token: int) -> np.ndarray:
@@ -194,6 +240,53 @@ class OracleDecoder:
             x = (x + _linear(gate, L["wd"], L["bd"])).astype(np.float32)
         self.length += 1
         return _linear(_rmsnorm(x, w.final_norm, cfg.eps), w.head, w.head_bias)
+
+    def prefill(self, tokens) -> np.ndarray:
+        """Transformer.prefill: the prompt in chunks of 32 rows (prefillLayers),
+        each chunk through every block at m = chunk rows (TransformerBlock /
+        Attention.prefillInto: row t at position start + t attends to the cache
+        up to its own position); the logits of the last token."""
+        cfg, w = self.cfg, self.w
+        hd, group = cfg.head_dim, cfg.heads // cfg.kv_heads
+        scale = np.float32(1.0) / np.float32(math.sqrt(float(hd)))
+        tokens = list(tokens)
+        if not tokens:
+            raise ValueError("Prompt cannot be empty")
+        if self.length + len(tokens) > self.max_seq:
+            raise ValueError("KV cache full")
+        x = None
+        for c0 in range(0, len(tokens), 32):
+            chunk = tokens[c0:c0 + 32]
+            T, start = len(chunk), self.length
+            x = np.stack([self.embed(t) for t in chunk]).astype(np.float32)
+            for l, L in enumerate(w.layers):
+                n1 = np.stack([_rmsnorm(r, L["norm1"], cfg.eps) for r in x])
+                q = _linear_rows(n1, L["wq"], L["bq"])
+                k = _linear_rows(n1, L["wk"], L["bk"])
+                v = _linear_rows(n1, L["wv"], L["bv"])
+                q = np.stack([_rope(q[t], hd, self.freqs, start + t) for t in range(T)])
+                k = np.stack([_rope(k[t], hd, self.freqs, start + t) for t in range(T)])
+                self.keys[l, :, start:start + T, :] = k.reshape(T, cfg.kv_heads, hd).transpose(1, 0, 2)
+                self.values[l, :, start:start + T, :] = v.reshape(T, cfg.kv_heads, hd).transpose(1, 0, 2)
+                ctx = np.empty((T, cfg.dim), np.float32)
+                end = start + T
+                visible = np.arange(end)[None, :] <= (start + np.arange(T))[:, None]  # [T x end]
+                for h in range(cfg.heads):
+                    keys = self.keys[l, h // group, :end, :]
+                    vals = self.values[l, h // group, :end, :]
+                    sc = (q[:, h * hd:(h + 1) * hd] @ keys.T).astype(np.float32) * scale
+                    mx = np.maximum(np.float32(-1e9), np.where(visible, sc, -np.inf).max(axis=1))
+                    e = np.where(visible, np.exp((sc - mx[:, None]).astype(np.float64)), 0.0).astype(np.float32)
+                    wts = e * (np.float32(1.0) / np.sum(e, axis=1, dtype=np.float32))[:, None]
+                    ctx[:, h * hd:(h + 1) * hd] = (wts @ vals).astype(np.float32)
+                x = (x + _linear_rows(ctx, L["wo"], L["bo"])).astype(np.float32)
+                n2 = np.stack([_rmsnorm(r, L["norm2"], cfg.eps) for r in x])
+                gate = _linear_rows(n2, L["wg"], L["bg"])
+                up = _linear_rows(n2, L["wu"], L["bu"])
+                act = (gate / (np.float32(1.0) + np.exp(-gate.astype(np.float64)).astype(np.float32)) * up)
+                x = (x + _linear_rows(act.astype(np.float32), L["wd"], L["bd"])).astype(np.float32)
+            self.length += T
+        return _linear(_rmsnorm(x[-1], w.final_norm, cfg.eps), w.head, w.head_bias)
 
 
 def argmax(logits: np.ndarray) -> int:

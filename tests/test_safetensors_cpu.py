@@ -20,7 +20,9 @@ from oracle import safetensors_oracle as SO
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 GOLDEN = os.path.join(ROOT, "tests", "golden")
-REF_FIXTURES = "/root/reference/Engine/kotensor/src/test/resources/hf"
+# The reference's own fixtures (src/test/resources/hf), copied unchanged by
+# tests/golden/make_hf_golden.py.
+REF_FIXTURES = os.path.join(GOLDEN, "hf")
 
 
 @pytest.fixture(scope="module")
@@ -46,7 +48,6 @@ def test_oracle_conversion_matches_golden_fixture():
             assert _same_f32(got, z[name]), name
 
 
-@pytest.mark.skipif(not os.path.isdir(REF_FIXTURES), reason="reference fixtures not on this machine")
 def test_oracle_conversion_matches_reference_known_answers():
     """The reference's own dtype fixture and its expected values (HuggingFaceImportTest)."""
     d = os.path.join(REF_FIXTURES, "dtypes")
@@ -67,11 +68,10 @@ def test_half_to_float_matches_binary16_for_every_pattern():
 
 def _fixture_files():
     files = [os.path.join(GOLDEN, "dtypes.safetensors")]
-    if os.path.isdir(REF_FIXTURES):
-        for sub in sorted(os.listdir(REF_FIXTURES)):
-            for f in sorted(os.listdir(os.path.join(REF_FIXTURES, sub))):
-                if f.endswith(".safetensors"):
-                    files.append(os.path.join(REF_FIXTURES, sub, f))
+    for sub in sorted(os.listdir(REF_FIXTURES)):
+        for f in sorted(os.listdir(os.path.join(REF_FIXTURES, sub))):
+            if f.endswith(".safetensors"):
+                files.append(os.path.join(REF_FIXTURES, sub, f))
     return files
 
 
@@ -166,6 +166,19 @@ def test_malformed_files_fail_like_the_reference(st, tmp_path, case, header, dat
         st.SafeTensorsFile(path)
     with pytest.raises((ValueError, OSError, json.JSONDecodeError)):
         SO.parse(str(path))
+
+
+@pytest.mark.parametrize("case,header", [
+    # an end offset whose sum with the data start overflows int64 must not pass the bounds check
+    ("end near 2^63", b'{"a":{"dtype":"U8","shape":[1],"data_offsets":[0,9223372036854775800]}}'),
+    ("negative dimension", b'{"a":{"dtype":"U8","shape":[-1],"data_offsets":[0,1]}}'),
+    ("dimension beyond int32", b'{"a":{"dtype":"U8","shape":[4294967297],"data_offsets":[0,1]}}'),
+])
+def test_native_reader_rejects_out_of_range_numbers(st, tmp_path, case, header):
+    path = tmp_path / "bad.safetensors"
+    _write_raw(path, header, b"x")
+    with pytest.raises(ValueError):
+        st.SafeTensorsFile(path)
 
 
 def test_missing_file_is_an_io_error(st, tmp_path):
