@@ -160,8 +160,11 @@ kt_status kt_comm_destroy(kt_comm* comm);
  * memory (CUDA IPC areas set up on the first such call -- a collective -- and
  * agreed once per shard by every rank); KT_TP_FUSED=0 keeps the NCCL path.
  * Its waits for the other ranks are bounded: ranks that reach the same call more
- * than 2 s apart make it fail (context error word set, kt_ctx_take_error), where
- * NCCL would wait indefinitely. */
+ * than the communicator's wait limit apart (2 s unless kt_comm_set_wait_limit)
+ * make it fail (context error word set, kt_ctx_take_error), where NCCL would
+ * wait indefinitely; so does a rank whose flag shows a call other than this one.
+ * After such a failure the ranks' call counters disagree: call
+ * kt_comm_exchange_reset on every rank before the next fused call. */
 kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* w_shard, const float* a_shard_dev,
                                   float* c_dev, int32_t m, int32_t accumulate, float alpha, const float* bias_dev,
                                   void* stream);
@@ -169,6 +172,20 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
 /* 1 in *ready once this communicator's peer-memory exchange areas are set up
  * and every rank agreed to use them (the fused m = 1 row-parallel GEMV), else 0. */
 kt_status kt_comm_exchange_ready(const kt_comm* comm, int32_t* ready);
+
+/* Limit, in seconds (0 < seconds <= 3600), of a fused row-parallel call's wait
+ * for the other ranks' partials (no reference counterpart; default 2 s).
+ * Applies to calls launched after it; the context's other bounded waits (TMA
+ * copies inside a kernel) keep their 2 s limit. */
+kt_status kt_comm_set_wait_limit(kt_comm* comm, double seconds);
+
+/* Collective (every rank, same call order; no reference counterpart): waits
+ * until this rank's device is idle, agrees with every rank that all are, zeroes
+ * this rank's exchange area (call counter, flags, receive rows) and agrees
+ * again, so the next fused call starts from the same call number everywhere.
+ * Needed after a fused call failed (kt_ctx_take_error != 0); a no-op on a
+ * communicator whose exchange is not set up, apart from the agreements. */
+kt_status kt_comm_exchange_reset(kt_comm* comm, void* stream);
 
 /* Column-parallel outputs (kt_qmatmul on w_shard = kt_qweight_shard(W, axis 1,
  * P, rank), equal widths n_shard = N / P) gathered into y_full [m x N] on every rank. */
@@ -207,12 +224,16 @@ kt_status kt_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float
 
 /* kt_qmatmul for callers that must not have the library allocate device
  * memory (no counterpart in the reference, whose MatMul works in host
- * memory).  Same kernels and results; the split-K workspace of the INT4
- * tensor-core GEMV is a 4 MiB array inside the library image instead of a
- * buffer allocated on first use.  The first call on a device looks up that
- * array's address: make it before capturing a stream.  One array per device:
- * calls that overlap in time on a device race on it, so order them on one
- * stream.  Shapes whose workspace exceeds 4 MiB return KT_ERR_INVALID_ARGUMENT. */
+ * memory): a decode loop on a fixed memory budget, or a host runtime that
+ * accounts for every device byte itself.  The same kernels as kt_qmatmul for
+ * every m, with bit-identical results; their scratch (split-K counters and
+ * partial tiles of the INT4 tensor-core GEMVs, the bf16 activations and split-K
+ * partials of the tcgen05 GEMM) is a 16 MiB array inside the library image
+ * instead of a buffer allocated on first use.  The first call on a device
+ * looks up that array's address: make it before capturing a stream.  One array
+ * per device: calls that overlap in time on a device race on it, so order them
+ * on one stream.  Shapes whose scratch exceeds 16 MiB (e.g. the GEMM at
+ * m x K > 8 Mi activations) return KT_ERR_INVALID_ARGUMENT; kt_qmatmul takes them. */
 kt_status kt_qmatmul_noalloc(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float* c_dev, int32_t m,
                              int32_t accumulate, float alpha, const float* bias_dev, void* stream);
 

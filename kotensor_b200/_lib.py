@@ -97,6 +97,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_allgather_columns": ([P, P, P, I32, I32, P], I32),
     "kt_argmax_column_parallel": ([P, P, I32, I32, I32, P, P], I32),
     "kt_comm_exchange_ready": ([P, ctypes.POINTER(I32)], I32),
+    "kt_comm_set_wait_limit": ([P, ctypes.c_double], I32),
+    "kt_comm_exchange_reset": ([P, P], I32),
     "kt_rmsnorm": ([P, P, P, P, I32, I32, F32, P], I32),
     "kt_add_rmsnorm": ([P, P, P, P, P, I32, I32, F32, P], I32),
     "kt_rope_kv": ([P, P, I32, I32, I32, I32, P, P, P, I32, I32, P, P], I32),

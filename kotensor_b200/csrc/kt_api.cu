@@ -105,6 +105,16 @@ void free_weight(kt_qweight* w) {
 
 }  // namespace
 
+// 5..8 rows in two passes of the INT4 tensor-core GEMV: measured faster than
+// the fp32 streaming kernel from ~16 MB of weight bytes (4096 x 14336 INT4:
+// 2 x 19.9 us against 54 us), slower on small weights where the extra launch
+// dominates.
+bool mma_in_two_passes(const QView& v, int32_t m, const float* a) {
+    const int64_t weight_bytes = static_cast<int64_t>(v.rows) * v.bytes_per_row;
+    return m > kGemvMmaMaxM && m <= 2 * kGemvMmaMaxM && weight_bytes >= (static_cast<int64_t>(16) << 20) &&
+           gemv_mma_supported(v, kGemvMmaMaxM, a);
+}
+
 cudaError_t stream_workspace(kt_ctx* ctx, cudaStream_t s, size_t bytes, void** out) {
     std::lock_guard<std::mutex> lock(ctx->ws_mutex);
     kt_ctx::Workspace* hit = nullptr;
@@ -151,16 +161,6 @@ kt_status grow(float** buf, size_t* cap, size_t need) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
     *cap = need;
     return KT_OK;
-}
-
-// 5..8 rows in two passes of the INT4 tensor-core GEMV: measured faster than
-// the fp32 streaming kernel from ~16 MB of weight bytes (4096 x 14336 INT4:
-// 2 x 19.9 us against 54 us), slower on small weights where the extra launch
-// dominates.
-bool mma_in_two_passes(const QView& v, int32_t m, const float* a) {
-    const int64_t weight_bytes = static_cast<int64_t>(v.rows) * v.bytes_per_row;
-    return m > kGemvMmaMaxM && m <= 2 * kGemvMmaMaxM && weight_bytes >= (static_cast<int64_t>(16) << 20) &&
-           gemv_mma_supported(v, kGemvMmaMaxM, a);
 }
 
 kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,

@@ -94,7 +94,10 @@ __device__ __forceinline__ float ld_dsmem(uint32_t local, uint32_t rank) {
     return v;
 }
 // System-scope flag store / load (peer GPUs' memory) and a bounded wait for a
-// flag to reach `epoch` (wrap-around safe); false after the 2 s limit.
+// flag to reach `epoch`.  True only when the flag equals `epoch`: a flag beyond
+// it (wrap-around safe comparison) means the peer is more than one call ahead,
+// which only happens after an earlier call of the exchange timed out, and the
+// slot then holds another call's data -- false, as after `limit_ns`.
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -103,14 +106,16 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ bool wait_epoch_sys(const uint32_t* p, uint32_t epoch) {
-    if (static_cast<int32_t>(ld_acquire_sys(p) - epoch) >= 0) return true;
+__device__ __forceinline__ bool wait_epoch_sys(const uint32_t* p, uint32_t epoch, uint64_t limit_ns) {
+    uint32_t v = ld_acquire_sys(p);
+    if (v == epoch) return true;
     const uint64_t t0 = globaltimer();
-    while (static_cast<int32_t>(ld_acquire_sys(p) - epoch) < 0) {
-        if (globaltimer() - t0 > kWaitLimitNs) return false;
+    while (static_cast<int32_t>(v - epoch) < 0) {
+        if (globaltimer() - t0 > limit_ns) return false;
         __nanosleep(100);
+        v = ld_acquire_sys(p);
     }
-    return true;
+    return v == epoch;
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }

@@ -45,6 +45,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 
 #include "kt_internal.h"
@@ -554,9 +555,17 @@ cudaError_t launch_cfg(const QView& w, const GemvParams& p, const GemvConfig& cf
 struct GemvOverrides {
     int lb, ck;
 };
-GemvOverrides& overrides() {
-    static GemvOverrides o{env_int("KT_GEMV_LB", 0), env_int("KT_GEMV_CK", 0)};
-    return o;
+// Process-wide, set and read from any host thread.
+std::atomic<int>& override_lb() {
+    static std::atomic<int> v{env_int("KT_GEMV_LB", 0)};
+    return v;
+}
+std::atomic<int>& override_ck() {
+    static std::atomic<int> v{env_int("KT_GEMV_CK", 0)};
+    return v;
+}
+GemvOverrides overrides() {
+    return GemvOverrides{override_lb().load(std::memory_order_relaxed), override_ck().load(std::memory_order_relaxed)};
 }
 
 // One CTA per SM: pick bytes per lane and the K-cluster so the grid covers as
@@ -637,7 +646,10 @@ GemvParams make_params(const QView& w, const MatmulArgs& a) {
 
 }  // namespace
 
-void set_gemv_tuning(int lane_bytes, int cluster_k) { overrides() = GemvOverrides{lane_bytes, cluster_k}; }
+void set_gemv_tuning(int lane_bytes, int cluster_k) {
+    override_lb().store(lane_bytes, std::memory_order_relaxed);
+    override_ck().store(cluster_k, std::memory_order_relaxed);
+}
 
 bool gemv_fast_supported(const QView& w, int32_t m, const float* a) {
     if (m < 1 || m > kGemvMaxM || w.tmap_w128 == nullptr) return false;

@@ -34,6 +34,7 @@
 // split over CTAs when the column tiles alone cannot fill the GPU; the last
 // CTA of a tile sums the split partials in split order (deterministic).
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 
 #include "kt_device.cuh"
@@ -414,7 +415,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int64_t f = (static_cast<int64_t>(epoch & 1u) * p.tp.tile_cap + blockIdx.x) * P;
             for (int q = 0; q < P; ++q) st_release_sys(p.tp.flags[q] + f + p.tp.rank, epoch);
             bool ok = true;
-            for (int src = 0; src < P && ok; ++src) ok = wait_epoch_sys(p.tp.flags[p.tp.rank] + f + src, epoch);
+            for (int src = 0; src < P && ok; ++src)
+                ok = wait_epoch_sys(p.tp.flags[p.tp.rank] + f + src, epoch, p.tp.wait_ns);
             if (!ok) atomicOr(p.err, 1);
             s_tp_ok = ok ? 1 : 0;
         }
@@ -492,13 +494,18 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 int tiles_of(int R) { return (R + kTileBytes - 1) / kTileBytes; }
 
+// Per-device caches below are atomics: host threads may launch on one device
+// concurrently (a lost race only repeats an idempotent query).
 int blocks_per_sm() {
     constexpr int kMaxDevices = 64;
-    static int cache[kMaxDevices] = {};
+    static std::atomic<int> cache[kMaxDevices] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    int* slot = dev >= 0 && dev < kMaxDevices ? &cache[dev] : nullptr;
-    if (slot != nullptr && *slot != 0) return *slot;
+    std::atomic<int>* slot = dev >= 0 && dev < kMaxDevices ? &cache[dev] : nullptr;
+    if (slot != nullptr) {
+        const int c = slot->load(std::memory_order_acquire);
+        if (c != 0) return c;
+    }
     int n = 0;
     if (cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) != cudaSuccess ||
@@ -506,7 +513,7 @@ int blocks_per_sm() {
         n = 1;
     cudaGetLastError();
     n = std::max(n, 1);
-    if (slot != nullptr) *slot = n;
+    if (slot != nullptr) slot->store(n, std::memory_order_release);
     return n;
 }
 
@@ -515,11 +522,11 @@ int min_splits(int K) {
     return (K + per - 1) / per;
 }
 
-int& split_override() {
-    static int o = [] {
+std::atomic<int>& split_override() {
+    static std::atomic<int> o{[] {
         const char* v = std::getenv("KT_IMMA_SPLITS");
         return v ? std::atoi(v) : 0;
-    }();
+    }()};
     return o;
 }
 
@@ -533,7 +540,8 @@ int choose_splits(int R, int K, int sm_count) {
     const int k_stages = K / kRowsPerStage;
     int s = std::min(kMaxSplits, std::max(1, slots / tiles));
     s = std::min(s, std::max(1, k_stages / kPairs));
-    if (split_override() >= 1) s = split_override();
+    const int pinned = split_override().load(std::memory_order_relaxed);
+    if (pinned >= 1) s = pinned;
     s = std::max(s, min_splits(K));
     return tiles > kTicketCapEach ? min_splits(K) : s;
 }
@@ -542,26 +550,29 @@ int choose_splits(int R, int K, int sm_count) {
 // (setting them on every launch costs host time on a latency-bound call).
 cudaError_t prepare_kernel() {
     constexpr int kMaxDevices = 64;
-    static bool done[kMaxDevices] = {};
+    static std::atomic<bool> done[kMaxDevices] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < kMaxDevices && done[dev]) return cudaSuccess;
+    if (dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
     e = cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes));
     if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) done[dev] = true;
+    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) done[dev].store(true, std::memory_order_release);
     return e;
 }
 
 // Clusters of `c` CTAs of this kernel the GPU holds at once (cached per device).
 int active_clusters(int c) {
     constexpr int kMaxDevices = 64;
-    static int cache[kMaxDevices][kMaxSplits + 1] = {};
+    static std::atomic<int> cache[kMaxDevices][kMaxSplits + 1] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    int* slot = dev >= 0 && dev < kMaxDevices ? &cache[dev][c] : nullptr;
-    if (slot != nullptr && *slot != 0) return *slot - 1;
+    std::atomic<int>* slot = dev >= 0 && dev < kMaxDevices ? &cache[dev][c] : nullptr;
+    if (slot != nullptr) {
+        const int v = slot->load(std::memory_order_acquire);
+        if (v != 0) return v - 1;
+    }
     int n = 0;
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(1, c, 1);
@@ -580,7 +591,7 @@ int active_clusters(int c) {
         cudaOccupancyMaxActiveClusters(&n, gemv_imma_kernel, &lc) != cudaSuccess)
         n = 0;
     cudaGetLastError();
-    if (slot != nullptr) *slot = n + 1;
+    if (slot != nullptr) slot->store(n + 1, std::memory_order_release);
     return n;
 }
 
@@ -610,7 +621,7 @@ Plan plan_for(int R, int K, int sm_count, bool no_cluster = false) {
     if (!no_cluster && s > 1 && s <= kMaxSplits && clusters_enabled() && stages_per_slice <= 4) {
         for (int c = s; c >= std::max(2, min_splits(K)); --c) {
             if (active_clusters(c) >= tiles) return {c, true};
-            if (split_override() >= 1) break;  // a pinned count is used as given
+            if (split_override().load(std::memory_order_relaxed) >= 1) break;  // a pinned count is used as given
         }
     }
     return {s, false};
@@ -618,7 +629,7 @@ Plan plan_for(int R, int K, int sm_count, bool no_cluster = false) {
 
 }  // namespace
 
-void set_imma_tuning(int k_splits) { split_override() = k_splits; }
+void set_imma_tuning(int k_splits) { split_override().store(k_splits, std::memory_order_relaxed); }
 
 bool gemv_imma_supported(const QView& w, int32_t m, const float* a) {
     if (w.bits != 4 || m != 1 || w.tmap_mma == nullptr) return false;

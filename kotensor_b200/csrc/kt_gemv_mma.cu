@@ -57,6 +57,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 
 #include "kt_internal.h"
@@ -578,24 +579,27 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 struct MmaOverrides {
-    int splits;
+    std::atomic<int> splits;
 };
 MmaOverrides& mma_overrides() {
-    static MmaOverrides o{[] {
+    static MmaOverrides o{{[] {
         const char* v = std::getenv("KT_MMA_SPLITS");
         return v ? std::atoi(v) : 0;
-    }()};
+    }()}};
     return o;
 }
 
 // CTAs of this kernel one SM holds (cached per device).
 int blocks_per_sm() {
     constexpr int kMaxDevices = 64;
-    static int cache[kMaxDevices] = {};
+    static std::atomic<int> cache[kMaxDevices] = {};  // host threads may race here
     int dev = 0;
     cudaGetDevice(&dev);
-    int* slot = dev >= 0 && dev < kMaxDevices ? &cache[dev] : nullptr;
-    if (slot != nullptr && *slot != 0) return *slot;
+    std::atomic<int>* slot = dev >= 0 && dev < kMaxDevices ? &cache[dev] : nullptr;
+    if (slot != nullptr) {
+        const int c = slot->load(std::memory_order_acquire);
+        if (c != 0) return c;
+    }
     int n = 0;
     auto kernel = gemv_mma_kernel<1>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)) !=
@@ -604,7 +608,7 @@ int blocks_per_sm() {
         n = 1;
     cudaGetLastError();
     n = std::max(n, 1);
-    if (slot != nullptr) *slot = n;
+    if (slot != nullptr) slot->store(n, std::memory_order_release);
     return n;
 }
 
@@ -639,7 +643,7 @@ int choose_splits(int R, int K, int m, int sm_count) {
     const int k_stages = K / kRowsPerStage;
     int s = std::max(1, slots / tiles);
     s = std::min(s, std::max(1, k_stages / kPairs));
-    const int o = mma_overrides().splits;
+    const int o = mma_overrides().splits.load(std::memory_order_relaxed);
     if (o >= 1) s = o;
     s = std::max(s, min_splits(K, m));
     return tiles > kTicketCap ? min_splits(K, m) : s;
@@ -666,7 +670,7 @@ cudaError_t launch_m(const QView& w, const MmaParams& p, int splits, cudaStream_
 
 }  // namespace
 
-void set_mma_tuning(int k_splits) { mma_overrides().splits = k_splits; }
+void set_mma_tuning(int k_splits) { mma_overrides().splits.store(k_splits, std::memory_order_relaxed); }
 
 bool gemv_mma_supported(const QView& w, int32_t m, const float* a) {
     (void)a;

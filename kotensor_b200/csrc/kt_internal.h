@@ -107,6 +107,10 @@ __device__ __forceinline__ float lora_term(const LoraEpilogue& l, int t, int col
 }
 #endif
 
+// m = 5..8 on a weight large enough that two passes of the m <= 4 INT4
+// tensor-core GEMV beat one fp32 streaming pass (kt_api.cu).
+bool mma_in_two_passes(const QView& v, int32_t m, const float* a);
+
 // The dispatch behind kt_qmatmul (kt_api.cu): argument-checked by the caller.
 kt_status run_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
                       float alpha, const float* bias, cudaStream_t s, const LoraEpilogue* lora = nullptr);
@@ -174,6 +178,7 @@ struct TpExchange {
     uint32_t* const* flags = nullptr;  // device array [P]: rank q's flags, mapped here ([2][tile_cap][P])
     uint32_t* state = nullptr;         // this rank's own {calls completed, CTAs exited in this call}
     int32_t nranks = 0, rank = 0, n_cap = 0, tile_cap = 0;
+    uint64_t wait_ns = 0;              // limit of the wait for the other ranks' flags
 };
 
 struct MatmulArgs {

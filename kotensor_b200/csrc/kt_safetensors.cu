@@ -604,7 +604,12 @@ void parse_header(kt_stfile* f) {
         if (shape && shape->kind == JValue::Arr) {
             if (shape->arr.size() > static_cast<size_t>(kMaxRank))
                 bad("Tensor " + name + " has more than " + std::to_string(kMaxRank) + " dimensions");
-            for (const auto& d : shape->arr) e.shape.push_back(static_cast<int32_t>(as_long(d, "shape of " + name)));
+            for (const auto& d : shape->arr) {
+                const int64_t dim = as_long(d, "shape of " + name);
+                if (dim < 0 || dim > INT32_MAX)
+                    bad("Tensor " + name + " has dimension " + std::to_string(dim) + " outside [0, 2^31)");
+                e.shape.push_back(static_cast<int32_t>(dim));
+            }
         }
         if (!offsets || offsets->kind != JValue::Arr || offsets->arr.size() < 2)
             bad("Tensor " + name + " has no data_offsets");
@@ -612,7 +617,7 @@ void parse_header(kt_stfile* f) {
         const int64_t end = as_long(offsets->arr[1], "data_offsets of " + name);
         // The reference checks end >= start and the end against the file size;
         // a negative start is refused as well.
-        if (start < 0 || end < start || f->data_start + end > f->file_bytes)
+        if (start < 0 || end < start || end > f->file_bytes - f->data_start)  // no signed overflow
             bad("Tensor " + name + " data range [" + std::to_string(start) + ", " + std::to_string(end) +
                 ") exceeds file " + std::to_string(f->file_bytes));
         e.offset = start;

@@ -190,6 +190,7 @@ struct kt_comm {
     void* peers[kTpMaxRanks] = {};      // every rank's area as mapped here (own at [rank])
     float** d_recv = nullptr;           // device arrays of the P receive / flag pointers
     uint32_t** d_flags = nullptr;
+    uint64_t wait_ns = 2000000000ull;   // limit of a fused call's wait for the other ranks (2 s)
 };
 
 namespace {
@@ -410,6 +411,7 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
             args.tp.rank = comm->rank;
             args.tp.n_cap = kTpNCap;
             args.tp.tile_cap = kTpTileCap;
+            args.tp.wait_ns = comm->wait_ns;
             args.tp.state = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(comm->area) +
                                                         tp_recv_bytes(comm->nranks) + tp_flag_bytes(comm->nranks));
             const size_t need = kt::gemv_imma_workspace_bytes(v, ctx->sm_count, true);
@@ -451,6 +453,35 @@ kt_status kt_allgather_columns(kt_comm* comm, const float* y_shard, float* y_ful
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("gather columns: ") + cudaGetErrorString(e));
     return KT_OK;
+}
+
+kt_status kt_comm_set_wait_limit(kt_comm* comm, double seconds) {
+    if (!comm) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (!(seconds > 0.0) || seconds > 3600.0)
+        return fail_tp(KT_ERR_INVALID_ARGUMENT, "wait limit must be in (0, 3600] seconds");
+    comm->wait_ns = static_cast<uint64_t>(seconds * 1e9);
+    return KT_OK;
+}
+
+// Collective: after a fused call timed out, the ranks' call counters and flags
+// disagree.  Every rank waits for its own work, all ranks agree that they are
+// idle, each zeroes its exchange area (counters, flags, receive rows), and a
+// second agreement makes sure no rank starts a call before every area is clear.
+kt_status kt_comm_exchange_reset(kt_comm* comm, void* stream) {
+    if (!comm) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSetDevice(comm->ctx->device);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("exchange reset: ") + cudaGetErrorString(e));
+    bool every = false;
+    kt_status st = all_agree(comm, true, s, &every);
+    if (st != KT_OK) return st;
+    if (comm->p2p_state == 1) {
+        e = cudaMemsetAsync(comm->area, 0, tp_area_bytes(comm->nranks), s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("exchange reset: ") + cudaGetErrorString(e));
+    }
+    return all_agree(comm, true, s, &every);
 }
 
 kt_status kt_comm_exchange_ready(const kt_comm* comm, int32_t* ready) {

@@ -145,6 +145,17 @@ class Comm:
         _lib.check(_lib.load().kt_comm_exchange_ready(self.handle, ctypes.byref(out)))
         return bool(out.value)
 
+    def set_wait_limit(self, seconds: float) -> None:
+        """Limit of a fused row-parallel call's wait for the other ranks (default 2 s)."""
+        _lib.check(_lib.load().kt_comm_set_wait_limit(self.handle, float(seconds)))
+
+    def reset_exchange(self) -> None:
+        """Collective: clears every rank's exchange area after a fused call
+        failed (kt_comm_exchange_reset), on torch's current stream."""
+        import torch
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self._ctx.device).cuda_stream)
+        _lib.check(_lib.load().kt_comm_exchange_reset(self.handle, stream))
+
     def close(self) -> None:
         if self._handle:
             _lib.load().kt_comm_destroy(self._handle)

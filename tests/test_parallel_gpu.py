@@ -264,3 +264,70 @@ def test_tensor_parallel_on_two_gpus(kt, tmp_path):
             assert rel_err(y1, ref1) <= TOL_FP32
     # every rank holds the same bits (rank-order sum of the same partials)
     assert np.array_equal(np.load(tmp_path / "m1_0.npy")[:, 1], np.load(tmp_path / "m1_1.npy")[:, 1])
+
+
+def _two_gpu_timeout_rank(rank, world, port, out_dir):
+    """Rank 1 skips one fused row-parallel call: rank 0's bounded wait for its
+    partials runs out (a flag nothing sets), the call fails with the context
+    error word set instead of hanging, the ranks learn of it on the host, reset
+    the exchange together and the next call is correct on both."""
+    from datetime import timedelta
+    import torch.distributed as dist
+    import kotensor_b200 as kt
+    from kotensor_b200 import parallel as P
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    comm = None
+    try:
+        ctx = kt.Context.get(rank)
+        comm = P.Comm.from_process_group(ctx=ctx)
+        k, n = 4096, 2048
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(23)
+        w = torch.randn((k, n), generator=gen, device="cuda") * 0.02
+        x = torch.randn((2, k), generator=gen, device="cuda")
+        qt = kt.QuantizedTensor.quantize(w, kt.Quantization(4))
+        row = P.RowParallelQuantizedLinear(qt, comm)
+        y = torch.empty((1, n), device="cuda")
+        row.forward_into(x[0:1, row.k_begin:row.k_end].contiguous(), y)  # sets the exchange up
+        torch.cuda.synchronize()
+        assert comm.exchange_ready() and ctx.take_error() == 0
+        comm.set_wait_limit(0.005)
+        errors = torch.zeros(1, dtype=torch.int32)
+        if rank == 0:
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            row.forward_into(x[0:1, row.k_begin:row.k_end].contiguous(), y)  # rank 1 never arrives
+            t1.record()
+            torch.cuda.synchronize()
+            errors[0] = ctx.take_error()
+            np.save(os.path.join(out_dir, "timeout_ms.npy"), np.array([t0.elapsed_time(t1)]))
+        dist.all_reduce(errors)  # every rank learns of the failure on the host
+        assert int(errors[0]) != 0
+        comm.set_wait_limit(2.0)
+        comm.reset_exchange()
+        x1 = x[1:2].contiguous()
+        ref = torch.empty((1, n), device="cuda")
+        kt.MatMul.multiply_quantized(x1, qt, ref, 1, accumulate=False)
+        row.forward_into(x1[:, row.k_begin:row.k_end].contiguous(), y)
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"after_{rank}.npy"), np.stack([ref.cpu().numpy()[0], y.cpu().numpy()[0]]))
+        assert ctx.take_error() == 0
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_fused_exchange_times_out_and_recovers_on_two_gpus(kt, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_two_gpu_timeout_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    assert float(np.load(tmp_path / "timeout_ms.npy")[0]) < 1000.0  # the 5 ms limit, not the 2 s default
+    for r in range(2):
+        ref, y = np.load(tmp_path / f"after_{r}.npy")
+        assert rel_err(y, ref) <= TOL_FP32

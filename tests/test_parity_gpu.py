@@ -444,3 +444,66 @@ def test_int8_tensor_core_gemm_matches_the_oracle(kt, oracle, m, k, n, g):
     ref = oracle.multiply_quantized(a, ref_t, c=c0, accumulate=True, alpha=0.5, threads=8) + bias[None, :]
     assert rel_err(y, ref) <= TOL_BF16, rel_err(y, ref)
     assert kt.Context.get().take_error() == 0
+
+
+BENCH_SHAPES = [(2048, 5632), (5632, 2048), (4096, 14336), (14336, 4096)]  # BASELINE config 2 (K, N)
+
+
+@pytest.mark.parametrize("k,n", BENCH_SHAPES)
+def test_bench_weights_gemv_against_oracle(kt, oracle, k, n):
+    """The four weights bench.py times, quantized on the
+    device (bit-exact) and multiplied at m = 1 on the integer tensor-core GEMV,
+    plus m = 4 and two passes of m = 4 (m = 8) on the fp16 one."""
+    from kotensor_b200 import _lib
+    rng = np.random.default_rng(k + 3 * n)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    qt = kt.QuantizedTensor.quantize(dev(w), kt.Quantization(4))
+    ref_t = oracle.quantize(w, 4, 64)
+    q, s, z = qt.download()
+    assert np.array_equal(q, ref_t.qdata) and np.array_equal(s.view(np.uint32), ref_t.scales.view(np.uint32))
+    assert np.array_equal(z, ref_t.zeros)
+    assert qt.matmul_path(1) == _lib.KT_PATH_GEMV_MMA
+    for m in (1, 4, 8):
+        a = rng.standard_normal((m, k), dtype=np.float32)
+        y = run_matmul(kt, qt, a)
+        assert rel_err(y, oracle.multiply_quantized(a, ref_t, threads=8)) <= TOL_FP32, m
+    assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("k,n", [(4096, 14336), (14336, 4096)])
+@pytest.mark.parametrize("m", [16, 128, 512])
+def test_bench_weights_gemm_against_oracle(kt, oracle, k, n, m):
+    """The prefill / batched-decode GEMM on the Llama-8B FFN weights bench.py
+    times (BASELINE config 2 at M = 16, 128, 512), within the bf16 tolerance."""
+    from kotensor_b200 import _lib
+    rng = np.random.default_rng(k + n + m)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 4, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, 64)
+    assert qt.matmul_path(m) == _lib.KT_PATH_TENSOR_CORE
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    y = run_matmul(kt, qt, a)
+    assert rel_err(y, oracle.multiply_quantized(a, ref_t, threads=8)) <= TOL_BF16
+    assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("k,n", BENCH_SHAPES)
+@pytest.mark.parametrize("factor,count", [(50.0, 1), (100.0, 1), (100.0, 4), (75.0, 16)])
+def test_int4_gemv_with_outlier_channels(kt, oracle, k, n, factor, count):
+    """LLM-style activations: a few channels at 50-100x the row's rms inside one
+    1,024-row slice.  The m = 1 kernel rounds x to 15 bits relative to the
+    largest |x| among each warp's rows, so an outlier coarsens its neighbours'
+    rounding; the result must stay within the fp32 tolerance."""
+    rng = np.random.default_rng(int(factor) * count + k)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 4, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, 64)
+    a = rng.standard_normal((1, k), dtype=np.float32)
+    rms = float(np.sqrt(np.mean(a.astype(np.float64) ** 2)))
+    base = int(rng.integers(0, k // 1024)) * 1024
+    idx = base + rng.choice(1024, count, replace=False)
+    a[0, idx] = (np.where(rng.random(count) < 0.5, -1.0, 1.0) * factor * rms).astype(np.float32)
+    y = run_matmul(kt, qt, a)
+    ref = oracle.multiply_quantized(a, ref_t, threads=8)
+    assert rel_err(y, ref) <= TOL_FP32, rel_err(y, ref)
+    assert kt.Context.get().take_error() == 0
