@@ -73,6 +73,30 @@ def rope_inv_freq(head_dim: int, base: float, scaling: Optional[tuple]) -> np.nd
     return out
 
 
+def tensor_parallel_plan(cfg: DecoderConfig, parts: int, rank: int) -> dict:
+    """Rank ``rank``'s share of a decoder split over ``parts`` ranks: query and
+    key/value heads (contiguous blocks), the columns [q0, q1) of the query
+    projection (= the rows of the output projection), [k0, k1) of the key and
+    value projections, the block [h0, h1) of whole groups of the hidden width
+    (gate / up columns, down-projection rows) and the lm head's vocabulary
+    columns [v0, v1).  Requires heads and kv_heads divisible by ``parts`` and
+    the output projection's rows to split on group boundaries."""
+    from .parallel import COLUMNS, ROWS, shard_bounds
+    if parts < 1 or not 0 <= rank < parts:
+        raise ValueError(f"rank {rank} of {parts}")
+    if cfg.heads % parts or cfg.kv_heads % parts:
+        raise ValueError(f"{cfg.heads} query / {cfg.kv_heads} key-value heads do not split over {parts} ranks")
+    hd, g = cfg.head_dim, cfg.group_size
+    heads, kv = cfg.heads // parts, cfg.kv_heads // parts
+    q0, q1 = rank * heads * hd, (rank + 1) * heads * hd
+    k0, k1 = rank * kv * hd, (rank + 1) * kv * hd
+    if parts > 1 and (q0 % g or (q1 % g and q1 != cfg.dim)):
+        raise ValueError(f"{q1 - q0} output-projection rows per rank is not a multiple of the group size {g}")
+    hidden = shard_bounds(ROWS, cfg.hidden, g, parts, rank) if parts > 1 else (0, cfg.hidden)
+    vocab = shard_bounds(COLUMNS, cfg.vocab, g, parts, rank) if parts > 1 else (0, cfg.vocab)
+    return {"heads": heads, "kv_heads": kv, "q": (q0, q1), "kv": (k0, k1), "hidden": hidden, "vocab": vocab}
+
+
 def _upload(w) -> QuantizedTensor:
     """A QuantizedTensor, or host arrays in the reference layout (objects with
     qdata / scales / zeros / rows / columns / bits / group_size)."""
@@ -96,11 +120,26 @@ class DeviceDecoder:
     of dicts with wq wk wv wo wg wu wd, their biases bq bk bv bo bg bu bd and the
     RMSNorm weights norm1 norm2), ``final_norm``, ``head`` ([dim x vocab]),
     ``head_bias``.  ``batch`` sequences decode together (one KV cache each, the
-    same position): every matmul of a step runs at m = batch."""
+    same position): every matmul of a step runs at m = batch.
+
+    ``comm`` (a parallel.Comm over P ranks, one process per GPU, every rank
+    building the decoder from the same weights): tensor parallelism
+    (``tensor_parallel_plan``).  Rank r keeps its block of query heads and of
+    key/value heads -- the q|k|v projection column-parallel over them,
+    attention and its KV cache local -- the output projection row-parallel over
+    the same rows, the gate|up projection column-parallel and the down
+    projection row-parallel over one block of whole groups of the hidden width,
+    and the lm head column-parallel over the vocabulary with the greedy argmax
+    taken across shards (argmaxOfLastToken's rule, Transformer.kt:255-266).
+    The two row-parallel products of a layer end in the only exchange: an
+    all-reduce of [batch x dim] partial sums (fused into the m = 1 GEMV over
+    peer memory, else NCCL), after which every rank holds the whole residual
+    stream."""
 
     max_block_rows = 65535
 
-    def __init__(self, cfg: DecoderConfig, weights, max_seq: int, device: Optional[int] = None, batch: int = 1):
+    def __init__(self, cfg: DecoderConfig, weights, max_seq: int, device: Optional[int] = None, batch: int = 1,
+                 comm=None):
         self.cfg = cfg
         self.max_seq = max_seq
         self.ctx = Context.get(device)
@@ -112,36 +151,59 @@ class DeviceDecoder:
                 return a.detach().to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
             return torch.as_tensor(np.ascontiguousarray(a, dtype=np.float32).reshape(-1)).to(dev)
 
-        from .parallel import concat_columns
+        from .parallel import COLUMNS, ROWS, concat_columns, slice_weight
+        self.comm = comm
+        P = comm.world if comm is not None else 1
+        plan = tensor_parallel_plan(cfg, P, comm.rank if comm is not None else 0)
+        self.parts = P
+        self.heads_local, self.kv_local = plan["heads"], plan["kv_heads"]
+        q0, q1 = plan["q"]
+        k0, k1 = plan["kv"]
+        h0, h1 = plan["hidden"]
+        v0, v1 = plan["vocab"]
+        self.q_width, self.kv_width = q1 - q0, k1 - k0
+        self.hidden_local, self.vocab_begin, self.vocab_local = h1 - h0, v0, v1 - v0
+
+        def cols(w, b, e):
+            return w if P == 1 else slice_weight(w, COLUMNS, b, e)
+
         self.layers = []
         for L in weights.layers:
             d = {k: (_upload(v) if k.startswith("w") else vec(v)) for k, v in L.items()}
             # q|k|v and gate|up as one matmul each: per-column quantization makes
             # the fused weight's columns exactly the separate weights' columns
-            d["wqkv"] = concat_columns([d["wq"], d["wk"], d["wv"]])
-            d["bqkv"] = torch.cat([d["bq"], d["bk"], d["bv"]])
-            d["wgu"] = concat_columns([d["wg"], d["wu"]])
-            d["bgu"] = torch.cat([d["bg"], d["bu"]])
+            # (and a rank's column shard exactly those columns of the weight)
+            d["wqkv"] = concat_columns([cols(d["wq"], q0, q1), cols(d["wk"], k0, k1), cols(d["wv"], k0, k1)])
+            d["bqkv"] = torch.cat([d["bq"][q0:q1], d["bk"][k0:k1], d["bv"][k0:k1]])
+            d["wgu"] = concat_columns([cols(d["wg"], h0, h1), cols(d["wu"], h0, h1)])
+            d["bgu"] = torch.cat([d["bg"][h0:h1], d["bu"][h0:h1]])
+            if P > 1:  # row-parallel: this rank's rows; the bias is added once, after the exchange
+                d["wo"] = slice_weight(d["wo"], ROWS, q0, q1)
+                d["wd"] = slice_weight(d["wd"], ROWS, h0, h1)
             for k in ("wq", "wk", "wv", "wg", "wu", "bq", "bk", "bv", "bg", "bu"):
                 del d[k]
             self.layers.append(d)
-        self.head = _upload(weights.head)
-        self.head_bias = vec(weights.head_bias)
+        full_head = _upload(weights.head)
+        self.head = cols(full_head, v0, v1)
+        self.head_bias = vec(weights.head_bias)[v0:v1].contiguous()
+        # tied embeddings look tokens up in the whole head (any column may be asked for)
+        self.lookup_head = full_head if cfg.tied else None
         self.embedding = None if cfg.tied else _upload(weights.embedding)
         self.final_norm = vec(weights.final_norm)
         if batch < 1:
             raise ValueError(f"batch must be positive, got {batch}")
         self.batch = batch
         # one KV cache per sequence, each in the reference's layout [L][kvH][maxSeq][hd]
-        self.keys = torch.zeros((batch, cfg.layers, cfg.kv_heads, max_seq, cfg.head_dim), **f32)
+        # (this rank's key/value heads under tensor parallelism)
+        self.keys = torch.zeros((batch, cfg.layers, self.kv_local, max_seq, cfg.head_dim), **f32)
         self.values = torch.zeros_like(self.keys)
-        self.cache_stride = cfg.layers * cfg.kv_heads * max_seq * cfg.head_dim
+        self.cache_stride = cfg.layers * self.kv_local * max_seq * cfg.head_dim
         self.inv_freq = vec(rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling))
         self.token = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.next_token = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.position = torch.zeros(1, dtype=torch.int32, device=dev)  # shared: sequences advance together
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.logits = torch.empty((batch, cfg.vocab), **f32)
+        self.logits = torch.empty((batch, self.vocab_local), **f32)  # this rank's vocabulary columns
         self._head_in = torch.empty((batch, cfg.dim), **f32)
         self._last_rows = torch.empty(batch, dtype=torch.int32, device=dev)
         self._step_bufs = self._buffers(batch, tokens=self.token)
@@ -149,6 +211,8 @@ class DeviceDecoder:
         self.length = 0
         self.scale = float(np.float32(1.0) / np.float32(math.sqrt(float(cfg.head_dim))))
         self._graph = None
+        if P > 1:
+            self._warm_exchanges()
 
     # -- helpers
     @staticmethod
@@ -171,16 +235,57 @@ class DeviceDecoder:
         b.rows = rows
         b.x = torch.empty((rows, cfg.dim), **f32)
         b.normed = torch.empty((rows, cfg.dim), **f32)
-        b.qkv = torch.empty((rows, cfg.dim + 2 * kv), **f32)
-        b.ctx = torch.empty((rows, cfg.dim), **f32)
+        b.qkv = torch.empty((rows, self.q_width + 2 * self.kv_width), **f32)
+        b.ctx = torch.empty((rows, self.q_width), **f32)
         b.attn = torch.empty((rows, cfg.dim), **f32)
-        b.gu = torch.empty((rows, 2 * cfg.hidden), **f32)
-        b.act = torch.empty((rows, cfg.hidden), **f32)
+        b.gu = torch.empty((rows, 2 * self.hidden_local), **f32)
+        b.act = torch.empty((rows, self.hidden_local), **f32)
         b.ffn = torch.empty((rows, cfg.dim), **f32)
         b.tokens = tokens if tokens is not None else torch.empty(rows, dtype=torch.int32, device=dev)
-        b.scores = torch.empty(_lib.load().kt_attention_scratch_floats(rows, cfg.heads, cfg.head_dim, self.max_seq),
-                               **f32)  # attention scratch
+        b.scores = torch.empty(_lib.load().kt_attention_scratch_floats(rows, self.heads_local, cfg.head_dim,
+                                                                       self.max_seq), **f32)  # attention scratch
         return b
+
+    def _row_parallel(self, x, w, out, rows: int, bias) -> None:
+        """out[rows x dim] = x . W + bias: the local product, or under tensor
+        parallelism this rank's rows of W and the all-reduce of the partials."""
+        if self.comm is None:
+            MatMul.multiply_quantized(x, w, out, rows, accumulate=False, bias=bias)
+        else:
+            from .parallel import matmul_row_parallel
+            matmul_row_parallel(self.comm, x, w, out, rows, accumulate=False, bias=bias)
+
+    def _warm_exchanges(self) -> None:
+        """Collective (every rank, at construction): each row-parallel shard
+        agrees its exchange once at m = batch (the fused peer-memory GEMV at
+        m = 1 is set up and agreed on its first call, and the agreement
+        synchronizes the stream, which a CUDA graph capture cannot), and the
+        communicator's scratch grows to the step's size, so a captured step
+        neither sets up nor allocates."""
+        dev = self.position.device
+        m = self.batch
+        x_o = torch.zeros((m, self.q_width), dtype=torch.float32, device=dev)
+        x_d = torch.zeros((m, self.hidden_local), dtype=torch.float32, device=dev)
+        out = torch.empty((m, self.cfg.dim), dtype=torch.float32, device=dev)
+        for L in self.layers:
+            self._row_parallel(x_o, L["wo"], out, m, None)
+            self._row_parallel(x_d, L["wd"], out, m, None)
+        from .parallel import argmax_column_parallel
+        self.logits.zero_()
+        argmax_column_parallel(self.comm, self.logits, self.vocab_begin, self.next_token)
+        torch.cuda.current_stream(self.ctx.device).synchronize()
+
+    def gather_logits(self):
+        """The whole [batch x vocab] logits on every rank (an all-gather of the
+        ranks' vocabulary columns; the logits themselves when not sharded)."""
+        if self.comm is None:
+            return self.logits
+        from .parallel import allgather_columns
+        if self.cfg.vocab % self.parts:
+            raise ValueError("the vocabulary does not split evenly: gather the shards with their offsets")
+        full = torch.empty((self.batch, self.cfg.vocab), dtype=torch.float32, device=self.logits.device)
+        allgather_columns(self.comm, self.logits, full, self.batch)
+        return full
 
     def _layers(self, b: "_Rows", rows: int, rows_per_seq: int, seq0: int = 0) -> None:
         """Embedding lookup of b.tokens[:rows] through every block; leaves the
@@ -192,27 +297,28 @@ class DeviceDecoder:
         s, p = self._stream(), self._p
         keys = ctypes.c_void_p(self.keys.data_ptr() + seq0 * self.cache_stride * self.keys.element_size())
         values = ctypes.c_void_p(self.values.data_ptr() + seq0 * self.cache_stride * self.values.element_size())
-        hd, kvh = cfg.head_dim, cfg.kv_heads
-        kv = kvh * hd
+        hd, kvh = cfg.head_dim, self.kv_local
+        kv = self.kv_width
         if cfg.tied:
-            _lib.check(L_.kt_dequantize_column(h, self.head.handle, p(b.tokens), rows, p(b.x), p(self.status), s))
+            _lib.check(L_.kt_dequantize_column(h, self.lookup_head.handle, p(b.tokens), rows, p(b.x), p(self.status),
+                                               s))
         else:
             _lib.check(L_.kt_dequantize_rows(h, self.embedding.handle, p(b.tokens), rows, p(b.x), p(self.status), s))
         _lib.check(L_.kt_rmsnorm(h, p(b.x), p(self.layers[0]["norm1"]), p(b.normed), rows, cfg.dim, cfg.eps, s))
         for l, L in enumerate(self.layers):
             MatMul.multiply_quantized(b.normed[:rows], L["wqkv"], b.qkv[:rows], rows, accumulate=False,
                                       bias=L["bqkv"])
-            _lib.check(L_.kt_rope_kv_seqs(h, p(b.qkv), rows, cfg.dim, kvh, hd, p(self.inv_freq), keys,
+            _lib.check(L_.kt_rope_kv_seqs(h, p(b.qkv), rows, self.q_width, kvh, hd, p(self.inv_freq), keys,
                                           values, self.max_seq, l, p(self.position), rows_per_seq,
                                           self.cache_stride, s))
             _lib.check(L_.kt_attention_seqs(h, p(b.qkv), keys, values, p(b.ctx), p(b.scores), rows,
-                                            cfg.dim + 2 * kv, cfg.heads, kvh, hd, self.max_seq, l, self.scale,
-                                            p(self.position), rows_per_seq, self.cache_stride, s))
-            MatMul.multiply_quantized(b.ctx[:rows], L["wo"], b.attn[:rows], rows, accumulate=False, bias=L["bo"])
+                                            self.q_width + 2 * kv, self.heads_local, kvh, hd, self.max_seq, l,
+                                            self.scale, p(self.position), rows_per_seq, self.cache_stride, s))
+            self._row_parallel(b.ctx[:rows], L["wo"], b.attn[:rows], rows, L["bo"])
             _lib.check(L_.kt_add_rmsnorm(h, p(b.x), p(b.attn), p(L["norm2"]), p(b.normed), rows, cfg.dim, cfg.eps, s))
             MatMul.multiply_quantized(b.normed[:rows], L["wgu"], b.gu[:rows], rows, accumulate=False, bias=L["bgu"])
-            _lib.check(L_.kt_silu_mul_rows(h, p(b.gu), p(b.act), rows, cfg.hidden, s))
-            MatMul.multiply_quantized(b.act[:rows], L["wd"], b.ffn[:rows], rows, accumulate=False, bias=L["bd"])
+            _lib.check(L_.kt_silu_mul_rows(h, p(b.gu), p(b.act), rows, self.hidden_local, s))
+            self._row_parallel(b.act[:rows], L["wd"], b.ffn[:rows], rows, L["bd"])
             nxt = self.layers[l + 1]["norm1"] if l + 1 < len(self.layers) else self.final_norm
             _lib.check(L_.kt_add_rmsnorm(h, p(b.x), p(b.ffn), p(nxt), p(b.normed), rows, cfg.dim, cfg.eps, s))
 
@@ -221,7 +327,11 @@ class DeviceDecoder:
         L_ = _lib.load()
         h, s, p = self.ctx.handle, self._stream(), self._p
         MatMul.multiply_quantized(normed, self.head, self.logits, self.batch, accumulate=False, bias=self.head_bias)
-        _lib.check(L_.kt_argmax(h, p(self.logits), self.batch, self.cfg.vocab, p(self.next_token), s))
+        if self.comm is None:
+            _lib.check(L_.kt_argmax(h, p(self.logits), self.batch, self.cfg.vocab, p(self.next_token), s))
+        else:  # every rank's best column, merged across ranks: the same token everywhere
+            from .parallel import argmax_column_parallel
+            argmax_column_parallel(self.comm, self.logits, self.vocab_begin, self.next_token)
         _lib.check(L_.kt_increment(h, p(self.position), advance, s))
         self.token.copy_(self.next_token)
 
@@ -263,6 +373,10 @@ class DeviceDecoder:
         per = min(self.batch, self.max_block_rows // T)
         if self._prefill_bufs is None or self._prefill_bufs.rows < per * T:
             self._prefill_bufs = self._buffers(per * T)
+        if self.comm is not None:
+            # a larger block may replace the communicator's scratch that a
+            # captured step refers to: capture again before the next replay
+            self._graph = None
         b = self._prefill_bufs
         flat = torch.tensor([t for pr in prompts for t in pr], dtype=torch.int32)
         L_ = _lib.load()
@@ -341,6 +455,8 @@ class DeviceDecoder:
         """Transformer.saveQuantized: the reference's file, byte for byte, written
         from HBM (q|k|v and gate|up are split back into their projections)."""
         from .parallel import COLUMNS, slice_weight
+        if self.comm is not None:
+            raise ValueError("save_quantized needs the whole model: save from an unsharded decoder")
         from .safetensors import SafeTensorsEntry, quantized_entries, save_entries
         cfg = self.cfg
         kv = cfg.kv_heads * cfg.head_dim

@@ -331,3 +331,88 @@ def test_fused_exchange_times_out_and_recovers_on_two_gpus(kt, tmp_path):
     for r in range(2):
         ref, y = np.load(tmp_path / f"after_{r}.npy")
         assert rel_err(y, ref) <= TOL_FP32
+
+
+TP_MODEL = dict(vocab=4096, dim=512, layers=3, heads=8, kv_heads=4, hidden=1024, rope_theta=500000.0,
+                rope_scaling=(8.0, 1.0, 4.0, 8192), bits=4, group_size=64, tied=False, qkv_bias=True)
+
+
+def _two_gpu_decoder_rank(rank, world, port, out_dir):
+    """The tensor-parallel decoder (heads, gate|up columns and vocabulary split
+    over two ranks, two all-reduces per layer) against a one-GPU decoder of the
+    same weights on this rank, step by step: batch 1 (the fused peer-memory
+    exchange) eagerly and as CUDA-graph replays, batch 3 (NCCL all-reduce)."""
+    from datetime import timedelta
+    import torch.distributed as dist
+    import kotensor_b200 as kt
+    from kotensor_b200 import decoder as D
+    from kotensor_b200 import parallel as P
+    from oracle import decoder_oracle as DO
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    comm = None
+    try:
+        ctx = kt.Context.get(rank)
+        comm = P.Comm.from_process_group(ctx=ctx)
+        weights = DO.DecoderWeights.random(DO.DecoderConfig(**TP_MODEL), seed=77)
+        cfg = D.DecoderConfig(**TP_MODEL)
+        rng = np.random.default_rng(5)
+        log = []
+        for batch in (1, 3):
+            tp = D.DeviceDecoder(cfg, weights, max_seq=48, batch=batch, comm=comm)
+            one = D.DeviceDecoder(cfg, weights, max_seq=48, batch=batch)
+            # prompts of at most 8 rows in all: every matmul on the fp32-accumulate kernels
+            prompts = [rng.integers(0, cfg.vocab, 6 if batch == 1 else 2).tolist() for _ in range(batch)]
+            tp.prefill(prompts)
+            one.prefill(prompts)
+            for step in range(12):
+                mine = tp.next_token.cpu().numpy().copy()
+                got = tp.gather_logits().cpu().numpy()
+                want = one.logits.reshape(batch, -1).cpu().numpy()
+                log.append((batch, step, got, want, mine))
+                toks = mine.tolist()
+                if step < 6:
+                    tp.step(toks)
+                else:  # the captured step: the exchanges inside a CUDA graph
+                    if tp._graph is None:
+                        tp.capture()
+                    tp.token.copy_(torch.tensor(toks, dtype=torch.int32))
+                    tp._graph.replay()
+                    tp.length += 1
+                one.step(toks)
+            torch.cuda.synchronize()
+            assert int(tp.status.item()) == 0
+            del tp, one
+        np.save(os.path.join(out_dir, f"dec_{rank}.npy"), np.array(log, dtype=object), allow_pickle=True)
+        assert ctx.take_error() == 0
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_decoder_on_two_gpus(kt, tmp_path):
+    """Logits of every step within the fp32 tolerance of the one-GPU decoder's,
+    the same bits and the same greedy tokens on both ranks, and each token the
+    one-GPU decoder's best up to a tie at the measured error."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    from oracle import decoder_oracle as DO
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_two_gpu_decoder_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    logs = [np.load(tmp_path / f"dec_{r}.npy", allow_pickle=True) for r in range(2)]
+    ties = 0
+    for e0, e1 in zip(*logs):
+        batch, step, got, want, mine = e0
+        assert np.array_equal(mine, e1[4]), (batch, step)
+        assert np.array_equal(got, e1[2]), (batch, step)
+        for q in range(batch):
+            err = float(np.abs(got[q].astype(np.float64) - want[q]).max())
+            assert err <= TOL_FP32 * float(np.abs(want[q]).max()), (batch, step, q)
+            best = DO.argmax(want[q])
+            if int(mine[q]) != best:
+                assert float(want[q][best]) - float(want[q][int(mine[q])]) <= 2 * err, (batch, step, q)
+                ties += 1
+    assert ties <= 2
