@@ -8,22 +8,25 @@
 // (0..7) is one word column of the tile row and row g + 8 the same word's high
 // nibbles, so every A register is a weight word as it lies in shared memory,
 // masked: w & 0x0F0F0F0F (low nibbles, q) or w & 0xF0F0F0F0 (high nibbles,
-// 16 q).  No byte shuffling: two AND per word per row.  B row 4 rho + sigma,
-// column n carries the activation part (n / 4: 0 = high, 1 = low byte) of row
-// rho when sigma == n % 4 and 0 otherwise, so D[g][n] is the dot product of
-// the rows with column "byte n % 4 of word g" -- 32 columns x 8 rows x 2
-// nibbles per MMA, every output lane of the MMA useful.
+// 16 q).  No byte shuffling: two AND per word per row.  Two MMAs share those A
+// registers.  In the first, B row 4 rho + sigma, column n carries activation
+// part n / 4 (0 = high, 1 = middle byte) of row rho when sigma == n % 4 and 0
+// otherwise, so D[g][n] is the dot product of the rows with column "byte n % 4
+// of word g" -- 32 columns x 8 rows x 2 nibbles, every output lane useful; in
+// the second, columns 0-3 carry the low byte the same way (columns 4-7 zero).
 //
-// Exactness.  x is scaled by a power of two 2^sh per slice (max|x 2^sh| in
-// [2^13, 2^14)), rounded to an integer X (15-bit magnitude) and split
-// X = 256 xh + xl with xh, xl signed bytes; the products are exact integers in
-// s32.  Per group (combineGroup, MatMul.kt:804-828), with SX the group's sum
-// of X over this warp's rows and D = 256 D_hi + D_lo:
+// Exactness.  x is scaled by a power of two 2^sh per warp (max|x 2^sh| in
+// [2^21, 2^22)), rounded to an integer X (22-bit magnitude, the precision of
+// an fp32 mantissa relative to the warp's largest |x|) and split
+// X = 65536 xh + 256 xm + xl into signed bytes; the products are exact
+// integers in s32.  Per group (combineGroup, MatMul.kt:804-828), with SX the
+// group's sum of X over this warp's rows and D = 65536 D_h + 256 D_m + D_l:
 //     low nibble:  y += scale * (D - zero * SX)
 //     high nibble: y += scale * (D / 16 - zero * SX)
 // and y is multiplied by 2^-sh once at the end.  The products are exact, so
-// the only rounding besides fp32 accumulation is x's 15-bit quantization
-// (relative to the slice's max|x|).
+// the only roundings are x's 22-bit quantization relative to the warp's max|x|
+// and fp32 accumulation -- fp32 class for any spread of magnitudes inside a
+// warp's rows up to 2^22 (outlier channels included).
 //
 // Tiling and streaming are those of the fp16 kernel (kt_gemv_mma.cu): a CTA
 // owns 128 packed bytes of every row (256 output columns); 4 pairs of warps
@@ -62,7 +65,7 @@ constexpr int kSlotRingBytes = kStages * kScaleSlotBytes;
 constexpr int kMainBytes = kPairs * kRingBytes;
 constexpr int kCT = 2 * kTileBytes;                                   // 256 output columns per tile
 constexpr int kRedBytes = kWarps * 8 * 32 * 4;                        // reuses the rings
-constexpr int kXsBytes = kMaxSliceRows * 2;                           // [row]{xh, xl}
+constexpr int kXsBytes = kMaxSliceRows * 4;                           // [row]{xh, xm, xl, 0}
 constexpr int kSxBytes = kMaxSliceRows / kBlockRows * 4;              // [block] sum of X
 constexpr int kXsPairBytes = kXsBytes + kSxBytes;
 constexpr size_t kSmemBytes = static_cast<size_t>(kMainBytes) + kPairs * kSlotRingBytes +
@@ -128,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     unsigned char* ring = smem + pair * kRingBytes;
     unsigned char* slots = smem + kMainBytes + pair * kSlotRingBytes;
     unsigned char* xstage = smem + kMainBytes + kPairs * kSlotRingBytes + pair * kXsPairBytes;
-    uint8_t* xs = xstage;                                                   // [row]{xh, xl}
+    uint8_t* xs = xstage;                                                   // [row]{xh, xm, xl, 0}
     int32_t* sxb = reinterpret_cast<int32_t*>(xstage + kXsBytes);           // [block] sum of X
     const uint32_t bars =
         smem_u32(smem + kMainBytes + kPairs * kSlotRingBytes + kPairs * kXsPairBytes) +
@@ -187,9 +190,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     // ---- stage x for this warp's rows, the 8-row blocks hw, hw + 2, ... of the
     // slice: float4 f of the warp is rows 8 (2 (f / 2) + hw) + 4 (f % 2) .. + 3.
-    // Each warp picks its own power of two 2^sh (max|x 2^sh| in [2^13, 2^14)),
-    // so X fits 15 bits and xh = (X + 128) >> 8 stays in [-64, 64]; the warp's
-    // results are unscaled before the warps are summed.
+    // Each warp picks its own power of two 2^sh (max|x 2^sh| in [2^21, 2^22)),
+    // so |X| < 2^22; X = 65536 xh + 256 xm + xl with xh = (X + 32896) >> 16 in
+    // [-64, 64], the remainder in [-32896, 32639] and so xm = (rem + 128) >> 8
+    // and xl = rem - 256 xm in [-128, 127]; the warp's results are unscaled
+    // before the warps are summed.
     const int n_rows = r_end - r_begin;
     const int n_f4 = n_rows / 8;  // <= 128: four per lane
     float4 xv[4];
@@ -203,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    int sh = mx > 0.0f ? 13 - ilogbf(mx) : 0;
+    int sh = mx > 0.0f ? 21 - ilogbf(mx) : 0;
     sh = max(-126, min(126, sh));
     const float sc = ldexpf(1.0f, sh);
     const float unscale = ldexpf(1.0f, -sh);
@@ -213,33 +218,35 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int row = 8 * (2 * (f >> 1) + hw) + 4 * (f & 1);
         const float v[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
         int X[4];
-        uint32_t packed_lo = 0, packed_hi = 0;  // {xh, xl} of rows row, row+1 | row+2, row+3
+        uint32_t packed[4];  // {xh, xm, xl, 0} of rows row .. row + 3
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             X[k] = __float2int_rn(v[k] * sc);
-            const int xh = (X[k] + 128) >> 8;
-            const int xl = X[k] - (xh << 8);
-            const uint32_t pr = (static_cast<uint32_t>(xh) & 0xFFu) | ((static_cast<uint32_t>(xl) & 0xFFu) << 8);
-            if (k < 2) packed_lo |= pr << (16 * k);
-            else packed_hi |= pr << (16 * (k - 2));
+            const int xh = (X[k] + 32896) >> 16;
+            const int rem = X[k] - (xh << 16);
+            const int xm = (rem + 128) >> 8;
+            const int xl = rem - (xm << 8);
+            packed[k] = (static_cast<uint32_t>(xh) & 0xFFu) | ((static_cast<uint32_t>(xm) & 0xFFu) << 8) |
+                        ((static_cast<uint32_t>(xl) & 0xFFu) << 16);
         }
         const int s4 = X[0] + X[1] + X[2] + X[3];
         const int s8 = s4 + __shfl_xor_sync(0xffffffffu, s4, 1);  // the block's 8 rows (lanes f, f ^ 1)
         if (f < n_f4) {
-            *reinterpret_cast<uint2*>(xs + 2 * row) = make_uint2(packed_lo, packed_hi);
+            *reinterpret_cast<uint4*>(xs + 4 * row) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
             if ((f & 1) == 0) sxb[row / kBlockRows] = s8;
         }
     }
     __syncwarp();  // staged x visible to the warp (each warp reads only its own rows)
 
-    // B fragments: column n = g carries part g / 4 (0 = xh, 1 = xl) in byte g % 4.
-    // From the word {xh, xl}(row 2t), {xh, xl}(row 2t+1) of a block:
-    // b0 = that part of row 2t in byte g % 4, b1 the same of row 2t+1.
+    // B fragments: in the first MMA column n = g carries part g / 4 (0 = xh,
+    // 1 = xm) in byte g % 4, in the second columns g < 4 carry xl in byte g.
+    // From the words {xh, xm, xl, 0} of rows 2t and 2t + 1 of a block: b0 = that
+    // part of row 2t in byte g % 4, b1 the same of row 2t + 1 (selector nibbles
+    // >= 4 pick the zero operand).
     const uint32_t part_byte = static_cast<uint32_t>(g >> 2);
     const uint32_t pos = static_cast<uint32_t>(g & 3);
-    uint32_t sel0 = 0x4444u, sel1 = 0x4444u;  // selector nibbles >= 4 pick the zero operand
-    sel0 = (sel0 & ~(0xFu << (4 * pos))) | (part_byte << (4 * pos));
-    sel1 = (sel1 & ~(0xFu << (4 * pos))) | ((2u + part_byte) << (4 * pos));
+    const uint32_t sel_hm = (0x4444u & ~(0xFu << (4 * pos))) | (part_byte << (4 * pos));
+    const uint32_t sel_l = g < 4 ? (0x4444u & ~(0xFu << (4 * pos))) | (2u << (4 * pos)) : 0x4444u;
     // this lane's 16-byte chunk (words 4g .. 4g+3) of rows 2t and 2t+1 of a block, swizzled
     // (16-byte chunk c of row r sits at chunk c ^ (r & 7)); blocks start on multiples of 8 rows
     const int off0 = (2 * t) * kTileBytes + ((g ^ (2 * t)) << 4);
@@ -252,10 +259,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     float y[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) y[e] = 0.0f;
-    int c[4][4];
+    int c[4][4];  // {xh, xm} parts
+    int e[4][4];  // xl part (columns 0-3)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0;
-    int sx = 0;  // this warp's sum of X over the group's rows so far
+    for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = e[j][0] = e[j][1] = e[j][2] = e[j][3] = 0;
+    long long sx = 0;  // this warp's sum of X over the group's rows so far (|X| < 2^22: 64-bit for any group size)
     bool ok = true;
     int done = 0;
     int gi = g_first;
@@ -291,22 +299,32 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int bb = 0; bb < 2; ++bb) {
             const int blk = 2 * bb + hw;                  // 8-row block of the stage
             const int brow = st * kRowsPerStage + blk * kBlockRows;  // inside the slice
-            const uint32_t xw = *reinterpret_cast<const uint32_t*>(xs + 2 * (brow + 2 * t));
-            const uint32_t b0 = prmt(xw, 0u, sel0), b1 = prmt(xw, 0u, sel1);
+            const uint2 xw = *reinterpret_cast<const uint2*>(xs + 4 * (brow + 2 * t));
+            const uint32_t b0 = prmt(xw.x, 0u, sel_hm), b1 = prmt(xw.y, 0u, sel_hm);
+            const uint32_t l0 = prmt(xw.x, 0u, sel_l), l1 = prmt(xw.y, 0u, sel_l);
             const uint4 w0 = *reinterpret_cast<const uint4*>(stage + blk * kBlockRows * kTileBytes + off0);
             const uint4 w1 = *reinterpret_cast<const uint4*>(stage + blk * kBlockRows * kTileBytes + off1);
             sx += sxb[brow / kBlockRows];
-            imma_16832(c[0], w0.x & 0x0F0F0F0Fu, w0.x & 0xF0F0F0F0u, w1.x & 0x0F0F0F0Fu, w1.x & 0xF0F0F0F0u, b0, b1);
-            imma_16832(c[1], w0.y & 0x0F0F0F0Fu, w0.y & 0xF0F0F0F0u, w1.y & 0x0F0F0F0Fu, w1.y & 0xF0F0F0F0u, b0, b1);
-            imma_16832(c[2], w0.z & 0x0F0F0F0Fu, w0.z & 0xF0F0F0F0u, w1.z & 0x0F0F0F0Fu, w1.z & 0xF0F0F0F0u, b0, b1);
-            imma_16832(c[3], w0.w & 0x0F0F0F0Fu, w0.w & 0xF0F0F0F0u, w1.w & 0x0F0F0F0Fu, w1.w & 0xF0F0F0F0u, b0, b1);
+            const uint32_t a[4][4] = {
+                {w0.x & 0x0F0F0F0Fu, w0.x & 0xF0F0F0F0u, w1.x & 0x0F0F0F0Fu, w1.x & 0xF0F0F0F0u},
+                {w0.y & 0x0F0F0F0Fu, w0.y & 0xF0F0F0F0u, w1.y & 0x0F0F0F0Fu, w1.y & 0xF0F0F0F0u},
+                {w0.z & 0x0F0F0F0Fu, w0.z & 0xF0F0F0F0u, w1.z & 0x0F0F0F0Fu, w1.z & 0xF0F0F0F0u},
+                {w0.w & 0x0F0F0F0Fu, w0.w & 0xF0F0F0F0u, w1.w & 0x0F0F0F0Fu, w1.w & 0xF0F0F0F0u}};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                imma_16832(c[j], a[j][0], a[j][1], a[j][2], a[j][3], b0, b1);
+                imma_16832(e[j], a[j][0], a[j][1], a[j][2], a[j][3], l0, l1);
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + 8 * slot);
         if (r_begin + (st + 1) * kRowsPerStage >= group_end) {
             // Group epilogue.  C of lane (g, t): c[j][0..1] = D[g][2t..2t+1] (low
-            // nibbles, byte 2u + 0/1, part t / 2), c[j][2..3] the high nibbles.
-            // Lanes t and t ^ 2 hold the two parts of the same bytes.
+            // nibbles, byte 2u + 0/1, part t / 2: xh or xm), c[j][2..3] the high
+            // nibbles; lanes t and t ^ 2 hold the two parts of the same bytes.
+            // e[j] of lanes t < 2 holds the xl part of those bytes (low nibbles in
+            // e[j][0..1], high in e[j][2..3]); lanes t >= 2 own the high nibbles
+            // and take theirs from lane t ^ 2.
             const unsigned char* sl = slots + ((gi - g_first) & (kStages - 1)) * kScaleSlotBytes;
             const float* s_arr = reinterpret_cast<const float*>(sl + (low_owner ? 0 : kTileBytes * 4));
             const uint8_t* z_arr = sl + kTileBytes * (low_owner ? 8 : 9);
@@ -317,11 +335,17 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const int send1 = low_owner ? c[j][3] : c[j][1];
                 const int recv0 = __shfl_xor_sync(0xffffffffu, send0, 2);
                 const int recv1 = __shfl_xor_sync(0xffffffffu, send1, 2);
-                // D = 256 D_hi + D_lo in fp32 (no int32 overflow for any group size)
-                const float d0 = low_owner ? fmaf(static_cast<float>(c[j][0]), 256.0f, static_cast<float>(recv0))
-                                           : fmaf(static_cast<float>(recv0), 256.0f, static_cast<float>(c[j][2]));
-                const float d1 = low_owner ? fmaf(static_cast<float>(c[j][1]), 256.0f, static_cast<float>(recv1))
-                                           : fmaf(static_cast<float>(recv1), 256.0f, static_cast<float>(c[j][3]));
+                const int lrecv0 = __shfl_xor_sync(0xffffffffu, e[j][2], 2);
+                const int lrecv1 = __shfl_xor_sync(0xffffffffu, e[j][3], 2);
+                // D = 65536 D_h + 256 D_m + D_l in fp32 (no int32 overflow for any group size)
+                const float dh0 = static_cast<float>(low_owner ? c[j][0] : recv0);
+                const float dm0 = static_cast<float>(low_owner ? recv0 : c[j][2]);
+                const float dl0 = static_cast<float>(low_owner ? e[j][0] : lrecv0);
+                const float dh1 = static_cast<float>(low_owner ? c[j][1] : recv1);
+                const float dm1 = static_cast<float>(low_owner ? recv1 : c[j][3]);
+                const float dl1 = static_cast<float>(low_owner ? e[j][1] : lrecv1);
+                const float d0 = fmaf(dh0, 65536.0f, fmaf(dm0, 256.0f, dl0));
+                const float d1 = fmaf(dh1, 65536.0f, fmaf(dm1, 256.0f, dl1));
                 const int b = 16 * g + 4 * j + 2 * u;  // byte of the tile row
                 const float2 s2 = *reinterpret_cast<const float2*>(s_arr + b);
                 const uint32_t z2 = *reinterpret_cast<const uint16_t*>(z_arr + b);
@@ -330,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 y[2 * j + 1] = fmaf(s2.y, fmaf(d1, k16, -static_cast<float>(z2 >> 8) * sxf), y[2 * j + 1]);
             }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0;
+            for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = e[j][0] = e[j][1] = e[j][2] = e[j][3] = 0;
             sx = 0;
             ++gi;
             group_end = min((gi + 1) * p.gs, r_end);

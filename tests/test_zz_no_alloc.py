@@ -39,7 +39,7 @@ def call(lib, fn, qt, x, y, m, accumulate=False, alpha=1.0):
 # with and without split-K), the generic kernel (ragged N)
 CASES = [(4, 4096, 14336, 1), (4, 14336, 4096, 1), (4, 768, 32000, 1), (4, 2048, 5632, 4), (4, 14336, 4096, 2),
          (4, 4096, 14336, 6), (4, 2048, 5632, 7), (8, 2048, 2048, 1), (8, 2048, 2048, 64), (4, 4096, 14336, 16),
-         (4, 4096, 14336, 64), (4, 2048, 5632, 128), (8, 2048, 2048, 9), (4, 512, 1000, 12)]
+         (4, 4096, 14336, 64), (4, 2048, 5632, 96), (8, 2048, 2048, 9), (4, 512, 1000, 12)]
 
 
 @pytest.mark.parametrize("bits,k,n,m", CASES)
