@@ -317,6 +317,33 @@ kt_status kt_attention_decode(kt_ctx* ctx, const float* q_dev, const float* k_ca
                               float* context_dev, float* scores_dev, int32_t rows, int32_t q_stride, int32_t heads,
                               int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t layer, float scale,
                               const int32_t* position_dev, void* stream);
+/* SwiGLU.forwardInto (SwiGLU.kt:19-25) over a fused gate | up weight W
+ * [K x 2H] (gate columns, then up columns; kt_qweight_concat_columns):
+ *   act[m x H] = silu(g) * u,  [g | u] = alpha * a[m x K] . dequant(W) + bias
+ * Where the m = 1 INT4 GEMV takes the weight, silu(g) * u is formed in its
+ * epilogue (gate column j and up column H + j are the two nibbles of byte j of
+ * the split-half packing) and gu_dev is not touched; elsewhere the product goes
+ * through gu_dev ([m x 2H], may be NULL only on the fused path) and a separate
+ * kernel.  Same results as kt_qmatmul followed by kt_silu_mul_rows. */
+kt_status kt_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float* gu_dev, float* act_dev,
+                            int32_t m, float alpha, const float* bias_dev, void* stream);
+/* One decode token per sequence, the middle of Attention.decodeInto
+ * (Attention.kt:207-239) in one launch: for fused q|k|v rows (row r = sequence
+ * r, whose caches start cache_stride floats after the previous sequence's, at
+ * position *position_dev) RoPE of the query and key heads (RoPE.kt:117-137),
+ * key and value into the cache (Attention.kt:225-232), attendHead for every
+ * query head (Attention.kt:295-328) and the merge of the position blocks --
+ * kt_rope_kv_seqs followed by kt_attention_seqs at rows_per_seq = 1, with the
+ * query rotated in registers (qkv_dev is not written).  scratch_dev: the
+ * kt_attention_scratch_floats(rows, heads, head_dim, max_seq) floats of the
+ * attention, zero-filled before the first call (its last rows x heads words
+ * are merge counters that every call leaves at zero).  heads / kv_heads <= 8,
+ * head_dim even and <= 128, else KT_ERR_UNSUPPORTED. */
+kt_status kt_attention_rope_decode(kt_ctx* ctx, const float* qkv_dev, int32_t rows, int32_t q_width, int32_t heads,
+                                   int32_t kv_heads, int32_t head_dim, const float* inv_freq_dev, float* k_cache,
+                                   float* v_cache, float* context_dev, float* scratch_dev, int32_t max_seq,
+                                   int32_t layer, float scale, const int32_t* position_dev, int64_t cache_stride,
+                                   void* stream);
 /* gate = silu(gate) * up (SwiGLU.forwardInto, Tensor.kt:231-237). */
 kt_status kt_silu_mul(kt_ctx* ctx, float* gate_dev, const float* up_dev, int64_t n, void* stream);
 /* x += y, then out = RMSNorm(x) with `weight` (the residual add of

@@ -1011,6 +1011,49 @@ kt_status kt_attention_seqs(kt_ctx* ctx, const float* q, const float* k_cache, c
     return KT_OK;
 }
 
+kt_status kt_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* a, float* gu, float* act, int32_t m,
+                            float alpha, const float* bias, void* stream) {
+    if (!ctx || !w) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
+    if (m == 0) return KT_OK;
+    if (!a || !act) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (w->columns % 2 != 0)
+        return fail(KT_ERR_INVALID_ARGUMENT, "SwiGLU needs a gate | up weight with an even number of columns");
+    const cudaStream_t s = pick(ctx, stream);
+    const QView v = view(w);
+    if (swiglu_fused_supported(v, m, a)) {
+        MatmulArgs args{a, act, bias, m, 0, alpha, ctx->d_error};
+        args.swiglu = 1;
+        const size_t need = gemv_imma_workspace_bytes(v, ctx->sm_count);
+        void* ws = nullptr;
+        if (need > 0) KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "qmatmul workspace");
+        KT_CUDA_TRY(launch_gemv_imma(v, args, ctx->sm_count, s, ws, need), "qmatmul_swiglu launch");
+        return KT_OK;
+    }
+    if (!gu) return fail(KT_ERR_INVALID_ARGUMENT, "this shape needs the gate | up scratch gu");
+    const kt_status st = run_matmul(ctx, w, a, gu, m, 0, alpha, bias, s);
+    if (st != KT_OK) return st;
+    KT_CUDA_TRY(launch_silu_mul_rows(gu, act, m, w->columns / 2, s), "silu_mul launch");
+    return KT_OK;
+}
+
+kt_status kt_attention_rope_decode(kt_ctx* ctx, const float* qkv, int32_t rows, int32_t q_width, int32_t heads,
+                                   int32_t kv_heads, int32_t head_dim, const float* inv_freq, float* k_cache,
+                                   float* v_cache, float* context, float* scratch, int32_t max_seq, int32_t layer,
+                                   float scale, const int32_t* position_dev, int64_t cache_stride, void* stream) {
+    if (!ctx || !qkv || !inv_freq || !k_cache || !v_cache || !context || !scratch || !position_dev || rows <= 0 ||
+        rows > 65535 || heads <= 0 || kv_heads <= 0 || head_dim <= 0 || q_width != heads * head_dim ||
+        max_seq <= 0 || layer < 0 || cache_stride < 0 || (rows > 1 && cache_stride == 0))
+        return fail(KT_ERR_INVALID_ARGUMENT, "bad fused attention arguments");
+    if (!attention_fused_supported(heads, kv_heads, head_dim))
+        return fail(KT_ERR_UNSUPPORTED, "fused decode attention needs heads / kv_heads <= 8 and an even head_dim <= 128");
+    KT_CUDA_TRY(launch_attention_decode_fused(qkv, rows, q_width, heads, kv_heads, head_dim, inv_freq, k_cache,
+                                              v_cache, context, scratch, max_seq, layer, scale, position_dev,
+                                              cache_stride, pick(ctx, stream)),
+                "fused attention launch");
+    return KT_OK;
+}
+
 kt_status kt_attention_decode(kt_ctx* ctx, const float* q, const float* k_cache, const float* v_cache, float* context,
                               float* scores, int32_t rows, int32_t q_stride, int32_t heads, int32_t kv_heads,
                               int32_t head_dim, int32_t max_seq, int32_t layer, float scale,

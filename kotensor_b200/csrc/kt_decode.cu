@@ -394,6 +394,177 @@ __global__ void __launch_bounds__(kThreads) attention_group_kernel(
     }
 }
 
+// One decode token per sequence (row t = sequence t, at position *pos), the
+// whole of Attention.decodeInto's middle in one launch: each block (kv head,
+// split, row) applies RoPE to its G query heads (RoPE.applyInPlace, RoPE.kt:
+// 117-137, the rope kernel's arithmetic), the block whose split holds the
+// current position also rotates this kv head's key and stores key and value in
+// the cache (KVCache layout) before reading it, every active block writes its
+// split's partials (max, sum of exponentials, weighted values), and the last
+// active block of the (kv head, row) to finish -- an acq_rel ticket -- merges
+// the splits in split order into the context (deterministic).  Every ticket is
+// back at zero when the launch ends.  Rows of one sequence that attend to each
+// other's new keys (a prefill) keep the separate rope / store and attention
+// kernels.
+template <int G, int KPER>
+__global__ void __launch_bounds__(kThreads) attention_decode_fused_kernel(
+    const float* __restrict__ qkv, int q_width, const float* __restrict__ inv_freq, float* __restrict__ kc,
+    float* __restrict__ vc, float* __restrict__ scratch, int32_t* __restrict__ tickets, float* __restrict__ ctx,
+    int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale, const int32_t* __restrict__ pos,
+    int64_t cache_stride) {
+    dev::pdl_wait();  // qkv comes from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
+    constexpr int kWarps = kThreads / 32;
+    static_assert(G <= kWarps, "one warp per query head finishes the statistics");
+    __shared__ float sc[G][kSpan];
+    __shared__ float stat[G][2];  // max, sum of exponentials
+    __shared__ float part[kWarps][G][KPER * 32];
+    __shared__ int s_last;
+    const int kvh = blockIdx.x, split = blockIdx.y, t = blockIdx.z;
+    const int p = *pos;
+    const int j0 = split * kSpan;
+    const int j1 = min(j0 + kSpan, p + 1);
+    if (j0 >= j1) return;  // past the current position
+    kc += t * cache_stride;
+    vc += t * cache_stride;
+    const int n = j1 - j0;
+    const int half = head_dim / 2;
+    const int kv_width = kv_heads * head_dim;
+    const float* row = qkv + static_cast<int64_t>(t) * (q_width + 2 * kv_width);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t base = ((static_cast<int64_t>(layer) * kv_heads + kvh) * max_seq) * head_dim;
+    // rotated element d of a head vector v at position p
+    auto rotated = [&](const float* v, int d) {
+        const int i = d < half ? d : d - half;
+        float sn, cs;
+        sincosf(static_cast<float>(p) * inv_freq[i], &sn, &cs);
+        const float x1 = v[i], x2 = v[i + half];
+        return d < half ? x1 * cs - x2 * sn : x1 * sn + x2 * cs;
+    };
+    if (j1 == p + 1) {  // this split holds the current position: its key and value into the cache
+        const float* kr = row + q_width + kvh * head_dim;
+        const float* vr = row + q_width + kv_width + kvh * head_dim;
+        const int64_t off = base + static_cast<int64_t>(p) * head_dim;
+        for (int d = threadIdx.x; d < head_dim; d += kThreads) {
+            kc[off + d] = rotated(kr, d);
+            vc[off + d] = vr[d];
+        }
+        __syncthreads();  // the block's stores are visible to its own reads below
+    }
+    float qv[G][KPER];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float* qh = row + static_cast<int64_t>(kvh * G + g) * head_dim;
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) {
+            const int d = lane + 32 * i;
+            qv[g][i] = d < head_dim ? rotated(qh, d) : 0.0f;
+        }
+    }
+    for (int j = j0 + warp; j < j1; j += kWarps) {
+        const float* kr = kc + base + static_cast<int64_t>(j) * head_dim;
+        float kv[KPER];
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) {
+            const int d = lane + 32 * i;
+            kv[i] = d < head_dim ? kr[d] : 0.0f;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float dot = 0.0f;
+#pragma unroll
+            for (int i = 0; i < KPER; ++i) dot = fmaf(qv[g][i], kv[i], dot);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            if (lane == 0) sc[g][j - j0] = dot * scale;
+        }
+    }
+    __syncthreads();
+    if (warp < G) {  // head `warp`: max and sum of exponentials over this split
+        const float s0 = lane < n ? sc[warp][lane] : -FLT_MAX;
+        const float s1 = lane + 32 < n ? sc[warp][lane + 32] : -FLT_MAX;
+        float mx = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float e0 = lane < n ? expf(s0 - mx) : 0.0f;
+        const float e1 = lane + 32 < n ? expf(s1 - mx) : 0.0f;
+        if (lane < n) sc[warp][lane] = e0;
+        if (lane + 32 < n) sc[warp][lane + 32] = e1;
+        float sum = e0 + e1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            stat[warp][0] = mx;
+            stat[warp][1] = sum;
+        }
+    }
+    __syncthreads();
+    float acc[G][KPER];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) acc[g][i] = 0.0f;
+    for (int j = j0 + warp; j < j1; j += kWarps) {
+        const float* vr = vc + base + static_cast<int64_t>(j) * head_dim;
+        float vv[KPER];
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) {
+            const int d = lane + 32 * i;
+            vv[i] = d < head_dim ? vr[d] : 0.0f;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float w = sc[g][j - j0];
+#pragma unroll
+            for (int i = 0; i < KPER; ++i) acc[g][i] = fmaf(w, vv[i], acc[g][i]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) part[warp][g][lane + 32 * i] = acc[g][i];
+    __syncthreads();
+    const int64_t splits = (max_seq + kSpan - 1) / kSpan;
+    for (int idx = threadIdx.x; idx < G * head_dim; idx += kThreads) {
+        const int g = idx / head_dim, d = idx - g * head_dim;
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) v += part[w][g][d];
+        float* out = scratch + ((static_cast<int64_t>(t) * heads + kvh * G + g) * splits + split) * (head_dim + 2);
+        out[2 + d] = v;
+        if (d == 0) {
+            out[0] = stat[g][0];
+            out[1] = stat[g][1];
+        }
+    }
+    // the last of the row's active splits to arrive merges them (the barrier
+    // orders every thread's partial stores before thread 0's acq_rel ticket)
+    const int active = p / kSpan + 1;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int32_t* ticket = tickets + static_cast<int64_t>(t) * kv_heads + kvh;
+        s_last = active == 1 || dev::atomic_add_acq_rel(ticket, 1) == active - 1;
+        if (s_last && active > 1) *ticket = 0;  // every split has arrived: ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    const int stride = head_dim + 2;
+    for (int idx = threadIdx.x; idx < G * head_dim; idx += kThreads) {
+        const int g = idx / head_dim, d = idx - g * head_dim;
+        const int h = kvh * G + g;
+        const float* hb = scratch + (static_cast<int64_t>(t) * heads + h) * splits * stride;
+        float m = -1e9f;
+        for (int s2 = 0; s2 < active; ++s2) m = fmaxf(m, __ldcg(hb + s2 * stride));
+        float l = 0.0f, v = 0.0f;
+        for (int s2 = 0; s2 < active; ++s2) {
+            const float e = expf(__ldcg(hb + s2 * stride) - m);
+            l += __ldcg(hb + s2 * stride + 1) * e;
+            v += __ldcg(hb + s2 * stride + 2 + d) * e;
+        }
+        ctx[(static_cast<int64_t>(t) * heads + h) * head_dim + d] = v * (1.0f / l);
+    }
+}
+
 __global__ void attention_merge_kernel(const float* __restrict__ scratch, float* __restrict__ ctx, int heads,
                                        int head_dim, int max_seq, const int32_t* __restrict__ pos, int rows_per_seq) {
     dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
@@ -571,8 +742,49 @@ cudaError_t launch_rope_kv(float* qkv, int rows, int q_width, int kv_heads, int 
         qkv, q_width, kv_heads, head_dim, inv_freq, kc, vc, max_seq, layer, pos, rows_per_seq, cache_stride);
     return cudaGetLastError();
 }
+// Split partials [rows][heads][splits][head_dim + 2], then one merge ticket
+// (int32) per (row, head) for the fused decode kernel.
 size_t attention_scratch_floats(int rows, int heads, int head_dim, int max_seq) {
-    return static_cast<size_t>(rows) * heads * ((max_seq + kSpan - 1) / kSpan) * (head_dim + 2);
+    return static_cast<size_t>(rows) * heads * ((max_seq + kSpan - 1) / kSpan) * (head_dim + 2) +
+           static_cast<size_t>(rows) * heads;
+}
+
+bool attention_fused_supported(int heads, int kv_heads, int head_dim) {
+    return kv_heads > 0 && heads % kv_heads == 0 && heads / kv_heads <= 8 && head_dim % 2 == 0 && head_dim <= 128;
+}
+
+cudaError_t launch_attention_decode_fused(const float* qkv, int rows, int q_width, int heads, int kv_heads,
+                                          int head_dim, const float* inv_freq, float* kc, float* vc, float* ctx,
+                                          float* scratch, int max_seq, int layer, float scale, const int32_t* pos,
+                                          int64_t cache_stride, cudaStream_t s) {
+    if (!attention_fused_supported(heads, kv_heads, head_dim)) return cudaErrorInvalidValue;
+    const int splits = (max_seq + kSpan - 1) / kSpan;
+    int32_t* tickets = reinterpret_cast<int32_t*>(
+        scratch + static_cast<size_t>(rows) * heads * splits * (head_dim + 2));
+    const dim3 grid(kv_heads, splits, rows);
+    const int group = heads / kv_heads;
+#define KT_FUSED_CASE(G_, KP_)                                                                                  \
+    launch_pdl(attention_decode_fused_kernel<G_, KP_>, grid, dim3(kThreads), 0, s, qkv, q_width, inv_freq, kc, vc, \
+               scratch, tickets, ctx, heads, kv_heads, head_dim, max_seq, layer, scale, pos, cache_stride)
+#define KT_FUSED_GROUPS(KP_)              \
+    switch (group) {                      \
+        case 1: KT_FUSED_CASE(1, KP_); break; \
+        case 2: KT_FUSED_CASE(2, KP_); break; \
+        case 3: KT_FUSED_CASE(3, KP_); break; \
+        case 4: KT_FUSED_CASE(4, KP_); break; \
+        case 5: KT_FUSED_CASE(5, KP_); break; \
+        case 6: KT_FUSED_CASE(6, KP_); break; \
+        case 7: KT_FUSED_CASE(7, KP_); break; \
+        default: KT_FUSED_CASE(8, KP_); break; \
+    }
+    if (head_dim <= 64) {
+        KT_FUSED_GROUPS(2)
+    } else {
+        KT_FUSED_GROUPS(4)
+    }
+#undef KT_FUSED_GROUPS
+#undef KT_FUSED_CASE
+    return cudaGetLastError();
 }
 cudaError_t launch_rope(float* v, int rows, int width, int head_dim, const float* inv_freq, const int32_t* pos,
                         cudaStream_t s) {

@@ -85,6 +85,7 @@ struct ImmaParams {
     float alpha;
     int32_t accumulate;
     LoraEpilogue lora;
+    int32_t swiglu;    // y[byte] = silu(gate column byte) * (up column half + byte) instead of both columns
     int32_t cluster;   // split-K inside a cluster (1) or through partials in global memory (0)
     float* partials;   // split-K: [tiles][splits][256]
     int32_t* tickets;  // [tiles], zero on entry and on exit
@@ -455,9 +456,34 @@ __global__ void __launch_bounds__(kThreads, 2)
             *out = r;
         }
     };
+    // SwiGLU epilogue (p.swiglu; no exchange, no accumulate): every thread of
+    // the CTA with its column tid; the gate column of byte b (low nibble, thread
+    // b) and its up column (high nibble, thread 128 + b) meet in shared memory
+    // (SwiGLU.forwardInto: silu(gate) * up, Tensor.kt:231-237).
+    __shared__ float s_swig[kCT];
+    auto swiglu_out = [&](int b, float g, float u) {
+        g = fmaf(p.alpha, g, 0.0f);  // the arithmetic of emit(), so both paths give the same bits
+        u = fmaf(p.alpha, u, 0.0f);
+        if (p.bias != nullptr) {
+            g += p.bias[b];
+            u += p.bias[half + b];
+        }
+        if (p.lora.p != nullptr) {
+            g += lora_term(p.lora, 0, b, p.N);
+            u += lora_term(p.lora, 0, half + b, p.N);
+        }
+        p.y[b] = g / (1.0f + expf(-g)) * u;
+    };
+    auto finish_swiglu = [&](float val) {
+        s_swig[tid] = val;
+        __syncthreads();
+        const int byte = tile_b0 + tid;
+        if (tid < kTileBytes && byte < p.R) swiglu_out(byte, s_swig[tid], s_swig[tid + kTileBytes]);
+    };
     const int S = gridDim.y;
     if (S == 1) {
-        finish(tid, v);
+        if (p.swiglu) finish_swiglu(v);
+        else finish(tid, v);
         tp_exit();
         return;
     }
@@ -470,6 +496,20 @@ __global__ void __launch_bounds__(kThreads, 2)
         __shared__ float cpart[kCT];
         cpart[tid] = v;
         cluster_sync();
+        if (p.swiglu) {  // rank r sums both columns of bytes [r * per, (r + 1) * per)
+            const int per = (kTileBytes + S - 1) / S;
+            const int b = static_cast<int>(cluster_rank()) * per + tid;
+            if (tid < per && b < kTileBytes && tile_b0 + b < p.R) {
+                float g = 0.0f, u = 0.0f;
+                for (int j = 0; j < S; ++j) {  // split order
+                    g += ld_dsmem(smem_u32(cpart + b), j);
+                    u += ld_dsmem(smem_u32(cpart + kTileBytes + b), j);
+                }
+                swiglu_out(tile_b0 + b, g, u);
+            }
+            cluster_sync();
+            return;
+        }
         const int per = (kCT + S - 1) / S;
         const int col = static_cast<int>(cluster_rank()) * per + tid;
         if (tid < per && col < kCT) {
@@ -511,7 +551,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int j = 0; j < 32; ++j)
             if (s0 + j < S) sum += tv[j];
     }
-    finish(tid, sum);
+    if (p.swiglu) finish_swiglu(sum);
+    else finish(tid, sum);
     if (tid == 0) p.tickets[blockIdx.x] = 0;  // ready for the next launch on this workspace
     tp_exit();
 }
@@ -669,6 +710,10 @@ size_t gemv_imma_workspace_bytes(const QView& w, int sm_count, bool no_cluster) 
            static_cast<size_t>(tiles_of(w.bytes_per_row)) * plan.splits * kCT * sizeof(float);
 }
 
+bool swiglu_fused_supported(const QView& w, int32_t m, const float* a) {
+    return gemv_imma_supported(w, m, a) && w.columns == 2 * w.bytes_per_row;
+}
+
 bool gemv_imma_tp_supported(const QView& w, int sm_count) {
     if (!gemv_imma_supported(w, 1, nullptr)) return false;
     const Plan plan = plan_for(w.bytes_per_row, w.rows, sm_count, true);
@@ -693,6 +738,8 @@ cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, 
     p.accumulate = a.accumulate;
     p.lora = a.lora;
     p.tp = a.tp;
+    p.swiglu = a.swiglu;
+    if (a.swiglu && (a.tp.nranks > 0 || a.accumulate || w.columns != 2 * w.bytes_per_row)) return cudaErrorInvalidValue;
     const bool no_cluster = a.tp.nranks > 0;
     const Plan plan = plan_for(p.R, p.K, sm_count, no_cluster);
     p.cluster = plan.cluster ? 1 : 0;

@@ -191,6 +191,10 @@ struct MatmulArgs {
     int32_t* err;  // context error word (bounded-wait timeouts)
     LoraEpilogue lora;
     TpExchange tp;
+    // SwiGLU epilogue (fused gate|up weight, N = 2H, split-half packed so gate
+    // column j and up column H + j are the two nibbles of byte j): c receives
+    // [m x H] silu(gate) * up instead of [m x N] (accumulate must be 0).
+    int32_t swiglu = 0;
 };
 // Largest m the fp32-accumulate streaming kernel takes.
 constexpr int kGemvMaxM = 8;
@@ -213,6 +217,8 @@ cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& args, int sm_count
 
 // ---- kt_gemv_imma.cu  (INT4, m = 1: integer tensor-core products, fp32 group combine)
 bool gemv_imma_supported(const QView& w, int32_t m, const float* a);
+// The kernels that take MatmulArgs::swiglu for this weight and m.
+bool swiglu_fused_supported(const QView& w, int32_t m, const float* a);
 void set_imma_tuning(int k_splits);
 size_t gemv_imma_workspace_bytes(const QView& w, int sm_count, bool no_cluster = false);
 // The shard can run the exchange-fused GEMV: the m = 1 kernel applies, and its
@@ -250,6 +256,15 @@ cudaError_t launch_rope_kv(float* qkv, int rows, int q_width, int kv_heads, int 
                            float* kc, float* vc, int max_seq, int layer, const int32_t* pos, int rows_per_seq,
                            int64_t cache_stride, cudaStream_t s);
 size_t attention_scratch_floats(int rows, int heads, int head_dim, int max_seq);
+// One decode token per sequence (row r = sequence r at position *pos): RoPE of
+// the query and key heads, key / value into the cache, attention and the merge
+// of its splits in one launch; scratch as attention_scratch_floats, its
+// tickets zero before the first launch (each launch leaves them zero).
+bool attention_fused_supported(int heads, int kv_heads, int head_dim);
+cudaError_t launch_attention_decode_fused(const float* qkv, int rows, int q_width, int heads, int kv_heads,
+                                          int head_dim, const float* inv_freq, float* kc, float* vc, float* ctx,
+                                          float* scratch, int max_seq, int layer, float scale, const int32_t* pos,
+                                          int64_t cache_stride, cudaStream_t s);
 cudaError_t launch_silu_mul_rows(const float* gu, float* out, int rows, int hidden, cudaStream_t s);
 cudaError_t launch_rope(float* v, int rows, int width, int head_dim, const float* inv_freq, const int32_t* pos,
                         cudaStream_t s);

@@ -211,6 +211,8 @@ class DeviceDecoder:
         self.length = 0
         self.scale = float(np.float32(1.0) / np.float32(math.sqrt(float(cfg.head_dim))))
         self._graph = None
+        g_ = self.heads_local // self.kv_local
+        self._fused_attention = g_ <= 8 and cfg.head_dim % 2 == 0 and cfg.head_dim <= 128
         if P > 1:
             self._warm_exchanges()
 
@@ -242,8 +244,9 @@ class DeviceDecoder:
         b.act = torch.empty((rows, self.hidden_local), **f32)
         b.ffn = torch.empty((rows, cfg.dim), **f32)
         b.tokens = tokens if tokens is not None else torch.empty(rows, dtype=torch.int32, device=dev)
-        b.scores = torch.empty(_lib.load().kt_attention_scratch_floats(rows, self.heads_local, cfg.head_dim,
-                                                                       self.max_seq), **f32)  # attention scratch
+        # attention scratch; zero-filled: its tail holds the fused kernel's merge counters
+        b.scores = torch.zeros(_lib.load().kt_attention_scratch_floats(rows, self.heads_local, cfg.head_dim,
+                                                                       self.max_seq), **f32)
         return b
 
     def _row_parallel(self, x, w, out, rows: int, bias) -> None:
@@ -308,16 +311,24 @@ class DeviceDecoder:
         for l, L in enumerate(self.layers):
             MatMul.multiply_quantized(b.normed[:rows], L["wqkv"], b.qkv[:rows], rows, accumulate=False,
                                       bias=L["bqkv"])
-            _lib.check(L_.kt_rope_kv_seqs(h, p(b.qkv), rows, self.q_width, kvh, hd, p(self.inv_freq), keys,
-                                          values, self.max_seq, l, p(self.position), rows_per_seq,
-                                          self.cache_stride, s))
-            _lib.check(L_.kt_attention_seqs(h, p(b.qkv), keys, values, p(b.ctx), p(b.scores), rows,
-                                            self.q_width + 2 * kv, self.heads_local, kvh, hd, self.max_seq, l,
-                                            self.scale, p(self.position), rows_per_seq, self.cache_stride, s))
+            if rows_per_seq == 1 and self._fused_attention:
+                # one token per sequence: RoPE, cache store, attention and merge in one launch
+                _lib.check(L_.kt_attention_rope_decode(h, p(b.qkv), rows, self.q_width, self.heads_local, kvh, hd,
+                                                       p(self.inv_freq), keys, values, p(b.ctx), p(b.scores),
+                                                       self.max_seq, l, self.scale, p(self.position),
+                                                       self.cache_stride, s))
+            else:
+                _lib.check(L_.kt_rope_kv_seqs(h, p(b.qkv), rows, self.q_width, kvh, hd, p(self.inv_freq), keys,
+                                              values, self.max_seq, l, p(self.position), rows_per_seq,
+                                              self.cache_stride, s))
+                _lib.check(L_.kt_attention_seqs(h, p(b.qkv), keys, values, p(b.ctx), p(b.scores), rows,
+                                                self.q_width + 2 * kv, self.heads_local, kvh, hd, self.max_seq, l,
+                                                self.scale, p(self.position), rows_per_seq, self.cache_stride, s))
             self._row_parallel(b.ctx[:rows], L["wo"], b.attn[:rows], rows, L["bo"])
             _lib.check(L_.kt_add_rmsnorm(h, p(b.x), p(b.attn), p(L["norm2"]), p(b.normed), rows, cfg.dim, cfg.eps, s))
-            MatMul.multiply_quantized(b.normed[:rows], L["wgu"], b.gu[:rows], rows, accumulate=False, bias=L["bgu"])
-            _lib.check(L_.kt_silu_mul_rows(h, p(b.gu), p(b.act), rows, self.hidden_local, s))
+            # gate|up with silu(gate) * up (in the GEMV's epilogue where it applies)
+            _lib.check(L_.kt_qmatmul_swiglu(h, L["wgu"].handle, p(b.normed), p(b.gu), p(b.act), rows, 1.0,
+                                            p(L["bgu"]), s))
             self._row_parallel(b.act[:rows], L["wd"], b.ffn[:rows], rows, L["bd"])
             nxt = self.layers[l + 1]["norm1"] if l + 1 < len(self.layers) else self.final_norm
             _lib.check(L_.kt_add_rmsnorm(h, p(b.x), p(b.ffn), p(nxt), p(b.normed), rows, cfg.dim, cfg.eps, s))

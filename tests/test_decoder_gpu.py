@@ -184,3 +184,55 @@ def test_batched_graph_replay_matches_eager_steps(kt, oracle):
     assert out_graph == out_eager
     assert torch.equal(a.logits, b.logits)
     assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("heads,kv_heads,head_dim", [(12, 12, 64), (14, 2, 64), (32, 8, 128), (4, 1, 8), (7, 7, 128)])
+@pytest.mark.parametrize("position", [0, 63, 64, 200])
+def test_fused_decode_attention_matches_the_separate_kernels(kt, heads, kv_heads, head_dim, position):
+    """kt_attention_rope_decode (RoPE, cache store, attention and merge in one
+    launch) against kt_rope_kv_seqs + kt_attention_seqs on the same rows: the
+    same cache entries and the same context within float32 rounding, on three
+    sequences with caches cache_stride apart; twice in a row (the merge
+    counters are left at zero)."""
+    import ctypes
+    from kotensor_b200 import _lib
+    from kotensor_b200 import decoder as D
+    lib = kt.load_library()
+    h = kt.Context.get().handle
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rows, layers, max_seq, layer = 3, 2, 256, 1
+    q_width, kv = heads * head_dim, kv_heads * head_dim
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(heads * 1000 + position)
+    qkv = torch.randn((rows, q_width + 2 * kv), generator=gen, device="cuda")
+    cache = torch.randn((2, rows, layers, kv_heads, max_seq, head_dim), generator=gen, device="cuda")
+    stride = layers * kv_heads * max_seq * head_dim
+    inv = torch.as_tensor(D.rope_inv_freq(head_dim, 500000.0, (8.0, 1.0, 4.0, 8192))).cuda()
+    pos = torch.tensor([position], dtype=torch.int32, device="cuda")
+    scale = float(1.0 / np.sqrt(head_dim))
+    nsc = lib.kt_attention_scratch_floats(rows, heads, head_dim, max_seq)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    # the separate kernels
+    ref_cache = cache.clone()
+    ref_qkv = qkv.clone()
+    ref_ctx = torch.empty((rows, q_width), device="cuda")
+    sc = torch.zeros(nsc, device="cuda")
+    _lib.check(lib.kt_rope_kv_seqs(h, p(ref_qkv), rows, q_width, kv_heads, head_dim, p(inv), p(ref_cache[0]),
+                                   p(ref_cache[1]), max_seq, layer, p(pos), 1, stride, s))
+    _lib.check(lib.kt_attention_seqs(h, p(ref_qkv), p(ref_cache[0]), p(ref_cache[1]), p(ref_ctx), p(sc), rows,
+                                     q_width + 2 * kv, heads, kv_heads, head_dim, max_seq, layer, scale, p(pos), 1,
+                                     stride, s))
+    fused_sc = torch.zeros(nsc, device="cuda")
+    for _ in range(2):
+        got_cache = cache.clone()
+        got_ctx = torch.full((rows, q_width), float("nan"), device="cuda")
+        _lib.check(lib.kt_attention_rope_decode(h, p(qkv), rows, q_width, heads, kv_heads, head_dim, p(inv),
+                                                p(got_cache[0]), p(got_cache[1]), p(got_ctx), p(fused_sc), max_seq,
+                                                layer, scale, p(pos), stride, s))
+        torch.cuda.synchronize()
+        assert torch.allclose(got_cache, ref_cache, rtol=1e-6, atol=1e-6)
+        err = (got_ctx - ref_ctx).abs().max().item() / ref_ctx.abs().max().item()
+        assert err <= 1e-5, err
+        ntick = rows * heads
+        assert not torch.any(fused_sc[nsc - ntick:].view(torch.int32)).item()  # counters back at zero
+    assert kt.Context.get().take_error() == 0

@@ -507,3 +507,40 @@ def test_int4_gemv_with_outlier_channels(kt, oracle, k, n, factor, count):
     ref = oracle.multiply_quantized(a, ref_t, threads=8)
     assert rel_err(y, ref) <= TOL_FP32, rel_err(y, ref)
     assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("k,h", [(896, 4864), (4096, 14336), (2048, 5632), (768, 2048), (512, 1024)])
+@pytest.mark.parametrize("m", [1, 3])
+def test_swiglu_epilogue_equals_matmul_then_silu(kt, oracle, k, h, m):
+    """kt_qmatmul_swiglu on a fused gate | up weight [K x 2H]: at m = 1 the
+    silu(gate) * up product is formed in the INT4 GEMV's epilogue (every
+    split-K route: one CTA per tile, clusters, partials in global memory) and
+    must equal kt_qmatmul followed by kt_silu_mul_rows bit for bit; other m take
+    that route themselves.  Both within the fp32 tolerance of the oracle."""
+    import ctypes
+    from kotensor_b200 import _lib
+    lib = kt.load_library()
+    rng = np.random.default_rng(k + h + m)
+    w = (rng.standard_normal((k, 2 * h), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 4, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, 2 * h), 4, 64)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    bias = (rng.standard_normal(2 * h, dtype=np.float32) * 0.1).astype(np.float32)
+    ad, bd = dev(a), dev(bias)
+    h_ = kt.Context.get().handle
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    gu = torch.empty((m, 2 * h), device="cuda")
+    want = torch.empty((m, h), device="cuda")
+    _lib.check(lib.kt_qmatmul(h_, qt.handle, p(ad), p(gu), m, 0, 1.0, p(bd), s))
+    _lib.check(lib.kt_silu_mul_rows(h_, p(gu), p(want), m, h, s))
+    for _ in range(2):
+        got = torch.full((m, h), float("nan"), device="cuda")
+        _lib.check(lib.kt_qmatmul_swiglu(h_, qt.handle, p(ad), p(gu), p(got), m, 1.0, p(bd), s))
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+    g_u = oracle.multiply_quantized(a, ref_t, threads=8) + bias[None, :]
+    g, u = g_u[:, :h].astype(np.float64), g_u[:, h:].astype(np.float64)
+    ref = g / (1.0 + np.exp(-g)) * u
+    assert rel_err(got.cpu().numpy(), ref) <= TOL_FP32
+    assert kt.Context.get().take_error() == 0
