@@ -327,6 +327,24 @@ kt_status kt_attention_decode(kt_ctx* ctx, const float* q_dev, const float* k_ca
  * kernel.  Same results as kt_qmatmul followed by kt_silu_mul_rows. */
 kt_status kt_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* a_dev, float* gu_dev, float* act_dev,
                             int32_t m, float alpha, const float* bias_dev, void* stream);
+/* RMSNorm.forwardInto (RMSNorm.kt:71-90) followed by a projection, the start
+ * of both halves of TransformerBlock.decodeInto (TransformerBlock.kt:40-47):
+ *   c[m x N] = (accumulate ? c : 0) + RMSNorm(x)[m x K] . dequant(W) + bias
+ * with RMSNorm(x) = x * (1 / sqrt(mean(x^2) + eps)) * norm_weight per row.
+ * Where the m = 1 INT4 GEMV takes the weight (and norm_weight_dev is 16-byte
+ * aligned) the norm is applied while the GEMV stages x -- every CTA sums the
+ * row's squares itself -- and xn_dev is not touched; elsewhere kt_rmsnorm
+ * writes xn_dev ([m x K], may be NULL only on the fused path), then
+ * kt_qmatmul.  Within the fp32 tolerance of the two calls. */
+kt_status kt_rmsnorm_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* x_dev, const float* norm_weight_dev,
+                             float eps, float* xn_dev, float* c_dev, int32_t m, int32_t accumulate,
+                             const float* bias_dev, void* stream);
+/* The same followed by SwiGLU over a gate | up weight (kt_qmatmul_swiglu):
+ * act[m x H] = silu(g) * u, [g | u] = RMSNorm(x) . dequant(W) + bias; both the
+ * norm and silu(g) * u fused into the m = 1 INT4 GEMV where it applies. */
+kt_status kt_rmsnorm_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* x_dev,
+                                    const float* norm_weight_dev, float eps, float* xn_dev, float* gu_dev,
+                                    float* act_dev, int32_t m, const float* bias_dev, void* stream);
 /* One decode token per sequence, the middle of Attention.decodeInto
  * (Attention.kt:207-239) in one launch: for fused q|k|v rows (row r = sequence
  * r, whose caches start cache_stride floats after the previous sequence's, at
@@ -338,7 +356,7 @@ kt_status kt_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* a_dev
  * kt_attention_scratch_floats(rows, heads, head_dim, max_seq) floats of the
  * attention, zero-filled before the first call (its last rows x heads words
  * are merge counters that every call leaves at zero).  heads / kv_heads <= 8,
- * head_dim even and <= 128, else KT_ERR_UNSUPPORTED. */
+ * head_dim even and <= 128, max_seq <= 16384, else KT_ERR_UNSUPPORTED. */
 kt_status kt_attention_rope_decode(kt_ctx* ctx, const float* qkv_dev, int32_t rows, int32_t q_width, int32_t heads,
                                    int32_t kv_heads, int32_t head_dim, const float* inv_freq_dev, float* k_cache,
                                    float* v_cache, float* context_dev, float* scratch_dev, int32_t max_seq,

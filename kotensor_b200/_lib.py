@@ -110,6 +110,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_attention_seqs": ([P, P, P, P, P, P, I32, I32, I32, I32, I32, I32, I32, F32, P, I32, I64, P], I32),
     "kt_rope_kv_seqs": ([P, P, I32, I32, I32, I32, P, P, P, I32, I32, P, I32, I64, P], I32),
     "kt_qmatmul_swiglu": ([P, P, P, P, P, I32, F32, P, P], I32),
+    "kt_rmsnorm_qmatmul": ([P, P, P, P, F32, P, P, I32, I32, P, P], I32),
+    "kt_rmsnorm_qmatmul_swiglu": ([P, P, P, P, F32, P, P, P, I32, P, P], I32),
     "kt_attention_rope_decode": ([P, P, I32, I32, I32, I32, I32, P, P, P, P, P, I32, I32, F32, P, I64, P], I32),
     "kt_silu_mul": ([P, P, P, I64, P], I32),
     "kt_add": ([P, P, P, I64, P], I32),

@@ -1037,6 +1037,50 @@ kt_status kt_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* a, fl
     return KT_OK;
 }
 
+namespace {
+// RMSNorm + matmul (+ SwiGLU): the m = 1 INT4 GEMV normalises its input row
+// while staging it; elsewhere kt_rmsnorm into xn, then the matmul.
+kt_status rmsnorm_matmul(kt_ctx* ctx, const kt_qweight* w, const float* x, const float* norm_w, float eps,
+                         float* xn, float* gu, float* c, int32_t m, int32_t accumulate, const float* bias,
+                         bool swiglu, void* stream) {
+    if (!ctx || !w) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
+    if (m == 0) return KT_OK;
+    if (!x || !norm_w || !c) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (swiglu && w->columns % 2 != 0)
+        return fail(KT_ERR_INVALID_ARGUMENT, "SwiGLU needs a gate | up weight with an even number of columns");
+    const cudaStream_t s = pick(ctx, stream);
+    const QView v = view(w);
+    const bool fused = norm_fused_supported(v, m, x) && reinterpret_cast<uintptr_t>(norm_w) % 16 == 0 &&
+                       (!swiglu || swiglu_fused_supported(v, m, x));
+    if (fused) {
+        MatmulArgs args{x, c, bias, m, accumulate, 1.0f, ctx->d_error};
+        args.norm_weight = norm_w;
+        args.norm_eps = eps;
+        args.swiglu = swiglu ? 1 : 0;
+        const size_t need = gemv_imma_workspace_bytes(v, ctx->sm_count);
+        void* ws = nullptr;
+        if (need > 0) KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "qmatmul workspace");
+        KT_CUDA_TRY(launch_gemv_imma(v, args, ctx->sm_count, s, ws, need), "rmsnorm_qmatmul launch");
+        return KT_OK;
+    }
+    if (!xn || (swiglu && !gu)) return fail(KT_ERR_INVALID_ARGUMENT, "this shape needs the scratch rows xn / gu");
+    KT_CUDA_TRY(launch_rmsnorm(x, norm_w, xn, m, w->rows, eps, s), "rmsnorm launch");
+    if (!swiglu) return run_matmul(ctx, w, xn, c, m, accumulate, 1.0f, bias, s);
+    return kt_qmatmul_swiglu(ctx, w, xn, gu, c, m, 1.0f, bias, stream);
+}
+}  // namespace
+
+kt_status kt_rmsnorm_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* x, const float* norm_w, float eps,
+                             float* xn, float* c, int32_t m, int32_t accumulate, const float* bias, void* stream) {
+    return rmsnorm_matmul(ctx, w, x, norm_w, eps, xn, nullptr, c, m, accumulate, bias, false, stream);
+}
+
+kt_status kt_rmsnorm_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* x, const float* norm_w, float eps,
+                                    float* xn, float* gu, float* act, int32_t m, const float* bias, void* stream) {
+    return rmsnorm_matmul(ctx, w, x, norm_w, eps, xn, gu, act, m, 0, bias, true, stream);
+}
+
 kt_status kt_attention_rope_decode(kt_ctx* ctx, const float* qkv, int32_t rows, int32_t q_width, int32_t heads,
                                    int32_t kv_heads, int32_t head_dim, const float* inv_freq, float* k_cache,
                                    float* v_cache, float* context, float* scratch, int32_t max_seq, int32_t layer,
@@ -1045,8 +1089,9 @@ kt_status kt_attention_rope_decode(kt_ctx* ctx, const float* qkv, int32_t rows, 
         rows > 65535 || heads <= 0 || kv_heads <= 0 || head_dim <= 0 || q_width != heads * head_dim ||
         max_seq <= 0 || layer < 0 || cache_stride < 0 || (rows > 1 && cache_stride == 0))
         return fail(KT_ERR_INVALID_ARGUMENT, "bad fused attention arguments");
-    if (!attention_fused_supported(heads, kv_heads, head_dim))
-        return fail(KT_ERR_UNSUPPORTED, "fused decode attention needs heads / kv_heads <= 8 and an even head_dim <= 128");
+    if (!attention_fused_supported(heads, kv_heads, head_dim, max_seq))
+        return fail(KT_ERR_UNSUPPORTED,
+                    "fused decode attention needs heads / kv_heads <= 8, an even head_dim <= 128 and max_seq <= 16384");
     KT_CUDA_TRY(launch_attention_decode_fused(qkv, rows, q_width, heads, kv_heads, head_dim, inv_freq, k_cache,
                                               v_cache, context, scratch, max_seq, layer, scale, position_dev,
                                               cache_stride, pick(ctx, stream)),

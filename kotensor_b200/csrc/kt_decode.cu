@@ -197,6 +197,7 @@ __global__ void kv_store_kernel(const float* __restrict__ k, const float* __rest
 // reference's initial maximum), ctx = sum acc_s e^(m_s - M) / sum l_s e^(m_s - M).
 constexpr int kMaxHeadDim = 254;
 constexpr int kSpan = 64;  // positions per block
+constexpr int kMaxFusedSplits = 256;  // position blocks the fused decode kernel merges (max_seq <= 16384)
 
 __global__ void __launch_bounds__(kThreads) attention_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
@@ -433,50 +434,88 @@ __global__ void __launch_bounds__(kThreads) attention_decode_fused_kernel(
     const float* row = qkv + static_cast<int64_t>(t) * (q_width + 2 * kv_width);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t base = ((static_cast<int64_t>(layer) * kv_heads + kvh) * max_seq) * head_dim;
-    // rotated element d of a head vector v at position p
-    auto rotated = [&](const float* v, int d) {
-        const int i = d < half ? d : d - half;
-        float sn, cs;
-        sincosf(static_cast<float>(p) * inv_freq[i], &sn, &cs);
-        const float x1 = v[i], x2 = v[i + half];
-        return d < half ? x1 * cs - x2 * sn : x1 * sn + x2 * cs;
-    };
+    // RoPE factors of this lane's dims d = lane + 32 i (they depend on the dim only)
+    float cs[KPER], sn[KPER];
+#pragma unroll
+    for (int i = 0; i < KPER; ++i) {
+        const int d = lane + 32 * i;
+        const int fi = d < half ? d : d - half;
+        cs[i] = 1.0f;
+        sn[i] = 0.0f;
+        if (d < head_dim) sincosf(static_cast<float>(p) * __ldg(inv_freq + fi), &sn[i], &cs[i]);
+    }
     if (j1 == p + 1) {  // this split holds the current position: its key and value into the cache
         const float* kr = row + q_width + kvh * head_dim;
         const float* vr = row + q_width + kv_width + kvh * head_dim;
         const int64_t off = base + static_cast<int64_t>(p) * head_dim;
         for (int d = threadIdx.x; d < head_dim; d += kThreads) {
-            kc[off + d] = rotated(kr, d);
+            const int i = d < half ? d : d - half;
+            float s1, c1;
+            sincosf(static_cast<float>(p) * __ldg(inv_freq + i), &s1, &c1);
+            const float x1 = kr[i], x2 = kr[i + half];
+            kc[off + d] = d < half ? x1 * c1 - x2 * s1 : x1 * s1 + x2 * c1;
             vc[off + d] = vr[d];
         }
         __syncthreads();  // the block's stores are visible to its own reads below
     }
-    float qv[G][KPER];
+    // the G query vectors: every load issued first (no load waits on another),
+    // then the rotation pairs (d, d + half) -- in this lane's registers when
+    // half is a multiple of 32, else loaded beside them
+    float qv[G][KPER], qp[G][KPER];
+    const bool in_lane = (half & 31) == 0;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         const float* qh = row + static_cast<int64_t>(kvh * G + g) * head_dim;
 #pragma unroll
         for (int i = 0; i < KPER; ++i) {
             const int d = lane + 32 * i;
-            qv[g][i] = d < head_dim ? rotated(qh, d) : 0.0f;
+            qv[g][i] = d < head_dim ? qh[d] : 0.0f;
+            qp[g][i] = !in_lane && d < head_dim ? qh[d < half ? d + half : d - half] : 0.0f;
         }
     }
-    for (int j = j0 + warp; j < j1; j += kWarps) {
-        const float* kr = kc + base + static_cast<int64_t>(j) * head_dim;
-        float kv[KPER];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float rq[KPER];
 #pragma unroll
         for (int i = 0; i < KPER; ++i) {
             const int d = lane + 32 * i;
-            kv[i] = d < head_dim ? kr[d] : 0.0f;
+            const int sh = half >> 5;  // partner element index offset when in_lane
+            const float partner = in_lane ? qv[g][d < half ? min(i + sh, KPER - 1) : max(i - sh, 0)] : qp[g][i];
+            const float x1 = d < half ? qv[g][i] : partner, x2 = d < half ? partner : qv[g][i];
+            rq[i] = d < head_dim ? (d < half ? x1 * cs[i] - x2 * sn[i] : x1 * sn[i] + x2 * cs[i]) : 0.0f;
         }
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) qv[g][i] = rq[i];
+    }
+    // a warp's positions j0 + warp + 8 jj: their key and value rows are loaded
+    // together (one memory round trip), the value rows kept in registers until
+    // the softmax weights are known
+    constexpr int kPer = kSpan / kWarps;  // positions per warp
+    float kr_[kPer][KPER], vr_[kPer][KPER];
+#pragma unroll
+    for (int jj = 0; jj < kPer; ++jj) {
+        const int j = j0 + warp + kWarps * jj;
+        const float* kr = kc + base + static_cast<int64_t>(j) * head_dim;
+        const float* vr = vc + base + static_cast<int64_t>(j) * head_dim;
+#pragma unroll
+        for (int i = 0; i < KPER; ++i) {
+            const int d = lane + 32 * i;
+            const bool ok = j < j1 && d < head_dim;
+            kr_[jj][i] = ok ? kr[d] : 0.0f;
+            vr_[jj][i] = ok ? vr[d] : 0.0f;
+        }
+    }
+#pragma unroll
+    for (int jj = 0; jj < kPer; ++jj) {
+        const int j = j0 + warp + kWarps * jj;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             float dot = 0.0f;
 #pragma unroll
-            for (int i = 0; i < KPER; ++i) dot = fmaf(qv[g][i], kv[i], dot);
+            for (int i = 0; i < KPER; ++i) dot = fmaf(qv[g][i], kr_[jj][i], dot);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-            if (lane == 0) sc[g][j - j0] = dot * scale;
+            if (lane == 0 && j < j1) sc[g][j - j0] = dot * scale;
         }
     }
     __syncthreads();
@@ -504,19 +543,16 @@ __global__ void __launch_bounds__(kThreads) attention_decode_fused_kernel(
     for (int g = 0; g < G; ++g)
 #pragma unroll
         for (int i = 0; i < KPER; ++i) acc[g][i] = 0.0f;
-    for (int j = j0 + warp; j < j1; j += kWarps) {
-        const float* vr = vc + base + static_cast<int64_t>(j) * head_dim;
-        float vv[KPER];
 #pragma unroll
-        for (int i = 0; i < KPER; ++i) {
-            const int d = lane + 32 * i;
-            vv[i] = d < head_dim ? vr[d] : 0.0f;
-        }
+    for (int jj = 0; jj < kPer; ++jj) {
+        const int j = j0 + warp + kWarps * jj;
+        if (j < j1) {
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float w = sc[g][j - j0];
+            for (int g = 0; g < G; ++g) {
+                const float w = sc[g][j - j0];
 #pragma unroll
-            for (int i = 0; i < KPER; ++i) acc[g][i] = fmaf(w, vv[i], acc[g][i]);
+                for (int i = 0; i < KPER; ++i) acc[g][i] = fmaf(w, vr_[jj][i], acc[g][i]);
+            }
         }
     }
 #pragma unroll
@@ -548,20 +584,61 @@ __global__ void __launch_bounds__(kThreads) attention_decode_fused_kernel(
     }
     __syncthreads();
     if (!s_last) return;
+    // merge: warp g loads head g's split statistics (32 splits per lane
+    // round), takes the maximum and the sum of exponentials (fixed reduction
+    // order) and keeps each split's factor in shared memory; then each thread
+    // sums the splits' values for its outputs with every load of a chunk of 8
+    // splits in flight at once
     const int stride = head_dim + 2;
-    for (int idx = threadIdx.x; idx < G * head_dim; idx += kThreads) {
-        const int g = idx / head_dim, d = idx - g * head_dim;
-        const int h = kvh * G + g;
-        const float* hb = scratch + (static_cast<int64_t>(t) * heads + h) * splits * stride;
+    __shared__ float coef[G][kMaxFusedSplits];
+    __shared__ float inv_l[G];
+    if (warp < G) {
+        const float* hb = scratch + (static_cast<int64_t>(t) * heads + kvh * G + warp) * splits * stride;
         float m = -1e9f;
-        for (int s2 = 0; s2 < active; ++s2) m = fmaxf(m, __ldcg(hb + s2 * stride));
-        float l = 0.0f, v = 0.0f;
-        for (int s2 = 0; s2 < active; ++s2) {
+        for (int s2 = lane; s2 < active; s2 += 32) m = fmaxf(m, __ldcg(hb + s2 * stride));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int s2 = lane; s2 < active; s2 += 32) {
             const float e = expf(__ldcg(hb + s2 * stride) - m);
-            l += __ldcg(hb + s2 * stride + 1) * e;
-            v += __ldcg(hb + s2 * stride + 2 + d) * e;
+            coef[warp][s2] = e;
+            l = fmaf(__ldcg(hb + s2 * stride + 1), e, l);
         }
-        ctx[(static_cast<int64_t>(t) * heads + h) * head_dim + d] = v * (1.0f / l);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) inv_l[warp] = 1.0f / l;
+    }
+    __syncthreads();
+    constexpr int kOuts = (G * KPER * 32 + kThreads - 1) / kThreads;  // outputs per thread
+    float vsum[kOuts];
+#pragma unroll
+    for (int o2 = 0; o2 < kOuts; ++o2) vsum[o2] = 0.0f;
+    for (int s0 = 0; s0 < active; s0 += 8) {
+        float u[kOuts][8];
+#pragma unroll
+        for (int o2 = 0; o2 < kOuts; ++o2) {
+            const int idx = threadIdx.x + kThreads * o2;
+            const int g = idx / head_dim, d = idx - g * head_dim;
+            const float* hv =
+                scratch + (static_cast<int64_t>(t) * heads + kvh * G + g) * splits * stride + 2 + d;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) u[o2][j] = idx < G * head_dim && s0 + j < active ? __ldcg(hv + (s0 + j) * stride) : 0.0f;
+        }
+#pragma unroll
+        for (int o2 = 0; o2 < kOuts; ++o2) {
+            const int g = min((threadIdx.x + kThreads * o2) / head_dim, G - 1);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (s0 + j < active) vsum[o2] = fmaf(u[o2][j], coef[g][s0 + j], vsum[o2]);
+        }
+    }
+#pragma unroll
+    for (int o2 = 0; o2 < kOuts; ++o2) {
+        const int idx = threadIdx.x + kThreads * o2;
+        if (idx < G * head_dim) {
+            const int g = idx / head_dim, d = idx - g * head_dim;
+            ctx[(static_cast<int64_t>(t) * heads + kvh * G + g) * head_dim + d] = vsum[o2] * inv_l[g];
+        }
     }
 }
 
@@ -749,15 +826,16 @@ size_t attention_scratch_floats(int rows, int heads, int head_dim, int max_seq) 
            static_cast<size_t>(rows) * heads;
 }
 
-bool attention_fused_supported(int heads, int kv_heads, int head_dim) {
-    return kv_heads > 0 && heads % kv_heads == 0 && heads / kv_heads <= 8 && head_dim % 2 == 0 && head_dim <= 128;
+bool attention_fused_supported(int heads, int kv_heads, int head_dim, int max_seq) {
+    return kv_heads > 0 && heads % kv_heads == 0 && heads / kv_heads <= 8 && head_dim % 2 == 0 && head_dim <= 128 &&
+           (max_seq + kSpan - 1) / kSpan <= kMaxFusedSplits;
 }
 
 cudaError_t launch_attention_decode_fused(const float* qkv, int rows, int q_width, int heads, int kv_heads,
                                           int head_dim, const float* inv_freq, float* kc, float* vc, float* ctx,
                                           float* scratch, int max_seq, int layer, float scale, const int32_t* pos,
                                           int64_t cache_stride, cudaStream_t s) {
-    if (!attention_fused_supported(heads, kv_heads, head_dim)) return cudaErrorInvalidValue;
+    if (!attention_fused_supported(heads, kv_heads, head_dim, max_seq)) return cudaErrorInvalidValue;
     const int splits = (max_seq + kSpan - 1) / kSpan;
     int32_t* tickets = reinterpret_cast<int32_t*>(
         scratch + static_cast<size_t>(rows) * heads * splits * (head_dim + 2));

@@ -86,6 +86,8 @@ struct ImmaParams {
     int32_t accumulate;
     LoraEpilogue lora;
     int32_t swiglu;    // y[byte] = silu(gate column byte) * (up column half + byte) instead of both columns
+    const float* norm_w;  // RMSNorm of x before the product (NULL: off)
+    float norm_eps;
     int32_t cluster;   // split-K inside a cluster (1) or through partials in global memory (0)
     float* partials;   // split-K: [tiles][splits][256]
     int32_t* tickets;  // [tiles], zero on entry and on exit
@@ -196,6 +198,30 @@ __global__ void __launch_bounds__(kThreads, 2)
     // [-64, 64], the remainder in [-32896, 32639] and so xm = (rem + 128) >> 8
     // and xl = rem - 256 xm in [-128, 127]; the warp's results are unscaled
     // before the warps are summed.
+    // RMSNorm prologue (p.norm_w): every CTA sums the squares of the whole row
+    // of x (the same order in every CTA, so every CTA gets the same scale) and
+    // stages x * scale * w for its rows (RMSNorm.kt:71-90).
+    float nrm = 1.0f;
+    if (p.norm_w != nullptr) {
+        __shared__ float s_nred[kWarps];
+        float ss = 0.0f;
+#pragma unroll 4
+        for (int i = 4 * tid; i < p.K; i += 4 * kThreads) {
+            const float4 v4 = __ldg(reinterpret_cast<const float4*>(p.x + i));
+            ss = fmaf(v4.x, v4.x, ss);
+            ss = fmaf(v4.y, v4.y, ss);
+            ss = fmaf(v4.z, v4.z, ss);
+            ss = fmaf(v4.w, v4.w, ss);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) s_nred[warp] = ss;
+        __syncthreads();
+        float tot = 0.0f;
+#pragma unroll
+        for (int w2 = 0; w2 < kWarps; ++w2) tot += s_nred[w2];
+        nrm = 1.0f / sqrtf(tot / static_cast<float>(p.K) + p.norm_eps);
+    }
     const int n_rows = r_end - r_begin;
     const int n_f4 = n_rows / 8;  // <= 128: four per lane
     float4 xv[4];
@@ -205,6 +231,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int f = lane + 32 * i;
         const int row = 8 * (2 * (f >> 1) + hw) + 4 * (f & 1);
         xv[i] = f < n_f4 ? __ldg(reinterpret_cast<const float4*>(p.x + r_begin + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p.norm_w != nullptr && f < n_f4) {
+            const float4 w4 = __ldg(reinterpret_cast<const float4*>(p.norm_w + r_begin + row));
+            xv[i] = make_float4(xv[i].x * nrm * w4.x, xv[i].y * nrm * w4.y, xv[i].z * nrm * w4.z, xv[i].w * nrm * w4.w);
+        }
         mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xv[i].x), fabsf(xv[i].y)), fmaxf(fabsf(xv[i].z), fabsf(xv[i].w))));
     }
 #pragma unroll
@@ -710,6 +740,8 @@ size_t gemv_imma_workspace_bytes(const QView& w, int sm_count, bool no_cluster) 
            static_cast<size_t>(tiles_of(w.bytes_per_row)) * plan.splits * kCT * sizeof(float);
 }
 
+bool norm_fused_supported(const QView& w, int32_t m, const float* a) { return gemv_imma_supported(w, m, a); }
+
 bool swiglu_fused_supported(const QView& w, int32_t m, const float* a) {
     return gemv_imma_supported(w, m, a) && w.columns == 2 * w.bytes_per_row;
 }
@@ -739,6 +771,9 @@ cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, 
     p.lora = a.lora;
     p.tp = a.tp;
     p.swiglu = a.swiglu;
+    p.norm_w = a.norm_weight;
+    p.norm_eps = a.norm_eps;
+    if (a.norm_weight != nullptr && reinterpret_cast<uintptr_t>(a.norm_weight) % 16 != 0) return cudaErrorInvalidValue;
     if (a.swiglu && (a.tp.nranks > 0 || a.accumulate || w.columns != 2 * w.bytes_per_row)) return cudaErrorInvalidValue;
     const bool no_cluster = a.tp.nranks > 0;
     const Plan plan = plan_for(p.R, p.K, sm_count, no_cluster);

@@ -195,6 +195,11 @@ struct MatmulArgs {
     // column j and up column H + j are the two nibbles of byte j): c receives
     // [m x H] silu(gate) * up instead of [m x N] (accumulate must be 0).
     int32_t swiglu = 0;
+    // RMSNorm of the input row before the product (RMSNorm.forwardInto,
+    // RMSNorm.kt:71-90): a is read as a * (1 / sqrt(mean(a^2) + eps)) * norm_weight
+    // (norm_weight NULL: off; m = 1 INT4 GEMV only).
+    const float* norm_weight = nullptr;
+    float norm_eps = 0.0f;
 };
 // Largest m the fp32-accumulate streaming kernel takes.
 constexpr int kGemvMaxM = 8;
@@ -219,6 +224,8 @@ cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& args, int sm_count
 bool gemv_imma_supported(const QView& w, int32_t m, const float* a);
 // The kernels that take MatmulArgs::swiglu for this weight and m.
 bool swiglu_fused_supported(const QView& w, int32_t m, const float* a);
+// The kernels that take MatmulArgs::norm_weight for this weight and m.
+bool norm_fused_supported(const QView& w, int32_t m, const float* a);
 void set_imma_tuning(int k_splits);
 size_t gemv_imma_workspace_bytes(const QView& w, int sm_count, bool no_cluster = false);
 // The shard can run the exchange-fused GEMV: the m = 1 kernel applies, and its
@@ -260,7 +267,7 @@ size_t attention_scratch_floats(int rows, int heads, int head_dim, int max_seq);
 // the query and key heads, key / value into the cache, attention and the merge
 // of its splits in one launch; scratch as attention_scratch_floats, its
 // tickets zero before the first launch (each launch leaves them zero).
-bool attention_fused_supported(int heads, int kv_heads, int head_dim);
+bool attention_fused_supported(int heads, int kv_heads, int head_dim, int max_seq);
 cudaError_t launch_attention_decode_fused(const float* qkv, int rows, int q_width, int heads, int kv_heads,
                                           int head_dim, const float* inv_freq, float* kc, float* vc, float* ctx,
                                           float* scratch, int max_seq, int layer, float scale, const int32_t* pos,

@@ -205,6 +205,7 @@ class DeviceDecoder:
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.logits = torch.empty((batch, self.vocab_local), **f32)  # this rank's vocabulary columns
         self._head_in = torch.empty((batch, cfg.dim), **f32)
+        self._head_xn = torch.empty((batch, cfg.dim), **f32)
         self._last_rows = torch.empty(batch, dtype=torch.int32, device=dev)
         self._step_bufs = self._buffers(batch, tokens=self.token)
         self._prefill_bufs = None  # prefill buffers, allocated on first use
@@ -212,7 +213,7 @@ class DeviceDecoder:
         self.scale = float(np.float32(1.0) / np.float32(math.sqrt(float(cfg.head_dim))))
         self._graph = None
         g_ = self.heads_local // self.kv_local
-        self._fused_attention = g_ <= 8 and cfg.head_dim % 2 == 0 and cfg.head_dim <= 128
+        self._fused_attention = g_ <= 8 and cfg.head_dim % 2 == 0 and cfg.head_dim <= 128 and max_seq <= 16384
         if P > 1:
             self._warm_exchanges()
 
@@ -239,24 +240,23 @@ class DeviceDecoder:
         b.normed = torch.empty((rows, cfg.dim), **f32)
         b.qkv = torch.empty((rows, self.q_width + 2 * self.kv_width), **f32)
         b.ctx = torch.empty((rows, self.q_width), **f32)
-        b.attn = torch.empty((rows, cfg.dim), **f32)
         b.gu = torch.empty((rows, 2 * self.hidden_local), **f32)
         b.act = torch.empty((rows, self.hidden_local), **f32)
-        b.ffn = torch.empty((rows, cfg.dim), **f32)
         b.tokens = tokens if tokens is not None else torch.empty(rows, dtype=torch.int32, device=dev)
         # attention scratch; zero-filled: its tail holds the fused kernel's merge counters
         b.scores = torch.zeros(_lib.load().kt_attention_scratch_floats(rows, self.heads_local, cfg.head_dim,
                                                                        self.max_seq), **f32)
         return b
 
-    def _row_parallel(self, x, w, out, rows: int, bias) -> None:
-        """out[rows x dim] = x . W + bias: the local product, or under tensor
+    def _row_parallel(self, x, w, out, rows: int, bias, accumulate: bool = True) -> None:
+        """out[rows x dim] (+)= x . W + bias (the residual add of
+        TransformerBlock.decodeInto): the local product, or under tensor
         parallelism this rank's rows of W and the all-reduce of the partials."""
         if self.comm is None:
-            MatMul.multiply_quantized(x, w, out, rows, accumulate=False, bias=bias)
+            MatMul.multiply_quantized(x, w, out, rows, accumulate=accumulate, bias=bias)
         else:
             from .parallel import matmul_row_parallel
-            matmul_row_parallel(self.comm, x, w, out, rows, accumulate=False, bias=bias)
+            matmul_row_parallel(self.comm, x, w, out, rows, accumulate=accumulate, bias=bias)
 
     def _warm_exchanges(self) -> None:
         """Collective (every rank, at construction): each row-parallel shard
@@ -271,8 +271,8 @@ class DeviceDecoder:
         x_d = torch.zeros((m, self.hidden_local), dtype=torch.float32, device=dev)
         out = torch.empty((m, self.cfg.dim), dtype=torch.float32, device=dev)
         for L in self.layers:
-            self._row_parallel(x_o, L["wo"], out, m, None)
-            self._row_parallel(x_d, L["wd"], out, m, None)
+            self._row_parallel(x_o, L["wo"], out, m, None, accumulate=False)
+            self._row_parallel(x_d, L["wd"], out, m, None, accumulate=False)
         from .parallel import argmax_column_parallel
         self.logits.zero_()
         argmax_column_parallel(self.comm, self.logits, self.vocab_begin, self.next_token)
@@ -292,9 +292,14 @@ class DeviceDecoder:
 
     def _layers(self, b: "_Rows", rows: int, rows_per_seq: int, seq0: int = 0) -> None:
         """Embedding lookup of b.tokens[:rows] through every block; leaves the
-        final-normed rows in b.normed.  Row r is sequence seq0 + r / rows_per_seq
-        at position *position + r % rows_per_seq (one sequence's prompt, or one
-        token of each of `rows` sequences)."""
+        residual rows in b.x (the head applies the final norm).  Row r is
+        sequence seq0 + r / rows_per_seq at position *position + r %
+        rows_per_seq (one sequence's prompt, or one token of each of `rows`
+        sequences).  Per layer: norm1 + q|k|v, RoPE / cache / attention, the
+        output projection added to the residual, norm2 + gate|up + SiLU * up,
+        the down projection added to the residual -- five launches at batch 1,
+        where the GEMV applies each norm while staging its input row and forms
+        silu(gate) * up in its epilogue."""
         L_ = _lib.load()
         cfg, h = self.cfg, self.ctx.handle
         s, p = self._stream(), self._p
@@ -307,12 +312,12 @@ class DeviceDecoder:
                                                s))
         else:
             _lib.check(L_.kt_dequantize_rows(h, self.embedding.handle, p(b.tokens), rows, p(b.x), p(self.status), s))
-        _lib.check(L_.kt_rmsnorm(h, p(b.x), p(self.layers[0]["norm1"]), p(b.normed), rows, cfg.dim, cfg.eps, s))
         for l, L in enumerate(self.layers):
-            MatMul.multiply_quantized(b.normed[:rows], L["wqkv"], b.qkv[:rows], rows, accumulate=False,
-                                      bias=L["bqkv"])
-            if rows_per_seq == 1 and self._fused_attention:
-                # one token per sequence: RoPE, cache store, attention and merge in one launch
+            _lib.check(L_.kt_rmsnorm_qmatmul(h, L["wqkv"].handle, p(b.x), p(L["norm1"]), cfg.eps, p(b.normed),
+                                             p(b.qkv), rows, 0, p(L["bqkv"]), s))
+            if rows == 1 and self._fused_attention:
+                # one token of one sequence: RoPE, cache store, attention and merge in one launch
+                # (measured slower than the separate kernels once several sequences share a step)
                 _lib.check(L_.kt_attention_rope_decode(h, p(b.qkv), rows, self.q_width, self.heads_local, kvh, hd,
                                                        p(self.inv_freq), keys, values, p(b.ctx), p(b.scores),
                                                        self.max_seq, l, self.scale, p(self.position),
@@ -324,20 +329,18 @@ class DeviceDecoder:
                 _lib.check(L_.kt_attention_seqs(h, p(b.qkv), keys, values, p(b.ctx), p(b.scores), rows,
                                                 self.q_width + 2 * kv, self.heads_local, kvh, hd, self.max_seq, l,
                                                 self.scale, p(self.position), rows_per_seq, self.cache_stride, s))
-            self._row_parallel(b.ctx[:rows], L["wo"], b.attn[:rows], rows, L["bo"])
-            _lib.check(L_.kt_add_rmsnorm(h, p(b.x), p(b.attn), p(L["norm2"]), p(b.normed), rows, cfg.dim, cfg.eps, s))
-            # gate|up with silu(gate) * up (in the GEMV's epilogue where it applies)
-            _lib.check(L_.kt_qmatmul_swiglu(h, L["wgu"].handle, p(b.normed), p(b.gu), p(b.act), rows, 1.0,
-                                            p(L["bgu"]), s))
-            self._row_parallel(b.act[:rows], L["wd"], b.ffn[:rows], rows, L["bd"])
-            nxt = self.layers[l + 1]["norm1"] if l + 1 < len(self.layers) else self.final_norm
-            _lib.check(L_.kt_add_rmsnorm(h, p(b.x), p(b.ffn), p(nxt), p(b.normed), rows, cfg.dim, cfg.eps, s))
+            self._row_parallel(b.ctx[:rows], L["wo"], b.x[:rows], rows, L["bo"])  # x += attention output
+            _lib.check(L_.kt_rmsnorm_qmatmul_swiglu(h, L["wgu"].handle, p(b.x), p(L["norm2"]), cfg.eps,
+                                                    p(b.normed), p(b.gu), p(b.act), rows, p(L["bgu"]), s))
+            self._row_parallel(b.act[:rows], L["wd"], b.x[:rows], rows, L["bd"])  # x += feed-forward output
 
-    def _head(self, normed, advance: int) -> None:
-        """The head on `batch` normed rows, greedy argmax per row, position += advance."""
+    def _head(self, x_rows, advance: int) -> None:
+        """The final norm and the head on `batch` residual rows, greedy argmax
+        per row, position += advance."""
         L_ = _lib.load()
         h, s, p = self.ctx.handle, self._stream(), self._p
-        MatMul.multiply_quantized(normed, self.head, self.logits, self.batch, accumulate=False, bias=self.head_bias)
+        _lib.check(L_.kt_rmsnorm_qmatmul(h, self.head.handle, p(x_rows), p(self.final_norm), self.cfg.eps,
+                                         p(self._head_xn), p(self.logits), self.batch, 0, p(self.head_bias), s))
         if self.comm is None:
             _lib.check(L_.kt_argmax(h, p(self.logits), self.batch, self.cfg.vocab, p(self.next_token), s))
         else:  # every rank's best column, merged across ranks: the same token everywhere
@@ -352,7 +355,7 @@ class DeviceDecoder:
         the position and feeds the next tokens back."""
         b = self._step_bufs
         self._layers(b, self.batch, 1)
-        self._head(b.normed, 1)
+        self._head(b.x, 1)
 
     def _result(self):
         return self.logits[0] if self.batch == 1 else self.logits
@@ -399,7 +402,7 @@ class DeviceDecoder:
             # the head only on each sequence's last row
             self._last_rows[:s1 - s0].copy_(torch.tensor([q * T + T - 1 for q in range(s1 - s0)], dtype=torch.int32))
             dst = ctypes.c_void_p(self._head_in.data_ptr() + s0 * self.cfg.dim * self._head_in.element_size())
-            _lib.check(L_.kt_gather_rows(self.ctx.handle, self._p(b.normed), self._p(self._last_rows), s1 - s0,
+            _lib.check(L_.kt_gather_rows(self.ctx.handle, self._p(b.x), self._p(self._last_rows), s1 - s0,
                                          self.cfg.dim, dst, self._stream()))
         self._head(self._head_in, T)
         self.length += T

@@ -544,3 +544,57 @@ def test_swiglu_epilogue_equals_matmul_then_silu(kt, oracle, k, h, m):
     ref = g / (1.0 + np.exp(-g)) * u
     assert rel_err(got.cpu().numpy(), ref) <= TOL_FP32
     assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("bits,k,n", [(4, 896, 1152), (4, 4096, 6144), (4, 896, 9728), (4, 4096, 28672),
+                                      (8, 768, 2304)])
+@pytest.mark.parametrize("m", [1, 3])
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_rmsnorm_prologue_matches_rmsnorm_then_matmul(kt, oracle, bits, k, n, m, swiglu):
+    """kt_rmsnorm_qmatmul(_swiglu): RMSNorm(x) . W + bias (then silu(gate) * up).
+    At m = 1 on INT4 the norm is applied while the GEMV stages x (each CTA sums
+    the row's squares itself); elsewhere kt_rmsnorm then the matmul.  Within
+    1e-5 of the separate kernels (the squares are added in another order) and
+    within the fp32 tolerance of the oracle; accumulate into c included."""
+    import ctypes
+    from kotensor_b200 import _lib
+    lib = kt.load_library()
+    rng = np.random.default_rng(k + n + m + bits + swiglu)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, bits, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), bits, 64)
+    xh = (rng.standard_normal((m, k), dtype=np.float32) * 3).astype(np.float32)
+    nwh = (1.0 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    bh = (0.1 * rng.standard_normal(n)).astype(np.float32)
+    x, nw, bias = dev(xh), dev(nwh), dev(bh)
+    h_ = kt.Context.get().handle
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    xn = torch.empty((m, k), device="cuda")
+    gu = torch.empty((m, n), device="cuda")
+    out_n = n // 2 if swiglu else n
+    c0 = torch.randn((m, out_n), device="cuda")
+    want = c0.clone()
+    _lib.check(lib.kt_rmsnorm(h_, p(x), p(nw), p(xn), m, k, 1e-6, s))
+    if swiglu:
+        _lib.check(lib.kt_qmatmul_swiglu(h_, qt.handle, p(xn), p(gu), p(want), m, 1.0, p(bias), s))
+    else:
+        _lib.check(lib.kt_qmatmul(h_, qt.handle, p(xn), p(want), m, 1, 1.0, p(bias), s))
+    got = c0.clone()
+    if swiglu:
+        _lib.check(lib.kt_rmsnorm_qmatmul_swiglu(h_, qt.handle, p(x), p(nw), 1e-6, p(xn), p(gu), p(got), m, p(bias), s))
+    else:
+        _lib.check(lib.kt_rmsnorm_qmatmul(h_, qt.handle, p(x), p(nw), 1e-6, p(xn), p(got), m, 1, p(bias), s))
+    torch.cuda.synchronize()
+    assert ((got - want).abs().max() / want.abs().max()).item() <= 1e-5
+    # against the oracle: RMSNorm in float64, the quantized product
+    xd = xh.astype(np.float64)
+    xnh = (xd / np.sqrt((xd * xd).mean(axis=1, keepdims=True) + 1e-6) * nwh).astype(np.float32)
+    y = oracle.multiply_quantized(xnh, ref_t, threads=8) + bh[None, :]
+    if swiglu:
+        g, u = y[:, :n // 2].astype(np.float64), y[:, n // 2:].astype(np.float64)
+        ref = g / (1.0 + np.exp(-g)) * u
+    else:
+        ref = c0.cpu().numpy() + y
+    assert rel_err(got.cpu().numpy(), ref) <= TOL_FP32
+    assert kt.Context.get().take_error() == 0
