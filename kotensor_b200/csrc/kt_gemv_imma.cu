@@ -1,4 +1,4 @@
-// kt_gemv_imma.cu -- INT4 decode GEMV for one token (m = 1) on integer
+// kt_gemv_imma.cu -- INT4 / INT8 decode GEMV for one token (m = 1) on integer
 // tensor-core products: MatMul.multiplyQuantized (Engine/kotensor/src/main/
 // kotlin/MatMul.kt:460-536, :599-828) for m = 1, the decode step's shape.
 //
@@ -28,6 +28,11 @@
 // and fp32 accumulation -- fp32 class for any spread of magnitudes inside a
 // warp's rows up to 2^22 (outlier channels included).
 //
+// INT8 weights (BITS = 8) run the same pipeline on signed bytes (s8 x s8
+// MMAs): A rows g and g + 8 are words 4g + 2jj and 4g + 2jj + 1 of the lane's
+// 16-byte chunk (two MMA pairs per chunk instead of four), a tile is 128
+// output columns, and the group combine has no zero point (out += scale * D).
+//
 // Tiling and streaming are those of the fp16 kernel (kt_gemv_mma.cu): a CTA
 // owns 128 packed bytes of every row (256 output columns); 4 pairs of warps
 // own consecutive K-slices; each pair streams its slice through a ring of
@@ -38,6 +43,7 @@
 // CTA of a tile sums the split partials in split order (deterministic).
 #include <algorithm>
 #include <atomic>
+#include <initializer_list>
 #include <cstdlib>
 
 #include "kt_device.cuh"
@@ -63,7 +69,9 @@ constexpr int kScaleSlotBytes = 2 * kTileBytes * 4 + 2 * kTileBytes;  // 1280: s
 constexpr int kRingBytes = kStages * kStageBytes;
 constexpr int kSlotRingBytes = kStages * kScaleSlotBytes;
 constexpr int kMainBytes = kPairs * kRingBytes;
-constexpr int kCT = 2 * kTileBytes;                                   // 256 output columns per tile
+// output columns per tile: 256 (INT4, two nibbles per byte) or 128 (INT8)
+template <int BITS>
+constexpr int ct_of() { return BITS == 4 ? 2 * kTileBytes : kTileBytes; }
 constexpr int kRedBytes = kWarps * 8 * 32 * 4;                        // reuses the rings
 constexpr int kXsBytes = kMaxSliceRows * 4;                           // [row]{xh, xm, xl, 0}
 constexpr int kSxBytes = kMaxSliceRows / kBlockRows * 4;              // [block] sum of X
@@ -102,14 +110,25 @@ __device__ __forceinline__ void imma_16832(int (&c)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void imma_16832_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ void pair_barrier(int pair) {
     asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
 }
 
 // Shared memory: rings[4 slices][NS][32][128] (later red[8][8][32]) |
 // slots[4][NS][1280] | x staging[4][kXsPairBytes] | mbarriers[4][2][NS].
+template <int BITS>
 __global__ void __launch_bounds__(kThreads, 2)
     gemv_imma_kernel(const __grid_constant__ CUtensorMap tmap, ImmaParams p) {
+    constexpr int kCT = ct_of<BITS>();
+    constexpr int kJ = BITS == 4 ? 4 : 2;  // MMA pairs per 8-row block and warp
     extern __shared__ __align__(1024) unsigned char smem[];
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -158,7 +177,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     // slot (group - g_first) % NS (lanes 1-4 of warp 0; the arming arrive of
     // lane 0 is still pending, so their complete_tx cannot finish the phase).
     int p_row = r_begin, p_gi = g_first, p_gstart = r_begin, p_issued = 0;
-    const uint32_t sbytes = static_cast<uint32_t>(tile_cols) * 10;
+    // INT4: lanes 1-4 copy the low / high nibble columns' scales and zero
+    // points (s_lo, s_hi, z_lo, z_hi); INT8: lane 1 copies the tile's scales
+    const uint32_t sbytes = static_cast<uint32_t>(tile_cols) * (BITS == 4 ? 10 : 4);
+    const int n_copy_lanes = BITS == 4 ? 4 : 1;
     const uint32_t lane_off = lane <= 2 ? (lane - 1) * kTileBytes * 4 : kTileBytes * (5 + lane);
     const uint32_t lane_bytes = lane <= 2 ? tile_cols * 4 : tile_cols;
     const unsigned char* lane_src =
@@ -174,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             tma_load_2d(ring_s + slot * kStageBytes, &tmap, tile_b0, p_row, bar);
         }
         if (group_start) {
-            if (lane >= 1 && lane <= 4) {
+            if (lane >= 1 && lane <= n_copy_lanes) {
                 const uint32_t dst = slots_s + ((p_gi - g_first) & (kStages - 1)) * kScaleSlotBytes + lane_off;
                 bulk_load(dst, lane_src + static_cast<int64_t>(p_gi) * p.N * lane_esize, lane_bytes, bar);
             }
@@ -287,13 +309,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     // each (u = t & 1); low nibbles for t < 2, high nibbles for t >= 2.
     const int u = t & 1;
     const bool low_owner = t < 2;
-    float y[8];
+    float y[2 * kJ];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) y[e] = 0.0f;
-    int c[4][4];  // {xh, xm} parts
-    int e[4][4];  // xl part (columns 0-3)
+    for (int e = 0; e < 2 * kJ; ++e) y[e] = 0.0f;
+    int c[kJ][4];  // {xh, xm} parts
+    int e[kJ][4];  // xl part (columns 0-3)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = e[j][0] = e[j][1] = e[j][2] = e[j][3] = 0;
+    for (int j = 0; j < kJ; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = e[j][0] = e[j][1] = e[j][2] = e[j][3] = 0;
     long long sx = 0;  // this warp's sum of X over the group's rows so far (|X| < 2^22: 64-bit for any group size)
     bool ok = true;
     int done = 0;
@@ -336,15 +358,22 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint4 w0 = *reinterpret_cast<const uint4*>(stage + blk * kBlockRows * kTileBytes + off0);
             const uint4 w1 = *reinterpret_cast<const uint4*>(stage + blk * kBlockRows * kTileBytes + off1);
             sx += sxb[brow / kBlockRows];
-            const uint32_t a[4][4] = {
-                {w0.x & 0x0F0F0F0Fu, w0.x & 0xF0F0F0F0u, w1.x & 0x0F0F0F0Fu, w1.x & 0xF0F0F0F0u},
-                {w0.y & 0x0F0F0F0Fu, w0.y & 0xF0F0F0F0u, w1.y & 0x0F0F0F0Fu, w1.y & 0xF0F0F0F0u},
-                {w0.z & 0x0F0F0F0Fu, w0.z & 0xF0F0F0F0u, w1.z & 0x0F0F0F0Fu, w1.z & 0xF0F0F0F0u},
-                {w0.w & 0x0F0F0F0Fu, w0.w & 0xF0F0F0F0u, w1.w & 0x0F0F0F0Fu, w1.w & 0xF0F0F0F0u}};
+            if constexpr (BITS == 4) {
+                const uint32_t a[4][4] = {
+                    {w0.x & 0x0F0F0F0Fu, w0.x & 0xF0F0F0F0u, w1.x & 0x0F0F0F0Fu, w1.x & 0xF0F0F0F0u},
+                    {w0.y & 0x0F0F0F0Fu, w0.y & 0xF0F0F0F0u, w1.y & 0x0F0F0F0Fu, w1.y & 0xF0F0F0F0u},
+                    {w0.z & 0x0F0F0F0Fu, w0.z & 0xF0F0F0F0u, w1.z & 0x0F0F0F0Fu, w1.z & 0xF0F0F0F0u},
+                    {w0.w & 0x0F0F0F0Fu, w0.w & 0xF0F0F0F0u, w1.w & 0x0F0F0F0Fu, w1.w & 0xF0F0F0F0u}};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                imma_16832(c[j], a[j][0], a[j][1], a[j][2], a[j][3], b0, b1);
-                imma_16832(e[j], a[j][0], a[j][1], a[j][2], a[j][3], l0, l1);
+                for (int j = 0; j < kJ; ++j) {
+                    imma_16832(c[j], a[j][0], a[j][1], a[j][2], a[j][3], b0, b1);
+                    imma_16832(e[j], a[j][0], a[j][1], a[j][2], a[j][3], l0, l1);
+                }
+            } else {  // A rows g, g + 8: words 4g + 2jj, 4g + 2jj + 1 of rows 2t (a0, a1) and 2t + 1 (a2, a3)
+                imma_16832_s8(c[0], w0.x, w0.y, w1.x, w1.y, b0, b1);
+                imma_16832_s8(e[0], w0.x, w0.y, w1.x, w1.y, l0, l1);
+                imma_16832_s8(c[kJ - 1], w0.z, w0.w, w1.z, w1.w, b0, b1);
+                imma_16832_s8(e[kJ - 1], w0.z, w0.w, w1.z, w1.w, l0, l1);
             }
         }
         __syncwarp();
@@ -361,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint8_t* z_arr = sl + kTileBytes * (low_owner ? 8 : 9);
             const float sxf = static_cast<float>(sx);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < kJ; ++j) {
                 const int send0 = low_owner ? c[j][2] : c[j][0];
                 const int send1 = low_owner ? c[j][3] : c[j][1];
                 const int recv0 = __shfl_xor_sync(0xffffffffu, send0, 2);
@@ -377,15 +406,22 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const float dl1 = static_cast<float>(low_owner ? e[j][1] : lrecv1);
                 const float d0 = fmaf(dh0, 65536.0f, fmaf(dm0, 256.0f, dl0));
                 const float d1 = fmaf(dh1, 65536.0f, fmaf(dm1, 256.0f, dl1));
-                const int b = 16 * g + 4 * j + 2 * u;  // byte of the tile row
-                const float2 s2 = *reinterpret_cast<const float2*>(s_arr + b);
-                const uint32_t z2 = *reinterpret_cast<const uint16_t*>(z_arr + b);
-                const float k16 = low_owner ? 1.0f : 0.0625f;
-                y[2 * j] = fmaf(s2.x, fmaf(d0, k16, -static_cast<float>(z2 & 0xFFu) * sxf), y[2 * j]);
-                y[2 * j + 1] = fmaf(s2.y, fmaf(d1, k16, -static_cast<float>(z2 >> 8) * sxf), y[2 * j + 1]);
+                if constexpr (BITS == 4) {
+                    const int b = 16 * g + 4 * j + 2 * u;  // byte of the tile row
+                    const float2 s2 = *reinterpret_cast<const float2*>(s_arr + b);
+                    const uint32_t z2 = *reinterpret_cast<const uint16_t*>(z_arr + b);
+                    const float k16 = low_owner ? 1.0f : 0.0625f;
+                    y[2 * j] = fmaf(s2.x, fmaf(d0, k16, -static_cast<float>(z2 & 0xFFu) * sxf), y[2 * j]);
+                    y[2 * j + 1] = fmaf(s2.y, fmaf(d1, k16, -static_cast<float>(z2 >> 8) * sxf), y[2 * j + 1]);
+                } else {  // word 4g + 2j (rows g, lanes t < 2) or 4g + 2j + 1 (rows g + 8), bytes 2u, 2u + 1
+                    const int b = 16 * g + 8 * j + (low_owner ? 0 : 4) + 2 * u;
+                    const float2 s2 = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(sl) + b);
+                    y[2 * j] = fmaf(s2.x, d0, y[2 * j]);
+                    y[2 * j + 1] = fmaf(s2.y, d1, y[2 * j + 1]);
+                }
             }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = e[j][0] = e[j][1] = e[j][2] = e[j][3] = 0;
+            for (int j = 0; j < kJ; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = e[j][0] = e[j][1] = e[j][2] = e[j][3] = 0;
             sx = 0;
             ++gi;
             group_end = min((gi + 1) * p.gs, r_end);
@@ -404,24 +440,32 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     float* red = reinterpret_cast<float*>(smem);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) red[(warp * 8 + e) * 32 + lane] = y[e] * unscale;
+    for (int e = 0; e < 2 * kJ; ++e) red[(warp * 8 + e) * 32 + lane] = y[e] * unscale;
     __syncthreads();
-    // column col = tid: byte b = col % 128 of the tile row, high nibble if
-    // col >= 128; its lane (g, t) and register e as assigned above
+    // column col = tid (< kCT): byte b = col % 128 of the tile row; INT4: high
+    // nibble if col >= 128, lane half hi = the nibble, j = the word of the
+    // chunk; INT8: the word jw of the chunk is j = jw / 2, lane half hi = jw % 2.
+    // Its lane (g, t) and register e as assigned above.
     float v = 0.0f;
-    {
+    if (tid < kCT) {
         const int b = tid & (kTileBytes - 1);
-        const int hi = tid >> 7;
-        const int gg = b >> 4, j = (b >> 2) & 3, sg = b & 3;
+        const int gg = b >> 4, jw = (b >> 2) & 3, sg = b & 3;
+        const int hi = BITS == 4 ? tid >> 7 : jw & 1;
+        const int j = BITS == 4 ? jw : jw >> 1;
         const int ln = 4 * gg + 2 * hi + (sg >> 1);
         const int e = 2 * j + (sg & 1);
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) v += red[(w * 8 + e) * 32 + ln];
     }
+    // output column of tile column col (INT4: low nibbles then high nibbles)
+    auto out_col_of = [&](int col) {
+        const int byte = tile_b0 + (col & (kTileBytes - 1));
+        return BITS == 4 && col >= kTileBytes ? half + byte : byte;
+    };
     auto emit = [&](int col, float val) {
         const int byte = tile_b0 + (col & (kTileBytes - 1));
-        const int out_col = col < kTileBytes ? byte : half + byte;
-        if (byte < p.R && out_col < p.N) {
+        const int out_col = out_col_of(col);
+        if (col < kCT && byte < p.R && out_col < p.N) {
             float* out = p.y + out_col;
             float r = fmaf(p.alpha, val, p.accumulate ? *out : 0.0f);
             if (p.bias != nullptr) r += p.bias[out_col];
@@ -458,8 +502,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int P = p.tp.nranks;
         const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.tp.state) + 1u;
         const int byte = tile_b0 + (col & (kTileBytes - 1));
-        const int out_col = col < kTileBytes ? byte : half + byte;
-        const bool valid = byte < p.R && out_col < p.N;
+        const int out_col = out_col_of(col);
+        const bool valid = col < kCT && byte < p.R && out_col < p.N;
         const int64_t slot_base = static_cast<int64_t>(epoch & 1u) * P * p.tp.n_cap;
         if (valid) {
             const float mine = p.alpha * val;
@@ -490,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // the CTA with its column tid; the gate column of byte b (low nibble, thread
     // b) and its up column (high nibble, thread 128 + b) meet in shared memory
     // (SwiGLU.forwardInto: silu(gate) * up, Tensor.kt:231-237).
-    __shared__ float s_swig[kCT];
+    __shared__ float s_swig[2 * kTileBytes];
     auto swiglu_out = [&](int b, float g, float u) {
         g = fmaf(p.alpha, g, 0.0f);  // the arithmetic of emit(), so both paths give the same bits
         u = fmaf(p.alpha, u, 0.0f);
@@ -524,16 +568,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         // (= split) order through distributed shared memory; a second barrier
         // keeps every CTA's shared memory alive until all ranks have read it.
         __shared__ float cpart[kCT];
-        cpart[tid] = v;
+        if (tid < kCT) cpart[tid] = v;
         cluster_sync();
-        if (p.swiglu) {  // rank r sums both columns of bytes [r * per, (r + 1) * per)
+        if (BITS == 4 && p.swiglu) {  // rank r sums both columns of bytes [r * per, (r + 1) * per)
             const int per = (kTileBytes + S - 1) / S;
             const int b = static_cast<int>(cluster_rank()) * per + tid;
             if (tid < per && b < kTileBytes && tile_b0 + b < p.R) {
                 float g = 0.0f, u = 0.0f;
                 for (int j = 0; j < S; ++j) {  // split order
                     g += ld_dsmem(smem_u32(cpart + b), j);
-                    u += ld_dsmem(smem_u32(cpart + kTileBytes + b), j);
+                    u += ld_dsmem(smem_u32(cpart + (kCT - kTileBytes) + b), j);
                 }
                 swiglu_out(tile_b0 + b, g, u);
             }
@@ -561,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // thread's store before thread 0's acq_rel atomic; the second barrier hands
     // the acquire to the whole CTA).
     float* tile_parts = p.partials + static_cast<int64_t>(blockIdx.x) * S * kCT;
-    __stcg(tile_parts + static_cast<int64_t>(blockIdx.y) * kCT + tid, v);
+    if (tid < kCT) __stcg(tile_parts + static_cast<int64_t>(blockIdx.y) * kCT + tid, v);
     __syncthreads();
     if (tid == 0) s_last = atomic_add_acq_rel(p.tickets + blockIdx.x, 1) == S - 1;
     __syncthreads();
@@ -576,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int j = 0; j < 32; ++j)
             tv[j] = s0 + j == static_cast<int>(blockIdx.y) ? v
-                    : s0 + j < S ? __ldcg(tile_parts + static_cast<int64_t>(s0 + j) * kCT + tid) : 0.0f;
+                    : s0 + j < S && tid < kCT ? __ldcg(tile_parts + static_cast<int64_t>(s0 + j) * kCT + tid) : 0.0f;
 #pragma unroll
         for (int j = 0; j < 32; ++j)
             if (s0 + j < S) sum += tv[j];
@@ -602,9 +646,10 @@ int blocks_per_sm() {
         if (c != 0) return c;
     }
     int n = 0;
-    if (cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    // the INT4 kernel: the INT8 one has the same shared memory and no more registers
+    if (cudaFuncSetAttribute(gemv_imma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_imma_kernel, kThreads, kSmemBytes) != cudaSuccess)
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_imma_kernel<4>, kThreads, kSmemBytes) != cudaSuccess)
         n = 1;
     cudaGetLastError();
     n = std::max(n, 1);
@@ -650,9 +695,11 @@ cudaError_t prepare_kernel() {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
-    e = cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes));
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    for (auto kernel : {gemv_imma_kernel<4>, gemv_imma_kernel<8>}) {
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    }
     if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) done[dev].store(true, std::memory_order_release);
     return e;
 }
@@ -680,10 +727,10 @@ int active_clusters(int c) {
     attr[0].val.clusterDim.z = 1;
     lc.attrs = attr;
     lc.numAttrs = 1;
-    if (cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemv_imma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) != cudaSuccess ||
-        cudaFuncSetAttribute(gemv_imma_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
-        cudaOccupancyMaxActiveClusters(&n, gemv_imma_kernel, &lc) != cudaSuccess)
+        cudaFuncSetAttribute(gemv_imma_kernel<4>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, gemv_imma_kernel<4>, &lc) != cudaSuccess)
         n = 0;
     cudaGetLastError();
     if (slot != nullptr) slot->store(n + 1, std::memory_order_release);
@@ -727,7 +774,7 @@ Plan plan_for(int R, int K, int sm_count, bool no_cluster = false) {
 void set_imma_tuning(int k_splits) { split_override().store(k_splits, std::memory_order_relaxed); }
 
 bool gemv_imma_supported(const QView& w, int32_t m, const float* a) {
-    if (w.bits != 4 || m != 1 || w.tmap_mma == nullptr) return false;
+    if ((w.bits != 4 && w.bits != 8) || m != 1 || w.tmap_mma == nullptr) return false;
     if (a != nullptr && reinterpret_cast<uintptr_t>(a) % 16 != 0) return false;
     return w.columns % 32 == 0 && w.rows % kRowsPerStage == 0 && w.group_size % kRowsPerStage == 0 &&
            min_splits(w.rows) <= 65535 && (min_splits(w.rows) == 1 || tiles_of(w.bytes_per_row) <= kTicketCapEach);
@@ -737,7 +784,8 @@ size_t gemv_imma_workspace_bytes(const QView& w, int sm_count, bool no_cluster) 
     const Plan plan = plan_for(w.bytes_per_row, w.rows, sm_count, no_cluster);
     if (plan.splits <= 1 || plan.cluster) return 0;
     return kWorkspaceReservedBytes +
-           static_cast<size_t>(tiles_of(w.bytes_per_row)) * plan.splits * kCT * sizeof(float);
+           static_cast<size_t>(tiles_of(w.bytes_per_row)) * plan.splits * (w.bits == 4 ? ct_of<4>() : ct_of<8>()) *
+               sizeof(float);
 }
 
 bool norm_fused_supported(const QView& w, int32_t m, const float* a) { return gemv_imma_supported(w, m, a); }
@@ -800,7 +848,7 @@ cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, 
     attr[1].val.clusterDim.z = 1;
     lc.attrs = attr;
     lc.numAttrs = plan.cluster ? 2 : 1;
-    return cudaLaunchKernelEx(&lc, gemv_imma_kernel, *w.tmap_mma, p);
+    return cudaLaunchKernelEx(&lc, w.bits == 4 ? gemv_imma_kernel<4> : gemv_imma_kernel<8>, *w.tmap_mma, p);
 }
 
 }  // namespace kt

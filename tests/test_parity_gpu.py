@@ -598,3 +598,32 @@ def test_rmsnorm_prologue_matches_rmsnorm_then_matmul(kt, oracle, bits, k, n, m,
         ref = c0.cpu().numpy() + y
     assert rel_err(got.cpu().numpy(), ref) <= TOL_FP32
     assert kt.Context.get().take_error() == 0
+
+
+@pytest.mark.parametrize("k_splits", [0, 1, 2, 5, 37])
+@pytest.mark.parametrize("k,n,g", [(2048, 2048, 64), (768, 32000, 64), (4096, 1024, 32), (960, 2304, 96),
+                                   (14336, 4096, 64)])
+def test_int8_tensor_core_gemv_matches_the_oracle(kt, oracle, k_splits, k, n, g):
+    """INT8 weights at m = 1 on the integer tensor-core GEMV (signed-byte MMAs,
+    128 output columns per tile): every K-split count (clusters and partials in
+    global memory), accumulate / alpha / bias, a wide dynamic range, within the
+    fp32 tolerance of the oracle; BASELINE config 1's 2048 x 2048 included."""
+    from kotensor_b200 import _lib
+    lib = kt.load_library()
+    rng = np.random.default_rng(k + n + g + k_splits)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 8, g)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, None, (k, n), 8, g)
+    assert qt.matmul_path(1) == _lib.KT_PATH_GEMV_MMA
+    try:
+        lib.kt_set_gemv_mma_tuning(k_splits)
+        a = (rng.standard_normal((1, k), dtype=np.float32) * np.float32(3.0)).astype(np.float32)
+        a[0, : k // 3] *= np.float32(1e-3)
+        c0 = rng.standard_normal((1, n), dtype=np.float32)
+        bias = rng.standard_normal(n, dtype=np.float32)
+        y = run_matmul(kt, qt, a, c0=c0, accumulate=True, alpha=0.75, bias=bias)
+        ref = oracle.multiply_quantized(a, ref_t, c=c0, accumulate=True, alpha=0.75, threads=8) + bias[None, :]
+        assert rel_err(y, ref) <= TOL_FP32, rel_err(y, ref)
+    finally:
+        lib.kt_set_gemv_mma_tuning(0)
+    assert kt.Context.get().take_error() == 0
