@@ -93,29 +93,31 @@ __device__ __forceinline__ float ld_dsmem(uint32_t local, uint32_t rank) {
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
     return v;
 }
-// System-scope flag store / load (peer GPUs' memory) and a bounded wait for a
-// flag to reach `epoch`.  True only when the flag equals `epoch`: a flag beyond
-// it (wrap-around safe comparison) means the peer is more than one call ahead,
-// which only happens after an earlier call of the exchange timed out, and the
-// slot then holds another call's data -- false, as after `limit_ns`.
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// 64-bit words of the fused exchange: {call number (high half), value bits (low half)}
+// stored and loaded whole at system scope (peer GPUs' memory), no ordering implied.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ bool wait_epoch_sys(const uint32_t* p, uint32_t epoch, uint64_t limit_ns) {
-    uint32_t v = ld_acquire_sys(p);
-    if (v == epoch) return true;
-    const uint64_t t0 = globaltimer();
-    while (static_cast<int32_t>(v - epoch) < 0) {
-        if (globaltimer() - t0 > limit_ns) return false;
-        __nanosleep(100);
-        v = ld_acquire_sys(p);
+// Bounded wait for the word at p to carry call number `epoch`; its value in
+// *out.  False after limit_ns, or at once when the word carries a later call
+// (a peer ran ahead after an earlier call of the exchange timed out).
+__device__ __forceinline__ bool wait_word_sys(const unsigned long long* p, uint32_t epoch, uint64_t limit_ns,
+                                              float* out) {
+    unsigned long long w = ld_relaxed_sys_u64(p);
+    uint64_t t0 = 0;
+    while (static_cast<uint32_t>(w >> 32) != epoch) {
+        if (static_cast<int32_t>(static_cast<uint32_t>(w >> 32) - epoch) > 0) return false;
+        if (t0 == 0) t0 = globaltimer();
+        else if (globaltimer() - t0 > limit_ns) return false;
+        w = ld_relaxed_sys_u64(p);
     }
-    return v == epoch;
+    *out = __uint_as_float(static_cast<uint32_t>(w));
+    return true;
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }

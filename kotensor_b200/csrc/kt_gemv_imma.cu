@@ -473,27 +473,14 @@ __global__ void __launch_bounds__(kThreads, 2)
             *out = r;
         }
     };
-    // Row-parallel exchange (p.tp.nranks > 0), every thread of the CTA with its
-    // column: the call's number is this rank's count of completed calls + 1
-    // (the counter advances only when every CTA of the grid has exited, so the
-    // whole grid reads one value, and a replayed CUDA graph gets new ones);
-    // alpha * partial goes to every rank's receive area (slot epoch & 1, row of
-    // this rank), a CTA barrier, then thread 0 publishes the tile's flag on
-    // every rank (release at system scope, after the barrier: cumulative over
-    // the CTA's stores) and waits for every rank's flag of the tile here
-    // (acquire, bounded); the barrier hands the acquire to the CTA, which sums
-    // the ranks' rows in rank order (the same bits on every rank).
-    __shared__ int s_tp_ok;
-    auto tp_exit = [&]() {
-        if (p.tp.nranks == 0 || tid != 0) return;
-        __threadfence();
-        const uint32_t total = gridDim.x * gridDim.y;
-        if (atomicAdd(p.tp.state + 1, 1u) == total - 1) {  // the grid's last CTA
-            p.tp.state[1] = 0;
-            p.tp.state[0] += 1;
-            __threadfence();
-        }
-    };
+    // Row-parallel exchange (p.tp.nranks > 0), every thread with its column:
+    // the call's number is this rank's count of completed calls + 1 (the
+    // counter advances only when every CTA of the grid has exited, so the whole
+    // grid reads one value, and a replayed CUDA graph gets new ones).  The
+    // thread stores {number, alpha * partial} as one 64-bit word into every
+    // rank's receive area (slot number & 1, row of this rank), then reads the
+    // column's word of every rank in rank order until each carries this number
+    // (bounded) and sums their values -- the same bits on every rank.
     auto finish = [&](int col, float val) {
         if (p.tp.nranks == 0) {
             emit(col, val);
@@ -503,31 +490,38 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.tp.state) + 1u;
         const int byte = tile_b0 + (col & (kTileBytes - 1));
         const int out_col = out_col_of(col);
-        const bool valid = col < kCT && byte < p.R && out_col < p.N;
+        if (!(col < kCT && byte < p.R && out_col < p.N)) return;
         const int64_t slot_base = static_cast<int64_t>(epoch & 1u) * P * p.tp.n_cap;
-        if (valid) {
-            const float mine = p.alpha * val;
-            for (int q = 0; q < P; ++q) p.tp.recv[q][slot_base + static_cast<int64_t>(p.tp.rank) * p.tp.n_cap + out_col] = mine;
+        const unsigned long long word =
+            (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(p.alpha * val);
+        for (int q = 0; q < P; ++q)
+            st_relaxed_sys_u64(p.tp.recv[q] + slot_base + static_cast<int64_t>(p.tp.rank) * p.tp.n_cap + out_col, word);
+        const unsigned long long* mine = p.tp.recv[p.tp.rank] + slot_base + out_col;
+        float sum = 0.0f;
+        for (int src = 0; src < P; ++src) {
+            float v = 0.0f;
+            if (!wait_word_sys(mine + static_cast<int64_t>(src) * p.tp.n_cap, epoch, p.tp.wait_ns, &v)) {
+                atomicOr(p.err, 1);
+                return;
+            }
+            sum += v;
         }
-        __syncthreads();
-        if (tid == 0) {
-            const int64_t f = (static_cast<int64_t>(epoch & 1u) * p.tp.tile_cap + blockIdx.x) * P;
-            for (int q = 0; q < P; ++q) st_release_sys(p.tp.flags[q] + f + p.tp.rank, epoch);
-            bool ok = true;
-            for (int src = 0; src < P && ok; ++src)
-                ok = wait_epoch_sys(p.tp.flags[p.tp.rank] + f + src, epoch, p.tp.wait_ns);
-            if (!ok) atomicOr(p.err, 1);
-            s_tp_ok = ok ? 1 : 0;
-        }
-        __syncthreads();
-        if (valid && s_tp_ok) {
-            const float* row0 = p.tp.recv[p.tp.rank] + slot_base + out_col;
-            float sum = 0.0f;
-            for (int src = 0; src < P; ++src) sum += __ldcv(row0 + static_cast<int64_t>(src) * p.tp.n_cap);
-            float* out = p.y + out_col;
-            float r = sum + (p.accumulate ? *out : 0.0f);
-            if (p.bias != nullptr) r += p.bias[out_col];
-            *out = r;
+        float* out = p.y + out_col;
+        float r = sum + (p.accumulate ? *out : 0.0f);
+        if (p.bias != nullptr) r += p.bias[out_col];
+        *out = r;
+    };
+    // the grid's last CTA to exit advances this rank's call counter
+    auto tp_exit = [&]() {  // every thread of the CTA (uniform)
+        if (p.tp.nranks == 0) return;
+        __syncthreads();  // every thread of the CTA has read this call's number
+        if (tid != 0) return;
+        __threadfence();
+        const uint32_t total = gridDim.x * gridDim.y;
+        if (atomicAdd(p.tp.state + 1, 1u) == total - 1) {  // the grid's last CTA
+            p.tp.state[1] = 0;
+            p.tp.state[0] += 1;
+            __threadfence();
         }
     };
     // SwiGLU epilogue (p.swiglu; no exchange, no accumulate): every thread of

@@ -167,18 +167,18 @@ cudaError_t launch_dequantize_rows(const QView& w, const int32_t* rows, int32_t 
                                    int32_t* d_status, cudaStream_t s);
 
 // ---- kt_gemv.cu  (fp32-accumulate CUDA-core kernels; small m)
-// Row-parallel exchange fused into the m = 1 INT4 GEMV (set up by kt_tp.cu):
-// the last CTA of each column tile publishes alpha * its partial to every
-// rank's receive area over peer memory, raises its flag there, waits (bounded)
-// for every rank's flag of the tile and writes
-// c = sum over ranks in rank order + (accumulate ? c : 0) + bias.
-// nranks == 0: no exchange (the plain kernel).
+// Row-parallel exchange fused into the m = 1 GEMV (set up by kt_tp.cu): the
+// thread finishing output column j stores {call number, alpha * its partial}
+// as one 64-bit word into every rank's receive area over peer memory, then
+// polls (bounded) the word of every rank for column j until it carries this
+// call's number and writes c = sum over ranks in rank order + (accumulate ? c
+// : 0) + bias.  A word is stored and read whole, so its number vouches for
+// its value: no fences, no separate flags.  nranks == 0: no exchange.
 struct TpExchange {
-    float* const* recv = nullptr;      // device array [P]: rank q's receive area, mapped here ([2][P][n_cap] floats)
-    uint32_t* const* flags = nullptr;  // device array [P]: rank q's flags, mapped here ([2][tile_cap][P])
-    uint32_t* state = nullptr;         // this rank's own {calls completed, CTAs exited in this call}
-    int32_t nranks = 0, rank = 0, n_cap = 0, tile_cap = 0;
-    uint64_t wait_ns = 0;              // limit of the wait for the other ranks' flags
+    unsigned long long* const* recv = nullptr;  // device array [P]: rank q's receive area ([2][P][n_cap] words), mapped here
+    uint32_t* state = nullptr;                  // this rank's own {calls completed, CTAs exited in this call}
+    int32_t nranks = 0, rank = 0, n_cap = 0;
+    uint64_t wait_ns = 0;                       // limit of the wait for the other ranks' words
 };
 
 struct MatmulArgs {

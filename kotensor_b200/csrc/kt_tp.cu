@@ -11,11 +11,11 @@
 // Row-parallel at m = 1 (decode) with INT4 shards runs one kernel per rank
 // instead: the m = 1 GEMV with the exchange fused into its epilogue (one-shot
 // all-reduce over peer memory, kt_gemv_imma.cu).  Each rank owns an exchange
-// area -- receive rows [2][P][kTpNCap] floats and flags [2][kTpTileCap][P] --
+// area -- receive rows [2][P][kTpNCap] of 64-bit words {call number, value} --
 // mapped into every other rank's process with CUDA IPC (handles all-gathered
-// through NCCL); the last CTA of a column tile stores its partial into every
-// rank's area, raises the tile's flag there, waits for every rank's flag and
-// sums the rows in rank order.  Set up on the first such call (a collective:
+// through NCCL); the thread finishing an output column stores its word into
+// every rank's area, then polls the column's word of every rank until each
+// carries this call's number and sums the values in rank order.  Set up on the first such call (a collective:
 // every rank takes part and all use the fused kernel or none), and agreed once
 // per shard; KT_TP_FUSED=0 keeps the NCCL path.
 //
@@ -176,7 +176,6 @@ __global__ void merge_argmax_kernel(const int32_t* __restrict__ gathered, int32_
 
 constexpr int kTpMaxRanks = 8;
 constexpr int32_t kTpNCap = 65536;     // output columns of a fused row-parallel GEMV
-constexpr int32_t kTpTileCap = 256;    // its column tiles (256 columns each)
 
 struct kt_comm {
     kt_ctx* ctx = nullptr;
@@ -188,8 +187,7 @@ struct kt_comm {
     int p2p_state = 0;                  // 0 not set up, 1 ready, 2 unavailable
     void* area = nullptr;               // this rank's area (cudaMalloc)
     void* peers[kTpMaxRanks] = {};      // every rank's area as mapped here (own at [rank])
-    float** d_recv = nullptr;           // device arrays of the P receive / flag pointers
-    uint32_t** d_flags = nullptr;
+    unsigned long long** d_recv = nullptr;  // device array of the P receive-area pointers
     uint64_t wait_ns = 2000000000ull;   // limit of a fused call's wait for the other ranks (2 s)
 };
 
@@ -217,10 +215,9 @@ cudaError_t comm_scratch(kt_comm* c, size_t floats, float** out) {
     return cudaSuccess;
 }
 
-size_t tp_recv_bytes(int P) { return static_cast<size_t>(2) * P * kTpNCap * sizeof(float); }
-size_t tp_flag_bytes(int P) { return static_cast<size_t>(2) * kTpTileCap * P * sizeof(uint32_t); }
-// receive rows | flags | this rank's own call counter and CTA exit count
-size_t tp_area_bytes(int P) { return tp_recv_bytes(P) + tp_flag_bytes(P) + 16; }
+size_t tp_recv_bytes(int P) { return static_cast<size_t>(2) * P * kTpNCap * sizeof(unsigned long long); }
+// receive rows | this rank's own call counter and CTA exit count
+size_t tp_area_bytes(int P) { return tp_recv_bytes(P) + 16; }
 
 bool tp_fused_enabled() {
     static const bool on = [] {
@@ -253,10 +250,8 @@ void release_p2p(kt_comm* c) {
         if (q != c->rank && c->peers[q] != nullptr) cudaIpcCloseMemHandle(c->peers[q]);
     cudaFree(c->area);
     cudaFree(c->d_recv);
-    cudaFree(c->d_flags);
     c->area = nullptr;
     c->d_recv = nullptr;
-    c->d_flags = nullptr;
     for (void*& p : c->peers) p = nullptr;
     cudaGetLastError();
 }
@@ -294,16 +289,10 @@ kt_status setup_p2p(kt_comm* c, cudaStream_t s) {
                 ok = cudaIpcOpenMemHandle(&c->peers[q], all[q], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
     }
     if (ok) {
-        float* recv[kTpMaxRanks];
-        uint32_t* flags[kTpMaxRanks];
-        for (int q = 0; q < P; ++q) {
-            recv[q] = static_cast<float*>(c->peers[q]);
-            flags[q] = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(c->peers[q]) + tp_recv_bytes(P));
-        }
-        ok = cudaMalloc(&c->d_recv, sizeof(float*) * P) == cudaSuccess &&
-             cudaMalloc(&c->d_flags, sizeof(uint32_t*) * P) == cudaSuccess &&
-             cudaMemcpy(c->d_recv, recv, sizeof(float*) * P, cudaMemcpyHostToDevice) == cudaSuccess &&
-             cudaMemcpy(c->d_flags, flags, sizeof(uint32_t*) * P, cudaMemcpyHostToDevice) == cudaSuccess;
+        unsigned long long* recv[kTpMaxRanks];
+        for (int q = 0; q < P; ++q) recv[q] = static_cast<unsigned long long*>(c->peers[q]);
+        ok = cudaMalloc(&c->d_recv, sizeof(unsigned long long*) * P) == cudaSuccess &&
+             cudaMemcpy(c->d_recv, recv, sizeof(unsigned long long*) * P, cudaMemcpyHostToDevice) == cudaSuccess;
     }
     cudaGetLastError();
     bool every = false;
@@ -385,7 +374,6 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
             }
             const kt::QView v = kt::view(w);
             const bool mine = comm->p2p_state == 1 && w->columns <= kTpNCap &&
-                              (w->bytes_per_row + 127) / 128 <= kTpTileCap &&
                               kt::gemv_imma_tp_supported(v, ctx->sm_count);
             bool every = false;
             const kt_status st = all_agree(comm, mine, s, &every);
@@ -406,14 +394,12 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
             }
             kt::MatmulArgs args{a, c, bias, 1, accumulate, alpha, ctx->d_error};
             args.tp.recv = comm->d_recv;
-            args.tp.flags = comm->d_flags;
             args.tp.nranks = comm->nranks;
             args.tp.rank = comm->rank;
             args.tp.n_cap = kTpNCap;
-            args.tp.tile_cap = kTpTileCap;
             args.tp.wait_ns = comm->wait_ns;
             args.tp.state = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(comm->area) +
-                                                        tp_recv_bytes(comm->nranks) + tp_flag_bytes(comm->nranks));
+                                                        tp_recv_bytes(comm->nranks));
             const size_t need = kt::gemv_imma_workspace_bytes(v, ctx->sm_count, true);
             void* ws = nullptr;
             cudaError_t e = cudaSuccess;
