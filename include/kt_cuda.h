@@ -356,7 +356,7 @@ kt_status kt_rmsnorm_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const floa
  * kt_attention_scratch_floats(rows, heads, head_dim, max_seq) floats of the
  * attention, zero-filled before the first call (its last rows x heads words
  * are merge counters that every call leaves at zero).  heads / kv_heads <= 8,
- * head_dim even and <= 128, max_seq <= 16384, else KT_ERR_UNSUPPORTED. */
+ * head_dim 64 or 128, max_seq <= 16384, else KT_ERR_UNSUPPORTED. */
 kt_status kt_attention_rope_decode(kt_ctx* ctx, const float* qkv_dev, int32_t rows, int32_t q_width, int32_t heads,
                                    int32_t kv_heads, int32_t head_dim, const float* inv_freq_dev, float* k_cache,
                                    float* v_cache, float* context_dev, float* scratch_dev, int32_t max_seq,

@@ -1091,7 +1091,7 @@ kt_status kt_attention_rope_decode(kt_ctx* ctx, const float* qkv, int32_t rows, 
         return fail(KT_ERR_INVALID_ARGUMENT, "bad fused attention arguments");
     if (!attention_fused_supported(heads, kv_heads, head_dim, max_seq))
         return fail(KT_ERR_UNSUPPORTED,
-                    "fused decode attention needs heads / kv_heads <= 8, an even head_dim <= 128 and max_seq <= 16384");
+                    "fused decode attention needs heads / kv_heads <= 8, head_dim 64 or 128 and max_seq <= 16384");
     KT_CUDA_TRY(launch_attention_decode_fused(qkv, rows, q_width, heads, kv_heads, head_dim, inv_freq, k_cache,
                                               v_cache, context, scratch, max_seq, layer, scale, position_dev,
                                               cache_stride, pick(ctx, stream)),

@@ -407,8 +407,214 @@ __global__ void __launch_bounds__(kThreads) attention_group_kernel(
 // back at zero when the launch ends.  Rows of one sequence that attend to each
 // other's new keys (a prefill) keep the separate rope / store and attention
 // kernels.
-template <int G, int KPER>
+template <int G, int HD>
 __global__ void __launch_bounds__(kThreads) attention_decode_fused_kernel(
+    const float* __restrict__ qkv, int q_width, const float* __restrict__ inv_freq, float* __restrict__ kc,
+    float* __restrict__ vc, float* __restrict__ scratch, int32_t* __restrict__ tickets, float* __restrict__ ctx,
+    int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale, const int32_t* __restrict__ pos,
+    int64_t cache_stride) {
+    dev::pdl_wait();  // qkv comes from the previous kernel (programmatic dependent launch)
+    dev::pdl_launch_dependents();
+    constexpr int kWarps = kThreads / 32;
+    static_assert(G <= kWarps, "one warp per query head finishes the statistics");
+    static_assert(HD % 4 == 0 && HD <= 128 && kThreads % HD == 0, "head_dim layout");
+    constexpr int kQ = HD / 4;                 // dims of a key row per thread (4 threads per position)
+    constexpr int kPG = kThreads / HD;         // position groups of the value pass
+    __shared__ __align__(16) float qs[G][HD];  // the rotated query heads
+    __shared__ float sc[G][kSpan];
+    __shared__ float stat[G][2];               // max, sum of exponentials
+    __shared__ float part[kPG][G][HD];
+    __shared__ int s_last;
+    const int kvh = blockIdx.x, split = blockIdx.y, t = blockIdx.z;
+    const int p = *pos;
+    const int j0 = split * kSpan;
+    const int j1 = min(j0 + kSpan, p + 1);
+    if (j0 >= j1) return;  // past the current position
+    kc += t * cache_stride;
+    vc += t * cache_stride;
+    const int n = j1 - j0;
+    constexpr int half = HD / 2;
+    const int kv_width = kv_heads * HD;
+    const float* row = qkv + static_cast<int64_t>(t) * (q_width + 2 * kv_width);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t base = ((static_cast<int64_t>(layer) * kv_heads + kvh) * max_seq) * HD;
+    // RoPE of element d of a head vector v at position p (the rope kernel's arithmetic)
+    auto rotated = [&](const float* v, int d) {
+        const int i = d < half ? d : d - half;
+        float s1, c1;
+        sincosf(static_cast<float>(p) * __ldg(inv_freq + i), &s1, &c1);
+        const float x1 = v[i], x2 = v[i + half];
+        return d < half ? x1 * c1 - x2 * s1 : x1 * s1 + x2 * c1;
+    };
+    if (j1 == p + 1) {  // this split holds the current position: its key and value into the cache
+        const float* kr = row + q_width + kvh * HD;
+        const float* vr = row + q_width + kv_width + kvh * HD;
+        const int64_t off = base + static_cast<int64_t>(p) * HD;
+        for (int d = threadIdx.x; d < HD; d += kThreads) {
+            kc[off + d] = rotated(kr, d);
+            vc[off + d] = vr[d];
+        }
+    }
+    for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
+        const int g = idx / HD, d = idx - g * HD;
+        qs[g][d] = rotated(row + static_cast<int64_t>(kvh * G + g) * HD, d);
+    }
+    __syncthreads();  // the query heads, and the block's own cache stores, visible to the block
+    // scores: four threads per position, each a quarter of the key row
+    {
+        const int jp = threadIdx.x >> 2, qd = threadIdx.x & 3;
+        const int j = j0 + jp;
+        float kq[kQ];
+        const float* kr = kc + base + static_cast<int64_t>(j) * HD + qd * kQ;
+#pragma unroll
+        for (int i = 0; i < kQ; i += 4) {
+            const float4 k4 = j < j1 ? *reinterpret_cast<const float4*>(kr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            kq[i] = k4.x;
+            kq[i + 1] = k4.y;
+            kq[i + 2] = k4.z;
+            kq[i + 3] = k4.w;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float dot = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kQ; ++i) dot = fmaf(qs[g][qd * kQ + i], kq[i], dot);
+            dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+            dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+            if (qd == 0 && j < j1) sc[g][jp] = dot * scale;
+        }
+    }
+    __syncthreads();
+    if (warp < G) {  // head `warp`: max and sum of exponentials over this split
+        const float s0 = lane < n ? sc[warp][lane] : -FLT_MAX;
+        const float s1 = lane + 32 < n ? sc[warp][lane + 32] : -FLT_MAX;
+        float mx = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float e0 = lane < n ? expf(s0 - mx) : 0.0f;
+        const float e1 = lane + 32 < n ? expf(s1 - mx) : 0.0f;
+        if (lane < n) sc[warp][lane] = e0;
+        if (lane + 32 < n) sc[warp][lane + 32] = e1;
+        float sum = e0 + e1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            stat[warp][0] = mx;
+            stat[warp][1] = sum;
+        }
+    }
+    __syncthreads();
+    // weighted values: thread (position group pg, dim d) over positions j0 + pg + kPG i
+    {
+        const int d = threadIdx.x % HD, pg = threadIdx.x / HD;
+        float acc[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) acc[g] = 0.0f;
+        constexpr int kPer = kSpan / kPG;
+        float vv[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int j = j0 + pg + kPG * i;
+            vv[i] = j < j1 ? vc[base + static_cast<int64_t>(j) * HD + d] : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int jl = pg + kPG * i;
+            if (j0 + jl < j1) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) acc[g] = fmaf(sc[g][jl], vv[i], acc[g]);
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) part[pg][g][d] = acc[g];
+    }
+    __syncthreads();
+    const int64_t splits = (max_seq + kSpan - 1) / kSpan;
+    for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
+        const int g = idx / HD, d = idx - g * HD;
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kPG; ++w) v += part[w][g][d];  // fixed order
+        float* out = scratch + ((static_cast<int64_t>(t) * heads + kvh * G + g) * splits + split) * (HD + 2);
+        out[2 + d] = v;
+        if (d == 0) {
+            out[0] = stat[g][0];
+            out[1] = stat[g][1];
+        }
+    }
+    // the last of the row's active splits to arrive merges them (the barrier
+    // orders every thread's partial stores before thread 0's acq_rel ticket)
+    const int active = p / kSpan + 1;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int32_t* ticket = tickets + static_cast<int64_t>(t) * kv_heads + kvh;
+        s_last = active == 1 || dev::atomic_add_acq_rel(ticket, 1) == active - 1;
+        if (s_last && active > 1) *ticket = 0;  // every split has arrived: ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    // merge: warp g loads head g's split statistics, takes the maximum and the
+    // sum of exponentials (fixed reduction order) and keeps each split's factor
+    // in shared memory; then each thread sums the splits' values for its
+    // outputs with every load of a chunk of 8 splits in flight at once
+    constexpr int stride = HD + 2;
+    __shared__ float coef[G][kMaxFusedSplits];
+    __shared__ float inv_l[G];
+    if (warp < G) {
+        const float* hb = scratch + (static_cast<int64_t>(t) * heads + kvh * G + warp) * splits * stride;
+        float m = -1e9f;
+        for (int s2 = lane; s2 < active; s2 += 32) m = fmaxf(m, __ldcg(hb + s2 * stride));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int s2 = lane; s2 < active; s2 += 32) {
+            const float e = expf(__ldcg(hb + s2 * stride) - m);
+            coef[warp][s2] = e;
+            l = fmaf(__ldcg(hb + s2 * stride + 1), e, l);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) inv_l[warp] = 1.0f / l;
+    }
+    __syncthreads();
+    constexpr int kOuts = (G * HD + kThreads - 1) / kThreads;  // outputs per thread
+    float vsum[kOuts];
+#pragma unroll
+    for (int o2 = 0; o2 < kOuts; ++o2) vsum[o2] = 0.0f;
+    for (int s0 = 0; s0 < active; s0 += 8) {
+        float u[kOuts][8];
+#pragma unroll
+        for (int o2 = 0; o2 < kOuts; ++o2) {
+            const int idx = threadIdx.x + kThreads * o2;
+            const int g = idx / HD, d = idx - g * HD;
+            const float* hv = scratch + (static_cast<int64_t>(t) * heads + kvh * G + g) * splits * stride + 2 + d;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                u[o2][j] = idx < G * HD && s0 + j < active ? __ldcg(hv + (s0 + j) * stride) : 0.0f;
+        }
+#pragma unroll
+        for (int o2 = 0; o2 < kOuts; ++o2) {
+            const int g = min((threadIdx.x + kThreads * o2) / HD, G - 1);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (s0 + j < active) vsum[o2] = fmaf(u[o2][j], coef[g][s0 + j], vsum[o2]);
+        }
+    }
+#pragma unroll
+    for (int o2 = 0; o2 < kOuts; ++o2) {
+        const int idx = threadIdx.x + kThreads * o2;
+        if (idx < G * HD) {
+            const int g = idx / HD, d = idx - g * HD;
+            ctx[(static_cast<int64_t>(t) * heads + kvh * G + g) * HD + d] = vsum[o2] * inv_l[g];
+        }
+    }
+}
+
+// The same for head_dim 128 with a warp per position (a lane holds KPER dims
+// of the G query vectors in registers; key and value rows of the warp's
+// positions loaded together), measured faster than the kernel above there.
+template <int G, int KPER>
+__global__ void __launch_bounds__(kThreads) attention_decode_fused_wide_kernel(
     const float* __restrict__ qkv, int q_width, const float* __restrict__ inv_freq, float* __restrict__ kc,
     float* __restrict__ vc, float* __restrict__ scratch, int32_t* __restrict__ tickets, float* __restrict__ ctx,
     int heads, int kv_heads, int head_dim, int max_seq, int layer, float scale, const int32_t* __restrict__ pos,
@@ -827,7 +1033,7 @@ size_t attention_scratch_floats(int rows, int heads, int head_dim, int max_seq) 
 }
 
 bool attention_fused_supported(int heads, int kv_heads, int head_dim, int max_seq) {
-    return kv_heads > 0 && heads % kv_heads == 0 && heads / kv_heads <= 8 && head_dim % 2 == 0 && head_dim <= 128 &&
+    return kv_heads > 0 && heads % kv_heads == 0 && heads / kv_heads <= 8 && (head_dim == 64 || head_dim == 128) &&
            (max_seq + kSpan - 1) / kSpan <= kMaxFusedSplits;
 }
 
@@ -855,9 +1061,13 @@ cudaError_t launch_attention_decode_fused(const float* qkv, int rows, int q_widt
         case 7: KT_FUSED_CASE(7, KP_); break; \
         default: KT_FUSED_CASE(8, KP_); break; \
     }
-    if (head_dim <= 64) {
-        KT_FUSED_GROUPS(2)
+    if (head_dim == 64) {
+        KT_FUSED_GROUPS(64)
     } else {
+#undef KT_FUSED_CASE
+#define KT_FUSED_CASE(G_, KP_)                                                                                  \
+    launch_pdl(attention_decode_fused_wide_kernel<G_, KP_>, grid, dim3(kThreads), 0, s, qkv, q_width, inv_freq, kc, \
+               vc, scratch, tickets, ctx, heads, kv_heads, head_dim, max_seq, layer, scale, pos, cache_stride)
         KT_FUSED_GROUPS(4)
     }
 #undef KT_FUSED_GROUPS

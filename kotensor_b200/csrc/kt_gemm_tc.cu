@@ -858,16 +858,28 @@ __global__ void x_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __r
 // to m = 128 (one token tile); above, gemm_tc_kernel's 256-token tiles
 // dequantize each weight tile half as often (measured faster at m = 512).
 // KT_GEMM_TS=0 keeps every m on gemm_tc_kernel, for comparison.
+// Largest m the TMEM-A kernel takes, in token tiles of at most kTsMaxNT
+// (KT_GEMM_TS_MAX; default kTsMaxNT: one token tile).
+int ts_max_m() {
+    static const int v = [] {
+        const char* e = std::getenv("KT_GEMM_TS_MAX");
+        return e ? std::max(0, std::atoi(e)) : kTsMaxNT;
+    }();
+    return v;
+}
 bool use_ts(const QView& w, int m) {
     static const bool on = [] {
         const char* v = std::getenv("KT_GEMM_TS");
         return v == nullptr || std::atoi(v) != 0;
     }();
-    return on && w.bits == 4 && w.tmap_mma != nullptr && m <= kTsMaxNT;
+    return on && w.bits == 4 && w.tmap_mma != nullptr && m <= std::max(kTsMaxNT, ts_max_m());
 }
 
-// Tokens per CTA (the MMA's N): m rounded up to 16, at most 256.
-int nt_for(const QView& w, int m) { return std::min(kMaxNT, (m + 15) / 16 * 16); }
+// Tokens per CTA (the MMA's N): m rounded up to 16, at most 256 (128 on the
+// TMEM-A kernel).
+int nt_for(const QView& w, int m) {
+    return std::min(use_ts(w, m) ? kTsMaxNT : kMaxNT, (m + 15) / 16 * 16);
+}
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 

@@ -33,6 +33,7 @@
 #include <mutex>
 #include <string>
 
+#include "kt_device.cuh"
 #include "kt_internal.h"
 
 namespace {
@@ -118,6 +119,69 @@ __global__ void gather_columns_kernel(const float* __restrict__ gathered, float*
 
 int blocks_for(int64_t total) { return static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16)); }
 
+// Row-parallel above m = 1 (or on shards the fused GEMV does not take): the
+// partial product sits in the communicator's scratch; one kernel exchanges it
+// over peer memory the way the fused GEMV's epilogue does -- every thread
+// stores {call number, value} words for its elements into every rank's receive
+// row, then reads every rank's word of each of its elements in rank order until
+// it carries this call's number (bounded; a later number fails at once) and
+// writes c = sum + (accumulate ? c : 0) + bias -- and the grid's last CTA
+// advances this rank's call counter.  The grid is small enough to be resident
+// at once (a thread never waits for a CTA of its own grid).
+struct LLExchange {
+    unsigned long long* const* recv;  // [P] receive areas ([2][P][cap] words), mapped here
+    uint32_t* state;                  // this rank's {calls completed, CTAs exited in this call}
+    int32_t nranks, rank, cap;
+    uint64_t wait_ns;
+    int32_t* err;
+};
+__global__ void __launch_bounds__(256) ll_allreduce_kernel(const float* __restrict__ part, float* __restrict__ c,
+                                                           const float* __restrict__ bias, int64_t total, int32_t n,
+                                                           int32_t accumulate, LLExchange x) {
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(x.state) + 1u;
+    const int64_t slot_base = static_cast<int64_t>(epoch & 1u) * x.nranks * x.cap;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (int64_t i = first; i < total; i += step) {
+        const unsigned long long word = (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(part[i]);
+        for (int q = 0; q < x.nranks; ++q)
+            kt::dev::st_relaxed_sys_u64(x.recv[q] + slot_base + static_cast<int64_t>(x.rank) * x.cap + i, word);
+    }
+    bool ok = true;
+    for (int64_t i = first; i < total && ok; i += step) {
+        const unsigned long long* mine = x.recv[x.rank] + slot_base + i;
+        float sum = 0.0f;
+        for (int src = 0; src < x.nranks && ok; ++src) {
+            float v = 0.0f;
+            ok = kt::dev::wait_word_sys(mine + static_cast<int64_t>(src) * x.cap, epoch, x.wait_ns, &v);
+            sum += v;
+        }
+        if (ok) {
+            float r = sum + (accumulate ? c[i] : 0.0f);
+            if (bias != nullptr) r += bias[i % n];
+            c[i] = r;
+        }
+    }
+    if (!ok) atomicOr(x.err, 1);
+    __syncthreads();  // every thread of the CTA has read this call's number
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(x.state + 1, 1u) == gridDim.x - 1) {  // the grid's last CTA
+            x.state[1] = 0;
+            x.state[0] += 1;
+            __threadfence();
+        }
+    }
+}
+
+bool tp_ll_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("KT_TP_LL");
+        return v == nullptr || std::atoi(v) != 0;
+    }();
+    return on;
+}
+
 // Greedy decoding over an lm head split along N (argmaxOfLastToken,
 // Transformer.kt:255-266, kept across shards): per row the largest logit above
 // -1e9 and, among equal ones, the lowest column.  Stage 1 on every rank: the
@@ -175,7 +239,7 @@ __global__ void merge_argmax_kernel(const int32_t* __restrict__ gathered, int32_
 }  // namespace
 
 constexpr int kTpMaxRanks = 8;
-constexpr int32_t kTpNCap = 65536;     // output columns of a fused row-parallel GEMV
+constexpr int32_t kTpNCap = 262144;    // words of a rank's receive row: m x N of one exchange
 
 struct kt_comm {
     kt_ctx* ctx = nullptr;
@@ -410,6 +474,28 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
         }
     }
     const int64_t total = static_cast<int64_t>(m) * w_shard->columns;
+    if (tp_fused_enabled() && tp_ll_enabled() && total <= kTpNCap && comm->p2p_state != 2) {
+        if (comm->p2p_state == 0) {  // collective, same call order everywhere
+            const kt_status st = setup_p2p(comm, s);
+            if (st != KT_OK) return st;
+        }
+        if (comm->p2p_state == 1) {
+            float* part = nullptr;
+            cudaError_t e = comm_scratch(comm, static_cast<size_t>(total), &part);
+            if (e != cudaSuccess)
+                return fail_tp(KT_ERR_OUT_OF_MEMORY, std::string("TP scratch: ") + cudaGetErrorString(e));
+            kt_status st = kt::run_qmatmul(ctx, w_shard, a_shard, part, m, 0, alpha, nullptr, s);
+            if (st != KT_OK) return st;
+            LLExchange x{comm->d_recv,
+                         reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(comm->area) + tp_recv_bytes(comm->nranks)),
+                         comm->nranks, comm->rank, kTpNCap, comm->wait_ns, ctx->d_error};
+            const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, ctx->sm_count));
+            ll_allreduce_kernel<<<blocks, 256, 0, s>>>(part, c, bias, total, w_shard->columns, accumulate, x);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("exchange: ") + cudaGetErrorString(e));
+            return KT_OK;
+        }
+    }
     float* sum = nullptr;
     cudaError_t e = comm_scratch(comm, static_cast<size_t>(total), &sum);
     if (e != cudaSuccess) return fail_tp(KT_ERR_OUT_OF_MEMORY, std::string("TP scratch: ") + cudaGetErrorString(e));

@@ -213,7 +213,7 @@ class DeviceDecoder:
         self.scale = float(np.float32(1.0) / np.float32(math.sqrt(float(cfg.head_dim))))
         self._graph = None
         g_ = self.heads_local // self.kv_local
-        self._fused_attention = g_ <= 8 and cfg.head_dim % 2 == 0 and cfg.head_dim <= 128 and max_seq <= 16384
+        self._fused_attention = g_ <= 8 and cfg.head_dim in (64, 128) and max_seq <= 16384
         if P > 1:
             self._warm_exchanges()
 
@@ -315,9 +315,10 @@ class DeviceDecoder:
         for l, L in enumerate(self.layers):
             _lib.check(L_.kt_rmsnorm_qmatmul(h, L["wqkv"].handle, p(b.x), p(L["norm1"]), cfg.eps, p(b.normed),
                                              p(b.qkv), rows, 0, p(L["bqkv"]), s))
-            if rows == 1 and self._fused_attention:
-                # one token of one sequence: RoPE, cache store, attention and merge in one launch
-                # (measured slower than the separate kernels once several sequences share a step)
+            if rows_per_seq == 1 and self._fused_attention and (rows == 1 or cfg.head_dim == 64):
+                # one token per sequence: RoPE, cache store, attention and merge in one launch
+                # (with head_dim 128 measured slower than the separate kernels once
+                # several sequences share a step)
                 _lib.check(L_.kt_attention_rope_decode(h, p(b.qkv), rows, self.q_width, self.heads_local, kvh, hd,
                                                        p(self.inv_freq), keys, values, p(b.ctx), p(b.scores),
                                                        self.max_seq, l, self.scale, p(self.position),

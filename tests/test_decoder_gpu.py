@@ -186,7 +186,7 @@ def test_batched_graph_replay_matches_eager_steps(kt, oracle):
     assert kt.Context.get().take_error() == 0
 
 
-@pytest.mark.parametrize("heads,kv_heads,head_dim", [(12, 12, 64), (14, 2, 64), (32, 8, 128), (4, 1, 8), (7, 7, 128)])
+@pytest.mark.parametrize("heads,kv_heads,head_dim", [(12, 12, 64), (14, 2, 64), (32, 8, 128), (8, 1, 64), (7, 7, 128)])
 @pytest.mark.parametrize("position", [0, 63, 64, 200])
 def test_fused_decode_attention_matches_the_separate_kernels(kt, heads, kv_heads, head_dim, position):
     """kt_attention_rope_decode (RoPE, cache store, attention and merge in one
@@ -236,3 +236,17 @@ def test_fused_decode_attention_matches_the_separate_kernels(kt, heads, kv_heads
         ntick = rows * heads
         assert not torch.any(fused_sc[nsc - ntick:].view(torch.int32)).item()  # counters back at zero
     assert kt.Context.get().take_error() == 0
+
+
+def test_fused_decode_attention_rejects_other_head_dims(kt):
+    """The fused kernel is built for head_dim 64 and 128; other shapes are
+    refused (the decoder then runs the separate kernels)."""
+    import ctypes
+    from kotensor_b200 import _lib
+    lib = kt.load_library()
+    t = torch.zeros(4096, device="cuda")
+    pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+    p = ctypes.c_void_p(t.data_ptr())
+    st = lib.kt_attention_rope_decode(kt.Context.get().handle, p, 1, 32, 4, 1, 8, p, p, p, p, p, 16, 0, 0.1,
+                                      ctypes.c_void_p(pos.data_ptr()), 0, None)
+    assert st == _lib.KT_ERR_UNSUPPORTED
