@@ -1051,17 +1051,23 @@ kt_status rmsnorm_matmul(kt_ctx* ctx, const kt_qweight* w, const float* x, const
         return fail(KT_ERR_INVALID_ARGUMENT, "SwiGLU needs a gate | up weight with an even number of columns");
     const cudaStream_t s = pick(ctx, stream);
     const QView v = view(w);
-    const bool fused = norm_fused_supported(v, m, x) && reinterpret_cast<uintptr_t>(norm_w) % 16 == 0 &&
-                       (!swiglu || swiglu_fused_supported(v, m, x));
-    if (fused) {
-        MatmulArgs args{x, c, bias, m, accumulate, 1.0f, ctx->d_error};
+    const bool norm_in = norm_fused_supported(v, m, x) && reinterpret_cast<uintptr_t>(norm_w) % 16 == 0;
+    const bool swiglu_in = swiglu && swiglu_fused_supported(v, m, x);
+    if (norm_in && swiglu && !swiglu_in && !gu)
+        return fail(KT_ERR_INVALID_ARGUMENT, "this shape needs the gate | up scratch gu");
+    if (norm_in) {
+        // the norm in the GEMV's prologue; silu(gate) * up in its epilogue, or
+        // (weights whose gate and up columns do not share a tile) a separate kernel
+        MatmulArgs args{x, swiglu && !swiglu_in ? gu : c, bias, m, swiglu ? 0 : accumulate, 1.0f, ctx->d_error};
         args.norm_weight = norm_w;
         args.norm_eps = eps;
-        args.swiglu = swiglu ? 1 : 0;
+        args.swiglu = swiglu_in ? 1 : 0;
         const size_t need = gemv_imma_workspace_bytes(v, ctx->sm_count);
         void* ws = nullptr;
         if (need > 0) KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "qmatmul workspace");
         KT_CUDA_TRY(launch_gemv_imma(v, args, ctx->sm_count, s, ws, need), "rmsnorm_qmatmul launch");
+        if (swiglu && !swiglu_in)
+            KT_CUDA_TRY(launch_silu_mul_rows(gu, c, m, w->columns / 2, s), "silu_mul launch");
         return KT_OK;
     }
     if (!xn || (swiglu && !gu)) return fail(KT_ERR_INVALID_ARGUMENT, "this shape needs the scratch rows xn / gu");

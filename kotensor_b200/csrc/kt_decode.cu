@@ -317,22 +317,33 @@ __global__ void __launch_bounds__(kThreads) attention_group_kernel(
         }
     }
     const int64_t base = ((static_cast<int64_t>(layer) * kv_heads + kvh) * max_seq) * head_dim;
-    for (int j = j0 + warp; j < j1; j += kWarps) {
-        const float* kr = kc + base + static_cast<int64_t>(j) * head_dim;
-        float kv[KPER];
+    // four of the warp's positions per round: their key rows are loaded before
+    // any is used (more bytes in flight per warp on long, many-sequence steps)
+    constexpr int kRound = 4;
+    for (int jb = j0 + warp; jb < j1; jb += kWarps * kRound) {
+        float kv[kRound][KPER];
 #pragma unroll
-        for (int i = 0; i < KPER; ++i) {
-            const int d = lane + 32 * i;
-            kv[i] = d < head_dim ? kr[d] : 0.0f;
+        for (int r = 0; r < kRound; ++r) {
+            const int j = jb + kWarps * r;
+            const float* kr = kc + base + static_cast<int64_t>(j) * head_dim;
+#pragma unroll
+            for (int i = 0; i < KPER; ++i) {
+                const int d = lane + 32 * i;
+                kv[r][i] = j < j1 && d < head_dim ? kr[d] : 0.0f;
+            }
         }
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            float dot = 0.0f;
+        for (int r = 0; r < kRound; ++r) {
+            const int j = jb + kWarps * r;
 #pragma unroll
-            for (int i = 0; i < KPER; ++i) dot = fmaf(qv[g][i], kv[i], dot);
+            for (int g = 0; g < G; ++g) {
+                float dot = 0.0f;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-            if (lane == 0) sc[g][j - j0] = dot * scale;
+                for (int i = 0; i < KPER; ++i) dot = fmaf(qv[g][i], kv[r][i], dot);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+                if (lane == 0 && j < j1) sc[g][j - j0] = dot * scale;
+            }
         }
     }
     __syncthreads();
@@ -360,19 +371,29 @@ __global__ void __launch_bounds__(kThreads) attention_group_kernel(
     for (int g = 0; g < G; ++g)
 #pragma unroll
         for (int i = 0; i < KPER; ++i) acc[g][i] = 0.0f;
-    for (int j = j0 + warp; j < j1; j += kWarps) {
-        const float* vr = vc + base + static_cast<int64_t>(j) * head_dim;
-        float vv[KPER];
+    for (int jb = j0 + warp; jb < j1; jb += kWarps * kRound) {
+        float vv[kRound][KPER];
 #pragma unroll
-        for (int i = 0; i < KPER; ++i) {
-            const int d = lane + 32 * i;
-            vv[i] = d < head_dim ? vr[d] : 0.0f;
+        for (int r = 0; r < kRound; ++r) {
+            const int j = jb + kWarps * r;
+            const float* vr = vc + base + static_cast<int64_t>(j) * head_dim;
+#pragma unroll
+            for (int i = 0; i < KPER; ++i) {
+                const int d = lane + 32 * i;
+                vv[r][i] = j < j1 && d < head_dim ? vr[d] : 0.0f;
+            }
         }
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float w = sc[g][j - j0];
+        for (int r = 0; r < kRound; ++r) {
+            const int j = jb + kWarps * r;
+            if (j < j1) {
 #pragma unroll
-            for (int i = 0; i < KPER; ++i) acc[g][i] = fmaf(w, vv[i], acc[g][i]);
+                for (int g = 0; g < G; ++g) {
+                    const float w = sc[g][j - j0];
+#pragma unroll
+                    for (int i = 0; i < KPER; ++i) acc[g][i] = fmaf(w, vv[r][i], acc[g][i]);
+                }
+            }
         }
     }
 #pragma unroll
