@@ -10,7 +10,10 @@
 // Every kernel reads the token position (and token id) from device memory so
 // a whole step can be captured once into a CUDA graph and replayed.  The KV
 // cache is the reference's: fp32 keys / values [layers][kvHeads][maxSeq][headDim].
+#include <algorithm>
+#include <atomic>
 #include <cfloat>
+#include <cstdlib>
 
 #include "kt_device.cuh"
 #include "kt_internal.h"
@@ -408,6 +411,190 @@ __global__ void __launch_bounds__(kThreads) attention_group_kernel(
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) v += part[w][g][d];
         float* out = scratch + ((static_cast<int64_t>(t) * heads + kvh * G + g) * splits + split) * (head_dim + 2);
+        out[2 + d] = v;
+        if (d == 0) {
+            out[0] = stat[g][0];
+            out[1] = stat[g][1];
+        }
+    }
+}
+
+// The same partials as attention_group_kernel for head_dim 64 and 128 with
+// 16-byte aligned cache rows, the split's key and value rows staged in shared
+// memory by bulk copies issued before any arithmetic (64 positions: 32 or 64
+// KB in flight per block at once, where register loads keep a few KB per
+// warp), one block per (kv head, split, row).  Scores: lane l of a warp takes
+// position l of its half of the split and a quarter of the dims (the key rows
+// land 4 floats apart, so 32 lanes reading one column offset hit every bank
+// once per wavefront; the query is a broadcast), the four quarters summed in
+// order.  Values: warp w takes positions w, w + 8, ..., a lane holds HD / 32
+// dims of the G heads.  Waits on the copies are bounded: on a timeout the
+// block sets the error word, drains its copies (again bounded) and returns.
+template <int HD>
+struct StagedAttention {
+    static constexpr int kPad = HD + 4;  // floats between staged key rows
+    static constexpr int kQuarter = HD / 4;
+    template <int G>
+    static constexpr size_t smem_bytes() {
+        return sizeof(float) * (static_cast<size_t>(kSpan) * kPad + kSpan * HD + G * HD + 4 * G * kSpan + kSpan * G);
+    }
+};
+
+template <int G, int HD>
+__global__ void __launch_bounds__(kThreads) attention_group_staged_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    float* __restrict__ scratch, int heads, int kv_heads, int max_seq, int layer, float scale, int q_stride,
+    const int32_t* __restrict__ pos, int rows_per_seq, int64_t cache_stride, int32_t* __restrict__ err) {
+    using S = StagedAttention<HD>;
+    constexpr int kWarps = kThreads / 32;
+    static_assert(G <= kWarps && G * HD <= kSpan * S::kPad / kWarps, "one warp per head; partials fit the key area");
+    extern __shared__ __align__(16) float sm[];
+    float* ks = sm;                         // [kSpan][kPad]
+    float* vs = ks + kSpan * S::kPad;       // [kSpan][HD]
+    float* qs = vs + kSpan * HD;            // [G][HD]
+    float* sp = qs + G * HD;                // [4][G][kSpan] score quarters
+    float* pw = sp + 4 * G * kSpan;         // [kSpan][G] exp(score - max)
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ float stat[G][2];
+    dev::pdl_wait();  // the cache rows and q may come from the previous kernel
+    dev::pdl_launch_dependents();
+    const int kvh = blockIdx.x, split = blockIdx.y, t = blockIdx.z;
+    const int seq = t / rows_per_seq;
+    const int tp = t - seq * rows_per_seq;
+    const int j0 = split * kSpan;
+    const int j1 = min(j0 + kSpan, *pos + tp + 1);
+    if (j0 >= j1) return;  // past the current position: the merge skips this split
+    const int n = j1 - j0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t base =
+        seq * cache_stride + ((static_cast<int64_t>(layer) * kv_heads + kvh) * max_seq + j0) * HD;
+    const uint32_t bar_k = dev::smem_u32(&bars[0]), bar_v = dev::smem_u32(&bars[1]);
+    if (threadIdx.x == 0) {
+        dev::mbar_init(bar_k, 1);
+        dev::mbar_init(bar_v, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (warp == 0) {
+        if (lane == 0) {
+            dev::mbar_expect_tx(bar_k, static_cast<uint32_t>(n * HD * sizeof(float)));
+            dev::mbar_expect_tx(bar_v, static_cast<uint32_t>(n * HD * sizeof(float)));
+            dev::bulk_load(dev::smem_u32(vs), vc + base, static_cast<uint32_t>(n * HD * sizeof(float)), bar_v);
+        }
+        __syncwarp();
+        for (int j = lane; j < n; j += 32)
+            dev::bulk_load(dev::smem_u32(ks + j * S::kPad), kc + base + static_cast<int64_t>(j) * HD,
+                           HD * sizeof(float), bar_k);
+    }
+    const float* qh = q + static_cast<int64_t>(t) * q_stride + static_cast<int64_t>(kvh) * G * HD;
+    for (int i = threadIdx.x; i < G * HD; i += kThreads) qs[i] = qh[i];
+    __syncthreads();  // qs
+    bool ok = dev::mbar_wait_bounded(bar_k, 0);
+    if (__syncthreads_or(!ok)) {
+        if (threadIdx.x == 0) {
+            atomicOr(err, 1);
+            dev::mbar_wait_bounded(bar_k, 0);  // copies still in flight land before the block exits
+            dev::mbar_wait_bounded(bar_v, 0);
+        }
+        return;
+    }
+    {   // score quarters: lane -> position, warp -> (half of the positions, quarter of the dims)
+        // four running sums per head (dims 4i, 4i+1, 4i+2, 4i+3 of the quarter),
+        // added pairwise at the end: short dependency chains, and rounding
+        // closer to a tree sum than one chain of HD / 4
+        const int j = (warp & 1) * 32 + lane, dq = warp >> 1;
+        float acc[G][4];
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[g][e] = 0.0f;
+        if (j < n) {
+            const float* kr = ks + j * S::kPad + dq * S::kQuarter;
+            const float* qq = qs + dq * S::kQuarter;
+#pragma unroll
+            for (int c = 0; c < S::kQuarter; c += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(qq + g * HD + c);
+                    acc[g][0] = fmaf(q4.x, k4.x, acc[g][0]);
+                    acc[g][1] = fmaf(q4.y, k4.y, acc[g][1]);
+                    acc[g][2] = fmaf(q4.z, k4.z, acc[g][2]);
+                    acc[g][3] = fmaf(q4.w, k4.w, acc[g][3]);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                sp[(dq * G + g) * kSpan + j] = (acc[g][0] + acc[g][1]) + (acc[g][2] + acc[g][3]);
+        }
+    }
+    __syncthreads();
+    if (warp < G) {  // head `warp`: max and sum of exponentials over this split
+        const int g = warp;
+        auto score = [&](int j) {
+            return (((sp[(0 * G + g) * kSpan + j] + sp[(1 * G + g) * kSpan + j]) + sp[(2 * G + g) * kSpan + j]) +
+                    sp[(3 * G + g) * kSpan + j]) * scale;
+        };
+        const float s0 = lane < n ? score(lane) : -FLT_MAX;
+        const float s1 = lane + 32 < n ? score(lane + 32) : -FLT_MAX;
+        float mx = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float e0 = lane < n ? expf(s0 - mx) : 0.0f;
+        const float e1 = lane + 32 < n ? expf(s1 - mx) : 0.0f;
+        pw[lane * G + g] = e0;
+        pw[(lane + 32) * G + g] = e1;
+        float sum = e0 + e1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            stat[g][0] = mx;
+            stat[g][1] = sum;
+        }
+    }
+    ok = dev::mbar_wait_bounded(bar_v, 0);
+    if (__syncthreads_or(!ok)) {  // also publishes pw and stat
+        if (threadIdx.x == 0) {
+            atomicOr(err, 1);
+            dev::mbar_wait_bounded(bar_v, 0);
+        }
+        return;
+    }
+    constexpr int kDims = HD / 32;  // per lane: 2 or 4 consecutive dims
+    float acc[G][kDims];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < kDims; ++i) acc[g][i] = 0.0f;
+    for (int j = warp; j < n; j += kWarps) {
+        float v[kDims];
+        if constexpr (kDims == 4) {
+            const float4 v4 = *reinterpret_cast<const float4*>(vs + j * HD + 4 * lane);
+            v[0] = v4.x, v[1] = v4.y, v[2] = v4.z, v[3] = v4.w;
+        } else {
+            const float2 v2 = *reinterpret_cast<const float2*>(vs + j * HD + 2 * lane);
+            v[0] = v2.x, v[1] = v2.y;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float w = pw[j * G + g];
+#pragma unroll
+            for (int i = 0; i < kDims; ++i) acc[g][i] = fmaf(w, v[i], acc[g][i]);
+        }
+    }
+    float* part = ks;  // [kWarps][G][HD]; the key rows are no longer read
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < kDims; ++i) part[(warp * G + g) * HD + kDims * lane + i] = acc[g][i];
+    __syncthreads();
+    const int64_t splits = (max_seq + kSpan - 1) / kSpan;
+    for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
+        const int g = idx / HD, d = idx - g * HD;
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) v += part[(w * G + g) * HD + d];
+        float* out = scratch + ((static_cast<int64_t>(t) * heads + kvh * G + g) * splits + split) * (HD + 2);
         out[2 + d] = v;
         if (d == 0) {
             out[0] = stat[g][0];
@@ -1107,14 +1294,81 @@ cudaError_t launch_kv_store(const float* k, const float* v, float* kc, float* vc
         k, v, kc, vc, rows, kv_heads, head_dim, max_seq, layer, pos);
     return cudaGetLastError();
 }
+// Dynamic shared memory of every staged-attention instantiation (once per device).
+template <int HD>
+cudaError_t prepare_staged_attention() {
+    constexpr int kMaxDevices = 64;
+    static std::atomic<bool> done[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+#define KT_STAGED_ATTR(G_)                                                                                    \
+    if (e == cudaSuccess)                                                                                     \
+        e = cudaFuncSetAttribute(attention_group_staged_kernel<G_, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 static_cast<int>(StagedAttention<HD>::template smem_bytes<G_>()));
+    KT_STAGED_ATTR(1) KT_STAGED_ATTR(2) KT_STAGED_ATTR(3) KT_STAGED_ATTR(4)
+    KT_STAGED_ATTR(5) KT_STAGED_ATTR(6) KT_STAGED_ATTR(7) KT_STAGED_ATTR(8)
+#undef KT_STAGED_ATTR
+    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) done[dev].store(true, std::memory_order_release);
+    return e;
+}
+
+bool staged_attention_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("KT_ATTN_STAGED");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+template <int HD>
+cudaError_t launch_staged_attention(dim3 grid, int group, cudaStream_t s, const float* q, const float* kc,
+                                    const float* vc, float* scores, int heads, int kv_heads, int max_seq, int layer,
+                                    float scale, int q_stride, const int32_t* pos, int rows_per_seq,
+                                    int64_t cache_stride, int32_t* err) {
+    const cudaError_t e = prepare_staged_attention<HD>();
+    if (e != cudaSuccess) return e;
+#define KT_STAGED_CASE(G_)                                                                                        \
+    return launch_pdl(attention_group_staged_kernel<G_, HD>, grid, dim3(kThreads),                                 \
+                      StagedAttention<HD>::template smem_bytes<G_>(), s, q, kc, vc, scores, heads, kv_heads, max_seq, \
+                      layer, scale, q_stride, pos, rows_per_seq, cache_stride, err)
+    switch (group) {
+        case 1: KT_STAGED_CASE(1);
+        case 2: KT_STAGED_CASE(2);
+        case 3: KT_STAGED_CASE(3);
+        case 4: KT_STAGED_CASE(4);
+        case 5: KT_STAGED_CASE(5);
+        case 6: KT_STAGED_CASE(6);
+        case 7: KT_STAGED_CASE(7);
+        default: KT_STAGED_CASE(8);
+    }
+#undef KT_STAGED_CASE
+}
+
 cudaError_t launch_attention_decode(const float* q, const float* kc, const float* vc, float* ctx, float* scores,
                                     int rows, int q_stride, int heads, int kv_heads, int head_dim, int max_seq,
                                     int layer, float scale, const int32_t* pos, int rows_per_seq,
-                                    int64_t cache_stride, cudaStream_t s) {
+                                    int64_t cache_stride, int32_t* err, cudaStream_t s) {
     if (head_dim > kMaxHeadDim) return cudaErrorInvalidValue;
     const int splits = (max_seq + kSpan - 1) / kSpan;
     const int group = heads / kv_heads;
     const dim3 ggrid(kv_heads, splits, rows);
+    // staged: head_dim 64 / 128, cache rows on 16-byte boundaries (bulk copies)
+    const bool aligned = (reinterpret_cast<uintptr_t>(kc) & 15) == 0 && (reinterpret_cast<uintptr_t>(vc) & 15) == 0 &&
+                         cache_stride % 4 == 0;
+    if (staged_attention_enabled() && aligned && group <= 8 && (head_dim == 64 || head_dim == 128)) {
+        const cudaError_t e =
+            head_dim == 64
+                ? launch_staged_attention<64>(ggrid, group, s, q, kc, vc, scores, heads, kv_heads, max_seq, layer,
+                                              scale, q_stride, pos, rows_per_seq, cache_stride, err)
+                : launch_staged_attention<128>(ggrid, group, s, q, kc, vc, scores, heads, kv_heads, max_seq, layer,
+                                               scale, q_stride, pos, rows_per_seq, cache_stride, err);
+        if (e != cudaSuccess) return e;
+        launch_pdl(attention_merge_kernel, dim3(dim3(heads, rows)), dim3(128), 0, s, scores, ctx, heads, head_dim,
+                   max_seq, pos, rows_per_seq);
+        return cudaGetLastError();
+    }
 #define KT_GROUP_CASE(G_, KP_)                                                                                     \
     launch_pdl(attention_group_kernel<G_, KP_>, dim3(ggrid), dim3(kThreads), 0, s, q, kc, vc, scores, heads, kv_heads, head_dim,       \
                                                                max_seq, layer, scale, q_stride, pos, rows_per_seq, \

@@ -28,14 +28,15 @@
 // Unpacking without int->float conversions.  A nibble or byte q placed in the
 // top mantissa bits of the float 2^23 (bits 0x4B000000) gives the exact float
 // 2^23 + q*2^p with one LOP3 (the 2^23 pattern comes in as a kernel argument so
-// the mask is the instruction's only immediate); fp32 FMAs accumulate
-// T = sum_l a_l*(2^23 + q*2^p) and the group epilogue recovers
-// sum_l a_l*q = T*2^-p - 2^(23-p)*sum_l a_l.
+// the mask is the instruction's only immediate); one exact FADD removes the
+// offset (q*2^p for INT4; INT8 bytes are offset to unsigned by xor 0x80 and
+// 2^23 + 2^22 is removed, leaving the signed b*2^15), and fp32 FMAs accumulate
+// T = sum_l a_l*q*2^p alone -- fp32-class, where accumulating the offset too
+// (an earlier version) cost up to 11 bits of the accumulator.
 //   INT4 low nibbles sit at bits 16-19 (p = 16), high nibbles at bits 12-15
-//   (p = 12): 3 shift/permute ops + 8 LOP3 + 8 FFMA per 32-bit word of 8 weights.
-//   INT8 bytes are offset to unsigned (xor 0x80) and sit at bits 15-22 (p = 15).
-// The leading 2^23 term costs at most ~11 bits of the fp32 accumulator, a
-// relative error below 1e-4 of max|c| (the tolerance is 1e-3).
+//   (p = 12): 3 shift/permute ops + 8 LOP3 + 8 FADD + 8 FFMA per 32-bit word of
+//   8 weights.  INT8 bytes sit at bits 15-22 (p = 15).
+// The group epilogue: y += scale * (T*2^-p - zero * sum_l a_l).
 //
 // Split-K and the reduction order.  Each warp owns one contiguous row range
 // ("slice").  Slice partials are reduced in a fixed order: across the 8 warps
@@ -127,13 +128,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
-// (w & MASK) | magic as a float: one LOP3 (0xEA = a & b | c).
+// (w & MASK) | magic as a float, less the float's offset OFF: one LOP3
+// (0xEA = a & b | c) and one exact FADD.
 template <uint32_t MASK>
-__device__ __forceinline__ float nib(uint32_t w, uint32_t magic) {
+__device__ __forceinline__ float nib(uint32_t w, uint32_t magic, float off) {
     uint32_t d;
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(w), "n"(MASK), "r"(magic));
-    return __uint_as_float(d);
+    return __uint_as_float(d) - off;
 }
+constexpr float kOff4 = 8388608.0f;    // 2^23: the INT4 float 2^23 + q 2^p less 2^23 is q 2^p
+constexpr float kOff8 = 12582912.0f;   // 2^23 + 2^22: the INT8 float 2^23 + (b + 128) 2^15 less this is b 2^15
 
 // One 32-bit word of 4 packed INT4 bytes: low nibbles -> columns lo+0..3,
 // high nibbles -> columns hi+0..3 (indices into the lane's T array).
@@ -142,14 +146,14 @@ __device__ __forceinline__ void fma_int4_word(uint32_t w, uint32_t magic, const 
                                               int lo, int hi) {
     const uint32_t wl = w << 8, wr = w >> 8;
     const uint32_t t = __byte_perm(w, 0u, 0x4034);  // byte0 -> bits 16-23, byte3 -> bits 8-15
-    const float f_lo0 = nib<0x000F0000u>(t, magic);
-    const float f_hi3 = nib<0x0000F000u>(t, magic);
-    const float f_lo1 = nib<0x000F0000u>(wl, magic);
-    const float f_hi0 = nib<0x0000F000u>(wl, magic);
-    const float f_lo2 = nib<0x000F0000u>(w, magic);
-    const float f_hi1 = nib<0x0000F000u>(w, magic);
-    const float f_lo3 = nib<0x000F0000u>(wr, magic);
-    const float f_hi2 = nib<0x0000F000u>(wr, magic);
+    const float f_lo0 = nib<0x000F0000u>(t, magic, kOff4);
+    const float f_hi3 = nib<0x0000F000u>(t, magic, kOff4);
+    const float f_lo1 = nib<0x000F0000u>(wl, magic, kOff4);
+    const float f_hi0 = nib<0x0000F000u>(wl, magic, kOff4);
+    const float f_lo2 = nib<0x000F0000u>(w, magic, kOff4);
+    const float f_hi1 = nib<0x0000F000u>(w, magic, kOff4);
+    const float f_lo3 = nib<0x000F0000u>(wr, magic, kOff4);
+    const float f_hi2 = nib<0x0000F000u>(wr, magic, kOff4);
 #pragma unroll
     for (int m = 0; m < M; ++m) {
         T[m][lo + 0] = fmaf(xv[m], f_lo0, T[m][lo + 0]);
@@ -168,10 +172,10 @@ template <int M, int C>
 __device__ __forceinline__ void fma_int8_word(uint32_t w, uint32_t magic, const float (&xv)[M], float (&T)[M][C],
                                               int at) {
     const uint32_t u = w ^ 0x80808080u;  // two's complement byte b -> unsigned b + 128
-    const float f0 = nib<0x007F8000u>(u << 15, magic);
-    const float f1 = nib<0x007F8000u>(u << 7, magic);
-    const float f2 = nib<0x007F8000u>(u >> 1, magic);
-    const float f3 = nib<0x007F8000u>(u >> 9, magic);
+    const float f0 = nib<0x007F8000u>(u << 15, magic, kOff8);
+    const float f1 = nib<0x007F8000u>(u << 7, magic, kOff8);
+    const float f2 = nib<0x007F8000u>(u >> 1, magic, kOff8);
+    const float f3 = nib<0x007F8000u>(u >> 9, magic, kOff8);
 #pragma unroll
     for (int m = 0; m < M; ++m) {
         T[m][at + 0] = fmaf(xv[m], f0, T[m][at + 0]);
@@ -294,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     };
-    // Group epilogue: y += scale * (T * 2^-p - (offset + zero) * rowSum); resets T and rs.
+    // Group epilogue: y += scale * (T * 2^-p - zero * rowSum); resets T and rs.
     auto finish_group = [&]() {
 #pragma unroll
         for (int j = 0; j < C; ++j) {
@@ -304,10 +308,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int jj = lo ? j : j - LB;
                 const uint32_t zb = (zw[(lo ? 0 : S::WORDS) + jj / 4] >> (8 * (jj % 4))) & 0xFFu;
                 pscale = lo ? 0x1p-16f : 0x1p-12f;
-                zoff = (lo ? 128.0f : 2048.0f) + static_cast<float>(zb);
+                zoff = static_cast<float>(zb);
             } else {
                 pscale = 0x1p-15f;
-                zoff = 384.0f;
+                zoff = 0.0f;
             }
 #pragma unroll
             for (int m = 0; m < M; ++m) y[m][j] = fmaf(sc[j], fmaf(T[m][j], pscale, -zoff * rs[m]), y[m][j]);

@@ -9,17 +9,19 @@
 // run on mma.sync.m16n8k16 (fp16 inputs, fp32 accumulate) and the CUDA cores
 // only turn nibbles into fp16 operands: 6 instructions per 256 weights.
 //
-// Exactness.  The A operand holds the raw nibbles as exact fp16 values: two
-// bytes of two rows are interleaved with PRMT and LOP3 masks each nibble into
-// the mantissa of 1024.0h (0x6400), giving 1024 + q (low nibble) and
-// 1024 + 16 q (high nibble).  The offsets are removed per group with the sum
-// of x.  The B operand holds x split into two fp16 terms, hi = fp16(x') and
-// lo = fp16(x' - hi), with x' = x * 2^s and 2^s a power of two per (slice,
-// token) that puts the slice's max|x| in [2^14, 2^15): a 22-bit significand,
-// exact products, fp32 accumulation.  Each group's accumulator C is then
+// Exactness.  The A operand holds the raw nibbles as exact fp16 values with
+// no offset: two bytes of two rows are interleaved with PRMT and one AND masks
+// each nibble into the low mantissa bits of a zero exponent, the fp16
+// subnormal q * 2^-24 (low nibble) or 16 q * 2^-24 (high nibble).  The B
+// operand holds x split into two fp16 terms, hi = fp16(x') and lo = fp16(x' -
+// hi), with x' = x * 2^s and 2^s a power of two per (slice, token) that puts
+// the slice's max|x| in [2^14, 2^15): a 22-bit significand, exact products,
+// fp32 accumulation of sum q x' alone.  (An earlier encoding OR-ed the nibble
+// into 1024.0h, exact as well, but then the accumulator carried 1024 sum x'
+// beside sum q x' and lost ~8 bits to it.)  Each group's accumulator C is
 // combined as in the reference (combineGroup, MatMul.kt:804-828):
-//     y[j] += scale[g,j] * (2^-s C - (1024 + zero[g,j]) * sum_l x_l)    (low)
-//     y[j] += scale[g,j] * (2^-s C / 16 - (64 + zero[g,j]) * sum_l x_l) (high)
+//     y[j] += scale[g,j] * (2^(24-s) C - zero[g,j] * sum_l x_l)      (low)
+//     y[j] += scale[g,j] * (2^(20-s) C - zero[g,j] * sum_l x_l)      (high)
 // with sum_l x_l the group's sum of (hi + lo) * 2^-s, i.e. of what the tensor
 // cores saw.
 //
@@ -112,7 +114,6 @@ struct MmaParams {
     const float* bias;
     int32_t* err;
     int32_t K, N, R, gs;
-    uint32_t h1024;        // 0x64006400: f16x2 {1024, 1024}
     float alpha;
     int32_t accumulate;
     LoraEpilogue lora;
@@ -179,12 +180,6 @@ __device__ __forceinline__ int atomic_add_acq_rel(int32_t* p, int v) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
-template <uint32_t MASK>
-__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t c) {
-    uint32_t d;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "n"(MASK), "r"(c));
-    return d;
-}
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t d;
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
@@ -200,10 +195,9 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4],
 
 // The 8 MMAs of one 16-row step from the four 8-byte row chunks w[0..3]
 // (rows 2t, 2t+1, 2t+8, 2t+9); MMA i = 4k + j <-> byte 4k + j of the chunk.
-// A holds {1024 + q} (low nibbles) and {1024 + 16 q} (high nibbles), exact in
-// fp16; the 1024 offset and the 16x are removed in the group epilogue.
-__device__ __forceinline__ void mma_step(float (&c)[8][4], const uint2 (&w)[4], uint32_t b0, uint32_t b1,
-                                         uint32_t h1024) {
+// A holds the fp16 subnormals q * 2^-24 (low nibbles) and 16 q * 2^-24 (high
+// nibbles); the 2^24 and the 16x are removed in the group epilogue.
+__device__ __forceinline__ void mma_step(float (&c)[8][4], const uint2 (&w)[4], uint32_t b0, uint32_t b1) {
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
         const uint32_t w0 = (&w[0].x)[k], w1 = (&w[1].x)[k], w2 = (&w[2].x)[k], w3 = (&w[3].x)[k];
@@ -213,10 +207,10 @@ __device__ __forceinline__ void mma_step(float (&c)[8][4], const uint2 (&w)[4], 
             const uint32_t p01 = prmt(w0, w1, sel);  // byte j of rows 2t and 2t+1 at bits 0-7 / 16-23
             const uint32_t p23 = prmt(w2, w3, sel);
             uint32_t a[4];
-            a[0] = lop3_and_or<0x000F000Fu>(p01, h1024);
-            a[1] = lop3_and_or<0x00F000F0u>(p01, h1024);
-            a[2] = lop3_and_or<0x000F000Fu>(p23, h1024);
-            a[3] = lop3_and_or<0x00F000F0u>(p23, h1024);
+            a[0] = p01 & 0x000F000Fu;
+            a[1] = p01 & 0x00F000F0u;
+            a[2] = p23 & 0x000F000Fu;
+            a[3] = p23 & 0x00F000F0u;
             mma_16816(c[4 * k + j], a, b0, b1);
         }
     }
@@ -410,7 +404,6 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int i = 0; i < 8; ++i) c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0.0f;
 
-    const uint32_t h1024 = p.h1024;
     float rs = 0.0f;  // this token's sum of x over the group's rows in this slice
     bool ok = true;
     int done = 0;     // stages whose copies this lane saw complete
@@ -456,15 +449,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
             for (int i = 0; i < 4; ++i)
                 w[i] = *reinterpret_cast<const uint2*>(stage + ks * kStep * kTileBytes + soff[i]);
-            mma_step(c, w, b0, b1, h1024);
+            mma_step(c, w, b0, b1);
         }
         __syncwarp();  // every lane of this warp has read the stage
         if (lane == 0) mbar_arrive(empty + 8 * slot);
         rs += chunk_sum[st * M + ttok];
         if (r_begin + (st + 1) * kRowsPerStage >= group_end) {
             // Group epilogue for token t:
-            //   low:  y += scale * (2^-s C - (1024 + zero) rowSum)
-            //   high: y += scale * (2^-s C / 16 - (64 + zero) rowSum)
+            //   low:  y += scale * (2^(24-s) C - zero rowSum)
+            //   high: y += scale * (2^(20-s) C - zero rowSum)
             // Columns beyond the tile's bytes hold stale slot data; their
             // outputs are never written.
             if (t_active) {
@@ -486,12 +479,12 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const float* s_hi = reinterpret_cast<const float*>(sl + kTileBytes * 4) + 8 * gb + i0;
                 const uint8_t* z_lo = sl + kTileBytes * 8 + 8 * gb + i0;
                 const uint8_t* z_hi = sl + kTileBytes * 9 + 8 * gb + i0;
-                const float un16 = un_t * 0.0625f;
+                const float un_lo = un_t * 16777216.0f, un_hi = un_t * 1048576.0f;  // 2^24, 2^20 (exact)
 #pragma unroll
                 for (int e = 0; e < kNB; ++e) {
                     const float zlf = static_cast<float>(z_lo[e]), zhf = static_cast<float>(z_hi[e]);
-                    y[e] = fmaf(s_lo[e], fmaf(cs[e][0] + cs[e][1], un_t, -(1024.0f + zlf) * rs), y[e]);
-                    y[kNB + e] = fmaf(s_hi[e], fmaf(cs[e][2] + cs[e][3], un16, -(64.0f + zhf) * rs), y[kNB + e]);
+                    y[e] = fmaf(s_lo[e], fmaf(cs[e][0] + cs[e][1], un_lo, -zlf * rs), y[e]);
+                    y[kNB + e] = fmaf(s_hi[e], fmaf(cs[e][2] + cs[e][3], un_hi, -zhf * rs), y[kNB + e]);
                 }
             }
 #pragma unroll
@@ -699,7 +692,6 @@ cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, c
     p.N = w.columns;
     p.R = w.bytes_per_row;
     p.gs = w.group_size;
-    p.h1024 = 0x64006400u;
     p.alpha = a.alpha;
     p.accumulate = a.accumulate;
     p.lora = a.lora;
