@@ -345,39 +345,6 @@ kt_status kt_rmsnorm_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* x_de
 kt_status kt_rmsnorm_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* x_dev,
                                     const float* norm_weight_dev, float eps, float* xn_dev, float* gu_dev,
                                     float* act_dev, int32_t m, const float* bias_dev, void* stream);
-
-/* A chain of one-token products in one launch: the consecutive projections of
- * a decode step (TransformerBlock.decodeInto, TransformerBlock.kt:40-47: an
- * FFN's gate | up product and its down product fed the SwiGLU of the first),
- * each MatMul.multiplyQuantized (MatMul.kt:460-536) at m = 1:
- *   step i:  c_i[N] = (accumulate ? c_i : 0) + alpha * x_i . dequant(W_i) + bias
- * with x_i = a_dev, or the output of an earlier step (input_step >= 0, a_dev
- * ignored), optionally RMSNorm'd first (norm_weight_dev, as kt_rmsnorm_qmatmul)
- * and with SwiGLU's silu(gate) * up formed in the epilogue (swiglu = 1, a gate |
- * up weight, c_i [N / 2], as kt_qmatmul_swiglu).  The arithmetic of each step
- * is that of the m = 1 integer tensor-core GEMV; the launch is persistent, one
- * or two CTAs per SM walking the steps in order, so the weights of step i + 1
- * stream in while step i finishes and step i + 1 waits for its input.
- * Weights the m = 1 GEMV takes (INT4 / INT8, K a multiple of 32), at most
- * kt_chain_max_steps() steps, each with at most as many column tiles (256
- * columns INT4, 128 INT8) as the GPU holds CTAs of the kernel; otherwise
- * KT_ERR_UNSUPPORTED and nothing runs (run the steps one by one).  Replaces a
- * sequence of kt_qmatmul / kt_rmsnorm_qmatmul / kt_rmsnorm_qmatmul_swiglu calls
- * on one stream, within the same fp32 tolerance. */
-typedef struct kt_chain_step {
-    const kt_qweight* weight;
-    const float* a_dev;           /* [K]; ignored when input_step >= 0 */
-    int32_t input_step;           /* -1, or the earlier step whose output is this step's input */
-    float* c_dev;                 /* [N] ([N / 2] with swiglu) */
-    int32_t accumulate;
-    float alpha;
-    const float* bias_dev;        /* [N] or NULL */
-    const float* norm_weight_dev; /* [K] RMSNorm weight, 16-byte aligned, or NULL */
-    float norm_eps;
-    int32_t swiglu;
-} kt_chain_step;
-int32_t kt_chain_max_steps(void);
-kt_status kt_qmatmul_chain(kt_ctx* ctx, const kt_chain_step* steps, int32_t n_steps, void* stream);
 /* One decode token per sequence, the middle of Attention.decodeInto
  * (Attention.kt:207-239) in one launch: for fused q|k|v rows (row r = sequence
  * r, whose caches start cache_stride floats after the previous sequence's, at

@@ -56,14 +56,6 @@ class KtInfo(ctypes.Structure):
     ]
 
 
-class ChainStep(ctypes.Structure):
-    """kt_chain_step (include/kt_cuda.h)."""
-    _fields_ = [("weight", ctypes.c_void_p), ("a_dev", ctypes.c_void_p), ("input_step", ctypes.c_int32),
-                ("c_dev", ctypes.c_void_p), ("accumulate", ctypes.c_int32), ("alpha", ctypes.c_float),
-                ("bias_dev", ctypes.c_void_p), ("norm_weight_dev", ctypes.c_void_p), ("norm_eps", ctypes.c_float),
-                ("swiglu", ctypes.c_int32)]
-
-
 # name -> (argtypes, restype); the single source of the Python-side signatures.
 P, I32, I64, F32, SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 PP = ctypes.POINTER(ctypes.c_void_p)
@@ -120,8 +112,6 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_qmatmul_swiglu": ([P, P, P, P, P, I32, F32, P, P], I32),
     "kt_rmsnorm_qmatmul": ([P, P, P, P, F32, P, P, I32, I32, P, P], I32),
     "kt_rmsnorm_qmatmul_swiglu": ([P, P, P, P, F32, P, P, P, I32, P, P], I32),
-    "kt_chain_max_steps": ([], I32),
-    "kt_qmatmul_chain": ([P, P, I32, P], I32),
     "kt_attention_rope_decode": ([P, P, I32, I32, I32, I32, I32, P, P, P, P, P, I32, I32, F32, P, I64, P], I32),
     "kt_silu_mul": ([P, P, P, I64, P], I32),
     "kt_add": ([P, P, P, I64, P], I32),

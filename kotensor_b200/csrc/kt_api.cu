@@ -1087,46 +1087,6 @@ kt_status kt_rmsnorm_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const floa
     return rmsnorm_matmul(ctx, w, x, norm_w, eps, xn, gu, act, m, 0, bias, true, stream);
 }
 
-int32_t kt_chain_max_steps(void) { return kChainMaxSteps; }
-
-kt_status kt_qmatmul_chain(kt_ctx* ctx, const kt_chain_step* steps, int32_t n_steps, void* stream) {
-    if (!ctx || !steps) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
-    if (n_steps < 1 || n_steps > kChainMaxSteps)
-        return fail(KT_ERR_INVALID_ARGUMENT, "a chain has 1.." + std::to_string(kChainMaxSteps) + " steps, got " +
-                                                 std::to_string(n_steps));
-    ChainStep cs[kChainMaxSteps];
-    for (int32_t i = 0; i < n_steps; ++i) {
-        const kt_chain_step& st = steps[i];
-        const std::string at = "chain step " + std::to_string(i) + ": ";
-        if (!st.weight || !st.c_dev) return fail(KT_ERR_INVALID_ARGUMENT, at + "NULL argument");
-        if (st.input_step >= i || st.input_step < -1)
-            return fail(KT_ERR_INVALID_ARGUMENT, at + "input_step must name an earlier step or be -1");
-        const QView v = view(st.weight);
-        const float* a = st.input_step >= 0 ? steps[st.input_step].c_dev : st.a_dev;
-        if (!a) return fail(KT_ERR_INVALID_ARGUMENT, at + "NULL argument");
-        if (st.swiglu && st.accumulate) return fail(KT_ERR_INVALID_ARGUMENT, at + "SwiGLU does not accumulate");
-        if (st.input_step >= 0) {
-            const kt_chain_step& in = steps[st.input_step];
-            const int32_t width = in.swiglu ? in.weight->columns / 2 : in.weight->columns;
-            if (width != st.weight->rows)
-                return fail(KT_ERR_INVALID_ARGUMENT, at + "input width " + std::to_string(width) +
-                                                         " != in-features " + std::to_string(st.weight->rows));
-        }
-        if (st.norm_weight_dev && reinterpret_cast<uintptr_t>(st.norm_weight_dev) % 16 != 0)
-            return fail(KT_ERR_INVALID_ARGUMENT, at + "norm_weight_dev must be 16-byte aligned");
-        if (!gemv_chain_step_supported(v, a, st.swiglu != 0, ctx->sm_count))
-            return fail(KT_ERR_UNSUPPORTED, at + "this weight does not run in a chain (run the steps one by one)");
-        cs[i] = ChainStep{v, a, st.input_step, st.c_dev, st.accumulate, st.alpha, st.bias_dev, st.norm_weight_dev,
-                          st.norm_eps, st.swiglu};
-    }
-    const cudaStream_t s = pick(ctx, stream);
-    const size_t need = gemv_chain_workspace_bytes(cs, n_steps, ctx->sm_count);
-    void* ws = nullptr;
-    KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "chain workspace");
-    KT_CUDA_TRY(launch_gemv_chain(cs, n_steps, ctx->sm_count, s, ws, need, ctx->d_error), "chain launch");
-    return KT_OK;
-}
-
 kt_status kt_attention_rope_decode(kt_ctx* ctx, const float* qkv, int32_t rows, int32_t q_width, int32_t heads,
                                    int32_t kv_heads, int32_t head_dim, const float* inv_freq, float* k_cache,
                                    float* v_cache, float* context, float* scratch, int32_t max_seq, int32_t layer,

@@ -120,16 +120,12 @@ kt_status run_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c
 // counters of the INT4 GEMV and of the INT4 GEMM at fixed offsets (zero
 // between launches, whatever shapes ran before); kernels use the rest freely.
 cudaError_t stream_workspace(kt_ctx* ctx, cudaStream_t s, size_t bytes, void** out);
-constexpr size_t kWorkspaceReservedBytes = static_cast<size_t>(112) << 10;
+constexpr size_t kWorkspaceReservedBytes = static_cast<size_t>(96) << 10;
 constexpr size_t kGemvTicketOffset = 0;
 constexpr size_t kGemmTicketOffset = static_cast<size_t>(32) << 10;
 constexpr size_t kLoraTicketOffset = static_cast<size_t>(64) << 10;
-constexpr size_t kChainCounterOffset = static_cast<size_t>(96) << 10;
 constexpr int kTicketCapEach = 8192;  // counters per kernel family
-// The GEMV chain (kt_gemv_chain.cu): per step a finished-tile counter, the
-// grid's exit counter, then the split-K tickets of every step.
-constexpr int kChainMaxSteps = 8;
-constexpr int kChainTicketCap = (16 << 10) / 4 - kChainMaxSteps - 1;
+
 
 // A 2-D tiled TMA descriptor (kt_api.cu): `inner` x `outer` elements of
 // `elem_bytes`, rows `row_bytes` apart, box `box_inner` x `box_outer`.
@@ -239,24 +235,6 @@ size_t gemv_imma_workspace_bytes(const QView& w, int sm_count, bool no_cluster =
 bool gemv_imma_tp_supported(const QView& w, int sm_count);
 cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s, void* workspace,
                              size_t workspace_bytes);
-// A chain of m = 1 GEMVs in one persistent launch (kt_gemv_chain.cu): step i
-// reads `a` (input = -1) or the output of an earlier step `input`.
-struct ChainStep {
-    QView w;
-    const float* a;
-    int32_t input;
-    float* c;
-    int32_t accumulate;
-    float alpha;
-    const float* bias;
-    const float* norm_weight;
-    float norm_eps;
-    int32_t swiglu;
-};
-bool gemv_chain_step_supported(const QView& w, const float* a, bool swiglu, int sm_count);
-size_t gemv_chain_workspace_bytes(const ChainStep* steps, int n, int sm_count);
-cudaError_t launch_gemv_chain(const ChainStep* steps, int n, int sm_count, cudaStream_t s, void* workspace,
-                              size_t workspace_bytes, int32_t* err);
 
 
 // ---- kt_gemm_tc.cu  (INT4, m >= 9: bf16 tcgen05 MMAs, TMEM accumulators)

@@ -348,43 +348,6 @@ class MatMul:
             _lib.check(st)
 
     @staticmethod
-    def multiply_chain(steps) -> None:
-        """kt_qmatmul_chain: consecutive one-token products in one launch (CUDA
-        tensors, torch's current stream).  Each step is a dict with ``weight``,
-        ``c`` and either ``a`` (a [K] tensor) or ``input`` (the index of an
-        earlier step whose ``c`` is this step's input), and optionally
-        ``accumulate`` (False), ``alpha`` (1.0), ``bias``, ``norm_weight`` /
-        ``norm_eps`` (RMSNorm of the input first) and ``swiglu`` (False).
-        Raises KtError (KT_ERR_UNSUPPORTED) for weights the chain does not take."""
-        n = len(steps)
-        arr = (_lib.ChainStep * max(1, n))()
-        keep = []
-        for i, st in enumerate(steps):
-            w = st["weight"]
-            inp = int(st.get("input", -1))
-            a = st.get("a")
-            if inp < 0:
-                _require_f32_device(f"steps[{i}].a", a)
-            _require_f32_device(f"steps[{i}].c", st["c"])
-            for key in ("bias", "norm_weight"):
-                if st.get(key) is not None:
-                    _require_f32_device(f"steps[{i}].{key}", st[key])
-            keep.append(w)
-            arr[i].weight = w.handle
-            arr[i].a_dev = a.data_ptr() if inp < 0 else None
-            arr[i].input_step = inp
-            arr[i].c_dev = st["c"].data_ptr()
-            arr[i].accumulate = int(bool(st.get("accumulate", False)))
-            arr[i].alpha = float(st.get("alpha", 1.0))
-            arr[i].bias_dev = st["bias"].data_ptr() if st.get("bias") is not None else None
-            arr[i].norm_weight_dev = st["norm_weight"].data_ptr() if st.get("norm_weight") is not None else None
-            arr[i].norm_eps = float(st.get("norm_eps", 0.0))
-            arr[i].swiglu = int(bool(st.get("swiglu", False)))
-        ctx = steps[0]["weight"]._ctx if n else Context.get()
-        _lib.check(_lib.load().kt_qmatmul_chain(ctx.handle, ctypes.cast(arr, ctypes.c_void_p), n,
-                                                _stream_of(steps[0]["c"]) if n else None))
-
-    @staticmethod
     def multiply_by_quantized_transposed(dy, weight: QuantizedTensor, dx, m: int, accumulate: bool = True) -> None:
         """dx[m x K] = (accumulate ? dx : 0) + dy[m x N] . dequant(W)^T (device tensors)."""
         k, n = weight.rows, weight.columns
