@@ -1100,7 +1100,7 @@ kt_status kt_attention_rope_decode(kt_ctx* ctx, const float* qkv, int32_t rows, 
                     "fused decode attention needs heads / kv_heads <= 8, head_dim 64 or 128 and max_seq <= 16384");
     KT_CUDA_TRY(launch_attention_decode_fused(qkv, rows, q_width, heads, kv_heads, head_dim, inv_freq, k_cache,
                                               v_cache, context, scratch, max_seq, layer, scale, position_dev,
-                                              cache_stride, pick(ctx, stream)),
+                                              cache_stride, ctx->d_error, pick(ctx, stream)),
                 "fused attention launch");
     return KT_OK;
 }

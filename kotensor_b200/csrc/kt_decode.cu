@@ -1056,6 +1056,264 @@ __global__ void __launch_bounds__(kThreads) attention_decode_fused_wide_kernel(
     }
 }
 
+// The fused decode step of attention_decode_fused_kernel (RoPE of the query
+// heads, the current key / value into the cache, the split partials, the
+// last block's merge) with the split's key and value rows staged in shared
+// memory by bulk copies, as attention_group_staged_kernel: the copies of the
+// cached rows start before anything else; the block holding the current
+// position writes that row into the cache and into its staged tile itself.
+// Waits on the copies are bounded (error word, drain, return).
+template <int G, int HD>
+__global__ void __launch_bounds__(kThreads) attention_decode_staged_kernel(
+    const float* __restrict__ qkv, int q_width, const float* __restrict__ inv_freq, float* __restrict__ kc,
+    float* __restrict__ vc, float* __restrict__ scratch, int32_t* __restrict__ tickets, float* __restrict__ ctx,
+    int heads, int kv_heads, int max_seq, int layer, float scale, const int32_t* __restrict__ pos,
+    int64_t cache_stride, int32_t* __restrict__ err) {
+    using S = StagedAttention<HD>;
+    constexpr int kWarps = kThreads / 32;
+    static_assert(G <= kWarps && G * HD <= kSpan * S::kPad / kWarps, "one warp per head; partials fit the key area");
+    static_assert(G * kMaxFusedSplits + G <= kSpan * S::kPad, "merge factors fit the key area");
+    extern __shared__ __align__(16) float sm[];
+    float* ks = sm;                         // [kSpan][kPad]
+    float* vs = ks + kSpan * S::kPad;       // [kSpan][HD]
+    float* qs = vs + kSpan * HD;            // [G][HD] rotated query heads
+    float* sp = qs + G * HD;                // [4][G][kSpan] score quarters
+    float* pw = sp + 4 * G * kSpan;         // [kSpan][G] exp(score - max)
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ float stat[G][2];
+    __shared__ int s_last;
+    dev::pdl_wait();  // qkv comes from the previous kernel; the cache rows from earlier steps
+    dev::pdl_launch_dependents();
+    const int kvh = blockIdx.x, split = blockIdx.y, t = blockIdx.z;
+    const int p = *pos;
+    const int j0 = split * kSpan;
+    const int j1 = min(j0 + kSpan, p + 1);
+    if (j0 >= j1) return;  // past the current position
+    const int n = j1 - j0;
+    const bool holds_current = j1 == p + 1;
+    const int n_old = holds_current ? n - 1 : n;  // rows already in the cache
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t base = t * cache_stride + ((static_cast<int64_t>(layer) * kv_heads + kvh) * max_seq + j0) * HD;
+    const uint32_t bar_k = dev::smem_u32(&bars[0]), bar_v = dev::smem_u32(&bars[1]);
+    if (threadIdx.x == 0) {
+        dev::mbar_init(bar_k, 1);
+        dev::mbar_init(bar_v, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t bytes = static_cast<uint32_t>(n_old * HD * sizeof(float));
+        if (lane == 0) {
+            dev::mbar_expect_tx(bar_k, bytes);
+            dev::mbar_expect_tx(bar_v, bytes);
+            if (n_old > 0) dev::bulk_load(dev::smem_u32(vs), vc + base, bytes, bar_v);
+        }
+        __syncwarp();
+        for (int j = lane; j < n_old; j += 32)
+            dev::bulk_load(dev::smem_u32(ks + j * S::kPad), kc + base + static_cast<int64_t>(j) * HD,
+                           HD * sizeof(float), bar_k);
+    }
+    constexpr int half = HD / 2;
+    const int kv_width = kv_heads * HD;
+    const float* row = qkv + static_cast<int64_t>(t) * (q_width + 2 * kv_width);
+    // RoPE of element d of a head vector v at position p (the rope kernel's arithmetic)
+    auto rotated = [&](const float* v, int d) {
+        const int i = d < half ? d : d - half;
+        float s1, c1;
+        sincosf(static_cast<float>(p) * __ldg(inv_freq + i), &s1, &c1);
+        const float x1 = v[i], x2 = v[i + half];
+        return d < half ? x1 * c1 - x2 * s1 : x1 * s1 + x2 * c1;
+    };
+    if (holds_current) {  // this step's key and value: into the cache and the staged tile
+        const float* kr = row + q_width + kvh * HD;
+        const float* vr = row + q_width + kv_width + kvh * HD;
+        const int64_t off = base + static_cast<int64_t>(n - 1) * HD;
+        for (int d = threadIdx.x; d < HD; d += kThreads) {
+            const float kd = rotated(kr, d), vd = vr[d];
+            kc[off + d] = kd;
+            vc[off + d] = vd;
+            ks[(n - 1) * S::kPad + d] = kd;
+            vs[(n - 1) * HD + d] = vd;
+        }
+    }
+    for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
+        const int g = idx / HD, d = idx - g * HD;
+        qs[idx] = rotated(row + static_cast<int64_t>(kvh * G + g) * HD, d);
+    }
+    bool ok = dev::mbar_wait_bounded(bar_k, 0);
+    if (__syncthreads_or(!ok)) {  // also publishes qs and the current row
+        if (threadIdx.x == 0) {
+            atomicOr(err, 1);
+            dev::mbar_wait_bounded(bar_k, 0);
+            dev::mbar_wait_bounded(bar_v, 0);
+        }
+        return;
+    }
+    {   // score quarters: lane -> position, warp -> (half of the positions, quarter of the dims)
+        const int j = (warp & 1) * 32 + lane, dq = warp >> 1;
+        float acc[G][4];
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[g][e] = 0.0f;
+        if (j < n) {
+            const float* kr = ks + j * S::kPad + dq * S::kQuarter;
+            const float* qq = qs + dq * S::kQuarter;
+#pragma unroll
+            for (int c = 0; c < S::kQuarter; c += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(qq + g * HD + c);
+                    acc[g][0] = fmaf(q4.x, k4.x, acc[g][0]);
+                    acc[g][1] = fmaf(q4.y, k4.y, acc[g][1]);
+                    acc[g][2] = fmaf(q4.z, k4.z, acc[g][2]);
+                    acc[g][3] = fmaf(q4.w, k4.w, acc[g][3]);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                sp[(dq * G + g) * kSpan + j] = (acc[g][0] + acc[g][1]) + (acc[g][2] + acc[g][3]);
+        }
+    }
+    __syncthreads();
+    if (warp < G) {  // head `warp`: max and sum of exponentials over this split
+        const int g = warp;
+        auto score = [&](int j) {
+            return (((sp[(0 * G + g) * kSpan + j] + sp[(1 * G + g) * kSpan + j]) + sp[(2 * G + g) * kSpan + j]) +
+                    sp[(3 * G + g) * kSpan + j]) * scale;
+        };
+        const float s0 = lane < n ? score(lane) : -FLT_MAX;
+        const float s1 = lane + 32 < n ? score(lane + 32) : -FLT_MAX;
+        float mx = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float e0 = lane < n ? expf(s0 - mx) : 0.0f;
+        const float e1 = lane + 32 < n ? expf(s1 - mx) : 0.0f;
+        pw[lane * G + g] = e0;
+        pw[(lane + 32) * G + g] = e1;
+        float sum = e0 + e1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            stat[g][0] = mx;
+            stat[g][1] = sum;
+        }
+    }
+    ok = dev::mbar_wait_bounded(bar_v, 0);
+    if (__syncthreads_or(!ok)) {  // also publishes pw and stat
+        if (threadIdx.x == 0) {
+            atomicOr(err, 1);
+            dev::mbar_wait_bounded(bar_v, 0);
+        }
+        return;
+    }
+    constexpr int kDims = HD / 32;  // per lane: 2 or 4 consecutive dims
+    float acc[G][kDims];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < kDims; ++i) acc[g][i] = 0.0f;
+    for (int j = warp; j < n; j += kWarps) {
+        float v[kDims];
+        if constexpr (kDims == 4) {
+            const float4 v4 = *reinterpret_cast<const float4*>(vs + j * HD + 4 * lane);
+            v[0] = v4.x, v[1] = v4.y, v[2] = v4.z, v[3] = v4.w;
+        } else {
+            const float2 v2 = *reinterpret_cast<const float2*>(vs + j * HD + 2 * lane);
+            v[0] = v2.x, v[1] = v2.y;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float w = pw[j * G + g];
+#pragma unroll
+            for (int i = 0; i < kDims; ++i) acc[g][i] = fmaf(w, v[i], acc[g][i]);
+        }
+    }
+    float* part = ks;  // [kWarps][G][HD]; the key rows are no longer read
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < kDims; ++i) part[(warp * G + g) * HD + kDims * lane + i] = acc[g][i];
+    __syncthreads();
+    const int64_t splits = (max_seq + kSpan - 1) / kSpan;
+    for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
+        const int g = idx / HD, d = idx - g * HD;
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) v += part[(w * G + g) * HD + d];
+        float* out = scratch + ((static_cast<int64_t>(t) * heads + kvh * G + g) * splits + split) * (HD + 2);
+        out[2 + d] = v;
+        if (d == 0) {
+            out[0] = stat[g][0];
+            out[1] = stat[g][1];
+        }
+    }
+    // the last of the row's active splits to arrive merges them (the barrier
+    // orders every thread's partial stores before thread 0's acq_rel ticket)
+    const int active = p / kSpan + 1;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int32_t* ticket = tickets + static_cast<int64_t>(t) * kv_heads + kvh;
+        s_last = active == 1 || dev::atomic_add_acq_rel(ticket, 1) == active - 1;
+        if (s_last && active > 1) *ticket = 0;  // every split has arrived: ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    // merge (attention_decode_fused_kernel's): split factors in the key area
+    constexpr int stride = HD + 2;
+    float* coef = ks;                         // [G][kMaxFusedSplits]
+    float* inv_l = ks + G * kMaxFusedSplits;  // [G]
+    if (warp < G) {
+        const float* hb = scratch + (static_cast<int64_t>(t) * heads + kvh * G + warp) * splits * stride;
+        float m = -1e9f;
+        for (int s2 = lane; s2 < active; s2 += 32) m = fmaxf(m, __ldcg(hb + s2 * stride));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int s2 = lane; s2 < active; s2 += 32) {
+            const float e = expf(__ldcg(hb + s2 * stride) - m);
+            coef[warp * kMaxFusedSplits + s2] = e;
+            l = fmaf(__ldcg(hb + s2 * stride + 1), e, l);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) inv_l[warp] = 1.0f / l;
+    }
+    __syncthreads();
+    constexpr int kOuts = (G * HD + kThreads - 1) / kThreads;  // outputs per thread
+    float vsum[kOuts];
+#pragma unroll
+    for (int o2 = 0; o2 < kOuts; ++o2) vsum[o2] = 0.0f;
+    for (int s0 = 0; s0 < active; s0 += 8) {
+        float u[kOuts][8];
+#pragma unroll
+        for (int o2 = 0; o2 < kOuts; ++o2) {
+            const int idx = threadIdx.x + kThreads * o2;
+            const int g = idx / HD, d = idx - g * HD;
+            const float* hv = scratch + (static_cast<int64_t>(t) * heads + kvh * G + g) * splits * stride + 2 + d;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                u[o2][j] = idx < G * HD && s0 + j < active ? __ldcg(hv + (s0 + j) * stride) : 0.0f;
+        }
+#pragma unroll
+        for (int o2 = 0; o2 < kOuts; ++o2) {
+            const int g = min((threadIdx.x + kThreads * o2) / HD, G - 1);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (s0 + j < active) vsum[o2] = fmaf(u[o2][j], coef[g * kMaxFusedSplits + s0 + j], vsum[o2]);
+        }
+    }
+#pragma unroll
+    for (int o2 = 0; o2 < kOuts; ++o2) {
+        const int idx = threadIdx.x + kThreads * o2;
+        if (idx < G * HD) {
+            const int g = idx / HD, d = idx - g * HD;
+            ctx[(static_cast<int64_t>(t) * heads + kvh * G + g) * HD + d] = vsum[o2] * inv_l[g];
+        }
+    }
+}
+
 __global__ void attention_merge_kernel(const float* __restrict__ scratch, float* __restrict__ ctx, int heads,
                                        int head_dim, int max_seq, const int32_t* __restrict__ pos, int rows_per_seq) {
     dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
@@ -1245,16 +1503,70 @@ bool attention_fused_supported(int heads, int kv_heads, int head_dim, int max_se
            (max_seq + kSpan - 1) / kSpan <= kMaxFusedSplits;
 }
 
+bool staged_attention_enabled();
+
+// Dynamic shared memory of every staged fused-decode instantiation (once per device).
+template <int HD>
+cudaError_t prepare_staged_decode() {
+    constexpr int kMaxDevices = 64;
+    static std::atomic<bool> done[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+#define KT_STAGED_ATTR(G_)                                                                                     \
+    if (e == cudaSuccess)                                                                                      \
+        e = cudaFuncSetAttribute(attention_decode_staged_kernel<G_, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 static_cast<int>(StagedAttention<HD>::template smem_bytes<G_>()));
+    KT_STAGED_ATTR(1) KT_STAGED_ATTR(2) KT_STAGED_ATTR(3) KT_STAGED_ATTR(4)
+    KT_STAGED_ATTR(5) KT_STAGED_ATTR(6) KT_STAGED_ATTR(7) KT_STAGED_ATTR(8)
+#undef KT_STAGED_ATTR
+    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) done[dev].store(true, std::memory_order_release);
+    return e;
+}
+
 cudaError_t launch_attention_decode_fused(const float* qkv, int rows, int q_width, int heads, int kv_heads,
                                           int head_dim, const float* inv_freq, float* kc, float* vc, float* ctx,
                                           float* scratch, int max_seq, int layer, float scale, const int32_t* pos,
-                                          int64_t cache_stride, cudaStream_t s) {
+                                          int64_t cache_stride, int32_t* err, cudaStream_t s) {
     if (!attention_fused_supported(heads, kv_heads, head_dim, max_seq)) return cudaErrorInvalidValue;
     const int splits = (max_seq + kSpan - 1) / kSpan;
     int32_t* tickets = reinterpret_cast<int32_t*>(
         scratch + static_cast<size_t>(rows) * heads * splits * (head_dim + 2));
     const dim3 grid(kv_heads, splits, rows);
     const int group = heads / kv_heads;
+    // staged: the cache rows on 16-byte boundaries (bulk copies); measured faster
+    // than the register-loading kernels at head_dim 128 and with several rows, and
+    // a little slower at head_dim 64 on one row (where a step's tiles are small)
+    const bool aligned = (reinterpret_cast<uintptr_t>(kc) & 15) == 0 && (reinterpret_cast<uintptr_t>(vc) & 15) == 0 &&
+                         cache_stride % 4 == 0;
+    if (staged_attention_enabled() && aligned && (head_dim == 128 || rows > 1)) {
+#define KT_SFUSED_CASE(G_, HD_)                                                                                  \
+    e = launch_pdl(attention_decode_staged_kernel<G_, HD_>, grid, dim3(kThreads),                               \
+                   StagedAttention<HD_>::template smem_bytes<G_>(), s, qkv, q_width, inv_freq, kc, vc, scratch, \
+                   tickets, ctx, heads, kv_heads, max_seq, layer, scale, pos, cache_stride, err)
+#define KT_SFUSED_GROUPS(HD_)                    \
+    switch (group) {                             \
+        case 1: KT_SFUSED_CASE(1, HD_); break;   \
+        case 2: KT_SFUSED_CASE(2, HD_); break;   \
+        case 3: KT_SFUSED_CASE(3, HD_); break;   \
+        case 4: KT_SFUSED_CASE(4, HD_); break;   \
+        case 5: KT_SFUSED_CASE(5, HD_); break;   \
+        case 6: KT_SFUSED_CASE(6, HD_); break;   \
+        case 7: KT_SFUSED_CASE(7, HD_); break;   \
+        default: KT_SFUSED_CASE(8, HD_); break;  \
+    }
+        cudaError_t e = head_dim == 64 ? prepare_staged_decode<64>() : prepare_staged_decode<128>();
+        if (e != cudaSuccess) return e;
+        if (head_dim == 64) {
+            KT_SFUSED_GROUPS(64)
+        } else {
+            KT_SFUSED_GROUPS(128)
+        }
+#undef KT_SFUSED_GROUPS
+#undef KT_SFUSED_CASE
+        return e;
+    }
 #define KT_FUSED_CASE(G_, KP_)                                                                                  \
     launch_pdl(attention_decode_fused_kernel<G_, KP_>, grid, dim3(kThreads), 0, s, qkv, q_width, inv_freq, kc, vc, \
                scratch, tickets, ctx, heads, kv_heads, head_dim, max_seq, layer, scale, pos, cache_stride)

@@ -272,7 +272,7 @@ bool attention_fused_supported(int heads, int kv_heads, int head_dim, int max_se
 cudaError_t launch_attention_decode_fused(const float* qkv, int rows, int q_width, int heads, int kv_heads,
                                           int head_dim, const float* inv_freq, float* kc, float* vc, float* ctx,
                                           float* scratch, int max_seq, int layer, float scale, const int32_t* pos,
-                                          int64_t cache_stride, cudaStream_t s);
+                                          int64_t cache_stride, int32_t* err, cudaStream_t s);
 cudaError_t launch_silu_mul_rows(const float* gu, float* out, int rows, int hidden, cudaStream_t s);
 cudaError_t launch_rope(float* v, int rows, int width, int head_dim, const float* inv_freq, const int32_t* pos,
                         cudaStream_t s);
