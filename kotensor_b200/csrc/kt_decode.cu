@@ -1314,6 +1314,205 @@ __global__ void __launch_bounds__(kThreads) attention_decode_staged_kernel(
     }
 }
 
+// Causal attention for a prompt (rows_per_seq > 1), the partials of
+// attention_partial_kernel for a tile of query rows at once: one block per (kv
+// head, split of 64 positions, tile of 64 / G rows of one sequence), so the
+// split's key and value rows -- staged in shared memory by bulk copies with the
+// tile's query rows -- are read once per tile instead of once per row.  Scores:
+// thread (tq, tj) forms the 4 x 4 products of query vectors tq + 16a (vector
+// r G + g: row r, head g of the group) and positions tj + 16b, one fp32 chain
+// over the head dims; a position past a row's own (causal) is masked out.  Warp
+// w takes the softmax statistics of query vectors 8w .. 8w + 7; then thread
+// (tq, td) sums the weighted value rows for its four query vectors and HD / 16
+// dims.  A row with no position in this split writes nothing (the merge reads
+// only the splits up to each row's position).  Waits on the copies are bounded.
+template <int G, int HD>
+struct PrefillAttention {
+    static constexpr int QT = 64 / G;     // query rows per block
+    static constexpr int QV = QT * G;     // query vectors per block (<= 64)
+    static constexpr int kPad = HD + 4;   // floats between staged key rows
+    static constexpr int kPp = kSpan + 4; // floats between rows of exp(score - max)
+    static constexpr int kQArea = 64 * HD > 64 * kPp ? 64 * HD : 64 * kPp;
+    __host__ __device__ static constexpr size_t smem_bytes() {
+        return sizeof(float) * (static_cast<size_t>(kSpan) * kPad + kSpan * HD + kQArea);
+    }
+};
+
+template <int G, int HD>
+__global__ void __launch_bounds__(kThreads) attention_prefill_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    float* __restrict__ scratch, int heads, int kv_heads, int max_seq, int layer, float scale, int q_stride,
+    const int32_t* __restrict__ pos, int rows_per_seq, int64_t cache_stride, int32_t* __restrict__ err) {
+    using S = PrefillAttention<G, HD>;
+    constexpr int QT = S::QT, QV = S::QV;
+    static_assert(kThreads == 256 && QV <= 64, "16 x 16 threads over 64 query vectors x 64 positions");
+    extern __shared__ __align__(16) float sm[];
+    float* ks = sm;                         // [kSpan][kPad]
+    float* vs = ks + kSpan * S::kPad;       // [kSpan][HD]
+    float* qs = vs + kSpan * HD;            // [QV][HD], then ps [64][kPp]
+    float* ps = qs;
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ float stat[64][2];
+    dev::pdl_wait();  // q and the cache rows come from the previous kernels
+    dev::pdl_launch_dependents();
+    const int kvh = blockIdx.x, split = blockIdx.y, tile = blockIdx.z;
+    const int tiles_per_seq = (rows_per_seq + QT - 1) / QT;
+    const int seq = tile / tiles_per_seq;
+    const int r0 = (tile - seq * tiles_per_seq) * QT;  // first row of the tile inside its sequence
+    const int nr = min(QT, rows_per_seq - r0);
+    const int p0 = *pos;
+    const int j0 = split * kSpan;
+    const int last = p0 + r0 + nr - 1;  // the position of the tile's last row
+    if (j0 > last) return;              // no row of the tile sees this split
+    const int n = min(kSpan, last + 1 - j0);
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int64_t base = seq * cache_stride + ((static_cast<int64_t>(layer) * kv_heads + kvh) * max_seq + j0) * HD;
+    const int64_t row0 = static_cast<int64_t>(seq) * rows_per_seq + r0;  // global row of the tile's first row
+    const uint32_t bar_kq = dev::smem_u32(&bars[0]), bar_v = dev::smem_u32(&bars[1]);
+    if (tid == 0) {
+        dev::mbar_init(bar_kq, 1);
+        dev::mbar_init(bar_v, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t kv_bytes = static_cast<uint32_t>(n * HD * sizeof(float));
+        constexpr uint32_t q_row_bytes = G * HD * sizeof(float);
+        if (lane == 0) {
+            dev::mbar_expect_tx(bar_kq, kv_bytes + nr * q_row_bytes);
+            dev::mbar_expect_tx(bar_v, kv_bytes);
+            dev::bulk_load(dev::smem_u32(vs), vc + base, kv_bytes, bar_v);
+        }
+        __syncwarp();
+        for (int j = lane; j < n; j += 32)
+            dev::bulk_load(dev::smem_u32(ks + j * S::kPad), kc + base + static_cast<int64_t>(j) * HD,
+                           HD * sizeof(float), bar_kq);
+        for (int r = lane; r < nr; r += 32)
+            dev::bulk_load(dev::smem_u32(qs + r * G * HD),
+                           q + (row0 + r) * q_stride + static_cast<int64_t>(kvh) * G * HD, q_row_bytes, bar_kq);
+    }
+    bool ok = dev::mbar_wait_bounded(bar_kq, 0);
+    if (__syncthreads_or(!ok)) {
+        if (tid == 0) {
+            atomicOr(err, 1);
+            dev::mbar_wait_bounded(bar_kq, 0);
+            dev::mbar_wait_bounded(bar_v, 0);
+        }
+        return;
+    }
+    const int tq = tid >> 4, tj = tid & 15;
+    float sc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) sc[a][b] = 0.0f;
+#pragma unroll 4
+    for (int d = 0; d < HD; d += 4) {
+        float4 qv[4], kv[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+            qv[a] = tq + 16 * a < QV ? *reinterpret_cast<const float4*>(qs + (tq + 16 * a) * HD + d)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) kv[b] = *reinterpret_cast<const float4*>(ks + (tj + 16 * b) * S::kPad + d);
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                sc[a][b] = fmaf(qv[a].x, kv[b].x, sc[a][b]);
+                sc[a][b] = fmaf(qv[a].y, kv[b].y, sc[a][b]);
+                sc[a][b] = fmaf(qv[a].z, kv[b].z, sc[a][b]);
+                sc[a][b] = fmaf(qv[a].w, kv[b].w, sc[a][b]);
+            }
+    }
+    __syncthreads();  // every thread is done with qs: its area becomes ps
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int qi = tq + 16 * a;
+        const int r = qi / G;
+        const int lim = p0 + r0 + r - j0;  // the row sees positions j0 .. j0 + lim
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int jj = tj + 16 * b;
+            ps[qi * S::kPp + jj] = qi < QV && r < nr && jj < n && jj <= lim ? sc[a][b] * scale : -FLT_MAX;
+        }
+    }
+    __syncthreads();
+    // softmax statistics: warp w, query vectors 8w .. 8w + 7, lane -> positions lane, lane + 32
+    for (int i = 0; i < 8; ++i) {
+        const int qi = 8 * warp + i;
+        const float s0 = ps[qi * S::kPp + lane], s1 = ps[qi * S::kPp + lane + 32];
+        float mx = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const bool any = mx > -FLT_MAX;
+        const float e0 = any && s0 > -FLT_MAX ? expf(s0 - mx) : 0.0f;
+        const float e1 = any && s1 > -FLT_MAX ? expf(s1 - mx) : 0.0f;
+        ps[qi * S::kPp + lane] = e0;
+        ps[qi * S::kPp + lane + 32] = e1;
+        float sum = e0 + e1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            stat[qi][0] = mx;
+            stat[qi][1] = sum;
+        }
+    }
+    ok = dev::mbar_wait_bounded(bar_v, 0);
+    if (__syncthreads_or(!ok)) {  // also publishes ps and stat
+        if (tid == 0) {
+            atomicOr(err, 1);
+            dev::mbar_wait_bounded(bar_v, 0);
+        }
+        return;
+    }
+    // weighted values: thread (tq, td), query vectors tq + 16a, dims 4 td + 64 c
+    constexpr int kC = HD / 64;  // float4 columns per thread: 1 (HD 64) or 2 (HD 128)
+    const int td = tj;
+    float4 o[4][kC];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < kC; ++c) o[a][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int jj = 0; jj < n; ++jj) {
+        float pv[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) pv[a] = ps[(tq + 16 * a) * S::kPp + jj];
+#pragma unroll
+        for (int c = 0; c < kC; ++c) {
+            const float4 v4 = *reinterpret_cast<const float4*>(vs + jj * HD + 64 * c + 4 * td);
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                o[a][c].x = fmaf(pv[a], v4.x, o[a][c].x);
+                o[a][c].y = fmaf(pv[a], v4.y, o[a][c].y);
+                o[a][c].z = fmaf(pv[a], v4.z, o[a][c].z);
+                o[a][c].w = fmaf(pv[a], v4.w, o[a][c].w);
+            }
+        }
+    }
+    const int64_t splits = (max_seq + kSpan - 1) / kSpan;
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int qi = tq + 16 * a;
+        const int r = qi / G, g = qi - r * G;
+        if (qi >= QV || r >= nr || j0 > p0 + r0 + r) continue;  // no position of this split for the row
+        float* out = scratch + (((row0 + r) * heads + kvh * G + g) * splits + split) * (HD + 2);
+#pragma unroll
+        for (int c = 0; c < kC; ++c) {  // rows of HD + 2 floats: 8-byte aligned only
+            float* dst = out + 2 + 64 * c + 4 * td;
+            dst[0] = o[a][c].x;
+            dst[1] = o[a][c].y;
+            dst[2] = o[a][c].z;
+            dst[3] = o[a][c].w;
+        }
+        if (td == 0) {
+            out[0] = stat[qi][0];
+            out[1] = stat[qi][1];
+        }
+    }
+}
+
 __global__ void attention_merge_kernel(const float* __restrict__ scratch, float* __restrict__ ctx, int heads,
                                        int head_dim, int max_seq, const int32_t* __restrict__ pos, int rows_per_seq) {
     dev::pdl_wait();  // inputs may come from the previous kernel (programmatic dependent launch)
@@ -1658,6 +1857,58 @@ cudaError_t launch_staged_attention(dim3 grid, int group, cudaStream_t s, const 
 #undef KT_STAGED_CASE
 }
 
+bool prefill_attention_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("KT_ATTN_PREFILL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+template <int G, int HD>
+cudaError_t launch_prefill_attention_g(int rows, int rows_per_seq, int splits, cudaStream_t s, const float* q,
+                                       const float* kc, const float* vc, float* scores, int heads, int kv_heads,
+                                       int max_seq, int layer, float scale, int q_stride, const int32_t* pos,
+                                       int64_t cache_stride, int32_t* err) {
+    using P = PrefillAttention<G, HD>;
+    constexpr int kMaxDevices = 64;
+    static std::atomic<bool> done[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (!(dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire))) {
+        e = cudaFuncSetAttribute(attention_prefill_kernel<G, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(P::smem_bytes()));
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < kMaxDevices) done[dev].store(true, std::memory_order_release);
+    }
+    const int tiles = (rows / rows_per_seq) * ((rows_per_seq + P::QT - 1) / P::QT);
+    return launch_pdl(attention_prefill_kernel<G, HD>, dim3(kv_heads, splits, tiles), dim3(kThreads), P::smem_bytes(),
+                      s, q, kc, vc, scores, heads, kv_heads, max_seq, layer, scale, q_stride, pos, rows_per_seq,
+                      cache_stride, err);
+}
+
+template <int HD>
+cudaError_t launch_prefill_attention(int group, int rows, int rows_per_seq, int splits, cudaStream_t s,
+                                     const float* q, const float* kc, const float* vc, float* scores, int heads,
+                                     int kv_heads, int max_seq, int layer, float scale, int q_stride,
+                                     const int32_t* pos, int64_t cache_stride, int32_t* err) {
+#define KT_PREFILL_CASE(G_)                                                                                      \
+    return launch_prefill_attention_g<G_, HD>(rows, rows_per_seq, splits, s, q, kc, vc, scores, heads, kv_heads, \
+                                              max_seq, layer, scale, q_stride, pos, cache_stride, err)
+    switch (group) {
+        case 1: KT_PREFILL_CASE(1);
+        case 2: KT_PREFILL_CASE(2);
+        case 3: KT_PREFILL_CASE(3);
+        case 4: KT_PREFILL_CASE(4);
+        case 5: KT_PREFILL_CASE(5);
+        case 6: KT_PREFILL_CASE(6);
+        case 7: KT_PREFILL_CASE(7);
+        default: KT_PREFILL_CASE(8);
+    }
+#undef KT_PREFILL_CASE
+}
+
 cudaError_t launch_attention_decode(const float* q, const float* kc, const float* vc, float* ctx, float* scores,
                                     int rows, int q_stride, int heads, int kv_heads, int head_dim, int max_seq,
                                     int layer, float scale, const int32_t* pos, int rows_per_seq,
@@ -1669,6 +1920,21 @@ cudaError_t launch_attention_decode(const float* q, const float* kc, const float
     // staged: head_dim 64 / 128, cache rows on 16-byte boundaries (bulk copies)
     const bool aligned = (reinterpret_cast<uintptr_t>(kc) & 15) == 0 && (reinterpret_cast<uintptr_t>(vc) & 15) == 0 &&
                          cache_stride % 4 == 0;
+    // a prompt: tiles of query rows per block (the query rows copied in bulk too)
+    if (rows_per_seq > 1 && prefill_attention_enabled() && aligned && group <= 8 && (head_dim == 64 || head_dim == 128) &&
+        (reinterpret_cast<uintptr_t>(q) & 15) == 0 && q_stride % 4 == 0) {
+        const cudaError_t e =
+            head_dim == 64 ? launch_prefill_attention<64>(group, rows, rows_per_seq, splits, s, q, kc, vc, scores,
+                                                          heads, kv_heads, max_seq, layer, scale, q_stride, pos,
+                                                          cache_stride, err)
+                           : launch_prefill_attention<128>(group, rows, rows_per_seq, splits, s, q, kc, vc, scores,
+                                                           heads, kv_heads, max_seq, layer, scale, q_stride, pos,
+                                                           cache_stride, err);
+        if (e != cudaSuccess) return e;
+        launch_pdl(attention_merge_kernel, dim3(dim3(heads, rows)), dim3(128), 0, s, scores, ctx, heads, head_dim,
+                   max_seq, pos, rows_per_seq);
+        return cudaGetLastError();
+    }
     if (staged_attention_enabled() && aligned && group <= 8 && (head_dim == 64 || head_dim == 128)) {
         const cudaError_t e =
             head_dim == 64

@@ -315,10 +315,10 @@ class DeviceDecoder:
         for l, L in enumerate(self.layers):
             _lib.check(L_.kt_rmsnorm_qmatmul(h, L["wqkv"].handle, p(b.x), p(L["norm1"]), cfg.eps, p(b.normed),
                                              p(b.qkv), rows, 0, p(L["bqkv"]), s))
-            if rows_per_seq == 1 and self._fused_attention and (rows == 1 or (cfg.head_dim == 64 and rows <= 8)):
+            if rows_per_seq == 1 and self._fused_attention and rows <= (16 if cfg.head_dim == 128 else 8):
                 # one token per sequence: RoPE, cache store, attention and merge in one launch
-                # (measured slower than the separate kernels -- the streamed attention --
-                # once more sequences share a step: beyond 1 at head_dim 128, beyond 8 at 64)
+                # (measured slower than the separate kernels once more sequences share a
+                # step: beyond 16 at head_dim 128, beyond 8 at 64)
                 _lib.check(L_.kt_attention_rope_decode(h, p(b.qkv), rows, self.q_width, self.heads_local, kvh, hd,
                                                        p(self.inv_freq), keys, values, p(b.ctx), p(b.scores),
                                                        self.max_seq, l, self.scale, p(self.position),
