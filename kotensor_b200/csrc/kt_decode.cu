@@ -432,8 +432,16 @@ __global__ void __launch_bounds__(kThreads) attention_group_kernel(
 // block sets the error word, drains its copies (again bounded) and returns.
 template <int HD>
 struct StagedAttention {
-    static constexpr int kPad = HD + 4;  // floats between staged key rows
+    // head_dim 128: the key tile arrives as one bulk copy (rows 512 bytes apart)
+    // and lane l reads float4 chunk (i + l) mod 8 of its quarter row at step i, so
+    // 8 consecutive lanes cover all 32 banks; head_dim 64 (quarters of 4 chunks):
+    // one copy per row, rows landing 4 floats apart
+    static constexpr bool kRot = HD == 128;
+    static constexpr int kPad = kRot ? HD : HD + 4;  // floats between staged key rows
     static constexpr int kQuarter = HD / 4;
+    __device__ static int chunk(int c, int lane) {
+        return kRot ? (((c >> 2) + lane) & (kQuarter / 4 - 1)) << 2 : c;
+    }
     template <int G>
     static constexpr size_t smem_bytes() {
         return sizeof(float) * (static_cast<size_t>(kSpan) * kPad + kSpan * HD + G * HD + 4 * G * kSpan + kSpan * G);
@@ -482,9 +490,14 @@ __global__ void __launch_bounds__(kThreads) attention_group_staged_kernel(
             dev::bulk_load(dev::smem_u32(vs), vc + base, static_cast<uint32_t>(n * HD * sizeof(float)), bar_v);
         }
         __syncwarp();
-        for (int j = lane; j < n; j += 32)
-            dev::bulk_load(dev::smem_u32(ks + j * S::kPad), kc + base + static_cast<int64_t>(j) * HD,
-                           HD * sizeof(float), bar_k);
+        if constexpr (S::kRot) {
+            if (lane == 0)
+                dev::bulk_load(dev::smem_u32(ks), kc + base, static_cast<uint32_t>(n * HD * sizeof(float)), bar_k);
+        } else {
+            for (int j = lane; j < n; j += 32)
+                dev::bulk_load(dev::smem_u32(ks + j * S::kPad), kc + base + static_cast<int64_t>(j) * HD,
+                               HD * sizeof(float), bar_k);
+        }
     }
     const float* qh = q + static_cast<int64_t>(t) * q_stride + static_cast<int64_t>(kvh) * G * HD;
     for (int i = threadIdx.x; i < G * HD; i += kThreads) qs[i] = qh[i];
@@ -513,10 +526,11 @@ __global__ void __launch_bounds__(kThreads) attention_group_staged_kernel(
             const float* qq = qs + dq * S::kQuarter;
 #pragma unroll
             for (int c = 0; c < S::kQuarter; c += 4) {
-                const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+                const int cc = S::chunk(c, lane);
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + cc);
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const float4 q4 = *reinterpret_cast<const float4*>(qq + g * HD + c);
+                    const float4 q4 = *reinterpret_cast<const float4*>(qq + g * HD + cc);
                     acc[g][0] = fmaf(q4.x, k4.x, acc[g][0]);
                     acc[g][1] = fmaf(q4.y, k4.y, acc[g][1]);
                     acc[g][2] = fmaf(q4.z, k4.z, acc[g][2]);
@@ -1109,9 +1123,13 @@ __global__ void __launch_bounds__(kThreads) attention_decode_staged_kernel(
             if (n_old > 0) dev::bulk_load(dev::smem_u32(vs), vc + base, bytes, bar_v);
         }
         __syncwarp();
-        for (int j = lane; j < n_old; j += 32)
-            dev::bulk_load(dev::smem_u32(ks + j * S::kPad), kc + base + static_cast<int64_t>(j) * HD,
-                           HD * sizeof(float), bar_k);
+        if constexpr (S::kRot) {
+            if (lane == 0 && n_old > 0) dev::bulk_load(dev::smem_u32(ks), kc + base, bytes, bar_k);
+        } else {
+            for (int j = lane; j < n_old; j += 32)
+                dev::bulk_load(dev::smem_u32(ks + j * S::kPad), kc + base + static_cast<int64_t>(j) * HD,
+                               HD * sizeof(float), bar_k);
+        }
     }
     constexpr int half = HD / 2;
     const int kv_width = kv_heads * HD;
@@ -1161,10 +1179,11 @@ __global__ void __launch_bounds__(kThreads) attention_decode_staged_kernel(
             const float* qq = qs + dq * S::kQuarter;
 #pragma unroll
             for (int c = 0; c < S::kQuarter; c += 4) {
-                const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+                const int cc = S::chunk(c, lane);
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + cc);
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const float4 q4 = *reinterpret_cast<const float4*>(qq + g * HD + c);
+                    const float4 q4 = *reinterpret_cast<const float4*>(qq + g * HD + cc);
                     acc[g][0] = fmaf(q4.x, k4.x, acc[g][0]);
                     acc[g][1] = fmaf(q4.y, k4.y, acc[g][1]);
                     acc[g][2] = fmaf(q4.z, k4.z, acc[g][2]);
