@@ -152,6 +152,19 @@ kt_status kt_comm_unique_id(void* id_out /* 128 bytes */);
 kt_status kt_comm_init(kt_ctx* ctx, int32_t nranks, int32_t rank, const void* unique_id, kt_comm** out);
 kt_status kt_comm_destroy(kt_comm* comm);
 
+/* A communicator of nranks (2..8) in which only `rank` exists: no NCCL, every
+ * rank's exchange area allocated on this GPU, the exchange ready at once.  A
+ * row-parallel call whose exchange runs over peer memory (the fused m = 1
+ * GEMV; the small-product exchange) stores its partials and then waits for
+ * ranks that never arrive until the wait limit runs out
+ * (kt_comm_set_wait_limit), sets the context error word and returns; the
+ * context stays usable.  Calls that need NCCL (larger row-parallel products,
+ * kt_allgather_columns, kt_argmax_column_parallel) fail with
+ * KT_ERR_INVALID_ARGUMENT.  It exists to test the failure path of the fused
+ * exchange on one GPU; it has no counterpart in the reference, whose
+ * multi-rank path is not part of this library. */
+kt_status kt_comm_init_detached(kt_ctx* ctx, int32_t nranks, int32_t rank, kt_comm** out);
+
 /* Row-parallel multiplyQuantized: w_shard = kt_qweight_shard(W, axis 0, P, rank),
  * a_shard = the matching columns of a, contiguous [m x K_rank] on the device:
  *   c[m x N] = (accumulate ? c : 0) + alpha * sum_ranks a_shard . dequant(w_shard) + bias

@@ -253,6 +253,7 @@ struct kt_comm {
     void* peers[kTpMaxRanks] = {};      // every rank's area as mapped here (own at [rank])
     unsigned long long** d_recv = nullptr;  // device array of the P receive-area pointers
     uint64_t wait_ns = 2000000000ull;   // limit of a fused call's wait for the other ranks (2 s)
+    bool detached = false;              // kt_comm_init_detached: no NCCL, every area local
 };
 
 namespace {
@@ -293,6 +294,10 @@ bool tp_fused_enabled() {
 
 // Every rank's agreement on a local yes / no (sum of ones over NCCL).
 kt_status all_agree(kt_comm* c, bool mine, cudaStream_t s, bool* all) {
+    if (c->detached) {  // the ranks that never run take this rank's answer
+        *all = mine;
+        return KT_OK;
+    }
     float* f = nullptr;
     cudaError_t e = comm_scratch(c, 1, &f);
     if (e != cudaSuccess) return fail_tp(KT_ERR_OUT_OF_MEMORY, std::string("TP scratch: ") + cudaGetErrorString(e));
@@ -311,7 +316,10 @@ kt_status all_agree(kt_comm* c, bool mine, cudaStream_t s, bool* all) {
 
 void release_p2p(kt_comm* c) {
     for (int q = 0; q < c->nranks && q < kTpMaxRanks; ++q)
-        if (q != c->rank && c->peers[q] != nullptr) cudaIpcCloseMemHandle(c->peers[q]);
+        if (q != c->rank && c->peers[q] != nullptr) {
+            if (c->detached) cudaFree(c->peers[q]);  // allocated here, not mapped
+            else cudaIpcCloseMemHandle(c->peers[q]);
+        }
     cudaFree(c->area);
     cudaFree(c->d_recv);
     c->area = nullptr;
@@ -407,6 +415,47 @@ kt_status kt_comm_init(kt_ctx* ctx, int32_t nranks, int32_t rank, const void* un
     return KT_OK;
 }
 
+// Only `rank` of nranks exists: every rank's exchange area is allocated and
+// zeroed on this GPU, so the fused exchange is ready without a collective and
+// its waits for the absent ranks run into the wait limit.
+kt_status kt_comm_init_detached(kt_ctx* ctx, int32_t nranks, int32_t rank, kt_comm** out) {
+    if (!ctx || !out) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    if (nranks < 2 || nranks > kTpMaxRanks || rank < 0 || rank >= nranks)
+        return fail_tp(KT_ERR_INVALID_ARGUMENT, "rank " + std::to_string(rank) + " of " + std::to_string(nranks) +
+                                                    " (a detached communicator has 2.." +
+                                                    std::to_string(kTpMaxRanks) + " ranks)");
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+    auto* c = new (std::nothrow) kt_comm();
+    if (!c) return fail_tp(KT_ERR_OUT_OF_MEMORY, "host allocation failed");
+    c->ctx = ctx;
+    c->nranks = nranks;
+    c->rank = rank;
+    c->detached = true;
+    const size_t bytes = tp_area_bytes(nranks);
+    unsigned long long* recv[kTpMaxRanks] = {};
+    for (int q = 0; q < nranks && e == cudaSuccess; ++q) {
+        e = cudaMalloc(&c->peers[q], bytes);
+        if (e == cudaSuccess) e = cudaMemset(c->peers[q], 0, bytes);
+        recv[q] = static_cast<unsigned long long*>(c->peers[q]);
+    }
+    c->area = c->peers[rank];
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_recv, sizeof(unsigned long long*) * nranks);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(c->d_recv, recv, sizeof(unsigned long long*) * nranks, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        for (void* p : c->peers) cudaFree(p);
+        cudaFree(c->d_recv);
+        cudaGetLastError();
+        delete c;
+        return fail_tp(KT_ERR_OUT_OF_MEMORY, std::string("exchange areas: ") + cudaGetErrorString(e));
+    }
+    c->p2p_state = 1;
+    *out = c;
+    return KT_OK;
+}
+
 kt_status kt_comm_destroy(kt_comm* c) {
     if (!c) return KT_OK;
     cudaSetDevice(c->ctx->device);
@@ -496,6 +545,7 @@ kt_status kt_qmatmul_row_parallel(kt_ctx* ctx, kt_comm* comm, const kt_qweight* 
             return KT_OK;
         }
     }
+    if (comm->detached) return fail_tp(KT_ERR_INVALID_ARGUMENT, "a detached communicator has no collective");
     float* sum = nullptr;
     cudaError_t e = comm_scratch(comm, static_cast<size_t>(total), &sum);
     if (e != cudaSuccess) return fail_tp(KT_ERR_OUT_OF_MEMORY, std::string("TP scratch: ") + cudaGetErrorString(e));
@@ -514,6 +564,7 @@ kt_status kt_allgather_columns(kt_comm* comm, const float* y_shard, float* y_ful
                                void* stream) {
     if (!comm || !y_shard || !y_full) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     if (m <= 0 || n_shard <= 0) return fail_tp(KT_ERR_INVALID_ARGUMENT, "empty shard");
+    if (comm->detached) return fail_tp(KT_ERR_INVALID_ARGUMENT, "a detached communicator has no collective");
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int64_t per = static_cast<int64_t>(m) * n_shard;
     float* gathered = nullptr;
@@ -549,7 +600,10 @@ kt_status kt_comm_exchange_reset(kt_comm* comm, void* stream) {
     kt_status st = all_agree(comm, true, s, &every);
     if (st != KT_OK) return st;
     if (comm->p2p_state == 1) {
-        e = cudaMemsetAsync(comm->area, 0, tp_area_bytes(comm->nranks), s);
+        // a detached communicator clears every area (all of them are written here)
+        for (int q = 0; q < comm->nranks && e == cudaSuccess; ++q)
+            if (q == comm->rank || comm->detached)
+                e = cudaMemsetAsync(comm->peers[q], 0, tp_area_bytes(comm->nranks), s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return fail_tp(KT_ERR_CUDA, std::string("exchange reset: ") + cudaGetErrorString(e));
     }
@@ -567,6 +621,7 @@ kt_status kt_argmax_column_parallel(kt_comm* comm, const float* logits_shard, in
     if (!comm || !logits_shard || !out) return fail_tp(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     if (rows <= 0 || n_shard <= 0 || col_begin < 0 || static_cast<int64_t>(col_begin) + n_shard > kNoColumn)
         return fail_tp(KT_ERR_INVALID_ARGUMENT, "bad column-parallel argmax arguments");
+    if (comm->detached) return fail_tp(KT_ERR_INVALID_ARGUMENT, "a detached communicator has no collective");
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     float* scratch = nullptr;
     const size_t pair_words = 2 * static_cast<size_t>(rows);

@@ -120,6 +120,21 @@ class Comm:
         _lib.check(_lib.load().kt_comm_init(self._ctx.handle, world, rank, buf, ctypes.byref(h)))
         self._handle = h
 
+    @classmethod
+    def detached(cls, world: int, rank: int, ctx: Optional[Context] = None) -> "Comm":
+        """A communicator of `world` ranks of which only `rank` exists
+        (kt_comm_init_detached): every exchange area lives on this GPU, the
+        other ranks never arrive, so a fused m = 1 row-parallel call runs into
+        its wait limit and reports the timeout in the context's error word.
+        Calls that need NCCL raise.  For testing the failure path on one GPU."""
+        self = cls.__new__(cls)
+        self.world, self.rank = world, rank
+        self._ctx = ctx or Context.get()
+        h = ctypes.c_void_p()
+        _lib.check(_lib.load().kt_comm_init_detached(self._ctx.handle, world, rank, ctypes.byref(h)))
+        self._handle = h
+        return self
+
     @staticmethod
     def unique_id() -> bytes:
         buf = ctypes.create_string_buffer(Comm.ID_BYTES)

@@ -120,6 +120,54 @@ def test_fused_row_parallel_gemv_on_one_rank(kt):
     assert kt.Context.get().take_error() == 0
 
 
+def test_fused_exchange_times_out_on_one_gpu(kt, oracle):
+    """Failure path of the fused row-parallel exchange on one GPU: rank 0 of a
+    detached two-rank communicator (the other rank's area exists, nothing ever
+    writes it) waits for rank 1's partials until the 5 ms limit runs out, sets
+    the context error word and returns; the context then serves a correct
+    product, the exchange can be reset, and it times out the same way again.
+    Collectives on a detached communicator are refused."""
+    from kotensor_b200 import parallel as P
+    ctx = kt.Context.get()
+    assert ctx.take_error() == 0
+    comm = P.Comm.detached(2, 0)
+    try:
+        assert comm.exchange_ready()
+        comm.set_wait_limit(0.005)
+        k, n = 4096, 2048
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(29)
+        w = torch.randn((k, n), generator=gen, device="cuda") * 0.02
+        x = torch.randn((1, k), generator=gen, device="cuda")
+        qt = kt.QuantizedTensor.quantize(w, kt.Quantization(4))
+        shard = P.shard(qt, P.ROWS, 2, 0)
+        xs = x[:, :shard.rows].contiguous()
+        y = torch.zeros((1, n), device="cuda")
+        for attempt in range(2):
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            P.matmul_row_parallel(comm, xs, shard, y, 1)  # rank 1 never arrives
+            t1.record()
+            torch.cuda.synchronize()
+            assert t0.elapsed_time(t1) < 1000.0, attempt  # the 5 ms limit, not the 2 s default
+            assert ctx.take_error() != 0, attempt
+            # the context is still usable: an ordinary product is correct
+            ref = oracle.quantize(w.cpu().numpy(), 4, 64)
+            c = torch.full((1, n), float("nan"), device="cuda")
+            kt.MatMul.multiply_quantized(x, qt, c, 1, accumulate=False)
+            torch.cuda.synchronize()
+            y_ref = oracle.multiply_quantized(x.cpu().numpy(), ref)
+            assert rel_err(c.cpu().numpy(), y_ref) <= 1e-3
+            assert ctx.take_error() == 0
+            comm.reset_exchange()
+        with pytest.raises(Exception):
+            P.allgather_columns(comm, y, torch.empty((1, 2 * n), device="cuda"), 1)
+    finally:
+        comm.close()
+    assert ctx.take_error() == 0
+
+
 def _argmax_rule(logits):
     """argmaxOfLastToken per row: the largest logit above -1e9, the lowest column of a tie, 0 if none."""
     out = []
