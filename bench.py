@@ -746,10 +746,10 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
-def profile_decode(which: str) -> None:
+def profile_decode(which: str, batch: int = 1) -> None:
     """One captured decode step of a bench model (qwen: config 4, llama: config 5,
-    int8: config 3; batch 1) replayed once between cudaProfilerStart / Stop, for an
-    `ncu --profile-from-start off` launch list of the step's kernels."""
+    int8: config 3; `batch` sequences) replayed once between cudaProfilerStart /
+    Stop, for an `ncu --profile-from-start off` launch list of the step's kernels."""
     import numpy as np
     import torch
     import kotensor_b200 as kt
@@ -758,8 +758,9 @@ def profile_decode(which: str) -> None:
     prompt = {"qwen": 512, "llama": 1024, "int8": 128}[which]
     torch.cuda.set_device(0)
     cfg, w = decode_weights(kt, torch, seed=1, spec=spec)
-    dec = D.DeviceDecoder(cfg, w, max_seq=prompt + 64, batch=1)
-    dec.prefill([np.random.default_rng(0).integers(0, cfg.vocab, prompt).tolist()])
+    dec = D.DeviceDecoder(cfg, w, max_seq=prompt + 64, batch=batch)
+    rng = np.random.default_rng(0)
+    dec.prefill([rng.integers(0, cfg.vocab, prompt).tolist() for _ in range(batch)])
     dec.capture()
     for _ in range(3):
         dec._graph.replay()
@@ -770,7 +771,8 @@ def profile_decode(which: str) -> None:
         dec._graph.replay()
     b.record()
     torch.cuda.synchronize()
-    print(json.dumps({"profile_decode": which, "ms_per_step": round(a.elapsed_time(b) / 20, 4)}), flush=True)
+    print(json.dumps({"profile_decode": which, "batch": batch, "ms_per_step": round(a.elapsed_time(b) / 20, 4)}),
+          flush=True)
     torch.cuda.profiler.start()
     dec._graph.replay()
     torch.cuda.synchronize()
@@ -796,13 +798,14 @@ def main() -> None:
                     help="timed greedy steps of the INT8 163M decoder (BASELINE config 3; 0: skip)")
     ap.add_argument("--gemm-m", type=int, default=512,
                     help="also time the prefill GEMM at this M on the same weights (0: skip)")
+    ap.add_argument("--profile-batch", type=int, default=1, help="batch of the --profile-decode step")
     ap.add_argument("--profile-decode", choices=["qwen", "llama", "int8"], default=None,
                     help="instead of the bench: one decode step replayed between cudaProfilerStart / Stop")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.profile_decode:
-        profile_decode(args.profile_decode)
+        profile_decode(args.profile_decode, args.profile_batch)
         return
     if args.impl == "reference":
         run_reference(args)

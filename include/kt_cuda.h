@@ -253,10 +253,10 @@ kt_status kt_qmatmul_noalloc(kt_ctx* ctx, const kt_qweight* w, const float* a_de
 /* Which kernel family kt_qmatmul runs for this weight and m (for a 16-byte
  * aligned a), and so which tolerance applies: KT_PATH_GEMV (fp32 CUDA-core
  * streaming kernel), KT_PATH_GENERIC (fp32 kernel for unaligned shapes),
- * KT_PATH_TENSOR_CORE (bf16 tcgen05 kernel, 2e-2), KT_PATH_GEMV_MMA (INT4,
- * m <= 4, and m = 5..8 in two passes on weights of 16 MB or more: exact
- * integer weights on tensor cores with x as two integer parts (m = 1) or two
- * fp16 terms (m >= 2), fp32 group combine, 1e-3). */
+ * KT_PATH_TENSOR_CORE (bf16 tcgen05 kernel, 2e-2), KT_PATH_GEMV_MMA (INT4
+ * m <= 8, INT8 m = 1: exact integer weights on tensor cores with x as three
+ * integer parts (m = 1) or two fp16 terms (m >= 2; m = 5..8 as two groups of
+ * tokens in one launch), fp32 group combine, 1e-3). */
 enum { KT_PATH_GEMV = 0, KT_PATH_GENERIC = 1, KT_PATH_TENSOR_CORE = 2, KT_PATH_GEMV_MMA = 3 };
 kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out);
 
@@ -344,17 +344,19 @@ kt_status kt_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* a_dev
  * of both halves of TransformerBlock.decodeInto (TransformerBlock.kt:40-47):
  *   c[m x N] = (accumulate ? c : 0) + RMSNorm(x)[m x K] . dequant(W) + bias
  * with RMSNorm(x) = x * (1 / sqrt(mean(x^2) + eps)) * norm_weight per row.
- * Where the m = 1 INT4 GEMV takes the weight (and norm_weight_dev is 16-byte
- * aligned) the norm is applied while the GEMV stages x -- every CTA sums the
- * row's squares itself -- and xn_dev is not touched; elsewhere kt_rmsnorm
- * writes xn_dev ([m x K], may be NULL only on the fused path), then
- * kt_qmatmul.  Within the fp32 tolerance of the two calls. */
+ * Where an INT4 GEMV takes the weight (m = 1, or m = 2..8 with x_dev 16-byte
+ * aligned; norm_weight_dev 16-byte aligned) the norm is applied while the GEMV
+ * stages x -- every CTA sums the rows' squares itself -- and xn_dev is not
+ * touched; elsewhere kt_rmsnorm writes xn_dev ([m x K], may be NULL only on
+ * the fused path), then kt_qmatmul.  Within the fp32 tolerance of the two
+ * calls. */
 kt_status kt_rmsnorm_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* x_dev, const float* norm_weight_dev,
                              float eps, float* xn_dev, float* c_dev, int32_t m, int32_t accumulate,
                              const float* bias_dev, void* stream);
 /* The same followed by SwiGLU over a gate | up weight (kt_qmatmul_swiglu):
  * act[m x H] = silu(g) * u, [g | u] = RMSNorm(x) . dequant(W) + bias; both the
- * norm and silu(g) * u fused into the m = 1 INT4 GEMV where it applies. */
+ * norm and silu(g) * u fused into the m = 1 INT4 GEMV where it applies, the
+ * norm alone into the m = 2..8 one (gu_dev then receives [g | u]). */
 kt_status kt_rmsnorm_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* x_dev,
                                     const float* norm_weight_dev, float eps, float* xn_dev, float* gu_dev,
                                     float* act_dev, int32_t m, const float* bias_dev, void* stream);

@@ -105,16 +105,6 @@ void free_weight(kt_qweight* w) {
 
 }  // namespace
 
-// 5..8 rows in two passes of the INT4 tensor-core GEMV: measured faster than
-// the fp32 streaming kernel from ~16 MB of weight bytes (4096 x 14336 INT4:
-// 2 x 19.9 us against 54 us), slower on small weights where the extra launch
-// dominates.
-bool mma_in_two_passes(const QView& v, int32_t m, const float* a) {
-    const int64_t weight_bytes = static_cast<int64_t>(v.rows) * v.bytes_per_row;
-    return m > kGemvMmaMaxM && m <= 2 * kGemvMmaMaxM && weight_bytes >= (static_cast<int64_t>(16) << 20) &&
-           gemv_mma_supported(v, kGemvMmaMaxM, a);
-}
-
 cudaError_t stream_workspace(kt_ctx* ctx, cudaStream_t s, size_t bytes, void** out) {
     std::lock_guard<std::mutex> lock(ctx->ws_mutex);
     kt_ctx::Workspace* hit = nullptr;
@@ -185,25 +175,6 @@ kt_status run_matmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c,
             if (e != cudaSuccess) return cuda_fail(e, "qmatmul workspace");
         }
         e = launch_gemv_mma(v, args, ctx->sm_count, s, ws, need);
-    } else if (mma_in_two_passes(v, m, a)) {
-        // 5..8 rows of a large weight: the INT4 tensor-core GEMV on rows [0, 4)
-        // and [4, m) (two launches, each streaming the weight; faster than one
-        // fp32 pass once the weight is large enough to amortise the extra launch)
-        e = cudaSuccess;
-        for (int32_t r0 = 0; r0 < m && e == cudaSuccess; r0 += kGemvMmaMaxM) {
-            MatmulArgs part = args;
-            part.m = std::min<int32_t>(kGemvMmaMaxM, m - r0);
-            part.a = a + static_cast<int64_t>(r0) * w->rows;
-            part.c = c + static_cast<int64_t>(r0) * w->columns;
-            if (part.lora.p != nullptr) part.lora.p += static_cast<int64_t>(r0) * part.lora.rank;
-            const size_t need = gemv_mma_workspace_bytes(v, part.m, ctx->sm_count);
-            void* ws = nullptr;
-            if (need > 0) {
-                e = stream_workspace(ctx, s, need, &ws);
-                if (e != cudaSuccess) return cuda_fail(e, "qmatmul workspace");
-            }
-            e = launch_gemv_mma(v, part, ctx->sm_count, s, ws, need);
-        }
     } else if (gemv_fast_supported(v, m, a)) {
         e = launch_gemv(v, args, ctx->sm_count, s);
     } else if (gemm_tc_supported(v, m, a)) {
@@ -688,7 +659,7 @@ kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out) {
     if (!w || !path_out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
     const QView v = view(w);
-    const bool mma_rows = gemv_mma_supported(v, m, nullptr) || mma_in_two_passes(v, m, nullptr);
+    const bool mma_rows = gemv_mma_supported(v, m, nullptr);
     *path_out = gemv_imma_supported(v, m, nullptr) || mma_rows ? KT_PATH_GEMV_MMA
                 : gemv_fast_supported(v, m, nullptr) ? KT_PATH_GEMV
                 : gemm_tc_supported(v, m, nullptr)   ? KT_PATH_TENSOR_CORE
@@ -1055,6 +1026,22 @@ kt_status rmsnorm_matmul(kt_ctx* ctx, const kt_qweight* w, const float* x, const
     const bool swiglu_in = swiglu && swiglu_fused_supported(v, m, x);
     if (norm_in && swiglu && !swiglu_in && !gu)
         return fail(KT_ERR_INVALID_ARGUMENT, "this shape needs the gate | up scratch gu");
+    // 2..8 rows on the INT4 tensor-core GEMV: the norm in its prologue as well
+    // (float4 loads of each x row), silu(gate) * up by a separate kernel
+    const bool norm_mma = !norm_in && m >= 2 && gemv_mma_supported(v, m, x) &&
+                          reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(norm_w) % 16 == 0;
+    if (norm_mma) {
+        if (swiglu && !gu) return fail(KT_ERR_INVALID_ARGUMENT, "this shape needs the gate | up scratch gu");
+        MatmulArgs args{x, swiglu ? gu : c, bias, m, swiglu ? 0 : accumulate, 1.0f, ctx->d_error};
+        args.norm_weight = norm_w;
+        args.norm_eps = eps;
+        const size_t need = gemv_mma_workspace_bytes(v, m, ctx->sm_count);
+        void* ws = nullptr;
+        if (need > 0) KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "qmatmul workspace");
+        KT_CUDA_TRY(launch_gemv_mma(v, args, ctx->sm_count, s, ws, need), "rmsnorm_qmatmul launch");
+        if (swiglu) KT_CUDA_TRY(launch_silu_mul_rows(gu, c, m, w->columns / 2, s), "silu_mul launch");
+        return KT_OK;
+    }
     if (norm_in) {
         // the norm in the GEMV's prologue; silu(gate) * up in its epilogue, or
         // (weights whose gate and up columns do not share a tile) a separate kernel

@@ -1,6 +1,6 @@
-// kt_gemv_mma.cu -- INT4 decode GEMV (m <= 4) with tensor-core products:
+// kt_gemv_mma.cu -- INT4 decode GEMV (m <= 8) with tensor-core products:
 // MatMul.multiplyQuantized (Engine/kotensor/src/main/kotlin/MatMul.kt:460-536,
-// :599-828) for m = 1..4.
+// :599-828) for m = 1..8.
 //
 // Why tensor cores for a memory-bound GEMV.  B200's HBM streams ~13e12 INT4
 // weights/s while its CUDA cores issue ~3.7e13 lane instructions/s; an fp32
@@ -51,6 +51,13 @@
 // launched with programmatic stream serialization: the weight prefetch overlaps
 // the previous kernel, griddepcontrol.wait orders the reads of x and the writes
 // of y after it.
+//
+// Token groups.  One CTA carries at most 4 tokens (the 8 B columns); m = 5..8
+// runs as one launch with two groups of CTAs, tokens [0, 4) and [4, m), each
+// streaming the weight.  The group is the fastest-varying part of blockIdx.x,
+// so the two CTAs of a (tile, split) are scheduled together and the second
+// read of the tile mostly hits L2.  A group short of 4 tokens stages zeros for
+// the missing ones and writes no row for them.
 //
 // Reduction order (deterministic, no atomics, no global scratch): group
 // partials in registers per thread in row order; the 8 slices of a CTA through
@@ -119,8 +126,11 @@ struct MmaParams {
     LoraEpilogue lora;
     // split-K (gridDim.y > 1): per-CTA partial tiles and per-tile arrival
     // counters (zero on entry, left zero on exit)
-    float* partials;       // [tiles][splits][M][256]
-    int32_t* tickets;      // [tiles]
+    float* partials;       // [tiles][groups][splits][M][256]
+    int32_t* tickets;      // [tiles][groups]
+    int32_t m_total;       // rows of the call (token group z holds rows [4z, min(4z + M, m_total)))
+    const float* norm_w;   // RMSNorm of every x row before the product (NULL: off)
+    float norm_eps;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -234,9 +244,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int g = lane >> 2;     // MMA row group
     const int t = lane & 3;      // MMA k quad: rows 2t, 2t+1, 2t+8, 2t+9; token t of C
     const int gb = 8 * hw + g;   // this lane's 8-byte chunk of the tile row
-    const int tile_b0 = blockIdx.x * kTileBytes;
+    const int groups = (p.m_total + 3) / 4;                 // token groups (1 unless M == 4 and m > 4)
+    const int tile_b0 = static_cast<int>(blockIdx.x) / groups * kTileBytes;
     const int tile_cols = min(kTileBytes, p.R - tile_b0);  // packed bytes of this tile inside the row
     const int half = p.R;
+    const int row0 = 4 * (static_cast<int>(blockIdx.x) % groups);  // first row (token) of this CTA's group
+    const int mv = min(M, p.m_total - row0);                // tokens of the group that exist
 
     // K-slices: the K/32 stages spread evenly over splits x kPairs slices
     // (the host keeps every slice within max_slice_rows<M>())
@@ -316,6 +329,45 @@ __global__ void __launch_bounds__(kThreads, 2)
     pdl_launch_dependents();
     pdl_wait();  // x and y below may belong to the previous kernel
 
+    // RMSNorm prologue (p.norm_w; RMSNorm.forwardInto, RMSNorm.kt:71-90): every
+    // CTA sums the squares of its tokens' whole rows (the same order in every
+    // CTA, so all of them get the same scale) and stages x * scale * w.
+    float nrm[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) nrm[m] = 1.0f;
+    if (p.norm_w != nullptr) {
+        __shared__ float s_nred[kWarps][4];
+        float ss[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            ss[m] = 0.0f;
+            if (m >= mv) continue;
+            const float* xr = p.x + static_cast<int64_t>(row0 + m) * p.K;
+#pragma unroll 4
+            for (int i = 4 * tid; i < p.K; i += 4 * kThreads) {
+                const float4 v4 = __ldg(reinterpret_cast<const float4*>(xr + i));
+                ss[m] = fmaf(v4.x, v4.x, ss[m]);
+                ss[m] = fmaf(v4.y, v4.y, ss[m]);
+                ss[m] = fmaf(v4.z, v4.z, ss[m]);
+                ss[m] = fmaf(v4.w, v4.w, ss[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], o);
+            if (lane == 0) s_nred[warp][m] = ss[m];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int w2 = 0; w2 < kWarps; ++w2) tot += s_nred[w2][m];
+            nrm[m] = 1.0f / sqrtf(tot / static_cast<float>(p.K) + p.norm_eps);
+        }
+    }
+
     // Stage this slice's rows of x: thread pt of the pair holds rows pt + 64 j.
     const int pt = hw * 32 + lane;
     const int n_rows = r_end - r_begin;
@@ -324,12 +376,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     float xv[M][kPer];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-        const float* xm = p.x + static_cast<int64_t>(m) * p.K + r_begin;
+        const float* xm = p.x + static_cast<int64_t>(row0 + m) * p.K + r_begin;
         float mx = 0.0f;
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
             const int r = pt + 64 * j;
-            xv[m][j] = r < n_rows ? __ldg(xm + r) : 0.0f;
+            xv[m][j] = r < n_rows && m < mv ? __ldg(xm + r) : 0.0f;
+            if (p.norm_w != nullptr && r < n_rows) xv[m][j] = xv[m][j] * nrm[m] * __ldg(p.norm_w + r_begin + r);
             mx = fmaxf(mx, fabsf(xv[m][j]));
             if (64 * (j + 1) >= n_rows) break;  // pair-uniform
         }
@@ -527,11 +580,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int m = idx / CT, col = idx % CT;
         const int byte = tile_b0 + (col < kTileBytes ? col : col - kTileBytes);
         const int out_col = col < kTileBytes ? byte : half + byte;
-        if (byte < p.R && out_col < p.N) {
-            float* out = p.y + static_cast<int64_t>(m) * p.N + out_col;
+        if (m < mv && byte < p.R && out_col < p.N) {
+            float* out = p.y + static_cast<int64_t>(row0 + m) * p.N + out_col;
             float r = fmaf(p.alpha, v, p.accumulate ? *out : 0.0f);
             if (p.bias != nullptr) r += p.bias[out_col];
-            if (p.lora.p != nullptr) r += lora_term(p.lora, m, out_col, p.N);
+            if (p.lora.p != nullptr) r += lora_term(p.lora, row0 + m, out_col, p.N);
             *out = r;
         }
     };
@@ -547,11 +600,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     // and, in the last CTA, acquires the other CTAs' partials for the whole
     // CTA through the second barrier.
     __shared__ int s_last;
-    float* tile_parts = p.partials + static_cast<int64_t>(blockIdx.x) * S * (M * CT);
+    const int ticket = blockIdx.x;  // (tile, group)
+    float* tile_parts = p.partials + static_cast<int64_t>(ticket) * S * (M * CT);
     float* mine = tile_parts + static_cast<int64_t>(blockIdx.y) * (M * CT);
     for (int idx = tid; idx < M * CT; idx += kThreads) __stcg(mine + idx, part[idx]);
     __syncthreads();
-    if (tid == 0) s_last = atomic_add_acq_rel(p.tickets + blockIdx.x, 1) == S - 1;
+    if (tid == 0) s_last = atomic_add_acq_rel(p.tickets + ticket, 1) == S - 1;
     __syncthreads();
     if (!s_last) return;
     for (int idx = tid; idx < M * CT; idx += kThreads) {
@@ -568,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         emit(idx, v);
     }
-    if (tid == 0) p.tickets[blockIdx.x] = 0;  // ready for the next launch on this workspace
+    if (tid == 0) p.tickets[ticket] = 0;  // ready for the next launch on this workspace
 }
 
 struct MmaOverrides {
@@ -613,6 +667,10 @@ int tiles_of(int R) { return (R + kTileBytes - 1) / kTileBytes; }
 constexpr int kTicketCap = kTicketCapEach;
 constexpr size_t kTicketBytes = kWorkspaceReservedBytes;
 
+// CTA groups along grid z (4 tokens each) and tokens per CTA of a call with m rows.
+int groups_of(int m) { return (m + 3) / 4; }
+int m_per_cta(int m) { return std::min(m, 4); }
+
 int max_slice_rows_of(int m) {
     switch (m) {
         case 1: return max_slice_rows<1>();
@@ -628,10 +686,10 @@ int min_splits(int K, int m) {
     return (K + per - 1) / per;
 }
 
-// K-splits per column tile: enough CTAs to fill every SM slot in one wave
-// (at least one stage per slice), never fewer than min_splits.
+// K-splits per column tile: enough CTAs (over every token group) to fill every
+// SM slot in one wave (at least one stage per slice), never fewer than min_splits.
 int choose_splits(int R, int K, int m, int sm_count) {
-    const int tiles = tiles_of(R);
+    const int tiles = tiles_of(R) * groups_of(m);
     const int slots = blocks_per_sm() * sm_count;
     const int k_stages = K / kRowsPerStage;
     int s = std::max(1, slots / tiles);
@@ -643,13 +701,13 @@ int choose_splits(int R, int K, int m, int sm_count) {
 }
 
 template <int M>
-cudaError_t launch_m(const QView& w, const MmaParams& p, int splits, cudaStream_t s) {
+cudaError_t launch_m(const QView& w, const MmaParams& p, int splits, int groups, cudaStream_t s) {
     auto kernel = gemv_mma_kernel<M>;
     const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t lc = {};
-    lc.gridDim = dim3(tiles_of(p.R), splits, 1);
+    lc.gridDim = dim3(tiles_of(p.R) * groups, splits, 1);
     lc.blockDim = dim3(kThreads, 1, 1);
     lc.dynamicSmemBytes = kSmemBytes;
     lc.stream = s;
@@ -669,14 +727,15 @@ bool gemv_mma_supported(const QView& w, int32_t m, const float* a) {
     (void)a;
     if (w.bits != 4 || m < 1 || m > kGemvMmaMaxM || w.tmap_mma == nullptr) return false;
     return w.columns % 32 == 0 && w.rows % kRowsPerStage == 0 && w.group_size % kRowsPerStage == 0 &&
-           min_splits(w.rows, m) <= 65535 && (min_splits(w.rows, m) == 1 || tiles_of(w.bytes_per_row) <= kTicketCap);
+           min_splits(w.rows, m) <= 65535 &&
+           (min_splits(w.rows, m) == 1 || tiles_of(w.bytes_per_row) * groups_of(m) <= kTicketCap);
 }
 
 size_t gemv_mma_workspace_bytes(const QView& w, int32_t m, int sm_count) {
     const int splits = choose_splits(w.bytes_per_row, w.rows, m, sm_count);
     if (splits <= 1) return 0;
-    const size_t tiles = static_cast<size_t>(tiles_of(w.bytes_per_row));
-    return kTicketBytes + tiles * splits * static_cast<size_t>(m) * 2 * kTileBytes * sizeof(float);
+    const size_t tiles = static_cast<size_t>(tiles_of(w.bytes_per_row)) * groups_of(m);
+    return kTicketBytes + tiles * splits * static_cast<size_t>(m_per_cta(m)) * 2 * kTileBytes * sizeof(float);
 }
 
 cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, cudaStream_t s, void* workspace,
@@ -695,19 +754,23 @@ cudaError_t launch_gemv_mma(const QView& w, const MatmulArgs& a, int sm_count, c
     p.alpha = a.alpha;
     p.accumulate = a.accumulate;
     p.lora = a.lora;
+    p.m_total = a.m;
+    p.norm_w = a.norm_weight;
+    p.norm_eps = a.norm_eps;
     const int splits = choose_splits(p.R, p.K, a.m, sm_count);
+    const int groups = groups_of(a.m);
     if (splits > 1) {
         if (workspace == nullptr || workspace_bytes < gemv_mma_workspace_bytes(w, a.m, sm_count))
             return cudaErrorInvalidValue;
         p.tickets = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(workspace) + kGemvTicketOffset);
         p.partials = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kTicketBytes);
     }
-    switch (a.m) {
-        case 1: return launch_m<1>(w, p, splits, s);
-        case 2: return launch_m<2>(w, p, splits, s);
-        case 3: return launch_m<3>(w, p, splits, s);
-        case 4: return launch_m<4>(w, p, splits, s);
-        default: return cudaErrorInvalidValue;
+    if (a.m < 1 || a.m > kGemvMmaMaxM) return cudaErrorInvalidValue;
+    switch (m_per_cta(a.m)) {
+        case 1: return launch_m<1>(w, p, splits, groups, s);
+        case 2: return launch_m<2>(w, p, splits, groups, s);
+        case 3: return launch_m<3>(w, p, splits, groups, s);
+        default: return launch_m<4>(w, p, splits, groups, s);
     }
 }
 

@@ -107,10 +107,6 @@ __device__ __forceinline__ float lora_term(const LoraEpilogue& l, int t, int col
 }
 #endif
 
-// m = 5..8 on a weight large enough that two passes of the m <= 4 INT4
-// tensor-core GEMV beat one fp32 streaming pass (kt_api.cu).
-bool mma_in_two_passes(const QView& v, int32_t m, const float* a);
-
 // The dispatch behind kt_qmatmul (kt_api.cu): argument-checked by the caller.
 kt_status run_qmatmul(kt_ctx* ctx, const kt_qweight* w, const float* a, float* c, int32_t m, int32_t accumulate,
                       float alpha, const float* bias, cudaStream_t s, const LoraEpilogue* lora = nullptr);
@@ -198,7 +194,7 @@ struct MatmulArgs {
     int32_t swiglu = 0;
     // RMSNorm of the input row before the product (RMSNorm.forwardInto,
     // RMSNorm.kt:71-90): a is read as a * (1 / sqrt(mean(a^2) + eps)) * norm_weight
-    // (norm_weight NULL: off; m = 1 INT4 GEMV only).
+    // (norm_weight NULL: off; the INT4 GEMVs: m = 1 integer, m = 2..8 fp16 products).
     const float* norm_weight = nullptr;
     float norm_eps = 0.0f;
 };
@@ -209,8 +205,9 @@ void set_gemv_tuning(int lane_bytes, int cluster_k);
 cudaError_t launch_gemv(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s);
 cudaError_t launch_matmul_generic(const QView& w, const MatmulArgs& args, cudaStream_t s);
 
-// ---- kt_gemv_mma.cu  (INT4, m <= kGemvMmaMaxM: tensor-core products, fp32 group combine)
-constexpr int kGemvMmaMaxM = 4;
+// ---- kt_gemv_mma.cu  (INT4, m <= kGemvMmaMaxM: tensor-core products, fp32 group combine;
+// m = 5..8 as two groups of 4 tokens in one launch)
+constexpr int kGemvMmaMaxM = 8;
 bool gemv_mma_supported(const QView& w, int32_t m, const float* a);
 void set_mma_tuning(int k_splits);
 // Device workspace one launch needs (0: none): split-K partial tiles and

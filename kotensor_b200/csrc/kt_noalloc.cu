@@ -93,21 +93,6 @@ extern "C" kt_status kt_qmatmul_noalloc(kt_ctx* ctx, const kt_qweight* w, const 
         const size_t need = gemv_mma_workspace_bytes(v, m, ctx->sm_count);
         if (need > kStaticWorkspaceBytes) return too_big(need);
         e = launch_gemv_mma(v, args, ctx->sm_count, s, need > 0 ? ws : nullptr, kStaticWorkspaceBytes);
-    } else if (mma_in_two_passes(v, m, a)) {
-        // rows [0, 4) and [4, m) one after the other on the stream: both passes may use the array
-        for (int32_t r0 = 0; r0 < m; r0 += kGemvMmaMaxM) {
-            const size_t need = gemv_mma_workspace_bytes(v, std::min<int32_t>(kGemvMmaMaxM, m - r0), ctx->sm_count);
-            if (need > kStaticWorkspaceBytes) return too_big(need);
-        }
-        e = cudaSuccess;
-        for (int32_t r0 = 0; r0 < m && e == cudaSuccess; r0 += kGemvMmaMaxM) {
-            MatmulArgs part = args;
-            part.m = std::min<int32_t>(kGemvMmaMaxM, m - r0);
-            part.a = a + static_cast<int64_t>(r0) * w->rows;
-            part.c = c + static_cast<int64_t>(r0) * w->columns;
-            const size_t need = gemv_mma_workspace_bytes(v, part.m, ctx->sm_count);
-            e = launch_gemv_mma(v, part, ctx->sm_count, s, need > 0 ? ws : nullptr, kStaticWorkspaceBytes);
-        }
     } else if (gemv_fast_supported(v, m, a)) {
         e = launch_gemv(v, args, ctx->sm_count, s);
     } else if (gemm_tc_supported(v, m, a)) {

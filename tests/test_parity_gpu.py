@@ -338,7 +338,7 @@ def test_every_launch_shape_matches_the_oracle(kt, oracle, lane_bytes, cluster_k
 @pytest.mark.parametrize("k_splits", [1, 2, 5, 37])
 @pytest.mark.parametrize("k,n,g", [(2048, 5632, 64), (4864, 896, 64), (1024, 4096, 32), (960, 2048, 96)])
 def test_int4_tensor_core_gemv_matches_the_oracle(kt, oracle, k_splits, k, n, g):
-    """The INT4 m <= 4 tensor-core GEMV at several K-split counts (slices that
+    """The INT4 m <= 8 tensor-core GEMV at several K-split counts (slices that
     start and end inside groups, empty slices), ragged last tiles (896 columns)
     and group sizes 32 / 64 / 96, within the fp32 tolerance."""
     from kotensor_b200 import _lib
@@ -350,7 +350,7 @@ def test_int4_tensor_core_gemv_matches_the_oracle(kt, oracle, k_splits, k, n, g)
     assert qt.matmul_path(1) == _lib.KT_PATH_GEMV_MMA
     try:
         lib.kt_set_gemv_mma_tuning(k_splits)
-        for m in (1, 2, 4):
+        for m in (1, 2, 4, 6, 8):
             a = (rng.standard_normal((m, k), dtype=np.float32) * np.float32(3.0)).astype(np.float32)
             a[0, : k // 3] *= np.float32(1e-3)  # a wide dynamic range inside one row
             c0 = rng.standard_normal((m, n), dtype=np.float32)
@@ -453,7 +453,7 @@ BENCH_SHAPES = [(2048, 5632), (5632, 2048), (4096, 14336), (14336, 4096)]  # BAS
 def test_bench_weights_gemv_against_oracle(kt, oracle, k, n):
     """The four weights bench.py times, quantized on the
     device (bit-exact) and multiplied at m = 1 on the integer tensor-core GEMV,
-    plus m = 4 and two passes of m = 4 (m = 8) on the fp16 one."""
+    plus m = 4 and m = 5 / 8 (two token groups in one launch) on the fp16 one."""
     from kotensor_b200 import _lib
     rng = np.random.default_rng(k + 3 * n)
     w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
@@ -463,7 +463,8 @@ def test_bench_weights_gemv_against_oracle(kt, oracle, k, n):
     assert np.array_equal(q, ref_t.qdata) and np.array_equal(s.view(np.uint32), ref_t.scales.view(np.uint32))
     assert np.array_equal(z, ref_t.zeros)
     assert qt.matmul_path(1) == _lib.KT_PATH_GEMV_MMA
-    for m in (1, 4, 8):
+    for m in (1, 4, 5, 8):
+        assert qt.matmul_path(m) == _lib.KT_PATH_GEMV_MMA
         a = rng.standard_normal((m, k), dtype=np.float32)
         y = run_matmul(kt, qt, a)
         assert rel_err(y, oracle.multiply_quantized(a, ref_t, threads=8)) <= TOL_FP32, m
@@ -548,12 +549,13 @@ def test_swiglu_epilogue_equals_matmul_then_silu(kt, oracle, k, h, m):
 
 @pytest.mark.parametrize("bits,k,n", [(4, 896, 1152), (4, 4096, 6144), (4, 896, 9728), (4, 4096, 28672),
                                       (8, 768, 2304)])
-@pytest.mark.parametrize("m", [1, 3])
+@pytest.mark.parametrize("m", [1, 3, 6])
 @pytest.mark.parametrize("swiglu", [False, True])
 def test_rmsnorm_prologue_matches_rmsnorm_then_matmul(kt, oracle, bits, k, n, m, swiglu):
     """kt_rmsnorm_qmatmul(_swiglu): RMSNorm(x) . W + bias (then silu(gate) * up).
-    At m = 1 on INT4 the norm is applied while the GEMV stages x (each CTA sums
-    the row's squares itself); elsewhere kt_rmsnorm then the matmul.  Within
+    On INT4 (m = 1 integer GEMV, m = 3 and 6 fp16 GEMV, one and two token
+    groups) the norm is applied while the GEMV stages x (each CTA sums the
+    rows' squares itself); INT8 m > 1: kt_rmsnorm then the matmul.  Within
     1e-5 of the separate kernels (the squares are added in another order) and
     within the fp32 tolerance of the oracle; accumulate into c included."""
     import ctypes

@@ -33,12 +33,13 @@ def call(lib, fn, qt, x, y, m, accumulate=False, alpha=1.0):
 
 
 # (bits, K, N, m): every kernel family kt_qmatmul routes to -- the m = 1 integer
-# tensor-core GEMV (split-K in clusters and through the array), m = 2..4 and
-# two passes of m = 5..8 on the fp16 tensor-core GEMV, the fp32 streaming GEMV
-# (INT8, small INT4 at m = 5..8), the tcgen05 GEMM at m >= 9 (INT4 and INT8,
+# tensor-core GEMV (split-K in clusters and through the array), m = 2..8 on the
+# fp16 tensor-core GEMV (m = 5..8 as two token groups in one launch), the fp32
+# streaming GEMV (INT8 at m = 2..8), the tcgen05 GEMM at m >= 9 (INT4 and INT8,
 # with and without split-K), the generic kernel (ragged N)
 CASES = [(4, 4096, 14336, 1), (4, 14336, 4096, 1), (4, 768, 32000, 1), (4, 2048, 5632, 4), (4, 14336, 4096, 2),
-         (4, 4096, 14336, 6), (4, 2048, 5632, 7), (8, 2048, 2048, 1), (8, 2048, 2048, 64), (4, 4096, 14336, 16),
+         (4, 4096, 14336, 6), (4, 2048, 5632, 7), (8, 2048, 2048, 1), (8, 2048, 2048, 4), (8, 2048, 2048, 64),
+         (4, 4096, 14336, 16),
          (4, 4096, 14336, 64), (4, 2048, 5632, 96), (8, 2048, 2048, 9), (4, 512, 1000, 12)]
 
 
