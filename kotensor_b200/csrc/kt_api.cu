@@ -1001,6 +1001,16 @@ kt_status kt_qmatmul_swiglu(kt_ctx* ctx, const kt_qweight* w, const float* a, fl
         KT_CUDA_TRY(launch_gemv_imma(v, args, ctx->sm_count, s, ws, need), "qmatmul_swiglu launch");
         return KT_OK;
     }
+    if (gemm_tc_supported(v, m, a) && gemm_swiglu_fused(v, m, ctx->sm_count)) {
+        // m >= 9: silu(gate) * up in the GEMM's split-K reduction
+        MatmulArgs args{a, act, bias, m, 0, alpha, ctx->d_error};
+        args.swiglu = 1;
+        void* ws = nullptr;
+        KT_CUDA_TRY(stream_workspace(ctx, s, gemm_tc_workspace_bytes(v, m, ctx->sm_count), &ws), "qmatmul workspace");
+        KT_CUDA_TRY(launch_gemm_tc(v, args, ctx->sm_count, s, ws, gemm_tc_workspace_bytes(v, m, ctx->sm_count)),
+                    "qmatmul_swiglu launch");
+        return KT_OK;
+    }
     if (!gu) return fail(KT_ERR_INVALID_ARGUMENT, "this shape needs the gate | up scratch gu");
     const kt_status st = run_matmul(ctx, w, a, gu, m, 0, alpha, bias, s);
     if (st != KT_OK) return st;
@@ -1040,6 +1050,24 @@ kt_status rmsnorm_matmul(kt_ctx* ctx, const kt_qweight* w, const float* x, const
         if (need > 0) KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "qmatmul workspace");
         KT_CUDA_TRY(launch_gemv_mma(v, args, ctx->sm_count, s, ws, need), "rmsnorm_qmatmul launch");
         if (swiglu) KT_CUDA_TRY(launch_silu_mul_rows(gu, c, m, w->columns / 2, s), "silu_mul launch");
+        return KT_OK;
+    }
+    // m >= 9 on the tcgen05 GEMM: the norm in its bf16 pre-pass, silu(gate) * up
+    // in its split-K reduction where that applies, else a separate kernel
+    const bool norm_gemm = !norm_in && !norm_mma && gemm_tc_supported(v, m, x) &&
+                           reinterpret_cast<uintptr_t>(norm_w) % 16 == 0;
+    if (norm_gemm) {
+        const bool sw_in = swiglu && gemm_swiglu_fused(v, m, ctx->sm_count);
+        if (swiglu && !sw_in && !gu) return fail(KT_ERR_INVALID_ARGUMENT, "this shape needs the gate | up scratch gu");
+        MatmulArgs args{x, swiglu && !sw_in ? gu : c, bias, m, swiglu ? 0 : accumulate, 1.0f, ctx->d_error};
+        args.norm_weight = norm_w;
+        args.norm_eps = eps;
+        args.swiglu = sw_in ? 1 : 0;
+        const size_t need = gemm_tc_workspace_bytes(v, m, ctx->sm_count);
+        void* ws = nullptr;
+        KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "qmatmul workspace");
+        KT_CUDA_TRY(launch_gemm_tc(v, args, ctx->sm_count, s, ws, need), "rmsnorm_qmatmul launch");
+        if (swiglu && !sw_in) KT_CUDA_TRY(launch_silu_mul_rows(gu, c, m, w->columns / 2, s), "silu_mul launch");
         return KT_OK;
     }
     if (norm_in) {

@@ -95,6 +95,10 @@ struct GemmParams {
     float* partials;   // [tile][split][nt][256]
     int32_t* tickets;  // [tile], zero between launches
     int32_t reduce_kernel;  // 1: the partials are summed by split_reduce_kernel, not the last CTA
+    // SwiGLU in split_reduce_kernel (INT4 gate | up weight, N = 2R): y receives
+    // [M x R] silu(gate) * up, gate column b the low and up column R + b the
+    // high nibble of byte b (accumulate 0)
+    int32_t swiglu;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -805,8 +809,49 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(GemmParams p, int til
     constexpr int kQuads = kCT / 4;
     dev::pdl_launch_dependents();
     dev::pdl_wait();  // the partials are the previous kernel's output
-    const int64_t total = static_cast<int64_t>(tiles_x) * tiles_y * p.nt * kQuads;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    if (BITS == 4 && p.swiglu) {
+        // thread: 4 adjacent bytes of one token of one tile, their gate (low
+        // nibble) and up (high nibble) columns (SwiGLU.forwardInto,
+        // Tensor.kt:231-237; the arithmetic of kt_silu_mul_rows)
+        const int64_t total_b = static_cast<int64_t>(tiles_x) * tiles_y * p.nt * (kTileBytes / 4);
+        for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total_b; i += stride) {
+            const int q4 = static_cast<int>(i % (kTileBytes / 4)) * 4;
+            const int64_t rest = i / (kTileBytes / 4);
+            const int t = static_cast<int>(rest % p.nt);
+            const int64_t tile_id = rest / p.nt;
+            const int bx = static_cast<int>(tile_id % tiles_x);
+            const int tok = static_cast<int>(tile_id / tiles_x) * p.nt + t;
+            const float* parts = p.partials + tile_id * S * (static_cast<int64_t>(p.nt) * kCT);
+            float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), u4 = g4;
+#pragma unroll 4
+            for (int sp = 0; sp < S; ++sp) {
+                const float* row = parts + (static_cast<int64_t>(sp) * p.nt + t) * kCT;
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(row + q4));
+                const float4 b = __ldcg(reinterpret_cast<const float4*>(row + kTileBytes + q4));
+                g4.x += a.x; g4.y += a.y; g4.z += a.z; g4.w += a.w;
+                u4.x += b.x; u4.y += b.y; u4.z += b.z; u4.w += b.w;
+            }
+            const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int cb = bx * kTileBytes + q4 + j;
+                if (cb >= p.R || tok >= p.M) continue;
+                float g = fmaf(p.alpha, gv[j], 0.0f), u = fmaf(p.alpha, uv[j], 0.0f);
+                if (p.bias != nullptr) {
+                    g += p.bias[cb];
+                    u += p.bias[p.R + cb];
+                }
+                if (p.lora.p != nullptr) {
+                    g += lora_term(p.lora, tok, cb, p.N);
+                    u += lora_term(p.lora, tok, p.R + cb, p.N);
+                }
+                p.y[static_cast<int64_t>(tok) * p.R + cb] = g / (1.0f + expf(-g)) * u;
+            }
+        }
+        return;
+    }
+    const int64_t total = static_cast<int64_t>(tiles_x) * tiles_y * p.nt * kQuads;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
         const int q4 = static_cast<int>(i % kQuads) * 4;
         const int64_t rest = i / kQuads;
@@ -852,6 +897,46 @@ __global__ void x_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __r
     o.z = pack_bf16(b.x, b.y);
     o.w = pack_bf16(b.z, b.w);
     reinterpret_cast<uint4*>(xb)[i] = o;
+}
+
+// RMSNorm.forwardInto (RMSNorm.kt:71-90) of each x row, then bf16: one block
+// per row (K % 8 == 0), x * (1 / sqrt(mean(x^2) + eps)) * w rounded once.
+__global__ void __launch_bounds__(256) x_to_bf16_norm_kernel(const float* __restrict__ x,
+                                                             const float* __restrict__ w, float eps,
+                                                             __nv_bfloat16* __restrict__ xb, int K) {
+    dev::pdl_launch_dependents();
+    dev::pdl_wait();  // x is the previous kernel's output
+    __shared__ float red[8];
+    const float* xr = x + static_cast<int64_t>(blockIdx.x) * K;
+    float ss = 0.0f;
+    for (int i = 4 * threadIdx.x; i < K; i += 4 * 256) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(xr + i));
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float r = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
+    uint4* out = reinterpret_cast<uint4*>(xb + static_cast<int64_t>(blockIdx.x) * K);
+    for (int i = 8 * threadIdx.x; i < K; i += 8 * 256) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(xr + i));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(xr + i + 4));
+        const float4 wa = __ldg(reinterpret_cast<const float4*>(w + i));
+        const float4 wb = __ldg(reinterpret_cast<const float4*>(w + i + 4));
+        uint4 o;
+        o.x = pack_bf16(a.x * r * wa.x, a.y * r * wa.y);
+        o.y = pack_bf16(a.z * r * wa.z, a.w * r * wa.w);
+        o.z = pack_bf16(b.x * r * wb.x, b.y * r * wb.y);
+        o.w = pack_bf16(b.z * r * wb.z, b.w * r * wb.w);
+        out[i / 8] = o;
+    }
 }
 
 // INT4 weights with the 32-row swizzled TMA descriptor take gemm_ts_kernel up
@@ -936,6 +1021,12 @@ bool gemm_tc_supported(const QView& w, int32_t m, const float* a) {
     return w.rows % 8 == 0 && w.group_size % 32 == 0 && w.columns % 32 == 0;
 }
 
+bool gemm_swiglu_fused(const QView& w, int32_t m, int sm_count) {
+    if (!gemm_tc_supported(w, m, nullptr) || w.bits != 4 || w.columns != 2 * w.bytes_per_row) return false;
+    const int S = splits_for(w, m, sm_count);
+    return S > 1 && nt_for(w, m) * S >= kReduceKernelMin;
+}
+
 size_t gemm_tc_workspace_bytes(const QView& w, int32_t m, int sm_count) {
     const int S = splits_for(w, m, sm_count);
     size_t bytes = kWorkspaceReservedBytes + x_bytes(w, m);
@@ -953,9 +1044,13 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
         return cudaErrorInvalidValue;
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(ws + kWorkspaceReservedBytes);
+    if (a.swiglu && !gemm_swiglu_fused(w, a.m, sm_count)) return cudaErrorInvalidValue;
     const int64_t n8 = static_cast<int64_t>(a.m) * w.rows / 8;
-    cudaError_t e = launch_chained(x_to_bf16_kernel, dim3(static_cast<unsigned>((n8 + 255) / 256)), dim3(256), 0, s,
-                                   a.a, xb, n8);
+    cudaError_t e = a.norm_weight != nullptr
+                        ? launch_chained(x_to_bf16_norm_kernel, dim3(static_cast<unsigned>(a.m)), dim3(256), 0, s,
+                                         a.a, a.norm_weight, a.norm_eps, xb, w.rows)
+                        : launch_chained(x_to_bf16_kernel, dim3(static_cast<unsigned>((n8 + 255) / 256)), dim3(256),
+                                         0, s, a.a, xb, n8);
     if (e != cudaSuccess) return e;
 
     GemmParams p{};
@@ -986,6 +1081,7 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
     p.tickets = reinterpret_cast<int32_t*>(ws + kGemmTicketOffset);
     p.partials = reinterpret_cast<float*>(ws + kWorkspaceReservedBytes + x_bytes(w, a.m));
     p.reduce_kernel = S > 1 && p.nt * S >= kReduceKernelMin ? 1 : 0;
+    p.swiglu = a.swiglu;
 
     alignas(64) CUtensorMap tmap_x;
     if (!encode_tmap_2d(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, static_cast<uint64_t>(w.rows),
@@ -1002,7 +1098,7 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
     e = launch_chained(kernel, grid, dim3(ts ? kTsThreads : kThreads), smem, s, ts ? *w.tmap_mma : *w.tmap_raw64,
                        tmap_x, p);
     if (e != cudaSuccess || !p.reduce_kernel) return e;
-    const int64_t quads = static_cast<int64_t>(grid.x) * grid.y * p.nt * (w.bits == 4 ? 64 : 32);
+    const int64_t quads = static_cast<int64_t>(grid.x) * grid.y * p.nt * (p.swiglu ? 32 : w.bits == 4 ? 64 : 32);
     const int blocks = static_cast<int>(std::min<int64_t>((quads + 255) / 256, static_cast<int64_t>(sm_count) * 8));
     return launch_chained(w.bits == 4 ? split_reduce_kernel<4> : split_reduce_kernel<8>, dim3(blocks), dim3(256), 0,
                           s, p, static_cast<int>(grid.x), static_cast<int>(grid.y), S);

@@ -321,6 +321,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     int done = 0;
     int gi = g_first;
     int group_end = min((gi + 1) * p.gs, r_end);
+    const bool one_stage_groups = p.gs == kRowsPerStage;
     for (int st = 0; st < n_stages; ++st) {
         const int slot = st & (kStages - 1);
         if (ok) {
@@ -376,8 +377,13 @@ __global__ void __launch_bounds__(kThreads, 2)
                 imma_16832_s8(e[kJ - 1], w0.z, w0.w, w1.z, w1.w, l0, l1);
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty + 8 * slot);
+        // Release the stage once every lane of this warp has read it; with groups
+        // of one stage only after the group epilogue below, which reads the
+        // group's scale slot -- the slot the refill of stage st + NS - 1 reuses.
+        if (!one_stage_groups) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + 8 * slot);
+        }
         if (r_begin + (st + 1) * kRowsPerStage >= group_end) {
             // Group epilogue.  C of lane (g, t): c[j][0..1] = D[g][2t..2t+1] (low
             // nibbles, byte 2u + 0/1, part t / 2: xh or xm), c[j][2..3] the high
@@ -425,6 +431,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             sx = 0;
             ++gi;
             group_end = min((gi + 1) * p.gs, r_end);
+        }
+        if (one_stage_groups) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + 8 * slot);
         }
     }
     // After a timeout: wait (bounded) for this slice's copies still in flight

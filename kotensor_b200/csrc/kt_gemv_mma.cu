@@ -462,6 +462,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     int done = 0;     // stages whose copies this lane saw complete
     int gi = g_first;
     int group_end = min((gi + 1) * p.gs, r_end);
+    const bool one_stage_groups = p.gs == kRowsPerStage;
     for (int st = 0; st < n_stages; ++st) {
         const int slot = st & (kStages - 1);
         if (ok) {
@@ -504,8 +505,13 @@ __global__ void __launch_bounds__(kThreads, 2)
                 w[i] = *reinterpret_cast<const uint2*>(stage + ks * kStep * kTileBytes + soff[i]);
             mma_step(c, w, b0, b1);
         }
-        __syncwarp();  // every lane of this warp has read the stage
-        if (lane == 0) mbar_arrive(empty + 8 * slot);
+        // Release the stage once every lane of this warp has read it; with groups
+        // of one stage only after the group epilogue below, which reads the
+        // group's scale slot -- the slot the refill of stage st + NS reuses.
+        if (!one_stage_groups) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + 8 * slot);
+        }
         rs += chunk_sum[st * M + ttok];
         if (r_begin + (st + 1) * kRowsPerStage >= group_end) {
             // Group epilogue for token t:
@@ -545,6 +551,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             rs = 0.0f;
             ++gi;
             group_end = min((gi + 1) * p.gs, r_end);
+        }
+        if (one_stage_groups) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + 8 * slot);
         }
     }
     // After a timeout: wait (bounded) for this slice's copies still in flight

@@ -194,7 +194,8 @@ struct MatmulArgs {
     int32_t swiglu = 0;
     // RMSNorm of the input row before the product (RMSNorm.forwardInto,
     // RMSNorm.kt:71-90): a is read as a * (1 / sqrt(mean(a^2) + eps)) * norm_weight
-    // (norm_weight NULL: off; the INT4 GEMVs: m = 1 integer, m = 2..8 fp16 products).
+    // (norm_weight NULL: off; the INT4 GEMVs: m = 1 integer, m = 2..8 fp16
+    // products; the tcgen05 GEMM: in its bf16 pre-pass).
     const float* norm_weight = nullptr;
     float norm_eps = 0.0f;
 };
@@ -237,6 +238,9 @@ cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, 
 // ---- kt_gemm_tc.cu  (INT4, m >= 9: bf16 tcgen05 MMAs, TMEM accumulators)
 bool gemm_tc_supported(const QView& w, int32_t m, const float* a);
 size_t gemm_tc_workspace_bytes(const QView& w, int32_t m, int sm_count);
+// The GEMM forms silu(gate) * up in its split-K reduction for this INT4 gate | up
+// weight at this m (MatmulArgs::swiglu); elsewhere the caller runs kt_silu_mul_rows.
+bool gemm_swiglu_fused(const QView& w, int32_t m, int sm_count);
 cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& args, int sm_count, cudaStream_t s, void* workspace,
                            size_t workspace_bytes);
 

@@ -511,13 +511,14 @@ def test_int4_gemv_with_outlier_channels(kt, oracle, k, n, factor, count):
 
 
 @pytest.mark.parametrize("k,h", [(896, 4864), (4096, 14336), (2048, 5632), (768, 2048), (512, 1024)])
-@pytest.mark.parametrize("m", [1, 3])
+@pytest.mark.parametrize("m", [1, 3, 16, 64])
 def test_swiglu_epilogue_equals_matmul_then_silu(kt, oracle, k, h, m):
     """kt_qmatmul_swiglu on a fused gate | up weight [K x 2H]: at m = 1 the
     silu(gate) * up product is formed in the INT4 GEMV's epilogue (every
-    split-K route: one CTA per tile, clusters, partials in global memory) and
+    split-K route: one CTA per tile, clusters, partials in global memory), at
+    m >= 9 in the tcgen05 GEMM's split-K reduction where the GEMM splits K; it
     must equal kt_qmatmul followed by kt_silu_mul_rows bit for bit; other m take
-    that route themselves.  Both within the fp32 tolerance of the oracle."""
+    that route themselves.  Within the tolerance of the path against the oracle."""
     import ctypes
     from kotensor_b200 import _lib
     lib = kt.load_library()
@@ -543,21 +544,24 @@ def test_swiglu_epilogue_equals_matmul_then_silu(kt, oracle, k, h, m):
     g_u = oracle.multiply_quantized(a, ref_t, threads=8) + bias[None, :]
     g, u = g_u[:, :h].astype(np.float64), g_u[:, h:].astype(np.float64)
     ref = g / (1.0 + np.exp(-g)) * u
-    assert rel_err(got.cpu().numpy(), ref) <= TOL_FP32
+    assert rel_err(got.cpu().numpy(), ref) <= tol_for(qt, m)
     assert kt.Context.get().take_error() == 0
 
 
 @pytest.mark.parametrize("bits,k,n", [(4, 896, 1152), (4, 4096, 6144), (4, 896, 9728), (4, 4096, 28672),
                                       (8, 768, 2304)])
-@pytest.mark.parametrize("m", [1, 3, 6])
+@pytest.mark.parametrize("m", [1, 3, 6, 16])
 @pytest.mark.parametrize("swiglu", [False, True])
 def test_rmsnorm_prologue_matches_rmsnorm_then_matmul(kt, oracle, bits, k, n, m, swiglu):
     """kt_rmsnorm_qmatmul(_swiglu): RMSNorm(x) . W + bias (then silu(gate) * up).
     On INT4 (m = 1 integer GEMV, m = 3 and 6 fp16 GEMV, one and two token
     groups) the norm is applied while the GEMV stages x (each CTA sums the
-    rows' squares itself); INT8 m > 1: kt_rmsnorm then the matmul.  Within
-    1e-5 of the separate kernels (the squares are added in another order) and
-    within the fp32 tolerance of the oracle; accumulate into c included."""
+    rows' squares itself), at m = 16 in the tcgen05 GEMM's bf16 pre-pass;
+    INT8 m = 2..8: kt_rmsnorm then the matmul.  Within 1e-5 of the separate
+    kernels on the fp32 paths (the squares are added in another order; bf16
+    tolerance on the GEMM, where a last-bit change of the scale can move a
+    bf16 rounding) and within the path's tolerance of the oracle; accumulate
+    into c included."""
     import ctypes
     from kotensor_b200 import _lib
     lib = kt.load_library()
@@ -588,7 +592,8 @@ def test_rmsnorm_prologue_matches_rmsnorm_then_matmul(kt, oracle, bits, k, n, m,
     else:
         _lib.check(lib.kt_rmsnorm_qmatmul(h_, qt.handle, p(x), p(nw), 1e-6, p(xn), p(got), m, 1, p(bias), s))
     torch.cuda.synchronize()
-    assert ((got - want).abs().max() / want.abs().max()).item() <= 1e-5
+    tol = tol_for(qt, m)
+    assert ((got - want).abs().max() / want.abs().max()).item() <= (1e-5 if tol == TOL_FP32 else tol)
     # against the oracle: RMSNorm in float64, the quantized product
     xd = xh.astype(np.float64)
     xnh = (xd / np.sqrt((xd * xd).mean(axis=1, keepdims=True) + 1e-6) * nwh).astype(np.float32)
@@ -598,7 +603,7 @@ def test_rmsnorm_prologue_matches_rmsnorm_then_matmul(kt, oracle, bits, k, n, m,
         ref = g / (1.0 + np.exp(-g)) * u
     else:
         ref = c0.cpu().numpy() + y
-    assert rel_err(got.cpu().numpy(), ref) <= TOL_FP32
+    assert rel_err(got.cpu().numpy(), ref) <= tol
     assert kt.Context.get().take_error() == 0
 
 
