@@ -1876,9 +1876,314 @@ cudaError_t launch_staged_attention(dim3 grid, int group, cudaStream_t s, const 
 #undef KT_STAGED_CASE
 }
 
+// Causal attention for a prompt on tensor cores, flash style: one block per (kv
+// head, tile of 64 / G query rows of one sequence) walks the 64-position spans
+// up to the tile's last row with a running maximum and sum per query vector
+// (online softmax), so no partials are written and no merge runs.  Both
+// products run on mma.sync.m16n8k8 TF32 (operands rounded to 10-bit mantissas
+// with cvt.rna, fp32 accumulation); used where the prompt's matmuls already
+// run on the bf16 tensor-core GEMM (9 or more rows), whose tolerance covers the
+// rounding.  Warp w: query vectors 16 (w % 4) .. + 15 (vector r G + g: row r,
+// head g of the group), their fragments held in registers for the whole block;
+// for the scores positions 32 (w / 4) .. + 31 of the span, for the weighted
+// values dims (w / 4) HD / 2 .. + HD / 2.  The two warps of a row block
+// exchange their row maxima through shared memory each span and their sums at
+// the end.  Key and value tiles come in by 2-D TMA copies (boxes of 32 floats x
+// 64 positions, 128-byte swizzle: fragment reads hit distinct banks), double-
+// buffered (span s + 2 is copied while s + 1 is used); value rows past the last
+// position of the tile are zeroed (their probabilities are 0, but 0 * stale
+// data could be NaN).  Heavy tiles (late rows, many spans) are scheduled first.
+// Waits on the copies are bounded.
+template <int G, int HD>
+struct PrefillFlash {
+    static constexpr int QT = 64 / G;       // query rows per block
+    static constexpr int QV = QT * G;       // query vectors per block (<= 64)
+    static constexpr int kBoxes = HD / 32;  // TMA boxes per tile (32 floats = 128 bytes wide)
+    static constexpr int kStage = kSpan * HD;  // floats of one key or value tile
+    static constexpr int kPp = kSpan + 4;   // floats between rows of probabilities
+    static constexpr int kQP = 64 * HD > 64 * kPp ? 64 * HD : 64 * kPp;  // staged queries, then probabilities
+    __host__ __device__ static constexpr size_t smem_bytes() {
+        return 1024 + sizeof(float) * (4 * static_cast<size_t>(kStage) + kQP + 2 * 2 * 64);
+    }
+};
+
+// Offset (floats) of element (row, col) of a tile stored as kBoxes TMA boxes of
+// 64 rows x 32 floats with the 128-byte swizzle (16-byte chunk c of row r at
+// chunk c ^ (r & 7)).
+__device__ __forceinline__ int swz(int row, int col) {
+    return (col >> 5) * (kSpan * 32) + row * 32 + ((((col & 31) >> 2) ^ (row & 7)) << 2) + (col & 3);
+}
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int G, int HD>
+__global__ void __launch_bounds__(kThreads) attention_prefill_flash_kernel(
+    const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v, const float* __restrict__ q,
+    float* __restrict__ ctx, int heads, int kv_heads, int max_seq, int layer, float scale, int q_stride,
+    const int32_t* __restrict__ pos, int rows_per_seq, int64_t cache_rows_per_seq, int32_t* __restrict__ err) {
+    using S = PrefillFlash<G, HD>;
+    constexpr int QT = S::QT, QV = S::QV;
+    static_assert(kThreads == 256 && QV <= 64 && kSpan == 64, "8 warps over 64 query vectors x 64 positions");
+    extern __shared__ unsigned char smem_raw[];
+    float* base = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    float* ks = base;                        // [2][kBoxes][64][32] swizzled
+    float* vs = ks + 2 * S::kStage;          // [2][kBoxes][64][32] swizzled
+    float* qs = vs + 2 * S::kStage;          // [QT][G * HD] staged queries, then ps [64][kPp]
+    float* ps = qs;
+    float* red = qs + S::kQP;                // [2][2][64]: row maxima, then row sums, per half
+    __shared__ __align__(8) uint64_t bars[3];  // query, span stage 0, span stage 1
+    dev::pdl_wait();  // q and the cache rows come from the previous kernels
+    dev::pdl_launch_dependents();
+    const int kvh = blockIdx.x;
+    const int tile = gridDim.y - 1 - blockIdx.y;  // heavy tiles first
+    const int tiles_per_seq = (rows_per_seq + QT - 1) / QT;
+    const int seq = tile / tiles_per_seq;
+    const int r0 = (tile - seq * tiles_per_seq) * QT;  // first row of the tile inside its sequence
+    const int nr = min(QT, rows_per_seq - r0);
+    const int p0 = *pos;
+    const int last = p0 + r0 + nr - 1;  // the position of the tile's last row
+    const int n_spans = last / kSpan + 1;
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    // first cache row (of the 2-D [rows][HD] view) of this sequence, layer and kv head
+    const int cache_row0 = static_cast<int>(seq * cache_rows_per_seq + (static_cast<int64_t>(layer) * kv_heads + kvh) * max_seq);
+    const int64_t row0 = static_cast<int64_t>(seq) * rows_per_seq + r0;  // global row of the tile's first row
+    const uint32_t bar_q = dev::smem_u32(&bars[0]);
+    if (tid == 0) {
+        for (int i = 0; i < 3; ++i) dev::mbar_init(dev::smem_u32(&bars[i]), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    // span sp's key and value tiles into stage sp & 1 (one thread)
+    auto issue_span = [&](int sp) {
+        const int st = sp & 1;
+        const uint32_t bar = dev::smem_u32(&bars[1 + st]);
+        dev::mbar_expect_tx(bar, 2u * S::kStage * sizeof(float));
+#pragma unroll
+        for (int b = 0; b < S::kBoxes; ++b) {
+            dev::tma_load_2d(dev::smem_u32(ks + st * S::kStage + b * kSpan * 32), &tmap_k, 32 * b,
+                             cache_row0 + sp * kSpan, bar);
+            dev::tma_load_2d(dev::smem_u32(vs + st * S::kStage + b * kSpan * 32), &tmap_v, 32 * b,
+                             cache_row0 + sp * kSpan, bar);
+        }
+    };
+    constexpr uint32_t q_row_bytes = G * HD * sizeof(float);
+    if (warp == 0) {
+        if (lane == 0) {
+            dev::mbar_expect_tx(bar_q, nr * q_row_bytes);
+            issue_span(0);
+            if (n_spans > 1) issue_span(1);
+        }
+        __syncwarp();
+        for (int r = lane; r < nr; r += 32)
+            dev::bulk_load(dev::smem_u32(qs + r * G * HD), q + (row0 + r) * q_stride + static_cast<int64_t>(kvh) * G * HD,
+                           q_row_bytes, bar_q);
+    }
+    int issued = n_spans > 1 ? 2 : 1;  // spans whose copies were issued (thread 0's count)
+    bool ok = dev::mbar_wait_bounded(bar_q, 0);
+    if (__syncthreads_or(!ok)) {
+        if (tid == 0) {
+            atomicOr(err, 1);
+            dev::mbar_wait_bounded(bar_q, 0);
+            for (int sp = 0; sp < issued; ++sp) dev::mbar_wait_bounded(dev::smem_u32(&bars[1 + (sp & 1)]), 0);
+        }
+        return;
+    }
+    const int mt = warp & 3, half = warp >> 2;
+    const int qa = 16 * mt + g;  // this lane's query vectors qa and qa + 8
+    // this warp's query fragments for every k-step, tf32 (vectors past the tile's rows: zeros)
+    uint32_t qf[HD / 8][4];
+    {
+        const bool v0 = qa < nr * G, v8 = qa + 8 < nr * G;
+#pragma unroll
+        for (int ks8 = 0; ks8 < HD / 8; ++ks8) {
+            const int d = 8 * ks8 + t;
+            qf[ks8][0] = v0 ? to_tf32(qs[qa * HD + d]) : 0u;
+            qf[ks8][1] = v8 ? to_tf32(qs[(qa + 8) * HD + d]) : 0u;
+            qf[ks8][2] = v0 ? to_tf32(qs[qa * HD + d + 4]) : 0u;
+            qf[ks8][3] = v8 ? to_tf32(qs[(qa + 8) * HD + d + 4]) : 0u;
+        }
+    }
+    constexpr int kNt = HD / 16;  // n-tiles of 8 dims per warp for the weighted values
+    float o[kNt][4];
+#pragma unroll
+    for (int nt = 0; nt < kNt; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
+    float m_run[2] = {-FLT_MAX, -FLT_MAX}, l_run[2] = {0.0f, 0.0f};
+    int lim[2];  // the last position row qa + 8 h sees (-1: no such row)
+    bool row_ok[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int qi = qa + 8 * h, r = qi / G;
+        row_ok[h] = qi < QV && r < nr;
+        lim[h] = row_ok[h] ? p0 + r0 + r : -1;
+    }
+    const uint32_t pair_bar = 1 + mt;  // named barrier of warps mt and mt + 4
+    for (int sp = 0; sp < n_spans; ++sp) {
+        const int st = sp & 1;
+        const int j0 = sp * kSpan;
+        const int n = min(kSpan, last + 1 - j0);
+        ok = dev::mbar_wait_bounded(dev::smem_u32(&bars[1 + st]), (sp >> 1) & 1);
+        if (__syncthreads_or(!ok)) {  // (the first one also ends every warp's reads of qs)
+            if (tid == 0) {
+                atomicOr(err, 1);
+                for (int s2 = sp; s2 < issued; ++s2)
+                    dev::mbar_wait_bounded(dev::smem_u32(&bars[1 + (s2 & 1)]), (s2 >> 1) & 1);
+            }
+            return;
+        }
+        float* kst = ks + st * S::kStage;
+        float* vst = vs + st * S::kStage;
+        // the span's keys and values to tf32 in place (the swizzle keeps rows whole:
+        // 32 floats of a box row are one row); value rows past n: zeros
+        for (int i = tid; i < S::kStage / 4; i += kThreads) {
+            const int row = (i >> 3) & (kSpan - 1);  // box row of float4 i
+            float4* kp = reinterpret_cast<float4*>(kst) + i;
+            float4* vp = reinterpret_cast<float4*>(vst) + i;
+            float4 k4 = *kp;
+            k4 = make_float4(__uint_as_float(to_tf32(k4.x)), __uint_as_float(to_tf32(k4.y)),
+                             __uint_as_float(to_tf32(k4.z)), __uint_as_float(to_tf32(k4.w)));
+            *kp = k4;
+            float4 v4 = *vp;
+            v4 = row < n ? make_float4(__uint_as_float(to_tf32(v4.x)), __uint_as_float(to_tf32(v4.y)),
+                                       __uint_as_float(to_tf32(v4.z)), __uint_as_float(to_tf32(v4.w)))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+            *vp = v4;
+        }
+        __syncthreads();
+        // scores S = Q K^T: query vectors 16 mt .. + 15, positions 32 half .. + 31 of the span
+        float acc[4][4];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+        {
+            const uint32_t* kb = reinterpret_cast<const uint32_t*>(kst);
+#pragma unroll
+            for (int ks8 = 0; ks8 < HD / 8; ++ks8) {
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) {
+                    const int key = 32 * half + 8 * nt + g;
+                    mma_tf32(acc[nt], qf[ks8][0], qf[ks8][1], qf[ks8][2], qf[ks8][3], kb[swz(key, 8 * ks8 + t)],
+                             kb[swz(key, 8 * ks8 + t + 4)]);
+                }
+            }
+        }
+        // masked, scaled scores and this half's row maxima
+        float mx[2] = {-FLT_MAX, -FLT_MAX};
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const int jj = 32 * half + 8 * nt + 2 * t + c;
+                    const bool v = jj < n && j0 + jj <= lim[h];
+                    const float sv = v ? acc[nt][2 * h + c] * scale : -FLT_MAX;
+                    acc[nt][2 * h + c] = sv;
+                    mx[h] = fmaxf(mx[h], sv);
+                }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+            if (t == 0) red[half * 64 + qa + 8 * h] = mx[h];
+        }
+        asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+        float alpha[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float other = red[(1 - half) * 64 + qa + 8 * h];
+            const float m_new = fmaxf(m_run[h], fmaxf(mx[h], other));
+            // the running values are rescaled to the new maximum (nothing seen yet: nothing to rescale)
+            alpha[h] = m_run[h] > -FLT_MAX ? expf(m_run[h] - m_new) : 1.0f;
+            float sum = 0.0f;
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const float sv = acc[nt][2 * h + c];
+                    const float e = sv > -FLT_MAX ? expf(sv - m_new) : 0.0f;
+                    sum += e;
+                    const int jj = 32 * half + 8 * nt + 2 * t + c;
+                    *reinterpret_cast<uint32_t*>(ps + (qa + 8 * h) * S::kPp + jj) = to_tf32(e);
+                }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            l_run[h] = l_run[h] * alpha[h] + sum;
+            m_run[h] = m_new;
+        }
+#pragma unroll
+        for (int nt = 0; nt < kNt; ++nt) {
+            o[nt][0] *= alpha[0];
+            o[nt][1] *= alpha[0];
+            o[nt][2] *= alpha[1];
+            o[nt][3] *= alpha[1];
+        }
+        asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");  // both halves of P written
+        // weighted values O += P V: query vectors 16 mt .. + 15, dims HD / 2 half .. + HD / 2
+        {
+            const uint32_t* pa0 = reinterpret_cast<const uint32_t*>(ps + qa * S::kPp + t);
+            const uint32_t* pa8 = pa0 + 8 * S::kPp;
+            const uint32_t* vb = reinterpret_cast<const uint32_t*>(vst);
+            const int kend = (n + 7) & ~7;  // positions past n carry probability 0
+            for (int k0 = 0; k0 < kend; k0 += 8) {
+                const uint32_t a0 = pa0[k0], a1 = pa8[k0], a2 = pa0[k0 + 4], a3 = pa8[k0 + 4];
+#pragma unroll
+                for (int nt = 0; nt < kNt; ++nt) {
+                    const int d = (HD / 2) * half + 8 * nt + g;
+                    mma_tf32(o[nt], a0, a1, a2, a3, vb[swz(k0 + t, d)], vb[swz(k0 + t + 4, d)]);
+                }
+            }
+        }
+        __syncthreads();  // every warp is done with this stage, ps and red
+        if (tid == 0 && sp + 2 < n_spans) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_span(sp + 2);
+            ++issued;
+        }
+    }
+    // every row's sum over both halves, then O / l into the context rows
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        if (t == 0) red[128 + half * 64 + qa + 8 * h] = l_run[h];
+    asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        if (!row_ok[h]) continue;
+        const int qi = qa + 8 * h;
+        const int r = qi / G, gh = qi - r * G;
+        const float inv = 1.0f / (red[128 + qi] + red[128 + 64 + qi]);
+        float* out = ctx + ((row0 + r) * heads + kvh * G + gh) * HD + (HD / 2) * half;
+#pragma unroll
+        for (int nt = 0; nt < kNt; ++nt)
+            *reinterpret_cast<float2*>(out + 8 * nt + 2 * t) = make_float2(o[nt][2 * h] * inv, o[nt][2 * h + 1] * inv);
+    }
+}
+
 bool prefill_attention_enabled() {
     static const bool on = [] {
         const char* v = std::getenv("KT_ATTN_PREFILL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// The TF32 tensor-core (flash) prefill kernel for blocks of 9 rows or more
+// (KT_ATTN_PREFILL_MMA=0: the fp32 kernel and merge everywhere, for comparison).
+bool prefill_mma_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("KT_ATTN_PREFILL_MMA");
         return !(v && v[0] == '0');
     }();
     return on;
@@ -1905,6 +2210,59 @@ cudaError_t launch_prefill_attention_g(int rows, int rows_per_seq, int splits, c
     return launch_pdl(attention_prefill_kernel<G, HD>, dim3(kv_heads, splits, tiles), dim3(kThreads), P::smem_bytes(),
                       s, q, kc, vc, scores, heads, kv_heads, max_seq, layer, scale, q_stride, pos, rows_per_seq,
                       cache_stride, err);
+}
+
+template <int G, int HD>
+cudaError_t launch_prefill_flash_g(int rows, int rows_per_seq, cudaStream_t s, const float* q, const float* kc,
+                                   const float* vc, float* ctx, int heads, int kv_heads, int max_seq, int layer,
+                                   float scale, int q_stride, const int32_t* pos, int64_t cache_stride, int32_t* err) {
+    using F = PrefillFlash<G, HD>;
+    constexpr int kMaxDevices = 64;
+    static std::atomic<bool> done[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (!(dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire))) {
+        e = cudaFuncSetAttribute(attention_prefill_flash_kernel<G, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(F::smem_bytes()));
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < kMaxDevices) done[dev].store(true, std::memory_order_release);
+    }
+    // the caches of this call's sequences as 2-D [rows][HD] tensors, boxes of 32 floats x 64 positions
+    const int64_t rows_per_seq_cache = cache_stride / HD;
+    const int64_t cache_rows = static_cast<int64_t>(rows / rows_per_seq) * rows_per_seq_cache;
+    if (cache_rows > INT32_MAX) return cudaErrorInvalidValue;
+    alignas(64) CUtensorMap tk, tv;
+    if (!encode_tmap_2d(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, kc, HD, static_cast<uint64_t>(cache_rows),
+                        HD * sizeof(float), 32, kSpan, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap_2d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, vc, HD, static_cast<uint64_t>(cache_rows),
+                        HD * sizeof(float), 32, kSpan, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    const int tiles = (rows / rows_per_seq) * ((rows_per_seq + F::QT - 1) / F::QT);
+    return launch_pdl(attention_prefill_flash_kernel<G, HD>, dim3(kv_heads, tiles), dim3(kThreads), F::smem_bytes(), s,
+                      tk, tv, q, ctx, heads, kv_heads, max_seq, layer, scale, q_stride, pos, rows_per_seq,
+                      rows_per_seq_cache, err);
+}
+
+template <int HD>
+cudaError_t launch_prefill_flash(int group, int rows, int rows_per_seq, cudaStream_t s, const float* q,
+                                 const float* kc, const float* vc, float* ctx, int heads, int kv_heads, int max_seq,
+                                 int layer, float scale, int q_stride, const int32_t* pos, int64_t cache_stride,
+                                 int32_t* err) {
+#define KT_FLASH_CASE(G_)                                                                                       \
+    return launch_prefill_flash_g<G_, HD>(rows, rows_per_seq, s, q, kc, vc, ctx, heads, kv_heads, max_seq, layer, \
+                                          scale, q_stride, pos, cache_stride, err)
+    switch (group) {
+        case 1: KT_FLASH_CASE(1);
+        case 2: KT_FLASH_CASE(2);
+        case 3: KT_FLASH_CASE(3);
+        case 4: KT_FLASH_CASE(4);
+        case 5: KT_FLASH_CASE(5);
+        case 6: KT_FLASH_CASE(6);
+        case 7: KT_FLASH_CASE(7);
+        default: KT_FLASH_CASE(8);
+    }
+#undef KT_FLASH_CASE
 }
 
 template <int HD>
@@ -1942,6 +2300,15 @@ cudaError_t launch_attention_decode(const float* q, const float* kc, const float
     // a prompt: tiles of query rows per block (the query rows copied in bulk too)
     if (rows_per_seq > 1 && prefill_attention_enabled() && aligned && group <= 8 && (head_dim == 64 || head_dim == 128) &&
         (reinterpret_cast<uintptr_t>(q) & 15) == 0 && q_stride % 4 == 0) {
+        if (rows >= 9 && prefill_mma_enabled()) {
+            // 9 rows or more: the block's matmuls run on the bf16 GEMM, whose tolerance covers the TF32 products
+            return head_dim == 64 ? launch_prefill_flash<64>(group, rows, rows_per_seq, s, q, kc, vc, ctx, heads,
+                                                             kv_heads, max_seq, layer, scale, q_stride, pos,
+                                                             cache_stride, err)
+                                  : launch_prefill_flash<128>(group, rows, rows_per_seq, s, q, kc, vc, ctx, heads,
+                                                              kv_heads, max_seq, layer, scale, q_stride, pos,
+                                                              cache_stride, err);
+        }
         const cudaError_t e =
             head_dim == 64 ? launch_prefill_attention<64>(group, rows, rows_per_seq, splits, s, q, kc, vc, scores,
                                                           heads, kv_heads, max_seq, layer, scale, q_stride, pos,
