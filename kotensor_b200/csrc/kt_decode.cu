@@ -1880,8 +1880,10 @@ cudaError_t launch_staged_attention(dim3 grid, int group, cudaStream_t s, const 
 // head, tile of 64 / G query rows of one sequence) walks the 64-position spans
 // up to the tile's last row with a running maximum and sum per query vector
 // (online softmax), so no partials are written and no merge runs.  Both
-// products run on mma.sync.m16n8k8 TF32 (operands rounded to 10-bit mantissas
-// with cvt.rna, fp32 accumulation); used where the prompt's matmuls already
+// products run on mma.sync.m16n8k8 TF32 with fp32 accumulation: queries and
+// probabilities rounded to 10-bit mantissas with cvt.rna, keys and values
+// read as their fp32 bits (the tensor core ignores the low 13 mantissa bits:
+// TF32 rounded toward zero, no conversion pass per tile); used where the prompt's matmuls already
 // run on the bf16 tensor-core GEMM (9 or more rows), whose tolerance covers the
 // rounding.  Warp w: query vectors 16 (w % 4) .. + 15 (vector r G + g: row r,
 // head g of the group), their fragments held in registers for the whole block;
@@ -1907,12 +1909,11 @@ struct PrefillFlash {
     }
 };
 
-// Offset (floats) of element (row, col) of a tile stored as kBoxes TMA boxes of
-// 64 rows x 32 floats with the 128-byte swizzle (16-byte chunk c of row r at
-// chunk c ^ (r & 7)).
-__device__ __forceinline__ int swz(int row, int col) {
-    return (col >> 5) * (kSpan * 32) + row * 32 + ((((col & 31) >> 2) ^ (row & 7)) << 2) + (col & 3);
-}
+// A key or value tile in shared memory: kBoxes TMA boxes of 64 rows x 32 floats
+// with the 128-byte swizzle, so element (row, col) sits at float
+//   (col / 32) * 64 * 32 + row * 32 + (((col % 32) / 4) ^ (row % 8)) * 4 + col % 4
+// (16-byte chunk c of row r at chunk c ^ (r & 7)); the fragment loads below
+// hoist the lane's part of that offset.
 
 __device__ __forceinline__ uint32_t to_tf32(float x) {
     uint32_t r;
@@ -2046,37 +2047,27 @@ __global__ void __launch_bounds__(kThreads) attention_prefill_flash_kernel(
         }
         float* kst = ks + st * S::kStage;
         float* vst = vs + st * S::kStage;
-        // the span's keys and values to tf32 in place (the swizzle keeps rows whole:
-        // 32 floats of a box row are one row); value rows past n: zeros
-        for (int i = tid; i < S::kStage / 4; i += kThreads) {
-            const int row = (i >> 3) & (kSpan - 1);  // box row of float4 i
-            float4* kp = reinterpret_cast<float4*>(kst) + i;
-            float4* vp = reinterpret_cast<float4*>(vst) + i;
-            float4 k4 = *kp;
-            k4 = make_float4(__uint_as_float(to_tf32(k4.x)), __uint_as_float(to_tf32(k4.y)),
-                             __uint_as_float(to_tf32(k4.z)), __uint_as_float(to_tf32(k4.w)));
-            *kp = k4;
-            float4 v4 = *vp;
-            v4 = row < n ? make_float4(__uint_as_float(to_tf32(v4.x)), __uint_as_float(to_tf32(v4.y)),
-                                       __uint_as_float(to_tf32(v4.z)), __uint_as_float(to_tf32(v4.w)))
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-            *vp = v4;
+        if (n < kSpan) {  // value rows past n: zeros (the swizzle keeps rows whole: a box row is 32 floats of one row)
+            for (int i = tid; i < S::kStage / 4; i += kThreads)
+                if (((i >> 3) & (kSpan - 1)) >= n) reinterpret_cast<float4*>(vst)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            __syncthreads();
         }
-        __syncthreads();
         // scores S = Q K^T: query vectors 16 mt .. + 15, positions 32 half .. + 31 of the span
         float acc[4][4];
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
         {
-            const uint32_t* kb = reinterpret_cast<const uint32_t*>(kst);
+            // key row 32 half + 8 nt + g (row & 7 = g), dims 8 ks8 + t and + 4: box ks8 / 4,
+            // chunks 2 (ks8 % 4) and + 1, each XOR g
+            const uint32_t* krow = reinterpret_cast<const uint32_t*>(kst) + (32 * half + g) * 32 + t;
 #pragma unroll
             for (int ks8 = 0; ks8 < HD / 8; ++ks8) {
+                const uint32_t* k0p = krow + (ks8 >> 2) * (kSpan * 32) + (((2 * (ks8 & 3)) ^ g) << 2);
+                const uint32_t* k4p = krow + (ks8 >> 2) * (kSpan * 32) + (((2 * (ks8 & 3) + 1) ^ g) << 2);
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt) {
-                    const int key = 32 * half + 8 * nt + g;
-                    mma_tf32(acc[nt], qf[ks8][0], qf[ks8][1], qf[ks8][2], qf[ks8][3], kb[swz(key, 8 * ks8 + t)],
-                             kb[swz(key, 8 * ks8 + t + 4)]);
-                }
+                for (int nt = 0; nt < 4; ++nt)
+                    mma_tf32(acc[nt], qf[ks8][0], qf[ks8][1], qf[ks8][2], qf[ks8][3], k0p[nt * 8 * 32],
+                             k4p[nt * 8 * 32]);
             }
         }
         // masked, scaled scores and this half's row maxima
@@ -2135,15 +2126,24 @@ __global__ void __launch_bounds__(kThreads) attention_prefill_flash_kernel(
         {
             const uint32_t* pa0 = reinterpret_cast<const uint32_t*>(ps + qa * S::kPp + t);
             const uint32_t* pa8 = pa0 + 8 * S::kPp;
-            const uint32_t* vb = reinterpret_cast<const uint32_t*>(vst);
+            // value rows k0 + t and k0 + t + 4 (row & 7 = t, t + 4), dim (HD / 2) half + 8 nt + g:
+            // box half HD / 64 + nt / 4, chunk 2 (nt % 4) + g / 4 XOR the row's low bits, element g % 4
+            const uint32_t* vrow =
+                reinterpret_cast<const uint32_t*>(vst) + half * (HD / 64) * (kSpan * 32) + t * 32 + (g & 3);
+            int vo0[4], vo1[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                vo0[j] = ((2 * j + (g >> 2)) ^ t) << 2;
+                vo1[j] = (((2 * j + (g >> 2)) ^ (t + 4)) << 2) + 4 * 32;
+            }
             const int kend = (n + 7) & ~7;  // positions past n carry probability 0
             for (int k0 = 0; k0 < kend; k0 += 8) {
                 const uint32_t a0 = pa0[k0], a1 = pa8[k0], a2 = pa0[k0 + 4], a3 = pa8[k0 + 4];
+                const uint32_t* vk = vrow + k0 * 32;
 #pragma unroll
-                for (int nt = 0; nt < kNt; ++nt) {
-                    const int d = (HD / 2) * half + 8 * nt + g;
-                    mma_tf32(o[nt], a0, a1, a2, a3, vb[swz(k0 + t, d)], vb[swz(k0 + t + 4, d)]);
-                }
+                for (int nt = 0; nt < kNt; ++nt)
+                    mma_tf32(o[nt], a0, a1, a2, a3, vk[(nt >> 2) * (kSpan * 32) + vo0[nt & 3]],
+                             vk[(nt >> 2) * (kSpan * 32) + vo1[nt & 3]]);
             }
         }
         __syncthreads();  // every warp is done with this stage, ps and red
