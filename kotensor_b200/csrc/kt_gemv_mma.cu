@@ -697,12 +697,15 @@ int min_splits(int K, int m) {
 }
 
 // K-splits per column tile: enough CTAs (over every token group) to fill every
-// SM slot in one wave (at least one stage per slice), never fewer than min_splits.
+// SM slot in one wave (at least one stage per slice), at most kMaxSplits (the
+// tile's last CTA reads every split's partial tile: 37 splits of a 4-token tile
+// are 150 KB), never fewer than min_splits.
+constexpr int kMaxSplits = 16;
 int choose_splits(int R, int K, int m, int sm_count) {
     const int tiles = tiles_of(R) * groups_of(m);
     const int slots = blocks_per_sm() * sm_count;
     const int k_stages = K / kRowsPerStage;
-    int s = std::max(1, slots / tiles);
+    int s = std::min(kMaxSplits, std::max(1, slots / tiles));
     s = std::min(s, std::max(1, k_stages / kPairs));
     const int o = mma_overrides().splits.load(std::memory_order_relaxed);
     if (o >= 1) s = o;

@@ -250,3 +250,61 @@ def test_fused_decode_attention_rejects_other_head_dims(kt):
     st = lib.kt_attention_rope_decode(kt.Context.get().handle, p, 1, 32, 4, 1, 8, p, p, p, p, p, 16, 0, 0.1,
                                       ctypes.c_void_p(pos.data_ptr()), 0, None)
     assert st == _lib.KT_ERR_UNSUPPORTED
+
+
+def _causal_attention_ref(q, kc, vc, heads, kv_heads, head_dim, rows_per_seq, p0, scale):
+    """Attention.prefillInto / attendHead (Attention.kt:241-293, :295-328) in
+    float64: row r of sequence r // rows_per_seq at position p0 + r % rows_per_seq
+    attends to positions 0 .. its own of its sequence's cache (layer 0)."""
+    rows = q.shape[0]
+    g = heads // kv_heads
+    out = np.zeros((rows, heads * head_dim))
+    for r in range(rows):
+        seq, pos = r // rows_per_seq, p0 + r % rows_per_seq
+        for h in range(heads):
+            kv = h // g
+            qv = q[r, h * head_dim:(h + 1) * head_dim].astype(np.float64)
+            k = kc[seq, 0, kv, :pos + 1].astype(np.float64)
+            v = vc[seq, 0, kv, :pos + 1].astype(np.float64)
+            s = k @ qv * scale
+            e = np.exp(s - s.max())
+            out[r, h * head_dim:(h + 1) * head_dim] = (e / e.sum()) @ v
+    return out
+
+
+@pytest.mark.parametrize("heads,kv_heads,head_dim", [(32, 8, 128), (14, 2, 64), (12, 12, 64), (8, 1, 128)])
+@pytest.mark.parametrize("seqs,rows_per_seq,p0", [(1, 200, 0), (2, 37, 0), (1, 70, 50), (3, 5, 3), (1, 9, 120)])
+def test_prefill_attention_matches_float64(kt, heads, kv_heads, head_dim, seqs, rows_per_seq, p0):
+    """kt_attention_seqs on prompt blocks (rows_per_seq > 1) against a float64
+    restatement of causal attention: blocks of 9 rows or more run the flash
+    kernel on TF32 tensor cores (within 5e-3 of max|context|, inside the bf16
+    prefill tolerance), smaller ones the fp32 kernel and merge (1e-5); group
+    sizes 1, 4, 7, 8, head_dim 64 and 128, several sequences, partial query
+    tiles, a block starting after earlier positions (p0 > 0) and spans of 64
+    positions crossed."""
+    import ctypes
+    from kotensor_b200 import _lib
+    lib = kt.load_library()
+    h = kt.Context.get().handle
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rows, max_seq = seqs * rows_per_seq, 256
+    q_width, kv = heads * head_dim, kv_heads * head_dim
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(heads + 7 * rows + p0)
+    qkv = torch.randn((rows, q_width + 2 * kv), generator=gen, device="cuda")
+    cache = torch.randn((2, seqs, 1, kv_heads, max_seq, head_dim), generator=gen, device="cuda")
+    stride = kv_heads * max_seq * head_dim
+    pos = torch.tensor([p0], dtype=torch.int32, device="cuda")
+    scale = float(1.0 / np.sqrt(head_dim))
+    sc = torch.zeros(lib.kt_attention_scratch_floats(rows, heads, head_dim, max_seq), device="cuda")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    ctx = torch.full((rows, q_width), float("nan"), device="cuda")
+    _lib.check(lib.kt_attention_seqs(h, p(qkv), p(cache[0]), p(cache[1]), p(ctx), p(sc), rows, q_width + 2 * kv,
+                                     heads, kv_heads, head_dim, max_seq, 0, scale, p(pos), rows_per_seq, stride, s))
+    torch.cuda.synchronize()
+    ref = _causal_attention_ref(qkv[:, :q_width].cpu().numpy(), cache[0].cpu().numpy(), cache[1].cpu().numpy(),
+                                heads, kv_heads, head_dim, rows_per_seq, p0, scale)
+    got = ctx.cpu().numpy().astype(np.float64)
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err <= (5e-3 if rows >= 9 else 1e-5), err
+    assert kt.Context.get().take_error() == 0
