@@ -1903,7 +1903,8 @@ struct PrefillFlash {
     static constexpr int kBoxes = HD / 32;  // TMA boxes per tile (32 floats = 128 bytes wide)
     static constexpr int kStage = kSpan * HD;  // floats of one key or value tile
     static constexpr int kPp = kSpan + 4;   // floats between rows of probabilities
-    static constexpr int kQP = 64 * HD > 64 * kPp ? 64 * HD : 64 * kPp;  // staged queries, then probabilities
+    static constexpr int kQPad = HD + 4;    // floats between staged query vectors (fragment loads: bank 4g + t)
+    static constexpr int kQP = 64 * kQPad > 64 * kPp ? 64 * kQPad : 64 * kPp;  // staged queries, then probabilities
     __host__ __device__ static constexpr size_t smem_bytes() {
         return 1024 + sizeof(float) * (4 * static_cast<size_t>(kStage) + kQP + 2 * 2 * 64);
     }
@@ -1941,7 +1942,7 @@ __global__ void __launch_bounds__(kThreads) attention_prefill_flash_kernel(
     float* base = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     float* ks = base;                        // [2][kBoxes][64][32] swizzled
     float* vs = ks + 2 * S::kStage;          // [2][kBoxes][64][32] swizzled
-    float* qs = vs + 2 * S::kStage;          // [QT][G * HD] staged queries, then ps [64][kPp]
+    float* qs = vs + 2 * S::kStage;          // [64][kQPad] staged query vectors, then ps [64][kPp]
     float* ps = qs;
     float* red = qs + S::kQP;                // [2][2][64]: row maxima, then row sums, per half
     __shared__ __align__(8) uint64_t bars[3];  // query, span stage 0, span stage 1
@@ -1981,17 +1982,19 @@ __global__ void __launch_bounds__(kThreads) attention_prefill_flash_kernel(
                              cache_row0 + sp * kSpan, bar);
         }
     };
-    constexpr uint32_t q_row_bytes = G * HD * sizeof(float);
+    constexpr uint32_t q_vec_bytes = HD * sizeof(float);
     if (warp == 0) {
         if (lane == 0) {
-            dev::mbar_expect_tx(bar_q, nr * q_row_bytes);
+            dev::mbar_expect_tx(bar_q, nr * G * q_vec_bytes);
             issue_span(0);
             if (n_spans > 1) issue_span(1);
         }
         __syncwarp();
-        for (int r = lane; r < nr; r += 32)
-            dev::bulk_load(dev::smem_u32(qs + r * G * HD), q + (row0 + r) * q_stride + static_cast<int64_t>(kvh) * G * HD,
-                           q_row_bytes, bar_q);
+        for (int i = lane; i < nr * G; i += 32) {  // query vector i = row i / G, head i % G of the group
+            const int r = i / G, gh = i - r * G;
+            dev::bulk_load(dev::smem_u32(qs + i * S::kQPad),
+                           q + (row0 + r) * q_stride + static_cast<int64_t>(kvh * G + gh) * HD, q_vec_bytes, bar_q);
+        }
     }
     int issued = n_spans > 1 ? 2 : 1;  // spans whose copies were issued (thread 0's count)
     bool ok = dev::mbar_wait_bounded(bar_q, 0);
@@ -2012,10 +2015,10 @@ __global__ void __launch_bounds__(kThreads) attention_prefill_flash_kernel(
 #pragma unroll
         for (int ks8 = 0; ks8 < HD / 8; ++ks8) {
             const int d = 8 * ks8 + t;
-            qf[ks8][0] = v0 ? to_tf32(qs[qa * HD + d]) : 0u;
-            qf[ks8][1] = v8 ? to_tf32(qs[(qa + 8) * HD + d]) : 0u;
-            qf[ks8][2] = v0 ? to_tf32(qs[qa * HD + d + 4]) : 0u;
-            qf[ks8][3] = v8 ? to_tf32(qs[(qa + 8) * HD + d + 4]) : 0u;
+            qf[ks8][0] = v0 ? to_tf32(qs[qa * S::kQPad + d]) : 0u;
+            qf[ks8][1] = v8 ? to_tf32(qs[(qa + 8) * S::kQPad + d]) : 0u;
+            qf[ks8][2] = v0 ? to_tf32(qs[qa * S::kQPad + d + 4]) : 0u;
+            qf[ks8][3] = v8 ? to_tf32(qs[(qa + 8) * S::kQPad + d + 4]) : 0u;
         }
     }
     constexpr int kNt = HD / 16;  // n-tiles of 8 dims per warp for the weighted values
@@ -2126,15 +2129,18 @@ __global__ void __launch_bounds__(kThreads) attention_prefill_flash_kernel(
         {
             const uint32_t* pa0 = reinterpret_cast<const uint32_t*>(ps + qa * S::kPp + t);
             const uint32_t* pa8 = pa0 + 8 * S::kPp;
-            // value rows k0 + t and k0 + t + 4 (row & 7 = t, t + 4), dim (HD / 2) half + 8 nt + g:
-            // box half HD / 64 + nt / 4, chunk 2 (nt % 4) + g / 4 XOR the row's low bits, element g % 4
+            // value rows k0 + t and k0 + t + 4 (row & 7 = t, t + 4); n-tile nt takes box
+            // half HD / 64 + nt / 4 and, of it, chunks c = nt % 4 and c + 4: column g is
+            // element g % 4 of chunk c + 4 (g / 4), XOR the row's low bits -- over the 32
+            // lanes 8 distinct chunks x 4 elements, no bank conflict (adjacent chunks c, c + 1
+            // would meet the same four chunks after the XOR with rows 0-3)
             const uint32_t* vrow =
                 reinterpret_cast<const uint32_t*>(vst) + half * (HD / 64) * (kSpan * 32) + t * 32 + (g & 3);
             int vo0[4], vo1[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                vo0[j] = ((2 * j + (g >> 2)) ^ t) << 2;
-                vo1[j] = (((2 * j + (g >> 2)) ^ (t + 4)) << 2) + 4 * 32;
+            for (int c = 0; c < 4; ++c) {
+                vo0[c] = ((c + 4 * (g >> 2)) ^ t) << 2;
+                vo1[c] = (((c + 4 * (g >> 2)) ^ (t + 4)) << 2) + 4 * 32;
             }
             const int kend = (n + 7) & ~7;  // positions past n carry probability 0
             for (int k0 = 0; k0 < kend; k0 += 8) {
@@ -2165,9 +2171,12 @@ __global__ void __launch_bounds__(kThreads) attention_prefill_flash_kernel(
         const int r = qi / G, gh = qi - r * G;
         const float inv = 1.0f / (red[128 + qi] + red[128 + 64 + qi]);
         float* out = ctx + ((row0 + r) * heads + kvh * G + gh) * HD + (HD / 2) * half;
+        // C columns 2t, 2t + 1 of n-tile nt: elements 2 (t % 2), + 1 of chunk nt % 4 + 4 (t / 2)
+        // of box nt / 4 (the column order of the weighted values above)
 #pragma unroll
         for (int nt = 0; nt < kNt; ++nt)
-            *reinterpret_cast<float2*>(out + 8 * nt + 2 * t) = make_float2(o[nt][2 * h] * inv, o[nt][2 * h + 1] * inv);
+            *reinterpret_cast<float2*>(out + 32 * (nt >> 2) + 4 * ((nt & 3) + 4 * (t >> 1)) + 2 * (t & 1)) =
+                make_float2(o[nt][2 * h] * inv, o[nt][2 * h + 1] * inv);
     }
 }
 
