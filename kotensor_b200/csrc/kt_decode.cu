@@ -2309,7 +2309,8 @@ cudaError_t launch_attention_decode(const float* q, const float* kc, const float
     // a prompt: tiles of query rows per block (the query rows copied in bulk too)
     if (rows_per_seq > 1 && prefill_attention_enabled() && aligned && group <= 8 && (head_dim == 64 || head_dim == 128) &&
         (reinterpret_cast<uintptr_t>(q) & 15) == 0 && q_stride % 4 == 0) {
-        if (rows >= 9 && prefill_mma_enabled()) {
+        if (rows >= 9 && prefill_mma_enabled() && cache_stride % head_dim == 0) {
+            // (the TMA maps view the caches as [rows][head_dim]: sequences a whole number of rows apart)
             // 9 rows or more: the block's matmuls run on the bf16 GEMM, whose tolerance covers the TF32 products
             return head_dim == 64 ? launch_prefill_flash<64>(group, rows, rows_per_seq, s, q, kc, vc, ctx, heads,
                                                              kv_heads, max_seq, layer, scale, q_stride, pos,
