@@ -273,7 +273,8 @@ def _causal_attention_ref(q, kc, vc, heads, kv_heads, head_dim, rows_per_seq, p0
 
 
 @pytest.mark.parametrize("heads,kv_heads,head_dim", [(32, 8, 128), (14, 2, 64), (12, 12, 64), (8, 1, 128)])
-@pytest.mark.parametrize("seqs,rows_per_seq,p0", [(1, 200, 0), (2, 37, 0), (1, 70, 50), (3, 5, 3), (1, 9, 120)])
+@pytest.mark.parametrize("seqs,rows_per_seq,p0", [(1, 200, 0), (2, 37, 0), (1, 70, 50), (3, 5, 3), (1, 9, 120),
+                                                 (2, 160, 96)])
 def test_prefill_attention_matches_float64(kt, heads, kv_heads, head_dim, seqs, rows_per_seq, p0):
     """kt_attention_seqs on prompt blocks (rows_per_seq > 1) against a float64
     restatement of causal attention: blocks of 9 rows or more run the flash

@@ -488,6 +488,41 @@ def test_bench_weights_gemm_against_oracle(kt, oracle, k, n, m):
     assert kt.Context.get().take_error() == 0
 
 
+@pytest.mark.parametrize("k,n", [(4096, 6144), (4096, 4096), (14336, 4096)])
+def test_llama_prefill_gemm_against_oracle(kt, oracle, k, n):
+    """The GEMM of a 1,024-token prompt block on the Llama-3-8B-shaped
+    projections bench.py's prefill runs (q|k|v, output, down: 256-token tiles,
+    the output and down products split over K and summed by the reduction
+    kernel), plus RMSNorm fused into its bf16 pre-pass, within the bf16
+    tolerance of the oracle."""
+    import ctypes
+    from kotensor_b200 import _lib
+    lib = kt.load_library()
+    m = 1024
+    rng = np.random.default_rng(k + 2 * n)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 4, 64)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, 64)
+    assert qt.matmul_path(m) == _lib.KT_PATH_TENSOR_CORE
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    y = run_matmul(kt, qt, a)
+    y_ref = oracle.multiply_quantized(a, ref_t, threads=16)
+    assert rel_err(y, y_ref) <= TOL_BF16
+    # RMSNorm in the pre-pass (kt_rmsnorm_qmatmul at m = 1024) against the float64 norm then the oracle
+    nwh = (1.0 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    x, nw = dev(a), dev(nwh)
+    out = torch.empty((m, n), device="cuda")
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    _lib.check(lib.kt_rmsnorm_qmatmul(kt.Context.get().handle, qt.handle, p(x), p(nw), 1e-6, None, p(out), m, 0,
+                                      None, s))
+    torch.cuda.synchronize()
+    ad = a.astype(np.float64)
+    an = (ad / np.sqrt((ad * ad).mean(axis=1, keepdims=True) + 1e-6) * nwh).astype(np.float32)
+    assert rel_err(out.cpu().numpy(), oracle.multiply_quantized(an, ref_t, threads=16)) <= TOL_BF16
+    assert kt.Context.get().take_error() == 0
+
+
 @pytest.mark.parametrize("k,n", BENCH_SHAPES)
 @pytest.mark.parametrize("factor,count", [(50.0, 1), (100.0, 1), (100.0, 4), (75.0, 16)])
 def test_int4_gemv_with_outlier_channels(kt, oracle, k, n, factor, count):
