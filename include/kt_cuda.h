@@ -259,6 +259,9 @@ kt_status kt_qmatmul_noalloc(kt_ctx* ctx, const kt_qweight* w, const float* a_de
  * tokens in one launch), fp32 group combine, 1e-3). */
 enum { KT_PATH_GEMV = 0, KT_PATH_GENERIC = 1, KT_PATH_TENSOR_CORE = 2, KT_PATH_GEMV_MMA = 3 };
 kt_status kt_qmatmul_path(const kt_qweight* w, int32_t m, int32_t* path_out);
+/* The same for kt_qmatmul_t: KT_PATH_TENSOR_CORE (bf16 tcgen05, 2e-2) or
+ * KT_PATH_GENERIC (fp32 CUDA cores, 1e-3). */
+kt_status kt_qmatmul_t_path(const kt_qweight* w, int32_t m, int32_t* path_out);
 
 /* Pins the number of K-splits per column tile (>= 1; raised to the minimum
  * the shape needs) of the INT4 tensor-core GEMV; 0 restores the built-in
@@ -284,7 +287,10 @@ kt_status kt_qmatmul_host(kt_ctx* ctx, const kt_qweight* w, const float* a_host,
                           int32_t accumulate, float alpha, const float* bias_host);
 
 /* MatMul.multiplyByQuantizedTransposed(dy, W, dx, m, accumulate), MatMul.kt:954-981:
- *   dx[m x K] = (accumulate ? dx : 0) + dy[m x N] . dequant(W)^T        (device pointers) */
+ *   dx[m x K] = (accumulate ? dx : 0) + dy[m x N] . dequant(W)^T        (device pointers)
+ * INT4 at m >= 16 with N % 128 == 0 (group size 32, 64 or a multiple of 128)
+ * runs on the bf16 tcgen05 tensor cores (tolerance 2e-2 of max|dx|); every other
+ * case on the fp32 CUDA-core kernels (1e-3).  kt_qmatmul_t_path tells which. */
 kt_status kt_qmatmul_t(kt_ctx* ctx, const kt_qweight* w, const float* dy_dev, float* dx_dev, int32_t m,
                        int32_t accumulate, void* stream);
 

@@ -94,6 +94,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "kt_comm_init": ([P, I32, I32, P, PP], I32),
     "kt_comm_destroy": ([P], I32),
     "kt_comm_init_detached": ([P, I32, I32, PP], I32),
+    "kt_qmatmul_t_path": ([P, I32, ctypes.POINTER(I32)], I32),
     "kt_qmatmul_row_parallel": ([P, P, P, P, P, I32, I32, F32, P, P], I32),
     "kt_allgather_columns": ([P, P, P, I32, I32, P], I32),
     "kt_argmax_column_parallel": ([P, P, I32, I32, I32, P, P], I32),

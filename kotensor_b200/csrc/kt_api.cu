@@ -672,6 +672,13 @@ kt_status kt_set_gemv_tuning(int32_t lane_bytes, int32_t cluster_k) {
     return KT_OK;
 }
 
+kt_status kt_qmatmul_t_path(const kt_qweight* w, int32_t m, int32_t* path_out) {
+    if (!w || !path_out) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (m < 0) return fail(KT_ERR_INVALID_ARGUMENT, "Negative row count " + std::to_string(m));
+    *path_out = gemm_t_supported(view(w), m, nullptr) ? KT_PATH_TENSOR_CORE : KT_PATH_GENERIC;
+    return KT_OK;
+}
+
 kt_status kt_set_gemv_mma_tuning(int32_t k_splits) {
     set_mma_tuning(k_splits);
     set_imma_tuning(k_splits);
@@ -732,6 +739,14 @@ kt_status kt_qmatmul_t(kt_ctx* ctx, const kt_qweight* w, const float* dy, float*
     if (!dy || !dx) return fail(KT_ERR_INVALID_ARGUMENT, "NULL argument");
     const QView v = view(w);
     const cudaStream_t s = pick(ctx, stream);
+    if (gemm_t_supported(v, m, dy)) {  // m >= 16: bf16 tensor cores (tolerance 2e-2)
+        const size_t need = gemm_t_workspace_bytes(v, m, ctx->sm_count);
+        void* ws = nullptr;
+        KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "qmatmul_t workspace");
+        KT_CUDA_TRY(launch_gemm_t(v, dy, dx, m, accumulate, ctx->d_error, ctx->sm_count, s, ws, need),
+                    "qmatmul_t launch");
+        return KT_OK;
+    }
     const size_t need = matmul_t_workspace_bytes(v, m);
     void* ws = nullptr;
     if (need > 0) KT_CUDA_TRY(stream_workspace(ctx, s, need, &ws), "qmatmul_t workspace");

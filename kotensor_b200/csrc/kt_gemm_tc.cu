@@ -799,6 +799,233 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// MatMul.multiplyByQuantizedTransposed (MatMul.kt:954-981) on tcgen05, INT4,
+// m >= 16: dx[m x K] (+)= dy[m x N] . dequant(W)^T.  D[128 x nt] = A[128 x N] .
+// B[nt x N]^T with A = dequantized weight rows (one row per output row k of
+// dx, contraction over the N columns) and B = dy in bf16 (one row per token).
+// A CTA owns 128 rows k0 .. k0 + 127; a stage is one TMA box of those rows x 64
+// packed bytes (bytes n0 .. n0 + 63): its low nibbles are columns n0 .. n0 + 63
+// and its high nibbles columns R + n0 .. (split-half packing, R = N / 2), two
+// contraction blocks of 64 that accumulate into one TMEM accumulator against
+// the two matching 64-column tiles of dy.  Dequantizing warp w takes rows
+// 16 w .. + 15, lane l row 16 w + l / 2 and bytes 32 (l % 2) .. + 31: a PRMT
+// puts two adjacent bytes in the halves of a word, a LOP3 ORs each nibble into
+// the mantissa of bf16 128.0 (exact), (128 + q) - (128 + zero) is exact, and
+// one bf16 multiply by the column's scale rounds it -- the forward GEMM's
+// arithmetic, here with a scale and zero point per column of the pair.  The
+// epilogue, split-K partials and reduction are the one-accumulator (INT8)
+// path of the forward GEMM: output "columns" are rows k of dx.
+constexpr int kTRows = 128;              // output rows per CTA (the MMA's M)
+constexpr int kTMaxNT = 128;             // tokens per CTA (the MMA's N)
+constexpr int kTRawBytes = kTRows * 64;  // 8 KiB: 128 rows x 64 packed bytes
+constexpr int kTXBytes = kTMaxNT * 64 * 2;  // 16 KiB: a 64-column bf16 tile of dy
+constexpr int kTABytes = kTRows * 64 * 2;   // 16 KiB: a 64-column bf16 A tile
+constexpr int kTStageBytes = kTRawBytes + 2 * kTXBytes + 2 * kTABytes;  // 72 KiB
+constexpr int kTMaxGroups = 4;           // groups a 128-row tile can touch (group sizes 32, 64, multiples of 128)
+// per group: scales low [64] | scales high [64] | zeros low [64] | zeros high [64]
+constexpr int kTGroupBytes = 2 * 64 * 4 + 2 * 64;
+constexpr int kTScaleStageBytes = kTMaxGroups * kTGroupBytes;
+constexpr size_t kTSmemBytes = 1024 + static_cast<size_t>(kStages) * (kTStageBytes + kTScaleStageBytes) + kBarBytes;
+static_assert(kTStageBytes % 1024 == 0 && kTRawBytes % 1024 == 0 && kTXBytes % 1024 == 0, "1024-byte tiles");
+static_assert(kTSmemBytes <= 232448, "shared memory per CTA");
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_t_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_dy,
+                  GemmParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int k0 = blockIdx.x * kTRows;  // first output row (row of W, column of dx)
+    const int tok0 = blockIdx.y * p.nt;
+    const int ncols = p.K;               // the weight's columns N (the contraction; p.N is dx's row length)
+    const int half = ncols / 2;           // columns per nibble half (N % 128 == 0)
+    const int kb_total = half / 64;
+    const int kb_begin = static_cast<int>(static_cast<int64_t>(blockIdx.z) * kb_total / gridDim.z);
+    const int kb_end = static_cast<int>(static_cast<int64_t>(blockIdx.z + 1) * kb_total / gridDim.z);
+    const int n_kb = kb_end - kb_begin;
+    const int g_first = min(k0 / p.gs, p.G - 1);
+    const int g_last = min((k0 + kTRows - 1) / p.gs, p.G - 1);
+
+    const uint32_t raw_s = smem_u32(smem_raw);
+    const uint32_t base = (raw_s + 1023u) & ~1023u;
+    unsigned char* gbase = smem_raw + (base - raw_s);
+    const uint32_t scl = base + kStages * kTStageBytes;  // group slots [stage][group]
+    const uint32_t bars = scl + kStages * kTScaleStageBytes;
+    auto full_w = [&](int s) { return bars + 8 * s; };
+    auto full_x = [&](int s) { return bars + 8 * (kStages + s); };
+    auto full_a = [&](int s) { return bars + 8 * (2 * kStages + s); };
+    auto empty = [&](int s) { return bars + 8 * (3 * kStages + s); };
+    const uint32_t done = bars + 8 * (4 * kStages);
+    uint32_t* tmem_slot =
+        reinterpret_cast<uint32_t*>(gbase + kStages * (kTStageBytes + kTScaleStageBytes) + 8 * (4 * kStages + 1));
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full_w(s), 1);
+            mbar_init(full_x(s), 1);
+            mbar_init(full_a(s), kWorkers);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(p.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    dev::pdl_launch_dependents();
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            const uint32_t xtx = static_cast<uint32_t>(2 * p.nt * 64 * 2);
+            const uint32_t gtx = static_cast<uint32_t>((g_last - g_first + 1) * kTGroupBytes);
+            // the packed bytes and the group constants of block i -> full_w(i % NS)
+            auto issue_w = [&](int i) {
+                const int s = i % kStages;
+                const int n0 = (kb_begin + i) * 64;
+                mbar_expect_tx(full_w(s), kTRawBytes + gtx);
+                tma_load_2d(base + s * kTStageBytes, &tmap_w, n0, k0, full_w(s));
+                for (int g = g_first; g <= g_last; ++g) {
+                    const uint32_t dst = scl + s * kTScaleStageBytes + (g - g_first) * kTGroupBytes;
+                    const int64_t go = static_cast<int64_t>(g) * ncols;
+                    bulk_load(dst, p.scales + go + n0, 64 * 4, full_w(s));
+                    bulk_load(dst + 256, p.scales + go + half + n0, 64 * 4, full_w(s));
+                    bulk_load(dst + 512, p.zeros + go + n0, 64, full_w(s));
+                    bulk_load(dst + 576, p.zeros + go + half + n0, 64, full_w(s));
+                }
+            };
+            // the two bf16 tiles of dy (columns n0.., R + n0..) of block i -> full_x(i % NS)
+            auto issue_x = [&](int i) {
+                const int s = i % kStages;
+                const int n0 = (kb_begin + i) * 64;
+                const uint32_t xs = base + s * kTStageBytes + kTRawBytes;
+                mbar_expect_tx(full_x(s), xtx);
+                tma_load_2d(xs, &tmap_dy, n0, tok0, full_x(s));
+                tma_load_2d(xs + kTXBytes, &tmap_dy, half + n0, tok0, full_x(s));
+            };
+            // weights of the first stages before the wait (no kernel of the chain writes
+            // them), dy only after it: dy is the previous kernel's output
+            const int pre = min(n_kb, kStages);
+            for (int i = 0; i < pre; ++i) issue_w(i);
+            dev::pdl_wait();
+            for (int i = 0; i < pre; ++i) issue_x(i);
+            int issued = pre;
+            for (int i = pre; i < n_kb; ++i) {
+                const int s = i % kStages;
+                if (!mbar_wait_bounded(empty(s), ((i / kStages) - 1) & 1)) {
+                    atomicOr(p.err, 1);
+                    break;
+                }
+                issue_w(i);
+                issue_x(i);
+                ++issued;
+            }
+            // the last copies issued into each slot have landed before the CTA may exit
+            for (int i = max(0, issued - kStages); i < issued; ++i) {
+                if (!mbar_wait_bounded(full_w(i % kStages), (i / kStages) & 1)) break;
+                if (!mbar_wait_bounded(full_x(i % kStages), (i / kStages) & 1)) break;
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            for (int i = 0; i < n_kb; ++i) {
+                const int s = i % kStages;
+                const uint32_t par = (i / kStages) & 1;
+                if (!mbar_wait_bounded(full_x(s), par) || !mbar_wait_bounded(full_a(s), par)) {
+                    atomicOr(p.err, 1);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t xlo = base + s * kTStageBytes + kTRawBytes, xhi = xlo + kTXBytes;
+                const uint32_t alo = xhi + kTXBytes, ahi = alo + kTABytes;
+#pragma unroll
+                for (int kk = 0; kk < 64 / 16; ++kk) {
+                    const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+                    umma_bf16(tmem, umma_desc_sw128(alo + kk * 32), umma_desc_sw128(xlo + kk * 32), p.idesc, acc);
+                    umma_bf16(tmem, umma_desc_sw128(ahi + kk * 32), umma_desc_sw128(xhi + kk * 32), p.idesc, 1u);
+                }
+                umma_commit(empty(s));  // the stage is free once these MMAs have read it
+            }
+            umma_commit(done);
+            if (!mbar_wait_bounded(done, 0)) atomicOr(p.err, 1);  // no MMA in flight past this point
+        }
+    } else {
+        bool ok = true;
+        const int r = 16 * warp + (lane >> 1);  // row of the tile
+        const int hh = lane & 1;                // bytes 32 hh .. + 31 of the row
+        const int gsl = min((k0 + r) / p.gs, p.G - 1) - g_first;  // the row's group slot
+        for (int i = 0; i < n_kb; ++i) {
+            const int s = i % kStages;
+            if (!mbar_wait_bounded(full_w(s), (i / kStages) & 1)) {
+                if (lane == 0) atomicOr(p.err, 1);
+                ok = false;
+                break;
+            }
+            const unsigned char* st = gbase + s * kTStageBytes;
+            const uint4 wa = *reinterpret_cast<const uint4*>(st + r * 64 + 32 * hh);
+            const uint4 wb = *reinterpret_cast<const uint4*>(st + r * 64 + 32 * hh + 16);
+            const unsigned char* slot = gbase + kStages * kTStageBytes + s * kTScaleStageBytes + gsl * kTGroupBytes;
+            const float* s_lo = reinterpret_cast<const float*>(slot) + 32 * hh;
+            const float* s_hi = reinterpret_cast<const float*>(slot + 256) + 32 * hh;
+            const uint4 zla = *reinterpret_cast<const uint4*>(slot + 512 + 32 * hh);
+            const uint4 zlb = *reinterpret_cast<const uint4*>(slot + 512 + 32 * hh + 16);
+            const uint4 zha = *reinterpret_cast<const uint4*>(slot + 576 + 32 * hh);
+            const uint4 zhb = *reinterpret_cast<const uint4*>(slot + 576 + 32 * hh + 16);
+            const uint32_t wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+            const uint32_t zlv[8] = {zla.x, zla.y, zla.z, zla.w, zlb.x, zlb.y, zlb.z, zlb.w};
+            const uint32_t zhv[8] = {zha.x, zha.y, zha.z, zha.w, zhb.x, zhb.y, zhb.z, zhb.w};
+            uint32_t lo[16], hi[16];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    // bytes 4q + 2h2 and + 1 of the lane's 32 in the two halves of a word, each
+                    // nibble ORed into bf16 128.0: 128 + q exactly; the zero points alike
+                    const uint32_t sel = h2 ? 0x4342u : 0x4140u;
+                    const uint32_t pr = prmt(wv[q], 0u, sel);
+                    const uint32_t ql = lop3_and_or(pr, 0x000F000Fu, 0x43004300u);
+                    const uint32_t qh = lop3_and_or(pr >> 4, 0x000F000Fu, 0x43004300u);
+                    const uint32_t zl = lop3_and_or(prmt(zlv[q], 0u, sel), 0x000F000Fu, 0x43004300u);
+                    const uint32_t zh = lop3_and_or(prmt(zhv[q], 0u, sel), 0x000F000Fu, 0x43004300u);
+                    const int j = 4 * q + 2 * h2;
+                    const float2 sl2 = *reinterpret_cast<const float2*>(s_lo + j);
+                    const float2 sh2 = *reinterpret_cast<const float2*>(s_hi + j);
+                    lo[2 * q + h2] = bf2_sub_mul(ql, zl, pack_bf16(sl2.x, sl2.y));
+                    hi[2 * q + h2] = bf2_sub_mul(qh, zh, pack_bf16(sh2.x, sh2.y));
+                }
+            }
+            unsigned char* alo = gbase + s * kTStageBytes + kTRawBytes + 2 * kTXBytes;
+            unsigned char* ahi = alo + kTABytes;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 hh + c of row r, 128-byte swizzle
+                const uint32_t off = static_cast<uint32_t>(r * 128 + (((4 * hh + c) ^ (r & 7)) << 4));
+                *reinterpret_cast<uint4*>(alo + off) = make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
+                *reinterpret_cast<uint4*>(ahi + off) = make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> MMA reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full_a(s));
+        }
+        // output "columns" are rows k0 .. k0 + 127 of dx (the one-accumulator path)
+        gemm_epilogue<8>(p, tmem, 0, done, ok, k0, tok0, &s_last);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols)
+                     : "memory");
+    }
+}
+
 // Split-K partial tiles [tile][split][nt][columns] summed in split order, then
 // c = (accumulate ? c : 0) + alpha * sum + bias (+ LoRA term): the arithmetic,
 // in the same order, of the last-CTA reduction in gemm_tc_kernel, spread over
@@ -1102,6 +1329,92 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
     const int blocks = static_cast<int>(std::min<int64_t>((quads + 255) / 256, static_cast<int64_t>(sm_count) * 8));
     return launch_chained(w.bits == 4 ? split_reduce_kernel<4> : split_reduce_kernel<8>, dim3(blocks), dim3(256), 0,
                           s, p, static_cast<int>(grid.x), static_cast<int>(grid.y), S);
+}
+
+// ---- the transposed product on tcgen05 (gemm_t_kernel)
+
+bool gemm_t_supported(const QView& w, int32_t m, const float* dy) {
+    if (w.bits != 4 || m < 16 || w.columns % 128 != 0 || w.rows < 1) return false;
+    if (!(w.group_size == 32 || w.group_size == 64 || w.group_size % 128 == 0)) return false;
+    return dy == nullptr || reinterpret_cast<uintptr_t>(dy) % 16 == 0;
+}
+
+namespace {
+int t_nt(int m) { return std::min(kTMaxNT, (m + 15) / 16 * 16); }
+int t_splits(const QView& w, int m, int sm_count) {
+    const int tiles = ((w.rows + kTRows - 1) / kTRows) * ((m + t_nt(m) - 1) / t_nt(m));
+    const int kb_total = w.columns / 128;
+    int s = std::max(1, sm_count / tiles);
+    s = std::min({s, std::max(1, kb_total / kMinSplitBlocks), kMaxSplits});
+    if (tiles > kTicketCapEach) s = 1;
+    return s;
+}
+}  // namespace
+
+size_t gemm_t_workspace_bytes(const QView& w, int32_t m, int sm_count) {
+    const int S = t_splits(w, m, sm_count);
+    size_t bytes = kWorkspaceReservedBytes + align256(static_cast<size_t>(m) * w.columns * 2);
+    if (S > 1) {
+        const size_t tiles = static_cast<size_t>((w.rows + kTRows - 1) / kTRows) * ((m + t_nt(m) - 1) / t_nt(m));
+        bytes += tiles * S * static_cast<size_t>(t_nt(m)) * kTRows * sizeof(float);
+    }
+    return bytes;
+}
+
+cudaError_t launch_gemm_t(const QView& w, const float* dy, float* dx, int32_t m, int32_t accumulate, int32_t* err,
+                          int sm_count, cudaStream_t s, void* workspace, size_t workspace_bytes) {
+    if (!gemm_t_supported(w, m, dy) || workspace == nullptr ||
+        workspace_bytes < gemm_t_workspace_bytes(w, m, sm_count))
+        return cudaErrorInvalidValue;
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    __nv_bfloat16* dyb = reinterpret_cast<__nv_bfloat16*>(ws + kWorkspaceReservedBytes);
+    const int64_t n8 = static_cast<int64_t>(m) * w.columns / 8;
+    cudaError_t e = launch_chained(x_to_bf16_kernel, dim3(static_cast<unsigned>((n8 + 255) / 256)), dim3(256), 0, s,
+                                   dy, dyb, n8);
+    if (e != cudaSuccess) return e;
+    GemmParams p{};
+    p.scales = w.scales;
+    p.zeros = w.zeros;
+    p.y = dx;
+    p.err = err;
+    p.M = m;
+    p.K = w.columns;  // the contraction (the weight's columns)
+    p.N = w.rows;     // dx's row length: output "columns" are the weight's rows
+    p.R = w.rows;
+    p.gs = w.group_size;
+    p.G = w.groups;
+    p.nt = t_nt(m);
+    p.nt_cols = p.nt;
+    int cols = 32;
+    while (cols < p.nt) cols *= 2;
+    p.tmem_cols = cols;
+    // kind::f16: D f32, A and B bf16, both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28
+    p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(p.nt >> 3) << 17) |
+              (static_cast<uint32_t>(kTRows >> 4) << 24);
+    p.alpha = 1.0f;
+    p.accumulate = accumulate;
+    const int S = t_splits(w, m, sm_count);
+    p.tickets = reinterpret_cast<int32_t*>(ws + kGemmTicketOffset);
+    p.partials = reinterpret_cast<float*>(ws + kWorkspaceReservedBytes + align256(static_cast<size_t>(m) * w.columns * 2));
+    p.reduce_kernel = S > 1 && p.nt * S >= kReduceKernelMin ? 1 : 0;
+    alignas(64) CUtensorMap tmap_w, tmap_dy;
+    // packed rows as bytes: boxes of 64 bytes x 128 rows, no swizzle (rows read linearly)
+    if (!encode_tmap_2d(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.q, static_cast<uint64_t>(w.bytes_per_row),
+                        static_cast<uint64_t>(w.rows), static_cast<uint64_t>(w.bytes_per_row), 64, kTRows,
+                        CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_tmap_2d(&tmap_dy, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dyb, static_cast<uint64_t>(w.columns),
+                        static_cast<uint64_t>(m), static_cast<uint64_t>(w.columns) * 2, 64, static_cast<uint32_t>(p.nt),
+                        CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(gemm_t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTSmemBytes));
+    if (e != cudaSuccess) return e;
+    const dim3 grid((w.rows + kTRows - 1) / kTRows, (m + p.nt - 1) / p.nt, S);
+    e = launch_chained(gemm_t_kernel, grid, dim3(kThreads), kTSmemBytes, s, tmap_w, tmap_dy, p);
+    if (e != cudaSuccess || !p.reduce_kernel) return e;
+    const int64_t quads = static_cast<int64_t>(grid.x) * grid.y * p.nt * 32;
+    const int blocks = static_cast<int>(std::min<int64_t>((quads + 255) / 256, static_cast<int64_t>(sm_count) * 8));
+    return launch_chained(split_reduce_kernel<8>, dim3(blocks), dim3(256), 0, s, p, static_cast<int>(grid.x),
+                          static_cast<int>(grid.y), S);
 }
 
 }  // namespace kt

@@ -237,6 +237,12 @@ cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, 
 
 // ---- kt_gemm_tc.cu  (INT4, m >= 9: bf16 tcgen05 MMAs, TMEM accumulators)
 bool gemm_tc_supported(const QView& w, int32_t m, const float* a);
+// The transposed product (kt_qmatmul_t) on tcgen05: INT4, m >= 16, N % 128 == 0,
+// group size 32, 64 or a multiple of 128 (kt_gemm_tc.cu).
+bool gemm_t_supported(const QView& w, int32_t m, const float* dy);
+size_t gemm_t_workspace_bytes(const QView& w, int32_t m, int sm_count);
+cudaError_t launch_gemm_t(const QView& w, const float* dy, float* dx, int32_t m, int32_t accumulate, int32_t* err,
+                          int sm_count, cudaStream_t s, void* workspace, size_t workspace_bytes);
 size_t gemm_tc_workspace_bytes(const QView& w, int32_t m, int sm_count);
 // The GEMM forms silu(gate) * up in its split-K reduction for this INT4 gate | up
 // weight at this m (MatmulArgs::swiglu); elsewhere the caller runs kt_silu_mul_rows.

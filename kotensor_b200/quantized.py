@@ -292,6 +292,12 @@ class QuantizedTensor:
         _lib.check(_lib.load().kt_qmatmul_path(self._handle, int(m), ctypes.byref(out)))
         return out.value
 
+    def transposed_path(self, m: int) -> int:
+        """The kernel family kt_qmatmul_t runs for m rows of dy (KT_PATH_TENSOR_CORE or KT_PATH_GENERIC)."""
+        out = ctypes.c_int32()
+        _lib.check(_lib.load().kt_qmatmul_t_path(self._handle, int(m), ctypes.byref(out)))
+        return out.value
+
     def raw_value(self, row: int, column: int) -> int:
         """rawValue(row, column), QuantizedTensor.kt:172-180."""
         q = self.qdata

@@ -310,6 +310,48 @@ def test_transposed_matches_oracle(kt, oracle, k, n, m, bits):
     assert rel_err(dx.cpu().numpy(), ref) <= TOL_FP32
 
 
+# (K, N, m, group): INT4 at m >= 16 and N % 128 == 0 runs the tcgen05 transposed
+# kernel -- one or several 128-token tiles, ragged K (partial 128-row tiles and
+# partial groups), group sizes 32 / 64 / 128 / 256, split-K over N.
+@pytest.mark.parametrize("k,n,m,g", [(4096, 14336, 16, 64), (1000, 1024, 17, 32), (2048, 5632, 100, 128),
+                                     (896, 4864, 40, 64), (520, 256, 300, 256), (384, 2048, 130, 32)])
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_transposed_tensor_core_matches_oracle(kt, oracle, k, n, m, g, accumulate):
+    from kotensor_b200 import _lib
+    rng = np.random.default_rng(k + n + m)
+    w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+    ref_t = oracle.quantize(w, 4, g)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, g)
+    assert qt.transposed_path(m) == _lib.KT_PATH_TENSOR_CORE
+    dy = rng.standard_normal((m, n), dtype=np.float32)
+    dx0 = rng.standard_normal((m, k), dtype=np.float32)
+    dx = dev(dx0.copy()) if accumulate else torch.full((m, k), float("nan"), device="cuda")
+    kt.MatMul.multiply_by_quantized_transposed(dev(dy), qt, dx, m, accumulate=accumulate)
+    ref = oracle.multiply_by_quantized_transposed(dy, ref_t, dx=dx0 if accumulate else None,
+                                                  accumulate=accumulate, threads=8)
+    got = dx.cpu().numpy()
+    assert np.isfinite(got).all()
+    # the accumulated part is compared on dx alone so that dx0 cannot hide an error
+    assert rel_err(got - (dx0 if accumulate else 0), ref - (dx0 if accumulate else 0)) <= TOL_BF16
+    # deterministic: a second product gives the same bits
+    dx2 = dev(dx0.copy()) if accumulate else torch.zeros((m, k), device="cuda")
+    kt.MatMul.multiply_by_quantized_transposed(dev(dy), qt, dx2, m, accumulate=accumulate)
+    assert torch.equal(dx, dx2)
+    assert kt.Context.get().take_error() == 0
+
+
+def test_transposed_path_selection(kt, oracle):
+    from kotensor_b200 import _lib
+    rng = np.random.default_rng(3)
+    for bits, n, g, m, want in [(4, 1024, 64, 16, _lib.KT_PATH_TENSOR_CORE), (4, 1024, 64, 15, _lib.KT_PATH_GENERIC),
+                                (8, 1024, 64, 64, _lib.KT_PATH_GENERIC), (4, 1000, 64, 64, _lib.KT_PATH_GENERIC),
+                                (4, 1024, 96, 64, _lib.KT_PATH_GENERIC)]:
+        w = (rng.standard_normal((256, n)) * 0.02).astype(np.float32)
+        t = oracle.quantize(w, bits, g)
+        qt = kt.QuantizedTensor.from_arrays(t.qdata, t.scales, t.zeros, (256, n), bits, g)
+        assert qt.transposed_path(m) == want, (bits, n, g, m)
+
+
 def test_no_kernel_reported_a_timeout(kt):
     """Every bounded wait inside the kernels completed in the calls above."""
     assert kt.Context.get().take_error() == 0

@@ -104,7 +104,10 @@ def test_lora_backward_matches_oracle(kt, oracle, bits, k, n, m, rank):
     ref_dx, ref_ga, ref_gb = QO.lora_backward(x.cpu().numpy(), dy.cpu().numpy(), q, lora.lora_a.cpu().numpy(),
                                               lora.lora_b.cpu().numpy(), lora.scaling,
                                               lora._projected[:m].cpu().numpy())
-    assert _rel(dx.cpu().numpy() - 0.5, ref_dx) <= 1e-3
+    from kotensor_b200 import _lib
+    # kt_qmatmul_t takes the bf16 tcgen05 kernel for INT4 at m >= 16 (tolerance 2e-2)
+    dx_tol = 2e-2 if layer.weight.transposed_path(m) == _lib.KT_PATH_TENSOR_CORE else 1e-3
+    assert _rel(dx.cpu().numpy() - 0.5, ref_dx) <= dx_tol
     assert _rel(lora.grad_a.cpu().numpy(), ref_ga) <= 1e-4
     assert _rel(lora.grad_b.cpu().numpy(), ref_gb) <= 1e-4
     # gradients accumulate (Tensor.grad +=), bit-identically on a second pass
