@@ -288,9 +288,10 @@ kt_status kt_qmatmul_host(kt_ctx* ctx, const kt_qweight* w, const float* a_host,
 
 /* MatMul.multiplyByQuantizedTransposed(dy, W, dx, m, accumulate), MatMul.kt:954-981:
  *   dx[m x K] = (accumulate ? dx : 0) + dy[m x N] . dequant(W)^T        (device pointers)
- * INT4 at m >= 16 with N % 128 == 0 (group size 32, 64 or a multiple of 128)
- * runs on the bf16 tcgen05 tensor cores (tolerance 2e-2 of max|dx|); every other
- * case on the fp32 CUDA-core kernels (1e-3).  kt_qmatmul_t_path tells which. */
+ * At m >= 16, INT4 with N % 128 == 0 or INT8 with N % 64 == 0 (group size 32, 64
+ * or a multiple of 128) runs on the bf16 tcgen05 tensor cores (tolerance 2e-2 of
+ * max|dx|); every other case on the fp32 CUDA-core kernels (1e-3).
+ * kt_qmatmul_t_path tells which. */
 kt_status kt_qmatmul_t(kt_ctx* ctx, const kt_qweight* w, const float* dy_dev, float* dx_dev, int32_t m,
                        int32_t accumulate, void* stream);
 

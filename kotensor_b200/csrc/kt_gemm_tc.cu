@@ -800,8 +800,8 @@ __global__ void __launch_bounds__(kTsThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// MatMul.multiplyByQuantizedTransposed (MatMul.kt:954-981) on tcgen05, INT4,
-// m >= 16: dx[m x K] (+)= dy[m x N] . dequant(W)^T.  D[128 x nt] = A[128 x N] .
+// MatMul.multiplyByQuantizedTransposed (MatMul.kt:954-981) on tcgen05, INT4
+// (INT8 below), m >= 16: dx[m x K] (+)= dy[m x N] . dequant(W)^T.  D[128 x nt] = A[128 x N] .
 // B[nt x N]^T with A = dequantized weight rows (one row per output row k of
 // dx, contraction over the N columns) and B = dy in bf16 (one row per token).
 // A CTA owns 128 rows k0 .. k0 + 127; a stage is one TMA box of those rows x 64
@@ -816,6 +816,10 @@ __global__ void __launch_bounds__(kTsThreads, 1)
 // arithmetic, here with a scale and zero point per column of the pair.  The
 // epilogue, split-K partials and reduction are the one-accumulator (INT8)
 // path of the forward GEMM: output "columns" are rows k of dx.
+// INT8 (BITS = 8): a stage's 64 bytes are columns n0 .. n0 + 63 (one
+// contraction block, one dy tile, one A tile); the signed byte becomes q
+// exactly through the fp32 mantissa and one fp32 multiply by the column's
+// scale (QuantizedTensor.kt:201) is rounded to bf16, as in the forward GEMM.
 constexpr int kTRows = 128;              // output rows per CTA (the MMA's M)
 constexpr int kTMaxNT = 128;             // tokens per CTA (the MMA's N)
 constexpr int kTRawBytes = kTRows * 64;  // 8 KiB: 128 rows x 64 packed bytes
@@ -830,9 +834,11 @@ constexpr size_t kTSmemBytes = 1024 + static_cast<size_t>(kStages) * (kTStageByt
 static_assert(kTStageBytes % 1024 == 0 && kTRawBytes % 1024 == 0 && kTXBytes % 1024 == 0, "1024-byte tiles");
 static_assert(kTSmemBytes <= 232448, "shared memory per CTA");
 
+template <int BITS>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_t_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_dy,
                   GemmParams p) {
+    constexpr bool kInt4 = BITS == 4;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     __shared__ int s_last;
     const int warp = threadIdx.x >> 5;
@@ -840,7 +846,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int k0 = blockIdx.x * kTRows;  // first output row (row of W, column of dx)
     const int tok0 = blockIdx.y * p.nt;
     const int ncols = p.K;               // the weight's columns N (the contraction; p.N is dx's row length)
-    const int half = ncols / 2;           // columns per nibble half (N % 128 == 0)
+    const int half = kInt4 ? ncols / 2 : ncols;  // INT4: columns per nibble half (N % 128 == 0); bytes per row
     const int kb_total = half / 64;
     const int kb_begin = static_cast<int>(static_cast<int64_t>(blockIdx.z) * kb_total / gridDim.z);
     const int kb_end = static_cast<int>(static_cast<int64_t>(blockIdx.z + 1) * kb_total / gridDim.z);
@@ -885,8 +891,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     dev::pdl_launch_dependents();
     if (warp == kProducerWarp) {
         if (lane == 0) {
-            const uint32_t xtx = static_cast<uint32_t>(2 * p.nt * 64 * 2);
-            const uint32_t gtx = static_cast<uint32_t>((g_last - g_first + 1) * kTGroupBytes);
+            const uint32_t xtx = static_cast<uint32_t>((kInt4 ? 2 : 1) * p.nt * 64 * 2);
+            const uint32_t gtx = static_cast<uint32_t>((g_last - g_first + 1) * (kInt4 ? kTGroupBytes : 64 * 4));
             // the packed bytes and the group constants of block i -> full_w(i % NS)
             auto issue_w = [&](int i) {
                 const int s = i % kStages;
@@ -897,9 +903,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t dst = scl + s * kTScaleStageBytes + (g - g_first) * kTGroupBytes;
                     const int64_t go = static_cast<int64_t>(g) * ncols;
                     bulk_load(dst, p.scales + go + n0, 64 * 4, full_w(s));
-                    bulk_load(dst + 256, p.scales + go + half + n0, 64 * 4, full_w(s));
-                    bulk_load(dst + 512, p.zeros + go + n0, 64, full_w(s));
-                    bulk_load(dst + 576, p.zeros + go + half + n0, 64, full_w(s));
+                    if (kInt4) {
+                        bulk_load(dst + 256, p.scales + go + half + n0, 64 * 4, full_w(s));
+                        bulk_load(dst + 512, p.zeros + go + n0, 64, full_w(s));
+                        bulk_load(dst + 576, p.zeros + go + half + n0, 64, full_w(s));
+                    }
                 }
             };
             // the two bf16 tiles of dy (columns n0.., R + n0..) of block i -> full_x(i % NS)
@@ -909,7 +917,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t xs = base + s * kTStageBytes + kTRawBytes;
                 mbar_expect_tx(full_x(s), xtx);
                 tma_load_2d(xs, &tmap_dy, n0, tok0, full_x(s));
-                tma_load_2d(xs + kTXBytes, &tmap_dy, half + n0, tok0, full_x(s));
+                if (kInt4) tma_load_2d(xs + kTXBytes, &tmap_dy, half + n0, tok0, full_x(s));
             };
             // weights of the first stages before the wait (no kernel of the chain writes
             // them), dy only after it: dy is the previous kernel's output
@@ -950,7 +958,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kk = 0; kk < 64 / 16; ++kk) {
                     const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
                     umma_bf16(tmem, umma_desc_sw128(alo + kk * 32), umma_desc_sw128(xlo + kk * 32), p.idesc, acc);
-                    umma_bf16(tmem, umma_desc_sw128(ahi + kk * 32), umma_desc_sw128(xhi + kk * 32), p.idesc, 1u);
+                    if (kInt4)
+                        umma_bf16(tmem, umma_desc_sw128(ahi + kk * 32), umma_desc_sw128(xhi + kk * 32), p.idesc, 1u);
                 }
                 umma_commit(empty(s));  // the stage is free once these MMAs have read it
             }
@@ -973,42 +982,74 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint4 wa = *reinterpret_cast<const uint4*>(st + r * 64 + 32 * hh);
             const uint4 wb = *reinterpret_cast<const uint4*>(st + r * 64 + 32 * hh + 16);
             const unsigned char* slot = gbase + kStages * kTStageBytes + s * kTScaleStageBytes + gsl * kTGroupBytes;
-            const float* s_lo = reinterpret_cast<const float*>(slot) + 32 * hh;
-            const float* s_hi = reinterpret_cast<const float*>(slot + 256) + 32 * hh;
-            const uint4 zla = *reinterpret_cast<const uint4*>(slot + 512 + 32 * hh);
-            const uint4 zlb = *reinterpret_cast<const uint4*>(slot + 512 + 32 * hh + 16);
-            const uint4 zha = *reinterpret_cast<const uint4*>(slot + 576 + 32 * hh);
-            const uint4 zhb = *reinterpret_cast<const uint4*>(slot + 576 + 32 * hh + 16);
-            const uint32_t wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-            const uint32_t zlv[8] = {zla.x, zla.y, zla.z, zla.w, zlb.x, zlb.y, zlb.z, zlb.w};
-            const uint32_t zhv[8] = {zha.x, zha.y, zha.z, zha.w, zhb.x, zhb.y, zhb.z, zhb.w};
-            uint32_t lo[16], hi[16];
+            if constexpr (kInt4) {
+                const float* s_lo = reinterpret_cast<const float*>(slot) + 32 * hh;
+                const float* s_hi = reinterpret_cast<const float*>(slot + 256) + 32 * hh;
+                const uint4 zla = *reinterpret_cast<const uint4*>(slot + 512 + 32 * hh);
+                const uint4 zlb = *reinterpret_cast<const uint4*>(slot + 512 + 32 * hh + 16);
+                const uint4 zha = *reinterpret_cast<const uint4*>(slot + 576 + 32 * hh);
+                const uint4 zhb = *reinterpret_cast<const uint4*>(slot + 576 + 32 * hh + 16);
+                const uint32_t wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                const uint32_t zlv[8] = {zla.x, zla.y, zla.z, zla.w, zlb.x, zlb.y, zlb.z, zlb.w};
+                const uint32_t zhv[8] = {zha.x, zha.y, zha.z, zha.w, zhb.x, zhb.y, zhb.z, zhb.w};
+                uint32_t lo[16], hi[16];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
+                for (int q = 0; q < 8; ++q) {
 #pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2) {
-                    // bytes 4q + 2h2 and + 1 of the lane's 32 in the two halves of a word, each
-                    // nibble ORed into bf16 128.0: 128 + q exactly; the zero points alike
-                    const uint32_t sel = h2 ? 0x4342u : 0x4140u;
-                    const uint32_t pr = prmt(wv[q], 0u, sel);
-                    const uint32_t ql = lop3_and_or(pr, 0x000F000Fu, 0x43004300u);
-                    const uint32_t qh = lop3_and_or(pr >> 4, 0x000F000Fu, 0x43004300u);
-                    const uint32_t zl = lop3_and_or(prmt(zlv[q], 0u, sel), 0x000F000Fu, 0x43004300u);
-                    const uint32_t zh = lop3_and_or(prmt(zhv[q], 0u, sel), 0x000F000Fu, 0x43004300u);
-                    const int j = 4 * q + 2 * h2;
-                    const float2 sl2 = *reinterpret_cast<const float2*>(s_lo + j);
-                    const float2 sh2 = *reinterpret_cast<const float2*>(s_hi + j);
-                    lo[2 * q + h2] = bf2_sub_mul(ql, zl, pack_bf16(sl2.x, sl2.y));
-                    hi[2 * q + h2] = bf2_sub_mul(qh, zh, pack_bf16(sh2.x, sh2.y));
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        // bytes 4q + 2h2 and + 1 of the lane's 32 in the two halves of a word, each
+                        // nibble ORed into bf16 128.0: 128 + q exactly; the zero points alike
+                        const uint32_t sel = h2 ? 0x4342u : 0x4140u;
+                        const uint32_t pr = prmt(wv[q], 0u, sel);
+                        const uint32_t ql = lop3_and_or(pr, 0x000F000Fu, 0x43004300u);
+                        const uint32_t qh = lop3_and_or(pr >> 4, 0x000F000Fu, 0x43004300u);
+                        const uint32_t zl = lop3_and_or(prmt(zlv[q], 0u, sel), 0x000F000Fu, 0x43004300u);
+                        const uint32_t zh = lop3_and_or(prmt(zhv[q], 0u, sel), 0x000F000Fu, 0x43004300u);
+                        const int j = 4 * q + 2 * h2;
+                        const float2 sl2 = *reinterpret_cast<const float2*>(s_lo + j);
+                        const float2 sh2 = *reinterpret_cast<const float2*>(s_hi + j);
+                        lo[2 * q + h2] = bf2_sub_mul(ql, zl, pack_bf16(sl2.x, sl2.y));
+                        hi[2 * q + h2] = bf2_sub_mul(qh, zh, pack_bf16(sh2.x, sh2.y));
+                    }
                 }
-            }
-            unsigned char* alo = gbase + s * kTStageBytes + kTRawBytes + 2 * kTXBytes;
-            unsigned char* ahi = alo + kTABytes;
+                unsigned char* alo = gbase + s * kTStageBytes + kTRawBytes + 2 * kTXBytes;
+                unsigned char* ahi = alo + kTABytes;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 hh + c of row r, 128-byte swizzle
-                const uint32_t off = static_cast<uint32_t>(r * 128 + (((4 * hh + c) ^ (r & 7)) << 4));
-                *reinterpret_cast<uint4*>(alo + off) = make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
-                *reinterpret_cast<uint4*>(ahi + off) = make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
+                for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 hh + c of row r, 128-byte swizzle
+                    const uint32_t off = static_cast<uint32_t>(r * 128 + (((4 * hh + c) ^ (r & 7)) << 4));
+                    *reinterpret_cast<uint4*>(alo + off) =
+                        make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
+                    *reinterpret_cast<uint4*>(ahi + off) =
+                        make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
+                }
+            } else {
+                // bytes 32 hh .. + 31 of row r: columns n0 + 32 hh + j, each
+                // 2^23 + (q + 128) in an fp32 mantissa minus 2^23 + 128 (exactly q),
+                // times the column's scale in fp32, rounded to bf16
+                const float* sc = reinterpret_cast<const float*>(slot) + 32 * hh;
+                const uint32_t wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                uint32_t lo[16];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        const int j = 4 * q + 2 * h2;
+                        // byte j (j + 1) of the lane's 32 into the low byte of 0x4B000000
+                        const uint32_t b0 = prmt(wv[q], 0x4Bu, static_cast<uint32_t>(2 * h2) | 0x4550u);
+                        const uint32_t b1 = prmt(wv[q], 0x4Bu, static_cast<uint32_t>(2 * h2 + 1) | 0x4550u);
+                        const float q0 = __uint_as_float(b0 ^ 0x80u) - 8388736.0f;
+                        const float q1 = __uint_as_float(b1 ^ 0x80u) - 8388736.0f;
+                        const float2 s2 = *reinterpret_cast<const float2*>(sc + j);
+                        lo[2 * q + h2] = pack_bf16(__fmul_rn(s2.x, q0), __fmul_rn(s2.y, q1));
+                    }
+                }
+                unsigned char* alo = gbase + s * kTStageBytes + kTRawBytes + 2 * kTXBytes;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 hh + c of row r, 128-byte swizzle
+                    const uint32_t off = static_cast<uint32_t>(r * 128 + (((4 * hh + c) ^ (r & 7)) << 4));
+                    *reinterpret_cast<uint4*>(alo + off) =
+                        make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
+                }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> MMA reads
             __syncwarp();
@@ -1334,7 +1375,8 @@ cudaError_t launch_gemm_tc(const QView& w, const MatmulArgs& a, int sm_count, cu
 // ---- the transposed product on tcgen05 (gemm_t_kernel)
 
 bool gemm_t_supported(const QView& w, int32_t m, const float* dy) {
-    if (w.bits != 4 || m < 16 || w.columns % 128 != 0 || w.rows < 1) return false;
+    if (m < 16 || w.rows < 1) return false;
+    if (!(w.bits == 4 && w.columns % 128 == 0) && !(w.bits == 8 && w.columns % 64 == 0)) return false;
     if (!(w.group_size == 32 || w.group_size == 64 || w.group_size % 128 == 0)) return false;
     return dy == nullptr || reinterpret_cast<uintptr_t>(dy) % 16 == 0;
 }
@@ -1343,7 +1385,7 @@ namespace {
 int t_nt(int m) { return std::min(kTMaxNT, (m + 15) / 16 * 16); }
 int t_splits(const QView& w, int m, int sm_count) {
     const int tiles = ((w.rows + kTRows - 1) / kTRows) * ((m + t_nt(m) - 1) / t_nt(m));
-    const int kb_total = w.columns / 128;
+    const int kb_total = w.columns / (w.bits == 4 ? 128 : 64);  // stages of 64 packed bytes
     int s = std::max(1, sm_count / tiles);
     s = std::min({s, std::max(1, kb_total / kMinSplitBlocks), kMaxSplits});
     if (tiles > kTicketCapEach) s = 1;
@@ -1406,10 +1448,11 @@ cudaError_t launch_gemm_t(const QView& w, const float* dy, float* dx, int32_t m,
                         static_cast<uint64_t>(m), static_cast<uint64_t>(w.columns) * 2, 64, static_cast<uint32_t>(p.nt),
                         CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    e = cudaFuncSetAttribute(gemm_t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTSmemBytes));
+    auto kernel = w.bits == 4 ? gemm_t_kernel<4> : gemm_t_kernel<8>;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTSmemBytes));
     if (e != cudaSuccess) return e;
     const dim3 grid((w.rows + kTRows - 1) / kTRows, (m + p.nt - 1) / p.nt, S);
-    e = launch_chained(gemm_t_kernel, grid, dim3(kThreads), kTSmemBytes, s, tmap_w, tmap_dy, p);
+    e = launch_chained(kernel, grid, dim3(kThreads), kTSmemBytes, s, tmap_w, tmap_dy, p);
     if (e != cudaSuccess || !p.reduce_kernel) return e;
     const int64_t quads = static_cast<int64_t>(grid.x) * grid.y * p.nt * 32;
     const int blocks = static_cast<int>(std::min<int64_t>((quads + 255) / 256, static_cast<int64_t>(sm_count) * 8));

@@ -237,7 +237,7 @@ cudaError_t launch_gemv_imma(const QView& w, const MatmulArgs& a, int sm_count, 
 
 // ---- kt_gemm_tc.cu  (INT4, m >= 9: bf16 tcgen05 MMAs, TMEM accumulators)
 bool gemm_tc_supported(const QView& w, int32_t m, const float* a);
-// The transposed product (kt_qmatmul_t) on tcgen05: INT4, m >= 16, N % 128 == 0,
+// The transposed product (kt_qmatmul_t) on tcgen05: m >= 16, INT4 with N % 128 == 0 or INT8 with N % 64 == 0,
 // group size 32, 64 or a multiple of 128 (kt_gemm_tc.cu).
 bool gemm_t_supported(const QView& w, int32_t m, const float* dy);
 size_t gemm_t_workspace_bytes(const QView& w, int32_t m, int sm_count);

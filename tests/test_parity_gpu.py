@@ -310,18 +310,21 @@ def test_transposed_matches_oracle(kt, oracle, k, n, m, bits):
     assert rel_err(dx.cpu().numpy(), ref) <= TOL_FP32
 
 
-# (K, N, m, group): INT4 at m >= 16 and N % 128 == 0 runs the tcgen05 transposed
-# kernel -- one or several 128-token tiles, ragged K (partial 128-row tiles and
-# partial groups), group sizes 32 / 64 / 128 / 256, split-K over N.
-@pytest.mark.parametrize("k,n,m,g", [(4096, 14336, 16, 64), (1000, 1024, 17, 32), (2048, 5632, 100, 128),
-                                     (896, 4864, 40, 64), (520, 256, 300, 256), (384, 2048, 130, 32)])
+# (bits, K, N, m, group): at m >= 16, INT4 with N % 128 == 0 and INT8 with
+# N % 64 == 0 run the tcgen05 transposed kernel -- one or several 128-token
+# tiles, ragged K (partial 128-row tiles and partial groups), group sizes
+# 32 / 64 / 128 / 256, split-K over N.
+@pytest.mark.parametrize("bits,k,n,m,g", [(4, 4096, 14336, 16, 64), (4, 1000, 1024, 17, 32), (4, 2048, 5632, 100, 128),
+                                          (4, 896, 4864, 40, 64), (4, 520, 256, 300, 256), (4, 384, 2048, 130, 32),
+                                          (8, 4096, 14336, 16, 64), (8, 1000, 576, 17, 32), (8, 2048, 5632, 100, 128),
+                                          (8, 520, 64, 300, 256), (8, 384, 2048, 130, 64)])
 @pytest.mark.parametrize("accumulate", [False, True])
-def test_transposed_tensor_core_matches_oracle(kt, oracle, k, n, m, g, accumulate):
+def test_transposed_tensor_core_matches_oracle(kt, oracle, bits, k, n, m, g, accumulate):
     from kotensor_b200 import _lib
     rng = np.random.default_rng(k + n + m)
     w = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
-    ref_t = oracle.quantize(w, 4, g)
-    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), 4, g)
+    ref_t = oracle.quantize(w, bits, g)
+    qt = kt.QuantizedTensor.from_arrays(ref_t.qdata, ref_t.scales, ref_t.zeros, (k, n), bits, g)
     assert qt.transposed_path(m) == _lib.KT_PATH_TENSOR_CORE
     dy = rng.standard_normal((m, n), dtype=np.float32)
     dx0 = rng.standard_normal((m, k), dtype=np.float32)
@@ -344,8 +347,9 @@ def test_transposed_path_selection(kt, oracle):
     from kotensor_b200 import _lib
     rng = np.random.default_rng(3)
     for bits, n, g, m, want in [(4, 1024, 64, 16, _lib.KT_PATH_TENSOR_CORE), (4, 1024, 64, 15, _lib.KT_PATH_GENERIC),
-                                (8, 1024, 64, 64, _lib.KT_PATH_GENERIC), (4, 1000, 64, 64, _lib.KT_PATH_GENERIC),
-                                (4, 1024, 96, 64, _lib.KT_PATH_GENERIC)]:
+                                (8, 1024, 64, 64, _lib.KT_PATH_TENSOR_CORE), (8, 1000, 64, 64, _lib.KT_PATH_GENERIC),
+                                (8, 1024, 64, 15, _lib.KT_PATH_GENERIC), (4, 1000, 64, 64, _lib.KT_PATH_GENERIC),
+                                (4, 960, 64, 64, _lib.KT_PATH_GENERIC), (4, 1024, 96, 64, _lib.KT_PATH_GENERIC)]:
         w = (rng.standard_normal((256, n)) * 0.02).astype(np.float32)
         t = oracle.quantize(w, bits, g)
         qt = kt.QuantizedTensor.from_arrays(t.qdata, t.scales, t.zeros, (256, n), bits, g)
