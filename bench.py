@@ -449,7 +449,32 @@ def extra_points(kt, torch, weights, copies) -> dict:
             r.update(bound="tensor", frac=round(tf / tpeak, 4))
         return r
 
-    out = {"config2_int4": [point(weights, SHAPES, m, 4) for m in (4, 16, 128)]}
+    def tpoint(ws_copies, shapes, m):
+        # MatMul.multiplyByQuantizedTransposed (the QLoRA / fused-loss backward):
+        # dx[m x K] = dy[m x N] . deq(W)^T, the same bytes and flops as the product
+        dys = [torch.randn((m, n), generator=gen, device="cuda") for _, n in shapes]
+        dxs = [torch.empty((m, k), device="cuda") for k, _ in shapes]
+
+        def cycle():
+            for row in ws_copies:
+                for si in range(len(shapes)):
+                    kt.MatMul.multiply_by_quantized_transposed(dys[si], row[si], dxs[si], m, accumulate=False)
+
+        us = _graph_time_us(torch, cycle, len(ws_copies) * len(shapes))
+        bytes_ = sum(algo_bytes(k, n, m, 4) for k, n in shapes) / len(shapes)
+        flops = sum(2.0 * m * k * n for k, n in shapes) / len(shapes)
+        gbs, tf = bytes_ / (us / 1e6) / 1e9, flops / (us / 1e6) / 1e12
+        r = {"m": m, "us_per_launch": round(us, 2), "gbs": round(gbs, 1), "tflops": round(tf, 1),
+             "kernel": "gemm_t (tcgen05)" if ws_copies[0][-1].transposed_path(m) == _lib.KT_PATH_TENSOR_CORE
+             else "matmul_t (fp32)"}
+        if m <= 64:
+            r.update(bound="hbm", frac=round(gbs / peak, 4))
+        else:
+            r.update(bound="tensor", frac=round(tf / tpeak, 4))
+        return r
+
+    out = {"config2_int4": [point(weights, SHAPES, m, 4) for m in (4, 16, 128)],
+           "config2_int4_transposed": [tpoint(weights, SHAPES, m) for m in (16, 128)]}
     one = algo_bytes(2048, 2048, 1, 8) - 4 * 4096
     n8 = max(2, math.ceil(4 * L2_BYTES / one))
     c1 = []
