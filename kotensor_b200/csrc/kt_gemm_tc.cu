@@ -968,9 +968,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         bool ok = true;
-        const int r = 16 * warp + (lane >> 1);  // row of the tile
-        const int hh = lane & 1;                // bytes 32 hh .. + 31 of the row
+        const int r = 16 * warp + (lane >> 1);  // INT8: row of the tile
+        const int hh = lane & 1;                // INT8: bytes 32 hh .. + 31 of the row
         const int gsl = min((k0 + r) / p.gs, p.G - 1) - g_first;  // the row's group slot
+        const int c4 = threadIdx.x & 15, rg = threadIdx.x >> 4;  // INT4: bytes 4 c4 .., rows 8 rg ..
+        const int gsl4 = min((k0 + 8 * rg) / p.gs, p.G - 1) - g_first;
         for (int i = 0; i < n_kb; ++i) {
             const int s = i % kStages;
             if (!mbar_wait_bounded(full_w(s), (i / kStages) & 1)) {
@@ -979,53 +981,50 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             const unsigned char* st = gbase + s * kTStageBytes;
-            const uint4 wa = *reinterpret_cast<const uint4*>(st + r * 64 + 32 * hh);
-            const uint4 wb = *reinterpret_cast<const uint4*>(st + r * 64 + 32 * hh + 16);
-            const unsigned char* slot = gbase + kStages * kTStageBytes + s * kTScaleStageBytes + gsl * kTGroupBytes;
             if constexpr (kInt4) {
-                const float* s_lo = reinterpret_cast<const float*>(slot) + 32 * hh;
-                const float* s_hi = reinterpret_cast<const float*>(slot + 256) + 32 * hh;
-                const uint4 zla = *reinterpret_cast<const uint4*>(slot + 512 + 32 * hh);
-                const uint4 zlb = *reinterpret_cast<const uint4*>(slot + 512 + 32 * hh + 16);
-                const uint4 zha = *reinterpret_cast<const uint4*>(slot + 576 + 32 * hh);
-                const uint4 zhb = *reinterpret_cast<const uint4*>(slot + 576 + 32 * hh + 16);
-                const uint32_t wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-                const uint32_t zlv[8] = {zla.x, zla.y, zla.z, zla.w, zlb.x, zlb.y, zlb.z, zlb.w};
-                const uint32_t zhv[8] = {zha.x, zha.y, zha.z, zha.w, zhb.x, zhb.y, zhb.z, zhb.w};
-                uint32_t lo[16], hi[16];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-#pragma unroll
-                    for (int h2 = 0; h2 < 2; ++h2) {
-                        // bytes 4q + 2h2 and + 1 of the lane's 32 in the two halves of a word, each
-                        // nibble ORed into bf16 128.0: 128 + q exactly; the zero points alike
-                        const uint32_t sel = h2 ? 0x4342u : 0x4140u;
-                        const uint32_t pr = prmt(wv[q], 0u, sel);
-                        const uint32_t ql = lop3_and_or(pr, 0x000F000Fu, 0x43004300u);
-                        const uint32_t qh = lop3_and_or(pr >> 4, 0x000F000Fu, 0x43004300u);
-                        const uint32_t zl = lop3_and_or(prmt(zlv[q], 0u, sel), 0x000F000Fu, 0x43004300u);
-                        const uint32_t zh = lop3_and_or(prmt(zhv[q], 0u, sel), 0x000F000Fu, 0x43004300u);
-                        const int j = 4 * q + 2 * h2;
-                        const float2 sl2 = *reinterpret_cast<const float2*>(s_lo + j);
-                        const float2 sh2 = *reinterpret_cast<const float2*>(s_hi + j);
-                        lo[2 * q + h2] = bf2_sub_mul(ql, zl, pack_bf16(sl2.x, sl2.y));
-                        hi[2 * q + h2] = bf2_sub_mul(qh, zh, pack_bf16(sh2.x, sh2.y));
-                    }
-                }
+                // thread: bytes 4 c4 .. + 3 (columns n0 + 4 c4 .. + 3 low, R + n0 + .. high)
+                // of rows 8 rg .. 8 rg + 7, which share one group: the scales and zero
+                // points are converted once per stage, not per row.  Half-warps take
+                // their rows in opposite parity order (row loads conflict-free).
+                const unsigned char* slot =
+                    gbase + kStages * kTStageBytes + s * kTScaleStageBytes + gsl4 * kTGroupBytes;
+                const float4 sl = *reinterpret_cast<const float4*>(slot + 16 * c4);
+                const float4 sh = *reinterpret_cast<const float4*>(slot + 256 + 16 * c4);
+                const uint32_t zl = *reinterpret_cast<const uint32_t*>(slot + 512 + 4 * c4);
+                const uint32_t zh = *reinterpret_cast<const uint32_t*>(slot + 576 + 4 * c4);
+                const uint32_t sl0 = pack_bf16(sl.x, sl.y), sl1 = pack_bf16(sl.z, sl.w);
+                const uint32_t sh0 = pack_bf16(sh.x, sh.y), sh1 = pack_bf16(sh.z, sh.w);
+                // zero points as bf16 128 + z, two columns per word
+                const uint32_t zl0 = lop3_and_or(prmt(zl, 0u, 0x4140u), 0x000F000Fu, 0x43004300u);
+                const uint32_t zl1 = lop3_and_or(prmt(zl, 0u, 0x4342u), 0x000F000Fu, 0x43004300u);
+                const uint32_t zh0 = lop3_and_or(prmt(zh, 0u, 0x4140u), 0x000F000Fu, 0x43004300u);
+                const uint32_t zh1 = lop3_and_or(prmt(zh, 0u, 0x4342u), 0x000F000Fu, 0x43004300u);
                 unsigned char* alo = gbase + s * kTStageBytes + kTRawBytes + 2 * kTXBytes;
                 unsigned char* ahi = alo + kTABytes;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 hh + c of row r, 128-byte swizzle
-                    const uint32_t off = static_cast<uint32_t>(r * 128 + (((4 * hh + c) ^ (r & 7)) << 4));
-                    *reinterpret_cast<uint4*>(alo + off) =
-                        make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
-                    *reinterpret_cast<uint4*>(ahi + off) =
-                        make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
+                for (int jj = 0; jj < 8; ++jj) {
+                    const int rr = 8 * rg + (jj ^ (rg & 1));
+                    const uint32_t w = *reinterpret_cast<const uint32_t*>(st + rr * 64 + 4 * c4);
+                    // bytes (0, 1) and (2, 3) in the halves of a word; each nibble ORed into
+                    // bf16 128.0 is 128 + q exactly, minus 128 + zero exactly, times the scale
+                    const uint32_t p0 = prmt(w, 0u, 0x4140u), p1 = prmt(w, 0u, 0x4342u);
+                    const uint32_t lo0 = bf2_sub_mul(lop3_and_or(p0, 0x000F000Fu, 0x43004300u), zl0, sl0);
+                    const uint32_t lo1 = bf2_sub_mul(lop3_and_or(p1, 0x000F000Fu, 0x43004300u), zl1, sl1);
+                    const uint32_t hi0 = bf2_sub_mul(lop3_and_or(p0 >> 4, 0x000F000Fu, 0x43004300u), zh0, sh0);
+                    const uint32_t hi1 = bf2_sub_mul(lop3_and_or(p1 >> 4, 0x000F000Fu, 0x43004300u), zh1, sh1);
+                    // bf16 columns 4 c4 .. + 3 of row rr: 8 bytes of 16-byte chunk c4 / 2, 128-byte swizzle
+                    const uint32_t off =
+                        static_cast<uint32_t>(rr * 128 + (((c4 >> 1) ^ (rr & 7)) << 4) + 8 * (c4 & 1));
+                    *reinterpret_cast<uint2*>(alo + off) = make_uint2(lo0, lo1);
+                    *reinterpret_cast<uint2*>(ahi + off) = make_uint2(hi0, hi1);
                 }
             } else {
                 // bytes 32 hh .. + 31 of row r: columns n0 + 32 hh + j, each
                 // 2^23 + (q + 128) in an fp32 mantissa minus 2^23 + 128 (exactly q),
                 // times the column's scale in fp32, rounded to bf16
+                const uint4 wa = *reinterpret_cast<const uint4*>(st + r * 64 + 32 * hh);
+                const uint4 wb = *reinterpret_cast<const uint4*>(st + r * 64 + 32 * hh + 16);
+                const unsigned char* slot = gbase + kStages * kTStageBytes + s * kTScaleStageBytes + gsl * kTGroupBytes;
                 const float* sc = reinterpret_cast<const float*>(slot) + 32 * hh;
                 const uint32_t wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
                 uint32_t lo[16];
