@@ -830,11 +830,22 @@ constexpr int kTMaxGroups = 4;           // groups a 128-row tile can touch (gro
 // per group: scales low [64] | scales high [64] | zeros low [64] | zeros high [64]
 constexpr int kTGroupBytes = 2 * 64 * 4 + 2 * 64;
 constexpr int kTScaleStageBytes = kTMaxGroups * kTGroupBytes;
-constexpr size_t kTSmemBytes = 1024 + static_cast<size_t>(kStages) * (kTStageBytes + kTScaleStageBytes) + kBarBytes;
-static_assert(kTStageBytes % 1024 == 0 && kTRawBytes % 1024 == 0 && kTXBytes % 1024 == 0, "1024-byte tiles");
-static_assert(kTSmemBytes <= 232448, "shared memory per CTA");
+constexpr int kTBarBytes = 256;
+// A stage holds the dy tiles of this launch's nt tokens only (nt x 128 bytes each,
+// a multiple of 2 KiB), so at nt <= 48 the ring has room for a fourth stage.
+__host__ __device__ constexpr int t_stage_bytes(int nt) { return kTRawBytes + 2 * nt * 64 * 2 + 2 * kTABytes; }
+constexpr size_t t_smem_bytes(int stages, int nt) {
+    return 1024 + static_cast<size_t>(stages) * (t_stage_bytes(nt) + kTScaleStageBytes) + kTBarBytes;
+}
+constexpr int kTMaxNT4 = 48;  // the largest nt with four stages
+static_assert(kTStageBytes == t_stage_bytes(kTMaxNT) && kTRawBytes % 1024 == 0 && kTXBytes % 1024 == 0 &&
+              t_stage_bytes(16) % 1024 == 0, "1024-byte tiles");
+// + 1 KiB of static shared memory
+static_assert(t_smem_bytes(kStages, kTMaxNT) + 1024 <= 232448 && t_smem_bytes(4, kTMaxNT4) + 1024 <= 232448,
+              "shared memory per CTA");
+static_assert(8 * (4 * 4 + 1) + 4 <= kTBarBytes, "barrier area");
 
-template <int BITS>
+template <int BITS, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_t_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_dy,
                   GemmParams p) {
@@ -854,21 +865,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int g_first = min(k0 / p.gs, p.G - 1);
     const int g_last = min((k0 + kTRows - 1) / p.gs, p.G - 1);
 
+    const int xbytes = p.nt * 64 * 2;  // one dy tile: nt rows x 64 bf16
+    const int stage_bytes = kTRawBytes + 2 * xbytes + 2 * kTABytes;
     const uint32_t raw_s = smem_u32(smem_raw);
     const uint32_t base = (raw_s + 1023u) & ~1023u;
     unsigned char* gbase = smem_raw + (base - raw_s);
-    const uint32_t scl = base + kStages * kTStageBytes;  // group slots [stage][group]
-    const uint32_t bars = scl + kStages * kTScaleStageBytes;
+    const uint32_t scl = base + STAGES * stage_bytes;  // group slots [stage][group]
+    const uint32_t bars = scl + STAGES * kTScaleStageBytes;
     auto full_w = [&](int s) { return bars + 8 * s; };
-    auto full_x = [&](int s) { return bars + 8 * (kStages + s); };
-    auto full_a = [&](int s) { return bars + 8 * (2 * kStages + s); };
-    auto empty = [&](int s) { return bars + 8 * (3 * kStages + s); };
-    const uint32_t done = bars + 8 * (4 * kStages);
+    auto full_x = [&](int s) { return bars + 8 * (STAGES + s); };
+    auto full_a = [&](int s) { return bars + 8 * (2 * STAGES + s); };
+    auto empty = [&](int s) { return bars + 8 * (3 * STAGES + s); };
+    const uint32_t done = bars + 8 * (4 * STAGES);
     uint32_t* tmem_slot =
-        reinterpret_cast<uint32_t*>(gbase + kStages * (kTStageBytes + kTScaleStageBytes) + 8 * (4 * kStages + 1));
+        reinterpret_cast<uint32_t*>(gbase + STAGES * (stage_bytes + kTScaleStageBytes) + 8 * (4 * STAGES + 1));
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < STAGES; ++s) {
             mbar_init(full_w(s), 1);
             mbar_init(full_x(s), 1);
             mbar_init(full_a(s), kWorkers);
@@ -895,10 +908,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t gtx = static_cast<uint32_t>((g_last - g_first + 1) * (kInt4 ? kTGroupBytes : 64 * 4));
             // the packed bytes and the group constants of block i -> full_w(i % NS)
             auto issue_w = [&](int i) {
-                const int s = i % kStages;
+                const int s = i % STAGES;
                 const int n0 = (kb_begin + i) * 64;
                 mbar_expect_tx(full_w(s), kTRawBytes + gtx);
-                tma_load_2d(base + s * kTStageBytes, &tmap_w, n0, k0, full_w(s));
+                tma_load_2d(base + s * stage_bytes, &tmap_w, n0, k0, full_w(s));
                 for (int g = g_first; g <= g_last; ++g) {
                     const uint32_t dst = scl + s * kTScaleStageBytes + (g - g_first) * kTGroupBytes;
                     const int64_t go = static_cast<int64_t>(g) * ncols;
@@ -912,23 +925,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             // the two bf16 tiles of dy (columns n0.., R + n0..) of block i -> full_x(i % NS)
             auto issue_x = [&](int i) {
-                const int s = i % kStages;
+                const int s = i % STAGES;
                 const int n0 = (kb_begin + i) * 64;
-                const uint32_t xs = base + s * kTStageBytes + kTRawBytes;
+                const uint32_t xs = base + s * stage_bytes + kTRawBytes;
                 mbar_expect_tx(full_x(s), xtx);
                 tma_load_2d(xs, &tmap_dy, n0, tok0, full_x(s));
-                if (kInt4) tma_load_2d(xs + kTXBytes, &tmap_dy, half + n0, tok0, full_x(s));
+                if (kInt4) tma_load_2d(xs + xbytes, &tmap_dy, half + n0, tok0, full_x(s));
             };
             // weights of the first stages before the wait (no kernel of the chain writes
             // them), dy only after it: dy is the previous kernel's output
-            const int pre = min(n_kb, kStages);
+            const int pre = min(n_kb, STAGES);
             for (int i = 0; i < pre; ++i) issue_w(i);
             dev::pdl_wait();
             for (int i = 0; i < pre; ++i) issue_x(i);
             int issued = pre;
             for (int i = pre; i < n_kb; ++i) {
-                const int s = i % kStages;
-                if (!mbar_wait_bounded(empty(s), ((i / kStages) - 1) & 1)) {
+                const int s = i % STAGES;
+                if (!mbar_wait_bounded(empty(s), ((i / STAGES) - 1) & 1)) {
                     atomicOr(p.err, 1);
                     break;
                 }
@@ -937,23 +950,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++issued;
             }
             // the last copies issued into each slot have landed before the CTA may exit
-            for (int i = max(0, issued - kStages); i < issued; ++i) {
-                if (!mbar_wait_bounded(full_w(i % kStages), (i / kStages) & 1)) break;
-                if (!mbar_wait_bounded(full_x(i % kStages), (i / kStages) & 1)) break;
+            for (int i = max(0, issued - STAGES); i < issued; ++i) {
+                if (!mbar_wait_bounded(full_w(i % STAGES), (i / STAGES) & 1)) break;
+                if (!mbar_wait_bounded(full_x(i % STAGES), (i / STAGES) & 1)) break;
             }
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             for (int i = 0; i < n_kb; ++i) {
-                const int s = i % kStages;
-                const uint32_t par = (i / kStages) & 1;
+                const int s = i % STAGES;
+                const uint32_t par = (i / STAGES) & 1;
                 if (!mbar_wait_bounded(full_x(s), par) || !mbar_wait_bounded(full_a(s), par)) {
                     atomicOr(p.err, 1);
                     break;
                 }
                 tc_fence_after();
-                const uint32_t xlo = base + s * kTStageBytes + kTRawBytes, xhi = xlo + kTXBytes;
-                const uint32_t alo = xhi + kTXBytes, ahi = alo + kTABytes;
+                const uint32_t xlo = base + s * stage_bytes + kTRawBytes, xhi = xlo + xbytes;
+                const uint32_t alo = xhi + xbytes, ahi = alo + kTABytes;
 #pragma unroll
                 for (int kk = 0; kk < 64 / 16; ++kk) {
                     const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
@@ -974,20 +987,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c4 = threadIdx.x & 15, rg = threadIdx.x >> 4;  // INT4: bytes 4 c4 .., rows 8 rg ..
         const int gsl4 = min((k0 + 8 * rg) / p.gs, p.G - 1) - g_first;
         for (int i = 0; i < n_kb; ++i) {
-            const int s = i % kStages;
-            if (!mbar_wait_bounded(full_w(s), (i / kStages) & 1)) {
+            const int s = i % STAGES;
+            if (!mbar_wait_bounded(full_w(s), (i / STAGES) & 1)) {
                 if (lane == 0) atomicOr(p.err, 1);
                 ok = false;
                 break;
             }
-            const unsigned char* st = gbase + s * kTStageBytes;
+            const unsigned char* st = gbase + s * stage_bytes;
             if constexpr (kInt4) {
                 // thread: bytes 4 c4 .. + 3 (columns n0 + 4 c4 .. + 3 low, R + n0 + .. high)
                 // of rows 8 rg .. 8 rg + 7, which share one group: the scales and zero
                 // points are converted once per stage, not per row.  Half-warps take
                 // their rows in opposite parity order (row loads conflict-free).
                 const unsigned char* slot =
-                    gbase + kStages * kTStageBytes + s * kTScaleStageBytes + gsl4 * kTGroupBytes;
+                    gbase + STAGES * stage_bytes + s * kTScaleStageBytes + gsl4 * kTGroupBytes;
                 const float4 sl = *reinterpret_cast<const float4*>(slot + 16 * c4);
                 const float4 sh = *reinterpret_cast<const float4*>(slot + 256 + 16 * c4);
                 const uint32_t zl = *reinterpret_cast<const uint32_t*>(slot + 512 + 4 * c4);
@@ -999,7 +1012,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t zl1 = lop3_and_or(prmt(zl, 0u, 0x4342u), 0x000F000Fu, 0x43004300u);
                 const uint32_t zh0 = lop3_and_or(prmt(zh, 0u, 0x4140u), 0x000F000Fu, 0x43004300u);
                 const uint32_t zh1 = lop3_and_or(prmt(zh, 0u, 0x4342u), 0x000F000Fu, 0x43004300u);
-                unsigned char* alo = gbase + s * kTStageBytes + kTRawBytes + 2 * kTXBytes;
+                unsigned char* alo = gbase + s * stage_bytes + kTRawBytes + 2 * xbytes;
                 unsigned char* ahi = alo + kTABytes;
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) {
@@ -1024,7 +1037,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // times the column's scale in fp32, rounded to bf16
                 const uint4 wa = *reinterpret_cast<const uint4*>(st + r * 64 + 32 * hh);
                 const uint4 wb = *reinterpret_cast<const uint4*>(st + r * 64 + 32 * hh + 16);
-                const unsigned char* slot = gbase + kStages * kTStageBytes + s * kTScaleStageBytes + gsl * kTGroupBytes;
+                const unsigned char* slot = gbase + STAGES * stage_bytes + s * kTScaleStageBytes + gsl * kTGroupBytes;
                 const float* sc = reinterpret_cast<const float*>(slot) + 32 * hh;
                 const uint32_t wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
                 uint32_t lo[16];
@@ -1042,7 +1055,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         lo[2 * q + h2] = pack_bf16(__fmul_rn(s2.x, q0), __fmul_rn(s2.y, q1));
                     }
                 }
-                unsigned char* alo = gbase + s * kTStageBytes + kTRawBytes + 2 * kTXBytes;
+                unsigned char* alo = gbase + s * stage_bytes + kTRawBytes + 2 * xbytes;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 hh + c of row r, 128-byte swizzle
                     const uint32_t off = static_cast<uint32_t>(r * 128 + (((4 * hh + c) ^ (r & 7)) << 4));
@@ -1447,11 +1460,14 @@ cudaError_t launch_gemm_t(const QView& w, const float* dy, float* dx, int32_t m,
                         static_cast<uint64_t>(m), static_cast<uint64_t>(w.columns) * 2, 64, static_cast<uint32_t>(p.nt),
                         CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    auto kernel = w.bits == 4 ? gemm_t_kernel<4> : gemm_t_kernel<8>;
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTSmemBytes));
+    const bool four = p.nt <= kTMaxNT4;
+    auto kernel = w.bits == 4 ? (four ? gemm_t_kernel<4, 4> : gemm_t_kernel<4, kStages>)
+                              : (four ? gemm_t_kernel<8, 4> : gemm_t_kernel<8, kStages>);
+    const size_t smem = t_smem_bytes(four ? 4 : kStages, p.nt);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     const dim3 grid((w.rows + kTRows - 1) / kTRows, (m + p.nt - 1) / p.nt, S);
-    e = launch_chained(kernel, grid, dim3(kThreads), kTSmemBytes, s, tmap_w, tmap_dy, p);
+    e = launch_chained(kernel, grid, dim3(kThreads), smem, s, tmap_w, tmap_dy, p);
     if (e != cudaSuccess || !p.reduce_kernel) return e;
     const int64_t quads = static_cast<int64_t>(grid.x) * grid.y * p.nt * 32;
     const int blocks = static_cast<int>(std::min<int64_t>((quads + 255) / 256, static_cast<int64_t>(sm_count) * 8));
