@@ -74,3 +74,24 @@ def test_product_package_does_not_import_the_oracle():
             if f.endswith((".py", ".cu", ".h", ".cuh", ".cpp")):
                 text = open(os.path.join(dirpath, f), errors="replace").read()
                 assert "oracle" not in re.sub(r"#.*|//.*", "", text).lower().replace("oracle_", ""), f
+
+
+def test_matmul_argument_checks_follow_the_reference(kt):
+    """MatMul.multiplyQuantized's require(...) checks and messages (MatMul.kt:470-473) and
+    multiplyByQuantizedTransposed's (MatMul.kt:963-965), raised on the host before any
+    device work; m == 0 is a no-op."""
+    import numpy as np
+    from types import SimpleNamespace
+    w = SimpleNamespace(rows=4, columns=8)  # K = 4, N = 8: only the shape is read before the checks pass
+    with pytest.raises(ValueError, match="Negative row count -1"):
+        kt.MatMul.multiply_quantized(np.zeros(4, np.float32), w, np.zeros(8, np.float32), -1)
+    with pytest.raises(ValueError, match="a has 7 elements, needs 2 × 4"):
+        kt.MatMul.multiply_quantized(np.zeros(7, np.float32), w, np.zeros(16, np.float32), 2)
+    with pytest.raises(ValueError, match="c has 15 elements, needs 2 × 8"):
+        kt.MatMul.multiply_quantized(np.zeros(8, np.float32), w, np.zeros(15, np.float32), 2)
+    kt.MatMul.multiply_quantized(np.zeros(0, np.float32), w, np.zeros(0, np.float32), 0)
+    with pytest.raises(ValueError, match="dy has 15 elements, needs 2 × 8"):
+        kt.MatMul.multiply_by_quantized_transposed(np.zeros(15, np.float32), w, np.zeros(8, np.float32), 2)
+    with pytest.raises(ValueError, match="dx has 7 elements, needs 2 × 4"):
+        kt.MatMul.multiply_by_quantized_transposed(np.zeros(16, np.float32), w, np.zeros(7, np.float32), 2)
+    kt.MatMul.multiply_by_quantized_transposed(np.zeros(0, np.float32), w, np.zeros(0, np.float32), 0)
