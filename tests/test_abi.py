@@ -95,3 +95,23 @@ def test_matmul_argument_checks_follow_the_reference(kt):
     with pytest.raises(ValueError, match="dx has 7 elements, needs 2 × 4"):
         kt.MatMul.multiply_by_quantized_transposed(np.zeros(16, np.float32), w, np.zeros(7, np.float32), 2)
     kt.MatMul.multiply_by_quantized_transposed(np.zeros(0, np.float32), w, np.zeros(0, np.float32), 0)
+
+
+def test_quantized_tensor_constructor_checks_follow_the_reference(kt):
+    """QuantizedTensor's init require(...) checks and messages (QuantizedTensor.kt:63-70),
+    raised on the host before any device work."""
+    import numpy as np
+    QT = kt.QuantizedTensor
+    with pytest.raises(ValueError, match=r"needs a 2-D shape, got \[4, 0\]"):
+        QT.from_arrays(np.zeros(0, np.uint8), np.zeros(0, np.float32), None, (4, 0), 8, 64)
+    with pytest.raises(ValueError, match="bits must be 4 or 8"):
+        QT.from_arrays(np.zeros(16, np.uint8), np.zeros(4, np.float32), None, (4, 4), 3, 64)
+    # INT4 split-half packing: 5 columns take 3 bytes per row
+    with pytest.raises(ValueError, match="qdata has 10 bytes, expected 12"):
+        QT.from_arrays(np.zeros(10, np.uint8), np.zeros(5, np.float32), np.zeros(5, np.uint8), (4, 5), 4, 64)
+    with pytest.raises(ValueError, match="scales has 4 entries, expected 10"):
+        QT.from_arrays(np.zeros(12, np.uint8), np.zeros(4, np.float32), np.zeros(10, np.uint8), (4, 5), 4, 2)
+    with pytest.raises(ValueError, match="zeros has 5 entries, expected 10"):
+        QT.from_arrays(np.zeros(12, np.uint8), np.zeros(10, np.float32), np.zeros(5, np.uint8), (4, 5), 4, 2)
+    with pytest.raises(ValueError, match="4-bit tensors need zero points"):
+        QT.from_arrays(np.zeros(12, np.uint8), np.zeros(5, np.float32), None, (4, 5), 4, 64)
